@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Decode tokens/s of voxtral.cpp's decoder KV step on B200.
+
+One "step" = every stream appends one token and attends over its cache in all
+decoder layers (fused RoPE + K/V append + GQA flash-decoding attention per
+layer, through libvxk.so's C ABI).  Default workload = BASELINE config 2:
+64 streams per GPU, 30 layers (Voxtral-Mini-3B decoder shape: 32 q / 8 kv
+heads x 128), f16 cache in 16-token pages with a seeded random block table,
+contexts seeded uniform in [400, 4096].  Synthetic N(0, 0.5^2) activations.
+
+Multi-GPU: one process per GPU (torchrun); each rank owns its own 64 streams
+(weak scaling, no data-path collective); timing is max over ranks.
+
+`--impl reference` times the CPU restatement of the same path (the reference's
+ggml CPU backend cannot be built here: ggml is fetched at configure time and
+is absent) on the host cores, on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "voxtral.cpp_b200"))
+
+HD, NQ, NKV, BT = 128, 32, 8, 16
+CONFIGS = {
+    # name: layers, streams per GPU, ctx range, dtype, capacity
+    "2": dict(layers=30, streams=64, ctx=(400, 4096), dtype=1, capacity=8192,
+              desc="3B decoder, 64 streams/GPU, ctx~U[400,4096], f16 16-token pages, random block table"),
+    "3": dict(layers=26, streams=64, ctx=(8192, 8192), dtype=1, capacity=8192,
+              desc="4B realtime decoder, full 8192-slot sliding rings (steady state: one eviction per step)"),
+    "5": dict(layers=30, streams=32, ctx=(8192, 32768), dtype=8, capacity=32768 + 1024,
+              desc="3B decoder, q8_0 cache, ctx~U[8192,32768] (streams that fit one GPU)"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["vxk", "reference"], default="vxk")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="2")
+    ap.add_argument("--streams", type=int, default=0, help="override streams per GPU")
+    ap.add_argument("--seed", type=int, default=20261201)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def algorithmic_bytes(ctx: int, dtype: int) -> int:
+    """Bytes one decode token must move in one layer (per-layer figure of the
+    unit): K+V window reads + q/k/v fp32 reads + append write + fp32 output."""
+    if dtype == 8:
+        return 2176 * ctx + 43136
+    return 4096 * ctx + 45056
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(config: str):
+    """Per-launch DRAM bytes of decode_kernel from a committed ncu summary,
+    as bytes per algorithmic byte (scaled to this run's launches), or None."""
+    p = ROOT / "profiles" / f"decode_kernel_config{config}.traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return float(json.loads(p.read_text())["dram_bytes_per_algorithmic_byte"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, warmup=0):
+    """Times the CPU restatement (oracle/vx_cpu_step.c) of the same decode
+    step on all host cores.  Returns (tokens/s, steps done, threads)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    ctx0 = rng.integers(ctx_range[0], ctx_range[1] + 1, size=n_streams)
+    total = (steps or 0) + warmup + 64
+    cap = int(ctx0.max()) + total + 16
+    shape = (n_streams, layers, NKV, cap, HD)
+    block = (rng.standard_normal(1 << 22).astype(np.float32) * 0.5).astype(np.float16).view(np.uint16)
+    kc = np.resize(block, int(np.prod(shape))).reshape(shape)
+    vc = np.resize(block[::-1], int(np.prod(shape))).reshape(shape)
+    q = rng.standard_normal((n_streams, layers, NQ, HD), dtype=np.float32) * 0.5
+    k = rng.standard_normal((n_streams, layers, NKV, HD), dtype=np.float32) * 0.5
+    v = rng.standard_normal((n_streams, layers, NKV, HD), dtype=np.float32) * 0.5
+    rope = vx_oracle.rope_table(cap + 1, HD, 1e6)
+    pos = ctx0.astype(np.int64)
+    win = np.zeros(n_streams, dtype=np.int64)
+    threads = os.cpu_count() or 1
+    scale = float(np.float32(1.0 / np.sqrt(HD)))
+    for _ in range(warmup):
+        vx_oracle.cpu_decode_step_f16(kc, vc, q, k, v, pos, win, rope, scale, threads)
+        pos += 1
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        vx_oracle.cpu_decode_step_f16(kc, vc, q, k, v, pos, win, rope, scale, threads)
+        pos += 1
+        done += 1
+        el = time.perf_counter() - t0
+        if steps is not None and done >= steps:
+            break
+        if seconds is not None and el >= seconds:
+            break
+    el = time.perf_counter() - t0
+    return n_streams * done / el, done, threads, float(np.mean(ctx0))
+
+
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return
+    n_streams = 4
+    budget = 150.0
+    tps, done, threads, mean_ctx = cpu_sample(cfg["layers"], n_streams, cfg["ctx"], args.seed, seconds=budget,
+                                              steps=args.steps, warmup=min(args.warmup, 3))
+    line = {
+        "impl": "reference",
+        "metric": "decode tokens/s (KV append+GQA attn)",
+        "value": round(tps, 3),
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": done,
+        "warmup": min(args.warmup, 3),
+        "ms_per_step": round(1000.0 * n_streams / tps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 cache, fp32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": f"config {args.config}: {cfg['desc']}", "layers": cfg["layers"],
+                   "streams_sampled": n_streams, "mean_ctx": mean_ctx},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{n_streams} streams x {cfg['layers']} layers x {done} steps of the CPU "
+                                   f"restatement (oracle/vx_cpu_step.c), ggml absent"},
+        "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    cfg = dict(CONFIGS[args.config])
+    if args.streams:
+        cfg["streams"] = args.streams
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, world)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
+    import vxk
+
+    L, S = cfg["layers"], cfg["streams"]
+    dtype = cfg["dtype"]
+    rng = np.random.default_rng(args.seed + 1000 * rank)
+    lo, hi = cfg["ctx"]
+    ctx0 = rng.integers(lo, hi + 1, size=S)
+    total_steps = args.warmup + args.steps * (1 if args.no_e2e else 2) + 2
+    cap = cfg["capacity"]
+    need_pos = int(ctx0.max()) + total_steps + BT
+    pages_per_stream = [min(cap // BT, (int(c) + total_steps) // BT + 2) for c in ctx0]
+    n_blocks = int(sum(pages_per_stream)) + 64
+    max_prefill = int(min(cap, ctx0.max()))
+    prefill_chunk = min(max_prefill, 4096)
+    pool = vxk.Pool(device=local, n_layers=L, n_q_heads=NQ, n_kv_heads=NKV, head_dim=HD, block_tokens=BT,
+                    capacity=cap, n_blocks=n_blocks, max_streams=S, max_rows=max(S, prefill_chunk),
+                    max_position=need_pos + 16, dtype=dtype, alloc_seed=1234 + rank)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    streams = [pool.open_stream() for _ in range(S)]
+
+    # ---- fill caches to ctx0 (append only; values random) -------------------
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    kfill = torch.randn((prefill_chunk, NKV, HD), device="cuda", generator=gen) * 0.5
+    vfill = torch.randn((prefill_chunk, NKV, HD), device="cuda", generator=gen) * 0.5
+    for s, c in zip(streams, ctx0):
+        left = int(c)
+        while left > 0:
+            n = min(left, prefill_chunk)
+            pool.plan([s], [n], sh)
+            for layer in range(L):
+                pool.append_layer(layer, kfill.data_ptr(), vfill.data_ptr(), sh)
+            pool.commit()
+            left -= n
+    torch.cuda.synchronize()
+    del kfill, vfill
+
+    # ---- per-step inputs resident in HBM (4 rotating sets) -------------------
+    NSETS = 4
+    qs = torch.randn((NSETS, L, S, NQ, HD), device="cuda", generator=gen) * 0.5
+    ks = torch.randn((NSETS, L, S, NKV, HD), device="cuda", generator=gen) * 0.5
+    vs = torch.randn((NSETS, L, S, NKV, HD), device="cuda", generator=gen) * 0.5
+    out = torch.empty((L, S, NQ, HD), device="cuda")
+    ones = [1] * S
+    ctx_now = [int(c) for c in ctx0]
+
+    def step(i, ev=None):
+        pool.plan(streams, ones, sh)
+        st = i % NSETS
+        for layer in range(L):
+            if ev is not None:
+                ev[layer][0].record(stream)
+            pool.decode_layer(layer, qs[st, layer].data_ptr(), ks[st, layer].data_ptr(), vs[st, layer].data_ptr(),
+                              out[layer].data_ptr(), sh)
+            if ev is not None:
+                ev[layer][1].record(stream)
+        pool.commit()
+        for j in range(S):
+            ctx_now[j] = min(cap, ctx_now[j] + 1)
+
+    for i in range(args.warmup):
+        step(i)
+    pool.sync(sh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+
+    # ---- timed region --------------------------------------------------------
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    launches0 = pool.stats().kernel_launches
+    events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)] for _ in range(args.steps)]
+    bytes_per_step = []
+    ctx_means = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i, events[i])
+            bytes_per_step.append(sum(algorithmic_bytes(c, dtype) for c in ctx_now))
+            ctx_means.append(sum(ctx_now) / S)
+        end.record(stream)
+        torch.cuda.synchronize()
+    pool.sync(sh)
+    launches = pool.stats().kernel_launches - launches0
+    ms = start.elapsed_time(end)
+    launch_ms = [events[i][l][0].elapsed_time(events[i][l][1]) for i in range(args.steps) for l in range(L)]
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * S * args.steps / (ms / 1000.0)
+
+    # ---- roofline of the dominant kernel (decode_kernel) --------------------
+    peak, peak_kind = load_peaks()
+    bytes_per_launch = statistics.mean(bytes_per_step)  # one layer launch: every stream's token in that layer
+    avg_launch_s = statistics.mean(launch_ms) / 1000.0
+    achieved = bytes_per_launch / avg_launch_s / 1e9
+    traffic_ratio = load_traffic(args.config)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "frac_of_nominal_8000": round(achieved / 8000.0, 4),
+                "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_launch),
+                "algorithmic_bytes_per_launch": round(bytes_per_launch),
+                "avg_launch_us": round(avg_launch_s * 1e6, 2), "kernel": "decode_kernel<f16>" if dtype == 1 else
+                "decode_kernel<q8_0>"}
+
+    # ---- end to end through the host-buffer C-ABI entry point ----------------
+    e2e = None
+    if not args.no_e2e:
+        hq = torch.randn((L, S, NQ, HD)).mul_(0.5).pin_memory()
+        hk = torch.randn((L, S, NKV, HD)).mul_(0.5).pin_memory()
+        hv = torch.randn((L, S, NKV, HD)).mul_(0.5).pin_memory()
+        ho = torch.empty((L, S, NQ, HD)).pin_memory()
+        pool.decode_step_host(streams, hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr(), sh)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            pool.decode_step_host(streams, hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr(), sh)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ems], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(hq.numel() + hk.numel() + hv.numel()) * 4,
+               "d2h_bytes_per_step": int(ho.numel()) * 4, "ms_per_step": round(ems / args.steps, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and dtype == 1:
+        tps, done, threads, mean_ctx = cpu_sample(L, 4, cfg["ctx"], args.seed, seconds=args.cpu_seconds)
+        cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"4 streams (ctx~U{list(cfg['ctx'])}, mean {mean_ctx:.0f}) x {L} layers x {done} steps, "
+                         f"oracle/vx_cpu_step.c on {threads} host threads"}
+
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s (KV append+GQA attn)",
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 cache, fp32 accumulate" if dtype == 1 else "q8_0 cache, fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"config {args.config}: {cfg['desc']}", "layers": L, "streams_per_gpu": S,
+                       "global_batch": S * world, "mean_ctx_timed": round(statistics.mean(ctx_means), 1),
+                       "parallelism": f"streams sharded, {S}/GPU, no collective",
+                       "l2": "inputs larger than L2 (KV read per launch >> 126 MB)"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    pool.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,373 @@
+#ifndef VXK_H
+#define VXK_H
+
+/**
+ * @file vxk.h
+ * C ABI of the B200 (sm_100a) decoder KV-cache kernel layer for voxtral.cpp.
+ *
+ * This library replaces the ggml nodes that voxtral.cpp's decoder and
+ * streaming encoder emit for their KV caches:
+ *   - RoPE mode 0 on K and Q      (src/voxtral.cpp:2668-2671, 2463-2466)
+ *   - K/V append into the cache   (src/voxtral.cpp:2677-2714 set_rows / cpy)
+ *   - GQA attention over the cache (src/voxtral.cpp:2716-2854 flash_attn_ext)
+ *   - encoder windowed attention  (src/voxtral.cpp:2459-2487)
+ * and the host ring bookkeeping that drives them
+ *   (src/voxtral.cpp:1590-1656, 3636-3692; src/voxtral-internal.h:193-227,
+ *    381-435).
+ *
+ * Every function returns a vxk_status (numerically equal to the matching
+ * voxtral_status of include/voxtral.h:97-110 where one exists), never throws,
+ * and never frees caller memory.  Device pointers are plain CUDA device
+ * addresses; `cuda_stream` is a cudaStream_t passed as void*.  Kernel
+ * launches are asynchronous on that stream.  All calls on one pool must be
+ * serialised by the caller, like calls on one voxtral_context
+ * (include/voxtral.h:223).
+ */
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__) || defined(__clang__)
+#  define VXK_API __attribute__((visibility("default")))
+#else
+#  define VXK_API
+#endif
+
+#define VXK_API_VERSION 1u
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/** Status codes; 0..11 mirror voxtral_status (include/voxtral.h:97-110). */
+typedef enum vxk_status {
+    VXK_STATUS_OK = 0,
+    VXK_STATUS_INVALID_ARGUMENT = 1,
+    VXK_STATUS_INVALID_STATE = 2,
+    VXK_STATUS_OUT_OF_MEMORY = 3,
+    VXK_STATUS_NOT_READY = 5,
+    VXK_STATUS_BACKEND_ERROR = 9,
+    VXK_STATUS_INTERNAL_ERROR = 10,
+    VXK_STATUS_BUFFER_TOO_SMALL = 11,
+    VXK_STATUS_TIMEOUT = 12
+} vxk_status;
+
+/** Cache element formats; values are ggml_type numbers. */
+typedef enum vxk_dtype {
+    VXK_DTYPE_F16 = 1,
+    VXK_DTYPE_Q8_0 = 8,
+    VXK_DTYPE_BF16 = 30
+} vxk_dtype;
+
+/** Returns a static name for a status ("ok", "invalid_argument", ...). */
+VXK_API const char * vxk_status_string(vxk_status status);
+
+/** Returns VXK_API_VERSION. */
+VXK_API uint32_t vxk_api_version(void);
+
+/* ======================================================================== */
+/* Ring planners (host only, no device)                                     */
+/* ======================================================================== */
+
+/** Decoder ring state; replaces voxtral_decoder_kv_ring
+ *  (src/voxtral-internal.h:195-204).  Positions are absolute; storage
+ *  addressing is modulo `capacity`. */
+typedef struct vxk_decoder_kv_ring {
+    int64_t capacity;
+    int64_t used;
+    int64_t oldest_absolute_position;
+    int64_t next_absolute_position;
+    int64_t wraps;
+    int64_t evictions;
+    int64_t bytes_moved;
+    int64_t full_buffer_moves;
+} vxk_decoder_kv_ring;
+
+/** One physical ring segment (src/voxtral-internal.h:206-209). */
+typedef struct vxk_kv_seg {
+    int32_t slot;
+    int32_t len;
+} vxk_kv_seg;
+
+/** Decoder append plan; replaces voxtral_decoder_kv_plan_t
+ *  (src/voxtral-internal.h:211-223). */
+typedef struct vxk_decoder_kv_plan {
+    int64_t absolute_start;
+    int32_t n_new;
+    int32_t write_nseg;
+    vxk_kv_seg write_seg[2];
+    vxk_kv_seg read_seg[2];   /* oldest -> newest logical order */
+    int32_t read_nseg;
+    int32_t wrapped;
+    int64_t used_after;
+    int64_t oldest_after;
+    int64_t next_after;
+    int64_t evicted;
+} vxk_decoder_kv_plan;
+
+/** Plans appending n_new tokens at absolute_start; replaces
+ *  voxtral_decoder_kv_plan (src/voxtral.cpp:1618-1645).  Returns
+ *  VXK_STATUS_INVALID_ARGUMENT for exactly the cases the reference rejects. */
+VXK_API vxk_status vxk_decoder_kv_plan_make(const vxk_decoder_kv_ring * ring,
+                                            int64_t absolute_start, int32_t n_new,
+                                            vxk_decoder_kv_plan * out);
+
+/** Commits a plan; replaces decoder_kv_commit_plan (src/voxtral.cpp:1647-1656). */
+VXK_API vxk_status vxk_decoder_kv_plan_commit(vxk_decoder_kv_ring * ring,
+                                              const vxk_decoder_kv_plan * plan);
+
+/** Encoder ring plan; replaces voxtral_enc_kv_plan_t
+ *  (src/voxtral-internal.h:404-428). */
+typedef struct vxk_enc_kv_plan {
+    int64_t q_start;
+    int32_t n_new;
+    int32_t win_len;
+    int64_t win_start;
+    int64_t win_end;
+    vxk_kv_seg read_seg[2];
+    int32_t read_nseg;
+    int32_t read_wraps;
+    vxk_kv_seg write_seg[2];
+    int32_t write_nseg;
+    int32_t write_wraps;
+    int64_t conv_mel_start;
+    int64_t conv_mel_end;
+    int32_t conv_slice_start;
+    int32_t reserved;
+    int64_t evicted;
+} vxk_enc_kv_plan;
+
+/** Replaces voxtral_enc_kv_plan (src/voxtral.cpp:3656-3692). */
+VXK_API vxk_status vxk_enc_kv_plan_make(int64_t q_start, int32_t n_new, int32_t capacity,
+                                        int32_t window, vxk_enc_kv_plan * out);
+
+/** Replaces voxtral_enc_kv_mask_allows (src/voxtral.cpp:3636-3638);
+ *  returns 1 when a query at q_abs may attend a key at kv_abs. */
+VXK_API int32_t vxk_enc_kv_mask_allows(int64_t kv_abs, int64_t q_abs, int32_t window);
+
+/* ======================================================================== */
+/* Decoder paged KV pool                                                    */
+/* ======================================================================== */
+
+/** Opaque per-device pool of KV pages shared by many streams. */
+typedef struct vxk_pool vxk_pool;
+
+/**
+ * Pool configuration.  One page ("block") holds block_tokens consecutive
+ * positions of one stream for every layer and kv head.  A stream's logical
+ * position p lives in page block_table[stream][(p / block_tokens) %
+ * (capacity / block_tokens)] at row p % block_tokens, so a stream is a ring of
+ * `capacity` slots exactly like the reference's fixed decoder ring
+ * (src/voxtral.cpp:413-427), with page indirection.
+ */
+typedef struct vxk_pool_config {
+    uint32_t struct_size;
+    uint32_t api_version;
+    int32_t device;
+    int32_t n_layers;       /* 30 (3B offline) or 26 (4B realtime) */
+    int32_t n_q_heads;      /* 32 */
+    int32_t n_kv_heads;     /* 8 */
+    int32_t head_dim;       /* 128 */
+    int32_t block_tokens;   /* 16 */
+    int32_t n_blocks;       /* physical pages in the pool */
+    int32_t capacity;       /* per-stream ring capacity in tokens */
+    int32_t max_streams;
+    int32_t max_rows;       /* max query rows in one planned batch */
+    int32_t max_position;   /* RoPE table rows: every position must be below */
+    vxk_dtype dtype;        /* F16 or Q8_0 */
+    float rope_theta;       /* 1e6 */
+    uint32_t alloc_seed;    /* 0: pages handed out lowest index first; else a
+                               seeded permutation (random block tables) */
+} vxk_pool_config;
+
+/** Defaults: the 4B realtime decoder (26 layers, 32/8 heads x 128, 16-token
+ *  pages, 8192-slot ring, f16, theta 1e6); n_blocks/max_streams sized for one
+ *  stream. */
+VXK_API vxk_pool_config vxk_pool_default_config(void);
+
+/** Allocates the pool on `device` (pages zeroed once, like the reference's
+ *  one-time cache clear at src/voxtral.cpp:1443-1465). */
+VXK_API vxk_status vxk_pool_create(const vxk_pool_config * config, vxk_pool ** out_pool);
+/** Frees the pool.  NULL is safe.  No work may be in flight on it. */
+VXK_API void vxk_pool_destroy(vxk_pool * pool);
+/** Copies the last error message of the pool (or of the last failed create
+ *  when pool is NULL) into buf. */
+VXK_API vxk_status vxk_pool_last_error(const vxk_pool * pool, char * buf, size_t capacity);
+
+/** Pool occupancy counters. */
+typedef struct vxk_pool_stats {
+    int64_t pages_total;
+    int64_t pages_used;
+    int64_t pages_high_water;   /* 1 + highest physical page index in use */
+    int64_t streams_open;
+    int64_t compactions;
+    int64_t pages_moved;
+    int64_t bytes_moved;        /* device bytes copied by compaction */
+    int64_t device_bytes;       /* bytes allocated on the device */
+    int64_t kernel_launches;    /* kernels this pool has launched */
+} vxk_pool_stats;
+
+VXK_API vxk_status vxk_pool_get_stats(const vxk_pool * pool, vxk_pool_stats * out);
+
+/** Opens a stream (an empty ring).  Replaces voxtral_ctx_decoder_begin_incremental
+ *  (src/voxtral.cpp:5489-5496) for one stream. */
+VXK_API vxk_status vxk_stream_open(vxk_pool * pool, int32_t * out_stream);
+/** Closes a stream and returns its pages to the pool. */
+VXK_API vxk_status vxk_stream_close(vxk_pool * pool, int32_t stream);
+/** Logical reset (clear_kv_cache, src/voxtral.cpp:1590-1602): ring back to
+ *  empty, pages returned, no device bytes touched. */
+VXK_API vxk_status vxk_stream_reset(vxk_pool * pool, int32_t stream);
+/** Copies the stream's ring counters (wraps, evictions, bytes_moved ...). */
+VXK_API vxk_status vxk_stream_get_ring(const vxk_pool * pool, int32_t stream,
+                                       vxk_decoder_kv_ring * out);
+/** Window eviction: drops positions below new_oldest (which must lie in
+ *  [oldest, next]); pages whose every slot is dropped go back to the pool.
+ *  Counts the dropped positions as evictions. */
+VXK_API vxk_status vxk_stream_evict(vxk_pool * pool, int32_t stream, int64_t new_oldest);
+
+/**
+ * Plans one batch: stream_ids[i] appends n_new[i] tokens at its next absolute
+ * position (voxtral_decoder_kv_plan per stream, src/voxtral.cpp:5226-5231 and
+ * 5170-5177), allocating pages as needed.  The batch's query rows are the new
+ * tokens in order (stream by stream, position by position); row r of every
+ * per-layer buffer belongs to that token.  Row descriptors and block-table
+ * updates are copied to the device on cuda_stream.  A multi-token append
+ * must not evict (the reference only prefills an empty ring).
+ */
+VXK_API vxk_status vxk_batch_plan(vxk_pool * pool, const int32_t * stream_ids,
+                                  const int32_t * n_new, int32_t n_streams,
+                                  void * cuda_stream);
+/** Number of query rows of the planned batch. */
+VXK_API vxk_status vxk_batch_rows(const vxk_pool * pool, int32_t * out_rows);
+/** Commits every plan of the batch (decoder_kv_commit_plan). */
+VXK_API vxk_status vxk_batch_commit(vxk_pool * pool);
+/** Drops the planned batch without committing. */
+VXK_API vxk_status vxk_batch_abort(vxk_pool * pool);
+
+/**
+ * One decoder layer of a single-token batch (every stream n_new == 1), fused:
+ * rotate and append K/V at the new position, then GQA flash-decoding
+ * attention over the window [oldest_after, position] including the new
+ * token.  Replaces the RoPE + set_rows + flash_attn_ext nodes of
+ * build_decoder_layer (src/voxtral.cpp:2663-2821) on the step graph.
+ *   q   [rows][n_q_heads][head_dim]  fp32, before RoPE
+ *   k,v [rows][n_kv_heads][head_dim] fp32, K before RoPE
+ *   out [rows][n_q_heads][head_dim]  fp32
+ */
+VXK_API vxk_status vxk_decode_layer(vxk_pool * pool, int32_t layer, const float * q,
+                                    const float * k, const float * v, float * out,
+                                    void * cuda_stream);
+
+/** Appends the batch's new tokens to one layer (RoPE on K, f16/q8_0 store);
+ *  replaces src/voxtral.cpp:2663-2714 for prefill / multi-token batches. */
+VXK_API vxk_status vxk_append_layer(vxk_pool * pool, int32_t layer, const float * k,
+                                    const float * v, void * cuda_stream);
+
+/** Causal attention of the batch's query rows over one layer's cache (row at
+ *  position p attends [max(oldest, p - capacity + 1), p]); the prefill form of
+ *  src/voxtral.cpp:2741-2760 with the mask of src/voxtral.cpp:3316-3323. */
+VXK_API vxk_status vxk_attend_layer(vxk_pool * pool, int32_t layer, const float * q,
+                                    float * out, void * cuda_stream);
+
+/**
+ * End-to-end single-token step from HOST buffers: plans stream_ids (n_new 1
+ * each), copies every layer's q/k/v from host memory, runs all layers with
+ * vxk_decode_layer, copies the outputs back, waits and commits.  Host buffers
+ * are layer-major: h_q[layer][row][n_q_heads][head_dim], h_k/h_v
+ * [layer][row][n_kv_heads][head_dim], h_out like h_q.  Pinned host memory
+ * lets the copies overlap the layers.
+ */
+VXK_API vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids,
+                                        int32_t n_streams, const float * h_q,
+                                        const float * h_k, const float * h_v,
+                                        float * h_out, void * cuda_stream);
+
+/** Waits for cuda_stream with a bounded wait (timeout_ms) and reports any
+ *  device-side error flag of the pool's kernels (VXK_STATUS_TIMEOUT or
+ *  VXK_STATUS_BACKEND_ERROR). */
+VXK_API vxk_status vxk_sync(vxk_pool * pool, void * cuda_stream, int32_t timeout_ms);
+
+/** Page compaction: moves every live page above the lowest free pages down,
+ *  rewriting block tables, so that used pages form a prefix of the pool.
+ *  Counts the device bytes copied into the pool's and each moved stream's
+ *  bytes_moved (include/voxtral-stream.h:129-131 metric). */
+VXK_API vxk_status vxk_pool_compact(vxk_pool * pool, void * cuda_stream,
+                                    int64_t * out_pages_moved, int64_t * out_bytes_moved);
+
+/** Reads `n` logical positions [pos_start, pos_start+n) of one stream and
+ *  layer back to host in ggml row layout: f16 rows of n_kv_heads*head_dim
+ *  halves, or q8_0 rows of n_kv_heads*head_dim/32 blocks of 34 bytes
+ *  {f16 d; int8 qs[32]}.  Positions must lie in the stream's window.
+ *  Synchronises cuda_stream. */
+VXK_API vxk_status vxk_read_rows(vxk_pool * pool, int32_t layer, int32_t stream,
+                                 int64_t pos_start, int32_t n, void * k_out, void * v_out,
+                                 void * cuda_stream);
+
+/** Bytes of one ggml-layout row for the pool's dtype. */
+VXK_API int64_t vxk_pool_row_bytes(const vxk_pool * pool);
+
+/* ======================================================================== */
+/* Streaming-encoder windowed attention                                     */
+/* ======================================================================== */
+
+/** Opaque encoder KV rings for many streams on one device. */
+typedef struct vxk_enc_pool vxk_enc_pool;
+
+typedef struct vxk_enc_config {
+    uint32_t struct_size;
+    uint32_t api_version;
+    int32_t device;
+    int32_t n_layers;      /* 32 */
+    int32_t n_heads;       /* 32 in the released model, 20 in the bench */
+    int32_t head_dim;      /* 64 */
+    int32_t window;        /* 750 (VOXTRAL_ENC_WINDOW) */
+    int32_t capacity;      /* 878 (window + max_new) */
+    int32_t max_streams;
+    int32_t max_new;       /* rows per stream per batch, <= capacity - window */
+    int32_t max_position;  /* RoPE table rows */
+    vxk_dtype dtype;       /* BF16 or F16 */
+    float rope_theta;      /* 1e6 */
+    int32_t reserved;
+} vxk_enc_config;
+
+VXK_API vxk_enc_config vxk_enc_default_config(void);
+VXK_API vxk_status vxk_enc_create(const vxk_enc_config * config, vxk_enc_pool ** out);
+VXK_API void vxk_enc_destroy(vxk_enc_pool * pool);
+VXK_API vxk_status vxk_enc_last_error(const vxk_enc_pool * pool, char * buf, size_t capacity);
+VXK_API vxk_status vxk_enc_stream_open(vxk_enc_pool * pool, int32_t * out_stream);
+VXK_API vxk_status vxk_enc_stream_close(vxk_enc_pool * pool, int32_t stream);
+VXK_API vxk_status vxk_enc_stream_reset(vxk_enc_pool * pool, int32_t stream);
+/** Next absolute encoder frame of a stream and its eviction count. */
+VXK_API vxk_status vxk_enc_stream_position(const vxk_enc_pool * pool, int32_t stream,
+                                           int64_t * out_next, int64_t * out_evicted);
+
+/** Plans n_new frames per stream (voxtral_enc_kv_plan per stream,
+ *  src/voxtral.cpp:4072-4120); rows are stream-major like the decoder. */
+VXK_API vxk_status vxk_enc_batch_plan(vxk_enc_pool * pool, const int32_t * stream_ids,
+                                      const int32_t * n_new, int32_t n_streams,
+                                      void * cuda_stream);
+VXK_API vxk_status vxk_enc_batch_rows(const vxk_enc_pool * pool, int32_t * out_rows);
+VXK_API vxk_status vxk_enc_batch_commit(vxk_enc_pool * pool);
+
+/**
+ * One encoder layer: rotate and store the batch's new K (V unrotated) at
+ * slots abs % capacity, then masked attention of every new row over its
+ * window [max(0, q - window + 1), q] (src/voxtral.cpp:2459-2487 with the
+ * mask of src/voxtral.cpp:4104-4119), scale 1/sqrt(head_dim), MHA.
+ *   q, out [rows][n_heads][head_dim] fp32; k, v [rows][n_heads][head_dim].
+ */
+VXK_API vxk_status vxk_enc_layer(vxk_enc_pool * pool, int32_t layer, const float * q,
+                                 const float * k, const float * v, float * out,
+                                 void * cuda_stream);
+
+/** Reads n slots' K/V rows [slot0, slot0+n) of one stream/layer (raw 16-bit
+ *  elements, n_heads*head_dim per row).  Synchronises cuda_stream. */
+VXK_API vxk_status vxk_enc_read_slots(vxk_enc_pool * pool, int32_t layer, int32_t stream,
+                                      int32_t slot0, int32_t n, void * k_out, void * v_out,
+                                      void * cuda_stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* VXK_H */

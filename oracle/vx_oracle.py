@@ -1,0 +1,214 @@
+"""ctypes binding of the CPU oracle (vx_oracle.c / vx_cpu_step.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU legs.  The product (voxtral.cpp_b200/libvxk.so) never uses it.
+See vx_oracle.h for which parts are pinned and which are parity unpinned.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "libvxoracle.so"
+
+F32, F16, Q8_0, BF16 = 0, 1, 8, 30
+
+
+class DecRing(C.Structure):
+    _fields_ = [("capacity", C.c_int64), ("used", C.c_int64), ("oldest", C.c_int64),
+                ("next", C.c_int64), ("wraps", C.c_int64), ("evictions", C.c_int64),
+                ("bytes_moved", C.c_int64), ("full_buffer_moves", C.c_int64)]
+
+
+class Seg(C.Structure):
+    _fields_ = [("slot", C.c_int32), ("len", C.c_int32)]
+
+
+class DecPlan(C.Structure):
+    _fields_ = [("absolute_start", C.c_int64), ("n_new", C.c_int32), ("write_nseg", C.c_int32),
+                ("write_seg", Seg * 2), ("read_seg", Seg * 2), ("read_nseg", C.c_int32),
+                ("wrapped", C.c_int32), ("used_after", C.c_int64), ("oldest_after", C.c_int64),
+                ("next_after", C.c_int64), ("evicted", C.c_int64)]
+
+
+class EncPlan(C.Structure):
+    _fields_ = [("q_start", C.c_int64), ("n_new", C.c_int32), ("win_len", C.c_int32),
+                ("win_start", C.c_int64), ("win_end", C.c_int64), ("read_seg", Seg * 2),
+                ("read_nseg", C.c_int32), ("read_wraps", C.c_int32), ("write_seg", Seg * 2),
+                ("write_nseg", C.c_int32), ("write_wraps", C.c_int32),
+                ("conv_mel_start", C.c_int64), ("conv_mel_end", C.c_int64),
+                ("conv_slice_start", C.c_int32), ("pad_", C.c_int32), ("evicted", C.c_int64)]
+
+
+_lib = None
+
+
+def build() -> Path:
+    res = subprocess.run(["make", "-s", "-C", str(HERE)], capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"oracle build failed:\n{res.stdout}\n{res.stderr}")
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        L = C.CDLL(str(LIB_PATH))
+        P = C.c_void_p
+        L.vxo_dec_kv_plan.restype = C.c_int
+        L.vxo_dec_kv_plan.argtypes = [C.POINTER(DecRing), C.c_int64, C.c_int32, C.POINTER(DecPlan)]
+        L.vxo_dec_kv_commit.argtypes = [C.POINTER(DecRing), C.POINTER(DecPlan)]
+        L.vxo_enc_kv_plan.restype = C.c_int
+        L.vxo_enc_kv_plan.argtypes = [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.POINTER(EncPlan)]
+        L.vxo_enc_kv_mask_allows.restype = C.c_int
+        L.vxo_enc_kv_mask_allows.argtypes = [C.c_int64, C.c_int64, C.c_int32]
+        L.vxo_f32_to_f16.restype = C.c_uint16
+        L.vxo_f32_to_f16.argtypes = [C.c_float]
+        L.vxo_f16_to_f32.restype = C.c_float
+        L.vxo_f16_to_f32.argtypes = [C.c_uint16]
+        L.vxo_f32_to_f16_n.argtypes = [P, P, C.c_int64]
+        L.vxo_f32_to_bf16_n.argtypes = [P, P, C.c_int64]
+        L.vxo_quantize_row_q8_0.argtypes = [P, C.c_int64, P]
+        L.vxo_dequantize_row_q8_0.argtypes = [P, C.c_int64, P]
+        L.vxo_rope_cache.argtypes = [C.c_int64, C.c_int32, C.c_float, P]
+        L.vxo_rope_table.argtypes = [C.c_int64, C.c_int32, C.c_float, P]
+        L.vxo_rope_apply.argtypes = [P, C.c_int32, C.c_int32, C.c_int64, C.c_float, P]
+        L.vxo_row_bytes.restype = C.c_int64
+        L.vxo_row_bytes.argtypes = [C.c_int32, C.c_int32, C.c_int32]
+        L.vxo_kv_row.argtypes = [P, P, C.c_int32, C.c_int32, C.c_int64, C.c_float, C.c_int32, P, P]
+        L.vxo_row_to_f32.argtypes = [P, C.c_int32, C.c_int32, C.c_int32, P]
+        L.vxo_attn_row.argtypes = [P, C.c_int64, C.c_float, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                   P, P, C.c_int32, C.c_int64, C.c_float, P]
+        L.vxo_cpu_decode_step_f16.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int64,
+                                              P, P, P, P, P, P, P, P, C.c_int64, C.c_float, C.c_int32, P]
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+# ---- planners ---------------------------------------------------------------
+
+def dec_plan(ring: DecRing, start: int, n_new: int):
+    p = DecPlan()
+    ok = lib().vxo_dec_kv_plan(C.byref(ring), start, n_new, C.byref(p))
+    return bool(ok), p
+
+
+def dec_commit(ring: DecRing, p: DecPlan):
+    lib().vxo_dec_kv_commit(C.byref(ring), C.byref(p))
+
+
+def enc_plan(q_start: int, n_new: int, capacity: int, window: int):
+    p = EncPlan()
+    ok = lib().vxo_enc_kv_plan(q_start, n_new, capacity, window, C.byref(p))
+    return bool(ok), p
+
+
+def enc_mask_allows(kv: int, q: int, window: int) -> bool:
+    return bool(lib().vxo_enc_kv_mask_allows(kv, q, window))
+
+
+# ---- numerics ---------------------------------------------------------------
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, dtype=np.uint16)
+    lib().vxo_f32_to_f16_n(_ptr(x), _ptr(y), x.size)
+    return y
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, dtype=np.uint16)
+    lib().vxo_f32_to_bf16_n(_ptr(x), _ptr(y), x.size)
+    return y
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """Rows of values (last dim multiple of 32) -> ggml block_q8_0 bytes."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.shape[-1]
+    flat = x.reshape(-1, n)
+    out = np.empty((flat.shape[0], n // 32 * 34), dtype=np.uint8)
+    for i in range(flat.shape[0]):
+        row = np.ascontiguousarray(flat[i])
+        lib().vxo_quantize_row_q8_0(_ptr(row), n, out[i].ctypes.data)
+    return out.reshape(x.shape[:-1] + (n // 32 * 34,))
+
+
+def rope_cache(pos: int, n_dims: int, base: float) -> np.ndarray:
+    cs = np.empty(n_dims, dtype=np.float32)
+    lib().vxo_rope_cache(pos, n_dims, base, _ptr(cs))
+    return cs
+
+
+def rope_table(rows: int, n_dims: int, base: float) -> np.ndarray:
+    t = np.empty((rows, n_dims), dtype=np.float32)
+    lib().vxo_rope_table(rows, n_dims, base, _ptr(t))
+    return t
+
+
+def rope_apply(x: np.ndarray, pos: int, base: float) -> np.ndarray:
+    """x: [n_heads, head_dim] fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().vxo_rope_apply(_ptr(x), x.shape[0], x.shape[1], pos, base, _ptr(y))
+    return y
+
+
+def row_bytes(dtype: int, n_kv: int, head_dim: int) -> int:
+    return int(lib().vxo_row_bytes(dtype, n_kv, head_dim))
+
+
+def kv_row(k: np.ndarray, v: np.ndarray, pos: int, base: float, dtype: int):
+    """k, v: [n_kv, head_dim] fp32 -> stored (K rotated) row bytes in ggml layout."""
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    n_kv, hd = k.shape
+    rb = row_bytes(dtype, n_kv, hd)
+    ko = np.empty(rb, dtype=np.uint8)
+    vo = np.empty(rb, dtype=np.uint8)
+    lib().vxo_kv_row(_ptr(k), _ptr(v), n_kv, hd, pos, base, dtype, _ptr(ko), _ptr(vo))
+    return ko, vo
+
+
+def row_to_f32(row: np.ndarray, dtype: int, n_kv: int, head_dim: int) -> np.ndarray:
+    row = np.ascontiguousarray(row, dtype=np.uint8)
+    out = np.empty(n_kv * head_dim, dtype=np.float32)
+    lib().vxo_row_to_f32(_ptr(row), dtype, n_kv, head_dim, _ptr(out))
+    return out
+
+
+def attn_row(q: np.ndarray, q_pos: int, base: float, k_rows: np.ndarray, v_rows: np.ndarray,
+             dtype: int, n_kv: int, scale: float, rope_q: bool = True) -> np.ndarray:
+    """q: [n_q, hd] fp32 (pre-RoPE when rope_q); k_rows/v_rows: [n_keys, row_bytes] uint8."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k_rows = np.ascontiguousarray(k_rows, dtype=np.uint8)
+    v_rows = np.ascontiguousarray(v_rows, dtype=np.uint8)
+    n_q, hd = q.shape
+    out = np.empty_like(q)
+    lib().vxo_attn_row(_ptr(q), q_pos, base, 1 if rope_q else 0, n_q, n_kv, hd, _ptr(k_rows), _ptr(v_rows),
+                       dtype, k_rows.shape[0], scale, _ptr(out))
+    return out
+
+
+def cpu_decode_step_f16(k_cache, v_cache, q, k, v, pos, win, rope, scale, n_threads):
+    """Timed multi-core CPU step (vx_cpu_step.c); arrays as documented there."""
+    n_streams, n_layers, n_q, hd = q.shape
+    n_kv = k.shape[2]
+    cap = k_cache.shape[-2]
+    out = np.empty_like(q)
+    lib().vxo_cpu_decode_step_f16(n_streams, n_layers, n_q, n_kv, hd, cap, _ptr(k_cache), _ptr(v_cache),
+                                  _ptr(q), _ptr(k), _ptr(v), _ptr(pos), _ptr(win), _ptr(rope), rope.shape[0],
+                                  scale, n_threads, _ptr(out))
+    return out

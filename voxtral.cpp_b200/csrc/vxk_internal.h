@@ -1,0 +1,180 @@
+// Internal declarations shared by the host runtime (vxk_pool.cpp,
+// vxk_encoder_host.cpp) and the sm_100a kernels (vxk_decode.cu,
+// vxk_encoder.cu).  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vxk {
+
+// Decoder kernels are specialised for the Voxtral decoder head shape.
+constexpr int kHeadDim = 128;     // head_dim of both Voxtral decoders
+constexpr int kGroup = 4;         // query heads per kv head (32 / 8)
+constexpr int kBlockTokens = 16;  // positions per page
+constexpr int kQ8Block = 32;      // ggml QK8_0
+
+// Row flag: the fused decode kernel appends this row's K/V before attending.
+constexpr int32_t kRowAppend = 1;
+
+// One query row of a planned batch (one new token of one stream).
+struct RowDesc {
+    int32_t stream;     // pool stream id (block-table row)
+    int32_t pos;        // absolute position of the token
+    int32_t win_start;  // oldest absolute position the row attends
+    int32_t item_base;  // first work item of the row
+    int32_t n_chunks;   // work items (splits) of the row
+    int32_t flags;      // kRowAppend
+    int32_t reserved0;
+    int32_t reserved1;
+};
+static_assert(sizeof(RowDesc) == 32, "RowDesc layout");
+
+// One split of one row: logical pages [page_begin, page_end).
+struct WorkItem {
+    int32_t row;
+    int32_t chunk;
+    int32_t page_begin;
+    int32_t page_end;
+};
+static_assert(sizeof(WorkItem) == 16, "WorkItem layout");
+
+// Block-table update (index into the [max_streams][bt_cap] table, page id).
+struct TableUpdate {
+    int32_t index;
+    int32_t page;
+};
+
+// Partial record of one (work item, query head): acc[head_dim], m, l, pad.
+constexpr int kPartialStride = kHeadDim + 4;
+
+struct DecodeParams {
+    // cache of one layer
+    uint8_t * k_data;        // f16 halves or q8_0 int8 values
+    uint8_t * v_data;
+    uint8_t * k_scale;       // q8_0 f16 scales (nullptr for f16)
+    uint8_t * v_scale;
+    int32_t n_blocks;
+    int32_t n_kv;
+    int32_t n_q;
+    int32_t bt_cap;          // pages per stream ring
+    const int32_t * block_table;
+    const RowDesc * rows;
+    const WorkItem * items;
+    int32_t n_rows;
+    int32_t n_items;
+    const float * q;         // [rows][n_q][head_dim]
+    const float * k;         // [rows][n_kv][head_dim]
+    const float * v;
+    float * out;             // [rows][n_q][head_dim]
+    const float2 * rope;     // [rope_rows][head_dim / 2] (cos, sin)
+    int32_t rope_rows;
+    float scale_log2;        // softmax scale * log2(e)
+    float * partials;        // [n_items][n_q][kPartialStride]
+    int32_t * counters;      // [max_rows][n_kv], zero between launches
+    int32_t * error;         // device error word (0 = ok)
+    int32_t fuse_append;     // 1: rows flagged kRowAppend append first
+    int32_t dtype;           // 1 = f16, 8 = q8_0
+};
+
+struct AppendParams {
+    uint8_t * k_data;
+    uint8_t * v_data;
+    uint8_t * k_scale;
+    uint8_t * v_scale;
+    int32_t n_blocks;
+    int32_t n_kv;
+    int32_t bt_cap;
+    const int32_t * block_table;
+    const RowDesc * rows;
+    int32_t n_rows;
+    const float * k;
+    const float * v;
+    const float2 * rope;
+    int32_t rope_rows;
+    int32_t * error;
+    int32_t dtype;
+};
+
+struct GatherParams {
+    const uint8_t * k_data;
+    const uint8_t * v_data;
+    const uint8_t * k_scale;
+    const uint8_t * v_scale;
+    int32_t n_blocks;
+    int32_t n_kv;
+    int32_t bt_cap;
+    const int32_t * block_table;  // row of one stream
+    int64_t pos_start;
+    int32_t n;
+    uint8_t * k_out;   // f16: [n][n_kv][hd] halves; q8_0: [n][n_kv][hd] int8
+    uint8_t * v_out;
+    uint8_t * k_scale_out;  // q8_0: [n][n_kv][hd/32] f16
+    uint8_t * v_scale_out;
+    int32_t dtype;
+};
+
+struct CompactParams {
+    uint8_t * k_data;           // base of layer 0
+    uint8_t * v_data;
+    uint8_t * k_scale;
+    uint8_t * v_scale;
+    int64_t layer_data_bytes;   // bytes per layer of k_data
+    int64_t layer_scale_bytes;
+    int64_t page_data_bytes;    // bytes per page per layer (all kv heads)
+    int64_t page_scale_bytes;
+    int32_t n_layers;
+    const int2 * moves;         // (src, dst)
+    int32_t n_moves;
+};
+
+cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream);
+cudaError_t launch_append(const AppendParams & p, cudaStream_t stream);
+cudaError_t launch_table_updates(int32_t * table, const TableUpdate * updates, int32_t n,
+                                 cudaStream_t stream);
+cudaError_t launch_gather(const GatherParams & p, cudaStream_t stream);
+cudaError_t launch_compact(const CompactParams & p, cudaStream_t stream);
+
+// Shared-memory bytes the decode kernel needs (for the host's opt-in).
+int decode_smem_bytes(int dtype);
+
+// ---------------------------------------------------------------------------
+// Streaming encoder window attention
+// ---------------------------------------------------------------------------
+
+struct EncRowDesc {
+    int32_t stream;
+    int32_t pos;        // absolute frame of the query row
+    int32_t win_start;  // max(0, pos - window + 1)
+    int32_t slot;       // pos % capacity
+};
+static_assert(sizeof(EncRowDesc) == 16, "EncRowDesc layout");
+
+struct EncParams {
+    uint8_t * k_ring;       // [max_streams][n_layers][n_heads][capacity][head_dim] 16-bit
+    uint8_t * v_ring;
+    int32_t n_layers;
+    int32_t layer;
+    int32_t n_heads;
+    int32_t capacity;
+    int32_t window;
+    const EncRowDesc * rows;
+    int32_t n_rows;
+    const int32_t * group_first;  // first row of each (stream) group
+    int32_t n_groups;
+    const float * q;        // [rows][n_heads][64]
+    const float * k;
+    const float * v;
+    float * out;
+    const float2 * rope;    // [rope_rows][32]
+    int32_t rope_rows;
+    float scale_log2;
+    int32_t * error;
+    int32_t dtype;          // 30 = bf16, 1 = f16
+};
+
+cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream);
+cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream);
+int enc_smem_bytes();
+
+}  // namespace vxk

@@ -1,0 +1,366 @@
+"""ctypes binding of libvxk.so (include/vxk.h) for tests, smoke() and bench.py.
+
+The binding only marshals arguments: every computation happens in libvxk.so.
+Loading fails loudly when the library has not been built; there is no
+fallback path.  Device buffers are passed as integer device addresses
+(e.g. ``tensor.data_ptr()``), streams as integer cudaStream_t handles.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libvxk.so"
+
+STATUS = {
+    0: "ok", 1: "invalid_argument", 2: "invalid_state", 3: "out_of_memory", 5: "not_ready",
+    9: "backend_error", 10: "internal_error", 11: "buffer_too_small", 12: "timeout",
+}
+OK, INVALID_ARGUMENT, INVALID_STATE, OUT_OF_MEMORY = 0, 1, 2, 3
+NOT_READY, BACKEND_ERROR, INTERNAL_ERROR, BUFFER_TOO_SMALL, TIMEOUT = 5, 9, 10, 11, 12
+DTYPE_F16, DTYPE_Q8_0, DTYPE_BF16 = 1, 8, 30
+
+
+class VxkError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+
+
+class DecoderKvRing(C.Structure):
+    _fields_ = [("capacity", C.c_int64), ("used", C.c_int64),
+                ("oldest_absolute_position", C.c_int64), ("next_absolute_position", C.c_int64),
+                ("wraps", C.c_int64), ("evictions", C.c_int64), ("bytes_moved", C.c_int64),
+                ("full_buffer_moves", C.c_int64)]
+
+
+class KvSeg(C.Structure):
+    _fields_ = [("slot", C.c_int32), ("len", C.c_int32)]
+
+
+class DecoderKvPlan(C.Structure):
+    _fields_ = [("absolute_start", C.c_int64), ("n_new", C.c_int32), ("write_nseg", C.c_int32),
+                ("write_seg", KvSeg * 2), ("read_seg", KvSeg * 2), ("read_nseg", C.c_int32),
+                ("wrapped", C.c_int32), ("used_after", C.c_int64), ("oldest_after", C.c_int64),
+                ("next_after", C.c_int64), ("evicted", C.c_int64)]
+
+
+class EncKvPlan(C.Structure):
+    _fields_ = [("q_start", C.c_int64), ("n_new", C.c_int32), ("win_len", C.c_int32),
+                ("win_start", C.c_int64), ("win_end", C.c_int64), ("read_seg", KvSeg * 2),
+                ("read_nseg", C.c_int32), ("read_wraps", C.c_int32), ("write_seg", KvSeg * 2),
+                ("write_nseg", C.c_int32), ("write_wraps", C.c_int32),
+                ("conv_mel_start", C.c_int64), ("conv_mel_end", C.c_int64),
+                ("conv_slice_start", C.c_int32), ("reserved", C.c_int32), ("evicted", C.c_int64)]
+
+
+class PoolConfig(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("device", C.c_int32),
+                ("n_layers", C.c_int32), ("n_q_heads", C.c_int32), ("n_kv_heads", C.c_int32),
+                ("head_dim", C.c_int32), ("block_tokens", C.c_int32), ("n_blocks", C.c_int32),
+                ("capacity", C.c_int32), ("max_streams", C.c_int32), ("max_rows", C.c_int32),
+                ("max_position", C.c_int32), ("dtype", C.c_int32), ("rope_theta", C.c_float),
+                ("alloc_seed", C.c_uint32)]
+
+
+class PoolStats(C.Structure):
+    _fields_ = [("pages_total", C.c_int64), ("pages_used", C.c_int64),
+                ("pages_high_water", C.c_int64), ("streams_open", C.c_int64),
+                ("compactions", C.c_int64), ("pages_moved", C.c_int64),
+                ("bytes_moved", C.c_int64), ("device_bytes", C.c_int64),
+                ("kernel_launches", C.c_int64)]
+
+
+class EncConfig(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("device", C.c_int32),
+                ("n_layers", C.c_int32), ("n_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("window", C.c_int32), ("capacity", C.c_int32), ("max_streams", C.c_int32),
+                ("max_new", C.c_int32), ("max_position", C.c_int32), ("dtype", C.c_int32),
+                ("rope_theta", C.c_float), ("reserved", C.c_int32)]
+
+
+_P = C.c_void_p
+_I32 = C.c_int32
+_I64 = C.c_int64
+_I32P = C.POINTER(C.c_int32)
+_I64P = C.POINTER(C.c_int64)
+
+# name -> (restype, argtypes); every symbol declared in include/vxk.h
+SIGNATURES = {
+    "vxk_status_string": (C.c_char_p, [_I32]),
+    "vxk_api_version": (C.c_uint32, []),
+    "vxk_decoder_kv_plan_make": (_I32, [C.POINTER(DecoderKvRing), _I64, _I32, C.POINTER(DecoderKvPlan)]),
+    "vxk_decoder_kv_plan_commit": (_I32, [C.POINTER(DecoderKvRing), C.POINTER(DecoderKvPlan)]),
+    "vxk_enc_kv_plan_make": (_I32, [_I64, _I32, _I32, _I32, C.POINTER(EncKvPlan)]),
+    "vxk_enc_kv_mask_allows": (_I32, [_I64, _I64, _I32]),
+    "vxk_pool_default_config": (PoolConfig, []),
+    "vxk_pool_create": (_I32, [C.POINTER(PoolConfig), C.POINTER(_P)]),
+    "vxk_pool_destroy": (None, [_P]),
+    "vxk_pool_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_pool_get_stats": (_I32, [_P, C.POINTER(PoolStats)]),
+    "vxk_stream_open": (_I32, [_P, _I32P]),
+    "vxk_stream_close": (_I32, [_P, _I32]),
+    "vxk_stream_reset": (_I32, [_P, _I32]),
+    "vxk_stream_get_ring": (_I32, [_P, _I32, C.POINTER(DecoderKvRing)]),
+    "vxk_stream_evict": (_I32, [_P, _I32, _I64]),
+    "vxk_batch_plan": (_I32, [_P, _I32P, _I32P, _I32, _P]),
+    "vxk_batch_rows": (_I32, [_P, _I32P]),
+    "vxk_batch_commit": (_I32, [_P]),
+    "vxk_batch_abort": (_I32, [_P]),
+    "vxk_decode_layer": (_I32, [_P, _I32, _P, _P, _P, _P, _P]),
+    "vxk_append_layer": (_I32, [_P, _I32, _P, _P, _P]),
+    "vxk_attend_layer": (_I32, [_P, _I32, _P, _P, _P]),
+    "vxk_decode_step_host": (_I32, [_P, _I32P, _I32, _P, _P, _P, _P, _P]),
+    "vxk_sync": (_I32, [_P, _P, _I32]),
+    "vxk_pool_compact": (_I32, [_P, _P, _I64P, _I64P]),
+    "vxk_read_rows": (_I32, [_P, _I32, _I32, _I64, _I32, _P, _P, _P]),
+    "vxk_pool_row_bytes": (_I64, [_P]),
+    "vxk_enc_default_config": (EncConfig, []),
+    "vxk_enc_create": (_I32, [C.POINTER(EncConfig), C.POINTER(_P)]),
+    "vxk_enc_destroy": (None, [_P]),
+    "vxk_enc_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_enc_stream_open": (_I32, [_P, _I32P]),
+    "vxk_enc_stream_close": (_I32, [_P, _I32]),
+    "vxk_enc_stream_reset": (_I32, [_P, _I32]),
+    "vxk_enc_stream_position": (_I32, [_P, _I32, _I64P, _I64P]),
+    "vxk_enc_batch_plan": (_I32, [_P, _I32P, _I32P, _I32, _P]),
+    "vxk_enc_batch_rows": (_I32, [_P, _I32P]),
+    "vxk_enc_batch_commit": (_I32, [_P]),
+    "vxk_enc_layer": (_I32, [_P, _I32, _P, _P, _P, _P, _P]),
+    "vxk_enc_read_slots": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P]),
+}
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Loads libvxk.so; raises if it is missing (build it with build.py)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(f"{p} is not built; run voxtral.cpp_b200/build.py")
+    lib = C.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _i32_array(values):
+    arr = (C.c_int32 * len(values))(*values)
+    return arr
+
+
+class Pool:
+    """Owns one vxk_pool (decoder paged KV cache on one device)."""
+
+    def __init__(self, **cfg):
+        self.lib = load()
+        c = self.lib.vxk_pool_default_config()
+        for k, v in cfg.items():
+            if not hasattr(c, k):
+                raise AttributeError(k)
+            setattr(c, k, v)
+        self.config = c
+        h = C.c_void_p()
+        st = self.lib.vxk_pool_create(C.byref(c), C.byref(h))
+        if st != OK:
+            raise VxkError(st, self.last_error(None))
+        self.h = h
+
+    def last_error(self, handle="self") -> str:
+        buf = C.create_string_buffer(1024)
+        hv = self.h if handle == "self" else handle
+        self.lib.vxk_pool_last_error(hv, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st: int):
+        if st != OK:
+            raise VxkError(st, self.last_error())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_pool_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def open_stream(self) -> int:
+        sid = C.c_int32()
+        self._check(self.lib.vxk_stream_open(self.h, C.byref(sid)))
+        return sid.value
+
+    def close_stream(self, sid: int):
+        self._check(self.lib.vxk_stream_close(self.h, sid))
+
+    def reset_stream(self, sid: int):
+        self._check(self.lib.vxk_stream_reset(self.h, sid))
+
+    def ring(self, sid: int) -> DecoderKvRing:
+        r = DecoderKvRing()
+        self._check(self.lib.vxk_stream_get_ring(self.h, sid, C.byref(r)))
+        return r
+
+    def evict(self, sid: int, new_oldest: int):
+        self._check(self.lib.vxk_stream_evict(self.h, sid, new_oldest))
+
+    def plan(self, stream_ids, n_new, cuda_stream=0) -> int:
+        ids = _i32_array(list(stream_ids))
+        nn = _i32_array(list(n_new))
+        self._check(self.lib.vxk_batch_plan(self.h, ids, nn, len(stream_ids), C.c_void_p(cuda_stream)))
+        rows = C.c_int32()
+        self._check(self.lib.vxk_batch_rows(self.h, C.byref(rows)))
+        return rows.value
+
+    def commit(self):
+        self._check(self.lib.vxk_batch_commit(self.h))
+
+    def abort(self):
+        self._check(self.lib.vxk_batch_abort(self.h))
+
+    def decode_layer(self, layer, q, k, v, out, cuda_stream=0):
+        self._check(self.lib.vxk_decode_layer(self.h, layer, q, k, v, out, C.c_void_p(cuda_stream)))
+
+    def append_layer(self, layer, k, v, cuda_stream=0):
+        self._check(self.lib.vxk_append_layer(self.h, layer, k, v, C.c_void_p(cuda_stream)))
+
+    def attend_layer(self, layer, q, out, cuda_stream=0):
+        self._check(self.lib.vxk_attend_layer(self.h, layer, q, out, C.c_void_p(cuda_stream)))
+
+    def decode_step_host(self, stream_ids, h_q, h_k, h_v, h_out, cuda_stream=0):
+        ids = _i32_array(list(stream_ids))
+        self._check(self.lib.vxk_decode_step_host(self.h, ids, len(stream_ids), h_q, h_k, h_v, h_out,
+                                                  C.c_void_p(cuda_stream)))
+
+    def sync(self, cuda_stream=0, timeout_ms=60000):
+        self._check(self.lib.vxk_sync(self.h, C.c_void_p(cuda_stream), timeout_ms))
+
+    def compact(self, cuda_stream=0):
+        pm, bm = C.c_int64(), C.c_int64()
+        self._check(self.lib.vxk_pool_compact(self.h, C.c_void_p(cuda_stream), C.byref(pm), C.byref(bm)))
+        return pm.value, bm.value
+
+    def stats(self) -> PoolStats:
+        s = PoolStats()
+        self._check(self.lib.vxk_pool_get_stats(self.h, C.byref(s)))
+        return s
+
+    def row_bytes(self) -> int:
+        return int(self.lib.vxk_pool_row_bytes(self.h))
+
+    def read_rows(self, layer, sid, pos_start, n, cuda_stream=0):
+        import numpy as np
+        rb = self.row_bytes()
+        k = np.zeros((n, rb), dtype=np.uint8)
+        v = np.zeros((n, rb), dtype=np.uint8)
+        self._check(self.lib.vxk_read_rows(self.h, layer, sid, pos_start, n, k.ctypes.data, v.ctypes.data,
+                                           C.c_void_p(cuda_stream)))
+        return k, v
+
+
+class EncPool:
+    """Owns one vxk_enc_pool (streaming-encoder KV rings on one device)."""
+
+    def __init__(self, **cfg):
+        self.lib = load()
+        c = self.lib.vxk_enc_default_config()
+        for k, v in cfg.items():
+            if not hasattr(c, k):
+                raise AttributeError(k)
+            setattr(c, k, v)
+        self.config = c
+        h = C.c_void_p()
+        st = self.lib.vxk_enc_create(C.byref(c), C.byref(h))
+        if st != OK:
+            raise VxkError(st, self.last_error(None))
+        self.h = h
+
+    def last_error(self, handle="self") -> str:
+        buf = C.create_string_buffer(1024)
+        hv = self.h if handle == "self" else handle
+        self.lib.vxk_enc_last_error(hv, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st):
+        if st != OK:
+            raise VxkError(st, self.last_error())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_enc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def open_stream(self) -> int:
+        sid = C.c_int32()
+        self._check(self.lib.vxk_enc_stream_open(self.h, C.byref(sid)))
+        return sid.value
+
+    def position(self, sid):
+        nx, ev = C.c_int64(), C.c_int64()
+        self._check(self.lib.vxk_enc_stream_position(self.h, sid, C.byref(nx), C.byref(ev)))
+        return nx.value, ev.value
+
+    def plan(self, stream_ids, n_new, cuda_stream=0) -> int:
+        ids = _i32_array(list(stream_ids))
+        nn = _i32_array(list(n_new))
+        self._check(self.lib.vxk_enc_batch_plan(self.h, ids, nn, len(stream_ids), C.c_void_p(cuda_stream)))
+        rows = C.c_int32()
+        self._check(self.lib.vxk_enc_batch_rows(self.h, C.byref(rows)))
+        return rows.value
+
+    def commit(self):
+        self._check(self.lib.vxk_enc_batch_commit(self.h))
+
+    def layer(self, layer, q, k, v, out, cuda_stream=0):
+        self._check(self.lib.vxk_enc_layer(self.h, layer, q, k, v, out, C.c_void_p(cuda_stream)))
+
+    def read_slots(self, layer, sid, slot0, n, cuda_stream=0):
+        import numpy as np
+        c = self.config
+        k = np.zeros((n, c.n_heads * c.head_dim), dtype=np.uint16)
+        v = np.zeros_like(k)
+        self._check(self.lib.vxk_enc_read_slots(self.h, layer, sid, slot0, n, k.ctypes.data, v.ctypes.data,
+                                                C.c_void_p(cuda_stream)))
+        return k, v
+
+
+# ---- planners (host only) -------------------------------------------------
+
+def decoder_plan(ring: DecoderKvRing, start: int, n_new: int):
+    lib = load()
+    p = DecoderKvPlan()
+    st = lib.vxk_decoder_kv_plan_make(C.byref(ring), start, n_new, C.byref(p))
+    return st, p
+
+
+def decoder_commit(ring: DecoderKvRing, plan: DecoderKvPlan):
+    lib = load()
+    return lib.vxk_decoder_kv_plan_commit(C.byref(ring), C.byref(plan))
+
+
+def enc_plan(q_start: int, n_new: int, capacity: int, window: int):
+    lib = load()
+    p = EncKvPlan()
+    st = lib.vxk_enc_kv_plan_make(q_start, n_new, capacity, window, C.byref(p))
+    return st, p
+
+
+def enc_mask_allows(kv: int, q: int, window: int) -> bool:
+    return bool(load().vxk_enc_kv_mask_allows(kv, q, window))

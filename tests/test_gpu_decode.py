@@ -61,7 +61,7 @@ def test_fused_matches_unfused(vxk, oracle):
 @pytest.mark.parametrize("dtype", [F16, Q8])
 def test_many_streams_random_block_table(vxk, oracle, dtype):
     """Config 2 in miniature: uneven contexts, seeded random page order."""
-    d = Driver(vxk, oracle, seed=2, **_cfg(dtype=dtype, n_blocks=2048, alloc_seed=99))
+    d = Driver(vxk, oracle, seed=2, **_cfg(dtype=dtype, n_blocks=2048, alloc_seed=99, max_rows=2048))
     rng = np.random.default_rng(22)
     streams = [d.open() for _ in range(8)]
     ctx = rng.integers(400, 1200, size=len(streams))
@@ -194,6 +194,47 @@ def test_errors_are_statuses_not_faults(vxk, oracle):
     d.mirror.open(s)
     g, w = d.step([u], [20])
     assert max_err(g, w) <= ATOL
+
+
+@pytest.mark.parametrize("dtype", [F16, Q8])
+def test_back_to_back_layers(vxk, oracle, dtype):
+    """All layers of a step launched back to back with no host sync between
+    them (the decode launches after the first overlap their predecessor)."""
+    import torch
+
+    d = Driver(vxk, oracle, seed=12, **_cfg(n_layers=6, dtype=dtype, n_blocks=2048, max_rows=2048))
+    streams = [d.open() for _ in range(6)]
+    rng = np.random.default_rng(13)
+    for s in streams:
+        d.step([s], [int(rng.integers(300, 1500))], check_layers=[])
+    c = d.pool.config
+    for _ in range(3):
+        n = len(streams)
+        rows = d.pool.plan(streams, [1] * n, d.stream)
+        q = rand(rng, c.n_layers, n, c.n_q_heads, c.head_dim)
+        k = rand(rng, c.n_layers, n, c.n_kv_heads, c.head_dim)
+        v = rand(rng, c.n_layers, n, c.n_kv_heads, c.head_dim)
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        out = torch.full((c.n_layers, n, c.n_q_heads, c.head_dim), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        for layer in range(c.n_layers):
+            d.pool.decode_layer(layer, dq[layer].data_ptr(), dk[layer].data_ptr(), dv[layer].data_ptr(),
+                                out[layer].data_ptr(), d.stream)
+        d.pool.sync(d.stream)
+        d.pool.commit()
+        o = out.cpu().numpy()
+        worst = 0.0
+        for layer in range(c.n_layers):
+            for r, s in enumerate(streams):
+                pos = d.mirror.next[s]
+                d.mirror.append(s, layer, pos, k[layer, r], v[layer, r])
+                want = d.mirror.attend(s, layer, pos, max(0, pos - c.capacity + 1), q[layer, r])
+                worst = max(worst, float(np.max(np.abs(o[layer, r] - want))))
+        for s in streams:
+            d.mirror.advance(s, 1)
+        assert rows == n and worst <= ATOL
+    for s in streams[:2]:
+        d.check_cache(s)
 
 
 def test_end_to_end_host_step_matches_device_path(vxk, oracle):

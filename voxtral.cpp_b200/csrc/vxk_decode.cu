@@ -8,9 +8,23 @@
 //   table_update_kernel, gather_kernel, compact_kernel: block-table upkeep,
 //                   readback and page compaction.
 //
-// Cache layout (per layer): page-major [n_blocks][n_kv][16 tokens][128] so one
-// (page, kv head) tile is a contiguous 4 KiB (f16) or 2 KiB + 128 B (q8_0)
-// region that one cp.async.bulk copies into shared memory.
+// Cache layout (per layer): page-major [n_blocks][n_kv][tile], one tile = the
+// 16 positions of one page for one kv head, stored contiguously so a single
+// cp.async.bulk brings it into shared memory:
+//   f16  tile: 16 rows x 256 B; the 16-byte chunk c of row r is stored at
+//        chunk position c ^ (r & 7)  (4096 B)
+//   q8_0 tile: 16 rows x 128 B int8 values, chunk c of row r at c ^ (r & 7)
+//        (2048 B), then the ggml block scales as f16 [4 blocks][16 rows]
+//        (128 B) in a parallel array.
+// The XOR swizzle makes the ldmatrix reads of the tensor-core tiles
+// bank-conflict free without any shared-memory re-layout.
+//
+// The attention inner products run on the tensor cores with mma.sync
+// m16n8k16 (f16 inputs, fp32 accumulation):
+//   S^T[head][token] = Q[head][dim] . K^T      (A = Q, 4 real rows of 16)
+//   O^T[dim][head]  += V^T[dim][token] . P^T   (B = P, 4 real columns of 8)
+// q8_0 tiles are widened to f16 exactly in registers (int8 -> f16 magic
+// numbers) and their ggml block scales are applied per 32-value block.
 #include "vxk_internal.h"
 
 #include <cuda_fp16.h>
@@ -19,46 +33,55 @@
 namespace vxk {
 namespace {
 
-constexpr int NT = 128;            // threads per CTA
-constexpr int kStages = 8;         // bulk-copy ring depth
-constexpr int kGroupPages = 16;    // pages whose scores are held at once
-constexpr int kGroupTokens = kGroupPages * kBlockTokens;
+constexpr int NT = 128;            // threads per CTA (4 warps)
+constexpr int kWarps = NT / 32;
 constexpr int kMaxChunkPages = 128;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier wait: 2 s
 
 constexpr int kErrBadPage = 1;
 constexpr int kErrTimeout = 2;
+constexpr unsigned kFull = 0xffffffffu;
 
-template <int DT> struct Fmt;
-template <> struct Fmt<1> {
-    static constexpr int kData = kBlockTokens * kHeadDim * 2;  // 4096
-    static constexpr int kStage = kData;
+template <int DT> struct Cfg;
+template <> struct Cfg<1> {
+    static constexpr int kTile = kBlockTokens * kHeadDim * 2;   // 4096
+    static constexpr int kScale = 0;
+    static constexpr int kStages = 3;                            // per warp
 };
-template <> struct Fmt<8> {
-    static constexpr int kData = kBlockTokens * kHeadDim;                       // 2048
-    static constexpr int kScale = kBlockTokens * (kHeadDim / kQ8Block) * 2;     // 128
-    static constexpr int kStage = kData + kScale;                               // 2176
+template <> struct Cfg<8> {
+    static constexpr int kTile = kBlockTokens * kHeadDim;       // 2048
+    static constexpr int kScale = kBlockTokens * (kHeadDim / kQ8Block) * 2;  // 128
+    static constexpr int kStages = 5;
 };
+template <int DT>
+__host__ __device__ constexpr int stage_bytes() { return 2 * (Cfg<DT>::kTile + Cfg<DT>::kScale); }
 
 template <int DT>
 struct __align__(128) Smem {
-    uint8_t stage[kStages][Fmt<DT>::kStage];
-    uint64_t full[kStages];
-    float scores[kGroupTokens * kGroup];     // also the combine weights
-    uint8_t newk[kHeadDim * 2];
+    uint8_t stage[kWarps][Cfg<DT>::kStages][stage_bytes<DT>()];  // [K tile|K scales|V tile|V scales]
+    uint64_t full[kWarps][Cfg<DT>::kStages];
+    float merge[kWarps * kGroup * kHeadDim];  // per-warp O^T, then split-combine weights
+    uint8_t newk[kHeadDim * 2];      // appended row, plain order
     uint8_t newv[kHeadDim * 2];
     uint16_t newk_scale[kHeadDim / kQ8Block];
     uint16_t newv_scale[kHeadDim / kQ8Block];
-    int32_t pages[kMaxChunkPages];
-    float red_m[NT / 32][kGroup];
-    float red_l[NT / 32][kGroup];
-    float comb_m[kGroup];
-    float comb_l[kGroup];
+    float wm[kWarps][kGroup];        // per-warp running max / sum
+    float wl[kWarps][kGroup];
+    float red_m[kWarps][kGroup];     // combine reductions
+    float red_l[kWarps][kGroup];
     int32_t abort_flag;
     int32_t last_flag;
 };
-static_assert(sizeof(float) * 8 * kGroup * kHeadDim <= sizeof(uint8_t) * kStages * Fmt<8>::kStage,
-              "acc reduction buffer must fit in the stage ring");
+static_assert(256 * kGroup <= kWarps * kGroup * kHeadDim, "combine weights fit in the merge buffer");
+
+// Issue-side view of one work unit for one warp: pages of the split, kv head,
+// and (per lane j) the page ids of the warp's pages j, j+32, j+64, j+96.
+struct IssueUnit {
+    int npages;
+    int kvh;
+    int pid[4];
+};
+static_assert(kMaxSplitPages <= kWarps * 4 * 32, "page ids per lane cover the largest split");
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -71,8 +94,7 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-                 : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void mbar_fence_init() {
@@ -80,8 +102,7 @@ __device__ __forceinline__ void mbar_fence_init() {
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
 
@@ -107,10 +128,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, uint6
     }
 }
 
-// 1-D bulk copy global -> shared, completion counted on an mbarrier.  The
-// K/V stream is read once per launch, so it is marked evict-first in L2.
-__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes,
-                                         uint64_t * bar, uint64_t policy) {
+// 1-D bulk copy global -> shared (no multicast), completion counted on an
+// mbarrier.  The K/V stream is read once per launch: evict-first in L2.
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar,
+                                         uint64_t policy) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
         "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
@@ -124,24 +145,39 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
     return policy;
 }
 
-__device__ __forceinline__ void h8_to_f8(const uint4 & u, float * f) {
-    const __half2 * h = reinterpret_cast<const __half2 *>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = __half22float2(h[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2,
+                                        uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
 }
 
-// Exact int8 -> fp32 for the 4 signed bytes of a word: bias to unsigned,
-// splice under the exponent of 2^23, subtract (2^23 + 128).
-__device__ __forceinline__ void s8x4_to_f4(uint32_t w, float * f) {
-    const uint32_t u = w ^ 0x80808080u;
-    f[0] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)) - 8388736.0f;
-    f[1] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541u)) - 8388736.0f;
-    f[2] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7542u)) - 8388736.0f;
-    f[3] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543u)) - 8388736.0f;
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2,
+                                          uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// D += A(16x16 f16, row) * B(16x8 f16, col), fp32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// Exact int8 -> f16 pairs: bias the bytes to unsigned, splice them under the
+// f16 exponent of 1024 (0x64), subtract 1024 + 128.  `sel` picks the two
+// bytes (byte_perm selector with 4 = the 0x64 filler).
+__device__ __forceinline__ uint32_t s8pair_to_h2(uint32_t biased, uint32_t sel) {
+    const uint32_t h = __byte_perm(biased, 0x64646464u, sel);
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&h), __half2half2(__ushort_as_half(0x6480)));
+    return h2_bits(r);
 }
 
 // RoPE mode 0 on one adjacent pair, each product and sum rounded on its own
@@ -157,13 +193,17 @@ __device__ __forceinline__ void set_error(int32_t * err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// Byte offset of element pair / chunk inside a swizzled tile row.
+__device__ __forceinline__ int f16_chunk_off(int row, int chunk) { return row * 256 + ((chunk ^ (row & 7)) << 4); }
+__device__ __forceinline__ int q8_chunk_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+
 // ggml quantize_row_q8_0_ref on one 32-value block held as 16 pairs by 16
 // consecutive lanes (lane group aligned to 16): d = amax/127,
 // id = d ? 1/d : 0, q = roundf(x*id).
 __device__ __forceinline__ void q8_pair(float2 x, char2 & q, float & d) {
     float a = fmaxf(fabsf(x.x), fabsf(x.y));
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    for (int o = 1; o < 16; o <<= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, o));
     d = __fdiv_rn(a, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     q.x = static_cast<signed char>(static_cast<int>(roundf(__fmul_rn(x.x, id))));
@@ -171,474 +211,495 @@ __device__ __forceinline__ void q8_pair(float2 x, char2 & q, float & d) {
 }
 
 // Appends one (token, kv head) row with 128 threads: threads 0-63 rotate and
-// store K pairs, threads 64-127 store V pairs.  Writes the stored values also
-// to shared memory (newk/newv) when smem pointers are given.
+// store K pairs, threads 64-127 store V pairs, into the swizzled tile.  The
+// stored values are also written, in plain order, to shared memory when sk is
+// given (the fused decode patches them into its copy of the tile).
 template <int DT>
-__device__ __forceinline__ void append_head_row(const float * k, const float * v,
-                                                const float2 * cs, uint8_t * k_data,
-                                                uint8_t * v_data, uint8_t * k_scale,
-                                                uint8_t * v_scale, int64_t tile, int tok,
-                                                uint8_t * sk, uint8_t * sv, uint16_t * sks,
-                                                uint16_t * svs) {
+__device__ __forceinline__ void append_head_row(const float * k, const float * v, const float2 * cs,
+                                                uint8_t * k_data, uint8_t * v_data, uint8_t * k_scale,
+                                                uint8_t * v_scale, int64_t tile, int tok, uint8_t * sk,
+                                                uint8_t * sv, uint16_t * sks, uint16_t * svs) {
     const int tid = threadIdx.x;
     const bool is_k = tid < 64;
-    const int i = is_k ? tid : tid - 64;  // pair index 0..63
+    const int i = is_k ? tid : tid - 64;  // pair index 0..63 (dims 2i, 2i+1)
     float2 x = reinterpret_cast<const float2 *>(is_k ? k : v)[i];
     if (is_k) x = rope_pair(x, cs[i]);
     if constexpr (DT == 1) {
         const __half2 h = __floats2half2_rn(x.x, x.y);
-        uint8_t * base = (is_k ? k_data : v_data) + (tile * kBlockTokens + tok) * (kHeadDim * 2);
-        reinterpret_cast<__half2 *>(base)[i] = h;
+        uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<1>::kTile;
+        *reinterpret_cast<__half2 *>(t + f16_chunk_off(tok, i >> 2) + (i & 3) * 4) = h;
         if (sk) reinterpret_cast<__half2 *>(is_k ? sk : sv)[i] = h;
     } else {
         char2 q;
         float d;
         q8_pair(x, q, d);
-        uint8_t * base = (is_k ? k_data : v_data) + (tile * kBlockTokens + tok) * kHeadDim;
-        reinterpret_cast<char2 *>(base)[i] = q;
+        uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<8>::kTile;
+        *reinterpret_cast<char2 *>(t + q8_chunk_off(tok, i >> 3) + (i & 7) * 2) = q;
         if (sk) reinterpret_cast<char2 *>(is_k ? sk : sv)[i] = q;
         if ((i & 15) == 0) {
             const __half dh = __float2half_rn(d);
             const int blk = i >> 4;
-            uint8_t * sb = (is_k ? k_scale : v_scale) +
-                           (tile * kBlockTokens + tok) * (kHeadDim / kQ8Block) * 2;
-            reinterpret_cast<__half *>(sb)[blk] = dh;
+            uint8_t * sb = (is_k ? k_scale : v_scale) + tile * Cfg<8>::kScale;
+            reinterpret_cast<__half *>(sb)[blk * kBlockTokens + tok] = dh;
             if (sks) (is_k ? sks : svs)[blk] = __half_as_ushort(dh);
         }
     }
 }
 
-// Query dims owned by lane j (0..7) of a token group, slot s (0..15).
+// Persistent flash-decoding kernel.  Grid = one CTA per resident slot; CTA b
+// processes the work units (split, kv head) the host scheduled for it
+// (sched_units[sched_offsets[b] .. sched_offsets[b+1]), longest-first greedy),
+// one unit after the other.  Each warp streams its share of every unit's
+// pages (pages warp, warp+4, ...) through its own ring of ST stages; the ring
+// runs ahead across unit boundaries, so the next unit's pages are already in
+// flight while the CTA merges and writes the current one.
 template <int DT>
-__device__ __forceinline__ int q_dim(int j, int s) {
-    if constexpr (DT == 1) {
-        return (s < 8) ? 8 * j + s : 64 + 8 * j + (s - 8);
-    } else {
-        return 16 * j + s;
-    }
-}
-
-// Reduce-scatter of 4 per-head partial dot products across the 8 lanes of a
-// token group: returns the full sum of head hsel(j) = 2*bit2(j) + bit1(j).
-__device__ __forceinline__ float reduce_scatter4(const float s[4], int j) {
-    const bool hi2 = (j & 4) != 0;
-    float k0 = hi2 ? s[2] : s[0];
-    float k1 = hi2 ? s[3] : s[1];
-    const float o0 = hi2 ? s[0] : s[2];
-    const float o1 = hi2 ? s[1] : s[3];
-    k0 += __shfl_xor_sync(0xffffffffu, o0, 4);
-    k1 += __shfl_xor_sync(0xffffffffu, o1, 4);
-    const bool hi1 = (j & 2) != 0;
-    float r = hi1 ? k1 : k0;
-    const float o = hi1 ? k0 : k1;
-    r += __shfl_xor_sync(0xffffffffu, o, 2);
-    r += __shfl_xor_sync(0xffffffffu, r, 1);
-    return r;
-}
-
-template <int DT>
-__global__ void __launch_bounds__(NT, 4) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem<DT> & S = *reinterpret_cast<Smem<DT> *>(smem_raw);
+    constexpr int ST = Cfg<DT>::kStages;
+    constexpr int TILE = Cfg<DT>::kTile;
+    constexpr int SCALE = Cfg<DT>::kScale;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const int kvh = blockIdx.x % p.n_kv;
-    const int item_idx = blockIdx.x / p.n_kv;
-    if (item_idx >= p.n_items) return;
-    const WorkItem it = p.items[item_idx];
-    const RowDesc rd = p.rows[it.row];
-    const int last_page = rd.pos / kBlockTokens;
-    const int n_pages = it.page_end - it.page_begin;
-    const bool do_append =
-        p.fuse_append && (rd.flags & kRowAppend) && (it.page_end - 1 == last_page);
-    const int64_t kv_stride_tiles = p.n_kv;
+    const int g = lane >> 2;     // mma group: head (QK rows) / dim (PV rows)
+    const int c = lane & 3;      // mma thread-in-group: token pair / head pair
+    const bool real = lane < 16; // lanes whose QK rows are real heads 0..3
+    const int u0 = p.sched_offsets[blockIdx.x];
+    const int nu = p.sched_offsets[blockIdx.x + 1] - u0;
 
-    for (int i = tid; i < n_pages; i += NT) {
-        const int lp = it.page_begin + i;
-        int pg = p.block_table[(int64_t) rd.stream * p.bt_cap + (lp % p.bt_cap)];
-        if (pg < 0 || pg >= p.n_blocks) {
-            set_error(p.error, kErrBadPage);
-            pg = 0;
-        }
-        S.pages[i] = pg;
-    }
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&S.full[s], 1);
+        for (int w = 0; w < kWarps; ++w)
+            for (int s = 0; s < ST; ++s) mbar_init(&S.full[w][s], 1);
         S.abort_flag = 0;
         mbar_fence_init();
     }
     __syncthreads();
 
-    const int total = 2 * n_pages;
+    // ---- issue side (per warp, warp-uniform control, lane 0 copies) ---------
     const uint64_t policy = evict_first_policy();
-    int issued = 0;  // meaningful in thread 0 only
-    auto issue = [&](int L) {
-        const int gi = L / (2 * kGroupPages);
-        const int base = gi * 2 * kGroupPages;
-        const int np = min(kGroupPages, n_pages - gi * kGroupPages);
-        const int r = L - base;
-        const bool is_v = r >= np;
-        const int pi = is_v ? r - np : r;
-        const int64_t tile = (int64_t) S.pages[gi * kGroupPages + pi] * kv_stride_tiles + kvh;
-        const int st = L % kStages;
-        uint64_t * bar = &S.full[st];
-        if constexpr (DT == 1) {
-            mbar_expect_tx(bar, Fmt<1>::kData);
-            bulk_g2s(S.stage[st], (is_v ? p.v_data : p.k_data) + tile * Fmt<1>::kData,
-                     Fmt<1>::kData, bar, policy);
-        } else {
-            mbar_expect_tx(bar, Fmt<8>::kData + Fmt<8>::kScale);
-            bulk_g2s(S.stage[st], (is_v ? p.v_data : p.k_data) + tile * Fmt<8>::kData,
-                     Fmt<8>::kData, bar, policy);
-            bulk_g2s(S.stage[st] + Fmt<8>::kData,
-                     (is_v ? p.v_scale : p.k_scale) + tile * Fmt<8>::kScale, Fmt<8>::kScale,
-                     bar, policy);
+    auto share_of = [&](int npages) { return npages > warp ? (npages - warp + kWarps - 1) / kWarps : 0; };
+    // Descriptor of unit k for the issuing warp; lane j also fetches the page
+    // ids of the warp's pages j + 32 r of that unit (splits <= kMaxSplitPages).
+    auto fetch = [&](int k) -> IssueUnit {
+        IssueUnit r{0, 0, {0, 0, 0, 0}};
+        if (k >= nu) return r;
+        const int uid = p.sched_units[u0 + k];
+        const WorkItem it = p.items[uid / p.n_kv];
+        const int stream = p.rows[it.row].stream;
+        r.kvh = uid % p.n_kv;
+        r.npages = it.page_end - it.page_begin;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int pi = warp + kWarps * (lane + 32 * j);
+            if (pi < r.npages) {
+                const int lp = it.page_begin + pi;
+                int pg = p.block_table[(int64_t) stream * p.bt_cap + (lp % p.bt_cap)];
+                if (pg < 0 || pg >= p.n_blocks) {
+                    set_error(p.error, kErrBadPage);
+                    pg = 0;
+                }
+                r.pid[j] = pg;
+            }
+        }
+        return r;
+    };
+    IssueUnit cur = fetch(0);
+    IssueUnit nxt = fetch(1);
+    int iu = 0, ipi = 0, seq_issued = 0;
+    auto pump = [&](int seq_consumed) {
+        while (iu < nu && seq_issued - seq_consumed < ST) {
+            if (ipi >= share_of(cur.npages)) {
+                ++iu;
+                ipi = 0;
+                cur = nxt;
+                nxt = fetch(iu + 1);
+                continue;
+            }
+            const int hi = ipi >> 5;
+            const int reg = hi == 0 ? cur.pid[0] : hi == 1 ? cur.pid[1] : hi == 2 ? cur.pid[2] : cur.pid[3];
+            const int pg = __shfl_sync(kFull, reg, ipi & 31);
+            if (lane == 0) {
+                const int st = seq_issued % ST;
+                const int64_t tile = (int64_t) pg * p.n_kv + cur.kvh;
+                uint64_t * bar = &S.full[warp][st];
+                uint8_t * dst = S.stage[warp][st];
+                mbar_expect_tx(bar, stage_bytes<DT>());
+                bulk_g2s(dst, p.k_data + tile * TILE, TILE, bar, policy);
+                bulk_g2s(dst + TILE + SCALE, p.v_data + tile * TILE, TILE, bar, policy);
+                if constexpr (SCALE > 0) {
+                    bulk_g2s(dst + TILE, p.k_scale + tile * SCALE, SCALE, bar, policy);
+                    bulk_g2s(dst + 2 * TILE + SCALE, p.v_scale + tile * SCALE, SCALE, bar, policy);
+                }
+            }
+            ++seq_issued;
+            ++ipi;
         }
     };
-    if (tid == 0) {
-        const int n0 = min(kStages, total);
-        for (int L = 0; L < n0; ++L) issue(L);
-        issued = n0;
-    }
+    pump(0);
+    // Programmatic dependent launch: let the next launch on the stream start
+    // its prologue (descriptors, block table, first page copies) while this
+    // grid drains, and wait for the previous grid only now, before reading
+    // the layer inputs (q/k/v) or touching the split scratch.  Both are
+    // no-ops for a launch without the programmatic-serialization attribute.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // Query prologue: rotate this lane's 16 dims of the group's 4 heads and
-    // fold in scale*log2(e).
-    const int t = tid >> 3;   // token in page (QK phase)
-    const int j = tid & 7;    // lane in token group
-    float qv[kGroup][16];
-    {
-        const float * qrow = p.q + ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup) * kHeadDim;
-        const float2 * cs = p.rope + (int64_t) rd.pos * (kHeadDim / 2);
-#pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
-#pragma unroll
-            for (int s = 0; s < 16; s += 2) {
-                const int d = q_dim<DT>(j, s);
-                const float2 x = *reinterpret_cast<const float2 *>(qrow + g * kHeadDim + d);
-                const float2 r = rope_pair(x, cs[d >> 1]);
-                qv[g][s] = r.x * p.scale_log2;
-                qv[g][s + 1] = r.y * p.scale_log2;
-            }
-        }
-    }
-    if (do_append) {
-        const int tok = rd.pos % kBlockTokens;
-        const int64_t tile = (int64_t) S.pages[n_pages - 1] * kv_stride_tiles + kvh;
-        const int64_t krow = ((int64_t) it.row * p.n_kv + kvh) * kHeadDim;
-        append_head_row<DT>(p.k + krow, p.v + krow, p.rope + (int64_t) rd.pos * (kHeadDim / 2),
-                            p.k_data, p.v_data, p.k_scale, p.v_scale, tile, tok, S.newk,
-                            S.newv, S.newk_scale, S.newv_scale);
-    }
-    __syncthreads();
+    const int mi = lane >> 3;    // ldmatrix: matrix index of this lane's row address
+    const int mrow = lane & 7;   //           row within that matrix
+    int seq_consumed = 0;
+    for (int k = 0; k < nu; ++k) {
+        const int uid = p.sched_units[u0 + k];
+        const int item_idx = uid / p.n_kv;
+        const int kvh = uid % p.n_kv;
+        const WorkItem it = p.items[item_idx];
+        const RowDesc rd = p.rows[it.row];
+        const int last_page = rd.pos / kBlockTokens;
+        const int n_pages = it.page_end - it.page_begin;
+        const bool do_append = p.fuse_append && (rd.flags & kRowAppend) && (it.page_end - 1 == last_page);
+        pump(seq_consumed);
 
-    float m_run[kGroup], l_run[kGroup];
-    float acc[kGroup][8];
-#pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-        m_run[g] = -INFINITY;
-        l_run[g] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[g][i] = 0.0f;
-    }
-    const int g8 = tid >> 4;   // token pair (PV phase)
-    const int j16 = tid & 15;  // 8-dim slice (PV phase)
-    const int n_groups = (n_pages + kGroupPages - 1) / kGroupPages;
-    bool aborted = false;
-    int L = 0;
-
-    for (int gi = 0; gi < n_groups && !aborted; ++gi) {
-        const int np = min(kGroupPages, n_pages - gi * kGroupPages);
-        // ---- K phase: scores of the group's tokens --------------------------
-        for (int pi = 0; pi < np; ++pi, ++L) {
-            const int st = L % kStages;
-            if (!mbar_wait(&S.full[st], (L / kStages) & 1, kWaitNs)) S.abort_flag = 1;
-            const int lp = it.page_begin + gi * kGroupPages + pi;
-            const bool patch = do_append && lp == last_page && t == rd.pos % kBlockTokens;
-            float s[kGroup];
-            if constexpr (DT == 1) {
-                const uint8_t * row = S.stage[st] + t * (kHeadDim * 2);
-                uint4 a = *reinterpret_cast<const uint4 *>(row + 16 * j);
-                uint4 b = *reinterpret_cast<const uint4 *>(row + 128 + 16 * j);
-                if (patch) {
-                    a = *reinterpret_cast<const uint4 *>(S.newk + 16 * j);
-                    b = *reinterpret_cast<const uint4 *>(S.newk + 128 + 16 * j);
-                }
-                float kf[16];
-                h8_to_f8(a, kf);
-                h8_to_f8(b, kf + 8);
-#pragma unroll
-                for (int g = 0; g < kGroup; ++g) {
-                    float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        s0 = fmaf(qv[g][i], kf[i], s0);
-                        s1 = fmaf(qv[g][8 + i], kf[8 + i], s1);
-                    }
-                    s[g] = s0 + s1;
-                }
-            } else {
-                const uint8_t * row = S.stage[st] + t * kHeadDim;
-                uint4 a = *reinterpret_cast<const uint4 *>(row + 16 * j);
-                const uint16_t * sc = reinterpret_cast<const uint16_t *>(S.stage[st] + Fmt<8>::kData);
-                uint16_t dbits = sc[t * (kHeadDim / kQ8Block) + (j >> 1)];
-                if (patch) {
-                    a = *reinterpret_cast<const uint4 *>(S.newk + 16 * j);
-                    dbits = S.newk_scale[j >> 1];
-                }
-                const float d = __half2float(__ushort_as_half(dbits));
-                float kf[16];
-                s8x4_to_f4(a.x, kf);
-                s8x4_to_f4(a.y, kf + 4);
-                s8x4_to_f4(a.z, kf + 8);
-                s8x4_to_f4(a.w, kf + 12);
-#pragma unroll
-                for (int g = 0; g < kGroup; ++g) {
-                    float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        s0 = fmaf(qv[g][i], kf[i], s0);
-                        s1 = fmaf(qv[g][8 + i], kf[8 + i], s1);
-                    }
-                    s[g] = (s0 + s1) * d;
-                }
-            }
-            const float tot = reduce_scatter4(s, j);
-            if ((j & 1) == 0) {
-                const int h = ((j >> 2) & 1) * 2 + ((j >> 1) & 1);
-                const int tp = lp * kBlockTokens + t;
-                const bool valid = tp >= rd.win_start && tp <= rd.pos;
-                S.scores[(pi * kBlockTokens + t) * kGroup + h] = valid ? tot : -INFINITY;
-            }
-            __syncthreads();
-            if (S.abort_flag) {
-                aborted = true;
-                break;
-            }
-            if (tid == 0 && issued < total) issue(issued++);
-        }
-        if (aborted) break;
-
-        // ---- softmax of the group (log2 domain), merged into the run -------
+        // Query fragments (A operand rows = heads; lanes 16-31 hold zero rows).
+        // f16: a0 = dims 16ks+2c,+1 and a2 = dims 16ks+8+2c,+1 (mma k order);
+        // q8_0: a0 = dims 16ks+4c,+1 and a2 = dims 16ks+4c+2,+3, the k order the
+        // int8 ldmatrix delivers.  Scale*log2(e) is folded in.
+        uint32_t qa[8][2];
         {
-            const int n_tok = np * kBlockTokens;
-            const int h = tid & 3;
-            float lm = -INFINITY;
-            for (int k2 = tid >> 2; k2 < n_tok; k2 += NT / 4) lm = fmaxf(lm, S.scores[k2 * kGroup + h]);
-            lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 4));
-            lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 8));
-            lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 16));
-            if (lane < 4) S.red_m[warp][lane] = lm;
-            __syncthreads();
-            float m_new[kGroup];
+            const float * qrow = p.q + ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup + (g & 3)) * kHeadDim;
+            const float2 * cs = p.rope + (int64_t) rd.pos * (kHeadDim / 2);
 #pragma unroll
-            for (int g = 0; g < kGroup; ++g) {
-                float mg = S.red_m[0][g];
-#pragma unroll
-                for (int w = 1; w < NT / 32; ++w) mg = fmaxf(mg, S.red_m[w][g]);
-                m_new[g] = fmaxf(m_run[g], mg);
-            }
-            const float mh = h == 0 ? m_new[0] : h == 1 ? m_new[1] : h == 2 ? m_new[2] : m_new[3];
-            float ls = 0.0f;
-            for (int k2 = tid >> 2; k2 < n_tok; k2 += NT / 4) {
-                const float e = exp2f(S.scores[k2 * kGroup + h] - mh);
-                S.scores[k2 * kGroup + h] = e;
-                ls += e;
-            }
-            ls += __shfl_xor_sync(0xffffffffu, ls, 4);
-            ls += __shfl_xor_sync(0xffffffffu, ls, 8);
-            ls += __shfl_xor_sync(0xffffffffu, ls, 16);
-            if (lane < 4) S.red_l[warp][lane] = ls;
-            __syncthreads();
-#pragma unroll
-            for (int g = 0; g < kGroup; ++g) {
-                float lg = 0.0f;
-#pragma unroll
-                for (int w = 0; w < NT / 32; ++w) lg += S.red_l[w][g];
-                const float alpha = exp2f(m_run[g] - m_new[g]);
-                l_run[g] = l_run[g] * alpha + lg;
-                m_run[g] = m_new[g];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[g][i] *= alpha;
+            for (int ks = 0; ks < 8; ++ks) {
+                const int d0 = DT == 1 ? 16 * ks + 2 * c : 16 * ks + 4 * c;
+                const int d1 = DT == 1 ? 16 * ks + 8 + 2 * c : 16 * ks + 4 * c + 2;
+                uint32_t v0 = 0, v1 = 0;
+                if (real) {
+                    const float2 r0 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d0), cs[d0 >> 1]);
+                    const float2 r1 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d1), cs[d1 >> 1]);
+                    v0 = h2_bits(__floats2half2_rn(r0.x * p.scale_log2, r0.y * p.scale_log2));
+                    v1 = h2_bits(__floats2half2_rn(r1.x * p.scale_log2, r1.y * p.scale_log2));
+                }
+                qa[ks][0] = v0;
+                qa[ks][1] = v1;
             }
         }
+        if (do_append) {
+            const int lp = last_page;
+            int pg = p.block_table[(int64_t) rd.stream * p.bt_cap + (lp % p.bt_cap)];
+            if (pg < 0 || pg >= p.n_blocks) {
+                set_error(p.error, kErrBadPage);
+                pg = 0;
+            }
+            const int64_t tile = (int64_t) pg * p.n_kv + kvh;
+            const int64_t krow = ((int64_t) it.row * p.n_kv + kvh) * kHeadDim;
+            append_head_row<DT>(p.k + krow, p.v + krow, p.rope + (int64_t) rd.pos * (kHeadDim / 2), p.k_data,
+                                p.v_data, p.k_scale, p.v_scale, tile, rd.pos % kBlockTokens, S.newk, S.newv,
+                                S.newk_scale, S.newv_scale);
+        }
+        __syncthreads();
 
-        // ---- V phase: acc += p * V ----------------------------------------
-        for (int pi = 0; pi < np; ++pi, ++L) {
-            const int st = L % kStages;
-            if (!mbar_wait(&S.full[st], (L / kStages) & 1, kWaitNs)) S.abort_flag = 1;
-            const int lp = it.page_begin + gi * kGroupPages + pi;
-            const int patch_tok = (do_append && lp == last_page) ? rd.pos % kBlockTokens : -1;
-            const int t0 = g8, t1 = g8 + 8;
-            const float4 pa = *reinterpret_cast<const float4 *>(&S.scores[(pi * kBlockTokens + t0) * kGroup]);
-            const float4 pb = *reinterpret_cast<const float4 *>(&S.scores[(pi * kBlockTokens + t1) * kGroup]);
-            float fa[8], fb[8];
-            float wa[kGroup] = {pa.x, pa.y, pa.z, pa.w};
-            float wb[kGroup] = {pb.x, pb.y, pb.z, pb.w};
-            if constexpr (DT == 1) {
-                uint4 va = *reinterpret_cast<const uint4 *>(S.stage[st] + t0 * (kHeadDim * 2) + 16 * j16);
-                uint4 vb = *reinterpret_cast<const uint4 *>(S.stage[st] + t1 * (kHeadDim * 2) + 16 * j16);
-                if (t0 == patch_tok) va = *reinterpret_cast<const uint4 *>(S.newv + 16 * j16);
-                if (t1 == patch_tok) vb = *reinterpret_cast<const uint4 *>(S.newv + 16 * j16);
-                h8_to_f8(va, fa);
-                h8_to_f8(vb, fb);
-            } else {
-                uint2 va = *reinterpret_cast<const uint2 *>(S.stage[st] + t0 * kHeadDim + 8 * j16);
-                uint2 vb = *reinterpret_cast<const uint2 *>(S.stage[st] + t1 * kHeadDim + 8 * j16);
-                const uint16_t * sc = reinterpret_cast<const uint16_t *>(S.stage[st] + Fmt<8>::kData);
-                uint16_t da = sc[t0 * (kHeadDim / kQ8Block) + (j16 >> 2)];
-                uint16_t db = sc[t1 * (kHeadDim / kQ8Block) + (j16 >> 2)];
-                if (t0 == patch_tok) {
-                    va = *reinterpret_cast<const uint2 *>(S.newv + 8 * j16);
-                    da = S.newv_scale[j16 >> 2];
-                }
-                if (t1 == patch_tok) {
-                    vb = *reinterpret_cast<const uint2 *>(S.newv + 8 * j16);
-                    db = S.newv_scale[j16 >> 2];
-                }
-                s8x4_to_f4(va.x, fa);
-                s8x4_to_f4(va.y, fa + 4);
-                s8x4_to_f4(vb.x, fb);
-                s8x4_to_f4(vb.y, fb + 4);
-                const float dfa = __half2float(__ushort_as_half(da));
-                const float dfb = __half2float(__ushort_as_half(db));
+        float o[8][4];
 #pragma unroll
-                for (int g = 0; g < kGroup; ++g) {
-                    wa[g] *= dfa;
-                    wb[g] *= dfb;
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < kGroup; ++g) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    acc[g][i] = fmaf(wa[g], fa[i], acc[g][i]);
-                    acc[g][i] = fmaf(wb[g], fb[i], acc[g][i]);
-                }
-            }
-            __syncthreads();
-            if (S.abort_flag) {
-                aborted = true;
+        for (int mb = 0; mb < 8; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.0f;
+        float m_run = -INFINITY;
+        float l_part = 0.0f;
+        const int share = share_of(n_pages);
+        for (int i = 0; i < share; ++i) {
+            const int st = seq_consumed % ST;
+            // the outcome is made warp-uniform so the warp never splits
+            if (!__all_sync(kFull, mbar_wait(&S.full[warp][st], (seq_consumed / ST) & 1, kWaitNs))) {
+                S.abort_flag = 1;
                 break;
             }
-            if (tid == 0 && issued < total) issue(issued++);
-        }
-    }
+            const int lp = it.page_begin + warp + kWarps * i;
+            uint8_t * sk = S.stage[warp][st];
+            uint8_t * sv = sk + TILE + SCALE;
+            if (do_append && lp == last_page) {
+                // Replace the stale copy of the appended row by the new values.
+                const int t = rd.pos % kBlockTokens;
+                if constexpr (DT == 1) {
+                    const int ch = lane & 15;
+                    const uint4 val = *reinterpret_cast<const uint4 *>((lane < 16 ? S.newk : S.newv) + ch * 16);
+                    *reinterpret_cast<uint4 *>((lane < 16 ? sk : sv) + f16_chunk_off(t, ch)) = val;
+                } else {
+                    if (lane < 16) {
+                        const int ch = lane & 7;
+                        const uint4 val = *reinterpret_cast<const uint4 *>((lane < 8 ? S.newk : S.newv) + ch * 16);
+                        *reinterpret_cast<uint4 *>((lane < 8 ? sk : sv) + q8_chunk_off(t, ch)) = val;
+                    } else if (lane < 24) {
+                        const int b = lane & 3;
+                        const bool kk = lane < 20;
+                        reinterpret_cast<uint16_t *>((kk ? sk : sv) + TILE)[b * kBlockTokens + t] =
+                            kk ? S.newk_scale[b] : S.newv_scale[b];
+                    }
+                }
+                // The stage is refilled by the bulk-copy (async) proxy later:
+                // order these generic-proxy writes before that.
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+            }
 
-    if (aborted) {
-        // Drain the copies still in flight (bounded) before the CTA exits.
+            // ---- S^T = Q K^T for the page's 16 tokens (two n-blocks of 8) ---
+            float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint32_t kbase = smem_u32(sk);
+            if constexpr (DT == 1) {
+                const int row = mrow + ((mi >> 1) << 3);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(kbase + f16_chunk_off(row, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+                    mma16816(s0, qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+                    mma16816(s1, qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+                }
+            } else {
+                const int row = mrow + ((mi & 1) << 3);
+                const __half2 * dk = reinterpret_cast<const __half2 *>(sk + TILE);
+#pragma unroll
+                for (int blk = 0; blk < 4; ++blk) {
+                    uint32_t w0, w1, w2, w3;
+                    ldsm_x4(kbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
+                    float t0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    float t1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    w0 ^= 0x80808080u;
+                    w1 ^= 0x80808080u;
+                    w2 ^= 0x80808080u;
+                    w3 ^= 0x80808080u;
+                    mma16816(t0, qa[2 * blk][0], 0u, qa[2 * blk][1], 0u, s8pair_to_h2(w0, 0x4140u),
+                             s8pair_to_h2(w0, 0x4342u));
+                    mma16816(t1, qa[2 * blk][0], 0u, qa[2 * blk][1], 0u, s8pair_to_h2(w1, 0x4140u),
+                             s8pair_to_h2(w1, 0x4342u));
+                    mma16816(t0, qa[2 * blk + 1][0], 0u, qa[2 * blk + 1][1], 0u, s8pair_to_h2(w2, 0x4140u),
+                             s8pair_to_h2(w2, 0x4342u));
+                    mma16816(t1, qa[2 * blk + 1][0], 0u, qa[2 * blk + 1][1], 0u, s8pair_to_h2(w3, 0x4140u),
+                             s8pair_to_h2(w3, 0x4342u));
+                    const float2 d01 = __half22float2(dk[(blk * kBlockTokens + 2 * c) >> 1]);
+                    const float2 d89 = __half22float2(dk[(blk * kBlockTokens + 8 + 2 * c) >> 1]);
+                    s0[0] = fmaf(t0[0], d01.x, s0[0]);
+                    s0[1] = fmaf(t0[1], d01.y, s0[1]);
+                    s1[0] = fmaf(t1[0], d89.x, s1[0]);
+                    s1[1] = fmaf(t1[1], d89.y, s1[1]);
+                }
+            }
+
+            // ---- online softmax (log2 domain) for head g over tokens
+            //      2c, 2c+1, 8+2c, 9+2c of this page --------------------------
+            const int tp = lp * kBlockTokens;
+            float sc[4] = {s0[0], s0[1], s1[0], s1[1]};
+            const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int pos = tp + tk[j];
+                if (!real || pos < rd.win_start || pos > rd.pos) sc[j] = -INFINITY;
+            }
+            float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = real ? exp2f(m_run - m_new) : 1.0f;
+            float pr[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) pr[j] = real ? exp2f(sc[j] - m_new) : 0.0f;
+            if (real) m_run = m_new;
+            const __half2 p01 = __floats2half2_rn(pr[0], pr[1]);
+            const __half2 p89 = __floats2half2_rn(pr[2], pr[3]);
+            {
+                const float2 f0 = __half22float2(p01), f1 = __half22float2(p89);
+                l_part = l_part * alpha + ((f0.x + f0.y) + (f1.x + f1.y));
+            }
+            // rescale O^T columns (heads 2c, 2c+1) when any running max moved
+            if (__any_sync(kFull, alpha != 1.0f)) {
+                const float a_lo = __shfl_sync(kFull, alpha, (8 * c) & 31);
+                const float a_hi = __shfl_sync(kFull, alpha, (8 * c + 4) & 31);
+#pragma unroll
+                for (int mb = 0; mb < 8; ++mb) {
+                    o[mb][0] *= a_lo;
+                    o[mb][1] *= a_hi;
+                    o[mb][2] *= a_lo;
+                    o[mb][3] *= a_hi;
+                }
+            }
+
+            // ---- O^T += V^T P^T ---------------------------------------------
+            const uint32_t vbase = smem_u32(sv);
+            if constexpr (DT == 1) {
+                const uint32_t b0 = h2_bits(p01), b1 = h2_bits(p89);
+                const int row = mrow + ((mi >> 1) << 3);
+#pragma unroll
+                for (int mb = 0; mb < 8; ++mb) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(vbase + f16_chunk_off(row, 2 * mb + (mi & 1)), a0, a1, a2, a3);
+                    mma16816(o[mb], a0, a1, a2, a3, b0, b1);
+                }
+            } else {
+                const int row = mrow + ((mi & 1) << 3);
+                const __half2 * dv = reinterpret_cast<const __half2 *>(sv + TILE);
+#pragma unroll
+                for (int blk = 0; blk < 4; ++blk) {
+                    // fold the block scale (x128, exact) into the probabilities
+                    const float2 d01 = __half22float2(dv[(blk * kBlockTokens + 2 * c) >> 1]);
+                    const float2 d89 = __half22float2(dv[(blk * kBlockTokens + 8 + 2 * c) >> 1]);
+                    const uint32_t b0 =
+                        h2_bits(__floats2half2_rn(pr[0] * d01.x * 128.0f, pr[1] * d01.y * 128.0f));
+                    const uint32_t b1 =
+                        h2_bits(__floats2half2_rn(pr[2] * d89.x * 128.0f, pr[3] * d89.y * 128.0f));
+                    uint32_t w0, w1, w2, w3;
+                    ldsm_x4_t(vbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
+                    w0 ^= 0x80808080u;
+                    w1 ^= 0x80808080u;
+                    w2 ^= 0x80808080u;
+                    w3 ^= 0x80808080u;
+                    mma16816(o[2 * blk], s8pair_to_h2(w0, 0x4240u), s8pair_to_h2(w0, 0x4341u),
+                             s8pair_to_h2(w1, 0x4240u), s8pair_to_h2(w1, 0x4341u), b0, b1);
+                    mma16816(o[2 * blk + 1], s8pair_to_h2(w2, 0x4240u), s8pair_to_h2(w2, 0x4341u),
+                             s8pair_to_h2(w3, 0x4240u), s8pair_to_h2(w3, 0x4341u), b0, b1);
+                }
+            }
+            __syncwarp();
+            ++seq_consumed;
+            pump(seq_consumed);
+        }
+
+        // ---- merge the 4 warps' partial softmax states -----------------------
+        {
+            float l_h = l_part + __shfl_xor_sync(kFull, l_part, 1);
+            l_h += __shfl_xor_sync(kFull, l_h, 2);
+            if (real && c == 0) {
+                S.wm[warp][g] = m_run;
+                S.wl[warp][g] = l_h;
+            }
+            if (c < 2) {
+                const float post = DT == 1 ? 1.0f : 1.0f / 128.0f;
+#pragma unroll
+                for (int mb = 0; mb < 8; ++mb) {
+                    const int d0 = DT == 1 ? 16 * mb + g : 16 * mb + 2 * g;
+                    const int d1 = DT == 1 ? 16 * mb + 8 + g : 16 * mb + 2 * g + 1;
+                    float * h0 = S.merge + (warp * kGroup + 2 * c) * kHeadDim;
+                    float * h1 = h0 + kHeadDim;
+                    h0[d0] = o[mb][0] * post;
+                    h1[d0] = o[mb][1] * post;
+                    h0[d1] = o[mb][2] * post;
+                    h1[d1] = o[mb][3] * post;
+                }
+            }
+        }
+        __syncthreads();
+        if (S.abort_flag) {
+            // Drain this warp's copies still in flight (bounded) before exiting.
+            if (lane == 0) {
+                for (int l = seq_consumed; l < seq_issued; ++l) mbar_wait(&S.full[warp][l % ST], (l / ST) & 1, kWaitNs);
+                set_error(p.error, kErrTimeout);
+            }
+            return;
+        }
+        float M[kGroup], Lsum[kGroup], O[kGroup];
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h) {
+            float mm = S.wm[0][h];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) mm = fmaxf(mm, S.wm[w][h]);
+            float ls = 0.0f, os = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float wt = exp2f(S.wm[w][h] - mm);  // 0 for warps without pages
+                ls += S.wl[w][h] * wt;
+                os += S.merge[(w * kGroup + h) * kHeadDim + tid] * wt;
+            }
+            M[h] = mm;
+            Lsum[h] = ls;
+            O[h] = os;
+        }
+        // every thread has read the merge buffer before it is reused below
+        __syncthreads();
+
+        const int64_t out_base = ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup) * kHeadDim;
+        if (rd.n_chunks == 1) {
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h) p.out[out_base + h * kHeadDim + tid] = O[h] / Lsum[h];
+            continue;
+        }
+        {
+            float * part = p.partials + ((int64_t) item_idx * p.n_q + (int64_t) kvh * kGroup) * kPartialStride;
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h) part[h * kPartialStride + tid] = O[h];
+            if (tid < kGroup) {
+                part[tid * kPartialStride + kHeadDim] = M[tid];
+                part[tid * kPartialStride + kHeadDim + 1] = Lsum[tid];
+            }
+        }
+        __threadfence();
+        __syncthreads();
         if (tid == 0) {
-            for (int l = L + 1; l < issued; ++l) mbar_wait(&S.full[l % kStages], (l / kStages) & 1, kWaitNs);
-            set_error(p.error, kErrTimeout);
+            const int prev = atomicAdd(&p.counters[it.row * p.n_kv + kvh], 1);
+            S.last_flag = (prev == rd.n_chunks - 1);
         }
-        return;
-    }
+        __syncthreads();
+        if (!S.last_flag) continue;
+        __threadfence();
 
-    // ---- reduce acc over the 8 token pairs, emit output or partial ---------
-    float * red = reinterpret_cast<float *>(&S.stage[0][0]);  // [8][4][128]
-#pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-        float4 * dst = reinterpret_cast<float4 *>(red + (g8 * kGroup + g) * kHeadDim + 8 * j16);
-        dst[0] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-        dst[1] = make_float4(acc[g][4], acc[g][5], acc[g][6], acc[g][7]);
-    }
-    __syncthreads();
-    float o[kGroup];
-#pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-        float sum = 0.0f;
-#pragma unroll
-        for (int q2 = 0; q2 < 8; ++q2) sum += red[(q2 * kGroup + g) * kHeadDim + tid];
-        o[g] = sum;
-    }
-    const int64_t out_base = ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup) * kHeadDim;
-    if (rd.n_chunks == 1) {
-#pragma unroll
-        for (int g = 0; g < kGroup; ++g) p.out[out_base + g * kHeadDim + tid] = o[g] / l_run[g];
-        return;
-    }
-    {
-        float * part = p.partials + ((int64_t) item_idx * p.n_q + (int64_t) kvh * kGroup) * kPartialStride;
-#pragma unroll
-        for (int g = 0; g < kGroup; ++g) part[g * kPartialStride + tid] = o[g];
-        if (tid < kGroup) {
-            part[tid * kPartialStride + kHeadDim] = m_run[tid];
-            part[tid * kPartialStride + kHeadDim + 1] = l_run[tid];
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const int prev = atomicAdd(&p.counters[it.row * p.n_kv + kvh], 1);
-        S.last_flag = (prev == rd.n_chunks - 1);
-    }
-    __syncthreads();
-    if (!S.last_flag) return;
-    __threadfence();
-
-    // ---- last split of the (row, kv head): combine all splits --------------
-    const int nc = rd.n_chunks;
-    auto part_at = [&](int c, int g) -> const float * {
-        return p.partials +
-               ((int64_t) (rd.item_base + c) * p.n_q + (int64_t) kvh * kGroup + g) * kPartialStride;
-    };
-    {
+        // ---- last split of the (row, kv head): combine all splits -----------
+        const int nc = rd.n_chunks;
+        float * comb_w = S.merge;  // [split][head] weights
+        auto part_at = [&](int cc, int h) -> const float * {
+            return p.partials + ((int64_t) (rd.item_base + cc) * p.n_q + (int64_t) kvh * kGroup + h) * kPartialStride;
+        };
         float lm[kGroup];
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) lm[g] = -INFINITY;
-        for (int c = tid; c < nc; c += NT) {
+        for (int h = 0; h < kGroup; ++h) lm[h] = -INFINITY;
+        for (int cc = tid; cc < nc; cc += NT) {
 #pragma unroll
-            for (int g = 0; g < kGroup; ++g) lm[g] = fmaxf(lm[g], __ldcg(part_at(c, g) + kHeadDim));
+            for (int h = 0; h < kGroup; ++h) lm[h] = fmaxf(lm[h], __ldcg(part_at(cc, h) + kHeadDim));
         }
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
+        for (int h = 0; h < kGroup; ++h) {
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) lm[g] = fmaxf(lm[g], __shfl_xor_sync(0xffffffffu, lm[g], off));
+            for (int off = 16; off >= 1; off >>= 1) lm[h] = fmaxf(lm[h], __shfl_xor_sync(kFull, lm[h], off));
         }
         if (lane == 0) {
 #pragma unroll
-            for (int g = 0; g < kGroup; ++g) S.red_m[warp][g] = lm[g];
+            for (int h = 0; h < kGroup; ++h) S.red_m[warp][h] = lm[h];
         }
         __syncthreads();
-        float M[kGroup];
+        float Mx[kGroup];
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
-            M[g] = S.red_m[0][g];
+        for (int h = 0; h < kGroup; ++h) {
+            Mx[h] = S.red_m[0][h];
 #pragma unroll
-            for (int w = 1; w < NT / 32; ++w) M[g] = fmaxf(M[g], S.red_m[w][g]);
+            for (int w = 1; w < kWarps; ++w) Mx[h] = fmaxf(Mx[h], S.red_m[w][h]);
         }
         float ls[kGroup] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int c = tid; c < nc; c += NT) {
+        for (int cc = tid; cc < nc; cc += NT) {
 #pragma unroll
-            for (int g = 0; g < kGroup; ++g) {
-                const float * pc = part_at(c, g);
-                const float w = exp2f(__ldcg(pc + kHeadDim) - M[g]);
-                ls[g] += __ldcg(pc + kHeadDim + 1) * w;
-                S.scores[c * kGroup + g] = w;
+            for (int h = 0; h < kGroup; ++h) {
+                const float * pc = part_at(cc, h);
+                const float w = exp2f(__ldcg(pc + kHeadDim) - Mx[h]);
+                ls[h] += __ldcg(pc + kHeadDim + 1) * w;
+                comb_w[cc * kGroup + h] = w;
             }
         }
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
+        for (int h = 0; h < kGroup; ++h) {
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) ls[g] += __shfl_xor_sync(0xffffffffu, ls[g], off);
+            for (int off = 16; off >= 1; off >>= 1) ls[h] += __shfl_xor_sync(kFull, ls[h], off);
         }
         if (lane == 0) {
 #pragma unroll
-            for (int g = 0; g < kGroup; ++g) S.red_l[warp][g] = ls[g];
+            for (int h = 0; h < kGroup; ++h) S.red_l[warp][h] = ls[h];
         }
         __syncthreads();
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
-            float Lsum = 0.0f;
+        for (int h = 0; h < kGroup; ++h) {
+            float Lt = 0.0f;
 #pragma unroll
-            for (int w = 0; w < NT / 32; ++w) Lsum += S.red_l[w][g];
-            const float inv = 1.0f / Lsum;
-            float acc2 = 0.0f;
-            for (int c = 0; c < nc; ++c) acc2 = fmaf(S.scores[c * kGroup + g], __ldcg(part_at(c, g) + tid), acc2);
-            p.out[out_base + g * kHeadDim + tid] = acc2 * inv;
+            for (int w = 0; w < kWarps; ++w) Lt += S.red_l[w][h];
+            float acc = 0.0f;
+            for (int cc = 0; cc < nc; ++cc) acc = fmaf(comb_w[cc * kGroup + h], __ldcg(part_at(cc, h) + tid), acc);
+            p.out[out_base + h * kHeadDim + tid] = acc / Lt;
         }
+        if (tid == 0) p.counters[it.row * p.n_kv + kvh] = 0;
+        // the weights in the merge buffer are read before the next unit writes it
+        __syncthreads();
     }
-    if (tid == 0) p.counters[it.row * p.n_kv + kvh] = 0;
 }
 
 template <int DT>
@@ -655,9 +716,8 @@ __global__ void __launch_bounds__(NT) append_kernel(const AppendParams p) {
     }
     const int64_t tile = (int64_t) pg * p.n_kv + kvh;
     const int64_t krow = ((int64_t) row * p.n_kv + kvh) * kHeadDim;
-    append_head_row<DT>(p.k + krow, p.v + krow, p.rope + (int64_t) rd.pos * (kHeadDim / 2),
-                        p.k_data, p.v_data, p.k_scale, p.v_scale, tile, rd.pos % kBlockTokens,
-                        nullptr, nullptr, nullptr, nullptr);
+    append_head_row<DT>(p.k + krow, p.v + krow, p.rope + (int64_t) rd.pos * (kHeadDim / 2), p.k_data, p.v_data,
+                        p.k_scale, p.v_scale, tile, rd.pos % kBlockTokens, nullptr, nullptr, nullptr, nullptr);
 }
 
 __global__ void table_update_kernel(int32_t * table, const TableUpdate * up, int32_t n) {
@@ -665,6 +725,7 @@ __global__ void table_update_kernel(int32_t * table, const TableUpdate * up, int
     if (i < n) table[up[i].index] = up[i].page;
 }
 
+// Reads rows back in plain order (un-swizzled): one CTA per (position, head).
 template <int DT>
 __global__ void gather_kernel(const GatherParams p) {
     const int r = blockIdx.x / p.n_kv;
@@ -677,19 +738,23 @@ __global__ void gather_kernel(const GatherParams p) {
     const int64_t tile = (int64_t) pg * p.n_kv + kvh;
     const int tok = (int) (pos % kBlockTokens);
     constexpr int row_bytes = DT == 1 ? kHeadDim * 2 : kHeadDim;
-    const int64_t src = (tile * kBlockTokens + tok) * row_bytes;
+    constexpr int chunks = row_bytes / 16;
     const int64_t dst = ((int64_t) r * p.n_kv + kvh) * row_bytes;
-    for (int b = threadIdx.x; b < row_bytes / 4; b += blockDim.x) {
-        reinterpret_cast<uint32_t *>(p.k_out + dst)[b] = reinterpret_cast<const uint32_t *>(p.k_data + src)[b];
-        reinterpret_cast<uint32_t *>(p.v_out + dst)[b] = reinterpret_cast<const uint32_t *>(p.v_data + src)[b];
+    const uint8_t * kt = p.k_data + tile * Cfg<DT>::kTile;
+    const uint8_t * vt = p.v_data + tile * Cfg<DT>::kTile;
+    for (int ch = threadIdx.x; ch < chunks; ch += blockDim.x) {
+        const int off = DT == 1 ? f16_chunk_off(tok, ch) : q8_chunk_off(tok, ch);
+        *reinterpret_cast<uint4 *>(p.k_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(kt + off);
+        *reinterpret_cast<uint4 *>(p.v_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(vt + off);
     }
     if constexpr (DT == 8) {
-        constexpr int nsb = (kHeadDim / kQ8Block) * 2;
-        const int64_t ssrc = (tile * kBlockTokens + tok) * nsb;
-        const int64_t sdst = ((int64_t) r * p.n_kv + kvh) * nsb;
-        for (int b = threadIdx.x; b < nsb / 2; b += blockDim.x) {
-            reinterpret_cast<uint16_t *>(p.k_scale_out + sdst)[b] = reinterpret_cast<const uint16_t *>(p.k_scale + ssrc)[b];
-            reinterpret_cast<uint16_t *>(p.v_scale_out + sdst)[b] = reinterpret_cast<const uint16_t *>(p.v_scale + ssrc)[b];
+        constexpr int nb = kHeadDim / kQ8Block;
+        const int64_t sdst = ((int64_t) r * p.n_kv + kvh) * nb;
+        const uint16_t * ks = reinterpret_cast<const uint16_t *>(p.k_scale + tile * Cfg<8>::kScale);
+        const uint16_t * vs = reinterpret_cast<const uint16_t *>(p.v_scale + tile * Cfg<8>::kScale);
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+            reinterpret_cast<uint16_t *>(p.k_scale_out)[sdst + b] = ks[b * kBlockTokens + tok];
+            reinterpret_cast<uint16_t *>(p.v_scale_out)[sdst + b] = vs[b * kBlockTokens + tok];
         }
     }
 }
@@ -717,27 +782,53 @@ __global__ void __launch_bounds__(256) compact_kernel(const CompactParams p) {
     }
 }
 
-}  // namespace
-
-int decode_smem_bytes(int dtype) {
-    return dtype == 8 ? (int) sizeof(Smem<8>) : (int) sizeof(Smem<1>);
+template <int DT>
+cudaError_t launch_decode_t(const DecodeParams & p, cudaStream_t stream, bool pdl) {
+    const int smem = (int) sizeof(Smem<DT>);
+    // The opt-in is per device; remember which devices have it.
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64 || !(configured & (1ull << dev))) {
+        e = cudaFuncSetAttribute(decode_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) configured |= 1ull << dev;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned) p.n_ctas);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = (size_t) smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, decode_kernel<DT>, p);
 }
 
-cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream) {
-    if (p.n_items <= 0) return cudaSuccess;
-    const dim3 grid((unsigned) (p.n_items * p.n_kv));
-    if (p.dtype == 8) {
-        const int smem = (int) sizeof(Smem<8>);
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        decode_kernel<8><<<grid, NT, smem, stream>>>(p);
+}  // namespace
+
+int decode_smem_bytes(int dtype) { return dtype == 8 ? (int) sizeof(Smem<8>) : (int) sizeof(Smem<1>); }
+
+int decode_ctas_per_sm(int dtype) {
+    int n = 0;
+    if (dtype == 8) {
+        if (cudaFuncSetAttribute(decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<8>)) != cudaSuccess)
+            return 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<8>, NT, sizeof(Smem<8>)) != cudaSuccess) return 0;
     } else {
-        const int smem = (int) sizeof(Smem<1>);
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        decode_kernel<1><<<grid, NT, smem, stream>>>(p);
+        if (cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<1>)) != cudaSuccess)
+            return 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<1>, NT, sizeof(Smem<1>)) != cudaSuccess) return 0;
     }
-    return cudaGetLastError();
+    return n;
+}
+
+cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream, bool pdl) {
+    if (p.n_items <= 0 || p.n_ctas <= 0) return cudaSuccess;
+    return p.dtype == 8 ? launch_decode_t<8>(p, stream, pdl) : launch_decode_t<1>(p, stream, pdl);
 }
 
 cudaError_t launch_append(const AppendParams & p, cudaStream_t stream) {
@@ -751,8 +842,7 @@ cudaError_t launch_append(const AppendParams & p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_table_updates(int32_t * table, const TableUpdate * updates, int32_t n,
-                                 cudaStream_t stream) {
+cudaError_t launch_table_updates(int32_t * table, const TableUpdate * updates, int32_t n, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     table_update_kernel<<<(n + 255) / 256, 256, 0, stream>>>(table, updates, n);
     return cudaGetLastError();
@@ -762,9 +852,9 @@ cudaError_t launch_gather(const GatherParams & p, cudaStream_t stream) {
     if (p.n <= 0) return cudaSuccess;
     const dim3 grid((unsigned) (p.n * p.n_kv));
     if (p.dtype == 8) {
-        gather_kernel<8><<<grid, 64, 0, stream>>>(p);
+        gather_kernel<8><<<grid, 32, 0, stream>>>(p);
     } else {
-        gather_kernel<1><<<grid, 64, 0, stream>>>(p);
+        gather_kernel<1><<<grid, 32, 0, stream>>>(p);
     }
     return cudaGetLastError();
 }

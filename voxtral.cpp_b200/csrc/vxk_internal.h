@@ -48,6 +48,10 @@ struct TableUpdate {
 // Partial record of one (work item, query head): acc[head_dim], m, l, pad.
 constexpr int kPartialStride = kHeadDim + 4;
 
+// Largest split (pages of one work item) the decode kernel accepts: 4 warps,
+// each holding 4 page ids per lane.
+constexpr int kMaxSplitPages = 512;
+
 struct DecodeParams {
     // cache of one layer
     uint8_t * k_data;        // f16 halves or q8_0 int8 values
@@ -61,6 +65,9 @@ struct DecodeParams {
     const int32_t * block_table;
     const RowDesc * rows;
     const WorkItem * items;
+    const int32_t * sched_offsets;  // [n_ctas + 1] per-CTA ranges of sched_units
+    const int32_t * sched_units;    // unit = item * n_kv + kv head, per CTA in order
+    int32_t n_ctas;
     int32_t n_rows;
     int32_t n_items;
     const float * q;         // [rows][n_q][head_dim]
@@ -128,15 +135,20 @@ struct CompactParams {
     int32_t n_moves;
 };
 
-cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream);
+// pdl: launch with programmatic stream serialization.  Only valid when the
+// preceding kernel on the stream writes nothing the decode prologue reads
+// (row/work descriptors, block table, cache pages of this layer).
+cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream, bool pdl);
 cudaError_t launch_append(const AppendParams & p, cudaStream_t stream);
 cudaError_t launch_table_updates(int32_t * table, const TableUpdate * updates, int32_t n,
                                  cudaStream_t stream);
 cudaError_t launch_gather(const GatherParams & p, cudaStream_t stream);
 cudaError_t launch_compact(const CompactParams & p, cudaStream_t stream);
 
-// Shared-memory bytes the decode kernel needs (for the host's opt-in).
+// Shared-memory bytes the decode kernel needs, and how many of its CTAs are
+// resident per SM on the current device (0 on error).
 int decode_smem_bytes(int dtype);
+int decode_ctas_per_sm(int dtype);
 
 // ---------------------------------------------------------------------------
 // Streaming encoder window attention

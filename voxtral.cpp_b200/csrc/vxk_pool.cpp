@@ -103,6 +103,7 @@ std::vector<float2> build_rope_table(int32_t rows, int32_t n_dims, float base) {
 struct vxk_pool {
     vxk_pool_config cfg{};
     int sm_count = 148;
+    int32_t decode_slots = 0;        // resident decode CTAs on the device
     int32_t bt_cap = 0;
     int64_t tile_data_bytes = 0;
     int64_t tile_scale_bytes = 0;
@@ -129,6 +130,7 @@ struct vxk_pool {
     int stage_next = 0;
     size_t stage_bytes = 0;
     size_t off_items = 0;
+    size_t off_sched = 0;            // [n_ctas + 1] offsets, then the unit list
     size_t off_updates = 0;
     int64_t device_bytes = 0;
 
@@ -144,9 +146,14 @@ struct vxk_pool {
 
     bool planned = false;
     bool single_token = false;
+    bool items_ok = false;          // the batch's splits fit the scratch
+    int32_t batch_decodes = 0;      // decode launches since the plan
     std::vector<PlanEntry> plan;
     std::vector<vxk::RowDesc> rows;
     std::vector<vxk::WorkItem> items;
+    std::vector<int32_t> order;
+    std::vector<int32_t> sched;      // offsets (n_ctas + 1) followed by units
+    int32_t n_ctas = 0;
     std::vector<vxk::TableUpdate> updates;
     std::vector<NewPage> new_pages;
 
@@ -277,9 +284,14 @@ void rollback_new_pages(vxk_pool * p) {
 void clear_plan(vxk_pool * p) {
     p->planned = false;
     p->single_token = false;
+    p->items_ok = false;
+    p->batch_decodes = 0;
     p->plan.clear();
     p->rows.clear();
     p->items.clear();
+    p->order.clear();
+    p->sched.clear();
+    p->n_ctas = 0;
     p->updates.clear();
     p->new_pages.clear();
 }
@@ -318,11 +330,14 @@ void build_items(vxk_pool * p) {
     int32_t cp = 0;
     if (const char * env = std::getenv("VXK_CHUNK_PAGES")) cp = std::atoi(env);
     if (cp <= 0) {
-        // Enough splits for ~8 CTAs per SM, each split at most 16 pages.
-        cp = pow2_floor(std::max<int64_t>(1, total_pages * p->cfg.n_kv_heads / (8 * (int64_t) p->sm_count)));
-        cp = std::min(cp, 16);
+        // A split pays a fixed prologue (descriptor, block-table and first-copy
+        // latency) and epilogue (merge, partials), so splits are made as large
+        // as load balance allows: about 1.5 waves of the resident decode CTAs,
+        // the longest launched first.
+        const int64_t slots = std::max<int64_t>(1, p->decode_slots);
+        cp = pow2_floor(std::max<int64_t>(1, total_pages * p->cfg.n_kv_heads * 2 / (3 * slots)));
     }
-    cp = std::min(cp, 128);
+    cp = std::min(cp, kMaxSplitPages);
     while (true) {
         int64_t n_items = 0;
         int64_t max_chunks = 0;
@@ -332,9 +347,17 @@ void build_items(vxk_pool * p) {
             max_chunks = std::max(max_chunks, c);
         }
         if (n_items <= p->max_items && max_chunks <= 256) break;
-        if (cp >= 128) fail(VXK_STATUS_INVALID_ARGUMENT, "batch windows exceed the split scratch capacity");
+        if (cp >= kMaxSplitPages) {
+            // Append-only batches (prefill) never attend; an attention call on
+            // this batch reports the overflow.
+            p->items.clear();
+            p->order.clear();
+            p->items_ok = false;
+            return;
+        }
         cp *= 2;
     }
+    p->items_ok = true;
     p->items.clear();
     for (size_t r = 0; r < p->rows.size(); ++r) {
         const int32_t first = p->rows[r].win_start / bt;
@@ -351,6 +374,56 @@ void build_items(vxk_pool * p) {
             p->items.push_back(it);
         }
     }
+    // Longest splits first, then a greedy longest-processing-time assignment
+    // of the (split, kv head) units to the resident CTAs of the persistent
+    // decode kernel: each unit goes to the CTA with the least pages so far.
+    p->order.resize(p->items.size());
+    std::iota(p->order.begin(), p->order.end(), 0);
+    std::stable_sort(p->order.begin(), p->order.end(), [&](int32_t a, int32_t b) {
+        return p->items[(size_t) a].page_end - p->items[(size_t) a].page_begin >
+               p->items[(size_t) b].page_end - p->items[(size_t) b].page_begin;
+    });
+    const int32_t nkv = p->cfg.n_kv_heads;
+    const int64_t n_units = (int64_t) p->items.size() * nkv;
+    // Persistent grid (one CTA per resident slot, VXK_PERSISTENT=1) or one CTA
+    // per unit, launched longest-first and balanced by the hardware.
+    static const bool persistent = [] {
+        const char * e = std::getenv("VXK_PERSISTENT");
+        return e && e[0] == '1';
+    }();
+    const int32_t G = (int32_t) std::max<int64_t>(
+        1, persistent ? std::min<int64_t>(n_units, p->decode_slots) : n_units);
+    std::vector<std::pair<int64_t, int32_t>> heap;  // (pages assigned, cta) min-heap
+    heap.reserve((size_t) G);
+    for (int32_t b = 0; b < G; ++b) heap.emplace_back(0, b);
+    std::vector<int32_t> unit_cta((size_t) n_units);
+    std::vector<int32_t> count((size_t) G, 0);
+    auto cmp = [](const std::pair<int64_t, int32_t> & x, const std::pair<int64_t, int32_t> & y) {
+        return x.first != y.first ? x.first > y.first : x.second > y.second;
+    };
+    std::vector<int32_t> unit_list;
+    unit_list.reserve((size_t) n_units);
+    for (int32_t idx : p->order) {
+        const vxk::WorkItem & it = p->items[(size_t) idx];
+        for (int32_t h = 0; h < nkv; ++h) {
+            std::pop_heap(heap.begin(), heap.end(), cmp);
+            auto & top = heap.back();
+            top.first += it.page_end - it.page_begin;
+            const int32_t uid = idx * nkv + h;
+            unit_list.push_back(uid);
+            unit_cta[(size_t) uid] = top.second;
+            ++count[(size_t) top.second];
+            std::push_heap(heap.begin(), heap.end(), cmp);
+        }
+    }
+    p->n_ctas = G;
+    p->sched.assign((size_t) G + 1 + (size_t) n_units, 0);
+    for (int32_t b = 0; b < G; ++b) p->sched[(size_t) b + 1] = p->sched[(size_t) b] + count[(size_t) b];
+    std::vector<int32_t> fill(p->sched.begin(), p->sched.begin() + G);
+    for (int32_t uid : unit_list) {
+        const int32_t b = unit_cta[(size_t) uid];
+        p->sched[(size_t) G + 1 + (size_t) fill[(size_t) b]++] = uid;
+    }
 }
 
 void upload_plan(vxk_pool * p, cudaStream_t stream) {
@@ -363,8 +436,9 @@ void upload_plan(vxk_pool * p, cudaStream_t stream) {
     uint8_t * h = p->h_stage[idx];
     std::memcpy(h, p->rows.data(), rows_b);
     std::memcpy(h + p->off_items, p->items.data(), items_b);
+    std::memcpy(h + p->off_sched, p->sched.data(), p->sched.size() * sizeof(int32_t));
     if (upd_b) std::memcpy(h + p->off_updates, p->updates.data(), upd_b);
-    const size_t n = upd_b ? p->off_updates + upd_b : p->off_items + items_b;
+    const size_t n = upd_b ? p->off_updates + upd_b : p->off_sched + p->sched.size() * sizeof(int32_t);
     VXK_CUDA(cudaMemcpyAsync(p->d_stage, h, n, cudaMemcpyHostToDevice, stream));
     VXK_CUDA(cudaEventRecord(p->stage_ev[idx], stream));
     p->stage_next ^= 1;
@@ -388,6 +462,9 @@ vxk::DecodeParams decode_params(vxk_pool * p, int32_t layer, const float * q, co
     d.block_table = p->d_table;
     d.rows = reinterpret_cast<const vxk::RowDesc *>(p->d_stage);
     d.items = reinterpret_cast<const vxk::WorkItem *>(p->d_stage + p->off_items);
+    d.sched_offsets = reinterpret_cast<const int32_t *>(p->d_stage + p->off_sched);
+    d.sched_units = d.sched_offsets + p->n_ctas + 1;
+    d.n_ctas = p->n_ctas;
     d.n_rows = (int32_t) p->rows.size();
     d.n_items = (int32_t) p->items.size();
     d.q = q;
@@ -408,6 +485,20 @@ vxk::DecodeParams decode_params(vxk_pool * p, int32_t layer, const float * q, co
 void check_layer(vxk_pool * p, int32_t layer) {
     if (!p->planned) fail(VXK_STATUS_INVALID_STATE, "no batch is planned");
     if (layer < 0 || layer >= p->cfg.n_layers) fail(VXK_STATUS_INVALID_ARGUMENT, "layer out of range");
+}
+
+void check_attention(vxk_pool * p) {
+    if (!p->items_ok) fail(VXK_STATUS_INVALID_ARGUMENT, "batch windows exceed the split scratch capacity");
+}
+
+// Programmatic dependent launch is used only when this pool's previous
+// launch was a fused decode of the same batch: that kernel writes nothing the
+// next decode prologue reads (descriptors, block table, other layers' pages).
+// Any other launch of the pool (plan upload, append, attend, compaction,
+// readback) clears the condition.
+bool use_pdl(vxk_pool * p) {
+    static const bool disabled = std::getenv("VXK_NO_PDL") != nullptr;
+    return !disabled && p->batch_decodes > 0;
 }
 
 void do_plan(vxk_pool * p, const int32_t * ids, const int32_t * n_new, int32_t n, cudaStream_t stream) {
@@ -586,7 +677,12 @@ vxk_status vxk_pool_create(const vxk_pool_config * config, vxk_pool ** out_pool)
         p->d_error = device_alloc<int32_t>(p, sizeof(int32_t));
         VXK_CUDA(cudaMemset(p->d_error, 0, sizeof(int32_t)));
         p->off_items = align_up((size_t) c.max_rows * sizeof(vxk::RowDesc), 256);
-        p->off_updates = p->off_items + align_up((size_t) p->max_items * sizeof(vxk::WorkItem), 256);
+        p->decode_slots = p->sm_count * vxk::decode_ctas_per_sm((int) c.dtype);
+        if (p->decode_slots <= 0) fail(VXK_STATUS_BACKEND_ERROR, "cannot size the decode kernel grid");
+        p->off_sched = p->off_items + align_up((size_t) p->max_items * sizeof(vxk::WorkItem), 256);
+        // schedule: (grid + 1) offsets, grid <= units, then the unit list
+        p->off_updates = p->off_sched + align_up((2 * (size_t) p->max_items * (size_t) c.n_kv_heads + 1) *
+                                                     sizeof(int32_t), 256);
         p->stage_bytes = p->off_updates + align_up((size_t) p->max_updates * sizeof(vxk::TableUpdate), 256);
         p->d_stage = device_alloc<uint8_t>(p, p->stage_bytes);
         for (int i = 0; i < 2; ++i) {
@@ -792,10 +888,14 @@ vxk_status vxk_decode_layer(vxk_pool * pool, int32_t layer, const float * q, con
         check_layer(pool, layer);
         if (!pool->single_token) fail(VXK_STATUS_INVALID_STATE, "decode_layer needs a single-token batch");
         if (!q || !k || !v || !out) fail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        check_attention(pool);
         DeviceScope scope(pool->cfg.device);
         ++pool->launches;
+        const bool pdl = use_pdl(pool);
+        pool->batch_decodes = 0;
         VXK_CUDA(vxk::launch_decode(decode_params(pool, layer, q, k, v, out, 1),
-                                    static_cast<cudaStream_t>(cuda_stream)));
+                                    static_cast<cudaStream_t>(cuda_stream), pdl));
+        pool->batch_decodes = 1;
     });
 }
 
@@ -824,6 +924,7 @@ vxk_status vxk_append_layer(vxk_pool * pool, int32_t layer, const float * k, con
         a.error = pool->d_error;
         a.dtype = (int32_t) pool->cfg.dtype;
         ++pool->launches;
+        pool->batch_decodes = 0;
         VXK_CUDA(vxk::launch_append(a, static_cast<cudaStream_t>(cuda_stream)));
     });
 }
@@ -834,10 +935,12 @@ vxk_status vxk_attend_layer(vxk_pool * pool, int32_t layer, const float * q, flo
     return guarded(pool, [&] {
         check_layer(pool, layer);
         if (!q || !out) fail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        check_attention(pool);
         DeviceScope scope(pool->cfg.device);
         ++pool->launches;
+        pool->batch_decodes = 0;
         VXK_CUDA(vxk::launch_decode(decode_params(pool, layer, q, nullptr, nullptr, out, 0),
-                                    static_cast<cudaStream_t>(cuda_stream)));
+                                    static_cast<cudaStream_t>(cuda_stream), false));
     });
 }
 
@@ -870,6 +973,11 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
         }
         std::vector<int32_t> ones((size_t) std::max(0, n_streams), 1);
         do_plan(pool, stream_ids, ones.data(), n_streams, cs);
+        if (!pool->items_ok) {
+            rollback_new_pages(pool);
+            clear_plan(pool);
+            check_attention(pool);
+        }
         const size_t rows = pool->rows.size();
         VXK_CUDA(cudaEventRecord(pool->ev_begin, cs));
         VXK_CUDA(cudaStreamWaitEvent(pool->h2d, pool->ev_begin, 0));
@@ -890,7 +998,7 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
         for (int32_t l = 0; l < c.n_layers; ++l) {
             VXK_CUDA(cudaStreamWaitEvent(cs, pool->ev_in[(size_t) l], 0));
             ++pool->launches;
-            VXK_CUDA(vxk::launch_decode(decode_params(pool, l, dq(l), dk(l), dv(l), dout(l), 1), cs));
+            VXK_CUDA(vxk::launch_decode(decode_params(pool, l, dq(l), dk(l), dv(l), dout(l), 1), cs, false));
             VXK_CUDA(cudaEventRecord(pool->ev_out[(size_t) l], cs));
             VXK_CUDA(cudaStreamWaitEvent(pool->d2h, pool->ev_out[(size_t) l], 0));
             VXK_CUDA(cudaMemcpyAsync(h_out + (size_t) l * rows * q_per_row, dout(l), rows * q_per_row * sizeof(float),
@@ -1072,6 +1180,7 @@ vxk_status vxk_read_rows(vxk_pool * pool, int32_t layer, int32_t stream, int64_t
         g.v_scale_out = g.k_scale_out + align_up(scale_b, 256);
         g.dtype = (int32_t) pool->cfg.dtype;
         ++pool->launches;
+        pool->batch_decodes = 0;
         VXK_CUDA(vxk::launch_gather(g, cs));
         std::vector<uint8_t> host(need);
         VXK_CUDA(cudaMemcpyAsync(host.data(), pool->d_read, need, cudaMemcpyDeviceToHost, cs));

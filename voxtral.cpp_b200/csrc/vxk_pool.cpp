@@ -332,12 +332,12 @@ void build_items(vxk_pool * p) {
     if (cp <= 0) {
         // A split pays a fixed prologue (descriptor, block-table and first-copy
         // latency) and epilogue (merge, partials), so splits are made as large
-        // as load balance allows: about 1.5 waves of the resident decode CTAs,
-        // the longest launched first.
+        // as load balance allows: about one wave of the resident decode CTAs,
+        // launched longest first so the short ones fill the tail.
         const int64_t slots = std::max<int64_t>(1, p->decode_slots);
-        cp = pow2_floor(std::max<int64_t>(1, total_pages * p->cfg.n_kv_heads * 2 / (3 * slots)));
+        cp = pow2_floor(std::max<int64_t>(1, total_pages * p->cfg.n_kv_heads / slots));
     }
-    cp = std::min(cp, kMaxSplitPages);
+    cp = std::min(cp, vxk::kMaxSplitPages);
     while (true) {
         int64_t n_items = 0;
         int64_t max_chunks = 0;
@@ -347,7 +347,7 @@ void build_items(vxk_pool * p) {
             max_chunks = std::max(max_chunks, c);
         }
         if (n_items <= p->max_items && max_chunks <= 256) break;
-        if (cp >= kMaxSplitPages) {
+        if (cp >= vxk::kMaxSplitPages) {
             // Append-only batches (prefill) never attend; an attention call on
             // this batch reports the overflow.
             p->items.clear();

@@ -258,6 +258,32 @@ VXK_API vxk_status vxk_decode_layer(vxk_pool * pool, int32_t layer, const float 
                                     const float * k, const float * v, float * out,
                                     void * cuda_stream);
 
+/**
+ * vxk_decode_layer with no device allocation behind it.  It has no
+ * counterpart in the reference; it exists for callers that cannot call
+ * cudaMalloc on their decode path: real-time audio threads, where cudaMalloc
+ * may synchronise the whole device and has no latency bound, and host
+ * applications whose device memory is already fully reserved by another
+ * allocator.  The split scratch of the attention (per-split partial results
+ * and arrival counters) lives in a fixed array inside libvxk.so (8.66 MB per
+ * GPU that loads the library, held until the process exits) instead of
+ * memory the library allocates; this call allocates nothing and calls no
+ * allocating routine.
+ *
+ * Limits: a batch may need at most 512 x 32 x 132 partial floats (for 32
+ * query heads: 512 splits) and 256 x 8 counters (256 rows of 8 kv heads);
+ * larger batches return VXK_STATUS_INVALID_ARGUMENT with the sizes in the
+ * pool's error message.  The first call on a device looks up the array's
+ * device address (with that device current), so make that first call before
+ * any stream capture.  Every call shares the one array and clears its
+ * counters before launching; calls that overlap on the GPU (other streams,
+ * other pools on the same device) race on it.  Arguments, results and the
+ * launch are otherwise those of vxk_decode_layer.
+ */
+VXK_API vxk_status vxk_decode_layer_static_scratch(vxk_pool * pool, int32_t layer, const float * q,
+                                                   const float * k, const float * v, float * out,
+                                                   void * cuda_stream);
+
 /** Appends the batch's new tokens to one layer (RoPE on K, f16/q8_0 store);
  *  replaces src/voxtral.cpp:2663-2714 for prefill / multi-token batches. */
 VXK_API vxk_status vxk_append_layer(vxk_pool * pool, int32_t layer, const float * k,

@@ -30,6 +30,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace vxk {
 namespace {
 
@@ -829,6 +831,62 @@ int decode_ctas_per_sm(int dtype) {
 cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream, bool pdl) {
     if (p.n_items <= 0 || p.n_ctas <= 0) return cudaSuccess;
     return p.dtype == 8 ? launch_decode_t<8>(p, stream, pdl) : launch_decode_t<1>(p, stream, pdl);
+}
+
+// ---------------------------------------------------------------------------
+// Fixed split scratch for callers that must not allocate device memory.
+//
+// The decode kernel keeps per-split partial results and per-(row, kv head)
+// arrival counters in scratch memory.  vxk_decode_layer_static_scratch uses
+// this file-scope array for them instead of memory allocated by the library,
+// so a call performs no device allocation at all.  The array is part of the
+// module image: every GPU that loads libvxk.so holds its
+// kStaticScratchFloats * 4 bytes (about 8.7 MB) until the process exits.
+// Every call shares it, so two such calls that overlap on the GPU (different
+// streams, or different pools on one device) race on it.
+// ---------------------------------------------------------------------------
+namespace {
+static __device__ __align__(256) float g_static_scratch[kStaticScratchFloats];
+}  // namespace
+
+// Device address of g_static_scratch on the current device.  Host code may not
+// use the symbol itself as a device pointer, so the address is looked up once
+// per device (with that device current) and remembered.
+static cudaError_t static_scratch_address(float ** out) {
+    static std::mutex mu;
+    static float * addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && addr[dev]) {
+        *out = addr[dev];
+        return cudaSuccess;
+    }
+    void * ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) addr[dev] = static_cast<float *>(ptr);
+    *out = static_cast<float *>(ptr);
+    return cudaSuccess;
+}
+
+cudaError_t launch_decode_static_scratch(const DecodeParams & params, cudaStream_t stream) {
+    if (params.n_items <= 0 || params.n_ctas <= 0) return cudaSuccess;
+    if ((size_t) params.n_items * params.n_q * kPartialStride > kStaticScratchPartialFloats ||
+        (size_t) params.n_rows * params.n_kv > kStaticScratchCounters)
+        return cudaErrorInvalidValue;
+    float * base = nullptr;
+    cudaError_t e = static_scratch_address(&base);
+    if (e != cudaSuccess) return e;
+    DecodeParams p = params;
+    p.partials = base;
+    p.counters = reinterpret_cast<int32_t *>(base + kStaticScratchPartialFloats);
+    // The array keeps the previous call's contents; the arrival counters must
+    // start at zero (partials are written before they are read).
+    e = cudaMemsetAsync(p.counters, 0, (size_t) p.n_rows * p.n_kv * sizeof(int32_t), stream);
+    if (e != cudaSuccess) return e;
+    return p.dtype == 8 ? launch_decode_t<8>(p, stream, false) : launch_decode_t<1>(p, stream, false);
 }
 
 cudaError_t launch_append(const AppendParams & p, cudaStream_t stream) {

@@ -145,6 +145,19 @@ cudaError_t launch_table_updates(int32_t * table, const TableUpdate * updates, i
 cudaError_t launch_gather(const GatherParams & p, cudaStream_t stream);
 cudaError_t launch_compact(const CompactParams & p, cudaStream_t stream);
 
+// Fixed split scratch of vxk_decode_layer_static_scratch: partial records for
+// up to 512 splits x 32 query heads, then arrival counters for up to 256 rows
+// x 8 kv heads (8.66 MB of floats in total).
+constexpr size_t kStaticScratchPartialFloats = (size_t) 512 * 32 * kPartialStride;
+constexpr size_t kStaticScratchCounters = (size_t) 256 * 8;
+constexpr size_t kStaticScratchFloats = kStaticScratchPartialFloats + kStaticScratchCounters;
+
+// Same launch as launch_decode (without programmatic dependent launch), with
+// the split scratch in the library's fixed device array instead of
+// p.partials / p.counters.  Returns cudaErrorInvalidValue when the batch needs
+// more scratch than the array holds.  Allocates nothing.
+cudaError_t launch_decode_static_scratch(const DecodeParams & p, cudaStream_t stream);
+
 // Shared-memory bytes the decode kernel needs, and how many of its CTAs are
 // resident per SM on the current device (0 on error).
 int decode_smem_bytes(int dtype);

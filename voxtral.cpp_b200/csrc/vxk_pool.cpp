@@ -899,6 +899,32 @@ vxk_status vxk_decode_layer(vxk_pool * pool, int32_t layer, const float * q, con
     });
 }
 
+vxk_status vxk_decode_layer_static_scratch(vxk_pool * pool, int32_t layer, const float * q, const float * k,
+                                           const float * v, float * out, void * cuda_stream) {
+    if (!pool) return VXK_STATUS_INVALID_ARGUMENT;
+    return guarded(pool, [&] {
+        check_layer(pool, layer);
+        if (!pool->single_token) fail(VXK_STATUS_INVALID_STATE, "decode_layer needs a single-token batch");
+        if (!q || !k || !v || !out) fail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        check_attention(pool);
+        const size_t need_partials =
+            pool->items.size() * (size_t) pool->cfg.n_q_heads * (size_t) vxk::kPartialStride;
+        const size_t need_counters = pool->rows.size() * (size_t) pool->cfg.n_kv_heads;
+        if (need_partials > vxk::kStaticScratchPartialFloats || need_counters > vxk::kStaticScratchCounters) {
+            fail(VXK_STATUS_INVALID_ARGUMENT,
+                 "batch needs " + std::to_string(need_partials) + " partial floats and " +
+                     std::to_string(need_counters) + " counters; the static scratch holds " +
+                     std::to_string(vxk::kStaticScratchPartialFloats) + " and " +
+                     std::to_string(vxk::kStaticScratchCounters));
+        }
+        DeviceScope scope(pool->cfg.device);
+        ++pool->launches;
+        pool->batch_decodes = 0;
+        VXK_CUDA(vxk::launch_decode_static_scratch(decode_params(pool, layer, q, k, v, out, 1),
+                                                   static_cast<cudaStream_t>(cuda_stream)));
+    });
+}
+
 vxk_status vxk_append_layer(vxk_pool * pool, int32_t layer, const float * k, const float * v,
                             void * cuda_stream) {
     if (!pool) return VXK_STATUS_INVALID_ARGUMENT;

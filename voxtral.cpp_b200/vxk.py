@@ -110,6 +110,7 @@ SIGNATURES = {
     "vxk_batch_commit": (_I32, [_P]),
     "vxk_batch_abort": (_I32, [_P]),
     "vxk_decode_layer": (_I32, [_P, _I32, _P, _P, _P, _P, _P]),
+    "vxk_decode_layer_static_scratch": (_I32, [_P, _I32, _P, _P, _P, _P, _P]),
     "vxk_append_layer": (_I32, [_P, _I32, _P, _P, _P]),
     "vxk_attend_layer": (_I32, [_P, _I32, _P, _P, _P]),
     "vxk_decode_step_host": (_I32, [_P, _I32P, _I32, _P, _P, _P, _P, _P]),
@@ -231,6 +232,12 @@ class Pool:
 
     def decode_layer(self, layer, q, k, v, out, cuda_stream=0):
         self._check(self.lib.vxk_decode_layer(self.h, layer, q, k, v, out, C.c_void_p(cuda_stream)))
+
+    def decode_layer_static_scratch(self, layer, q, k, v, out, cuda_stream=0):
+        """decode_layer whose split scratch is the library's fixed device array
+        (no device allocation behind the call)."""
+        self._check(self.lib.vxk_decode_layer_static_scratch(self.h, layer, q, k, v, out,
+                                                             C.c_void_p(cuda_stream)))
 
     def append_layer(self, layer, k, v, cuda_stream=0):
         self._check(self.lib.vxk_append_layer(self.h, layer, k, v, C.c_void_p(cuda_stream)))

@@ -16,6 +16,8 @@
 #include <string>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 namespace {
 
 thread_local std::string g_enc_create_error;
@@ -48,7 +50,34 @@ struct EncPlan {
     vxk_enc_kv_plan plan;
 };
 
-constexpr int kEncRowsPerGroup = 16;
+// Query rows of one stream attended together (the N extent of the tensor-core
+// tiles).
+constexpr int kEncRowsPerGroup = 8;
+
+// 3-D tensor map {64 dims, capacity slots, rings} over one ring array, with
+// 8-slot x 64-dim boxes in the 128-byte swizzled layout and zero fill for
+// slots past the capacity.  cuTensorMapEncodeTiled is a driver entry point,
+// reached through the runtime so the library does not link libcuda.
+void encode_ring_map(CUtensorMap * map, void * ring, int32_t dtype, int32_t capacity, int64_t rings) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void * fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            efail(VXK_STATUS_BACKEND_ERROR, "cuTensorMapEncodeTiled is not available");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dims[3] = {64, (cuuint64_t) capacity, (cuuint64_t) rings};
+    const cuuint64_t strides[2] = {128, (cuuint64_t) capacity * 128};
+    const cuuint32_t box[3] = {64, 8, 1};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    const CUresult r = encode(map, dtype == VXK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              3, ring, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) efail(VXK_STATUS_BACKEND_ERROR, "cuTensorMapEncodeTiled failed for the encoder ring");
+}
 
 }  // namespace
 
@@ -68,6 +97,8 @@ struct vxk_enc_pool {
     std::vector<EncPlan> plan;
     std::vector<vxk::EncRowDesc> rows;
     std::vector<int32_t> group_first;
+    CUtensorMap map_k{};
+    CUtensorMap map_v{};
     std::string last_error;
 };
 
@@ -182,6 +213,14 @@ vxk_status vxk_enc_create(const vxk_enc_config * config, vxk_enc_pool ** out) {
             efail(VXK_STATUS_INVALID_ARGUMENT, "bad encoder shape");
         if (c.window < 1 || c.capacity <= c.window || c.max_new < 1 || c.max_new > c.capacity - c.window)
             efail(VXK_STATUS_INVALID_ARGUMENT, "need 1 <= max_new <= capacity - window");
+        {
+            // A row group's window (window - 1 + 8 keys), its alignment to
+            // 8-slot boxes and the zero pad of the last box must fit the
+            // attention kernel's 6 tiles of 128 keys.
+            const int pad = ((c.capacity + 7) & ~7) - c.capacity;
+            if (7 + (c.window - 1) + (kEncRowsPerGroup - 1) + pad >= 128 * vxk::enc_max_tiles())
+                efail(VXK_STATUS_INVALID_ARGUMENT, "window too large for the encoder attention tiles (max 752)");
+        }
         if (c.dtype != VXK_DTYPE_BF16 && c.dtype != VXK_DTYPE_F16)
             efail(VXK_STATUS_INVALID_ARGUMENT, "encoder dtype must be BF16 or F16");
         p->cfg = c;
@@ -194,6 +233,9 @@ vxk_status vxk_enc_create(const vxk_enc_config * config, vxk_enc_pool ** out) {
         VXK_ECUDA(cudaMalloc(&p->v_ring, ring_bytes));
         VXK_ECUDA(cudaMemset(p->k_ring, 0, ring_bytes));
         VXK_ECUDA(cudaMemset(p->v_ring, 0, ring_bytes));
+        const int64_t rings = (int64_t) c.max_streams * c.n_layers * c.n_heads;
+        encode_ring_map(&p->map_k, p->k_ring, (int32_t) c.dtype, c.capacity, rings);
+        encode_ring_map(&p->map_v, p->v_ring, (int32_t) c.dtype, c.capacity, rings);
         {
             const int32_t half = c.head_dim / 2;
             std::vector<float2> rope((size_t) c.max_position * half);
@@ -371,7 +413,7 @@ vxk_status vxk_enc_layer(vxk_enc_pool * pool, int32_t layer, const float * q, co
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         const vxk::EncParams e = enc_params(pool, layer, q, k, v, out);
         VXK_ECUDA(vxk::launch_enc_append(e, cs));
-        VXK_ECUDA(vxk::launch_enc_attention(e, cs));
+        VXK_ECUDA(vxk::launch_enc_attention(e, pool->map_k, pool->map_v, cs));
     });
 }
 

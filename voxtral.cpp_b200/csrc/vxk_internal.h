@@ -3,6 +3,7 @@
 // vxk_encoder.cu).  Not part of the public ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -199,7 +200,12 @@ struct EncParams {
 };
 
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream);
-cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream);
+// tmk / tmv: 3-D tensor maps {64, capacity, rings} over the K and V rings,
+// 8 x 64 boxes, 128-byte swizzle, zero out-of-bounds fill.
+cudaError_t launch_enc_attention(const EncParams & p, const CUtensorMap & tmk, const CUtensorMap & tmv,
+                                 cudaStream_t stream);
 int enc_smem_bytes();
+// Most 128-key tiles one row group may span (window + 2*7 + capacity pad <= 768).
+int enc_max_tiles();
 
 }  // namespace vxk

@@ -41,7 +41,102 @@ CONFIGS = {
               desc="4B realtime decoder, full 8192-slot sliding rings (steady state: one eviction per step)"),
     "5": dict(layers=30, streams=32, ctx=(8192, 32768), dtype=8, capacity=32768 + 1024,
               desc="3B decoder, q8_0 cache, ctx~U[8192,32768] (streams that fit one GPU)"),
+    "4": dict(kind="encoder", layers=32, streams=128, heads=20, rows=4, window=750, capacity=878, dtype=30,
+              desc="streaming encoder, 128 streams, 20 heads x 64, 4 new rows per 80 ms chunk, "
+                   "750-frame window in an 878-slot bf16 ring (steady state, rings wrapped)"),
 }
+
+
+def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
+    """Config 4: one step = one 80 ms chunk (4 new encoder rows) of every
+    stream through every encoder layer (append + tcgen05 window attention)."""
+    L, S, H, P = cfg["layers"], cfg["streams"], cfg["heads"], cfg["rows"]
+    W, CAP, HDE = cfg["window"], cfg["capacity"], 64
+    pool = vxk.EncPool(device=local, n_layers=L, n_heads=H, head_dim=HDE, window=W, capacity=CAP, max_streams=S,
+                       max_new=CAP - W, dtype=cfg["dtype"], max_position=65536)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    streams = [pool.open_stream() for _ in range(S)]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    fill = CAP - W
+    fq = torch.randn((S * fill, H, HDE), device="cuda", generator=gen) * 0.5
+    fo = torch.empty_like(fq)
+    pos = 0
+    while pos < CAP + 128:  # wrap every ring so each chunk sees a full 750-frame window
+        pool.plan(streams, [fill] * S, sh)
+        for layer in range(L):
+            pool.layer(layer, fq.data_ptr(), fq.data_ptr(), fq.data_ptr(), fo.data_ptr(), sh)
+        pool.commit()
+        pos += fill
+    torch.cuda.synchronize()
+    del fq, fo
+    NSETS = 2
+    qs = torch.randn((NSETS, L, S * P, H, HDE), device="cuda", generator=gen) * 0.5
+    ks = torch.randn((NSETS, L, S * P, H, HDE), device="cuda", generator=gen) * 0.5
+    vs = torch.randn((NSETS, L, S * P, H, HDE), device="cuda", generator=gen) * 0.5
+    out = torch.empty((L, S * P, H, HDE), device="cuda")
+
+    def step(i):
+        pool.plan(streams, [P] * S, sh)
+        st = i % NSETS
+        for layer in range(L):
+            pool.layer(layer, qs[st, layer].data_ptr(), ks[st, layer].data_ptr(), vs[st, layer].data_ptr(),
+                       out[layer].data_ptr(), sh)
+        pool.commit()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    keys = W + P - 1  # union of the chunk's windows
+    per_stream_layer = keys * H * HDE * 2 * 2 + 3 * P * H * HDE * 4 + P * H * HDE * 4 + 2 * P * H * HDE * 2
+    bytes_per_layer = S * per_stream_layer
+    layer_s = (ms / 1000.0) / (args.steps * L)
+    achieved = bytes_per_layer / layer_s / 1e9
+    peak, peak_kind = load_peaks()
+    flops_per_layer = S * H * P * keys * HDE * 2 * 2
+    if rank == 0:
+        line = {
+            "metric": "encoder chunks/s (KV append + windowed attention, 4 rows/chunk)",
+            "value": round(world * S * args.steps / (ms / 1000.0), 1),
+            "unit": "stream-chunks/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 ring, bf16 hi+lo operands, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"config 4: {cfg['desc']}", "layers": L, "streams_per_gpu": S, "heads": H,
+                       "parallelism": f"streams sharded, {S}/GPU, no collective",
+                       "l2": "inputs larger than L2 (window reads per launch >> 126 MB)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": bytes_per_layer,
+                         "avg_layer_us": round(layer_s * 1e6, 2), "kernel": "enc_tc_kernel (+ enc_append_kernel)",
+                         "tensor_tflops": round(flops_per_layer / layer_s / 1e12, 2)},
+            "cpu_baseline": None, "e2e": None,
+            "gpu_launches": int(args.steps * (L * 2 + 0)),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    pool.close()
 
 
 def parse():
@@ -187,8 +282,46 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
     return n_streams * done / el, done, threads, float(np.mean(ctx0))
 
 
+def encoder_cpu_sample(cfg, seed, seconds):
+    """Times the CPU restatement (oracle attention, one thread) of one
+    stream-layer of a config-4 chunk; returns stream-chunks/s for all layers."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    H, P, W = cfg["heads"], cfg["rows"], cfg["window"]
+    keys = W + P - 1
+    kr = vx_oracle.f32_to_bf16_bits(rng.standard_normal((keys, H * 64), dtype=np.float32) * 0.5).view(np.uint8)
+    vr = vx_oracle.f32_to_bf16_bits(rng.standard_normal((keys, H * 64), dtype=np.float32) * 0.5).view(np.uint8)
+    q = rng.standard_normal((H, 64), dtype=np.float32) * 0.5
+    scale = float(np.float32(0.125))
+    done = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for j in range(P):  # the chunk's rows, each over its own window
+            lo = j
+            vx_oracle.attn_row(q, 10000 + j, 1e6, kr[lo:lo + W], vr[lo:lo + W], vx_oracle.BF16, H, scale)
+        done += 1
+    el = time.perf_counter() - t0
+    return done / el / cfg["layers"], done
+
+
 def run_reference(args, cfg, rank, world):
     if rank != 0:
+        return
+    if cfg.get("kind") == "encoder":
+        cps, done = encoder_cpu_sample(cfg, args.seed, 20.0)
+        line = {"impl": "reference", "metric": "encoder chunks/s (KV append + windowed attention, 4 rows/chunk)",
+                "value": round(cps, 4), "unit": "stream-chunks/s", "n_gpus": args.gpus, "steps": done,
+                "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16 ring, fp64 accumulate", "data": "synthetic",
+                "config": {"workload": f"config {args.config}: {cfg['desc']}", "layers": cfg["layers"]},
+                "cpu_baseline": {"value": round(cps, 4), "unit": "stream-chunks/s", "cores": 1, "kind": "port",
+                                 "sample": f"{done} stream-layer chunks of the oracle's window attention, "
+                                           f"one thread, scaled to {cfg['layers']} layers"},
+                "e2e": {"value": round(cps, 4), "unit": "stream-chunks/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     n_streams = 4
     budget = 150.0
@@ -243,6 +376,13 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
     import vxk
+
+    if cfg.get("kind") == "encoder":
+        run_encoder(args, cfg, world, rank, local, dist, torch, vxk)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     L, S = cfg["layers"], cfg["streams"]
     dtype = cfg["dtype"]

@@ -8,8 +8,10 @@ layer, through libvxk.so's C ABI).  Default workload = BASELINE config 2:
 heads x 128), f16 cache in 16-token pages with a seeded random block table,
 contexts seeded uniform in [400, 4096].  Synthetic N(0, 0.5^2) activations.
 
-Multi-GPU: one process per GPU (torchrun); each rank owns its own 64 streams
-(weak scaling, no data-path collective); timing is max over ranks.
+Multi-GPU: one process per GPU (torchrun); the job has 64 streams per GPU,
+whose contexts are drawn once from the seed and dealt to ranks by
+longest-processing-time (vxk_shard.assign_streams); each rank owns its streams'
+pages (weak scaling, no data-path collective); timing is max over ranks.
 
 `--impl reference` times the CPU restatement of the same path (the reference's
 ggml CPU backend cannot be built here: ggml is fetched at configure time and
@@ -31,6 +33,7 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "voxtral.cpp_b200"))
+from vxk_shard import assign_streams, max_over_ranks  # noqa: E402
 
 HD, NQ, NKV, BT = 128, 32, 8, 16
 CONFIGS = {
@@ -103,10 +106,7 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(dist, ms, "cuda")
     keys = W + P - 1  # union of the chunk's windows
     per_stream_layer = keys * H * HDE * 2 * 2 + 3 * P * H * HDE * 4 + P * H * HDE * 4 + 2 * P * H * HDE * 2
     bytes_per_layer = S * per_stream_layer
@@ -114,6 +114,68 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
     achieved = bytes_per_layer / layer_s / 1e9
     peak, peak_kind = load_peaks()
     flops_per_layer = S * H * P * keys * HDE * 2 * 2
+    traffic_ratio, traffic_src = load_traffic(args.config)
+
+    # ---- end to end: per step, pinned host q/k/v of every layer go up on a
+    # copy stream (layer l's copy overlaps layer l-1's kernels), the layers
+    # run through the public vxk_enc_layer call, and the outputs come back.
+    e2e = None
+    if not args.no_e2e:
+        hq = torch.randn((L, S * P, H, HDE)).mul_(0.5).pin_memory()
+        hk = torch.randn((L, S * P, H, HDE)).mul_(0.5).pin_memory()
+        hv = torch.randn((L, S * P, H, HDE)).mul_(0.5).pin_memory()
+        ho = torch.empty((L, S * P, H, HDE)).pin_memory()
+        dq, dk, dv = (torch.empty_like(hq, device="cuda") for _ in range(3))
+        copy_stream = torch.cuda.Stream()
+        up = [torch.cuda.Event() for _ in range(L)]
+        done_ev = [torch.cuda.Event() for _ in range(L)]
+
+        def host_step():
+            pool.plan(streams, [P] * S, sh)
+            copy_stream.wait_stream(stream)
+            with torch.cuda.stream(copy_stream):
+                for layer in range(L):
+                    dq[layer].copy_(hq[layer], non_blocking=True)
+                    dk[layer].copy_(hk[layer], non_blocking=True)
+                    dv[layer].copy_(hv[layer], non_blocking=True)
+                    up[layer].record(copy_stream)
+            for layer in range(L):
+                stream.wait_event(up[layer])
+                pool.layer(layer, dq[layer].data_ptr(), dk[layer].data_ptr(), dv[layer].data_ptr(),
+                           out[layer].data_ptr(), sh)
+                done_ev[layer].record(stream)
+            with torch.cuda.stream(copy_stream):
+                for layer in range(L):
+                    copy_stream.wait_event(done_ev[layer])
+                    ho[layer].copy_(out[layer], non_blocking=True)
+            stream.wait_stream(copy_stream)
+            pool.commit()
+
+        host_step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        f0.record(stream)
+        for _ in range(args.steps):
+            host_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = f0.elapsed_time(f1)
+        ems = max_over_ranks(dist, ems, "cuda")
+        e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "stream-chunks/s",
+               "h2d_bytes_per_step": int(hq.numel() + hk.numel() + hv.numel()) * 4,
+               "d2h_bytes_per_step": int(ho.numel()) * 4, "ms_per_step": round(ems / args.steps, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cps, done = encoder_cpu_sample(cfg, args.seed, args.cpu_seconds)
+        cpu = {"value": round(cps, 4), "unit": "stream-chunks/s", "cores": 1, "kind": "port",
+               "sample": f"{done} stream-layer chunks ({P} rows x {H} heads over a {W}-frame window) of the "
+                         f"oracle's window attention on one host thread, scaled to {L} layers"}
+    if dist:
+        dist.barrier()
     if rank == 0:
         line = {
             "metric": "encoder chunks/s (KV append + windowed attention, 4 rows/chunk)",
@@ -128,10 +190,13 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
                        "l2": "inputs larger than L2 (window reads per launch >> 126 MB)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_layer),
+                         "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
+                                                           f"scaled to this launch)",
                          "algorithmic_bytes_per_launch": bytes_per_layer,
                          "avg_layer_us": round(layer_s * 1e6, 2), "kernel": "enc_tc_kernel (+ enc_append_kernel)",
                          "tensor_tflops": round(flops_per_layer / layer_s / 1e12, 2)},
-            "cpu_baseline": None, "e2e": None,
+            "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(args.steps * (L * 2 + 0)),
             "clocks": clocks.summary(),
         }
@@ -171,16 +236,30 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
+TRAFFIC_PROFILES = {
+    "2": "decode_kernel_f16_config2.md",
+    "3": "decode_kernel_f16_config2.md",   # same kernel and page format; ratio scaled to config 3
+    "5": "decode_kernel_q8_0_config5.md",
+    "4": "enc_tc_kernel_config4.md",
+}
+
+
 def load_traffic(config: str):
-    """Per-launch DRAM bytes of decode_kernel from a committed ncu summary,
-    as bytes per algorithmic byte (scaled to this run's launches), or None."""
-    p = ROOT / "profiles" / f"decode_kernel_config{config}.traffic.json"
-    if not p.exists():
-        return None
-    try:
-        return float(json.loads(p.read_text())["dram_bytes_per_algorithmic_byte"])
-    except Exception:
-        return None
+    """DRAM bytes per algorithmic byte of the dominant kernel, read from the
+    `dram_bytes_per_algorithmic_byte:` line of its committed ncu summary
+    (dram__bytes_read.sum + dram__bytes_write.sum of one captured launch over
+    that launch's algorithmic bytes).  Returns (ratio, file) or (None, None)."""
+    name = TRAFFIC_PROFILES.get(config)
+    p = ROOT / "profiles" / name if name else None
+    if p is None or not p.exists():
+        return None, None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_algorithmic_byte:"):
+            try:
+                return float(line.split(":", 1)[1]), f"profiles/{name}"
+            except ValueError:
+                break
+    return None, None
 
 
 class ClockSampler:
@@ -386,9 +465,12 @@ def main():
 
     L, S = cfg["layers"], cfg["streams"]
     dtype = cfg["dtype"]
-    rng = np.random.default_rng(args.seed + 1000 * rank)
+    # Contexts of the whole job are drawn once from the seed, then every rank
+    # takes its S streams by longest-processing-time on context length.
+    rng = np.random.default_rng(args.seed)
     lo, hi = cfg["ctx"]
-    ctx0 = rng.integers(lo, hi + 1, size=S)
+    ctx_all = rng.integers(lo, hi + 1, size=S * world)
+    ctx0 = ctx_all[assign_streams(ctx_all, world, S)[rank]]
     total_steps = args.warmup + args.steps * (1 if args.no_e2e else 2) + 2
     cap = cfg["capacity"]
     need_pos = int(ctx0.max()) + total_steps + BT
@@ -467,10 +549,7 @@ def main():
     pool.sync(sh)
     launches = pool.stats().kernel_launches - launches0
     ms = start.elapsed_time(end)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(dist, ms, "cuda")
     value = world * S * args.steps / (ms / 1000.0)
 
     # ---- roofline of the dominant kernel (decode_kernel) --------------------
@@ -481,11 +560,13 @@ def main():
     # in it (the small plan upload per step is charged to them too).
     avg_launch_s = (ms / 1000.0) / (args.steps * L)
     achieved = bytes_per_launch / avg_launch_s / 1e9
-    traffic_ratio = load_traffic(args.config)
+    traffic_ratio, traffic_src = load_traffic(args.config)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "frac_of_nominal_8000": round(achieved / 8000.0, 4),
                 "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_launch),
+                "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
+                                                  f"scaled to this launch)",
                 "algorithmic_bytes_per_launch": round(bytes_per_launch),
                 "avg_launch_us": round(avg_launch_s * 1e6, 2), "kernel": "decode_kernel<f16>" if dtype == 1 else
                 "decode_kernel<q8_0>"}
@@ -509,10 +590,7 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize()
         ems = e0.elapsed_time(e1)
-        if dist:
-            t = torch.tensor([ems], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
+        ems = max_over_ranks(dist, ems, "cuda")
         e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": int(hq.numel() + hk.numel() + hv.numel()) * 4,
                "d2h_bytes_per_step": int(ho.numel()) * 4, "ms_per_step": round(ems / args.steps, 3)}

@@ -6,23 +6,31 @@
 //                      (src/voxtral.cpp:2480-2487, mask of
 //                      src/voxtral.cpp:4104-4119), scale 1/sqrt(64), on the
 //                      5th-generation tensor cores (tcgen05.mma, TMEM
-//                      accumulators) fed by TMA tensor copies.
+//                      accumulators) fed by TMA bulk copies.
 //
-// Ring layout: [stream][layer][head][capacity][64] 16-bit, one (stream,
-// layer, head) ring = capacity x 128-byte rows.  A TMA tensor map views all
-// rings as a 3-D tensor {64, capacity, rings}; boxes of 8 slots x 64 dims land
-// in shared memory in the 128-byte-swizzled canonical layout the tensor
-// cores read.  The window is walked in boxes through a virtual ring of
-// round_up(capacity, 8) slots: slots past the real capacity read as zeros
-// (TMA out-of-bounds fill) and are masked.
+// Ring layout: [stream][layer][head][ring_slots][64] 16-bit, ring_slots =
+// round_up(capacity, 8); the pad slots stay zero.  Rows are stored
+// pre-swizzled: the 16-byte chunk c of slot s sits at chunk c ^ (s & 7).  A
+// run of slots that starts at a multiple of 8 therefore lands, by a plain
+// 1-D bulk copy into a 1024-byte-aligned buffer, in exactly the 128-byte
+// swizzled K-major layout the tensor cores read, and a 128-key tile is one
+// bulk copy (two where it crosses the end of the ring) instead of sixteen
+// tensor-map boxes.
 //
-// One CTA = one (row group, head), 5 warps:
-//   warp 4     TMA producer and tcgen05.mma issuer (one elected lane)
+// Work unit = (row group, head).  Persistent CTAs, one per SM, walk their
+// units through a warp-specialised pipeline (7 warps):
+//   warp 4     TMA producer: 16 KB stages (128 keys of K or V) into a
+//              10-stage shared-memory ring
+//   warp 5     tcgen05.mma issuer (one lane)
+//   warp 6     Q^T producer (RoPE, scale, bf16 hi/lo split)
 //   warps 0-3  own TMEM lane quadrants 0-3: softmax and epilogue
-// Two phases, exact softmax (no online rescaling):
+// Per unit, two phases with an exact softmax (no online rescaling):
 //   S^T[key][query] = K . Q^T   (M=128 keys per tile, N=8 queries, K=64)
 //   softmax over all keys of the window, P^T to shared memory
 //   O^T[dim][query] += V^T . P^T (M=64 dims, N=8, K=128 keys per tile)
+// Q, S, P and O are double-buffered by unit parity, so the tensor cores
+// compute unit i+1's scores while the softmax warps work on unit i, and the
+// ring keeps up to 160 KB of K/V reads in flight per SM.
 // bf16 operands carry 8 mantissa bits, so Q and P are each split into a bf16
 // high part and the bf16 residual (x = hi + lo) and both parts are
 // multiplied; products accumulate in fp32.
@@ -37,23 +45,38 @@ namespace vxk {
 namespace {
 
 constexpr int kEncHd = 64;
-constexpr int kTcThreads = 160;
-constexpr int kTcStages = 4;
+constexpr int kTcThreads = 224;         // 7 warps
+constexpr int kTcStages = 10;
 constexpr int kTcMaxTiles = 6;          // keys per group <= 6 x 128
 constexpr int kTcBoxes = 16;            // 8-slot boxes per 128-key tile
 constexpr int kTcStageBytes = 16384;    // 128 keys x 128 B
+constexpr int kTmemCols = 128;          // S^T 2 x 48 columns, O^T 2 x 8 columns
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 constexpr unsigned kFull = 0xffffffffu;
 
 // shared-memory map (offsets from a 1024-aligned base)
 constexpr int kOffStage = 0;
-constexpr int kOffQ = kTcStages * kTcStageBytes;                 // Q^T hi, lo: 2 x 1 KB
-constexpr int kOffP = kOffQ + 2048;                              // P^T hi, lo: tiles x 2 x 2 KB
-constexpr int kOffBar = kOffP + kTcMaxTiles * 2 * 2048;
-constexpr int kNumBars = 2 * kTcStages + 4;                      // full, mma, q, s, p, o
-constexpr int kOffMisc = kOffBar + kNumBars * 8;                 // tmem addr, abort
-constexpr int kOffRed = kOffMisc + 16;                           // [2][4 warps][8]
-constexpr int kTcSmem = kOffRed + 2 * 4 * 8 * 4 + 1024;          // + alignment slack
+constexpr int kOffQ = kTcStages * kTcStageBytes;                 // Q^T [2 sets][hi, lo] x 1 KB
+constexpr int kPBuf = kTcMaxTiles * 2 * 2048;                    // P^T [tiles][hi, lo] x 2 KB
+constexpr int kOffP = kOffQ + 2 * 2048;                          // 2 sets of kPBuf
+constexpr int kOffBar = kOffP + 2 * kPBuf;
+// mbarrier indices
+constexpr int kBarFull = 0;                    // stage landed (TMA tx count)
+constexpr int kBarEmpty = kTcStages;           // stage consumed (tcgen05.commit)
+constexpr int kBarQFull = 2 * kTcStages;       // [2] Q^T written
+constexpr int kBarQEmpty = kBarQFull + 2;      // [2] S MMAs done reading Q^T
+constexpr int kBarSFull = kBarQEmpty + 2;      // [2] S^T complete in TMEM
+constexpr int kBarSEmpty = kBarSFull + 2;      // [2] S^T read by the softmax warps
+constexpr int kBarPFull = kBarSEmpty + 2;      // [2] P^T written
+constexpr int kBarPEmpty = kBarPFull + 2;      // [2] PV MMAs done reading P^T
+constexpr int kBarOFull = kBarPEmpty + 2;      // [2] O^T complete in TMEM
+constexpr int kBarOEmpty = kBarOFull + 2;      // [2] O^T read by the epilogue
+constexpr int kBarDrain = kBarOEmpty + 2;      // all MMAs of the CTA done
+constexpr int kNumBars = kBarDrain + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;                 // tmem addr, abort flag
+constexpr int kOffRed = kOffMisc + 16;                           // max [4][8], sums [2][4][8]
+constexpr int kTcSmem = kOffRed + (32 + 64) * 4 + 1024;          // + alignment slack
+static_assert(kTcSmem <= 232448, "encoder attention exceeds 227 KB of shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -100,14 +123,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
     }
 }
 
-// 3-D TMA tile load (no multicast) into shared memory, counted on an mbarrier.
-__device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * map, int c0, int c1, int c2,
-                                            uint64_t * bar) {
+// 1-D bulk copy global -> shared (no multicast), completion counted on an
+// mbarrier; each ring row is read once per layer: evict-first in L2.
+__device__ __forceinline__ void bulk_load(void * dst, const void * src, uint32_t bytes, uint64_t * bar,
+                                          uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -202,67 +232,115 @@ __global__ void enc_append_kernel(const EncParams p) {
         const int64_t src = ((int64_t) r * p.n_heads + h) * kEncHd + 2 * i;
         const float2 kx = enc_rope_pair(*reinterpret_cast<const float2 *>(p.k + src), cs[i]);
         const float2 vx = *reinterpret_cast<const float2 *>(p.v + src);
-        const int64_t dst = (ring_index(p, rd.stream, h) * p.capacity + rd.slot) * kEncHd + 2 * i;
-        reinterpret_cast<uint32_t *>(p.k_ring)[dst / 2] = pack2<DT>(kx.x, kx.y);
-        reinterpret_cast<uint32_t *>(p.v_ring)[dst / 2] = pack2<DT>(vx.x, vx.y);
+        // byte 4i of the row = chunk i / 4, stored at chunk (i / 4) ^ (slot & 7)
+        const int64_t row = ring_index(p, rd.stream, h) * p.ring_slots + rd.slot;
+        const int64_t dst = row * (kEncHd * 2) + ((((i >> 2) ^ (rd.slot & 7))) << 4) + (i & 3) * 4;
+        *reinterpret_cast<uint32_t *>(p.k_ring + dst) = pack2<DT>(kx.x, kx.y);
+        *reinterpret_cast<uint32_t *>(p.v_ring + dst) = pack2<DT>(vx.x, vx.y);
     }
 }
 
+// Bounded wait on an mbarrier phase shared by the kernel's roles: gives up
+// when another role has raised the CTA's abort flag, or after kTcWaitNs, in
+// which case it raises the flag and sets the device error word.
+__device__ __forceinline__ bool enc_wait(uint64_t * bar, uint32_t parity, volatile int32_t * abort_flag,
+                                         int32_t * err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kTcWaitNs) {
+            *abort_flag = 1;
+            if (err) atomicCAS(err, 0, 2);
+            return false;
+        }
+    }
+}
+
+// Bounded wait that ignores the abort flag: used to let copies and MMAs that
+// are already in flight finish before the CTA exits.
+__device__ __forceinline__ void enc_drain(uint64_t * bar, uint32_t parity) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - t0 > kTcWaitNs) return;
+    }
+}
+
+// One unit of work: the rows of one group (<= 8 new frames of one stream) and
+// one head, attending the union of their windows, walked as nb 8-slot boxes
+// from slot s0 of the virtual ring, in T tiles of 16 boxes.
+struct EncUnit {
+    int r0, nr, h, ws, we, s0, nb, T;
+    int64_t ring;  // ring index (stream, layer, head)
+};
+
+__device__ __forceinline__ EncUnit enc_unit(const EncParams & p, int u, int vslots) {
+    EncUnit U;
+    const int grp = u / p.n_heads;
+    U.h = u - grp * p.n_heads;
+    U.r0 = p.group_first[grp];
+    U.nr = p.group_first[grp + 1] - U.r0;
+    const EncRowDesc first = p.rows[U.r0];
+    const EncRowDesc last = p.rows[U.r0 + U.nr - 1];
+    U.ring = ring_index(p, first.stream, U.h);
+    U.ws = first.win_start;
+    U.we = last.pos;
+    U.s0 = (U.ws % p.capacity) & ~7;
+    U.nb = (((U.we % p.capacity) - U.s0 + vslots) % vslots) / 8 + 1;
+    U.T = (U.nb + kTcBoxes - 1) / kTcBoxes;  // host guarantees T <= kTcMaxTiles
+    return U;
+}
+
+// Persistent, warp-specialised window attention.  CTA b handles units b,
+// b + gridDim.x, ...; unit i of a CTA uses buffer set i & 1 of Q, S, P and O,
+// so that unit i+1's S = K.Q^T runs on the tensor cores while the softmax
+// warps work on unit i.  Stage order through the shared-memory ring:
+// K(0), K(1), V(0), K(2), V(1), ..., V(last).
 template <int DT>
-__global__ void __launch_bounds__(kTcThreads) enc_tc_kernel(const __grid_constant__ CUtensorMap tmk,
-                                                            const __grid_constant__ CUtensorMap tmv,
-                                                            const EncParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t * base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * stages = base + kOffStage;
-    uint8_t * qt = base + kOffQ;
-    uint8_t * pt = base + kOffP;
-    uint64_t * full = reinterpret_cast<uint64_t *>(base + kOffBar);
-    uint64_t * mmab = full + kTcStages;
-    uint64_t * q_bar = mmab + kTcStages;
-    uint64_t * s_bar = q_bar + 1;
-    uint64_t * p_bar = q_bar + 2;
-    uint64_t * o_bar = q_bar + 3;
+    uint8_t * qbuf = base + kOffQ;
+    uint8_t * pbuf = base + kOffP;
+    uint64_t * bars = reinterpret_cast<uint64_t *>(base + kOffBar);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(base + kOffMisc);
-    int32_t * abort_flag = reinterpret_cast<int32_t *>(base + kOffMisc + 4);
-    float * red = reinterpret_cast<float *>(base + kOffRed);  // [2][4][8]
+    volatile int32_t * abort_flag = reinterpret_cast<volatile int32_t *>(base + kOffMisc + 4);
+    float * redmax = reinterpret_cast<float *>(base + kOffRed);  // [4 warps][8]
+    float * redsum = redmax + 32;                                // [2 sets][4 warps][8]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const int grp = blockIdx.x / p.n_heads;
-    const int h = blockIdx.x % p.n_heads;
-    if (grp >= p.n_groups) return;
-    const int r0 = p.group_first[grp];
-    const int nr = p.group_first[grp + 1] - r0;  // <= 8 rows
-    const EncRowDesc first = p.rows[r0];
-    const EncRowDesc last = p.rows[r0 + nr - 1];
-    const int ring = (int) ring_index(p, first.stream, h);
     const int cap = p.capacity;
-    const int vslots = (cap + 7) & ~7;           // virtual ring of whole boxes
-    const int ws = first.win_start;
-    const int we = last.pos;
-    const int s0 = (ws % cap) & ~7;               // first box slot
-    const int nb = (((we % cap) - s0 + vslots) % vslots) / 8 + 1;
-    const int T = (nb + kTcBoxes - 1) / kTcBoxes; // host guarantees T <= kTcMaxTiles
-    constexpr uint32_t fmt = DT == 30 ? 1u : 0u;  // BF16 / F16 operands
-    const uint32_t idesc_qk = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 17) | (8u << 24);
-    const uint32_t idesc_pv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 17) | (4u << 24);
+    const int vslots = p.ring_slots;  // round_up(capacity, 8): the ring walked in whole boxes
+    const int n_units = p.n_groups * p.n_heads;
+    const int stride = (int) gridDim.x;
+    if ((int) blockIdx.x >= n_units) return;
 
     if (tid == 0) {
         for (int s = 0; s < kTcStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&mmab[s], 1);
+            mbar_init(&bars[kBarFull + s], 1);
+            mbar_init(&bars[kBarEmpty + s], 1);
         }
-        mbar_init(q_bar, 128);
-        mbar_init(s_bar, 1);
-        mbar_init(p_bar, 128);
-        mbar_init(o_bar, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars[kBarQFull + b], 1);
+            mbar_init(&bars[kBarQEmpty + b], 1);
+            mbar_init(&bars[kBarSFull + b], 1);
+            mbar_init(&bars[kBarSEmpty + b], 128);
+            mbar_init(&bars[kBarPFull + b], 128);
+            mbar_init(&bars[kBarPEmpty + b], 1);
+            mbar_init(&bars[kBarOFull + b], 1);
+            mbar_init(&bars[kBarOEmpty + b], 128);
+        }
+        mbar_init(&bars[kBarDrain], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 4) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" ::"r"(smem_u32(tmem_slot))
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -270,208 +348,287 @@ __global__ void __launch_bounds__(kTcThreads) enc_tc_kernel(const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t s_tmem = tmem;        // S^T tile t in columns 8t .. 8t+7
-    const uint32_t o_tmem = tmem + 48;   // O^T in columns 48 .. 55
+    // TMEM columns: S^T of set b, tile t at 48b + 8t; O^T of set b at 96 + 8b.
 
     if (warp == 4) {
-        // ---------------- producer / MMA issuer ----------------
+        // ---------------- TMA producer ----------------
         if (lane == 0) {
-            const int nloads = 2 * T;  // K tiles, then V tiles
-            auto issue = [&](int L) {
-                const bool is_v = L >= T;
-                const int t = is_v ? L - T : L;
-                const int st = L % kTcStages;
+            uint32_t c = 0;
+            bool ok = true;
+            const uint64_t policy = evict_first_policy();
+            constexpr int kRowBytes = kEncHd * 2;
+            auto load = [&](const EncUnit & U, bool is_v, int t) -> bool {
+                const int st = (int) (c % kTcStages);
+                if (!enc_wait(&bars[kBarEmpty + st], ((c / kTcStages) & 1) ^ 1, abort_flag, p.error)) return false;
                 uint8_t * dst = stages + st * kTcStageBytes;
-                mbar_expect_tx(&full[st], kTcStageBytes);
-#pragma unroll 1
-                for (int b = 0; b < kTcBoxes; ++b) {
-                    const int gb = t * kTcBoxes + b;
-                    const int slot = gb < nb ? (s0 + 8 * gb) % vslots : 0;
-                    tma_load_3d(dst + b * 1024, is_v ? &tmv : &tmk, 0, slot, ring, &full[st]);
+                const uint8_t * ring = (is_v ? p.v_ring : p.k_ring) + U.ring * vslots * kRowBytes;
+                mbar_expect_tx(&bars[kBarFull + st], kTcStageBytes);
+                // 128 consecutive slots from s0 + 128 t, wrapping at the ring's end
+                // (rows past the window are read and masked)
+                int slot = (U.s0 + 128 * t) % vslots;
+                int done = 0;
+                while (done < 128) {
+                    const int n = min(128 - done, vslots - slot);
+                    bulk_load(dst + done * kRowBytes, ring + (int64_t) slot * kRowBytes, (uint32_t) (n * kRowBytes),
+                              &bars[kBarFull + st], policy);
+                    done += n;
+                    slot = 0;
                 }
+                ++c;
+                return true;
             };
-            int issued = 0;
-            while (issued < nloads && issued < kTcStages) issue(issued++);
-            bool ok = mbar_wait(q_bar, 0);
-            tc_fence_after();
-            int L = 0;
-            for (; ok && L < nloads; ++L) {
-                const int st = L % kTcStages;
-                if (L == T) {
-                    ok = mbar_wait(p_bar, 0);
+            EncUnit prev{};
+            bool have_prev = false;
+            for (int u = blockIdx.x; ok && u < n_units; u += stride) {
+                const EncUnit U = enc_unit(p, u, vslots);
+                for (int t = 0; ok && t < U.T; ++t) ok = load(U, false, t);
+                for (int t = 0; ok && have_prev && t < prev.T; ++t) ok = load(prev, true, t);
+                prev = U;
+                have_prev = true;
+            }
+            for (int t = 0; ok && have_prev && t < prev.T; ++t) ok = load(prev, true, t);
+            if (!ok || *abort_flag) {
+                // let every issued copy land before the CTA exits
+                for (uint32_t d = c > (uint32_t) kTcStages ? c - kTcStages : 0; d < c; ++d)
+                    enc_drain(&bars[kBarFull + d % kTcStages], (d / kTcStages) & 1);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ---------------- tcgen05.mma issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t fmt = DT == 30 ? 1u : 0u;  // BF16 / F16 operands
+            const uint32_t idesc_qk = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 17) | (8u << 24);
+            const uint32_t idesc_pv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 17) | (4u << 24);
+            uint32_t c = 0;
+            auto s_unit = [&](const EncUnit & U, int i) -> bool {
+                const int b = i & 1;
+                const uint32_t k = (uint32_t) (i >> 1) & 1;
+                if (!enc_wait(&bars[kBarQFull + b], k, abort_flag, p.error)) return false;
+                if (!enc_wait(&bars[kBarSEmpty + b], k ^ 1, abort_flag, p.error)) return false;
+                tc_fence_after();
+                const uint32_t qa = smem_u32(qbuf + b * 2048);
+                const uint32_t sd = tmem + 48 * b;
+                for (int t = 0; t < U.T; ++t) {
+                    const int st = (int) (c % kTcStages);
+                    if (!enc_wait(&bars[kBarFull + st], (c / kTcStages) & 1, abort_flag, p.error)) return false;
                     tc_fence_after();
-                    if (!ok) break;
-                }
-                if (!mbar_wait(&full[st], (L / kTcStages) & 1)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t sa = smem_u32(stages + st * kTcStageBytes);
-                if (L < T) {
-                    // S^T tile L = K . (Q_hi + Q_lo)^T
+                    const uint32_t sa = smem_u32(stages + st * kTcStageBytes);
+                    // S^T tile t = K . (Q_hi + Q_lo)^T
 #pragma unroll
                     for (int part = 0; part < 2; ++part) {
 #pragma unroll
                         for (int ks = 0; ks < 4; ++ks) {
-                            tc_mma(s_tmem + 8 * L, sw128_desc(sa + ks * 32, 16, 1024),
-                                   sw128_desc(smem_u32(qt + part * 1024) + ks * 32, 16, 1024), idesc_qk,
-                                   (part | ks) != 0);
+                            tc_mma(sd + 8 * t, sw128_desc(sa + ks * 32, 16, 1024),
+                                   sw128_desc(qa + part * 1024 + ks * 32, 16, 1024), idesc_qk, (part | ks) != 0);
                         }
                     }
-                } else {
+                    tc_commit(&bars[kBarEmpty + st]);
+                    ++c;
+                }
+                tc_commit(&bars[kBarQEmpty + b]);
+                tc_commit(&bars[kBarSFull + b]);
+                return true;
+            };
+            auto pv_unit = [&](const EncUnit & U, int i) -> bool {
+                const int b = i & 1;
+                const uint32_t k = (uint32_t) (i >> 1) & 1;
+                if (!enc_wait(&bars[kBarPFull + b], k, abort_flag, p.error)) return false;
+                if (!enc_wait(&bars[kBarOEmpty + b], k ^ 1, abort_flag, p.error)) return false;
+                tc_fence_after();
+                const uint32_t pa = smem_u32(pbuf + b * kPBuf);
+                const uint32_t od = tmem + 96 + 8 * b;
+                for (int t = 0; t < U.T; ++t) {
+                    const int st = (int) (c % kTcStages);
+                    if (!enc_wait(&bars[kBarFull + st], (c / kTcStages) & 1, abort_flag, p.error)) return false;
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(stages + st * kTcStageBytes);
                     // O^T += V^T . (P_hi + P_lo)^T for tile t
-                    const int t = L - T;
 #pragma unroll
                     for (int part = 0; part < 2; ++part) {
-                        const uint32_t pb = smem_u32(pt + (t * 2 + part) * 2048);
+                        const uint32_t pb = pa + (t * 2 + part) * 2048;
 #pragma unroll
                         for (int ks = 0; ks < 8; ++ks) {
-                            tc_mma(o_tmem, sw128_desc(sa + ks * 2048, 16, 1024),
+                            tc_mma(od, sw128_desc(sa + ks * 2048, 16, 1024),
                                    sw128_desc(pb + (ks >> 2) * 1024 + (ks & 3) * 32, 16, 1024), idesc_pv,
                                    (t | part | ks) != 0);
                         }
                     }
+                    tc_commit(&bars[kBarEmpty + st]);
+                    ++c;
                 }
-                tc_commit(&mmab[st]);
-                if (L == T - 1) tc_commit(s_bar);
-                if (L == nloads - 1) tc_commit(o_bar);
-                if (issued < nloads) {
-                    // refill this stage once the MMAs reading it are done
-                    if (!mbar_wait(&mmab[st], (L / kTcStages) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    issue(issued++);
-                }
+                tc_commit(&bars[kBarPEmpty + b]);
+                tc_commit(&bars[kBarOFull + b]);
+                return true;
+            };
+            bool ok = true;
+            EncUnit prev{};
+            int i = 0;
+            for (int u = blockIdx.x; ok && u < n_units; u += stride, ++i) {
+                const EncUnit U = enc_unit(p, u, vslots);
+                ok = s_unit(U, i);
+                if (ok && i > 0) ok = pv_unit(prev, i - 1);
+                prev = U;
             }
-            if (!ok) {
-                *abort_flag = 1;
-                if (p.error) atomicCAS(p.error, 0, 2);
-                // wake the consumers, then drain the copies not yet consumed
-                tc_commit(s_bar);
-                tc_commit(o_bar);
-                for (int l = L; l < issued; ++l) mbar_wait(&full[l % kTcStages], (l / kTcStages) & 1);
-            }
+            if (ok && i > 0) pv_unit(prev, i - 1);
+            // every MMA issued so far completes before the CTA frees TMEM
+            tc_commit(&bars[kBarDrain]);
+            enc_drain(&bars[kBarDrain], 0);
         }
         __syncwarp();
+    } else if (warp == 6) {
+        // ---------------- Q^T (hi, lo) producer ----------------
+        // 8 query rows x 64 dims per unit, rotated, scaled by log2(e)/sqrt(64),
+        // 128-byte swizzled K-major rows.  Lane l handles dims 2l, 2l+1.
+        int i = 0;
+        for (int u = blockIdx.x; u < n_units; u += stride, ++i) {
+            const EncUnit U = enc_unit(p, u, vslots);
+            const int b = i & 1;
+            const uint32_t k = (uint32_t) (i >> 1) & 1;
+            if (!__all_sync(kFull, enc_wait(&bars[kBarQEmpty + b], k ^ 1, abort_flag, p.error))) break;
+            uint8_t * qb = qbuf + b * 2048;
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+                float2 qv = make_float2(0.0f, 0.0f);
+                if (j < U.nr) {
+                    const EncRowDesc rd = p.rows[U.r0 + j];
+                    const float2 x =
+                        *reinterpret_cast<const float2 *>(p.q + ((int64_t) (U.r0 + j) * p.n_heads + U.h) * kEncHd + 2 * lane);
+                    const float2 rr = enc_rope_pair(x, p.rope[(int64_t) rd.pos * (kEncHd / 2) + lane]);
+                    qv = make_float2(rr.x * p.scale_log2, rr.y * p.scale_log2);
+                }
+                const uint16_t hx = to16<DT>(qv.x), hy = to16<DT>(qv.y);
+                const uint16_t lx = to16<DT>(qv.x - from16<DT>(hx)), ly = to16<DT>(qv.y - from16<DT>(hy));
+                const int off = j * 128 + (((lane >> 2) ^ j) << 4) + (lane & 3) * 4;
+                *reinterpret_cast<uint32_t *>(qb + off) = (uint32_t) hx | ((uint32_t) hy << 16);
+                *reinterpret_cast<uint32_t *>(qb + 1024 + off) = (uint32_t) lx | ((uint32_t) ly << 16);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[kBarQFull + b]);
+        }
     } else {
-        // ---------------- softmax / epilogue warps 0-3 ----------------
-        // Q^T (hi, lo): 8 rows x 64 dims, 128-byte swizzled K-major rows.
-        for (int idx = tid; idx < 8 * 32; idx += 128) {
-            const int j = idx >> 5;
-            const int i = idx & 31;  // pair: dims 2i, 2i+1
-            float2 qv = make_float2(0.0f, 0.0f);
-            if (j < nr) {
-                const EncRowDesc rd = p.rows[r0 + j];
-                const float2 x = *reinterpret_cast<const float2 *>(p.q + ((int64_t) (r0 + j) * p.n_heads + h) * kEncHd + 2 * i);
-                const float2 rr = enc_rope_pair(x, p.rope[(int64_t) rd.pos * (kEncHd / 2) + i]);
-                qv = make_float2(rr.x * p.scale_log2, rr.y * p.scale_log2);
-            }
-            const uint16_t hx = to16<DT>(qv.x), hy = to16<DT>(qv.y);
-            const uint16_t lx = to16<DT>(qv.x - from16<DT>(hx)), ly = to16<DT>(qv.y - from16<DT>(hy));
-            const int off = j * 128 + (((i >> 2) ^ j) << 4) + (i & 3) * 4;
-            *reinterpret_cast<uint32_t *>(qt + off) = (uint32_t) hx | ((uint32_t) hy << 16);
-            *reinterpret_cast<uint32_t *>(qt + 1024 + off) = (uint32_t) lx | ((uint32_t) ly << 16);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(q_bar);
-
-        float sv[kTcMaxTiles][8];
-        const bool have_s = mbar_wait(s_bar, 0);
-        tc_fence_after();
+        // ---------------- softmax and epilogue, warps 0-3 ----------------
+        // Thread r owns key row r of every tile (TMEM lane r).  The loop never
+        // leaves early, so the named barriers stay matched; after an abort
+        // every wait returns at once and no result is written.
         const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
-#pragma unroll
-        for (int t = 0; t < kTcMaxTiles; ++t) {
-            if (t < T) tmem_ld8(s_tmem + lane_off + 8 * t, sv[t]);
-        }
-        int qpos[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) qpos[j] = j < nr ? p.rows[r0 + j].pos : -1;
-        const int r = 32 * warp + lane;  // key row within a tile
-        float mx[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx[j] = -INFINITY;
-#pragma unroll
-        for (int t = 0; t < kTcMaxTiles; ++t) {
-            if (t >= T) break;
-            const int gb = t * kTcBoxes + (r >> 3);
-            const int slot = (s0 + 8 * gb) % vslots + (r & 7);
-            bool valid = have_s && !*abort_flag && gb < nb && slot < cap;
-            const int kp = we - (((we % cap) - slot + cap) % cap);
-            valid = valid && kp >= ws;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const bool ok = valid && j < nr && kp <= qpos[j] && kp >= qpos[j] - (p.window - 1);
-                sv[t][j] = ok ? sv[t][j] : -INFINITY;
-                mx[j] = fmaxf(mx[j], sv[t][j]);
+        const int r = 32 * warp + lane;
+        auto epilogue = [&](const EncUnit & U, int j) {
+            const int b = j & 1;
+            const uint32_t k = (uint32_t) (j >> 1) & 1;
+            const bool have_o = __all_sync(kFull, enc_wait(&bars[kBarOFull + b], k, abort_flag, p.error));
+            tc_fence_after();
+            float ov[8];
+            if (have_o) tmem_ld8(tmem + 96 + 8 * b + lane_off, ov);
+            tc_fence_before();
+            mbar_arrive(&bars[kBarOEmpty + b]);
+            if (have_o && !*abort_flag && lane < 16) {
+                const int dim = 16 * warp + lane;  // M=64 accumulator rows sit in lanes 0-15 of each quadrant
+                const float * ls = redsum + b * 32;
+                for (int q = 0; q < U.nr; ++q) {
+                    const float L = ls[q] + ls[8 + q] + ls[16 + q] + ls[24 + q];
+                    p.out[((int64_t) (U.r0 + q) * p.n_heads + U.h) * kEncHd + dim] = ov[q] / L;
+                }
             }
-        }
-        // per-query max over the 128 consumer threads
+        };
+        EncUnit prev{};
+        int i = 0;
+        for (int u = blockIdx.x; u < n_units; u += stride, ++i) {
+            const EncUnit U = enc_unit(p, u, vslots);
+            const int b = i & 1;
+            const uint32_t k = (uint32_t) (i >> 1) & 1;
+            float sv[kTcMaxTiles][8];
+            const bool have_s = __all_sync(kFull, enc_wait(&bars[kBarSFull + b], k, abort_flag, p.error));
+            tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) mx[j] = fmaxf(mx[j], __shfl_xor_sync(kFull, mx[j], o));
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) red[warp * 8 + j] = mx[j];
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        float M[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            M[j] = fmaxf(fmaxf(red[j], red[8 + j]), fmaxf(red[16 + j], red[24 + j]));
-            if (M[j] == -INFINITY) M[j] = 0.0f;  // padding queries
-        }
-        float ls[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ls[j] = 0.0f;
-#pragma unroll
-        for (int t = 0; t < kTcMaxTiles; ++t) {
-            if (t >= T) break;
-            uint8_t * ph = pt + (t * 2) * 2048 + (r >> 6) * 1024;
-            uint8_t * pl = ph + 2048;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float e = exp2f(sv[t][j] - M[j]);
-                const uint16_t hi = to16<DT>(e);
-                const float ehi = from16<DT>(hi);
-                const uint16_t lo = to16<DT>(e - ehi);
-                ls[j] += ehi + from16<DT>(lo);
-                const int off = j * 128 + ((((r & 63) >> 3) ^ j) << 4) + (r & 7) * 2;
-                *reinterpret_cast<uint16_t *>(ph + off) = hi;
-                *reinterpret_cast<uint16_t *>(pl + off) = lo;
+            for (int t = 0; t < kTcMaxTiles; ++t) {
+                if (have_s && t < U.T) tmem_ld8(tmem + 48 * b + lane_off + 8 * t, sv[t]);
             }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(p_bar);
+            tc_fence_before();
+            mbar_arrive(&bars[kBarSEmpty + b]);
+            int qpos[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+            for (int q = 0; q < 8; ++q) qpos[q] = q < U.nr ? p.rows[U.r0 + q].pos : -1;
+            float mx[8];
 #pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) ls[j] += __shfl_xor_sync(kFull, ls[j], o);
-        }
-        if (lane == 0) {
+            for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) red[32 + warp * 8 + j] = ls[j];
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const bool have_o = mbar_wait(o_bar, 0);
-        tc_fence_after();
-        float ov[8];
-        tmem_ld8(o_tmem + lane_off, ov);
-        if (have_o && !*abort_flag && lane < 16) {
-            const int dim = 16 * warp + lane;  // M=64 accumulator rows sit in lanes 0-15 of each quadrant
-            for (int j = 0; j < nr; ++j) {
-                const float L = red[32 + j] + red[40 + j] + red[48 + j] + red[56 + j];
-                p.out[((int64_t) (r0 + j) * p.n_heads + h) * kEncHd + dim] = ov[j] / L;
+            for (int t = 0; t < kTcMaxTiles; ++t) {
+                if (t >= U.T) break;
+                const int gb = t * kTcBoxes + (r >> 3);
+                const int slot = (U.s0 + 8 * gb) % vslots + (r & 7);
+                bool valid = have_s && gb < U.nb && slot < cap;
+                const int kp = U.we - (((U.we % cap) - slot + cap) % cap);
+                valid = valid && kp >= U.ws;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const bool ok = valid && q < U.nr && kp <= qpos[q] && kp >= qpos[q] - (p.window - 1);
+                    sv[t][q] = ok ? sv[t][q] : -INFINITY;
+                    mx[q] = fmaxf(mx[q], sv[t][q]);
+                }
             }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) mx[q] = fmaxf(mx[q], __shfl_xor_sync(kFull, mx[q], o));
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) redmax[warp * 8 + q] = mx[q];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            float M[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                M[q] = fmaxf(fmaxf(redmax[q], redmax[8 + q]), fmaxf(redmax[16 + q], redmax[24 + q]));
+                if (M[q] == -INFINITY) M[q] = 0.0f;  // padding queries
+            }
+            // P of set b is free once the PV MMAs of unit i-2 completed
+            enc_wait(&bars[kBarPEmpty + b], k ^ 1, abort_flag, p.error);
+            float ls[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) ls[q] = 0.0f;
+            uint8_t * pb = pbuf + b * kPBuf;
+#pragma unroll
+            for (int t = 0; t < kTcMaxTiles; ++t) {
+                if (t >= U.T) break;
+                uint8_t * ph = pb + (t * 2) * 2048 + (r >> 6) * 1024;
+                uint8_t * pl = ph + 2048;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float e = exp2f(sv[t][q] - M[q]);
+                    const uint16_t hi = to16<DT>(e);
+                    const float ehi = from16<DT>(hi);
+                    const uint16_t lo = to16<DT>(e - ehi);
+                    ls[q] += ehi + from16<DT>(lo);
+                    const int off = q * 128 + ((((r & 63) >> 3) ^ q) << 4) + (r & 7) * 2;
+                    *reinterpret_cast<uint16_t *>(ph + off) = hi;
+                    *reinterpret_cast<uint16_t *>(pl + off) = lo;
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&bars[kBarPFull + b]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) ls[q] += __shfl_xor_sync(kFull, ls[q], o);
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) redsum[b * 32 + warp * 8 + q] = ls[q];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (i > 0) epilogue(prev, i - 1);
+            prev = U;
         }
+        if (i > 0) epilogue(prev, i - 1);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
 }
 
@@ -491,19 +648,25 @@ cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_enc_attention(const EncParams & p, const CUtensorMap & tmk, const CUtensorMap & tmv,
-                                 cudaStream_t stream) {
+cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream) {
     if (p.n_groups <= 0) return cudaSuccess;
-    const unsigned grid = (unsigned) (p.n_groups * p.n_heads);
-    cudaError_t e;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    // persistent: one CTA per SM (the shared-memory ring allows no second)
+    const int units = p.n_groups * p.n_heads;
+    const unsigned grid = (unsigned) (units < sms ? units : sms);
     if (p.dtype == 30) {
         e = cudaFuncSetAttribute(enc_tc_kernel<30>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
         if (e != cudaSuccess) return e;
-        enc_tc_kernel<30><<<grid, kTcThreads, kTcSmem, stream>>>(tmk, tmv, p);
+        enc_tc_kernel<30><<<grid, kTcThreads, kTcSmem, stream>>>(p);
     } else {
         e = cudaFuncSetAttribute(enc_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
         if (e != cudaSuccess) return e;
-        enc_tc_kernel<1><<<grid, kTcThreads, kTcSmem, stream>>>(tmk, tmv, p);
+        enc_tc_kernel<1><<<grid, kTcThreads, kTcSmem, stream>>>(p);
     }
     return cudaGetLastError();
 }

@@ -16,7 +16,6 @@
 #include <string>
 #include <vector>
 
-#include <cudaTypedefs.h>
 
 namespace {
 
@@ -54,30 +53,10 @@ struct EncPlan {
 // tiles).
 constexpr int kEncRowsPerGroup = 8;
 
-// 3-D tensor map {64 dims, capacity slots, rings} over one ring array, with
-// 8-slot x 64-dim boxes in the 128-byte swizzled layout and zero fill for
-// slots past the capacity.  cuTensorMapEncodeTiled is a driver entry point,
-// reached through the runtime so the library does not link libcuda.
-void encode_ring_map(CUtensorMap * map, void * ring, int32_t dtype, int32_t capacity, int64_t rings) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-        void * fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess || !fn)
-            efail(VXK_STATUS_BACKEND_ERROR, "cuTensorMapEncodeTiled is not available");
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
-    const cuuint64_t dims[3] = {64, (cuuint64_t) capacity, (cuuint64_t) rings};
-    const cuuint64_t strides[2] = {128, (cuuint64_t) capacity * 128};
-    const cuuint32_t box[3] = {64, 8, 1};
-    const cuuint32_t elem[3] = {1, 1, 1};
-    const CUresult r = encode(map, dtype == VXK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                              3, ring, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) efail(VXK_STATUS_BACKEND_ERROR, "cuTensorMapEncodeTiled failed for the encoder ring");
-}
+// Stored rows per ring: the capacity rounded up to whole 8-slot groups (the
+// pad rows stay zero), so that 128-byte swizzled rows of any 8-aligned run of
+// slots form the tensor cores' shared-memory layout after a plain bulk copy.
+int32_t ring_slots_of(int32_t capacity) { return (capacity + 7) & ~7; }
 
 }  // namespace
 
@@ -97,8 +76,7 @@ struct vxk_enc_pool {
     std::vector<EncPlan> plan;
     std::vector<vxk::EncRowDesc> rows;
     std::vector<int32_t> group_first;
-    CUtensorMap map_k{};
-    CUtensorMap map_v{};
+    std::vector<uint8_t> h_read;  // readback staging of vxk_enc_read_slots
     std::string last_error;
 };
 
@@ -158,6 +136,7 @@ vxk::EncParams enc_params(vxk_enc_pool * p, int32_t layer, const float * q, cons
     e.layer = layer;
     e.n_heads = p->cfg.n_heads;
     e.capacity = p->cfg.capacity;
+    e.ring_slots = ring_slots_of(p->cfg.capacity);
     e.window = p->cfg.window;
     e.rows = reinterpret_cast<const vxk::EncRowDesc *>(p->d_stage);
     e.n_rows = (int32_t) p->rows.size();
@@ -228,14 +207,12 @@ vxk_status vxk_enc_create(const vxk_enc_config * config, vxk_enc_pool ** out) {
         VXK_ECUDA(cudaGetDeviceCount(&n_dev));
         if (c.device < 0 || c.device >= n_dev) efail(VXK_STATUS_INVALID_ARGUMENT, "no such CUDA device");
         EncDevice scope(c.device);
-        const size_t ring_bytes = (size_t) c.max_streams * c.n_layers * c.n_heads * (size_t) c.capacity * c.head_dim * 2;
+        const size_t ring_bytes =
+            (size_t) c.max_streams * c.n_layers * c.n_heads * (size_t) ring_slots_of(c.capacity) * c.head_dim * 2;
         VXK_ECUDA(cudaMalloc(&p->k_ring, ring_bytes));
         VXK_ECUDA(cudaMalloc(&p->v_ring, ring_bytes));
         VXK_ECUDA(cudaMemset(p->k_ring, 0, ring_bytes));
         VXK_ECUDA(cudaMemset(p->v_ring, 0, ring_bytes));
-        const int64_t rings = (int64_t) c.max_streams * c.n_layers * c.n_heads;
-        encode_ring_map(&p->map_k, p->k_ring, (int32_t) c.dtype, c.capacity, rings);
-        encode_ring_map(&p->map_v, p->v_ring, (int32_t) c.dtype, c.capacity, rings);
         {
             const int32_t half = c.head_dim / 2;
             std::vector<float2> rope((size_t) c.max_position * half);
@@ -413,7 +390,7 @@ vxk_status vxk_enc_layer(vxk_enc_pool * pool, int32_t layer, const float * q, co
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         const vxk::EncParams e = enc_params(pool, layer, q, k, v, out);
         VXK_ECUDA(vxk::launch_enc_append(e, cs));
-        VXK_ECUDA(vxk::launch_enc_attention(e, pool->map_k, pool->map_v, cs));
+        VXK_ECUDA(vxk::launch_enc_attention(e, cs));
     });
 }
 
@@ -429,15 +406,24 @@ vxk_status vxk_enc_read_slots(vxk_enc_pool * pool, int32_t layer, int32_t stream
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         VXK_ECUDA(cudaStreamSynchronize(cs));
         const size_t row_b = (size_t) c.head_dim * 2;
-        uint8_t * ko = static_cast<uint8_t *>(k_out);
-        uint8_t * vo = static_cast<uint8_t *>(v_out);
-        // out layout [n][n_heads][head_dim]
-        for (int32_t h = 0; h < c.n_heads; ++h) {
-            const size_t base = ((((size_t) stream * c.n_layers + layer) * c.n_heads + h) * (size_t) c.capacity + slot0) * row_b;
-            VXK_ECUDA(cudaMemcpy2D(ko + (size_t) h * row_b, (size_t) c.n_heads * row_b, pool->k_ring + base, row_b, row_b,
-                                   (size_t) n, cudaMemcpyDeviceToHost));
-            VXK_ECUDA(cudaMemcpy2D(vo + (size_t) h * row_b, (size_t) c.n_heads * row_b, pool->v_ring + base, row_b, row_b,
-                                   (size_t) n, cudaMemcpyDeviceToHost));
+        const int32_t rs = ring_slots_of(c.capacity);
+        uint8_t * outs[2] = {static_cast<uint8_t *>(k_out), static_cast<uint8_t *>(v_out)};
+        const uint8_t * rings[2] = {pool->k_ring, pool->v_ring};
+        pool->h_read.resize((size_t) n * row_b);
+        // out layout [n][n_heads][head_dim]; ring rows are stored with the
+        // 16-byte chunk c of slot s at chunk c ^ (s & 7)
+        for (int kv = 0; kv < 2; ++kv) {
+            for (int32_t h = 0; h < c.n_heads; ++h) {
+                const size_t base = ((((size_t) stream * c.n_layers + layer) * c.n_heads + h) * (size_t) rs + slot0) * row_b;
+                VXK_ECUDA(cudaMemcpy(pool->h_read.data(), rings[kv] + base, (size_t) n * row_b, cudaMemcpyDeviceToHost));
+                for (int32_t i = 0; i < n; ++i) {
+                    const int32_t slot = slot0 + i;
+                    const uint8_t * src = pool->h_read.data() + (size_t) i * row_b;
+                    uint8_t * dst = outs[kv] + ((size_t) i * c.n_heads + h) * row_b;
+                    for (size_t ch = 0; ch < row_b / 16; ++ch)
+                        std::memcpy(dst + ch * 16, src + ((ch ^ (size_t) (slot & 7)) * 16), 16);
+                }
+            }
         }
     });
 }

@@ -177,12 +177,13 @@ struct EncRowDesc {
 static_assert(sizeof(EncRowDesc) == 16, "EncRowDesc layout");
 
 struct EncParams {
-    uint8_t * k_ring;       // [max_streams][n_layers][n_heads][capacity][head_dim] 16-bit
+    uint8_t * k_ring;       // [max_streams][n_layers][n_heads][ring_slots][head_dim] 16-bit, rows swizzled
     uint8_t * v_ring;
     int32_t n_layers;
     int32_t layer;
     int32_t n_heads;
-    int32_t capacity;
+    int32_t capacity;       // logical ring capacity (slot = position % capacity)
+    int32_t ring_slots;     // stored rows per ring: round_up(capacity, 8), pad rows zero
     int32_t window;
     const EncRowDesc * rows;
     int32_t n_rows;
@@ -200,10 +201,7 @@ struct EncParams {
 };
 
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream);
-// tmk / tmv: 3-D tensor maps {64, capacity, rings} over the K and V rings,
-// 8 x 64 boxes, 128-byte swizzle, zero out-of-bounds fill.
-cudaError_t launch_enc_attention(const EncParams & p, const CUtensorMap & tmk, const CUtensorMap & tmv,
-                                 cudaStream_t stream);
+cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream);
 int enc_smem_bytes();
 // Most 128-key tiles one row group may span (window + 2*7 + capacity pad <= 768).
 int enc_max_tiles();

@@ -50,14 +50,14 @@ constexpr int kTcStages = 10;
 constexpr int kTcMaxTiles = 6;          // keys per group <= 6 x 128
 constexpr int kTcBoxes = 16;            // 8-slot boxes per 128-key tile
 constexpr int kTcStageBytes = 16384;    // 128 keys x 128 B
-constexpr int kTmemCols = 128;          // S^T 2 x 48 columns, O^T 2 x 8 columns
+constexpr int kTmemCols = 512;          // S^T 2 sets x 96 columns, O^T 2 sets x 4 accumulators x 16
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 constexpr unsigned kFull = 0xffffffffu;
 
 // shared-memory map (offsets from a 1024-aligned base)
 constexpr int kOffStage = 0;
 constexpr int kOffQ = kTcStages * kTcStageBytes;                 // Q^T [2 sets][hi, lo] x 1 KB
-constexpr int kPBuf = kTcMaxTiles * 2 * 2048;                    // P^T [tiles][hi, lo] x 2 KB
+constexpr int kPBuf = kTcMaxTiles * 4096;                        // P^T [tiles][key half][hi, lo] x 1 KB
 constexpr int kOffP = kOffQ + 2 * 2048;                          // 2 sets of kPBuf
 constexpr int kOffBar = kOffP + 2 * kPBuf;
 // mbarrier indices
@@ -167,16 +167,17 @@ __device__ __forceinline__ void tc_commit(uint64_t * bar) {
                  : "memory");
 }
 
-// 32 lanes x 8 columns of 32 bits from TMEM into registers.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
+// 32 lanes x 16 columns of 32 bits from TMEM into registers.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ float2 enc_rope_pair(float2 x, float2 cs) {
@@ -348,7 +349,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // TMEM columns: S^T of set b, tile t at 48b + 8t; O^T of set b at 96 + 8b.
+    // TMEM columns (N = 16: 8 queries' hi parts, then their lo parts):
+    //   S^T of set b, tile t      at 96 b + 16 t
+    //   O^T of set b, accumulator a at 192 + 64 b + 16 a (summed in the epilogue)
 
     if (warp == 4) {
         // ---------------- TMA producer ----------------
@@ -398,8 +401,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
         // ---------------- tcgen05.mma issuer ----------------
         if (lane == 0) {
             constexpr uint32_t fmt = DT == 30 ? 1u : 0u;  // BF16 / F16 operands
-            const uint32_t idesc_qk = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 17) | (8u << 24);
-            const uint32_t idesc_pv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 17) | (4u << 24);
+            // fp32 accumulate, N = 16; S: M = 128, K-major A; PV: M = 64, MN-major A
+            const uint32_t idesc_qk = (1u << 4) | (fmt << 7) | (fmt << 10) | (2u << 17) | (8u << 24);
+            const uint32_t idesc_pv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (2u << 17) | (4u << 24);
             uint32_t c = 0;
             auto s_unit = [&](const EncUnit & U, int i) -> bool {
                 const int b = i & 1;
@@ -408,23 +412,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
                 if (!enc_wait(&bars[kBarSEmpty + b], k ^ 1, abort_flag, p.error)) return false;
                 tc_fence_after();
                 const uint32_t qa = smem_u32(qbuf + b * 2048);
-                const uint32_t sd = tmem + 48 * b;
-                for (int t = 0; t < U.T; ++t) {
-                    const int st = (int) (c % kTcStages);
-                    if (!enc_wait(&bars[kBarFull + st], (c / kTcStages) & 1, abort_flag, p.error)) return false;
+                const uint32_t sd = tmem + 96 * b;
+                // tiles in pairs, their MMAs interleaved so that consecutive
+                // MMAs write different accumulators
+                for (int t = 0; t < U.T; t += 2) {
+                    const bool two = t + 1 < U.T;
+                    const int st0 = (int) (c % kTcStages);
+                    if (!enc_wait(&bars[kBarFull + st0], (c / kTcStages) & 1, abort_flag, p.error)) return false;
+                    const int st1 = (int) ((c + 1) % kTcStages);
+                    if (two && !enc_wait(&bars[kBarFull + st1], ((c + 1) / kTcStages) & 1, abort_flag, p.error))
+                        return false;
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(stages + st * kTcStageBytes);
-                    // S^T tile t = K . (Q_hi + Q_lo)^T
+                    const uint32_t sa0 = smem_u32(stages + st0 * kTcStageBytes);
+                    const uint32_t sa1 = smem_u32(stages + st1 * kTcStageBytes);
+                    // S^T tile = K . [Q_hi; Q_lo]^T
 #pragma unroll
-                    for (int part = 0; part < 2; ++part) {
-#pragma unroll
-                        for (int ks = 0; ks < 4; ++ks) {
-                            tc_mma(sd + 8 * t, sw128_desc(sa + ks * 32, 16, 1024),
-                                   sw128_desc(qa + part * 1024 + ks * 32, 16, 1024), idesc_qk, (part | ks) != 0);
-                        }
+                    for (int ks = 0; ks < 4; ++ks) {
+                        const uint64_t bq = sw128_desc(qa + ks * 32, 16, 1024);
+                        tc_mma(sd + 16 * t, sw128_desc(sa0 + ks * 32, 16, 1024), bq, idesc_qk, ks != 0);
+                        if (two) tc_mma(sd + 16 * (t + 1), sw128_desc(sa1 + ks * 32, 16, 1024), bq, idesc_qk, ks != 0);
                     }
-                    tc_commit(&bars[kBarEmpty + st]);
+                    tc_commit(&bars[kBarEmpty + st0]);
                     ++c;
+                    if (two) {
+                        tc_commit(&bars[kBarEmpty + st1]);
+                        ++c;
+                    }
                 }
                 tc_commit(&bars[kBarQEmpty + b]);
                 tc_commit(&bars[kBarSFull + b]);
@@ -437,22 +450,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
                 if (!enc_wait(&bars[kBarOEmpty + b], k ^ 1, abort_flag, p.error)) return false;
                 tc_fence_after();
                 const uint32_t pa = smem_u32(pbuf + b * kPBuf);
-                const uint32_t od = tmem + 96 + 8 * b;
+                const uint32_t od = tmem + 192 + 64 * b;
                 for (int t = 0; t < U.T; ++t) {
                     const int st = (int) (c % kTcStages);
                     if (!enc_wait(&bars[kBarFull + st], (c / kTcStages) & 1, abort_flag, p.error)) return false;
                     tc_fence_after();
                     const uint32_t sa = smem_u32(stages + st * kTcStageBytes);
-                    // O^T += V^T . (P_hi + P_lo)^T for tile t
+                    // O^T(acc ks % 4) += V^T . [P_hi; P_lo]^T over keys 16 ks .. 16 ks + 15 of tile t
 #pragma unroll
-                    for (int part = 0; part < 2; ++part) {
-                        const uint32_t pb = pa + (t * 2 + part) * 2048;
-#pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) {
-                            tc_mma(od, sw128_desc(sa + ks * 2048, 16, 1024),
-                                   sw128_desc(pb + (ks >> 2) * 1024 + (ks & 3) * 32, 16, 1024), idesc_pv,
-                                   (t | part | ks) != 0);
-                        }
+                    for (int ks = 0; ks < 8; ++ks) {
+                        tc_mma(od + 16 * (ks & 3), sw128_desc(sa + ks * 2048, 16, 1024),
+                               sw128_desc(pa + t * 4096 + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), idesc_pv,
+                               !(t == 0 && ks < 4));
                     }
                     tc_commit(&bars[kBarEmpty + st]);
                     ++c;
@@ -520,7 +529,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             const bool have_o = __all_sync(kFull, enc_wait(&bars[kBarOFull + b], k, abort_flag, p.error));
             tc_fence_after();
             float ov[8];
-            if (have_o) tmem_ld8(tmem + 96 + 8 * b + lane_off, ov);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) ov[q] = 0.0f;
+            if (have_o) {
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    float acc[16];
+                    tmem_ld16(tmem + 192 + 64 * b + 16 * a + lane_off, acc);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) ov[q] += acc[q] + acc[8 + q];
+                }
+            }
             tc_fence_before();
             mbar_arrive(&bars[kBarOEmpty + b]);
             if (have_o && !*abort_flag && lane < 16) {
@@ -543,7 +562,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             tc_fence_after();
 #pragma unroll
             for (int t = 0; t < kTcMaxTiles; ++t) {
-                if (have_s && t < U.T) tmem_ld8(tmem + 48 * b + lane_off + 8 * t, sv[t]);
+                if (have_s && t < U.T) {
+                    float sr[16];
+                    tmem_ld16(tmem + 96 * b + lane_off + 16 * t, sr);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) sv[t][q] = sr[q] + sr[8 + q];
+                }
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarSEmpty + b]);
@@ -593,8 +617,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
 #pragma unroll
             for (int t = 0; t < kTcMaxTiles; ++t) {
                 if (t >= U.T) break;
-                uint8_t * ph = pb + (t * 2) * 2048 + (r >> 6) * 1024;
-                uint8_t * pl = ph + 2048;
+                // B operand rows 0-7 = P_hi of queries 0-7, rows 8-15 = P_lo
+                uint8_t * ph = pb + t * 4096 + (r >> 6) * 2048;
+                uint8_t * pl = ph + 1024;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     const float e = exp2f(sv[t][q] - M[q]);

@@ -50,7 +50,7 @@ constexpr int kTcStages = 10;
 constexpr int kTcMaxTiles = 6;          // keys per group <= 6 x 128
 constexpr int kTcBoxes = 16;            // 8-slot boxes per 128-key tile
 constexpr int kTcStageBytes = 16384;    // 128 keys x 128 B
-constexpr int kTmemCols = 512;          // S^T 2 sets x 96 columns, O^T 2 sets x 4 accumulators x 16
+constexpr int kTmemCols = 512;          // S^T 2 sets x 96 columns, O^T 2 sets x 4 accumulators x 32
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -75,7 +75,8 @@ constexpr int kBarDrain = kBarOEmpty + 2;      // all MMAs of the CTA done
 constexpr int kNumBars = kBarDrain + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;                 // tmem addr, abort flag
 constexpr int kOffRed = kOffMisc + 16;                           // max [4][8], sums [2][4][8]
-constexpr int kTcSmem = kOffRed + (32 + 64) * 4 + 1024;          // + alignment slack
+constexpr int kOffEpi = kOffRed + (32 + 64) * 4;                 // O^T of keys 64-127 [8 queries][64 dims]
+constexpr int kTcSmem = kOffEpi + 8 * 64 * 4 + 1024;             // + alignment slack
 static_assert(kTcSmem <= 232448, "encoder attention exceeds 227 KB of shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
@@ -310,6 +311,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     volatile int32_t * abort_flag = reinterpret_cast<volatile int32_t *>(base + kOffMisc + 4);
     float * redmax = reinterpret_cast<float *>(base + kOffRed);  // [4 warps][8]
     float * redsum = redmax + 32;                                // [2 sets][4 warps][8]
+    float * epi = reinterpret_cast<float *>(base + kOffEpi);     // [8][64]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -351,7 +353,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     const uint32_t tmem = *tmem_slot;
     // TMEM columns (N = 16: 8 queries' hi parts, then their lo parts):
     //   S^T of set b, tile t      at 96 b + 16 t
-    //   O^T of set b, accumulator a at 192 + 64 b + 16 a (summed in the epilogue)
+    //   O^T of set b, accumulator a at 192 + 128 b + 32 a: an M = 128 x N = 32 block whose
+    //   lanes 0-63 x columns 0-15 hold dims 0-63 over keys 0-63 of each tile and lanes
+    //   64-127 x columns 16-31 dims 0-63 over keys 64-127 (the other quarters are unused
+    //   cross products); accumulators and halves are summed in the epilogue
 
     if (warp == 4) {
         // ---------------- TMA producer ----------------
@@ -401,9 +406,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
         // ---------------- tcgen05.mma issuer ----------------
         if (lane == 0) {
             constexpr uint32_t fmt = DT == 30 ? 1u : 0u;  // BF16 / F16 operands
-            // fp32 accumulate, N = 16; S: M = 128, K-major A; PV: M = 64, MN-major A
+            // fp32 accumulate.  S: M = 128 keys, N = 16, K-major A.  PV: M = 128 (dims of
+            // keys 0-63, then dims of keys 64-127: the V tile's two 64-key halves are two
+            // MN atoms 8 KB apart), N = 32, MN-major A.
             const uint32_t idesc_qk = (1u << 4) | (fmt << 7) | (fmt << 10) | (2u << 17) | (8u << 24);
-            const uint32_t idesc_pv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (2u << 17) | (4u << 24);
+            const uint32_t idesc_pv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (4u << 17) | (8u << 24);
             uint32_t c = 0;
             auto s_unit = [&](const EncUnit & U, int i) -> bool {
                 const int b = i & 1;
@@ -450,18 +457,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
                 if (!enc_wait(&bars[kBarOEmpty + b], k ^ 1, abort_flag, p.error)) return false;
                 tc_fence_after();
                 const uint32_t pa = smem_u32(pbuf + b * kPBuf);
-                const uint32_t od = tmem + 192 + 64 * b;
+                const uint32_t od = tmem + 192 + 128 * b;
                 for (int t = 0; t < U.T; ++t) {
                     const int st = (int) (c % kTcStages);
                     if (!enc_wait(&bars[kBarFull + st], (c / kTcStages) & 1, abort_flag, p.error)) return false;
                     tc_fence_after();
                     const uint32_t sa = smem_u32(stages + st * kTcStageBytes);
-                    // O^T(acc ks % 4) += V^T . [P_hi; P_lo]^T over keys 16 ks .. 16 ks + 15 of tile t
+                    // acc ks += [V^T(keys 16ks..) ; V^T(keys 64+16ks..)] . [P^T(keys 16ks..) | P^T(keys 64+16ks..)]
+                    // B rows: P_hi, P_lo of keys 16ks.., then P_hi, P_lo of keys 64+16ks.. (8 rows each)
 #pragma unroll
-                    for (int ks = 0; ks < 8; ++ks) {
-                        tc_mma(od + 16 * (ks & 3), sw128_desc(sa + ks * 2048, 16, 1024),
-                               sw128_desc(pa + t * 4096 + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), idesc_pv,
-                               !(t == 0 && ks < 4));
+                    for (int ks = 0; ks < 4; ++ks) {
+                        tc_mma(od + 32 * ks, sw128_desc(sa + ks * 2048, 8192, 1024),
+                               sw128_desc(pa + t * 4096 + ks * 32, 16, 1024), idesc_pv, t != 0);
                     }
                     tc_commit(&bars[kBarEmpty + st]);
                     ++c;
@@ -531,25 +538,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             float ov[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) ov[q] = 0.0f;
+            const int half = warp >> 1;  // lanes 0-63: keys 0-63 of each tile; lanes 64-127: keys 64-127
             if (have_o) {
 #pragma unroll
                 for (int a = 0; a < 4; ++a) {
                     float acc[16];
-                    tmem_ld16(tmem + 192 + 64 * b + 16 * a + lane_off, acc);
+                    tmem_ld16(tmem + 192 + 128 * b + 32 * a + 16 * half + lane_off, acc);
 #pragma unroll
                     for (int q = 0; q < 8; ++q) ov[q] += acc[q] + acc[8 + q];
                 }
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarOEmpty + b]);
-            if (have_o && !*abort_flag && lane < 16) {
-                const int dim = 16 * warp + lane;  // M=64 accumulator rows sit in lanes 0-15 of each quadrant
+            const int dim = 32 * (warp & 1) + lane;
+            if (half) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) epi[q * 64 + dim] = ov[q];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (!half && have_o && !*abort_flag) {
                 const float * ls = redsum + b * 32;
                 for (int q = 0; q < U.nr; ++q) {
                     const float L = ls[q] + ls[8 + q] + ls[16 + q] + ls[24 + q];
-                    p.out[((int64_t) (U.r0 + q) * p.n_heads + U.h) * kEncHd + dim] = ov[q] / L;
+                    p.out[((int64_t) (U.r0 + q) * p.n_heads + U.h) * kEncHd + dim] = (ov[q] + epi[q * 64 + dim]) / L;
                 }
             }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // epi is rewritten by the next epilogue
         };
         EncUnit prev{};
         int i = 0;

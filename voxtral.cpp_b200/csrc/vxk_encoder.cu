@@ -25,9 +25,11 @@
 //   warp 6     Q^T producer (RoPE, scale, bf16 hi/lo split)
 //   warps 0-3  own TMEM lane quadrants 0-3: softmax and epilogue
 // Per unit, two phases with an exact softmax (no online rescaling):
-//   S^T[key][query] = K . Q^T   (M=128 keys per tile, N=8 queries, K=64)
+//   S^T[key][query] = K . Q^T    (M=128 keys per tile, N=16 = 8 queries x
+//                                 {hi, lo}, K=64 dims: 4 MMAs per tile)
 //   softmax over all keys of the window, P^T to shared memory
-//   O^T[dim][query] += V^T . P^T (M=64 dims, N=8, K=128 keys per tile)
+//   O^T[dim][query] += V^T . P^T (per tile 4 MMAs of M=128 = the dims of
+//                                 keys 0-63 and of keys 64-127, N=32, K=16)
 // Q, S, P and O are double-buffered by unit parity, so the tensor cores
 // compute unit i+1's scores while the softmax warps work on unit i, and the
 // ring keeps up to 160 KB of K/V reads in flight per SM.
@@ -112,16 +114,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
-}
-
-// Bounded wait on an mbarrier phase; false after kTcWaitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kTcWaitNs) return false;
-    }
 }
 
 // 1-D bulk copy global -> shared (no multicast), completion counted on an
@@ -224,6 +216,11 @@ __device__ __forceinline__ int64_t ring_index(const EncParams & p, int stream, i
 // One CTA per row; thread t < 32*n_heads handles one (head, pair).
 template <int DT>
 __global__ void enc_append_kernel(const EncParams p) {
+    // Launched with programmatic stream serialization: wait for the previous
+    // grid (whatever produced k/v) before reading anything, then let the
+    // attention launch start its prologue.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int r = blockIdx.x;
     if (r >= p.n_rows) return;
     const EncRowDesc rd = p.rows[r];
@@ -351,6 +348,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Launched with programmatic stream serialization: only the barrier setup
+    // and the TMEM allocation above overlap the previous grid; every global
+    // read (rows, q, the rings the append kernel just wrote) comes after this.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // TMEM columns (N = 16: 8 queries' hi parts, then their lo parts):
     //   S^T of set b, tile t      at 96 b + 16 t
     //   O^T of set b, accumulator a at 192 + 128 b + 32 a: an M = 128 x N = 32 block whose
@@ -677,14 +679,28 @@ int enc_smem_bytes() { return kTcSmem; }
 
 int enc_max_tiles() { return kTcMaxTiles; }
 
+// Both encoder kernels wait (griddepcontrol.wait) before reading anything an
+// earlier grid may write, so they are always launched with programmatic
+// stream serialization: their launch and prologue overlap the previous grid.
+template <typename K>
+cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t stream, const EncParams & p) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream) {
     if (p.n_rows <= 0) return cudaSuccess;
-    if (p.dtype == 30) {
-        enc_append_kernel<30><<<p.n_rows, 256, 0, stream>>>(p);
-    } else {
-        enc_append_kernel<1><<<p.n_rows, 256, 0, stream>>>(p);
-    }
-    return cudaGetLastError();
+    if (p.dtype == 30) return launch_pdl(enc_append_kernel<30>, (unsigned) p.n_rows, 256, 0, stream, p);
+    return launch_pdl(enc_append_kernel<1>, (unsigned) p.n_rows, 256, 0, stream, p);
 }
 
 cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream) {
@@ -701,13 +717,12 @@ cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream) {
     if (p.dtype == 30) {
         e = cudaFuncSetAttribute(enc_tc_kernel<30>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
         if (e != cudaSuccess) return e;
-        enc_tc_kernel<30><<<grid, kTcThreads, kTcSmem, stream>>>(p);
+        return launch_pdl(enc_tc_kernel<30>, grid, kTcThreads, kTcSmem, stream, p);
     } else {
         e = cudaFuncSetAttribute(enc_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
         if (e != cudaSuccess) return e;
-        enc_tc_kernel<1><<<grid, kTcThreads, kTcSmem, stream>>>(p);
+        return launch_pdl(enc_tc_kernel<1>, grid, kTcThreads, kTcSmem, stream, p);
     }
-    return cudaGetLastError();
 }
 
 }  // namespace vxk

@@ -130,7 +130,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, uint6
     }
 }
 
-// 1-D bulk copy global -> shared (no multicast), completion counted on an
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on an
 // mbarrier.  The K/V stream is read once per launch: evict-first in L2.
 __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar,
                                          uint64_t policy) {

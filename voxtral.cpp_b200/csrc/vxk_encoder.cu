@@ -116,7 +116,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     return ok != 0;
 }
 
-// 1-D bulk copy global -> shared (no multicast), completion counted on an
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on an
 // mbarrier; each ring row is read once per layer: evict-first in L2.
 __device__ __forceinline__ void bulk_load(void * dst, const void * src, uint32_t bytes, uint64_t * bar,
                                           uint64_t policy) {

@@ -536,15 +536,14 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
             } else {
                 const int row = mrow + ((mi & 1) << 3);
                 const __half2 * dv = reinterpret_cast<const __half2 *>(sv + TILE);
+                // P as rounded for the row sum, x128 (exact) to keep P * d in the
+                // f16 normal range; the block scale is folded in with one f16 rounding
+                const __half2 p01s = __hmul2(p01, __float2half2_rn(128.0f));
+                const __half2 p89s = __hmul2(p89, __float2half2_rn(128.0f));
 #pragma unroll
                 for (int blk = 0; blk < 4; ++blk) {
-                    // fold the block scale (x128, exact) into the probabilities
-                    const float2 d01 = __half22float2(dv[(blk * kBlockTokens + 2 * c) >> 1]);
-                    const float2 d89 = __half22float2(dv[(blk * kBlockTokens + 8 + 2 * c) >> 1]);
-                    const uint32_t b0 =
-                        h2_bits(__floats2half2_rn(pr[0] * d01.x * 128.0f, pr[1] * d01.y * 128.0f));
-                    const uint32_t b1 =
-                        h2_bits(__floats2half2_rn(pr[2] * d89.x * 128.0f, pr[3] * d89.y * 128.0f));
+                    const uint32_t b0 = h2_bits(__hmul2(p01s, dv[(blk * kBlockTokens + 2 * c) >> 1]));
+                    const uint32_t b1 = h2_bits(__hmul2(p89s, dv[(blk * kBlockTokens + 8 + 2 * c) >> 1]));
                     uint32_t w0, w1, w2, w3;
                     ldsm_x4_t(vbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
                     w0 ^= 0x80808080u;

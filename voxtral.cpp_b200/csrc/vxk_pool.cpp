@@ -308,9 +308,10 @@ int32_t alloc_page(vxk_pool * p, int32_t stream, int32_t entry) {
     return pg;
 }
 
-int32_t pow2_floor(int64_t x) {
+// Smallest power of two >= x (x >= 1).
+int32_t pow2_ceil(int64_t x) {
     int32_t r = 1;
-    while ((int64_t) r * 2 <= x && r < (1 << 30)) r *= 2;
+    while ((int64_t) r < x && r < (1 << 30)) r *= 2;
     return r;
 }
 
@@ -331,11 +332,14 @@ void build_items(vxk_pool * p) {
     if (const char * env = std::getenv("VXK_CHUNK_PAGES")) cp = std::atoi(env);
     if (cp <= 0) {
         // A split pays a fixed prologue (descriptor, block-table and first-copy
-        // latency) and epilogue (merge, partials), so splits are made as large
-        // as load balance allows: about one wave of the resident decode CTAs,
-        // launched longest first so the short ones fill the tail.
+        // latency) and epilogue (partials written, read back and combined by
+        // the row's last CTA), so splits are made as large as load balance
+        // allows: at most about one wave of the resident decode CTAs' worth
+        // of pages each (rounded up to a power of two), launched longest first
+        // so the short ones fill the tail.  For 64 streams of <= 4096 tokens
+        // this leaves every (stream, kv head) unsplit.
         const int64_t slots = std::max<int64_t>(1, p->decode_slots);
-        cp = pow2_floor(std::max<int64_t>(1, total_pages * p->cfg.n_kv_heads / slots));
+        cp = pow2_ceil(std::max<int64_t>(1, (total_pages * p->cfg.n_kv_heads + slots - 1) / slots));
     }
     cp = std::min(cp, vxk::kMaxSplitPages);
     while (true) {

@@ -132,6 +132,11 @@ struct vxk_pool {
     size_t off_items = 0;
     size_t off_sched = 0;            // [n_ctas + 1] offsets, then the unit list
     size_t off_updates = 0;
+    // offsets of the current plan's regions, packed so that one small copy
+    // carries exactly the bytes the batch uses (each <= the static offset)
+    size_t cur_items = 0;
+    size_t cur_sched = 0;
+    size_t cur_updates = 0;
     int64_t device_bytes = 0;
 
     std::vector<StreamState> streams;
@@ -435,20 +440,24 @@ void upload_plan(vxk_pool * p, cudaStream_t stream) {
     const size_t items_b = p->items.size() * sizeof(vxk::WorkItem);
     const size_t upd_b = p->updates.size() * sizeof(vxk::TableUpdate);
     if (p->updates.size() > (size_t) p->max_updates) fail(VXK_STATUS_INTERNAL_ERROR, "too many table updates");
+    const size_t sched_b = p->sched.size() * sizeof(int32_t);
+    p->cur_items = align_up(rows_b, 256);
+    p->cur_sched = p->cur_items + align_up(items_b, 256);
+    p->cur_updates = p->cur_sched + align_up(sched_b, 256);
     const int idx = p->stage_next;
     VXK_CUDA(cudaEventSynchronize(p->stage_ev[idx]));
     uint8_t * h = p->h_stage[idx];
     std::memcpy(h, p->rows.data(), rows_b);
-    std::memcpy(h + p->off_items, p->items.data(), items_b);
-    std::memcpy(h + p->off_sched, p->sched.data(), p->sched.size() * sizeof(int32_t));
-    if (upd_b) std::memcpy(h + p->off_updates, p->updates.data(), upd_b);
-    const size_t n = upd_b ? p->off_updates + upd_b : p->off_sched + p->sched.size() * sizeof(int32_t);
+    std::memcpy(h + p->cur_items, p->items.data(), items_b);
+    std::memcpy(h + p->cur_sched, p->sched.data(), sched_b);
+    if (upd_b) std::memcpy(h + p->cur_updates, p->updates.data(), upd_b);
+    const size_t n = p->cur_updates + upd_b;
     VXK_CUDA(cudaMemcpyAsync(p->d_stage, h, n, cudaMemcpyHostToDevice, stream));
     VXK_CUDA(cudaEventRecord(p->stage_ev[idx], stream));
     p->stage_next ^= 1;
     if (!p->updates.empty()) ++p->launches;
     VXK_CUDA(vxk::launch_table_updates(p->d_table,
-                                       reinterpret_cast<const vxk::TableUpdate *>(p->d_stage + p->off_updates),
+                                       reinterpret_cast<const vxk::TableUpdate *>(p->d_stage + p->cur_updates),
                                        (int32_t) p->updates.size(), stream));
 }
 
@@ -465,8 +474,8 @@ vxk::DecodeParams decode_params(vxk_pool * p, int32_t layer, const float * q, co
     d.bt_cap = p->bt_cap;
     d.block_table = p->d_table;
     d.rows = reinterpret_cast<const vxk::RowDesc *>(p->d_stage);
-    d.items = reinterpret_cast<const vxk::WorkItem *>(p->d_stage + p->off_items);
-    d.sched_offsets = reinterpret_cast<const int32_t *>(p->d_stage + p->off_sched);
+    d.items = reinterpret_cast<const vxk::WorkItem *>(p->d_stage + p->cur_items);
+    d.sched_offsets = reinterpret_cast<const int32_t *>(p->d_stage + p->cur_sched);
     d.sched_units = d.sched_offsets + p->n_ctas + 1;
     d.n_ctas = p->n_ctas;
     d.n_rows = (int32_t) p->rows.size();

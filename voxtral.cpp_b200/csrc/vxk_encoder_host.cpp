@@ -70,7 +70,8 @@ struct vxk_enc_pool {
     uint8_t * h_stage = nullptr;
     cudaEvent_t stage_ev = nullptr;
     size_t stage_bytes = 0;
-    size_t off_groups = 0;
+    size_t off_groups = 0;   // capacity of the row region
+    size_t cur_groups = 0;   // the current batch's group table, right after its rows
     std::vector<EncStream> streams;
     bool planned = false;
     std::vector<EncPlan> plan;
@@ -140,7 +141,7 @@ vxk::EncParams enc_params(vxk_enc_pool * p, int32_t layer, const float * q, cons
     e.window = p->cfg.window;
     e.rows = reinterpret_cast<const vxk::EncRowDesc *>(p->d_stage);
     e.n_rows = (int32_t) p->rows.size();
-    e.group_first = reinterpret_cast<const int32_t *>(p->d_stage + p->off_groups);
+    e.group_first = reinterpret_cast<const int32_t *>(p->d_stage + p->cur_groups);
     e.n_groups = (int32_t) p->group_first.size() - 1;
     e.q = q;
     e.k = k;
@@ -347,9 +348,11 @@ vxk_status vxk_enc_batch_plan(vxk_enc_pool * pool, const int32_t * stream_ids, c
         EncDevice scope(c.device);
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         VXK_ECUDA(cudaEventSynchronize(pool->stage_ev));
-        std::memcpy(pool->h_stage, pool->rows.data(), pool->rows.size() * sizeof(vxk::EncRowDesc));
-        std::memcpy(pool->h_stage + pool->off_groups, pool->group_first.data(), pool->group_first.size() * sizeof(int32_t));
-        VXK_ECUDA(cudaMemcpyAsync(pool->d_stage, pool->h_stage, pool->off_groups + pool->group_first.size() * sizeof(int32_t),
+        const size_t rows_b = pool->rows.size() * sizeof(vxk::EncRowDesc);
+        pool->cur_groups = (rows_b + 255) / 256 * 256;  // <= off_groups: one copy of the used bytes
+        std::memcpy(pool->h_stage, pool->rows.data(), rows_b);
+        std::memcpy(pool->h_stage + pool->cur_groups, pool->group_first.data(), pool->group_first.size() * sizeof(int32_t));
+        VXK_ECUDA(cudaMemcpyAsync(pool->d_stage, pool->h_stage, pool->cur_groups + pool->group_first.size() * sizeof(int32_t),
                                   cudaMemcpyHostToDevice, cs));
         VXK_ECUDA(cudaEventRecord(pool->stage_ev, cs));
         pool->planned = true;

@@ -321,9 +321,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, warmup=0):
+def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, warmup=0, dtype=1):
     """Times the CPU restatement (oracle/vx_cpu_step.c) of the same decode
-    step on all host cores.  Returns (tokens/s, steps done, threads)."""
+    step on all host cores, for an f16 (1) or q8_0 (8) cache.  Returns
+    (tokens/s, steps done, threads, mean context)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import vx_oracle
 
@@ -331,10 +332,19 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
     ctx0 = rng.integers(ctx_range[0], ctx_range[1] + 1, size=n_streams)
     total = (steps or 0) + warmup + 64
     cap = int(ctx0.max()) + total + 16
-    shape = (n_streams, layers, NKV, cap, HD)
-    block = (rng.standard_normal(1 << 22).astype(np.float32) * 0.5).astype(np.float16).view(np.uint16)
-    kc = np.resize(block, int(np.prod(shape))).reshape(shape)
-    vc = np.resize(block[::-1], int(np.prod(shape))).reshape(shape)
+    if dtype == 8:
+        # rows of ggml q8_0 blocks (34 B per 32 values), tiled from quantized noise
+        row_b = HD // 32 * 34
+        shape = (n_streams, layers, NKV, cap, row_b)
+        src = (rng.standard_normal(1 << 20).astype(np.float32) * 0.5)
+        block = np.ascontiguousarray(vx_oracle.quantize_q8_0(src), dtype=np.uint8).reshape(-1)
+        kc = np.resize(block, int(np.prod(shape))).reshape(shape)
+        vc = np.resize(block, int(np.prod(shape))).reshape(shape)
+    else:
+        shape = (n_streams, layers, NKV, cap, HD)
+        block = (rng.standard_normal(1 << 22).astype(np.float32) * 0.5).astype(np.float16).view(np.uint16)
+        kc = np.resize(block, int(np.prod(shape))).reshape(shape).view(np.uint8)
+        vc = np.resize(block[::-1], int(np.prod(shape))).reshape(shape).view(np.uint8)
     q = rng.standard_normal((n_streams, layers, NQ, HD), dtype=np.float32) * 0.5
     k = rng.standard_normal((n_streams, layers, NKV, HD), dtype=np.float32) * 0.5
     v = rng.standard_normal((n_streams, layers, NKV, HD), dtype=np.float32) * 0.5
@@ -344,12 +354,12 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
     threads = os.cpu_count() or 1
     scale = float(np.float32(1.0 / np.sqrt(HD)))
     for _ in range(warmup):
-        vx_oracle.cpu_decode_step_f16(kc, vc, q, k, v, pos, win, rope, scale, threads)
+        vx_oracle.cpu_decode_step(dtype, kc, vc, q, k, v, pos, win, rope, scale, threads)
         pos += 1
     done = 0
     t0 = time.perf_counter()
     while True:
-        vx_oracle.cpu_decode_step_f16(kc, vc, q, k, v, pos, win, rope, scale, threads)
+        vx_oracle.cpu_decode_step(dtype, kc, vc, q, k, v, pos, win, rope, scale, threads)
         pos += 1
         done += 1
         el = time.perf_counter() - t0
@@ -359,6 +369,12 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
             break
     el = time.perf_counter() - t0
     return n_streams * done / el, done, threads, float(np.mean(ctx0))
+
+
+def cpu_streams(dtype: int) -> int:
+    """Streams in the CPU sample: 4, or 2 for the q8_0 config whose contexts
+    (up to 32K positions x 30 layers) would otherwise need > 8 GB of host memory."""
+    return 2 if dtype == 8 else 4
 
 
 def encoder_cpu_sample(cfg, seed, seconds):
@@ -402,10 +418,10 @@ def run_reference(args, cfg, rank, world):
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
-    n_streams = 4
+    n_streams = cpu_streams(cfg["dtype"])
     budget = 150.0
     tps, done, threads, mean_ctx = cpu_sample(cfg["layers"], n_streams, cfg["ctx"], args.seed, seconds=budget,
-                                              steps=args.steps, warmup=min(args.warmup, 3))
+                                              steps=args.steps, warmup=min(args.warmup, 3), dtype=cfg["dtype"])
     line = {
         "impl": "reference",
         "metric": "decode tokens/s (KV append+GQA attn)",
@@ -418,7 +434,7 @@ def run_reference(args, cfg, rank, world):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f16 cache, fp32 accumulate",
+        "dtype": ("q8_0" if cfg["dtype"] == 8 else "f16") + " cache, fp32 accumulate",
         "data": "synthetic",
         "config": {"workload": f"config {args.config}: {cfg['desc']}", "layers": cfg["layers"],
                    "streams_sampled": n_streams, "mean_ctx": mean_ctx},
@@ -597,11 +613,12 @@ def main():
                "d2h_bytes_per_step": int(ho.numel()) * 4, "ms_per_step": round(ems / args.steps, 3)}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and dtype == 1:
-        tps, done, threads, mean_ctx = cpu_sample(L, 4, cfg["ctx"], args.seed, seconds=args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ns = cpu_streams(dtype)
+        tps, done, threads, mean_ctx = cpu_sample(L, ns, cfg["ctx"], args.seed, seconds=args.cpu_seconds, dtype=dtype)
         cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"4 streams (ctx~U{list(cfg['ctx'])}, mean {mean_ctx:.0f}) x {L} layers x {done} steps, "
-                         f"oracle/vx_cpu_step.c on {threads} host threads"}
+               "sample": f"{ns} streams (ctx~U{list(cfg['ctx'])}, mean {mean_ctx:.0f}) x {L} layers x {done} steps, "
+                         f"{'q8_0' if dtype == 8 else 'f16'} cache, oracle/vx_cpu_step.c on {threads} host threads"}
 
     if dist:
         dist.barrier()

@@ -9,6 +9,9 @@
  * fp32 online-softmax accumulation of ggml's CPU flash-attention loop
  * (running max M, running sum S, rescale on a new max), so it is a fair
  * multi-core CPU speed reference for src/voxtral.cpp:2629-2887.
+ * The cache rows are f16 (ggml type 1) or q8_0 (ggml type 8: blocks of an
+ * f16 scale and 32 int8, quantized on append by vxo_quantize_row_q8_0 and
+ * dequantized on read).
  * Parallel over (stream, kv head) work items inside a layer, with a barrier
  * between layers, like ggml's per-op thread split.
  */
@@ -30,11 +33,28 @@ static inline float h2f(uint16_t h) {
 static inline float h2f(uint16_t h) { return vxo_f16_to_f32(h); }
 #endif
 
+/* RoPE mode 0 on head_dim/2 adjacent pairs with each product and sum rounded
+ * on its own (as vx_oracle.c and ggml's CPU rope), even though the rest of
+ * this file is compiled with contraction for speed. */
+__attribute__((noinline, optimize("fp-contract=off"))) static void rope_rotate(const float * x,
+                                                                                const float * cs, int32_t hd,
+                                                                                float * y) {
+    for (int32_t i = 0; i < hd / 2; ++i) {
+        const float c = cs[2 * i], sn = cs[2 * i + 1];
+        const float x0 = x[2 * i], x1 = x[2 * i + 1];
+        const float a = x0 * c, b = x1 * sn, e = x0 * sn, f = x1 * c;
+        y[2 * i] = a - b;
+        y[2 * i + 1] = e + f;
+    }
+}
+
 typedef struct step_args {
     int32_t n_streams, n_layers, n_q, n_kv, hd;
     int64_t cap;
-    uint16_t * kc;
-    uint16_t * vc;
+    int32_t dtype;      /* VXO_F16 or VXO_Q8_0 */
+    int64_t row_bytes;  /* bytes of one kv head's row in the cache */
+    uint8_t * kc;
+    uint8_t * vc;
     const float * q;
     const float * k;
     const float * v;
@@ -59,23 +79,26 @@ static void do_item(const step_args * a, int32_t layer, int32_t s, int32_t kvh) 
     const int64_t p_new = a->pos[s];
     const float * cs = a->rope + (p_new < a->rope_rows ? p_new : 0) * hd;
     const int64_t base = (((int64_t) s * a->n_layers + layer) * a->n_kv + kvh) * a->cap;
-    uint16_t * kc = a->kc + base * hd;
-    uint16_t * vc = a->vc + base * hd;
+    uint8_t * kc = a->kc + base * a->row_bytes;
+    uint8_t * vc = a->vc + base * a->row_bytes;
     const int64_t sl = (int64_t) s * a->n_layers + layer;
+    const int q8 = a->dtype == VXO_Q8_0;
 
-    /* append: rotate K at p_new, round both rows to f16 at slot p_new % cap */
+    /* append: rotate K at p_new, store both rows (f16 RNE or q8_0) at slot p_new % cap */
     {
         const float * kr = a->k + (sl * a->n_kv + kvh) * hd;
         const float * vr = a->v + (sl * a->n_kv + kvh) * hd;
-        uint16_t * kd = kc + (p_new % a->cap) * hd;
-        uint16_t * vd = vc + (p_new % a->cap) * hd;
-        for (int32_t i = 0; i < hd / 2; ++i) {
-            const float c = cs[2 * i], sn = cs[2 * i + 1];
-            const float x0 = kr[2 * i], x1 = kr[2 * i + 1];
-            kd[2 * i] = vxo_f32_to_f16(x0 * c - x1 * sn);
-            kd[2 * i + 1] = vxo_f32_to_f16(x0 * sn + x1 * c);
+        uint8_t * kd = kc + (p_new % a->cap) * a->row_bytes;
+        uint8_t * vd = vc + (p_new % a->cap) * a->row_bytes;
+        float kx[256];
+        rope_rotate(kr, cs, hd, kx);
+        if (q8) {
+            vxo_quantize_row_q8_0(kx, hd, kd);
+            vxo_quantize_row_q8_0(vr, hd, vd);
+        } else {
+            for (int32_t i = 0; i < hd; ++i) ((uint16_t *) kd)[i] = vxo_f32_to_f16(kx[i]);
+            for (int32_t i = 0; i < hd; ++i) ((uint16_t *) vd)[i] = vxo_f32_to_f16(vr[i]);
         }
-        for (int32_t i = 0; i < hd; ++i) vd[i] = vxo_f32_to_f16(vr[i]);
     }
 
     float qr[8][256];
@@ -83,22 +106,22 @@ static void do_item(const step_args * a, int32_t layer, int32_t s, int32_t kvh) 
     float M[8], S[8];
     for (int32_t g = 0; g < group; ++g) {
         const float * qh = a->q + (sl * a->n_q + kvh * group + g) * hd;
-        for (int32_t i = 0; i < hd / 2; ++i) {
-            const float c = cs[2 * i], sn = cs[2 * i + 1];
-            const float x0 = qh[2 * i], x1 = qh[2 * i + 1];
-            qr[g][2 * i] = x0 * c - x1 * sn;
-            qr[g][2 * i + 1] = x0 * sn + x1 * c;
-        }
+        rope_rotate(qh, cs, hd, qr[g]);
         for (int32_t d = 0; d < hd; ++d) acc[g][d] = 0.0f;
         M[g] = -INFINITY;
         S[g] = 0.0f;
     }
     float kf[256], vf[256];
     for (int64_t p = a->win[s]; p <= p_new; ++p) {
-        const uint16_t * kr = kc + (p % a->cap) * hd;
-        const uint16_t * vr = vc + (p % a->cap) * hd;
-        for (int32_t d = 0; d < hd; ++d) kf[d] = h2f(kr[d]);
-        for (int32_t d = 0; d < hd; ++d) vf[d] = h2f(vr[d]);
+        const uint8_t * kr = kc + (p % a->cap) * a->row_bytes;
+        const uint8_t * vr = vc + (p % a->cap) * a->row_bytes;
+        if (q8) {
+            vxo_dequantize_row_q8_0(kr, hd, kf);
+            vxo_dequantize_row_q8_0(vr, hd, vf);
+        } else {
+            for (int32_t d = 0; d < hd; ++d) kf[d] = h2f(((const uint16_t *) kr)[d]);
+            for (int32_t d = 0; d < hd; ++d) vf[d] = h2f(((const uint16_t *) vr)[d]);
+        }
         for (int32_t g = 0; g < group; ++g) {
             float sdot = 0.0f;
             for (int32_t d = 0; d < hd; ++d) sdot += qr[g][d] * kf[d];
@@ -135,19 +158,19 @@ static void * worker(void * p) {
     return NULL;
 }
 
-void vxo_cpu_decode_step_f16(int32_t n_streams, int32_t n_layers, int32_t n_q, int32_t n_kv,
-                             int32_t head_dim, int64_t cap, uint16_t * k_cache,
-                             uint16_t * v_cache, const float * q, const float * k,
-                             const float * v, const int64_t * pos, const int64_t * win_start,
-                             const float * rope_cs, int64_t rope_rows, float scale,
-                             int32_t n_threads, float * out) {
+void vxo_cpu_decode_step(int32_t dtype, int32_t n_streams, int32_t n_layers, int32_t n_q, int32_t n_kv,
+                         int32_t head_dim, int64_t cap, uint8_t * k_cache, uint8_t * v_cache,
+                         const float * q, const float * k, const float * v, const int64_t * pos,
+                         const int64_t * win_start, const float * rope_cs, int64_t rope_rows, float scale,
+                         int32_t n_threads, float * out) {
     if (n_threads < 1) n_threads = 1;
     if (n_threads > 256) n_threads = 256;
     if (head_dim > 256 || n_q / n_kv > 8) return;
+    if (dtype != VXO_F16 && !(dtype == VXO_Q8_0 && head_dim % 32 == 0)) return;
     pthread_barrier_t bar;
     pthread_barrier_init(&bar, NULL, (unsigned) n_threads);
-    step_args a = {n_streams, n_layers, n_q, n_kv, head_dim, cap, k_cache, v_cache, q, k, v,
-                   pos, win_start, rope_cs, rope_rows, scale, out, n_threads, &bar};
+    step_args a = {n_streams, n_layers, n_q, n_kv, head_dim, cap, dtype, vxo_row_bytes(dtype, 1, head_dim),
+                   k_cache, v_cache, q, k, v, pos, win_start, rope_cs, rope_rows, scale, out, n_threads, &bar};
     pthread_t th[256];
     thread_arg ta[256];
     for (int32_t t = 0; t < n_threads; ++t) {
@@ -158,4 +181,14 @@ void vxo_cpu_decode_step_f16(int32_t n_streams, int32_t n_layers, int32_t n_q, i
     worker(&ta[0]);
     for (int32_t t = 1; t < n_threads; ++t) pthread_join(th[t], NULL);
     pthread_barrier_destroy(&bar);
+}
+
+void vxo_cpu_decode_step_f16(int32_t n_streams, int32_t n_layers, int32_t n_q, int32_t n_kv,
+                             int32_t head_dim, int64_t cap, uint16_t * k_cache,
+                             uint16_t * v_cache, const float * q, const float * k,
+                             const float * v, const int64_t * pos, const int64_t * win_start,
+                             const float * rope_cs, int64_t rope_rows, float scale,
+                             int32_t n_threads, float * out) {
+    vxo_cpu_decode_step(VXO_F16, n_streams, n_layers, n_q, n_kv, head_dim, cap, (uint8_t *) k_cache,
+                        (uint8_t *) v_cache, q, k, v, pos, win_start, rope_cs, rope_rows, scale, n_threads, out);
 }

@@ -147,6 +147,16 @@ void vxo_cpu_decode_step_f16(int32_t n_streams, int32_t n_layers, int32_t n_q,
                              const float * rope_cs, int64_t rope_rows,
                              float scale, int32_t n_threads, float * out);
 
+/* Same step for a cache of dtype VXO_F16 or VXO_Q8_0: rows of
+ * vxo_row_bytes(dtype, 1, head_dim) bytes per kv head (q8_0: ggml blocks,
+ * quantized on append, dequantized on read), layout
+ * [stream][layer][kv_head][cap][row bytes]. */
+void vxo_cpu_decode_step(int32_t dtype, int32_t n_streams, int32_t n_layers, int32_t n_q,
+                         int32_t n_kv, int32_t head_dim, int64_t cap, uint8_t * k_cache,
+                         uint8_t * v_cache, const float * q, const float * k, const float * v,
+                         const int64_t * pos, const int64_t * win_start, const float * rope_cs,
+                         int64_t rope_rows, float scale, int32_t n_threads, float * out);
+
 /* Fill a rope cos/sin table [rows][head_dim] with vxo_rope_cache. */
 void vxo_rope_table(int64_t rows, int32_t n_dims, float base, float * table);
 

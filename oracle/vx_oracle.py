@@ -87,6 +87,8 @@ def lib() -> C.CDLL:
                                    P, P, C.c_int32, C.c_int64, C.c_float, P]
         L.vxo_cpu_decode_step_f16.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int64,
                                               P, P, P, P, P, P, P, P, C.c_int64, C.c_float, C.c_int32, P]
+        L.vxo_cpu_decode_step.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                          C.c_int64, P, P, P, P, P, P, P, P, C.c_int64, C.c_float, C.c_int32, P]
         _lib = L
     return _lib
 
@@ -199,6 +201,19 @@ def attn_row(q: np.ndarray, q_pos: int, base: float, k_rows: np.ndarray, v_rows:
     out = np.empty_like(q)
     lib().vxo_attn_row(_ptr(q), q_pos, base, 1 if rope_q else 0, n_q, n_kv, hd, _ptr(k_rows), _ptr(v_rows),
                        dtype, k_rows.shape[0], scale, _ptr(out))
+    return out
+
+
+def cpu_decode_step(dtype, k_cache, v_cache, q, k, v, pos, win, rope, scale, n_threads):
+    """Timed multi-core CPU step for an f16 or q8_0 cache (vx_cpu_step.c):
+    caches uint8 [stream][layer][kv][cap][row bytes]."""
+    n_streams, n_layers, n_q, hd = q.shape
+    n_kv = k.shape[2]
+    cap = k_cache.shape[-2]
+    out = np.empty_like(q)
+    lib().vxo_cpu_decode_step(dtype, n_streams, n_layers, n_q, n_kv, hd, cap, _ptr(k_cache), _ptr(v_cache),
+                              _ptr(q), _ptr(k), _ptr(v), _ptr(pos), _ptr(win), _ptr(rope), rope.shape[0],
+                              scale, n_threads, _ptr(out))
     return out
 
 

@@ -108,3 +108,34 @@ def test_q8_0_row_roundtrip_within_half_step(oracle):
     err = np.abs(y - x).reshape(-1, 32)
     # half a step, plus |q| <= 127 times the f16 rounding of d (2^-11 relative)
     assert np.all(err <= d[:, None] * (0.5 + 127 * 2.0 ** -11) + 1e-6)
+
+
+def test_cpu_step_matches_oracle_for_f16_and_q8_0(oracle):
+    """The timed CPU step (bench's cpu_baseline / reference arm) computes the
+    same cache bytes and attention as the oracle, for both cache formats."""
+    rng = np.random.default_rng(5)
+    n_q, n_kv, hd, cap, ctx = 32, 8, 128, 64, 37
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    rope = oracle.rope_table(cap + 1, hd, 1e6)
+    for dtype in (1, 8):
+        rb = oracle.row_bytes(dtype, 1, hd)
+        kc = np.zeros((1, 1, n_kv, cap, rb), dtype=np.uint8)
+        vc = np.zeros_like(kc)
+        rows_k, rows_v = [], []
+        for p in range(ctx + 1):
+            k = rng.standard_normal((n_kv, hd)).astype(np.float32) * 0.5
+            v = rng.standard_normal((n_kv, hd)).astype(np.float32) * 0.5
+            kr, vr = oracle.kv_row(k, v, p, 1e6, dtype)
+            rows_k.append(kr)
+            rows_v.append(vr)
+            if p < ctx:
+                kc[0, 0, :, p] = kr.reshape(n_kv, rb)
+                vc[0, 0, :, p] = vr.reshape(n_kv, rb)
+        q = rng.standard_normal((1, 1, n_q, hd)).astype(np.float32) * 0.5
+        out = oracle.cpu_decode_step(dtype, kc, vc, q, k[None, None], v[None, None],
+                                     np.array([ctx], dtype=np.int64), np.zeros(1, dtype=np.int64),
+                                     rope, scale, 2)
+        np.testing.assert_array_equal(kc[0, 0, :, ctx].reshape(-1), rows_k[ctx])
+        np.testing.assert_array_equal(vc[0, 0, :, ctx].reshape(-1), rows_v[ctx])
+        want = oracle.attn_row(q[0, 0], ctx, 1e6, np.stack(rows_k), np.stack(rows_v), dtype, n_kv, scale)
+        assert np.max(np.abs(out[0, 0] - want)) < 1e-4, dtype

@@ -406,41 +406,34 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
         float m_run = -INFINITY;
         float l_part = 0.0f;
         const int share = share_of(n_pages);
-        for (int i = 0; i < share; ++i) {
-            const int st = seq_consumed % ST;
-            // the outcome is made warp-uniform so the warp never splits
-            if (!__all_sync(kFull, mbar_wait(&S.full[warp][st], (seq_consumed / ST) & 1, kWaitNs))) {
-                S.abort_flag = 1;
-                break;
-            }
-            const int lp = it.page_begin + warp + kWarps * i;
-            uint8_t * sk = S.stage[warp][st];
-            uint8_t * sv = sk + TILE + SCALE;
-            if (do_append && lp == last_page) {
-                // Replace the stale copy of the appended row by the new values.
-                const int t = rd.pos % kBlockTokens;
-                if constexpr (DT == 1) {
-                    const int ch = lane & 15;
-                    const uint4 val = *reinterpret_cast<const uint4 *>((lane < 16 ? S.newk : S.newv) + ch * 16);
-                    *reinterpret_cast<uint4 *>((lane < 16 ? sk : sv) + f16_chunk_off(t, ch)) = val;
-                } else {
-                    if (lane < 16) {
-                        const int ch = lane & 7;
-                        const uint4 val = *reinterpret_cast<const uint4 *>((lane < 8 ? S.newk : S.newv) + ch * 16);
-                        *reinterpret_cast<uint4 *>((lane < 8 ? sk : sv) + q8_chunk_off(t, ch)) = val;
-                    } else if (lane < 24) {
-                        const int b = lane & 3;
-                        const bool kk = lane < 20;
-                        reinterpret_cast<uint16_t *>((kk ? sk : sv) + TILE)[b * kBlockTokens + t] =
-                            kk ? S.newk_scale[b] : S.newv_scale[b];
-                    }
+        // Replaces the stale copy of the appended row in a stage by the new values.
+        auto patch = [&](uint8_t * sk, uint8_t * sv) {
+            // Replace the stale copy of the appended row by the new values.
+            const int t = rd.pos % kBlockTokens;
+            if constexpr (DT == 1) {
+                const int ch = lane & 15;
+                const uint4 val = *reinterpret_cast<const uint4 *>((lane < 16 ? S.newk : S.newv) + ch * 16);
+                *reinterpret_cast<uint4 *>((lane < 16 ? sk : sv) + f16_chunk_off(t, ch)) = val;
+            } else {
+                if (lane < 16) {
+                    const int ch = lane & 7;
+                    const uint4 val = *reinterpret_cast<const uint4 *>((lane < 8 ? S.newk : S.newv) + ch * 16);
+                    *reinterpret_cast<uint4 *>((lane < 8 ? sk : sv) + q8_chunk_off(t, ch)) = val;
+                } else if (lane < 24) {
+                    const int b = lane & 3;
+                    const bool kk = lane < 20;
+                    reinterpret_cast<uint16_t *>((kk ? sk : sv) + TILE)[b * kBlockTokens + t] =
+                        kk ? S.newk_scale[b] : S.newv_scale[b];
                 }
-                // The stage is refilled by the bulk-copy (async) proxy later:
-                // order these generic-proxy writes before that.
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
             }
-
+            // The stage is refilled by the bulk-copy (async) proxy later:
+            // order these generic-proxy writes before that.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+        };
+        // This lane's scores of head g for tokens 2c, 2c+1, 8+2c, 9+2c of one
+        // page (log2 domain), masked to the row's window.
+        auto page_scores = [&](const uint8_t * sk, int lp, float (&sc)[4]) {
             // ---- S^T = Q K^T for the page's 16 tokens (two n-blocks of 8) ---
             float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             float s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -484,44 +477,20 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
                 }
             }
 
-            // ---- online softmax (log2 domain) for head g over tokens
-            //      2c, 2c+1, 8+2c, 9+2c of this page --------------------------
             const int tp = lp * kBlockTokens;
-            float sc[4] = {s0[0], s0[1], s1[0], s1[1]};
+            sc[0] = s0[0];
+            sc[1] = s0[1];
+            sc[2] = s1[0];
+            sc[3] = s1[1];
             const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int pos = tp + tk[j];
                 if (!real || pos < rd.win_start || pos > rd.pos) sc[j] = -INFINITY;
             }
-            float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = real ? exp2f(m_run - m_new) : 1.0f;
-            float pr[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) pr[j] = real ? exp2f(sc[j] - m_new) : 0.0f;
-            if (real) m_run = m_new;
-            const __half2 p01 = __floats2half2_rn(pr[0], pr[1]);
-            const __half2 p89 = __floats2half2_rn(pr[2], pr[3]);
-            {
-                const float2 f0 = __half22float2(p01), f1 = __half22float2(p89);
-                l_part = l_part * alpha + ((f0.x + f0.y) + (f1.x + f1.y));
-            }
-            // rescale O^T columns (heads 2c, 2c+1) when any running max moved
-            if (__any_sync(kFull, alpha != 1.0f)) {
-                const float a_lo = __shfl_sync(kFull, alpha, (8 * c) & 31);
-                const float a_hi = __shfl_sync(kFull, alpha, (8 * c + 4) & 31);
-#pragma unroll
-                for (int mb = 0; mb < 8; ++mb) {
-                    o[mb][0] *= a_lo;
-                    o[mb][1] *= a_hi;
-                    o[mb][2] *= a_lo;
-                    o[mb][3] *= a_hi;
-                }
-            }
-
+        };
+        // O^T += V^T P^T for one page, P as f16 pairs (tokens 2c,2c+1 | 8+2c,9+2c).
+        auto page_values = [&](const uint8_t * sv, __half2 p01, __half2 p89) {
             // ---- O^T += V^T P^T ---------------------------------------------
             const uint32_t vbase = smem_u32(sv);
             if constexpr (DT == 1) {
@@ -556,8 +525,81 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
                              s8pair_to_h2(w3, 0x4240u), s8pair_to_h2(w3, 0x4341u), b0, b1);
                 }
             }
+        };
+        // Pages are consumed one at a time (f16) or two at a time (q8_0: the two
+        // pages' score, softmax and value work interleave, and the softmax
+        // bookkeeping is shared).
+        int i = 0;
+        while (i < share) {
+            const bool two = DT == 8 && i + 1 < share;
+            const int stA = seq_consumed % ST;
+            const int stB = (seq_consumed + 1) % ST;
+            bool ready = mbar_wait(&S.full[warp][stA], (seq_consumed / ST) & 1, kWaitNs);
+            if (two) ready = ready && mbar_wait(&S.full[warp][stB], ((seq_consumed + 1) / ST) & 1, kWaitNs);
+            // the outcome is made warp-uniform so the warp never splits
+            if (!__all_sync(kFull, ready)) {
+                S.abort_flag = 1;
+                break;
+            }
+            const int lpA = it.page_begin + warp + kWarps * i;
+            const int lpB = lpA + kWarps;
+            uint8_t * skA = S.stage[warp][stA];
+            uint8_t * skB = S.stage[warp][stB];
+            if (do_append && lpA == last_page) patch(skA, skA + TILE + SCALE);
+            if (two && do_append && lpB == last_page) patch(skB, skB + TILE + SCALE);
+            float scA[4], scB[4];
+            page_scores(skA, lpA, scA);
+            if (two) {
+                page_scores(skB, lpB, scB);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) scB[j] = -INFINITY;
+            }
+
+            // ---- online softmax (log2 domain) for head g --------------------
+            float mx = fmaxf(fmaxf(fmaxf(scA[0], scA[1]), fmaxf(scA[2], scA[3])),
+                             fmaxf(fmaxf(scB[0], scB[1]), fmaxf(scB[2], scB[3])));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = real ? exp2f(m_run - m_new) : 1.0f;
+            float prA[4], prB[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                prA[j] = real ? exp2f(scA[j] - m_new) : 0.0f;
+                prB[j] = real ? exp2f(scB[j] - m_new) : 0.0f;
+            }
+            if (real) m_run = m_new;
+            const __half2 p01A = __floats2half2_rn(prA[0], prA[1]);
+            const __half2 p89A = __floats2half2_rn(prA[2], prA[3]);
+            const __half2 p01B = __floats2half2_rn(prB[0], prB[1]);
+            const __half2 p89B = __floats2half2_rn(prB[2], prB[3]);
+            {
+                const float2 f0 = __half22float2(p01A), f1 = __half22float2(p89A);
+                float add = (f0.x + f0.y) + (f1.x + f1.y);
+                if (two) {
+                    const float2 g0 = __half22float2(p01B), g1 = __half22float2(p89B);
+                    add += (g0.x + g0.y) + (g1.x + g1.y);
+                }
+                l_part = l_part * alpha + add;
+            }
+            // rescale O^T columns (heads 2c, 2c+1) when any running max moved
+            if (__any_sync(kFull, alpha != 1.0f)) {
+                const float a_lo = __shfl_sync(kFull, alpha, (8 * c) & 31);
+                const float a_hi = __shfl_sync(kFull, alpha, (8 * c + 4) & 31);
+#pragma unroll
+                for (int mb = 0; mb < 8; ++mb) {
+                    o[mb][0] *= a_lo;
+                    o[mb][1] *= a_hi;
+                    o[mb][2] *= a_lo;
+                    o[mb][3] *= a_hi;
+                }
+            }
+            page_values(skA + TILE + SCALE, p01A, p89A);
+            if (two) page_values(skB + TILE + SCALE, p01B, p89B);
             __syncwarp();
-            ++seq_consumed;
+            seq_consumed += two ? 2 : 1;
+            i += two ? 2 : 1;
             pump(seq_consumed);
         }
 

@@ -392,6 +392,48 @@ VXK_API vxk_status vxk_enc_read_slots(vxk_enc_pool * pool, int32_t layer, int32_
                                       int32_t slot0, int32_t n, void * k_out, void * v_out,
                                       void * cuda_stream);
 
+/* ======================================================================== */
+/* Greedy head: tied logits and argmax                                      */
+/* ======================================================================== */
+
+/** Opaque greedy-head state for one device (scratch for a batch of rows). */
+typedef struct vxk_head vxk_head;
+
+typedef struct vxk_head_config {
+    uint32_t struct_size;
+    uint32_t api_version;
+    int32_t device;
+    int32_t dim;           /* 3072 (decoder width); a multiple of 64 */
+    int32_t vocab;         /* 131072 */
+    vxk_dtype dtype;       /* F16 or BF16: the type W is stored in */
+} vxk_head_config;
+
+VXK_API vxk_head_config vxk_head_default_config(void);
+VXK_API vxk_status vxk_head_create(const vxk_head_config * config, vxk_head ** out);
+VXK_API void vxk_head_destroy(vxk_head * head);
+VXK_API vxk_status vxk_head_last_error(const vxk_head * head, char * buf, size_t capacity);
+
+/**
+ * Greedy decoding head for a batch of rows: logits[r][v] = W[v] . x[r] and
+ * argmax[r] = the first v with the largest logit.  Replaces
+ * emit_logits_argmax (src/voxtral.cpp:2966-2972: ggml_mul_mat(tok_embeddings,
+ * last_hidden) then ggml_argmax) for a tied embedding matrix stored as f16 or
+ * bf16; x is rounded to W's type and products accumulate in fp32, like
+ * ggml's f16 / bf16 dot products.
+ *   w       [vocab][dim] f16 or bf16, device, 16-byte aligned
+ *   x       [rows][dim] fp32, device (the final-norm output)
+ *   argmax  [rows] int32, device
+ *   logits  [rows][vocab] fp32, device, or NULL to skip writing them
+ * Rows are processed 64 at a time (one pass over W per 64 rows).  Kernels
+ * are asynchronous on cuda_stream; vxk_head_sync reports device errors.
+ */
+VXK_API vxk_status vxk_head_logits_argmax(vxk_head * head, const void * w, const float * x, int32_t rows,
+                                          int32_t * argmax, float * logits, void * cuda_stream);
+
+/** Bounded wait for cuda_stream, then the head's device error word
+ *  (VXK_STATUS_TIMEOUT or VXK_STATUS_BACKEND_ERROR). */
+VXK_API vxk_status vxk_head_sync(vxk_head * head, void * cuda_stream, int32_t timeout_ms);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -227,3 +227,26 @@ def cpu_decode_step_f16(k_cache, v_cache, q, k, v, pos, win, rope, scale, n_thre
                                   _ptr(q), _ptr(k), _ptr(v), _ptr(pos), _ptr(win), _ptr(rope), rope.shape[0],
                                   scale, n_threads, _ptr(out))
     return out
+
+
+def logits_argmax(w_bits: np.ndarray, dtype: int, x: np.ndarray):
+    """Greedy head restated: emit_logits_argmax (src/voxtral.cpp:2966-2972),
+    ggml_mul_mat(tok_embeddings, last_hidden) then ggml_argmax, for a tied
+    embedding matrix stored as f16 (dtype 1) or bf16 (dtype 30).
+
+    w_bits [vocab][dim] uint16 patterns, x [rows][dim] fp32.  Like ggml's
+    f16 / bf16 dot products, each x row is first rounded to W's type; the
+    products are summed here in float64 (the exact-math target).  Returns
+    (logits float64 [rows][vocab], argmax int64 [rows]) with ties resolved to
+    the first index, as ggml_argmax does.
+    """
+    w_bits = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if dtype == 30:
+        wf = (w_bits.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        xr = (f32_to_bf16_bits(x).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    else:
+        wf = w_bits.view(np.float16).astype(np.float64)
+        xr = x.astype(np.float16).astype(np.float64)
+    logits = xr @ wf.T
+    return logits, np.argmax(logits, axis=1)

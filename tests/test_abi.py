@@ -69,6 +69,21 @@ def test_default_configs(vxk):
     e = lib.vxk_enc_default_config()
     assert (e.n_layers, e.n_heads, e.head_dim, e.window, e.capacity) == (32, 32, 64, 750, 878)
     assert e.struct_size == C.sizeof(vxk.EncConfig)
+    h = lib.vxk_head_default_config()
+    assert (h.dim, h.vocab, h.dtype) == (3072, 131072, vxk.DTYPE_F16)
+    assert h.struct_size == C.sizeof(vxk.HeadConfig)
+
+
+def test_head_create_rejects_bad_config_without_gpu(vxk):
+    lib = vxk.load()
+    h = C.c_void_p()
+    for field, value in (("dim", 100), ("vocab", 0), ("dtype", 8), ("struct_size", 8)):
+        c = lib.vxk_head_default_config()
+        setattr(c, field, value)
+        assert lib.vxk_head_create(C.byref(c), C.byref(h)) == vxk.INVALID_ARGUMENT, field
+        assert not h.value
+    assert lib.vxk_head_logits_argmax(None, None, None, 1, None, None, None) == vxk.INVALID_ARGUMENT
+    lib.vxk_head_destroy(None)
 
 
 def test_pool_create_rejects_bad_config_without_gpu(vxk):

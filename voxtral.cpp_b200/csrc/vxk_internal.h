@@ -206,4 +206,32 @@ int enc_smem_bytes();
 // Most 128-key tiles one row group may span (window + 2*7 + capacity pad <= 768).
 int enc_max_tiles();
 
+// ---------------------------------------------------------------------------
+// Greedy head: logits = W . x and argmax (vxk_head_*)
+// ---------------------------------------------------------------------------
+
+constexpr int kHeadRows = 64;          // batch rows per launch (M of the MMA)
+constexpr int kHeadMaxTileRows = 256;  // vocabulary rows per tile (N of the MMA)
+
+struct HeadParams {
+    const float * x;              // [n_rows][dim] fp32
+    uint16_t * xh;                // [64][dim] in W's 16-bit type
+    unsigned long long * best;    // [64] packed (ordered logit, inverted index)
+    int32_t * argmax;             // [n_rows]
+    float * logits;               // [n_rows][vocab] fp32, or nullptr
+    int32_t * error;              // device error word (0 = ok)
+    int32_t vocab;
+    int32_t dim;
+    int32_t n_rows;               // 1 .. 64
+    int32_t tile_rows;            // multiple of 32, <= 256
+    int32_t n_tiles;
+    int32_t dtype;                // 1 = f16, 30 = bf16
+};
+
+// tmw: 2-D tensor map {dim, vocab} over W with tile_rows x 64 boxes; tmx:
+// {dim, 64} over xh with 64 x 64 boxes; both 128-byte swizzle.
+cudaError_t launch_head(const HeadParams & p, const CUtensorMap & tmw, const CUtensorMap & tmx, int grid,
+                        cudaStream_t stream);
+int head_smem_bytes();
+
 }  // namespace vxk

@@ -81,6 +81,11 @@ class EncConfig(C.Structure):
                 ("rope_theta", C.c_float), ("reserved", C.c_int32)]
 
 
+class HeadConfig(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("device", C.c_int32),
+                ("dim", C.c_int32), ("vocab", C.c_int32), ("dtype", C.c_int32)]
+
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -131,6 +136,12 @@ SIGNATURES = {
     "vxk_enc_batch_commit": (_I32, [_P]),
     "vxk_enc_layer": (_I32, [_P, _I32, _P, _P, _P, _P, _P]),
     "vxk_enc_read_slots": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P]),
+    "vxk_head_default_config": (HeadConfig, []),
+    "vxk_head_create": (_I32, [C.POINTER(HeadConfig), C.POINTER(C.c_void_p)]),
+    "vxk_head_destroy": (None, [_P]),
+    "vxk_head_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_head_logits_argmax": (_I32, [_P, _P, _P, _I32, _P, _P, _P]),
+    "vxk_head_sync": (_I32, [_P, _P, _I32]),
 }
 
 _lib = None
@@ -346,6 +357,53 @@ class EncPool:
         self._check(self.lib.vxk_enc_read_slots(self.h, layer, sid, slot0, n, k.ctypes.data, v.ctypes.data,
                                                 C.c_void_p(cuda_stream)))
         return k, v
+
+
+class Head:
+    """Owns one vxk_head (greedy head: tied logits and argmax on one device)."""
+
+    def __init__(self, **cfg):
+        self.lib = load()
+        c = self.lib.vxk_head_default_config()
+        for k, v in cfg.items():
+            if not hasattr(c, k):
+                raise AttributeError(k)
+            setattr(c, k, v)
+        self.config = c
+        h = C.c_void_p()
+        st = self.lib.vxk_head_create(C.byref(c), C.byref(h))
+        if st != OK:
+            raise VxkError(st, self.last_error(None))
+        self.h = h
+
+    def last_error(self, handle="self") -> str:
+        buf = C.create_string_buffer(1024)
+        hv = self.h if handle == "self" else handle
+        self.lib.vxk_head_last_error(hv, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st):
+        if st != OK:
+            raise VxkError(st, self.last_error())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_head_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def logits_argmax(self, w_ptr, x_ptr, rows, argmax_ptr, logits_ptr=0, cuda_stream=0):
+        self._check(self.lib.vxk_head_logits_argmax(self.h, C.c_void_p(w_ptr), C.c_void_p(x_ptr), rows,
+                                                    C.c_void_p(argmax_ptr), C.c_void_p(logits_ptr or None),
+                                                    C.c_void_p(cuda_stream)))
+
+    def sync(self, cuda_stream=0, timeout_ms=10000):
+        self._check(self.lib.vxk_head_sync(self.h, C.c_void_p(cuda_stream), timeout_ms))
 
 
 # ---- planners (host only) -------------------------------------------------

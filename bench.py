@@ -44,6 +44,9 @@ CONFIGS = {
               desc="4B realtime decoder, full 8192-slot sliding rings (steady state: one eviction per step)"),
     "5": dict(layers=30, streams=32, ctx=(8192, 32768), dtype=8, capacity=32768 + 1024,
               desc="3B decoder, q8_0 cache, ctx~U[8192,32768] (streams that fit one GPU)"),
+    "head": dict(kind="head", rows=64, vocab=131072, dim=3072, dtype=1,
+                 desc="greedy head: tied logits (131072 x 3072 f16 embeddings) + argmax for 64 streams/GPU, "
+                      "logits written like the reference's decoder_logits"),
     "4": dict(kind="encoder", layers=32, streams=128, heads=20, rows=4, window=750, capacity=878, dtype=30,
               desc="streaming encoder, 128 streams, 20 heads x 64, 4 new rows per 80 ms chunk, "
                    "750-frame window in an 878-slot bf16 ring (steady state, rings wrapped)"),
@@ -204,6 +207,128 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
     pool.close()
 
 
+def run_head(args, cfg, world, rank, local, dist, torch, vxk):
+    """Greedy head: one step = logits of every stream's row over the whole
+    vocabulary (written out) and their argmax, through vxk_head_logits_argmax."""
+    R, V, D, dt = cfg["rows"], cfg["vocab"], cfg["dim"], cfg["dtype"]
+    head = vxk.Head(device=local, dim=D, vocab=V, dtype=dt)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    w = (torch.randn((V, D), device="cuda", generator=gen) * 0.02).to(torch.float16 if dt == 1 else torch.bfloat16)
+    NSETS = 4
+    xs = torch.randn((NSETS, R, D), device="cuda", generator=gen)
+    am = torch.empty((R,), dtype=torch.int32, device="cuda")
+    lg = torch.empty((R, V), device="cuda")
+
+    def step(i):
+        x = xs[i % NSETS]
+        head.logits_argmax(w.data_ptr(), x.data_ptr(), R, am.data_ptr(), lg.data_ptr(), sh)
+
+    for i in range(args.warmup):
+        step(i)
+    head.sync(sh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    head.sync(sh)
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    step_s = ms / 1000.0 / args.steps
+    bytes_per_step = V * D * 2 + R * D * 4 + R * V * 4 + R * 4  # W once, x, logits, argmax
+    achieved = bytes_per_step / step_s / 1e9
+    peak, peak_kind = load_peaks()
+
+    # end to end: x from pinned host memory, argmax back to the host, each step
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.randn((R, D)).pin_memory()
+        ha = torch.empty((R,), dtype=torch.int32).pin_memory()
+        dx = torch.empty((R, D), device="cuda")
+
+        def host_step():
+            dx.copy_(hx, non_blocking=True)
+            head.logits_argmax(w.data_ptr(), dx.data_ptr(), R, am.data_ptr(), lg.data_ptr(), sh)
+            ha.copy_(am, non_blocking=True)
+
+        host_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            host_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(dist, f0.elapsed_time(f1), "cuda")
+        e2e = {"value": round(world * R * args.steps / (ems / 1000.0), 1), "unit": "rows/s",
+               "h2d_bytes_per_step": int(hx.numel()) * 4, "d2h_bytes_per_step": int(ha.numel()) * 4,
+               "ms_per_step": round(ems / args.steps, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cps, done = head_cpu_sample(cfg, args.seed, args.cpu_seconds)
+        cpu = {"value": round(cps, 3), "unit": "rows/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{done} steps of 4 rows over a {V // 8}-row slice of the vocabulary "
+                         f"(oracle.logits_argmax, float64 BLAS), scaled to {R} rows x {V}"}
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "greedy head rows/s (tied logits + argmax)",
+            "value": round(world * R * args.steps / (ms / 1000.0), 1),
+            "unit": "rows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": ("f16" if dt == 1 else "bf16") + " weights and rows, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"config head: {cfg['desc']}", "rows_per_gpu": R, "vocab": V, "dim": D,
+                       "parallelism": f"rows sharded, {R}/GPU, no collective",
+                       "l2": "inputs larger than L2 (805 MB of weights per step)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_launch": bytes_per_step, "avg_step_us": round(step_s * 1e6, 2),
+                         "kernel": "head_kernel (+ x conversion and finish)",
+                         "tensor_tflops": round(2.0 * R * V * D / step_s / 1e12, 2)},
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(args.steps * 3),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    head.close()
+
+
+def head_cpu_sample(cfg, seed, seconds):
+    """Times the oracle's greedy head (float64 BLAS on all host cores) on 4
+    rows over 1/8 of the vocabulary; returns rows/s scaled to the full head."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    V, D = cfg["vocab"] // 8, cfg["dim"]
+    w = (rng.standard_normal((V, D), dtype=np.float32) * 0.02).astype(np.float16).view(np.uint16)
+    x = rng.standard_normal((4, D)).astype(np.float32)
+    vx_oracle.logits_argmax(w, cfg["dtype"], x)
+    done = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        vx_oracle.logits_argmax(w, cfg["dtype"], x)
+        done += 1
+    el = time.perf_counter() - t0
+    return 4 * done / el / 8.0, done
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -213,6 +338,7 @@ def parse():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="2")
     ap.add_argument("--streams", type=int, default=0, help="override streams per GPU")
     ap.add_argument("--layers", type=int, default=0, help="override decoder layers (profiling small cases)")
+    ap.add_argument("--vocab", type=int, default=0, help="override the greedy head's vocabulary (profiling)")
     ap.add_argument("--seed", type=int, default=20261201)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -404,6 +530,20 @@ def encoder_cpu_sample(cfg, seed, seconds):
 def run_reference(args, cfg, rank, world):
     if rank != 0:
         return
+    if cfg.get("kind") == "head":
+        cps, done = head_cpu_sample(cfg, args.seed, 20.0)
+        line = {"impl": "reference", "metric": "greedy head rows/s (tied logits + argmax)",
+                "value": round(cps, 4), "unit": "rows/s", "n_gpus": args.gpus, "steps": done, "warmup": 1,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16 weights, float64 accumulate", "data": "synthetic",
+                "config": {"workload": f"config head: {cfg['desc']}"},
+                "cpu_baseline": {"value": round(cps, 4), "unit": "rows/s", "cores": os.cpu_count() or 1,
+                                 "kind": "port",
+                                 "sample": f"{done} steps of 4 rows over 1/8 of the vocabulary (oracle.logits_argmax, "
+                                           f"float64 BLAS), scaled"},
+                "e2e": {"value": round(cps, 4), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if cfg.get("kind") == "encoder":
         cps, done = encoder_cpu_sample(cfg, args.seed, 20.0)
         line = {"impl": "reference", "metric": "encoder chunks/s (KV append + windowed attention, 4 rows/chunk)",
@@ -453,6 +593,8 @@ def main():
         cfg["streams"] = args.streams
     if args.layers:
         cfg["layers"] = args.layers
+    if args.vocab:
+        cfg["vocab"] = args.vocab
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -473,6 +615,12 @@ def main():
                                 device_id=torch.device("cuda", local))
     import vxk
 
+    if cfg.get("kind") == "head":
+        run_head(args, cfg, world, rank, local, dist, torch, vxk)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if cfg.get("kind") == "encoder":
         run_encoder(args, cfg, world, rank, local, dist, torch, vxk)
         if dist:

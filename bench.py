@@ -250,6 +250,7 @@ def run_head(args, cfg, world, rank, local, dist, torch, vxk):
     bytes_per_step = V * D * 2 + R * D * 4 + R * V * 4 + R * 4  # W once, x, logits, argmax
     achieved = bytes_per_step / step_s / 1e9
     peak, peak_kind = load_peaks()
+    traffic_ratio, traffic_src = load_traffic(args.config)
 
     # end to end: x from pinned host memory, argmax back to the host, each step
     e2e = None
@@ -297,7 +298,10 @@ def run_head(args, cfg, world, rank, local, dist, torch, vxk):
                        "parallelism": f"rows sharded, {R}/GPU, no collective",
                        "l2": "inputs larger than L2 (805 MB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_step),
+                         "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
+                                                           f"scaled to this step)",
                          "algorithmic_bytes_per_launch": bytes_per_step, "avg_step_us": round(step_s * 1e6, 2),
                          "kernel": "head_kernel (+ x conversion and finish)",
                          "tensor_tflops": round(2.0 * R * V * D / step_s / 1e12, 2)},
@@ -367,6 +371,7 @@ TRAFFIC_PROFILES = {
     "3": "decode_kernel_f16_config2.md",   # same kernel and page format; ratio scaled to config 3
     "5": "decode_kernel_q8_0_config5.md",
     "4": "enc_tc_kernel_config4.md",
+    "head": "head_kernel_config_head.md",
 }
 
 

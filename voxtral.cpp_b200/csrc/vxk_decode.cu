@@ -161,6 +161,16 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t & r0, uint32_t
                  : "r"(addr));
 }
 
+// D = A(16x32 s8, row) * B(32x8 s8, col), exact int32 dot products.
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 // D += A(16x16 f16, row) * B(16x8 f16, col), fp32 accumulate.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -366,23 +376,70 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
         // f16: a0 = dims 16ks+2c,+1 and a2 = dims 16ks+8+2c,+1 (mma k order);
         // q8_0: a0 = dims 16ks+4c,+1 and a2 = dims 16ks+4c+2,+3, the k order the
         // int8 ldmatrix delivers.  Scale*log2(e) is folded in.
+        // f16: qa[ks] = the f16 A fragment (dims 16ks+2c,+1 | 16ks+8+2c,+1).
+        // q8_0: the scores use exact int8 tensor-core dot products with the
+        // int8 cache; each head's rotated, scaled query is split into two
+        // int8 parts, q ~= qs * (254 * hi + lo) with qs = amax / (127 * 254),
+        // hi in A rows 0-7 and lo in the (otherwise padding) rows 8-15, so one
+        // m16n8k32 product yields both dots.  qa[ks][0] = hi, qa[ks][1] = lo
+        // for dims 16ks+4c .. 16ks+4c+3 (the k order of the int8 ldmatrix).
         uint32_t qa[8][2];
+        float qs = 0.0f;
         {
             const float * qrow = p.q + ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup + (g & 3)) * kHeadDim;
             const float2 * cs = p.rope + (int64_t) rd.pos * (kHeadDim / 2);
+            if constexpr (DT == 1) {
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const int d0 = DT == 1 ? 16 * ks + 2 * c : 16 * ks + 4 * c;
-                const int d1 = DT == 1 ? 16 * ks + 8 + 2 * c : 16 * ks + 4 * c + 2;
-                uint32_t v0 = 0, v1 = 0;
-                if (real) {
-                    const float2 r0 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d0), cs[d0 >> 1]);
-                    const float2 r1 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d1), cs[d1 >> 1]);
-                    v0 = h2_bits(__floats2half2_rn(r0.x * p.scale_log2, r0.y * p.scale_log2));
-                    v1 = h2_bits(__floats2half2_rn(r1.x * p.scale_log2, r1.y * p.scale_log2));
+                for (int ks = 0; ks < 8; ++ks) {
+                    const int d0 = 16 * ks + 2 * c;
+                    const int d1 = 16 * ks + 8 + 2 * c;
+                    uint32_t v0 = 0, v1 = 0;
+                    if (real) {
+                        const float2 r0 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d0), cs[d0 >> 1]);
+                        const float2 r1 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d1), cs[d1 >> 1]);
+                        v0 = h2_bits(__floats2half2_rn(r0.x * p.scale_log2, r0.y * p.scale_log2));
+                        v1 = h2_bits(__floats2half2_rn(r1.x * p.scale_log2, r1.y * p.scale_log2));
+                    }
+                    qa[ks][0] = v0;
+                    qa[ks][1] = v1;
                 }
-                qa[ks][0] = v0;
-                qa[ks][1] = v1;
+            } else {
+                float qv[8][4];
+                float amax = 0.0f;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const int d0 = 16 * ks + 4 * c;
+                    float2 r0 = make_float2(0.0f, 0.0f), r1 = make_float2(0.0f, 0.0f);
+                    if (real) {
+                        r0 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d0), cs[d0 >> 1]);
+                        r1 = rope_pair(*reinterpret_cast<const float2 *>(qrow + d0 + 2), cs[(d0 >> 1) + 1]);
+                    }
+                    qv[ks][0] = r0.x * p.scale_log2;
+                    qv[ks][1] = r0.y * p.scale_log2;
+                    qv[ks][2] = r1.x * p.scale_log2;
+                    qv[ks][3] = r1.y * p.scale_log2;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fabsf(qv[ks][j]));
+                }
+                // the head's 128 dims sit in the 4 lanes of one mma group
+                amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+                const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+                qs = amax > 0.0f ? amax / (127.0f * 254.0f) : 0.0f;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    uint32_t hi = 0, lo = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float x = qv[ks][j] * inv;
+                        const float h = rintf(x);                 // |h| <= 127
+                        const float l = rintf((x - h) * 254.0f);  // |x - h| <= 1/2: |l| <= 127
+                        hi |= ((uint32_t) (int32_t) h & 0xffu) << (8 * j);
+                        lo |= ((uint32_t) (int32_t) l & 0xffu) << (8 * j);
+                    }
+                    qa[ks][0] = hi;
+                    qa[ks][1] = lo;
+                }
             }
         }
         if (do_append) {
@@ -452,29 +509,24 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
                 const __half2 * dk = reinterpret_cast<const __half2 *>(sk + TILE);
 #pragma unroll
                 for (int blk = 0; blk < 4; ++blk) {
+                    // w0 / w2: tokens 0-7, dims 0-15 / 16-31 of the block; w1 / w3: tokens 8-15
                     uint32_t w0, w1, w2, w3;
                     ldsm_x4(kbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
-                    float t0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    float t1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    w0 ^= 0x80808080u;
-                    w1 ^= 0x80808080u;
-                    w2 ^= 0x80808080u;
-                    w3 ^= 0x80808080u;
-                    mma16816(t0, qa[2 * blk][0], 0u, qa[2 * blk][1], 0u, s8pair_to_h2(w0, 0x4140u),
-                             s8pair_to_h2(w0, 0x4342u));
-                    mma16816(t1, qa[2 * blk][0], 0u, qa[2 * blk][1], 0u, s8pair_to_h2(w1, 0x4140u),
-                             s8pair_to_h2(w1, 0x4342u));
-                    mma16816(t0, qa[2 * blk + 1][0], 0u, qa[2 * blk + 1][1], 0u, s8pair_to_h2(w2, 0x4140u),
-                             s8pair_to_h2(w2, 0x4342u));
-                    mma16816(t1, qa[2 * blk + 1][0], 0u, qa[2 * blk + 1][1], 0u, s8pair_to_h2(w3, 0x4140u),
-                             s8pair_to_h2(w3, 0x4342u));
+                    int t0[4], t1[4];
+                    imma16832(t0, qa[2 * blk][0], qa[2 * blk][1], qa[2 * blk + 1][0], qa[2 * blk + 1][1], w0, w2);
+                    imma16832(t1, qa[2 * blk][0], qa[2 * blk][1], qa[2 * blk + 1][0], qa[2 * blk + 1][1], w1, w3);
+                    // t[0], t[1]: hi dots of head g, tokens 2c, 2c+1; t[2], t[3]: lo dots
                     const float2 d01 = __half22float2(dk[(blk * kBlockTokens + 2 * c) >> 1]);
                     const float2 d89 = __half22float2(dk[(blk * kBlockTokens + 8 + 2 * c) >> 1]);
-                    s0[0] = fmaf(t0[0], d01.x, s0[0]);
-                    s0[1] = fmaf(t0[1], d01.y, s0[1]);
-                    s1[0] = fmaf(t1[0], d89.x, s1[0]);
-                    s1[1] = fmaf(t1[1], d89.y, s1[1]);
+                    s0[0] = fmaf((float) (t0[0] * 254 + t0[2]), d01.x, s0[0]);
+                    s0[1] = fmaf((float) (t0[1] * 254 + t0[3]), d01.y, s0[1]);
+                    s1[0] = fmaf((float) (t1[0] * 254 + t1[2]), d89.x, s1[0]);
+                    s1[1] = fmaf((float) (t1[1] * 254 + t1[3]), d89.y, s1[1]);
                 }
+                s0[0] *= qs;
+                s0[1] *= qs;
+                s1[0] *= qs;
+                s1[1] *= qs;
             }
 
             const int tp = lp * kBlockTokens;

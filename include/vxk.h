@@ -313,6 +313,18 @@ VXK_API vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_
  *  VXK_STATUS_BACKEND_ERROR). */
 VXK_API vxk_status vxk_sync(vxk_pool * pool, void * cuda_stream, int32_t timeout_ms);
 
+/**
+ * Exercises the failure path of the pool's kernels without a fault: launches
+ * one warp that waits, with the same bounded wait the decode kernel uses on
+ * its copies, on a barrier that nothing completes; after limit_ms (1..1000)
+ * it gives up and records a timeout in the pool's device error word, as a
+ * decode launch whose page copies never landed would.  The next vxk_sync on
+ * cuda_stream then returns VXK_STATUS_TIMEOUT and clears the word; the pool
+ * stays usable.  No counterpart in the reference: it lets a host test that
+ * its error handling sees device-side timeouts.
+ */
+VXK_API vxk_status vxk_pool_probe_wait_timeout(vxk_pool * pool, int32_t limit_ms, void * cuda_stream);
+
 /** Page compaction: moves every live page above the lowest free pages down,
  *  rewriting block tables, so that used pages form a prefix of the pool.
  *  Counts the device bytes copied into the pool's and each moved stream's

@@ -109,6 +109,7 @@ def test_null_handles_are_rejected(vxk):
     assert lib.vxk_batch_commit(None) == vxk.INVALID_ARGUMENT
     assert lib.vxk_decode_layer(None, 0, None, None, None, None, None) == vxk.INVALID_ARGUMENT
     assert lib.vxk_enc_layer(None, 0, None, None, None, None, None) == vxk.INVALID_ARGUMENT
+    assert lib.vxk_pool_probe_wait_timeout(None, 10, None) == vxk.INVALID_ARGUMENT
     lib.vxk_pool_destroy(None)
     lib.vxk_enc_destroy(None)
 

@@ -196,6 +196,26 @@ def test_errors_are_statuses_not_faults(vxk, oracle):
     assert max_err(g, w) <= ATOL
 
 
+def test_device_wait_timeout_is_reported_and_the_pool_recovers(vxk, oracle):
+    """A bounded device wait that runs out (a barrier nothing completes) is
+    reported by the next sync as a timeout, and the pool keeps working."""
+    d = Driver(vxk, oracle, seed=9, **_cfg(n_blocks=64, capacity=256))
+    s = d.open()
+    g, w = d.step([s], [30])
+    assert max_err(g, w) <= ATOL
+    d.pool.probe_wait_timeout(50, d.stream)
+    with pytest.raises(vxk.VxkError) as e:
+        d.pool.sync(d.stream)
+    assert e.value.status == vxk.TIMEOUT
+    d.pool.sync(d.stream)  # the error word was cleared
+    for _ in range(2):
+        g, w = d.step([s], [1])
+        assert max_err(g, w) <= ATOL
+    with pytest.raises(vxk.VxkError) as e:
+        d.pool.probe_wait_timeout(0, d.stream)
+    assert e.value.status == vxk.INVALID_ARGUMENT
+
+
 @pytest.mark.parametrize("dtype", [F16, Q8])
 def test_back_to_back_layers(vxk, oracle, dtype):
     """All layers of a step launched back to back with no host sync between

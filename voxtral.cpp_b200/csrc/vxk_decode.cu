@@ -903,7 +903,26 @@ cudaError_t launch_decode_t(const DecodeParams & p, cudaStream_t stream, bool pd
     return cudaLaunchKernelEx(&cfg, decode_kernel<DT>, p);
 }
 
+// Failure-path probe: a warp waits, with the decode kernel's own bounded
+// wait, on an mbarrier that nothing arrives on; when the limit passes it sets
+// the error word exactly as a decode launch whose copies never land would.
+__global__ void wait_probe_kernel(int32_t * error, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const bool landed = __all_sync(kFull, mbar_wait(&bar, 0, limit_ns));
+    if (!landed && threadIdx.x == 0) set_error(error, kErrTimeout);
+}
+
 }  // namespace
+
+cudaError_t launch_wait_probe(int32_t * error, uint64_t limit_ns, cudaStream_t stream) {
+    wait_probe_kernel<<<1, 32, 0, stream>>>(error, limit_ns);
+    return cudaGetLastError();
+}
 
 int decode_smem_bytes(int dtype) { return dtype == 8 ? (int) sizeof(Smem<8>) : (int) sizeof(Smem<1>); }
 

@@ -159,6 +159,11 @@ constexpr size_t kStaticScratchFloats = kStaticScratchPartialFloats + kStaticScr
 // more scratch than the array holds.  Allocates nothing.
 cudaError_t launch_decode_static_scratch(const DecodeParams & p, cudaStream_t stream);
 
+// Launches one warp that waits, with the decode kernel's bounded wait, on an
+// mbarrier nothing arrives on, and sets *error to the timeout code after
+// limit_ns (test of the failure path).
+cudaError_t launch_wait_probe(int32_t * error, uint64_t limit_ns, cudaStream_t stream);
+
 // Shared-memory bytes the decode kernel needs, and how many of its CTAs are
 // resident per SM on the current device (0 on error).
 int decode_smem_bytes(int dtype);

@@ -1061,6 +1061,17 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
     });
 }
 
+vxk_status vxk_pool_probe_wait_timeout(vxk_pool * pool, int32_t limit_ms, void * cuda_stream) {
+    if (!pool) return VXK_STATUS_INVALID_ARGUMENT;
+    return guarded(pool, [&] {
+        if (limit_ms < 1 || limit_ms > 1000) fail(VXK_STATUS_INVALID_ARGUMENT, "limit_ms must be in 1..1000");
+        DeviceScope scope(pool->cfg.device);
+        ++pool->launches;
+        VXK_CUDA(vxk::launch_wait_probe(pool->d_error, (uint64_t) limit_ms * 1000000ull,
+                                        static_cast<cudaStream_t>(cuda_stream)));
+    });
+}
+
 vxk_status vxk_sync(vxk_pool * pool, void * cuda_stream, int32_t timeout_ms) {
     if (!pool) return VXK_STATUS_INVALID_ARGUMENT;
     return guarded(pool, [&] {

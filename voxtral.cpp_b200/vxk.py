@@ -136,6 +136,7 @@ SIGNATURES = {
     "vxk_enc_batch_commit": (_I32, [_P]),
     "vxk_enc_layer": (_I32, [_P, _I32, _P, _P, _P, _P, _P]),
     "vxk_enc_read_slots": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P]),
+    "vxk_pool_probe_wait_timeout": (_I32, [_P, _I32, _P]),
     "vxk_head_default_config": (HeadConfig, []),
     "vxk_head_create": (_I32, [C.POINTER(HeadConfig), C.POINTER(C.c_void_p)]),
     "vxk_head_destroy": (None, [_P]),
@@ -263,6 +264,9 @@ class Pool:
 
     def sync(self, cuda_stream=0, timeout_ms=60000):
         self._check(self.lib.vxk_sync(self.h, C.c_void_p(cuda_stream), timeout_ms))
+
+    def probe_wait_timeout(self, limit_ms, cuda_stream=0):
+        self._check(self.lib.vxk_pool_probe_wait_timeout(self.h, limit_ms, C.c_void_p(cuda_stream)))
 
     def compact(self, cuda_stream=0):
         pm, bm = C.c_int64(), C.c_int64()

@@ -320,6 +320,7 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
     IssueUnit cur = fetch(0);
     IssueUnit nxt = fetch(1);
     int iu = 0, ipi = 0, seq_issued = 0;
+    int ist = 0;  // ring stage of copy seq_issued (seq_issued % ST, kept without a division)
     auto pump = [&](int seq_consumed) {
         while (iu < nu && seq_issued - seq_consumed < ST) {
             if (ipi >= share_of(cur.npages)) {
@@ -333,7 +334,7 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
             const int reg = hi == 0 ? cur.pid[0] : hi == 1 ? cur.pid[1] : hi == 2 ? cur.pid[2] : cur.pid[3];
             const int pg = __shfl_sync(kFull, reg, ipi & 31);
             if (lane == 0) {
-                const int st = seq_issued % ST;
+                const int st = ist;
                 const int64_t tile = (int64_t) pg * p.n_kv + cur.kvh;
                 uint64_t * bar = &S.full[warp][st];
                 uint8_t * dst = S.stage[warp][st];
@@ -346,6 +347,7 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
                 }
             }
             ++seq_issued;
+            ist = ist + 1 == ST ? 0 : ist + 1;
             ++ipi;
         }
     };
@@ -361,6 +363,8 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
     const int mi = lane >> 3;    // ldmatrix: matrix index of this lane's row address
     const int mrow = lane & 7;   //           row within that matrix
     int seq_consumed = 0;
+    int cst = 0;        // ring stage of seq_consumed
+    uint32_t cph = 0;   // and the parity of its fill ((seq_consumed / ST) & 1)
     for (int k = 0; k < nu; ++k) {
         const int uid = p.sched_units[u0 + k];
         const int item_idx = uid / p.n_kv;
@@ -534,11 +538,18 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
             sc[1] = s0[1];
             sc[2] = s1[0];
             sc[3] = s1[1];
-            const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
+            // Only a page that the window cuts (a split's first page when the
+            // ring has slid, the row's last page) needs the position mask; the
+            // test is warp-uniform.  Lanes 16-31 (padding heads) are not
+            // masked: their probabilities are forced to 0 below and they never
+            // meet the real lanes in a reduction.
+            if (tp < rd.win_start || tp + kBlockTokens - 1 > rd.pos) {
+                const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int pos = tp + tk[j];
-                if (!real || pos < rd.win_start || pos > rd.pos) sc[j] = -INFINITY;
+                for (int j = 0; j < 4; ++j) {
+                    const int pos = tp + tk[j];
+                    if (pos < rd.win_start || pos > rd.pos) sc[j] = -INFINITY;
+                }
             }
         };
         // O^T += V^T P^T for one page, P as f16 pairs (tokens 2c,2c+1 | 8+2c,9+2c).
@@ -584,10 +595,12 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
         int i = 0;
         while (i < share) {
             const bool two = DT == 8 && i + 1 < share;
-            const int stA = seq_consumed % ST;
-            const int stB = (seq_consumed + 1) % ST;
-            bool ready = mbar_wait(&S.full[warp][stA], (seq_consumed / ST) & 1, kWaitNs);
-            if (two) ready = ready && mbar_wait(&S.full[warp][stB], ((seq_consumed + 1) / ST) & 1, kWaitNs);
+            const int stA = cst;
+            const bool wrapA = cst + 1 == ST;
+            const int stB = wrapA ? 0 : cst + 1;
+            const uint32_t phB = wrapA ? cph ^ 1u : cph;
+            bool ready = mbar_wait(&S.full[warp][stA], cph, kWaitNs);
+            if (two) ready = ready && mbar_wait(&S.full[warp][stB], phB, kWaitNs);
             // the outcome is made warp-uniform so the warp never splits
             if (!__all_sync(kFull, ready)) {
                 S.abort_flag = 1;
@@ -651,6 +664,14 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
             if (two) page_values(skB + TILE + SCALE, p01B, p89B);
             __syncwarp();
             seq_consumed += two ? 2 : 1;
+            if (two) {
+                const bool wrapB = stB + 1 == ST;
+                cst = wrapB ? 0 : stB + 1;
+                cph = wrapB ? phB ^ 1u : phB;
+            } else {
+                cst = stB;
+                cph = phB;
+            }
             i += two ? 2 : 1;
             pump(seq_consumed);
         }

@@ -47,6 +47,10 @@ CONFIGS = {
     "head": dict(kind="head", rows=64, vocab=131072, dim=3072, dtype=1,
                  desc="greedy head: tied logits (131072 x 3072 f16 embeddings) + argmax for 64 streams/GPU, "
                       "logits written like the reference's decoder_logits"),
+    "proj": dict(kind="qmm", layers=30, rows=64,
+                 mats=(("q", 4096, 3072, 12), ("k", 1024, 3072, 12), ("v", 1024, 3072, 14), ("o", 3072, 4096, 12)),
+                 desc="decoder attention projections q/k/v/o of 30 layers for 64 batched streams/GPU, "
+                      "Q4_K_M types (attn_q/k/o Q4_K, attn_v Q6_K), distinct weights per layer"),
     "4": dict(kind="encoder", layers=32, streams=128, heads=20, rows=4, window=750, capacity=878, dtype=30,
               desc="streaming encoder, 128 streams, 20 heads x 64, 4 new rows per 80 ms chunk, "
                    "750-frame window in an 878-slot bf16 ring (steady state, rings wrapped)"),
@@ -313,6 +317,171 @@ def run_head(args, cfg, world, rank, local, dist, torch, vxk):
     head.close()
 
 
+def qmm_gguf_bytes(n, k, t):
+    return n * (k // 32 * 34 if t == 8 else k // 256 * (144 if t == 12 else 210))
+
+
+def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
+    """Quantized projections: one step = q, k, v (from the same normed rows)
+    and o of every layer for the GPU's batch of stream rows, each through
+    vxk_qweight_matmul (activation quantization + the int8 tensor-core
+    product)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    R, L = cfg["rows"], cfg["layers"]
+    rng = np.random.default_rng(args.seed + rank)
+    host = {name: vx_oracle.random_qblocks(t, n, k, rng) for name, n, k, t in cfg["mats"]}
+    mats = []
+    for _ in range(L):  # distinct device copies per layer: the step streams every layer's weights
+        mats.append({name: vxk.QWeight(host[name], device=local, type=t, n_rows=n, n_cols=k, max_batch=R)
+                     for name, n, k, t in cfg["mats"]})
+    dims = {name: (n, k) for name, n, k, _ in cfg["mats"]}
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    x = torch.randn((R, dims["q"][1]), device="cuda", generator=gen)
+    att = torch.randn((R, dims["o"][1]), device="cuda", generator=gen)
+    ys = {name: torch.empty((R, n), device="cuda") for name, (n, _) in dims.items()}
+
+    def step(s):
+        # q, k, v share the normed rows: one quantization and one launch
+        # (vxk_qweight_matmul_group); o multiplies the attention output
+        for layer in mats:
+            vxk.qweight_matmul_group([layer["q"], layer["k"], layer["v"]], x.data_ptr(), R,
+                                     [ys["q"].data_ptr(), ys["k"].data_ptr(), ys["v"].data_ptr()], s)
+            layer["o"].matmul(att.data_ptr(), R, ys["o"].data_ptr(), s)
+
+    # eager warm-up (raises the kernels' shared-memory limits), then the whole
+    # step captured once as a CUDA graph of the C-ABI launches: 120 launches of
+    # a few microseconds each are otherwise paced by the host
+    step(sh)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap):
+        step(cap.cuda_stream)
+    stream.wait_stream(cap)
+    for _ in range(args.warmup):
+        graph.replay()
+    mats[0]["q"].sync(sh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    for layer in mats:
+        for m in layer.values():
+            m.sync(sh)
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    step_s = ms / 1000.0 / args.steps
+    w_bytes = L * sum(qmm_gguf_bytes(n, k, t) for _, n, k, t in cfg["mats"])
+    io_bytes = L * R * 4 * (3 * dims["q"][1] + dims["o"][1] + sum(n for n, _ in dims.values()))
+    bytes_per_step = w_bytes + io_bytes
+    achieved = bytes_per_step / step_s / 1e9
+    peak, peak_kind = load_peaks()
+    traffic_ratio, traffic_src = load_traffic(args.config)
+
+    # end to end: the step's rows from pinned host memory, the last o rows back
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.randn((R, dims["q"][1])).pin_memory()
+        hy = torch.empty((R, dims["o"][0])).pin_memory()
+
+        def host_step():
+            x.copy_(hx, non_blocking=True)
+            graph.replay()
+            hy.copy_(ys["o"], non_blocking=True)
+
+        host_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            host_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(dist, f0.elapsed_time(f1), "cuda")
+        e2e = {"value": round(world * R * args.steps / (ems / 1000.0), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(hx.numel()) * 4, "d2h_bytes_per_step": int(hy.numel()) * 4,
+               "ms_per_step": round(ems / args.steps, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, done = qmm_cpu_sample(cfg, args.seed, args.cpu_seconds)
+        cpu = {"value": round(tps, 4), "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{done} single-row products of the k projection (1024 x 3072 Q4_K) by the oracle "
+                         f"(oracle/vx_qmm.c, one thread), scaled by weight count to q/k/v/o x {L} layers"}
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "attention-projection tokens/s (q/k/v/o, Q4_K_M, 30 layers)",
+            "value": round(world * R * args.steps / (ms / 1000.0), 1),
+            "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "Q4_K / Q6_K weights, Q8_K rows, int8 tensor-core dots, fp32 scales", "data": "synthetic",
+            "config": {"workload": f"config proj: {cfg['desc']}" + ("" if R == 64 else f" (run with {R} rows)"),
+                       "rows_per_gpu": R, "layers": L,
+                       "parallelism": f"stream rows sharded, {R}/GPU, no collective",
+                       "l2": f"inputs larger than L2 ({w_bytes / 1e6:.0f} MB of weights per step)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_step),
+                         "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
+                                                           f"scaled to this step)",
+                         "algorithmic_bytes_per_launch": bytes_per_step, "avg_step_us": round(step_s * 1e6, 2),
+                         "kernel": "qmm_kernel (+ qmm_act_kernel)",
+                         "int8_tops": round(2.0 * R * L * sum(n * k for _, n, k, _ in cfg["mats"]) / step_s / 1e12,
+                                            2)},
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(args.steps * L * 4),
+            "launch": "CUDA graph of the step's C-ABI calls (vxk_qweight_matmul_group for q/k/v, "
+                      "vxk_qweight_matmul for o), replayed per step",
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    for layer in mats:
+        for m in layer.values():
+            m.close()
+
+
+def qmm_cpu_sample(cfg, seed, seconds):
+    """Times the oracle's quantized product on one row of the k projection;
+    returns tokens/s scaled by weight count to all projections of all layers."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    _, n, k, t = cfg["mats"][1]
+    w = vx_oracle.random_qblocks(t, n, k, rng)
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    vx_oracle.qmatmul(t, w, n, k, x)
+    done = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        vx_oracle.qmatmul(t, w, n, k, x)
+        done += 1
+    el = time.perf_counter() - t0
+    per_row = el / done
+    scale = sum(nn * kk for _, nn, kk, _ in cfg["mats"]) / (n * k) * cfg["layers"]
+    return 1.0 / (per_row * scale), done
+
+
 def head_cpu_sample(cfg, seed, seconds):
     """Times the oracle's greedy head (float64 BLAS on all host cores) on 4
     rows over 1/8 of the vocabulary; returns rows/s scaled to the full head."""
@@ -549,6 +718,20 @@ def run_reference(args, cfg, rank, world):
                 "e2e": {"value": round(cps, 4), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
+    if cfg.get("kind") == "qmm":
+        tps, done = qmm_cpu_sample(cfg, args.seed, 20.0)
+        line = {"impl": "reference", "metric": "attention-projection tokens/s (q/k/v/o, Q4_K_M, 30 layers)",
+                "value": round(tps, 4), "unit": "tokens/s", "n_gpus": args.gpus, "steps": done, "warmup": 1,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "Q4_K / Q6_K weights, Q8_K rows, exact integer dots", "data": "synthetic",
+                "config": {"workload": f"config proj: {cfg['desc']}"},
+                "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": 1, "kind": "port",
+                                 "sample": f"{done} single-row products of the k projection by the oracle "
+                                           f"(oracle/vx_qmm.c), scaled by weight count"},
+                "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if cfg.get("kind") == "encoder":
         cps, done = encoder_cpu_sample(cfg, args.seed, 20.0)
         line = {"impl": "reference", "metric": "encoder chunks/s (KV append + windowed attention, 4 rows/chunk)",
@@ -596,6 +779,8 @@ def main():
     cfg = dict(CONFIGS[args.config])
     if args.streams:
         cfg["streams"] = args.streams
+        if cfg.get("kind") == "qmm":
+            cfg["rows"] = args.streams
     if args.layers:
         cfg["layers"] = args.layers
     if args.vocab:
@@ -622,6 +807,12 @@ def main():
 
     if cfg.get("kind") == "head":
         run_head(args, cfg, world, rank, local, dist, torch, vxk)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if cfg.get("kind") == "qmm":
+        run_qmm(args, cfg, world, rank, local, dist, torch, vxk)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

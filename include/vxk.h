@@ -446,6 +446,79 @@ VXK_API vxk_status vxk_head_logits_argmax(vxk_head * head, const void * w, const
  *  (VXK_STATUS_TIMEOUT or VXK_STATUS_BACKEND_ERROR). */
 VXK_API vxk_status vxk_head_sync(vxk_head * head, void * cuda_stream, int32_t timeout_ms);
 
+/* ======================================================================== */
+/* Quantized-weight matrix product (GGUF Q8_0 / Q4_K / Q6_K weights)        */
+/* ======================================================================== */
+
+/** GGUF block types of a weight matrix (ggml type ids). */
+typedef enum vxk_qtype {
+    VXK_QTYPE_Q8_0 = 8,   /* {f16 d; i8 q[32]}: 34 B per 32 values */
+    VXK_QTYPE_Q4_K = 12,  /* {f16 d, dmin; u8 scales[12]; u8 q[128]}: 144 B per 256 */
+    VXK_QTYPE_Q6_K = 14   /* {u8 ql[128]; u8 qh[64]; i8 scales[16]; f16 d}: 210 B per 256 */
+} vxk_qtype;
+
+/** One quantized weight matrix resident on a device, plus the scratch of
+ *  its products (one product at a time per matrix). */
+typedef struct vxk_qweight vxk_qweight;
+
+typedef struct vxk_qweight_config {
+    uint32_t struct_size;
+    uint32_t api_version;
+    int32_t device;
+    vxk_qtype type;
+    int32_t n_rows;      /* output features N (ggml ne[1]); a multiple of 64 */
+    int32_t n_cols;      /* input features K (ggml ne[0]); a multiple of 256, <= 32768 */
+    int32_t max_batch;   /* activation rows per product, 1..64 */
+    int32_t reserved;
+} vxk_qweight_config;
+
+VXK_API vxk_qweight_config vxk_qweight_default_config(void);
+
+/**
+ * Device layout of a weight: 16-row x 256-column tiles ("records"), ordered
+ * [row tile][column tile], each holding the tile's quants in the register
+ * order of the int8 tensor-core fragments, followed by its block scales
+ * (Q4_K's 6-bit scales and mins unpacked to bytes).  Record bytes: Q8_0
+ * 4352, Q4_K 2368, Q6_K 3360 (GGUF: 4352, 2304, 3360).  Pure host code.
+ */
+VXK_API vxk_status vxk_qweight_packed_bytes(vxk_qtype type, int32_t n_rows, int32_t n_cols, size_t * out_bytes);
+VXK_API vxk_status vxk_qweight_repack(vxk_qtype type, int32_t n_rows, int32_t n_cols, const void * gguf_blocks,
+                                      size_t gguf_bytes, void * out, size_t out_bytes);
+
+/** Repacks the host GGUF rows (n_rows x row bytes, ggml row order) and
+ *  uploads them; allocates the product scratch for max_batch rows. */
+VXK_API vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gguf_blocks,
+                                      size_t gguf_bytes, vxk_qweight ** out);
+VXK_API void vxk_qweight_destroy(vxk_qweight * w);
+VXK_API vxk_status vxk_qweight_last_error(const vxk_qweight * w, char * buf, size_t capacity);
+
+/**
+ * y[r][i] = W[i] . x[r] for r < rows, replacing ggml_mul_mat(W, x) of a
+ * quantized W (src/voxtral.cpp:2659-2661, 2857, 2877-2881, 2955) with
+ * ggml's CPU arithmetic: each x row is quantized like
+ * quantize_row_q8_0_ref (Q8_0 weights) or quantize_row_q8_K_ref (K-quants),
+ * block dot products are exact integers, and the blocks' scale factors are
+ * applied in fp32.
+ *   x [rows][n_cols] fp32, device;  y [rows][n_rows] fp32, device.
+ * Asynchronous on cuda_stream; vxk_qweight_sync reports device errors.
+ */
+VXK_API vxk_status vxk_qweight_matmul(vxk_qweight * w, const float * x, int32_t rows, float * y,
+                                      void * cuda_stream);
+
+/**
+ * The same product for up to 4 matrices that share x (the q, k and v
+ * projections of one layer: src/voxtral.cpp:2659-2661): x is quantized once
+ * and one launch covers every matrix's rows.  All matrices are on one device
+ * with equal n_cols and are all Q8_0 or all K-quants (Q4_K and Q6_K share
+ * the Q8_K quantization of x); ys[i] is [rows][ws[i] n_rows].  Uses ws[0]'s
+ * scratch and error word (read them with vxk_qweight_sync(ws[0], ...)).
+ */
+VXK_API vxk_status vxk_qweight_matmul_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows,
+                                            float * const * ys, void * cuda_stream);
+
+/** Bounded wait for cuda_stream, then the matrix's device error word. */
+VXK_API vxk_status vxk_qweight_sync(vxk_qweight * w, void * cuda_stream, int32_t timeout_ms);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -160,6 +160,14 @@ void vxo_cpu_decode_step(int32_t dtype, int32_t n_streams, int32_t n_layers, int
 /* Fill a rope cos/sin table [rows][head_dim] with vxo_rope_cache. */
 void vxo_rope_table(int64_t rows, int32_t n_dims, float base, float * table);
 
+/* Quantized-weight matrix product, ggml CPU semantics (vx_qmm.c).  Weight
+ * types: 8 = Q8_0, 12 = Q4_K, 14 = Q6_K (GGUF block layouts). */
+int64_t vxo_qrow_bytes(int32_t type, int64_t k);
+void vxo_quantize_row_q8_K(const float * x, int64_t k, float * d, int8_t * q, int16_t * bsums);
+void vxo_dequantize_row_w(int32_t type, const uint8_t * w, int64_t k, float * y);
+int32_t vxo_qmatmul(int32_t type, const uint8_t * w, int32_t n, int32_t k, const float * x, int32_t rows,
+                    double * y, double * mag);
+
 #ifdef __cplusplus
 }
 #endif

@@ -89,6 +89,12 @@ def lib() -> C.CDLL:
                                               P, P, P, P, P, P, P, P, C.c_int64, C.c_float, C.c_int32, P]
         L.vxo_cpu_decode_step.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_int64, P, P, P, P, P, P, P, P, C.c_int64, C.c_float, C.c_int32, P]
+        L.vxo_qrow_bytes.restype = C.c_int64
+        L.vxo_qrow_bytes.argtypes = [C.c_int32, C.c_int64]
+        L.vxo_quantize_row_q8_K.argtypes = [P, C.c_int64, P, P, P]
+        L.vxo_dequantize_row_w.argtypes = [C.c_int32, P, C.c_int64, P]
+        L.vxo_qmatmul.restype = C.c_int32
+        L.vxo_qmatmul.argtypes = [C.c_int32, P, C.c_int32, C.c_int32, P, C.c_int32, P, P]
         _lib = L
     return _lib
 
@@ -250,3 +256,71 @@ def logits_argmax(w_bits: np.ndarray, dtype: int, x: np.ndarray):
         xr = x.astype(np.float16).astype(np.float64)
     logits = xr @ wf.T
     return logits, np.argmax(logits, axis=1)
+
+
+Q4_K, Q6_K = 12, 14
+QBLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+
+def qrow_bytes(wtype: int, k: int) -> int:
+    return int(lib().vxo_qrow_bytes(wtype, k))
+
+
+def quantize_q8_K(x: np.ndarray):
+    """ggml quantize_row_q8_K_ref on one row: (d fp32 [k/256], q int8 [k],
+    bsums int16 [k/16])."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    k = x.size
+    d = np.empty(k // 256, np.float32)
+    q = np.empty(k, np.int8)
+    bs = np.empty(k // 16, np.int16)
+    lib().vxo_quantize_row_q8_K(_ptr(x), k, _ptr(d), _ptr(q), _ptr(bs))
+    return d, q, bs
+
+
+def dequantize_w(wtype: int, blocks: np.ndarray, k: int) -> np.ndarray:
+    """One row of GGUF blocks (uint8) of type Q8_0 / Q4_K / Q6_K -> fp32."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+    y = np.empty(k, np.float32)
+    lib().vxo_dequantize_row_w(wtype, _ptr(blocks), k, _ptr(y))
+    return y
+
+
+def qmatmul(wtype: int, w_blocks: np.ndarray, n: int, k: int, x: np.ndarray):
+    """ggml_mul_mat(W, x) for a quantized W restated (vx_qmm.c).
+
+    w_blocks: uint8 [n][row bytes] GGUF blocks; x: fp32 [rows][k].  Returns
+    (y float64 [rows][n], mag float64 [rows][n], terms per output): the
+    parity bound for an fp32 result is (terms + 4) * 2^-24 * mag.
+    """
+    w_blocks = np.ascontiguousarray(w_blocks, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = x.shape[0]
+    assert x.shape[1] == k and k <= 8192 and w_blocks.size == n * qrow_bytes(wtype, k)
+    y = np.empty((rows, n), np.float64)
+    mag = np.empty((rows, n), np.float64)
+    terms = lib().vxo_qmatmul(wtype, _ptr(w_blocks), n, k, _ptr(x), rows, _ptr(y), _ptr(mag))
+    if terms < 0:
+        raise ValueError(f"unsupported weight type {wtype}")
+    return y, mag, int(terms)
+
+
+def random_qblocks(wtype: int, n: int, k: int, rng: np.random.Generator) -> np.ndarray:
+    """Valid random GGUF blocks for an n x k weight (test input): random
+    quants and sub-block scales, block scales drawn so that the dequantized
+    weights are O(0.05), like a trained projection's."""
+    per, size = QBLOCK[wtype]
+    nb = k // per
+    blk = rng.integers(0, 256, size=(n, nb, size), dtype=np.uint8)
+    def f16(a):
+        return np.asarray(a, np.float16).view(np.uint16).view(np.uint8).reshape(a.shape + (2,))
+    if wtype == Q8_0:
+        blk[:, :, 0:2] = f16(rng.uniform(2e-4, 8e-4, (n, nb)))
+        blk[:, :, 2:] = rng.integers(-127, 128, size=(n, nb, 32)).astype(np.int8).view(np.uint8)
+    elif wtype == Q4_K:
+        blk[:, :, 0:2] = f16(rng.uniform(5e-4, 2e-3, (n, nb)))
+        blk[:, :, 2:4] = f16(rng.uniform(1e-3, 4e-3, (n, nb)))
+    else:
+        blk[:, :, 192:208] = rng.integers(-128, 128, size=(n, nb, 16)).astype(np.int8).view(np.uint8)
+        blk[:, :, 208:210] = f16(rng.uniform(2e-5, 6e-5, (n, nb)))
+    return blk.reshape(n, nb * size)

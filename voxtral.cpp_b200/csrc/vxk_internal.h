@@ -239,4 +239,51 @@ cudaError_t launch_head(const HeadParams & p, const CUtensorMap & tmw, const CUt
                         cudaStream_t stream);
 int head_smem_bytes();
 
+// ---------------------------------------------------------------------------
+// Quantized-weight matrix product (vxk_qweight_*)
+// ---------------------------------------------------------------------------
+
+constexpr int kQmmRows = 64;       // weight rows per CTA (4 warps x 16-row tiles)
+constexpr int kQmmUnit = 256;      // columns per record and per activation unit
+constexpr int kQmmMaxBatch = 64;   // activation rows per product (8 n-tiles of 8)
+
+constexpr int kQmmMaxGroup = 4;   // matrices sharing one activation quantization
+
+// One weight matrix of a product group.
+struct QmmMat {
+    const uint8_t * w;         // records [n_rows / 16][n_units][record bytes]
+    float * y;                 // [rows][n_rows] fp32
+    float * partials;          // [n_splits][nt * 8][n_rows] when n_splits > 1
+    int32_t * counters;        // [n_rows / 64] split arrivals, zero between products
+    int32_t type;              // 8 = Q8_0, 12 = Q4_K, 14 = Q6_K
+    int32_t n_rows;            // a multiple of 64
+    int32_t block0;            // first 64-row block of this matrix in the grid
+    int32_t reserved;
+};
+
+struct QmmParams {
+    QmmMat mats[kQmmMaxGroup]; // all Q8_0, or all K-quants (Q4_K / Q6_K): one x quantization
+    int32_t n_mats;
+    int32_t n_units;           // K / 256, shared by the group
+    int32_t rows;              // activation rows, 1 .. nt * 8
+    int32_t nt;                // n-tiles of 8 activation rows: 1, 2, 4 or 8
+    int32_t units_per_split;   // column units per CTA
+    int32_t n_splits;          // ceil(n_units / units_per_split)
+    const float * x;           // [rows][K] fp32
+    uint8_t * act;             // [n_units][nt][8 blocks][32 lanes][8 B] int8 B fragments
+    float * act_d;             // Q8_0: [n_units * 8][nt * 8]; K-quants: [n_units][nt * 8]
+    uint8_t * act_ms;          // K-quants: [n_units][nt][32 lanes][8 B] sums of 32 quantized
+                               // values as (h, l) int8 B fragments (zero-initialised)
+    int32_t * error;           // device error word (0 = ok)
+};
+
+// Record bytes of one 16 x 256 tile (4352 / 2368 / 3360), 0 for other types.
+int qmm_record_bytes(int type);
+// Dynamic shared memory of the product kernel for the group's types, p.nt
+// and `units` column units per split.
+int qmm_smem_bytes(const QmmParams & p, int units);
+// Activation quantization, then the product (both with programmatic
+// dependent launch on `stream`).
+cudaError_t launch_qmm(const QmmParams & p, cudaStream_t stream);
+
 }  // namespace vxk

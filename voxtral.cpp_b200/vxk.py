@@ -86,6 +86,14 @@ class HeadConfig(C.Structure):
                 ("dim", C.c_int32), ("vocab", C.c_int32), ("dtype", C.c_int32)]
 
 
+class QWeightConfig(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("device", C.c_int32),
+                ("type", C.c_int32), ("n_rows", C.c_int32), ("n_cols", C.c_int32), ("max_batch", C.c_int32),
+                ("reserved", C.c_int32)]
+
+
+QTYPE_Q8_0, QTYPE_Q4_K, QTYPE_Q6_K = 8, 12, 14
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -143,6 +151,15 @@ SIGNATURES = {
     "vxk_head_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
     "vxk_head_logits_argmax": (_I32, [_P, _P, _P, _I32, _P, _P, _P]),
     "vxk_head_sync": (_I32, [_P, _P, _I32]),
+    "vxk_qweight_default_config": (QWeightConfig, []),
+    "vxk_qweight_packed_bytes": (_I32, [_I32, _I32, _I32, C.POINTER(C.c_size_t)]),
+    "vxk_qweight_repack": (_I32, [_I32, _I32, _I32, _P, C.c_size_t, _P, C.c_size_t]),
+    "vxk_qweight_create": (_I32, [C.POINTER(QWeightConfig), _P, C.c_size_t, C.POINTER(C.c_void_p)]),
+    "vxk_qweight_destroy": (None, [_P]),
+    "vxk_qweight_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_qweight_matmul": (_I32, [_P, _P, _I32, _P, _P]),
+    "vxk_qweight_matmul_group": (_I32, [C.POINTER(C.c_void_p), _I32, _P, _I32, C.POINTER(C.c_void_p), _P]),
+    "vxk_qweight_sync": (_I32, [_P, _P, _I32]),
 }
 
 _lib = None
@@ -433,3 +450,83 @@ def enc_plan(q_start: int, n_new: int, capacity: int, window: int):
 
 def enc_mask_allows(kv: int, q: int, window: int) -> bool:
     return bool(load().vxk_enc_kv_mask_allows(kv, q, window))
+
+
+class QWeight:
+    """Owns one vxk_qweight: a GGUF Q8_0 / Q4_K / Q6_K matrix on one device
+    and the scratch of its products (ggml_mul_mat with ggml's CPU
+    arithmetic)."""
+
+    def __init__(self, gguf_blocks, **cfg):
+        import numpy as np
+
+        self.lib = load()
+        c = self.lib.vxk_qweight_default_config()
+        for k, v in cfg.items():
+            if not hasattr(c, k):
+                raise AttributeError(k)
+            setattr(c, k, v)
+        self.config = c
+        blocks = np.ascontiguousarray(gguf_blocks, dtype=np.uint8)
+        h = C.c_void_p()
+        st = self.lib.vxk_qweight_create(C.byref(c), blocks.ctypes.data, blocks.nbytes, C.byref(h))
+        if st != OK:
+            raise VxkError(st, self.last_error(None))
+        self.h = h
+
+    def last_error(self, handle="self") -> str:
+        buf = C.create_string_buffer(1024)
+        hv = self.h if handle == "self" else handle
+        self.lib.vxk_qweight_last_error(hv, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st):
+        if st != OK:
+            raise VxkError(st, self.last_error())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_qweight_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def matmul(self, x_ptr, rows, y_ptr, cuda_stream=0):
+        self._check(self.lib.vxk_qweight_matmul(self.h, C.c_void_p(x_ptr), rows, C.c_void_p(y_ptr),
+                                                C.c_void_p(cuda_stream)))
+
+    def sync(self, cuda_stream=0, timeout_ms=10000):
+        self._check(self.lib.vxk_qweight_sync(self.h, C.c_void_p(cuda_stream), timeout_ms))
+
+
+def qweight_matmul_group(mats, x_ptr, rows, y_ptrs, cuda_stream=0):
+    """vxk_qweight_matmul_group: one quantization of x, one launch for all of
+    `mats` (QWeight objects sharing n_cols and the activation family)."""
+    lib = load()
+    n = len(mats)
+    ws = (C.c_void_p * n)(*[m.h.value for m in mats])
+    ys = (C.c_void_p * n)(*y_ptrs)
+    st = lib.vxk_qweight_matmul_group(ws, n, C.c_void_p(x_ptr), rows, ys, C.c_void_p(cuda_stream))
+    if st != OK:
+        raise VxkError(st, mats[0].last_error() if n else "")
+
+
+def qweight_repack(qtype: int, n_rows: int, n_cols: int, gguf_blocks):
+    """Host repack of GGUF rows into the device record layout (vxk_qweight_repack)."""
+    import numpy as np
+
+    lib = load()
+    size = C.c_size_t()
+    st = lib.vxk_qweight_packed_bytes(qtype, n_rows, n_cols, C.byref(size))
+    if st != OK:
+        raise VxkError(st, "packed_bytes")
+    blocks = np.ascontiguousarray(gguf_blocks, dtype=np.uint8)
+    out = np.empty(size.value, np.uint8)
+    st = lib.vxk_qweight_repack(qtype, n_rows, n_cols, blocks.ctypes.data, blocks.nbytes, out.ctypes.data, out.nbytes)
+    if st != OK:
+        raise VxkError(st, "repack")
+    return out

@@ -388,7 +388,8 @@ def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
     ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
     step_s = ms / 1000.0 / args.steps
     w_bytes = L * sum(qmm_gguf_bytes(n, k, t) for _, n, k, t in cfg["mats"])
-    io_bytes = L * R * 4 * (3 * dims["q"][1] + dims["o"][1] + sum(n for n, _ in dims.values()))
+    # x read once for q/k/v (one quantization per group), the attention rows once, every output once
+    io_bytes = L * R * 4 * (dims["q"][1] + dims["o"][1] + sum(n for n, _ in dims.values()))
     bytes_per_step = w_bytes + io_bytes
     achieved = bytes_per_step / step_s / 1e9
     peak, peak_kind = load_peaks()
@@ -541,6 +542,7 @@ TRAFFIC_PROFILES = {
     "5": "decode_kernel_q8_0_config5.md",
     "4": "enc_tc_kernel_config4.md",
     "head": "head_kernel_config_head.md",
+    "proj": "qmm_kernel_config_proj.md",
 }
 
 

@@ -467,7 +467,7 @@ typedef struct vxk_qweight_config {
     int32_t device;
     vxk_qtype type;
     int32_t n_rows;      /* output features N (ggml ne[1]); a multiple of 64 */
-    int32_t n_cols;      /* input features K (ggml ne[0]); a multiple of 256, <= 32768 */
+    int32_t n_cols;      /* input features K (ggml ne[0]); a multiple of 256, <= 16384 */
     int32_t max_batch;   /* activation rows per product, 1..64 */
     int32_t reserved;
 } vxk_qweight_config;

@@ -248,13 +248,12 @@ constexpr int kQmmUnit = 256;      // columns per record and per activation unit
 constexpr int kQmmMaxBatch = 64;   // activation rows per product (8 n-tiles of 8)
 
 constexpr int kQmmMaxGroup = 4;   // matrices sharing one activation quantization
+constexpr int kQmmMaxSplits = 8;  // column splits of a 64-row block = CTAs of one (portable) cluster
 
 // One weight matrix of a product group.
 struct QmmMat {
     const uint8_t * w;         // records [n_rows / 16][n_units][record bytes]
     float * y;                 // [rows][n_rows] fp32
-    float * partials;          // [n_splits][nt * 8][n_rows] when n_splits > 1
-    int32_t * counters;        // [n_rows / 64] split arrivals, zero between products
     int32_t type;              // 8 = Q8_0, 12 = Q4_K, 14 = Q6_K
     int32_t n_rows;            // a multiple of 64
     int32_t block0;            // first 64-row block of this matrix in the grid
@@ -268,7 +267,7 @@ struct QmmParams {
     int32_t rows;              // activation rows, 1 .. nt * 8
     int32_t nt;                // n-tiles of 8 activation rows: 1, 2, 4 or 8
     int32_t units_per_split;   // column units per CTA
-    int32_t n_splits;          // ceil(n_units / units_per_split)
+    int32_t n_splits;          // ceil(n_units / units_per_split) <= kQmmMaxSplits: one cluster
     const float * x;           // [rows][K] fp32
     uint8_t * act;             // [n_units][nt][8 blocks][32 lanes][8 B] int8 B fragments
     float * act_d;             // Q8_0: [n_units * 8][nt * 8]; K-quants: [n_units][nt * 8]
@@ -282,8 +281,10 @@ int qmm_record_bytes(int type);
 // Dynamic shared memory of the product kernel for the group's types, p.nt
 // and `units` column units per split.
 int qmm_smem_bytes(const QmmParams & p, int units);
+// Resident product CTAs per SM for the family / p.nt at `smem` bytes.
+int qmm_ctas_per_sm(const QmmParams & p, int smem);
 // Activation quantization, then the product (both with programmatic
-// dependent launch on `stream`).
+// dependent launch on `stream`; the product's splits as one cluster).
 cudaError_t launch_qmm(const QmmParams & p, cudaStream_t stream);
 
 }  // namespace vxk

@@ -17,8 +17,9 @@
 //                   (mma.sync m16n8k32; m16n8k16 for Q6_K's 16-value
 //                   sub-blocks); sub-block scales are applied to the int32
 //                   results, block scales in fp32.  The column range can be
-//                   split over CTAs; the last CTA of a 64-row block sums the
-//                   splits' partials in split order.
+//                   split over the CTAs of a thread-block cluster, which sum
+//                   their partial blocks through distributed shared memory
+//                   in split order.
 // The weight stream is the HBM traffic (4352 / 2368 / 3360 bytes per 4096
 // weights); activations are a few hundred KB and stay in L2.
 #include "vxk_internal.h"
@@ -99,6 +100,25 @@ __device__ __forceinline__ uint64_t l2_policy(bool evict_first) {
     else
         asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
     return policy;
+}
+
+// Barrier over the CTAs of this thread-block cluster (release / acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory offset in cluster CTA `rank`, and a load from it.
+__device__ __forceinline__ uint32_t map_dsmem(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void set_error(int32_t * err, int code) {
@@ -243,7 +263,6 @@ __device__ __forceinline__ void qmm_cta(const QmmParams & p, const QmmMat & m, c
     uint64_t * bars = reinterpret_cast<uint64_t *>(sms + cap * L::kSumPerUnit);
     // bars[w * kStages + s]: weight ring stages; bars[16]: activations
     int32_t * s_abort = reinterpret_cast<int32_t *>(bars + 4 * kStages + 1);
-    int32_t * s_last = s_abort + 1;
     if (tid == 0) {
         for (int i = 0; i < 4 * kStages + 1; ++i) mbar_init(&bars[i], 1);
         *s_abort = 0;
@@ -445,77 +464,44 @@ __device__ __forceinline__ void qmm_cta(const QmmParams & p, const QmmMat & m, c
         if (lane == 0) {
             for (int l = consumed; l < issued; ++l) mbar_wait(&wbar[l % kStages], (uint32_t) (l / kStages) & 1u);
             set_error(p.error, kErrTimeout);
+            atomicExch(s_abort, 1);
         }
-        if (tid == 0 || lane == 0) atomicExch(s_abort, 1);
     }
-    __syncthreads();
-    if (*s_abort) return;
 
-    // ---- results: rows of this tile, columns (activation rows) of the batch ----
-    const int row0 = tile * 16 + g;
-    const int ncol = NT * 8;
-    if (p.n_splits == 1) {
+    // ---- results.  The splits of a 64-row block are one thread-block
+    // cluster: each CTA writes its partial block [columns][64 rows] into its
+    // own shared memory (the drained weight ring); after a cluster barrier
+    // CTA r sums slice r of the block over all splits, in split order, from
+    // the members' shared memory (DSMEM), and writes y.  Every CTA reaches
+    // both cluster barriers on every path (a CTA whose waits expired writes
+    // nothing; the error word reports it). ----
+    float * ptile = reinterpret_cast<float *>(ring);  // [NT * 8][64]
+    __syncthreads();
+    const bool live = *s_abort == 0;
+    if (live) {
+        const int r0 = warp * 16 + g;
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
             const int col = n * 8 + 2 * c;
-            if (col < p.rows) {
-                m.y[(int64_t) col * m.n_rows + row0] = acc[n][0];
-                m.y[(int64_t) col * m.n_rows + row0 + 8] = acc[n][2];
-            }
-            if (col + 1 < p.rows) {
-                m.y[(int64_t) (col + 1) * m.n_rows + row0] = acc[n][1];
-                m.y[(int64_t) (col + 1) * m.n_rows + row0 + 8] = acc[n][3];
-            }
+            ptile[col * kQmmRows + r0] = acc[n][0];
+            ptile[(col + 1) * kQmmRows + r0] = acc[n][1];
+            ptile[col * kQmmRows + r0 + 8] = acc[n][2];
+            ptile[(col + 1) * kQmmRows + r0 + 8] = acc[n][3];
         }
-        return;
     }
-    float * part = m.partials + (int64_t) split * ncol * m.n_rows;
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-        const int col = n * 8 + 2 * c;
-        part[(int64_t) col * m.n_rows + row0] = acc[n][0];
-        part[(int64_t) col * m.n_rows + row0 + 8] = acc[n][2];
-        part[(int64_t) (col + 1) * m.n_rows + row0] = acc[n][1];
-        part[(int64_t) (col + 1) * m.n_rows + row0 + 8] = acc[n][3];
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const int prev = atomicAdd(&m.counters[rb], 1);
-        *s_last = prev == p.n_splits - 1;
-    }
-    __syncthreads();
-    if (!*s_last) return;
-    __threadfence();
-    // the last split of this 64-row block sums all splits in split order,
-    // four rows per load
-    const int64_t base = (int64_t) rb * kQmmRows;
-    const int64_t sstride = (int64_t) ncol * m.n_rows;
-    for (int e = tid; e < p.rows * (kQmmRows / 4); e += kThreads) {
-        const int col = e / (kQmmRows / 4);
-        const int64_t idx = (int64_t) col * m.n_rows + base + 4 * (e % (kQmmRows / 4));
-        float4 s = __ldcg(reinterpret_cast<const float4 *>(m.partials + idx));
-        int sp = 1;
-        for (; sp + 3 < p.n_splits; sp += 4) {
-            const float4 a = __ldcg(reinterpret_cast<const float4 *>(m.partials + sp * sstride + idx));
-            const float4 b = __ldcg(reinterpret_cast<const float4 *>(m.partials + (sp + 1) * sstride + idx));
-            const float4 c4 = __ldcg(reinterpret_cast<const float4 *>(m.partials + (sp + 2) * sstride + idx));
-            const float4 d4 = __ldcg(reinterpret_cast<const float4 *>(m.partials + (sp + 3) * sstride + idx));
-            s.x = (((s.x + a.x) + b.x) + c4.x) + d4.x;
-            s.y = (((s.y + a.y) + b.y) + c4.y) + d4.y;
-            s.z = (((s.z + a.z) + b.z) + c4.z) + d4.z;
-            s.w = (((s.w + a.w) + b.w) + c4.w) + d4.w;
+    cluster_sync();
+    if (live) {
+        const int S = p.n_splits;
+        const int E = p.rows * kQmmRows;
+        const int e0 = (int) ((int64_t) E * split / S), e1 = (int) ((int64_t) E * (split + 1) / S);
+        const uint32_t local = smem_u32(ptile);
+        for (int e = e0 + tid; e < e1; e += kThreads) {
+            float sum = 0.0f;
+            for (int sp = 0; sp < S; ++sp) sum += ld_dsmem_f32(map_dsmem(local + 4u * (uint32_t) e, (uint32_t) sp));
+            m.y[(int64_t) (e / kQmmRows) * m.n_rows + (int64_t) rb * kQmmRows + (e % kQmmRows)] = sum;
         }
-        for (; sp < p.n_splits; ++sp) {
-            const float4 a = __ldcg(reinterpret_cast<const float4 *>(m.partials + sp * sstride + idx));
-            s.x += a.x;
-            s.y += a.y;
-            s.z += a.z;
-            s.w += a.w;
-        }
-        *reinterpret_cast<float4 *>(m.y + idx) = s;
     }
-    if (tid == 0) m.counters[rb] = 0;
+    cluster_sync();  // no CTA leaves while another still reads its shared memory
 }
 
 // The product over a group of matrices that share x (one weight type family):
@@ -539,18 +525,25 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p) {
     }
 }
 
+// Launch with programmatic dependent launch and, when cluster_y > 1, a
+// thread-block cluster of (1, cluster_y, 1).
 template <typename K>
-cudaError_t launch_pdl(K kernel, dim3 grid, unsigned block, size_t smem, cudaStream_t stream, const QmmParams & p) {
+cudaError_t launch_pdl(K kernel, dim3 grid, unsigned block, size_t smem, cudaStream_t stream, const QmmParams & p,
+                       unsigned cluster_y = 1) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = cluster_y;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = cluster_y > 1 ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
@@ -573,9 +566,9 @@ int layout_bytes_type(int type, int nt, int units) {
     }
 }
 
+// The shared-memory cap of an instantiation is raised once per device.
 template <int FAM, int NT>
-cudaError_t launch_fam(const QmmParams & p, int smem, cudaStream_t stream) {
-    // the shared-memory cap is raised once per device for each instantiation
+cudaError_t raise_smem() {
     static bool raised[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -586,9 +579,25 @@ cudaError_t launch_fam(const QmmParams & p, int smem, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         raised[dev] = true;
     }
+    return cudaSuccess;
+}
+
+template <int FAM, int NT>
+cudaError_t launch_fam(const QmmParams & p, int smem, cudaStream_t stream) {
+    cudaError_t e = raise_smem<FAM, NT>();
+    if (e != cudaSuccess) return e;
     const int blocks = p.mats[p.n_mats - 1].block0 + p.mats[p.n_mats - 1].n_rows / kQmmRows;
     return launch_pdl(qmm_kernel<FAM, NT>, dim3((unsigned) blocks, (unsigned) p.n_splits), kThreads, (size_t) smem,
-                      stream, p);
+                      stream, p, (unsigned) p.n_splits);
+}
+
+template <int FAM, int NT>
+int ctas_fam(int smem) {
+    if (raise_smem<FAM, NT>() != cudaSuccess) return 0;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmm_kernel<FAM, NT>, kThreads, (size_t) smem) != cudaSuccess)
+        return 0;
+    return n;
 }
 
 template <int FAM>
@@ -602,6 +611,16 @@ cudaError_t launch_nt(const QmmParams & p, int smem, cudaStream_t stream) {
     }
 }
 
+template <int FAM>
+int ctas_nt(int nt, int smem) {
+    switch (nt) {
+        case 1: return ctas_fam<FAM, 1>(smem);
+        case 2: return ctas_fam<FAM, 2>(smem);
+        case 4: return ctas_fam<FAM, 4>(smem);
+        default: return ctas_fam<FAM, 8>(smem);
+    }
+}
+
 }  // namespace
 
 int qmm_record_bytes(int type) { return rec_bytes(type); }
@@ -612,9 +631,14 @@ int qmm_smem_bytes(const QmmParams & p, int units) {
     return b;
 }
 
+int qmm_ctas_per_sm(const QmmParams & p, int smem) {
+    return p.mats[0].type == 8 ? ctas_nt<0>(p.nt, smem) : ctas_nt<1>(p.nt, smem);
+}
+
 cudaError_t launch_qmm(const QmmParams & p, cudaStream_t stream) {
     if (p.n_mats < 1 || p.n_mats > kQmmMaxGroup || p.rows < 1 || p.rows > p.nt * 8 || p.units_per_split < 1 ||
-        p.n_splits < 1)
+        p.n_splits < 1 || p.n_splits > kQmmMaxSplits ||
+        (int64_t) p.units_per_split * (p.n_splits - 1) >= p.n_units)
         return cudaErrorInvalidValue;
     const int fam = p.mats[0].type == 8 ? 0 : 1;
     for (int i = 0; i < p.n_mats; ++i)

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -69,7 +70,9 @@ private:
     int prev_ = 0, dev_ = 0;
 };
 
-constexpr int kMaxCols = 32768;
+// A split stages its quantized rows in shared memory and a 64-row block is cut
+// into at most 8 splits (one cluster): 64 column units at most.
+constexpr int kMaxCols = 16384;
 
 int64_t gguf_row_bytes(int type, int64_t k) {
     switch (type) {
@@ -85,7 +88,7 @@ void check_shape(int type, int32_t n_rows, int32_t n_cols) {
     if (n_rows < vxk::kQmmRows || n_rows % vxk::kQmmRows != 0)
         qfail(VXK_STATUS_INVALID_ARGUMENT, "n_rows must be a positive multiple of 64");
     if (n_cols < vxk::kQmmUnit || n_cols % vxk::kQmmUnit != 0 || n_cols > kMaxCols)
-        qfail(VXK_STATUS_INVALID_ARGUMENT, "n_cols must be a multiple of 256 in [256, 32768]");
+        qfail(VXK_STATUS_INVALID_ARGUMENT, "n_cols must be a multiple of 256 in [256, 16384]");
 }
 
 // Q4_K 6-bit scale and min of sub-block j from the 12 packed bytes.
@@ -191,9 +194,6 @@ struct vxk_qweight {
     uint8_t * act = nullptr;
     float * act_d = nullptr;
     uint8_t * act_ms = nullptr;
-    float * partials = nullptr;
-    int32_t * counters = nullptr;
-    int64_t partial_floats = 0;  // capacity of `partials`
     int32_t * d_error = nullptr;
     cudaEvent_t ev_sync = nullptr;
     std::string last_error;
@@ -221,35 +221,61 @@ vxk_status qguarded(vxk_qweight * w, F && body) {
 void free_qweight(vxk_qweight * w) {
     if (!w) return;
     QwDevice scope(w->cfg.device);
-    for (void * p : {(void *) w->w, (void *) w->act, (void *) w->act_d, (void *) w->act_ms, (void *) w->partials,
-                     (void *) w->counters, (void *) w->d_error})
+    for (void * p : {(void *) w->w, (void *) w->act, (void *) w->act_d, (void *) w->act_ms, (void *) w->d_error})
         if (p) cudaFree(p);
     if (w->ev_sync) cudaEventDestroy(w->ev_sync);
     delete w;
 }
 
 // Column units per CTA for p.nt activation n-tiles over the group's 64-row
-// blocks (p.mats): about two CTAs per SM, as many units per CTA as that
-// allows (fewer splits, less partial traffic), capped by the shared memory
-// that stages them.
+// blocks (p.mats).  A 64-row block is cut into at most 8 splits (one
+// cluster).  For each split size that fits shared memory, the runtime says how
+// many CTAs an SM holds; the plan minimises waves x (units per CTA + a fixed
+// 1.5-unit cost of a CTA's start and cluster reduction), preferring fewer
+// splits on ties (the rule was fitted to a sweep of split sizes on B200 at 16
+// and 64 rows).
 void plan_split(int32_t n_units, int32_t sms, vxk::QmmParams & p) {
-    int cap = n_units;
-    while (cap > 1 && vxk::qmm_smem_bytes(p, cap) > 232448) --cap;
     int64_t blocks = 0;
     for (int i = 0; i < p.n_mats; ++i) blocks += p.mats[i].n_rows / vxk::kQmmRows;
-    const int64_t target = 2 * (int64_t) std::max(1, sms);
-    int64_t per = ((int64_t) n_units * blocks + target - 1) / target;
-    per = std::max<int64_t>(1, std::min<int64_t>(per, cap));
-    p.units_per_split = (int32_t) per;
-    p.n_splits = (int32_t) ((n_units + per - 1) / per);
+    int best_per = 0;
+    double best_cost = 0.0;
+    for (int per = 1; per <= n_units; ++per) {
+        const int splits = (n_units + per - 1) / per;
+        if (splits > vxk::kQmmMaxSplits) continue;
+        if (per > 1 && (n_units + per - 2) / (per - 1) == splits) continue;  // same split count, more units
+        const int smem = vxk::qmm_smem_bytes(p, per);
+        if (smem > 232448) break;
+        const int per_sm = vxk::qmm_ctas_per_sm(p, smem);
+        if (per_sm < 1) continue;
+        const int64_t slots = (int64_t) std::max(1, sms) * per_sm;
+        const int64_t ctas = blocks * splits;
+        // from 32 rows on the product is bound by instruction issue, and the
+        // CTAs of a partial wave finish faster: count waves fractionally; at
+        // 1-16 rows each CTA is latency-bound: count whole waves
+        const double waves = p.nt >= 4 ? std::max(1.0, (double) ctas / (double) slots)
+                                       : (double) ((ctas + slots - 1) / slots);
+        const double cost = waves * (per + 1.5);
+        if (best_per == 0 || cost < best_cost - 1e-9 || (cost <= best_cost + 1e-9 && splits < (n_units + best_per - 1) / best_per)) {
+            best_per = per;
+            best_cost = cost;
+        }
+    }
+    if (const char * env = std::getenv("VXK_QMM_UNITS")) {
+        // fixed units per split (tuning); ignored when it does not fit
+        const int per = std::atoi(env);
+        if (per >= 1 && per <= n_units && (n_units + per - 1) / per <= vxk::kQmmMaxSplits &&
+            vxk::qmm_smem_bytes(p, per) <= 232448)
+            best_per = per;
+    }
+    if (best_per == 0) qfail(VXK_STATUS_INVALID_ARGUMENT, "no column split of this product fits shared memory");
+    p.units_per_split = best_per;
+    p.n_splits = (n_units + best_per - 1) / best_per;
 }
 
 vxk::QmmMat mat_of(const vxk_qweight * w, float * y, int32_t block0) {
     vxk::QmmMat m{};
     m.w = w->w;
     m.y = y;
-    m.partials = w->partials;
-    m.counters = w->counters;
     m.type = (int32_t) w->cfg.type;
     m.n_rows = w->cfg.n_rows;
     m.block0 = block0;
@@ -272,11 +298,6 @@ void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t row
         block0 += ws[i]->cfg.n_rows / vxk::kQmmRows;
     }
     plan_split(w0->n_units, w0->sms, p);
-    if (p.n_splits > 1)
-        for (int i = 0; i < n; ++i)
-            if ((int64_t) p.n_splits * p.nt * 8 * ws[i]->cfg.n_rows > ws[i]->partial_floats)
-                qfail(VXK_STATUS_INVALID_ARGUMENT, "the group's column split needs more partial scratch than a "
-                                                   "member matrix holds; multiply it on its own");
     p.x = x;
     p.act = w0->act;
     p.act_d = w0->act_d;
@@ -373,21 +394,6 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
         VXK_QCUDA(cudaMalloc(&w->act_d, (size_t) w->n_units * 8 * cols * sizeof(float)));
         VXK_QCUDA(cudaMalloc(&w->act_ms, (size_t) w->n_units * w->nt_max * 256));
         VXK_QCUDA(cudaMemset(w->act_ms, 0, (size_t) w->n_units * w->nt_max * 256));
-        // partials for the largest split count any n-tile count can use
-        int64_t part = 0;
-        for (int nt = 1; nt <= w->nt_max; nt *= 2) {
-            vxk::QmmParams p{};
-            p.n_mats = 1;
-            p.mats[0].type = (int32_t) c.type;
-            p.mats[0].n_rows = c.n_rows;
-            p.nt = nt;
-            plan_split(w->n_units, w->sms, p);
-            if (p.n_splits > 1) part = std::max<int64_t>(part, (int64_t) p.n_splits * nt * 8 * c.n_rows);
-        }
-        if (part > 0) VXK_QCUDA(cudaMalloc(&w->partials, (size_t) part * sizeof(float)));
-        w->partial_floats = part;
-        VXK_QCUDA(cudaMalloc(&w->counters, (size_t) (c.n_rows / vxk::kQmmRows) * sizeof(int32_t)));
-        VXK_QCUDA(cudaMemset(w->counters, 0, (size_t) (c.n_rows / vxk::kQmmRows) * sizeof(int32_t)));
         VXK_QCUDA(cudaMalloc(&w->d_error, sizeof(int32_t)));
         VXK_QCUDA(cudaMemset(w->d_error, 0, sizeof(int32_t)));
         VXK_QCUDA(cudaEventCreateWithFlags(&w->ev_sync, cudaEventDisableTiming));

@@ -435,7 +435,8 @@ def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "Q4_K / Q6_K weights, Q8_K rows, int8 tensor-core dots, fp32 scales", "data": "synthetic",
+            "dtype": "Q4_K / Q6_K weights, Q8_K rows, exact integer dots on the tensor cores, fp32 scales",
+            "data": "synthetic",
             "config": {"workload": f"config proj: {cfg['desc']}" + ("" if R == 64 else f" (run with {R} rows)"),
                        "rows_per_gpu": R, "layers": L,
                        "parallelism": f"stream rows sharded, {R}/GPU, no collective",
@@ -446,11 +447,13 @@ def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
                          "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
                                                            f"scaled to this step)",
                          "algorithmic_bytes_per_launch": bytes_per_step, "avg_step_us": round(step_s * 1e6, 2),
-                         "kernel": "qmm_kernel (+ qmm_act_kernel)",
+                         "kernel": "qtc_kernel for Q4_K from 17 rows, qmm_kernel otherwise (+ quantization kernels)",
                          "int8_tops": round(2.0 * R * L * sum(n * k for _, n, k, _ in cfg["mats"]) / step_s / 1e12,
                                             2)},
             "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": int(args.steps * L * 4),
+            # per layer: (quantize + product) for q/k/v and for o; from 17 rows the
+            # Q4_K members take the tcgen05 kernel and v (Q6_K) a separate pair
+            "gpu_launches": int(args.steps * L * (6 if R > 16 else 4)),
             "launch": "CUDA graph of the step's C-ABI calls (vxk_qweight_matmul_group for q/k/v, "
                       "vxk_qweight_matmul for o), replayed per step",
             "clocks": clocks.summary(),

@@ -276,6 +276,40 @@ struct QmmParams {
     int32_t * error;           // device error word (0 = ok)
 };
 
+// tcgen05 form for Q4_K (vxk_qmm_tc.cu): records of 128 rows x 256 columns,
+// [128 rows][128 quant bytes, 16-byte chunk c at c ^ (row % 8)] then
+// [128 rows][6-bit scales[8], mins[8]]; (d, dmin) f16 pairs in a separate
+// [blocks][units][128 rows] array read by the epilogue.
+constexpr int kQtcRecordBytes = 128 * 128 + 128 * 16;
+
+struct QtcMat {
+    const uint8_t * w;         // records [n_rows / 128][n_units][kQtcRecordBytes]
+    const uint8_t * dd;        // [n_rows / 128][n_units][128] (d, dmin) f16 pairs
+    float * y;                 // [rows][n_rows] fp32
+    int32_t n_rows;            // a multiple of 128
+    int32_t block0;            // first 128-row block of this matrix in the grid
+};
+
+struct QtcParams {
+    QtcMat mats[kQmmMaxGroup];
+    int32_t n_mats;
+    int32_t n_units;
+    int32_t rows;              // activation rows, 1 .. npad
+    int32_t npad;              // MMA N: rows padded to 16, 32 or 64
+    int32_t units_per_split;
+    int32_t n_splits;          // <= kQmmMaxSplits: one cluster
+    const float * x;           // [rows][K] fp32
+    uint8_t * b_tiles;         // [n_units][npad x 256 f16, 4 SW128 atoms]
+    uint8_t * bmin_tiles;      // [n_units][npad rows of 128 B, SW128; K 0..15 used]
+    float * dx;                // [n_units][npad]
+    int32_t * error;
+};
+
+// Quantization of x into the f16 tiles, then the tcgen05 product.
+cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream);
+// Clusters of cluster_y product CTAs the device runs at once (0 on error).
+int qtc_max_active_clusters(int npad, int cluster_y);
+
 // Record bytes of one 16 x 256 tile (4352 / 2368 / 3360), 0 for other types.
 int qmm_record_bytes(int type);
 // Dynamic shared memory of the product kernel for the group's types, p.nt

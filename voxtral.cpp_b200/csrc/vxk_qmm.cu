@@ -115,11 +115,48 @@ __device__ __forceinline__ uint32_t map_dsmem(uint32_t local, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
     return v;
 }
+
+// Sums column-major partial blocks [cols][R] of the S cluster CTAs (same
+// shared-memory offset `local` in each) for elements [4*e0, 4*e1), in split
+// order, four rows per load; every split's loads are issued before the sum.
+template <int R>
+__device__ __forceinline__ void cluster_reduce_store(uint32_t local, int S, int e0, int e1, int tid, int nthreads,
+                                                     float * y, int64_t n_rows, int64_t row0) {
+    const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    for (int e = e0 + tid; e < e1; e += nthreads) {
+        float4 v[kQmmMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kQmmMaxSplits; ++sp)
+            if (sp < S) v[sp] = ld_dsmem_f32x4(map_dsmem(local + 16u * (uint32_t) e, (uint32_t) sp));
+        float4 s = v[0];
+#pragma unroll
+        for (int sp = 1; sp < kQmmMaxSplits; ++sp)
+            if (sp < S) {
+                s.x += v[sp].x;
+                s.y += v[sp].y;
+                s.z += v[sp].z;
+                s.w += v[sp].w;
+            }
+        const int col = (4 * e) / R, row = (4 * e) % R;
+        float * dst = y + (int64_t) col * n_rows + row0 + row;
+        if (vec) {
+            *reinterpret_cast<float4 *>(dst) = s;
+        } else {
+            dst[0] = s.x;
+            dst[1] = s.y;
+            dst[2] = s.z;
+            dst[3] = s.w;
+        }
+    }
+}
+
 
 __device__ __forceinline__ void set_error(int32_t * err, int code) {
     if (err) atomicCAS(err, 0, code);
@@ -492,14 +529,10 @@ __device__ __forceinline__ void qmm_cta(const QmmParams & p, const QmmMat & m, c
     cluster_sync();
     if (live) {
         const int S = p.n_splits;
-        const int E = p.rows * kQmmRows;
-        const int e0 = (int) ((int64_t) E * split / S), e1 = (int) ((int64_t) E * (split + 1) / S);
-        const uint32_t local = smem_u32(ptile);
-        for (int e = e0 + tid; e < e1; e += kThreads) {
-            float sum = 0.0f;
-            for (int sp = 0; sp < S; ++sp) sum += ld_dsmem_f32(map_dsmem(local + 4u * (uint32_t) e, (uint32_t) sp));
-            m.y[(int64_t) (e / kQmmRows) * m.n_rows + (int64_t) rb * kQmmRows + (e % kQmmRows)] = sum;
-        }
+        const int E4 = p.rows * kQmmRows / 4;
+        const int e0 = (int) ((int64_t) E4 * split / S), e1 = (int) ((int64_t) E4 * (split + 1) / S);
+        cluster_reduce_store<kQmmRows>(smem_u32(ptile), S, e0, e1, tid, kThreads, m.y, m.n_rows,
+                                       (int64_t) rb * kQmmRows);
     }
     cluster_sync();  // no CTA leaves while another still reads its shared memory
 }

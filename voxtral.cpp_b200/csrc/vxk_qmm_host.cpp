@@ -183,6 +183,26 @@ void repack_record(int type, const uint8_t * src, int64_t row_bytes, int64_t til
 
 int nt_for(int32_t rows) { return rows <= 8 ? 1 : rows <= 16 ? 2 : rows <= 32 ? 4 : 8; }
 
+// Q4_K rows -> the tcgen05 layout (vxk_internal.h, kQtcRecordBytes): per
+// 128-row block and 256-column unit, each row's 128 quant bytes with 16-byte
+// chunk c stored at chunk c ^ (row % 8), then each row's unpacked 6-bit
+// scales and mins; the (d, dmin) pairs go to `dd` [block][unit][row].
+void repack_q4k_tc(const uint8_t * src, int32_t n_rows, int32_t n_cols, uint8_t * rec, uint8_t * dd) {
+    const int64_t units = n_cols / vxk::kQmmUnit;
+    const int64_t rb = gguf_row_bytes(VXK_QTYPE_Q4_K, n_cols);
+    for (int64_t b = 0; b < n_rows / 128; ++b)
+        for (int64_t u = 0; u < units; ++u) {
+            uint8_t * out = rec + (b * units + u) * vxk::kQtcRecordBytes;
+            uint8_t * d = dd + ((b * units + u) * 128) * 4;
+            for (int r = 0; r < 128; ++r) {
+                const uint8_t * blk = src + (b * 128 + r) * rb + u * 144;
+                for (int c = 0; c < 8; ++c) std::memcpy(out + r * 128 + ((c ^ (r & 7)) << 4), blk + 16 + 16 * c, 16);
+                for (int j = 0; j < 8; ++j) q4k_scale_min(blk + 4, j, out + 16384 + r * 16 + j, out + 16384 + r * 16 + 8 + j);
+                std::memcpy(d + r * 4, blk, 4);
+            }
+        }
+}
+
 }  // namespace
 
 struct vxk_qweight {
@@ -194,6 +214,12 @@ struct vxk_qweight {
     uint8_t * act = nullptr;
     float * act_d = nullptr;
     uint8_t * act_ms = nullptr;
+    // tcgen05 form (Q4_K): records, (d, dmin) pairs and the f16 activation tiles
+    uint8_t * w_tc = nullptr;
+    uint8_t * dd_tc = nullptr;
+    uint8_t * tc_b = nullptr;
+    uint8_t * tc_bmin = nullptr;
+    float * tc_dx = nullptr;
     int32_t * d_error = nullptr;
     cudaEvent_t ev_sync = nullptr;
     std::string last_error;
@@ -221,7 +247,8 @@ vxk_status qguarded(vxk_qweight * w, F && body) {
 void free_qweight(vxk_qweight * w) {
     if (!w) return;
     QwDevice scope(w->cfg.device);
-    for (void * p : {(void *) w->w, (void *) w->act, (void *) w->act_d, (void *) w->act_ms, (void *) w->d_error})
+    for (void * p : {(void *) w->w, (void *) w->act, (void *) w->act_d, (void *) w->act_ms, (void *) w->w_tc,
+                     (void *) w->dd_tc, (void *) w->tc_b, (void *) w->tc_bmin, (void *) w->tc_dx, (void *) w->d_error})
         if (p) cudaFree(p);
     if (w->ev_sync) cudaEventDestroy(w->ev_sync);
     delete w;
@@ -282,10 +309,71 @@ vxk::QmmMat mat_of(const vxk_qweight * w, float * y, int32_t block0) {
     return m;
 }
 
-// Quantizes x once and multiplies it by every matrix of ws (shared n_cols,
-// device and activation family), through the first matrix's scratch.
-void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
-               cudaStream_t stream) {
+// True when a product of `rows` rows with w runs on the tcgen05 kernel: Q4_K
+// weights from 17 rows up, where the int8 mma.sync kernel is bound by
+// instruction issue (VXK_QMM_TC=0 / 1 forces it off / on for every size).
+bool use_tc(const vxk_qweight * w, int32_t rows) {
+    if (!w->w_tc) return false;
+    static const int mode = [] {
+        const char * e = std::getenv("VXK_QMM_TC");
+        return e ? std::atoi(e) : -1;
+    }();
+    if (mode == 0) return false;
+    if (mode == 1) return true;
+    return rows > 16;
+}
+
+// Column units per CTA of the tcgen05 product (one 191 KB CTA per SM): the
+// fewest whole waves x (units per CTA + 1.5), splits <= 8, fewer splits on
+// ties; a wave holds as many clusters of `splits` CTAs as the runtime says fit.
+void plan_split_tc(int32_t n_units, int32_t sms, int64_t blocks, vxk::QtcParams & p) {
+    int best = 0;
+    double best_cost = 0.0;
+    for (int per = 1; per <= n_units; ++per) {
+        const int splits = (n_units + per - 1) / per;
+        if (splits > vxk::kQmmMaxSplits) continue;
+        if (per > 1 && (n_units + per - 2) / (per - 1) == splits) continue;
+        int clusters = vxk::qtc_max_active_clusters(p.npad, splits);
+        if (clusters < 1) clusters = std::max(1, sms / splits);
+        const int64_t waves = (blocks + clusters - 1) / clusters;
+        const double cost = (double) waves * (per + 1.5);
+        if (best == 0 || cost < best_cost - 1e-9) {
+            best = per;
+            best_cost = cost;
+        }
+    }
+    p.units_per_split = best;
+    p.n_splits = (n_units + best - 1) / best;
+}
+
+void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
+            int32_t * error, cudaStream_t stream) {
+    vxk_qweight * w0 = ws[0];
+    vxk::QtcParams p{};
+    p.n_mats = n;
+    p.n_units = w0->n_units;
+    p.rows = rows;
+    p.npad = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+    int32_t block0 = 0;
+    for (int i = 0; i < n; ++i) {
+        p.mats[i].w = ws[i]->w_tc;
+        p.mats[i].dd = ws[i]->dd_tc;
+        p.mats[i].y = ys[i];
+        p.mats[i].n_rows = ws[i]->cfg.n_rows;
+        p.mats[i].block0 = block0;
+        block0 += ws[i]->cfg.n_rows / 128;
+    }
+    plan_split_tc(w0->n_units, w0->sms, block0, p);
+    p.x = x;
+    p.b_tiles = w0->tc_b;
+    p.bmin_tiles = w0->tc_bmin;
+    p.dx = w0->tc_dx;
+    p.error = error;
+    VXK_QCUDA(vxk::launch_qtc(p, stream));
+}
+
+void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
+              int32_t * error, cudaStream_t stream) {
     vxk_qweight * w0 = ws[0];
     vxk::QmmParams p{};
     p.n_mats = n;
@@ -302,8 +390,30 @@ void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t row
     p.act = w0->act;
     p.act_d = w0->act_d;
     p.act_ms = w0->act_ms;
-    p.error = w0->d_error;
+    p.error = error;
     VXK_QCUDA(vxk::launch_qmm(p, stream));
+}
+
+// Quantizes x and multiplies it by every matrix of ws (shared n_cols, device
+// and activation family): the matrices that take the tcgen05 kernel in one
+// launch, the others in one int8 mma.sync launch, each with its own
+// quantization of x (the two kernels read different operand layouts).
+void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
+               cudaStream_t stream) {
+    vxk_qweight * tw[vxk::kQmmMaxGroup], * sw[vxk::kQmmMaxGroup];
+    float * ty[vxk::kQmmMaxGroup], * sy[vxk::kQmmMaxGroup];
+    int nt = 0, ns = 0;
+    for (int i = 0; i < n; ++i) {
+        if (use_tc(ws[i], rows)) {
+            tw[nt] = ws[i];
+            ty[nt++] = ys[i];
+        } else {
+            sw[ns] = ws[i];
+            sy[ns++] = ys[i];
+        }
+    }
+    if (nt) run_tc(tw, nt, x, rows, ty, ws[0]->d_error, stream);
+    if (ns) run_sync(sw, ns, x, rows, sy, ws[0]->d_error, stream);
 }
 
 }  // namespace
@@ -394,6 +504,18 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
         VXK_QCUDA(cudaMalloc(&w->act_d, (size_t) w->n_units * 8 * cols * sizeof(float)));
         VXK_QCUDA(cudaMalloc(&w->act_ms, (size_t) w->n_units * w->nt_max * 256));
         VXK_QCUDA(cudaMemset(w->act_ms, 0, (size_t) w->n_units * w->nt_max * 256));
+        if (c.type == VXK_QTYPE_Q4_K && c.n_rows % 128 == 0) {
+            const size_t recs = (size_t) (c.n_rows / 128) * w->n_units;
+            std::vector<uint8_t> hrec(recs * vxk::kQtcRecordBytes), hdd(recs * 128 * 4);
+            repack_q4k_tc(static_cast<const uint8_t *>(gguf_blocks), c.n_rows, c.n_cols, hrec.data(), hdd.data());
+            VXK_QCUDA(cudaMalloc(&w->w_tc, hrec.size()));
+            VXK_QCUDA(cudaMemcpy(w->w_tc, hrec.data(), hrec.size(), cudaMemcpyHostToDevice));
+            VXK_QCUDA(cudaMalloc(&w->dd_tc, hdd.size()));
+            VXK_QCUDA(cudaMemcpy(w->dd_tc, hdd.data(), hdd.size(), cudaMemcpyHostToDevice));
+            VXK_QCUDA(cudaMalloc(&w->tc_b, (size_t) w->n_units * 64 * 512));
+            VXK_QCUDA(cudaMalloc(&w->tc_bmin, (size_t) w->n_units * 64 * 128));
+            VXK_QCUDA(cudaMalloc(&w->tc_dx, (size_t) w->n_units * 64 * sizeof(float)));
+        }
         VXK_QCUDA(cudaMalloc(&w->d_error, sizeof(int32_t)));
         VXK_QCUDA(cudaMemset(w->d_error, 0, sizeof(int32_t)));
         VXK_QCUDA(cudaEventCreateWithFlags(&w->ev_sync, cudaEventDisableTiming));

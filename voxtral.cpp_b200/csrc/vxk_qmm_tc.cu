@@ -1,0 +1,689 @@
+// tcgen05 form of the quantized-weight product for Q4_K weights
+// (vxk_qweight_matmul / _group, include/vxk.h): the same arithmetic as
+// vxk_qmm.cu (ggml's CPU path: x quantized like quantize_row_q8_K_ref, exact
+// integer block dots, fp32 block factors), for batches where the int8
+// mma.sync kernel is bound by instruction issue.
+//
+// The sub-block scales are folded into the tensor-core operand instead of
+// multiplying int32 results: a weight's 4-bit quant q times its 6-bit
+// sub-block scale sc is an integer <= 945, exact in f16, and so are the
+// quantized activations (|q8| <= 127); the fp32 accumulator of one 256-column
+// unit then holds d-free sum_j sc_j * sum q4*q8 exactly (well below 2^24).
+// Q4_K's mins term sum_j m_j * s_j (s_j = sums of 32 quantized activations)
+// is one more K = 16 product: A = (m_0..m_7, 128 m_0..128 m_7), B = (l_0..l_7,
+// h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
+// d_x*d_w and d_x*dmin_w in fp32.
+//
+// CTA = 128 weight rows x a range of 256-column units; 11 warps:
+//   warps 0-3   dequant: thread = weight row (TMEM lane); per unit it reads the
+//               row's 128 quant bytes and 16 scale/min bytes from the raw
+//               ring, writes 128 columns of f16 pairs sc*q into TMEM
+//               (tcgen05.st) and the row's mins row into shared memory
+//   warps 4-7   epilogue: thread = weight row; tcgen05.ld of the unit's
+//               accumulators, fp32 block factors into registers
+//   warp 8      bulk copies of the raw weight records (HBM stream, evict-first)
+//   warp 9      bulk copies of the quantized activations (L2)
+//   warp 10     tcgen05.mma issuer: 16 MMAs (M = 128, N = rows padded to 16,
+//               K = 16, A from TMEM) + 1 mins MMA per unit
+// Column splits of a 128-row block are one thread-block cluster and reduce
+// their partial blocks through distributed shared memory, in split order.
+#include "vxk_internal.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace vxk {
+namespace {
+
+constexpr int kThreads = 352;
+constexpr int kRawStages = 4;
+constexpr int kActStages = 2;
+constexpr int kMaxN = 64;
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr unsigned kFull = 0xffffffffu;
+
+// shared-memory map (offsets from a 1024-aligned base)
+constexpr int kRawBytes = kQtcRecordBytes;                          // 18,432
+constexpr int kActB = kMaxN * 512;                                  // f16 B tile, 4 SW128 atoms
+constexpr int kActBMin = kMaxN * 128;                               // mins B tile (32 B used per row)
+constexpr int kActStage = kActB + kActBMin + 1024;                  // + dx (N floats), padded
+constexpr int kAMin = 128 * 128;                                    // mins A tile
+constexpr int kOffRaw = 0;
+constexpr int kOffAct = kOffRaw + kRawStages * kRawBytes;
+constexpr int kOffAMin = kOffAct + kActStages * kActStage;
+constexpr int kOffBar = kOffAMin + 2 * kAMin;
+// barriers
+constexpr int kBarRawFull = 0;
+constexpr int kBarRawEmpty = kBarRawFull + kRawStages;
+constexpr int kBarActFull = kBarRawEmpty + kRawStages;
+constexpr int kBarActEmpty = kBarActFull + kActStages;
+constexpr int kBarAFull = kBarActEmpty + kActStages;   // [2] A (TMEM) + mins A written
+constexpr int kBarAEmpty = kBarAFull + 2;              // [2] MMAs of the unit done
+constexpr int kBarDFull = kBarAEmpty + 2;              // [2] accumulators complete
+constexpr int kBarDEmpty = kBarDFull + 2;              // [2] accumulators read
+constexpr int kBarDrain = kBarDEmpty + 2;
+constexpr int kNumBars = kBarDrain + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;       // tmem base, abort flag
+constexpr int kSmem = kOffMisc + 16 + 1024;            // + alignment slack
+static_assert(kSmem <= 232448, "tcgen05 quantized product exceeds 227 KB of shared memory");
+static_assert(kRawStages * kRawBytes >= kMaxN * 128 * 4, "the reduction tile fits the raw ring");
+// TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] 384..511
+constexpr int kTmemCols = 512;
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait shared by the roles: gives up when another role raised the
+// CTA's abort flag, or after kWaitNs (then raises it and sets the error word).
+__device__ __forceinline__ bool tc_wait(uint64_t * bar, uint32_t parity, volatile int32_t * abort_flag,
+                                        int32_t * err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitNs) {
+            *abort_flag = 1;
+            if (err) atomicCAS(err, 0, 2);
+            return false;
+        }
+    }
+}
+
+// Bounded wait that ignores the abort flag (copies and MMAs already in flight).
+__device__ __forceinline__ void tc_drain(uint64_t * bar, uint32_t parity) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - t0 > kWaitNs) return;
+    }
+}
+
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy(bool evict_first) {
+    uint64_t policy;
+    if (evict_first)
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    else
+        asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle, descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t) ((saddr >> 4) & 0x3FFFu) | ((uint64_t) ((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t) ((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// D (TMEM) (+)= A (TMEM) . B (shared memory descriptor), kind::f16.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D (TMEM) (+)= A (smem) . B (smem), kind::f16.
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 columns of 32 bits from registers into TMEM.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// 32 lanes x 16 columns of 32 bits from TMEM into registers; the caller
+// waits (tcgen05.wait::ld) before using them, so several loads overlap.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t map_dsmem(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Sums column-major partial blocks [cols][R] of the S cluster CTAs (same
+// shared-memory offset `local` in each) for elements [4*e0, 4*e1), in split
+// order, four rows per load; every split's loads are issued before the sum.
+template <int R>
+__device__ __forceinline__ void cluster_reduce_store(uint32_t local, int S, int e0, int e1, int tid, int nthreads,
+                                                     float * y, int64_t n_rows, int64_t row0) {
+    const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    for (int e = e0 + tid; e < e1; e += nthreads) {
+        float4 v[kQmmMaxSplits];
+#pragma unroll
+        for (int sp = 0; sp < kQmmMaxSplits; ++sp)
+            if (sp < S) v[sp] = ld_dsmem_f32x4(map_dsmem(local + 16u * (uint32_t) e, (uint32_t) sp));
+        float4 s = v[0];
+#pragma unroll
+        for (int sp = 1; sp < kQmmMaxSplits; ++sp)
+            if (sp < S) {
+                s.x += v[sp].x;
+                s.y += v[sp].y;
+                s.z += v[sp].z;
+                s.w += v[sp].w;
+            }
+        const int col = (4 * e) / R, row = (4 * e) % R;
+        float * dst = y + (int64_t) col * n_rows + row0 + row;
+        if (vec) {
+            *reinterpret_cast<float4 *>(dst) = s;
+        } else {
+            dst[0] = s.x;
+            dst[1] = s.y;
+            dst[2] = s.z;
+            dst[3] = s.w;
+        }
+    }
+}
+
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// K position (0..255, the order of the tensor-core operands) of element e of a
+// 256-column unit.  Dequant word w (quant bytes 4w..4w+3 of the row, group
+// g = w/8 of 64 elements, l = 4(w%8)) fills positions 8w..8w+7 with elements
+// g*64 + {l, l+2, 32+l, 34+l, l+1, l+3, 33+l, 35+l}: the order in which
+// masking the nibbles of one 32-bit word yields f16 pairs.
+__device__ __forceinline__ int tc_position(int e) {
+    const int g = e >> 6, within = e & 63;
+    const int hi = within >= 32;
+    const int l = within & 31;
+    const int w = 8 * g + (l >> 2);
+    const int bb = l & 3;
+    const int s = (bb == 0 ? 0 : bb == 2 ? 1 : bb == 1 ? 4 : 5) + (hi ? 2 : 0);
+    return 8 * w + s;
+}
+
+// Byte offset of K position p of operand row n in a unit tile of `rows` rows:
+// 4 atoms of 64 positions, each [rows][128 B] with 128-byte swizzle.
+__device__ __forceinline__ int tc_tile_off(int n, int p, int rows) {
+    const int a = p >> 6, q = p & 63;
+    return a * rows * 128 + (n >> 3) * 1024 + (n & 7) * 128 + ((((q >> 3) ^ (n & 7))) << 4) + (q & 7) * 2;
+}
+
+// ---------------------------------------------------------------------------
+// Activation quantization for the tcgen05 product (quantize_row_q8_K_ref):
+// f16 B tiles in the K order above, the mins B rows (l_j, h_j) and d_x.
+// Grid (units, npad rows), 256 threads: thread t holds column 256u + t.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int u = blockIdx.x, r = blockIdx.y, t = threadIdx.x;
+    const int lane = t & 31, warp = t >> 5;
+    const int64_t K = (int64_t) p.n_units * kQmmUnit;
+    const float x = r < p.rows ? p.x[(int64_t) r * K + (int64_t) u * kQmmUnit + t] : 0.0f;
+    __shared__ unsigned long long red[8];
+    __shared__ float s_max;
+    unsigned long long key = ((unsigned long long) __float_as_uint(fabsf(x)) << 32) | (unsigned) (255 - t);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(kFull, key, o);
+        key = other > key ? other : key;
+    }
+    if (lane == 0) red[warp] = key;
+    __syncthreads();
+    unsigned long long best = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) best = red[w] > best ? red[w] : best;
+    const int arg = 255 - (int) (best & 0xffffffffu);
+    if (t == arg) s_max = x;
+    __syncthreads();
+    const float amax = __uint_as_float((unsigned) (best >> 32));
+    int q = 0;
+    float d = 0.0f;
+    if (amax != 0.0f) {
+        const float iscale = __fdiv_rn(-127.0f, s_max);
+        q = min(127, __float2int_rn(__fmul_rn(iscale, x)));
+        d = __fdiv_rn(1.0f, iscale);
+    }
+    const int np = p.npad;
+    uint8_t * tile = p.b_tiles + (int64_t) u * np * 512;
+    *reinterpret_cast<__half *>(tile + tc_tile_off(r, tc_position(t), np)) = __int2half_rn(q);
+    int s = q;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+    if (lane == 0) {
+        // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j)
+        uint8_t * mrow = p.bmin_tiles + (int64_t) u * np * 128 + (r >> 3) * 1024 + (r & 7) * 128;
+        *reinterpret_cast<__half *>(mrow + ((0 ^ (r & 7)) << 4) + warp * 2) = __int2half_rn(s & 127);
+        *reinterpret_cast<__half *>(mrow + ((1 ^ (r & 7)) << 4) + warp * 2) = __int2half_rn(s >> 7);
+    }
+    if (t == 0) p.dx[(int64_t) u * np + r] = d;
+}
+
+// ---------------------------------------------------------------------------
+// The product.
+// ---------------------------------------------------------------------------
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t * bars = reinterpret_cast<uint64_t *>(base + kOffBar);
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(base + kOffMisc);
+    volatile int32_t * abort_flag = reinterpret_cast<volatile int32_t *>(base + kOffMisc + 4);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // this CTA: 128-row block of matrix m, units [u0, u0 + nu)
+    QtcMat m = p.mats[0];
+#pragma unroll
+    for (int i = 1; i < kQmmMaxGroup; ++i)
+        if (i < p.n_mats && (int) blockIdx.x >= p.mats[i].block0) m = p.mats[i];
+    const int blk = (int) blockIdx.x - m.block0;
+    const int split = (int) blockIdx.y;
+    const int u0 = split * p.units_per_split;
+    const int nu = min(p.n_units, u0 + p.units_per_split) - u0;
+
+    if (tid == 0) {
+        for (int s = 0; s < kRawStages; ++s) {
+            mbar_init(&bars[kBarRawFull + s], 1);
+            mbar_init(&bars[kBarRawEmpty + s], 128);
+        }
+        for (int s = 0; s < kActStages; ++s) {
+            mbar_init(&bars[kBarActFull + s], 1);
+            mbar_init(&bars[kBarActEmpty + s], 1 + 128);   // MMA commit + epilogue threads
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars[kBarAFull + b], 128);
+            mbar_init(&bars[kBarAEmpty + b], 1);
+            mbar_init(&bars[kBarDFull + b], 1);
+            mbar_init(&bars[kBarDEmpty + b], 128);
+        }
+        mbar_init(&bars[kBarDrain], 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    float acc[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) acc[j] = 0.0f;
+
+    if (warp < 4) {
+        // ---------------- dequant: row r = 32 warp + lane ----------------
+        const int r = 32 * warp + lane;
+        const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
+        for (int i = 0; i < nu; ++i) {
+            const int s = i % kRawStages, b = i & 1;
+            bool ok = tc_wait(&bars[kBarRawFull + s], (uint32_t) (i / kRawStages) & 1u, abort_flag, p.error);
+            ok = ok && tc_wait(&bars[kBarAEmpty + b], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error);
+            if (!__all_sync(kFull, ok)) break;
+            tc_fence_after();
+            const uint8_t * raw = base + kOffRaw + s * kRawBytes;
+            const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
+            const uint32_t scw[2] = {scm.x, scm.y};
+            const uint32_t mnw[2] = {scm.z, scm.w};
+            // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word)
+#pragma unroll
+            for (int half = 0; half < 4; ++half) {
+                uint32_t cols[32];
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int c = 2 * half + cc;  // chunk: words 4c .. 4c+3, group c / 2
+                    const uint4 v4 = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
+                    const int g = c >> 1;
+                    const float sl = (float) ((scw[g >> 1] >> (8 * ((2 * g) & 3))) & 0xffu);
+                    const float sh = (float) ((scw[g >> 1] >> (8 * ((2 * g + 1) & 3))) & 0xffu);
+                    const __half2 slo = __float2half2_rn(sl), shi = __float2half2_rn(sh);
+                    const __half2 blo = __float2half2_rn(-1024.0f * sl), bhi = __float2half2_rn(-1024.0f * sh);
+                    const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t v = vw[k];
+                        const uint32_t h0 = (v & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t h1 = ((v >> 4) & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t h2 = ((v >> 8) & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t h3 = ((v >> 12) & 0x000F000Fu) | 0x64006400u;
+                        cols[16 * cc + 4 * k + 0] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h0), slo, blo));
+                        cols[16 * cc + 4 * k + 1] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h1), shi, bhi));
+                        cols[16 * cc + 4 * k + 2] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h2), slo, blo));
+                        cols[16 * cc + 4 * k + 3] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h3), shi, bhi));
+                    }
+                }
+                tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
+            }
+            // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact)
+            uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 1024 + (r & 7) * 128;
+            uint32_t m0[4], m1[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float a0 = (float) ((mnw[(2 * j) >> 2] >> (8 * ((2 * j) & 3))) & 0xffu);
+                const float a1 = (float) ((mnw[(2 * j + 1) >> 2] >> (8 * ((2 * j + 1) & 3))) & 0xffu);
+                m0[j] = h2_bits(__floats2half2_rn(a0, a1));
+                m1[j] = h2_bits(__floats2half2_rn(128.0f * a0, 128.0f * a1));
+            }
+            *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
+            *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
+            mbar_arrive(&bars[kBarRawEmpty + s]);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(&bars[kBarAFull + b]);
+        }
+    } else if (warp < 8) {
+        // ---------------- epilogue: row r = 32 (warp - 4) + lane ----------------
+        const int q = warp & 3;
+        const int r = 32 * q + lane;
+        const uint32_t lane_off = (uint32_t) (32 * q) << 16;
+        const uint32_t * dd = reinterpret_cast<const uint32_t *>(m.dd) + ((int64_t) blk * p.n_units + u0) * 128 + r;
+        uint32_t ddn = nu > 0 ? __ldg(dd) : 0u;
+        for (int i = 0; i < nu; ++i) {
+            const int b = i & 1, t = i % kActStages;
+            const uint32_t ddc = ddn;
+            if (i + 1 < nu) ddn = __ldg(dd + (int64_t) (i + 1) * 128);
+            bool ok = tc_wait(&bars[kBarDFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error);
+            ok = ok && tc_wait(&bars[kBarActFull + t], (uint32_t) (i / kActStages) & 1u, abort_flag, p.error);
+            if (!__all_sync(kFull, ok)) break;
+            tc_fence_after();
+            const float2 dw = __half22float2(*reinterpret_cast<const __half2 *>(&ddc));  // (d, dmin)
+            const float * dx = reinterpret_cast<const float *>(base + kOffAct + t * kActStage + kActB + kActBMin);
+            // 32 columns of D and of Dmin in flight per wait
+#pragma unroll
+            for (int c0 = 0; c0 < N; c0 += 32) {
+                constexpr int W = N < 32 ? N : 32;
+                uint32_t v[2][16], mm[2][16];
+#pragma unroll
+                for (int h = 0; h < W / 16; ++h) {
+                    tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * h + lane_off, v[h]);
+                    tmem_ld16_nowait(tmem + 384 + 64 * b + c0 + 16 * h + lane_off, mm[h]);
+                }
+                tmem_ld_wait();
+#pragma unroll
+                for (int h = 0; h < W / 16; ++h)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float x = dx[c0 + 16 * h + j];
+                        acc[c0 + 16 * h + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[h][j]),
+                                                    fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[h][j]),
+                                                         acc[c0 + 16 * h + j]));
+                    }
+            }
+            tc_fence_before();
+            mbar_arrive(&bars[kBarDEmpty + b]);
+            mbar_arrive(&bars[kBarActEmpty + t]);
+        }
+    } else if (warp == 8) {
+        // ---------------- raw weight records (HBM) ----------------
+        if (lane == 0) {
+            const uint64_t pol = l2_policy(true);
+            const uint8_t * src = m.w + ((int64_t) blk * p.n_units + u0) * kRawBytes;
+            int i = 0;
+            for (; i < nu; ++i) {
+                const int s = i % kRawStages;
+                if (!tc_wait(&bars[kBarRawEmpty + s], ((uint32_t) (i / kRawStages) & 1u) ^ 1u, abort_flag, p.error))
+                    break;
+                mbar_expect_tx(&bars[kBarRawFull + s], kRawBytes);
+                bulk_g2s(base + kOffRaw + s * kRawBytes, src + (int64_t) i * kRawBytes, kRawBytes,
+                         &bars[kBarRawFull + s], pol);
+            }
+            if (*abort_flag)
+                for (int d = i > kRawStages ? i - kRawStages : 0; d < i; ++d)
+                    tc_drain(&bars[kBarRawFull + d % kRawStages], (uint32_t) (d / kRawStages) & 1u);
+        }
+        __syncwarp();
+    } else if (warp == 9) {
+        // ---------------- quantized activations (L2), after the producer kernel ----------------
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (lane == 0) {
+            const uint64_t pol = l2_policy(false);
+            int i = 0;
+            for (; i < nu; ++i) {
+                const int t = i % kActStages, u = u0 + i;
+                if (!tc_wait(&bars[kBarActEmpty + t], ((uint32_t) (i / kActStages) & 1u) ^ 1u, abort_flag, p.error))
+                    break;
+                uint8_t * st = base + kOffAct + t * kActStage;
+                mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 128 + N * 4));
+                bulk_g2s(st, p.b_tiles + (int64_t) u * N * 512, N * 512, &bars[kBarActFull + t], pol);
+                bulk_g2s(st + kActB, p.bmin_tiles + (int64_t) u * N * 128, N * 128, &bars[kBarActFull + t], pol);
+                bulk_g2s(st + kActB + kActBMin, p.dx + (int64_t) u * N, N * 4, &bars[kBarActFull + t], pol);
+            }
+            if (*abort_flag)
+                for (int d = i > kActStages ? i - kActStages : 0; d < i; ++d)
+                    tc_drain(&bars[kBarActFull + d % kActStages], (uint32_t) (d / kActStages) & 1u);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- tcgen05.mma issuer ----------------
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        if (lane == 0) {
+            // fp32 D, f16 A and B, both K-major, N, M = 128
+            const uint32_t idesc = (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
+            for (int i = 0; i < nu; ++i) {
+                const int b = i & 1, t = i % kActStages;
+                if (!tc_wait(&bars[kBarAFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error)) break;
+                if (!tc_wait(&bars[kBarActFull + t], (uint32_t) (i / kActStages) & 1u, abort_flag, p.error)) break;
+                if (!tc_wait(&bars[kBarDEmpty + b], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error)) break;
+                tc_fence_after();
+                const uint32_t bt = smem_u32(base + kOffAct + t * kActStage);
+#pragma unroll
+                for (int ks = 0; ks < 16; ++ks)
+                    mma_ts(tmem + 256 + 64 * b, tmem + 128 * b + 8 * ks,
+                           sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024), idesc, ks != 0);
+                mma_ss(tmem + 384 + 64 * b, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
+                       sw128_desc(bt + kActB, 16, 1024), idesc, 0);
+                tc_commit(&bars[kBarAEmpty + b]);
+                tc_commit(&bars[kBarActEmpty + t]);
+                tc_commit(&bars[kBarDFull + b]);
+            }
+            // every MMA issued completes before the CTA frees TMEM
+            tc_commit(&bars[kBarDrain]);
+            tc_drain(&bars[kBarDrain], 0);
+        }
+        __syncwarp();
+    }
+
+    // ---- results: the splits of a 128-row block are one cluster; each CTA
+    // leaves its partial block [N columns][128 rows] in its own shared memory
+    // (the drained raw ring) and, after a cluster barrier, sums slice `split`
+    // of the block over all splits in split order (DSMEM).  Every thread of
+    // every CTA reaches both cluster barriers. ----
+    tc_fence_before();
+    __syncthreads();
+    float * ptile = reinterpret_cast<float *>(base + kOffRaw);
+    const bool live = *abort_flag == 0;
+    if (live && warp >= 4 && warp < 8) {
+        const int r = 32 * (warp & 3) + lane;
+#pragma unroll
+        for (int j = 0; j < N; ++j) ptile[j * 128 + r] = acc[j];
+    }
+    cluster_sync();
+    if (live) {
+        const int S = p.n_splits;
+        const int E4 = p.rows * 128 / 4;
+        const int e0 = (int) ((int64_t) E4 * split / S), e1 = (int) ((int64_t) E4 * (split + 1) / S);
+        cluster_reduce_store<128>(smem_u32(ptile), S, e0, e1, tid, kThreads, m.y, m.n_rows, (int64_t) blk * 128);
+    }
+    cluster_sync();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+template <typename K>
+cudaError_t launch_ex(K kernel, dim3 grid, unsigned block, size_t smem, cudaStream_t stream, const QtcParams & p,
+                      unsigned cluster_y) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = cluster_y;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cluster_y > 1 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+template <int N>
+cudaError_t launch_n(const QtcParams & p, cudaStream_t stream) {
+    static bool raised[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!raised[dev]) {
+        e = cudaFuncSetAttribute(qtc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess) return e;
+        raised[dev] = true;
+    }
+    const int blocks = p.mats[p.n_mats - 1].block0 + p.mats[p.n_mats - 1].n_rows / 128;
+    return launch_ex(qtc_kernel<N>, dim3((unsigned) blocks, (unsigned) p.n_splits), kThreads, kSmem, stream, p,
+                     (unsigned) p.n_splits);
+}
+
+template <int N>
+int clusters_n(int cluster_y) {
+    static bool raised[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (!raised[dev]) {
+        if (cudaFuncSetAttribute(qtc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+            return 0;
+        raised[dev] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1, (unsigned) cluster_y, 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned) cluster_y;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, qtc_kernel<N>, &cfg) != cudaSuccess) return 0;
+    return n;
+}
+
+}  // namespace
+
+int qtc_max_active_clusters(int npad, int cluster_y) {
+    switch (npad) {
+        case 16: return clusters_n<16>(cluster_y);
+        case 32: return clusters_n<32>(cluster_y);
+        default: return clusters_n<64>(cluster_y);
+    }
+}
+
+cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream) {
+    if (p.n_mats < 1 || p.n_mats > kQmmMaxGroup || p.rows < 1 || p.rows > p.npad || p.units_per_split < 1 ||
+        p.n_splits < 1 || p.n_splits > kQmmMaxSplits || (int64_t) p.units_per_split * (p.n_splits - 1) >= p.n_units)
+        return cudaErrorInvalidValue;
+    if (p.npad != 16 && p.npad != 32 && p.npad != 64) return cudaErrorInvalidValue;
+    for (int i = 0; i < p.n_mats; ++i)
+        if (p.mats[i].n_rows % 128 != 0) return cudaErrorInvalidValue;
+    cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) p.npad), 256, 0, stream, p, 1);
+    if (e != cudaSuccess) return e;
+    switch (p.npad) {
+        case 16: return launch_n<16>(p, stream);
+        case 32: return launch_n<32>(p, stream);
+        default: return launch_n<64>(p, stream);
+    }
+}
+
+}  // namespace vxk

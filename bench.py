@@ -451,9 +451,8 @@ def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
                          "int8_tops": round(2.0 * R * L * sum(n * k for _, n, k, _ in cfg["mats"]) / step_s / 1e12,
                                             2)},
             "cpu_baseline": cpu, "e2e": e2e,
-            # per layer: (quantize + product) for q/k/v and for o; from 17 rows the
-            # Q4_K members take the tcgen05 kernel and v (Q6_K) a separate pair
-            "gpu_launches": int(args.steps * L * (6 if R > 16 else 4)),
+            # per layer: (quantize + product) for q/k/v and for o
+            "gpu_launches": int(args.steps * L * 4),
             "launch": "CUDA graph of the step's C-ABI calls (vxk_qweight_matmul_group for q/k/v, "
                       "vxk_qweight_matmul for o), replayed per step",
             "clocks": clocks.summary(),

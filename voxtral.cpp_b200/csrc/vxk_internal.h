@@ -276,18 +276,24 @@ struct QmmParams {
     int32_t * error;           // device error word (0 = ok)
 };
 
-// tcgen05 form for Q4_K (vxk_qmm_tc.cu): records of 128 rows x 256 columns,
+// tcgen05 form for Q4_K / Q6_K (vxk_qmm_tc.cu): records of 128 rows x 256 columns,
 // [128 rows][128 quant bytes, 16-byte chunk c at c ^ (row % 8)] then
 // [128 rows][6-bit scales[8], mins[8]]; (d, dmin) f16 pairs in a separate
 // [blocks][units][128 rows] array read by the epilogue.
+// Q6_K: [128 rows][128 low-nibble bytes, chunk c at c ^ (row % 8)], then
+// [128 rows][64 high-2-bit bytes, chunk c at c ^ ((row / 2) % 4)], then
+// [128 rows][16 int8 scales]; `dd` holds (d, 0).
 constexpr int kQtcRecordBytes = 128 * 128 + 128 * 16;
+constexpr int kQtcRecordBytesQ6K = 128 * 128 + 128 * 64 + 128 * 16;
 
 struct QtcMat {
-    const uint8_t * w;         // records [n_rows / 128][n_units][kQtcRecordBytes]
+    const uint8_t * w;         // records [n_rows / 128][n_units][record bytes of the type]
     const uint8_t * dd;        // [n_rows / 128][n_units][128] (d, dmin) f16 pairs
     float * y;                 // [rows][n_rows] fp32
     int32_t n_rows;            // a multiple of 128
     int32_t block0;            // first 128-row block of this matrix in the grid
+    int32_t type;              // 12 = Q4_K, 14 = Q6_K
+    int32_t reserved;
 };
 
 struct QtcParams {

@@ -183,6 +183,29 @@ void repack_record(int type, const uint8_t * src, int64_t row_bytes, int64_t til
 
 int nt_for(int32_t rows) { return rows <= 8 ? 1 : rows <= 16 ? 2 : rows <= 32 ? 4 : 8; }
 
+// Q6_K rows -> the tcgen05 layout (vxk_internal.h, kQtcRecordBytesQ6K): per
+// 128-row block and unit, each row's 128 low-nibble bytes (chunk c at
+// c ^ (row % 8)), 64 high-2-bit bytes (chunk c at c ^ ((row / 2) % 4)) and 16
+// int8 scales; (d, 0) pairs to `dd`.
+void repack_q6k_tc(const uint8_t * src, int32_t n_rows, int32_t n_cols, uint8_t * rec, uint8_t * dd) {
+    const int64_t units = n_cols / vxk::kQmmUnit;
+    const int64_t rb = gguf_row_bytes(VXK_QTYPE_Q6_K, n_cols);
+    for (int64_t b = 0; b < n_rows / 128; ++b)
+        for (int64_t u = 0; u < units; ++u) {
+            uint8_t * out = rec + (b * units + u) * vxk::kQtcRecordBytesQ6K;
+            uint8_t * d = dd + ((b * units + u) * 128) * 4;
+            for (int r = 0; r < 128; ++r) {
+                const uint8_t * blk = src + (b * 128 + r) * rb + u * 210;
+                for (int c = 0; c < 8; ++c) std::memcpy(out + r * 128 + ((c ^ (r & 7)) << 4), blk + 16 * c, 16);
+                for (int c = 0; c < 4; ++c)
+                    std::memcpy(out + 16384 + r * 64 + ((c ^ ((r >> 1) & 3)) << 4), blk + 128 + 16 * c, 16);
+                std::memcpy(out + 24576 + r * 16, blk + 192, 16);
+                std::memcpy(d + r * 4, blk + 208, 2);
+                d[r * 4 + 2] = d[r * 4 + 3] = 0;
+            }
+        }
+}
+
 // Q4_K rows -> the tcgen05 layout (vxk_internal.h, kQtcRecordBytes): per
 // 128-row block and 256-column unit, each row's 128 quant bytes with 16-byte
 // chunk c stored at chunk c ^ (row % 8), then each row's unpacked 6-bit
@@ -310,7 +333,7 @@ vxk::QmmMat mat_of(const vxk_qweight * w, float * y, int32_t block0) {
 }
 
 // True when a product of `rows` rows with w runs on the tcgen05 kernel: Q4_K
-// weights from 17 rows up, where the int8 mma.sync kernel is bound by
+// and Q6_K weights from 17 rows up, where the int8 mma.sync kernel is bound by
 // instruction issue (VXK_QMM_TC=0 / 1 forces it off / on for every size).
 bool use_tc(const vxk_qweight * w, int32_t rows) {
     if (!w->w_tc) return false;
@@ -361,6 +384,7 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, 
         p.mats[i].y = ys[i];
         p.mats[i].n_rows = ws[i]->cfg.n_rows;
         p.mats[i].block0 = block0;
+        p.mats[i].type = (int32_t) ws[i]->cfg.type;
         block0 += ws[i]->cfg.n_rows / 128;
     }
     plan_split_tc(w0->n_units, w0->sms, block0, p);
@@ -504,10 +528,14 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
         VXK_QCUDA(cudaMalloc(&w->act_d, (size_t) w->n_units * 8 * cols * sizeof(float)));
         VXK_QCUDA(cudaMalloc(&w->act_ms, (size_t) w->n_units * w->nt_max * 256));
         VXK_QCUDA(cudaMemset(w->act_ms, 0, (size_t) w->n_units * w->nt_max * 256));
-        if (c.type == VXK_QTYPE_Q4_K && c.n_rows % 128 == 0) {
+        if ((c.type == VXK_QTYPE_Q4_K || c.type == VXK_QTYPE_Q6_K) && c.n_rows % 128 == 0) {
+            const bool q6 = c.type == VXK_QTYPE_Q6_K;
             const size_t recs = (size_t) (c.n_rows / 128) * w->n_units;
-            std::vector<uint8_t> hrec(recs * vxk::kQtcRecordBytes), hdd(recs * 128 * 4);
-            repack_q4k_tc(static_cast<const uint8_t *>(gguf_blocks), c.n_rows, c.n_cols, hrec.data(), hdd.data());
+            std::vector<uint8_t> hrec(recs * (q6 ? vxk::kQtcRecordBytesQ6K : vxk::kQtcRecordBytes)), hdd(recs * 128 * 4);
+            if (q6)
+                repack_q6k_tc(static_cast<const uint8_t *>(gguf_blocks), c.n_rows, c.n_cols, hrec.data(), hdd.data());
+            else
+                repack_q4k_tc(static_cast<const uint8_t *>(gguf_blocks), c.n_rows, c.n_cols, hrec.data(), hdd.data());
             VXK_QCUDA(cudaMalloc(&w->w_tc, hrec.size()));
             VXK_QCUDA(cudaMemcpy(w->w_tc, hrec.data(), hrec.size(), cudaMemcpyHostToDevice));
             VXK_QCUDA(cudaMalloc(&w->dd_tc, hdd.size()));

@@ -1,4 +1,4 @@
-// tcgen05 form of the quantized-weight product for Q4_K weights
+// tcgen05 form of the quantized-weight product for Q4_K and Q6_K weights
 // (vxk_qweight_matmul / _group, include/vxk.h): the same arithmetic as
 // vxk_qmm.cu (ggml's CPU path: x quantized like quantize_row_q8_K_ref, exact
 // integer block dots, fp32 block factors), for batches where the int8
@@ -9,6 +9,10 @@
 // sub-block scale sc is an integer <= 945, exact in f16, and so are the
 // quantized activations (|q8| <= 127); the fp32 accumulator of one 256-column
 // unit then holds d-free sum_j sc_j * sum q4*q8 exactly (well below 2^24).
+// Q6_K's scaled quants sc*q reach 4096, past f16's exact integers, so they
+// are two exact operands, 16*(sc>>4)*q and (sc&15)*q, multiplied into the
+// same accumulator (a unit in two halves of 128 columns, so both fit one A
+// buffer).
 // Q4_K's mins term sum_j m_j * s_j (s_j = sums of 32 quantized activations)
 // is one more K = 16 product: A = (m_0..m_7, 128 m_0..128 m_7), B = (l_0..l_7,
 // h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
@@ -45,7 +49,7 @@ constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr unsigned kFull = 0xffffffffu;
 
 // shared-memory map (offsets from a 1024-aligned base)
-constexpr int kRawBytes = kQtcRecordBytes;                          // 18,432
+constexpr int kRawBytes = kQtcRecordBytesQ6K;                      // ring stage: the larger record
 constexpr int kActB = kMaxN * 512;                                  // f16 B tile, 4 SW128 atoms
 constexpr int kActBMin = kMaxN * 128;                               // mins B tile (32 B used per row)
 constexpr int kActStage = kActB + kActBMin + 1024;                  // + dx (N floats), padded
@@ -69,6 +73,7 @@ constexpr int kOffMisc = kOffBar + kNumBars * 8;       // tmem base, abort flag
 constexpr int kSmem = kOffMisc + 16 + 1024;            // + alignment slack
 static_assert(kSmem <= 232448, "tcgen05 quantized product exceeds 227 KB of shared memory");
 static_assert(kRawStages * kRawBytes >= kMaxN * 128 * 4, "the reduction tile fits the raw ring");
+static_assert(kOffAct % 1024 == 0 && kOffAMin % 1024 == 0 && kActStage % 1024 == 0, "128-byte swizzle atoms align");
 // TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] 384..511
 constexpr int kTmemCols = 512;
 
@@ -341,6 +346,61 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     if (t == 0) p.dx[(int64_t) u * np + r] = d;
 }
 
+// One half (128 columns) of a Q6_K unit for row r into TMEM: A_hi = 16*(sc>>4)*q
+// at columns [abase, abase+64) and A_lo = (sc&15)*q at [abase+64, abase+128),
+// q = q6 - 32, in the K order of the Q4_K words (see tc_position): word
+// 8gg + 4c4 + k of half h holds elements 64gg + {l, l+2, 32+l, 34+l, l+1, l+3,
+// 33+l, 35+l} (l = 16c4 + 4k) of the half, the low (gg = 0) or high nibbles of
+// the quant bytes at l and 32+l and 2-bit fields 4gg and 4gg+2 of the high
+// plane byte at l.  Both parts are exact f16 integers.
+__device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int h, uint32_t abase) {
+    const uint8_t * ql = raw + r * 128;
+    const uint8_t * qh = raw + 16384 + r * 64;
+    uint4 A[2], B[2], H[2];
+#pragma unroll
+    for (int c4 = 0; c4 < 2; ++c4) {
+        A[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + c4) ^ (r & 7)) << 4));
+        B[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + 2 + c4) ^ (r & 7)) << 4));
+        H[c4] = *reinterpret_cast<const uint4 *>(qh + (((2 * h + c4) ^ ((r >> 1) & 3)) << 4));
+    }
+    const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    const __half2 c1056 = __float2half2_rn(1056.0f);
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 2; ++c4) {
+            const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two parts
+            const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
+            const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
+            const __half2 fah = __float2half2_rn((float) (16 * (sa >> 4))), fal = __float2half2_rn((float) (sa & 15));
+            const __half2 fbh = __float2half2_rn((float) (16 * (sb >> 4))), fbl = __float2half2_rn((float) (sb & 15));
+            const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
+            const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
+            const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int ns = 4 * gg, fa = 4 * gg, fb = 4 * gg + 2;
+                uint32_t pv[4];
+                pv[0] = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fa) & 0x00030003u) << 4) | 0x64006400u;
+                pv[1] = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fb) & 0x00030003u) << 4) | 0x64006400u;
+                pv[2] = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fa + 8)) & 0x00030003u) << 4) | 0x64006400u;
+                pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4) | 0x64006400u;
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                    const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&pv[x]), c1056);
+                    const bool pa = (x & 1) == 0;  // pv[0], pv[2] from the bytes at l, pv[1], pv[3] at 32+l
+                    hi[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fah : fbh));
+                    lo[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fal : fbl));
+                }
+            }
+        }
+        tmem_st32(abase + 32 * gg, hi);
+        tmem_st32(abase + 64 + 32 * gg, lo);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // The product.
 // ---------------------------------------------------------------------------
@@ -392,70 +452,84 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    float acc[N];
-#pragma unroll
-    for (int j = 0; j < N; ++j) acc[j] = 0.0f;
+    float * ptile = reinterpret_cast<float *>(base + kOffRaw);  // [N][128] partial block at the end
 
     if (warp < 4) {
         // ---------------- dequant: row r = 32 warp + lane ----------------
         const int r = 32 * warp + lane;
         const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
-        for (int i = 0; i < nu; ++i) {
-            const int s = i % kRawStages, b = i & 1;
-            bool ok = tc_wait(&bars[kBarRawFull + s], (uint32_t) (i / kRawStages) & 1u, abort_flag, p.error);
-            ok = ok && tc_wait(&bars[kBarAEmpty + b], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error);
-            if (!__all_sync(kFull, ok)) break;
-            tc_fence_after();
+        const bool q6 = m.type == 14;
+        const int phases = q6 ? 2 : 1;  // A buffers filled per unit (Q6_K: two halves)
+        int j = 0;                      // A-phase counter: buffer j & 1, use j >> 1
+        bool stop = false;
+        for (int i = 0; i < nu && !stop; ++i) {
+            const int s = i % kRawStages;
+            if (!__all_sync(kFull, tc_wait(&bars[kBarRawFull + s], (uint32_t) (i / kRawStages) & 1u, abort_flag,
+                                           p.error)))
+                break;
             const uint8_t * raw = base + kOffRaw + s * kRawBytes;
-            const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
-            const uint32_t scw[2] = {scm.x, scm.y};
-            const uint32_t mnw[2] = {scm.z, scm.w};
-            // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word)
-#pragma unroll
-            for (int half = 0; half < 4; ++half) {
-                uint32_t cols[32];
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const int c = 2 * half + cc;  // chunk: words 4c .. 4c+3, group c / 2
-                    const uint4 v4 = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
-                    const int g = c >> 1;
-                    const float sl = (float) ((scw[g >> 1] >> (8 * ((2 * g) & 3))) & 0xffu);
-                    const float sh = (float) ((scw[g >> 1] >> (8 * ((2 * g + 1) & 3))) & 0xffu);
-                    const __half2 slo = __float2half2_rn(sl), shi = __float2half2_rn(sh);
-                    const __half2 blo = __float2half2_rn(-1024.0f * sl), bhi = __float2half2_rn(-1024.0f * sh);
-                    const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint32_t v = vw[k];
-                        const uint32_t h0 = (v & 0x000F000Fu) | 0x64006400u;
-                        const uint32_t h1 = ((v >> 4) & 0x000F000Fu) | 0x64006400u;
-                        const uint32_t h2 = ((v >> 8) & 0x000F000Fu) | 0x64006400u;
-                        const uint32_t h3 = ((v >> 12) & 0x000F000Fu) | 0x64006400u;
-                        cols[16 * cc + 4 * k + 0] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h0), slo, blo));
-                        cols[16 * cc + 4 * k + 1] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h1), shi, bhi));
-                        cols[16 * cc + 4 * k + 2] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h2), slo, blo));
-                        cols[16 * cc + 4 * k + 3] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h3), shi, bhi));
-                    }
+            for (int h = 0; h < phases; ++h, ++j) {
+                const int b = j & 1;
+                if (!__all_sync(kFull, tc_wait(&bars[kBarAEmpty + b], ((uint32_t) (j >> 1) & 1u) ^ 1u, abort_flag,
+                                               p.error))) {
+                    stop = true;
+                    break;
                 }
-                tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
-            }
-            // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact)
-            uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 1024 + (r & 7) * 128;
-            uint32_t m0[4], m1[4];
+                tc_fence_after();
+                if (q6) {
+                    dequant_q6_half(raw, r, h, tmem + 128 * b + lane_off);
+                } else {
+                    const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
+                    const uint32_t scw[2] = {scm.x, scm.y};
+                    const uint32_t mnw[2] = {scm.z, scm.w};
+                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float a0 = (float) ((mnw[(2 * j) >> 2] >> (8 * ((2 * j) & 3))) & 0xffu);
-                const float a1 = (float) ((mnw[(2 * j + 1) >> 2] >> (8 * ((2 * j + 1) & 3))) & 0xffu);
-                m0[j] = h2_bits(__floats2half2_rn(a0, a1));
-                m1[j] = h2_bits(__floats2half2_rn(128.0f * a0, 128.0f * a1));
+                    for (int half = 0; half < 4; ++half) {
+                        uint32_t cols[32];
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const int c = 2 * half + cc;  // chunk: words 4c .. 4c+3, group c / 2
+                            const uint4 v4 = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
+                            const int g = c >> 1;
+                            const float sl = (float) ((scw[g >> 1] >> (8 * ((2 * g) & 3))) & 0xffu);
+                            const float sh = (float) ((scw[g >> 1] >> (8 * ((2 * g + 1) & 3))) & 0xffu);
+                            const __half2 slo = __float2half2_rn(sl), shi = __float2half2_rn(sh);
+                            const __half2 blo = __float2half2_rn(-1024.0f * sl), bhi = __float2half2_rn(-1024.0f * sh);
+                            const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t v = vw[k];
+                                const uint32_t h0 = (v & 0x000F000Fu) | 0x64006400u;
+                                const uint32_t h1 = ((v >> 4) & 0x000F000Fu) | 0x64006400u;
+                                const uint32_t h2 = ((v >> 8) & 0x000F000Fu) | 0x64006400u;
+                                const uint32_t h3 = ((v >> 12) & 0x000F000Fu) | 0x64006400u;
+                                cols[16 * cc + 4 * k + 0] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h0), slo, blo));
+                                cols[16 * cc + 4 * k + 1] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h1), shi, bhi));
+                                cols[16 * cc + 4 * k + 2] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h2), slo, blo));
+                                cols[16 * cc + 4 * k + 3] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h3), shi, bhi));
+                            }
+                        }
+                        tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
+                    }
+                    // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact)
+                    uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 1024 + (r & 7) * 128;
+                    uint32_t m0[4], m1[4];
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const float a0 = (float) ((mnw[(2 * jj) >> 2] >> (8 * ((2 * jj) & 3))) & 0xffu);
+                        const float a1 = (float) ((mnw[(2 * jj + 1) >> 2] >> (8 * ((2 * jj + 1) & 3))) & 0xffu);
+                        m0[jj] = h2_bits(__floats2half2_rn(a0, a1));
+                        m1[jj] = h2_bits(__floats2half2_rn(128.0f * a0, 128.0f * a1));
+                    }
+                    *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
+                    *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
+                }
+                if (h == phases - 1) mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tc_fence_before();
+                mbar_arrive(&bars[kBarAFull + b]);
             }
-            *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
-            *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
-            mbar_arrive(&bars[kBarRawEmpty + s]);
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc_fence_before();
-            mbar_arrive(&bars[kBarAFull + b]);
         }
     } else if (warp < 8) {
         // ---------------- epilogue: row r = 32 (warp - 4) + lane ----------------
@@ -464,6 +538,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         const uint32_t lane_off = (uint32_t) (32 * q) << 16;
         const uint32_t * dd = reinterpret_cast<const uint32_t *>(m.dd) + ((int64_t) blk * p.n_units + u0) * 128 + r;
         uint32_t ddn = nu > 0 ? __ldg(dd) : 0u;
+        float acc[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) acc[j] = 0.0f;
         for (int i = 0; i < nu; ++i) {
             const int b = i & 1, t = i % kActStages;
             const uint32_t ddc = ddn;
@@ -474,9 +551,26 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             tc_fence_after();
             const float2 dw = __half22float2(*reinterpret_cast<const __half2 *>(&ddc));  // (d, dmin)
             const float * dx = reinterpret_cast<const float *>(base + kOffAct + t * kActStage + kActB + kActBMin);
-            // 32 columns of D and of Dmin in flight per wait
+            if (m.type == 14) {
+                // Q6_K: acc += (d_w * d_x) * D
 #pragma unroll
-            for (int c0 = 0; c0 < N; c0 += 32) {
+                for (int c0 = 0; c0 < N; c0 += 32) {
+                    constexpr int W = N < 32 ? N : 32;
+                    uint32_t v[2][16];
+#pragma unroll
+                    for (int hh = 0; hh < W / 16; ++hh) tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * hh + lane_off, v[hh]);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int hh = 0; hh < W / 16; ++hh)
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dx[c0 + 16 * hh + jj]),
+                                                          __uint_as_float(v[hh][jj]), acc[c0 + 16 * hh + jj]);
+                }
+            } else {
+                // Q4_K: 32 columns of D and of Dmin in flight per wait
+#pragma unroll
+                for (int c0 = 0; c0 < N; c0 += 32) {
                 constexpr int W = N < 32 ? N : 32;
                 uint32_t v[2][16], mm[2][16];
 #pragma unroll
@@ -495,23 +589,30 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                                                          acc[c0 + 16 * h + j]));
                     }
             }
+            }
             tc_fence_before();
             mbar_arrive(&bars[kBarDEmpty + b]);
             mbar_arrive(&bars[kBarActEmpty + t]);
+        }
+        // Partial block into the raw ring: every raw read of this CTA happened
+        // before the last unit's MMAs, which this thread has waited for.
+        if (!*abort_flag) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) ptile[j * 128 + r] = acc[j];
         }
     } else if (warp == 8) {
         // ---------------- raw weight records (HBM) ----------------
         if (lane == 0) {
             const uint64_t pol = l2_policy(true);
-            const uint8_t * src = m.w + ((int64_t) blk * p.n_units + u0) * kRawBytes;
+            const uint32_t rec = m.type == 14 ? kQtcRecordBytesQ6K : kQtcRecordBytes;
+            const uint8_t * src = m.w + ((int64_t) blk * p.n_units + u0) * rec;
             int i = 0;
             for (; i < nu; ++i) {
                 const int s = i % kRawStages;
                 if (!tc_wait(&bars[kBarRawEmpty + s], ((uint32_t) (i / kRawStages) & 1u) ^ 1u, abort_flag, p.error))
                     break;
-                mbar_expect_tx(&bars[kBarRawFull + s], kRawBytes);
-                bulk_g2s(base + kOffRaw + s * kRawBytes, src + (int64_t) i * kRawBytes, kRawBytes,
-                         &bars[kBarRawFull + s], pol);
+                mbar_expect_tx(&bars[kBarRawFull + s], rec);
+                bulk_g2s(base + kOffRaw + s * kRawBytes, src + (int64_t) i * rec, rec, &bars[kBarRawFull + s], pol);
             }
             if (*abort_flag)
                 for (int d = i > kRawStages ? i - kRawStages : 0; d < i; ++d)
@@ -545,22 +646,45 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         if (lane == 0) {
             // fp32 D, f16 A and B, both K-major, N, M = 128
             const uint32_t idesc = (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
-            for (int i = 0; i < nu; ++i) {
-                const int b = i & 1, t = i % kActStages;
-                if (!tc_wait(&bars[kBarAFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error)) break;
+            const bool q6 = m.type == 14;
+            const int phases = q6 ? 2 : 1;
+            int j = 0;
+            bool stop = false;
+            for (int i = 0; i < nu && !stop; ++i) {
+                const int bd = i & 1, t = i % kActStages;
                 if (!tc_wait(&bars[kBarActFull + t], (uint32_t) (i / kActStages) & 1u, abort_flag, p.error)) break;
-                if (!tc_wait(&bars[kBarDEmpty + b], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error)) break;
-                tc_fence_after();
+                if (!tc_wait(&bars[kBarDEmpty + bd], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error)) break;
                 const uint32_t bt = smem_u32(base + kOffAct + t * kActStage);
+                const uint32_t dacc = tmem + 256 + 64 * bd;
+                for (int h = 0; h < phases; ++h, ++j) {
+                    const int b = j & 1;
+                    if (!tc_wait(&bars[kBarAFull + b], (uint32_t) (j >> 1) & 1u, abort_flag, p.error)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (q6) {
+                        // half h: K positions 128h .. 128h+127, A_hi then A_lo per step
 #pragma unroll
-                for (int ks = 0; ks < 16; ++ks)
-                    mma_ts(tmem + 256 + 64 * b, tmem + 128 * b + 8 * ks,
-                           sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024), idesc, ks != 0);
-                mma_ss(tmem + 384 + 64 * b, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
-                       sw128_desc(bt + kActB, 16, 1024), idesc, 0);
-                tc_commit(&bars[kBarAEmpty + b]);
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const int ks = 8 * h + kk;
+                            const uint64_t bdesc = sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024);
+                            mma_ts(dacc, tmem + 128 * b + 8 * kk, bdesc, idesc, (h | kk) != 0);
+                            mma_ts(dacc, tmem + 128 * b + 64 + 8 * kk, bdesc, idesc, 1);
+                        }
+                    } else {
+#pragma unroll
+                        for (int ks = 0; ks < 16; ++ks)
+                            mma_ts(dacc, tmem + 128 * b + 8 * ks,
+                                   sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024), idesc, ks != 0);
+                        mma_ss(tmem + 384 + 64 * bd, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
+                               sw128_desc(bt + kActB, 16, 1024), idesc, 0);
+                    }
+                    tc_commit(&bars[kBarAEmpty + b]);
+                }
+                if (stop) break;
                 tc_commit(&bars[kBarActEmpty + t]);
-                tc_commit(&bars[kBarDFull + b]);
+                tc_commit(&bars[kBarDFull + bd]);
             }
             // every MMA issued completes before the CTA frees TMEM
             tc_commit(&bars[kBarDrain]);
@@ -576,13 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     // every CTA reaches both cluster barriers. ----
     tc_fence_before();
     __syncthreads();
-    float * ptile = reinterpret_cast<float *>(base + kOffRaw);
     const bool live = *abort_flag == 0;
-    if (live && warp >= 4 && warp < 8) {
-        const int r = 32 * (warp & 3) + lane;
-#pragma unroll
-        for (int j = 0; j < N; ++j) ptile[j * 128 + r] = acc[j];
-    }
     cluster_sync();
     if (live) {
         const int S = p.n_splits;

@@ -47,6 +47,9 @@ CONFIGS = {
     "head": dict(kind="head", rows=64, vocab=131072, dim=3072, dtype=1,
                  desc="greedy head: tied logits (131072 x 3072 f16 embeddings) + argmax for 64 streams/GPU, "
                       "logits written like the reference's decoder_logits"),
+    "headq": dict(kind="headq", rows=64, vocab=131072, dim=3072, qtype=14,
+                  desc="greedy head over Q6_K tied embeddings (Q4_K_M's tok_embeddings, 131072 x 3072) for 64 "
+                       "streams/GPU, logits written like the reference's decoder_logits"),
     "proj": dict(kind="qmm", layers=30, rows=64,
                  mats=(("q", 4096, 3072, 12), ("k", 1024, 3072, 12), ("v", 1024, 3072, 14), ("o", 3072, 4096, 12)),
                  desc="decoder attention projections q/k/v/o of 30 layers for 64 batched streams/GPU, "
@@ -485,6 +488,140 @@ def qmm_cpu_sample(cfg, seed, seconds):
     return 1.0 / (per_row * scale), done
 
 
+def run_headq(args, cfg, world, rank, local, dist, torch, vxk):
+    """Greedy head over quantized embeddings: one step = the quantized logits
+    product of every stream's row (vxk_qweight) and their argmax, through
+    vxk_head_logits_argmax_q."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    R, V, D, t = cfg["rows"], cfg["vocab"], cfg["dim"], cfg["qtype"]
+    rng = np.random.default_rng(args.seed + rank)
+    w_host = vx_oracle.random_qblocks(t, V, D, rng)
+    qw = vxk.QWeight(w_host, device=local, type=t, n_rows=V, n_cols=D, max_batch=R)
+    del w_host
+    head = vxk.Head(device=local, dim=D, vocab=V, dtype=1)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    NSETS = 4
+    xs = torch.randn((NSETS, R, D), device="cuda", generator=gen)
+    am = torch.empty((R,), dtype=torch.int32, device="cuda")
+    lg = torch.empty((R, V), device="cuda")
+
+    def step(i):
+        head.logits_argmax_q(qw, xs[i % NSETS].data_ptr(), R, am.data_ptr(), lg.data_ptr(), sh)
+
+    for i in range(args.warmup):
+        step(i)
+    qw.sync(sh)
+    head.sync(sh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    qw.sync(sh)
+    head.sync(sh)
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    step_s = ms / 1000.0 / args.steps
+    bytes_per_step = qmm_gguf_bytes(V, D, t) + R * D * 4 + R * V * 4 + R * 4  # W once, x, logits, argmax
+    achieved = bytes_per_step / step_s / 1e9
+    peak, peak_kind = load_peaks()
+    traffic_ratio, traffic_src = load_traffic(args.config)
+
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.randn((R, D)).pin_memory()
+        ha = torch.empty((R,), dtype=torch.int32).pin_memory()
+        dx = torch.empty((R, D), device="cuda")
+
+        def host_step():
+            dx.copy_(hx, non_blocking=True)
+            head.logits_argmax_q(qw, dx.data_ptr(), R, am.data_ptr(), lg.data_ptr(), sh)
+            ha.copy_(am, non_blocking=True)
+
+        host_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            host_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(dist, f0.elapsed_time(f1), "cuda")
+        e2e = {"value": round(world * R * args.steps / (ems / 1000.0), 1), "unit": "rows/s",
+               "h2d_bytes_per_step": int(hx.numel()) * 4, "d2h_bytes_per_step": int(ha.numel()) * 4,
+               "ms_per_step": round(ems / args.steps, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cps, done = headq_cpu_sample(cfg, args.seed, args.cpu_seconds)
+        cpu = {"value": round(cps, 4), "unit": "rows/s", "cores": 1, "kind": "port",
+               "sample": f"{done} single-row products over a {V // 64}-row slice of the vocabulary by the oracle "
+                         f"(oracle/vx_qmm.c, one thread), scaled to {V} rows"}
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "greedy head rows/s (Q6_K tied logits + argmax)",
+            "value": round(world * R * args.steps / (ms / 1000.0), 1),
+            "unit": "rows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "Q6_K weights, Q8_K rows, exact integer dots on the tensor cores, fp32 scales",
+            "data": "synthetic",
+            "config": {"workload": f"config headq: {cfg['desc']}", "rows_per_gpu": R, "vocab": V, "dim": D,
+                       "parallelism": f"rows sharded, {R}/GPU, no collective",
+                       "l2": f"inputs larger than L2 ({qmm_gguf_bytes(V, D, t) / 1e6:.0f} MB of weights per step)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_step),
+                         "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
+                                                           f"scaled to this step)",
+                         "algorithmic_bytes_per_launch": bytes_per_step, "avg_step_us": round(step_s * 1e6, 2),
+                         "kernel": "qtc_kernel (+ quantization, argmax)"},
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(args.steps * 4),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    head.close()
+    qw.close()
+
+
+def headq_cpu_sample(cfg, seed, seconds):
+    """Times the oracle's quantized product on one row over 1/64 of the
+    vocabulary; returns rows/s scaled to the full head."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    V, D, t = cfg["vocab"] // 64, cfg["dim"], cfg["qtype"]
+    w = vx_oracle.random_qblocks(t, V, D, rng)
+    x = rng.standard_normal((1, D)).astype(np.float32)
+    vx_oracle.qmatmul(t, w, V, D, x)
+    done = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        vx_oracle.qmatmul(t, w, V, D, x)
+        done += 1
+    el = time.perf_counter() - t0
+    return done / el / 64.0, done
+
+
 def head_cpu_sample(cfg, seed, seconds):
     """Times the oracle's greedy head (float64 BLAS on all host cores) on 4
     rows over 1/8 of the vocabulary; returns rows/s scaled to the full head."""
@@ -545,6 +682,7 @@ TRAFFIC_PROFILES = {
     "4": "enc_tc_kernel_config4.md",
     "head": "head_kernel_config_head.md",
     "proj": "qmm_kernel_config_proj.md",
+    "headq": "qtc_kernel_config_headq.md",
 }
 
 
@@ -722,6 +860,19 @@ def run_reference(args, cfg, rank, world):
                 "e2e": {"value": round(cps, 4), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
+    if cfg.get("kind") == "headq":
+        cps, done = headq_cpu_sample(cfg, args.seed, 20.0)
+        line = {"impl": "reference", "metric": "greedy head rows/s (Q6_K tied logits + argmax)",
+                "value": round(cps, 4), "unit": "rows/s", "n_gpus": args.gpus, "steps": done, "warmup": 1,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "Q6_K weights, Q8_K rows, exact integer dots", "data": "synthetic",
+                "config": {"workload": f"config headq: {cfg['desc']}"},
+                "cpu_baseline": {"value": round(cps, 4), "unit": "rows/s", "cores": 1, "kind": "port",
+                                 "sample": f"{done} single-row products over 1/64 of the vocabulary by the oracle "
+                                           f"(oracle/vx_qmm.c), scaled"},
+                "e2e": {"value": round(cps, 4), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if cfg.get("kind") == "qmm":
         tps, done = qmm_cpu_sample(cfg, args.seed, 20.0)
         line = {"impl": "reference", "metric": "attention-projection tokens/s (q/k/v/o, Q4_K_M, 30 layers)",
@@ -811,6 +962,12 @@ def main():
 
     if cfg.get("kind") == "head":
         run_head(args, cfg, world, rank, local, dist, torch, vxk)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if cfg.get("kind") == "headq":
+        run_headq(args, cfg, world, rank, local, dist, torch, vxk)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

@@ -446,6 +446,23 @@ VXK_API vxk_status vxk_head_logits_argmax(vxk_head * head, const void * w, const
  *  (VXK_STATUS_TIMEOUT or VXK_STATUS_BACKEND_ERROR). */
 VXK_API vxk_status vxk_head_sync(vxk_head * head, void * cuda_stream, int32_t timeout_ms);
 
+typedef struct vxk_qweight vxk_qweight;
+
+/**
+ * The greedy head over GGUF-quantized tied embeddings (a Q4_K_M model stores
+ * tok_embeddings as Q6_K: src/voxtral-quantize.cpp:146-148): logits = the
+ * quantized product of x with W (vxk_qweight_matmul, ggml's arithmetic) and
+ * argmax[r] = the first index of row r's largest logit (ggml_argmax).
+ *   w       a vxk_qweight of vocab rows x dim columns on the head's device
+ *   x       [rows][dim] fp32, device; rows <= 64 and <= w's max_batch
+ *   argmax  [rows] int32, device
+ *   logits  [rows][vocab] fp32, device, or NULL: the head then keeps them in a
+ *           scratch it allocates on the first such call
+ * Device errors: vxk_qweight_sync(w) for the product, vxk_head_sync(head).
+ */
+VXK_API vxk_status vxk_head_logits_argmax_q(vxk_head * head, vxk_qweight * w, const float * x, int32_t rows,
+                                            int32_t * argmax, float * logits, void * cuda_stream);
+
 /* ======================================================================== */
 /* Quantized-weight matrix product (GGUF Q8_0 / Q4_K / Q6_K weights)        */
 /* ======================================================================== */
@@ -457,9 +474,9 @@ typedef enum vxk_qtype {
     VXK_QTYPE_Q6_K = 14   /* {u8 ql[128]; u8 qh[64]; i8 scales[16]; f16 d}: 210 B per 256 */
 } vxk_qtype;
 
-/** One quantized weight matrix resident on a device, plus the scratch of
- *  its products (one product at a time per matrix). */
-typedef struct vxk_qweight vxk_qweight;
+/* vxk_qweight (declared with the greedy head above): one quantized weight
+ * matrix resident on a device, plus the scratch of its products (one product
+ * at a time per matrix). */
 
 typedef struct vxk_qweight_config {
     uint32_t struct_size;

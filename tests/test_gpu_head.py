@@ -105,3 +105,63 @@ def test_head_full_vocabulary(vxk, oracle):
     want = np.argmax(ref, axis=1)
     assert np.max(np.abs(lg - ref)) <= LOGIT_TOL
     _check_argmax(am, ref, want)
+
+
+def _run_q(vxk, oracle, t, w_blocks, vocab, dim, x, keep_logits=True):
+    import torch
+
+    rows = x.shape[0]
+    qw = vxk.QWeight(w_blocks, type=t, n_rows=vocab, n_cols=dim, max_batch=64)
+    head = vxk.Head(dim=dim, vocab=vocab, dtype=F16)
+    stream = torch.cuda.current_stream().cuda_stream
+    xd = torch.from_numpy(x).cuda()
+    am = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+    lg = torch.full((rows, vocab), float("nan"), device="cuda")
+    head.logits_argmax_q(qw, xd.data_ptr(), rows, am.data_ptr(), lg.data_ptr() if keep_logits else 0, stream)
+    qw.sync(stream)
+    head.sync(stream)
+    out = am.cpu().numpy(), lg.cpu().numpy()
+    head.close()
+    qw.close()
+    return out
+
+
+@pytest.mark.parametrize("t", [14, 12, 8])   # Q6_K (Q4_K_M's tok_embeddings), Q4_K, Q8_0
+@pytest.mark.parametrize("rows", [1, 40])
+def test_quantized_head_matches_oracle(vxk, oracle, t, rows):
+    """Greedy head over quantized tied embeddings (vxk_head_logits_argmax_q):
+    logits within the quantized product's fp32 bound of the oracle
+    (oracle.qmatmul, ggml's arithmetic), argmax equal to the oracle's wherever
+    the top two logits are further apart than twice the bound; the same ids
+    when the head keeps the logits in its own scratch."""
+    rng = np.random.default_rng(400 + t + rows)
+    vocab, dim = 4096, 3072
+    w = oracle.random_qblocks(t, vocab, dim, rng)
+    x = rng.normal(0, 1, (rows, dim)).astype(np.float32)
+    am, lg = _run_q(vxk, oracle, t, w, vocab, dim, x)
+    ref, mag, terms = oracle.qmatmul(t, w, vocab, dim, x)
+    bound = (2 * terms + 8) * 2.0**-24 * mag + 1e-30
+    assert np.all(np.abs(lg.astype(np.float64) - ref) <= bound)
+    for r in range(rows):
+        order = np.argsort(-ref[r], kind="stable")
+        if ref[r, order[0]] - ref[r, order[1]] > 2 * bound[r].max():
+            assert am[r] == order[0]
+        else:
+            assert ref[r, am[r]] >= ref[r, order[0]] - 2 * bound[r].max()
+    am2, _ = _run_q(vxk, oracle, t, w, vocab, dim, x, keep_logits=False)
+    np.testing.assert_array_equal(am, am2)
+
+
+def test_quantized_head_first_index_on_exact_ties(vxk, oracle):
+    # rows 100 and 3000 hold the same blocks and the largest logit: ggml_argmax takes 100
+    rng = np.random.default_rng(9)
+    vocab, dim = 4096, 512
+    w = oracle.random_qblocks(8, vocab, dim, rng)
+    blk = w.reshape(vocab, dim // 32, 34)
+    blk[100, :, 0:2] = np.asarray([0.05] * (dim // 32), np.float16).view(np.uint8).reshape(-1, 2)
+    blk[100, :, 2:] = 127
+    blk[3000] = blk[100]
+    x = np.ones((2, dim), np.float32)
+    am, lg = _run_q(vxk, oracle, 8, w, vocab, dim, x)
+    assert lg[0, 100] == lg[0, 3000] and lg[0, 100] == lg[0].max()
+    assert list(am) == [100, 100]

@@ -27,6 +27,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 namespace vxk {
 namespace {
 
@@ -357,6 +359,38 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
     }
 }
 
+// Argmax of logits already in memory (the head over quantized embeddings):
+// every CTA scans a slice of one row and folds the first index of its largest
+// value into the row's key.  Grid (slices, rows).
+__global__ void __launch_bounds__(256) head_argmax_kernel(const float * logits, int32_t vocab,
+                                                          unsigned long long * best) {
+    __shared__ unsigned long long red[8];
+    const int r = blockIdx.y;
+    const float * row = logits + (int64_t) r * vocab;
+    unsigned long long key = 0ull;  // below every value's key
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < vocab; i += gridDim.x * 256) {
+        const unsigned long long k = best_key(row[i], i);
+        key = k > key ? k : key;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(kFull, key, o);
+        key = other > key ? other : key;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) key = red[w] > key ? red[w] : key;
+        key = red[0] > key ? red[0] : key;
+        atomicMax(&best[r], key);
+    }
+}
+
+__global__ void head_keys_to_ids_kernel(const unsigned long long * best, int32_t rows, int32_t * argmax) {
+    const int r = threadIdx.x;
+    if (r < rows) argmax[r] = (int32_t) (0xFFFFFFFFu - (uint32_t) (best[r] & 0xFFFFFFFFull));
+}
+
 template <typename K>
 cudaError_t launch_pdl(K kernel, dim3 grid, unsigned block, size_t smem, cudaStream_t stream, bool pdl,
                        const CUtensorMap * tmw, const CUtensorMap * tmx, const HeadParams & p) {
@@ -376,6 +410,17 @@ cudaError_t launch_pdl(K kernel, dim3 grid, unsigned block, size_t smem, cudaStr
 }  // namespace
 
 int head_smem_bytes() { return kHeadSmem; }
+
+cudaError_t launch_head_argmax(const float * logits, int32_t rows, int32_t vocab, unsigned long long * best,
+                               int32_t * argmax, cudaStream_t stream) {
+    if (rows <= 0 || rows > kHeadRows || vocab <= 0) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(best, 0, (size_t) rows * sizeof(unsigned long long), stream);
+    if (e != cudaSuccess) return e;
+    const int slices = std::max(1, std::min(64, (vocab + 2047) / 2048));
+    head_argmax_kernel<<<dim3((unsigned) slices, (unsigned) rows), 256, 0, stream>>>(logits, vocab, best);
+    head_keys_to_ids_kernel<<<1, kHeadRows, 0, stream>>>(best, rows, argmax);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_head(const HeadParams & p, const CUtensorMap & tmw, const CUtensorMap & tmx, int grid,
                         cudaStream_t stream) {

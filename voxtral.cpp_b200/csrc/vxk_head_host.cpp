@@ -85,6 +85,7 @@ struct vxk_head {
     vxk_head_config cfg{};
     uint16_t * xh = nullptr;
     unsigned long long * best = nullptr;
+    float * qlogits = nullptr;  // logits of the quantized path when the caller passes none
     int32_t * d_error = nullptr;
     cudaEvent_t ev_sync = nullptr;
     CUtensorMap map_x{};
@@ -118,6 +119,7 @@ void free_head(vxk_head * h) {
     HeadDevice scope(h->cfg.device);
     if (h->xh) cudaFree(h->xh);
     if (h->best) cudaFree(h->best);
+    if (h->qlogits) cudaFree(h->qlogits);
     if (h->d_error) cudaFree(h->d_error);
     if (h->ev_sync) cudaEventDestroy(h->ev_sync);
     delete h;
@@ -223,6 +225,31 @@ vxk_status vxk_head_logits_argmax(vxk_head * head, const void * w, const float *
             p.dtype = (int32_t) c.dtype;
             VXK_HCUDA(vxk::launch_head(p, map_w, head->map_x, head->grid, cs));
         }
+    });
+}
+
+vxk_status vxk_head_logits_argmax_q(vxk_head * head, vxk_qweight * w, const float * x, int32_t rows,
+                                    int32_t * argmax, float * logits, void * cuda_stream) {
+    if (!head) return VXK_STATUS_INVALID_ARGUMENT;
+    return hguarded(head, [&] {
+        const vxk_head_config & c = head->cfg;
+        if (!w || !x || !argmax) hfail(VXK_STATUS_INVALID_ARGUMENT, "null argument");
+        const vxk::QweightShape sh = vxk::qweight_shape(w);
+        if (sh.device != c.device || sh.n_rows != c.vocab || sh.n_cols != c.dim)
+            hfail(VXK_STATUS_INVALID_ARGUMENT, "the quantized embeddings must be vocab x dim on the head's device");
+        if (rows < 1 || rows > vxk::kHeadRows || rows > sh.max_batch)
+            hfail(VXK_STATUS_INVALID_ARGUMENT, "rows must be in [1, min(64, the matrix's max_batch)]");
+        HeadDevice scope(c.device);
+        cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
+        float * out = logits;
+        if (!out) {
+            if (!head->qlogits)
+                VXK_HCUDA(cudaMalloc(&head->qlogits, (size_t) vxk::kHeadRows * c.vocab * sizeof(float)));
+            out = head->qlogits;
+        }
+        const vxk_status st = vxk_qweight_matmul(w, x, rows, out, cuda_stream);
+        if (st != VXK_STATUS_OK) hfail(st, "quantized logits product failed");
+        VXK_HCUDA(vxk::launch_head_argmax(out, rows, c.vocab, head->best, argmax, cs));
     });
 }
 

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+struct vxk_qweight;
+
 namespace vxk {
 
 // Decoder kernels are specialised for the Voxtral decoder head shape.
@@ -238,6 +240,10 @@ struct HeadParams {
 cudaError_t launch_head(const HeadParams & p, const CUtensorMap & tmw, const CUtensorMap & tmx, int grid,
                         cudaStream_t stream);
 int head_smem_bytes();
+// Argmax of rows x vocab fp32 logits in device memory (first index of the
+// largest value per row) through the per-row keys `best`.
+cudaError_t launch_head_argmax(const float * logits, int32_t rows, int32_t vocab, unsigned long long * best,
+                               int32_t * argmax, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Quantized-weight matrix product (vxk_qweight_*)
@@ -315,6 +321,12 @@ struct QtcParams {
 cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream);
 // Clusters of cluster_y product CTAs the device runs at once (0 on error).
 int qtc_max_active_clusters(int npad, int cluster_y);
+
+// Shape of a quantized matrix (for the greedy head over quantized embeddings).
+struct QweightShape {
+    int32_t device, type, n_rows, n_cols, max_batch;
+};
+QweightShape qweight_shape(const vxk_qweight * w);
 
 // Record bytes of one 16 x 256 tile (4352 / 2368 / 3360), 0 for other types.
 int qmm_record_bytes(int type);

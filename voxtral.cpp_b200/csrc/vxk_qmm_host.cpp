@@ -442,6 +442,14 @@ void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t row
 
 }  // namespace
 
+namespace vxk {
+
+QweightShape qweight_shape(const vxk_qweight * w) {
+    return QweightShape{w->cfg.device, (int32_t) w->cfg.type, w->cfg.n_rows, w->cfg.n_cols, w->cfg.max_batch};
+}
+
+}  // namespace vxk
+
 extern "C" {
 
 vxk_qweight_config vxk_qweight_default_config(void) {

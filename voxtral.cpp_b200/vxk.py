@@ -151,6 +151,7 @@ SIGNATURES = {
     "vxk_head_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
     "vxk_head_logits_argmax": (_I32, [_P, _P, _P, _I32, _P, _P, _P]),
     "vxk_head_sync": (_I32, [_P, _P, _I32]),
+    "vxk_head_logits_argmax_q": (_I32, [_P, _P, _P, _I32, _P, _P, _P]),
     "vxk_qweight_default_config": (QWeightConfig, []),
     "vxk_qweight_packed_bytes": (_I32, [_I32, _I32, _I32, C.POINTER(C.c_size_t)]),
     "vxk_qweight_repack": (_I32, [_I32, _I32, _I32, _P, C.c_size_t, _P, C.c_size_t]),
@@ -422,6 +423,12 @@ class Head:
         self._check(self.lib.vxk_head_logits_argmax(self.h, C.c_void_p(w_ptr), C.c_void_p(x_ptr), rows,
                                                     C.c_void_p(argmax_ptr), C.c_void_p(logits_ptr or None),
                                                     C.c_void_p(cuda_stream)))
+
+    def logits_argmax_q(self, qweight, x_ptr, rows, argmax_ptr, logits_ptr=0, cuda_stream=0):
+        """Greedy head over quantized embeddings (vxk_head_logits_argmax_q)."""
+        self._check(self.lib.vxk_head_logits_argmax_q(self.h, qweight.h, C.c_void_p(x_ptr), rows,
+                                                      C.c_void_p(argmax_ptr), C.c_void_p(logits_ptr or None),
+                                                      C.c_void_p(cuda_stream)))
 
     def sync(self, cuda_stream=0, timeout_ms=10000):
         self._check(self.lib.vxk_head_sync(self.h, C.c_void_p(cuda_stream), timeout_ms))

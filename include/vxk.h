@@ -533,6 +533,54 @@ VXK_API vxk_status vxk_qweight_matmul(vxk_qweight * w, const float * x, int32_t 
 VXK_API vxk_status vxk_qweight_matmul_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows,
                                             float * const * ys, void * cuda_stream);
 
+/* ======================================================================== */
+/* GGUF model files                                                         */
+/* ======================================================================== */
+
+/** A GGUF file (v2/v3) mapped read-only: its metadata and tensor table, as the
+ *  reference's loader reads them (src/voxtral.cpp:1040-1190). */
+typedef struct vxk_gguf vxk_gguf;
+
+typedef struct vxk_gguf_tensor {
+    const char * name;   /* owned by the vxk_gguf */
+    int32_t type;        /* ggml_type (0 F32, 1 F16, 8 Q8_0, 12 Q4_K, 14 Q6_K, 30 BF16, ...) */
+    int32_t n_dims;
+    int64_t ne[4];       /* ggml order: ne[0] is the row length; unused dims are 1 */
+    uint64_t offset;     /* absolute file offset of the tensor's data */
+    uint64_t n_bytes;    /* 0 for a ggml type this library does not know */
+} vxk_gguf_tensor;
+
+/** Metadata value types (GGUF): 0 u8, 1 i8, 2 u16, 3 i16, 4 u32, 5 i32, 6 f32,
+ *  7 bool, 8 string, 9 array, 10 u64, 11 i64, 12 f64. */
+VXK_API vxk_status vxk_gguf_open(const char * path, vxk_gguf ** out);
+VXK_API void vxk_gguf_close(vxk_gguf * g);
+/** Last error of g, or of the last failed vxk_gguf_open when g is NULL. */
+VXK_API vxk_status vxk_gguf_last_error(const vxk_gguf * g, char * buf, size_t capacity);
+VXK_API uint32_t vxk_gguf_version(const vxk_gguf * g);
+VXK_API int64_t vxk_gguf_n_tensors(const vxk_gguf * g);
+VXK_API vxk_status vxk_gguf_get_tensor(const vxk_gguf * g, int64_t index, vxk_gguf_tensor * out);
+/** Index of the named tensor, -1 when absent. */
+VXK_API int64_t vxk_gguf_find_tensor(const vxk_gguf * g, const char * name);
+/** Host pointer to a tensor's bytes inside the mapping (valid until close). */
+VXK_API const void * vxk_gguf_tensor_data(const vxk_gguf * g, int64_t index);
+VXK_API int64_t vxk_gguf_n_keys(const vxk_gguf * g);
+VXK_API const char * vxk_gguf_key(const vxk_gguf * g, int64_t index);
+/** Value type of a key, -1 when absent. */
+VXK_API int32_t vxk_gguf_key_type(const vxk_gguf * g, const char * key);
+/** Integer and bool values widened to int64 (gguf_get_val_i32 / _bool / ...). */
+VXK_API vxk_status vxk_gguf_get_int(const vxk_gguf * g, const char * key, int64_t * out);
+/** f32 / f64 values. */
+VXK_API vxk_status vxk_gguf_get_float(const vxk_gguf * g, const char * key, double * out);
+VXK_API vxk_status vxk_gguf_get_str(const vxk_gguf * g, const char * key, const char ** out);
+/** Arrays: element type and count; numeric elements as raw little-endian
+ *  bytes in the mapping (data NULL for string arrays: use _get_array_str). */
+VXK_API vxk_status vxk_gguf_get_array(const vxk_gguf * g, const char * key, int32_t * elem_type, int64_t * count,
+                                      const void ** data);
+VXK_API vxk_status vxk_gguf_get_array_str(const vxk_gguf * g, const char * key, int64_t index, const char ** out);
+/** vxk_qweight_create for a 2-D Q8_0 / Q4_K / Q6_K tensor of the file. */
+VXK_API vxk_status vxk_qweight_create_from_gguf(const vxk_gguf * g, const char * tensor, int32_t device,
+                                                int32_t max_batch, vxk_qweight ** out);
+
 /** Bounded wait for cuda_stream, then the matrix's device error word. */
 VXK_API vxk_status vxk_qweight_sync(vxk_qweight * w, void * cuda_stream, int32_t timeout_ms);
 

@@ -155,3 +155,40 @@ def test_group_rejects_mixed_families_and_shapes(vxk, oracle):
             vxk.qweight_matmul_group(group, x.data_ptr(), 8, [y.data_ptr()] * len(group))
     for m in (a, b, c):
         m.close()
+
+
+def test_qweight_from_gguf_file(vxk, oracle, tmp_path):
+    """A model file's tensors straight to the device (vxk_qweight_create_from_gguf):
+    the product of each quantized tensor matches the oracle on the same bytes."""
+    gguf = pytest.importorskip("gguf")
+    import torch
+
+    rng = np.random.default_rng(31)
+    path = tmp_path / "m.gguf"
+    w = gguf.GGUFWriter(str(path), "voxtral_realtime")
+    spec = {"dec.blk.0.attn_q.weight": (Q4_K, gguf.GGMLQuantizationType.Q4_K),
+            "dec.blk.0.attn_v.weight": (Q6_K, gguf.GGMLQuantizationType.Q6_K),
+            "adapter.0.weight": (Q8_0, gguf.GGMLQuantizationType.Q8_0)}
+    n, k, rows = 256, 1024, 24
+    blocks = {}
+    for name, (t, gt) in spec.items():
+        blocks[name] = oracle.random_qblocks(t, n, k, rng)
+        w.add_tensor(name, blocks[name], raw_dtype=gt)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    g = vxk.Gguf(path)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    for name, (t, _) in spec.items():
+        qw = g.qweight(name, max_batch=rows)
+        y = torch.full((rows, n), float("nan"), device="cuda")
+        qw.matmul(xd.data_ptr(), rows, y.data_ptr(), stream)
+        qw.sync(stream)
+        _check(oracle, t, blocks[name], n, k, x, y.cpu().numpy())
+        qw.close()
+    with pytest.raises(vxk.VxkError):
+        g.qweight("absent")
+    g.close()

@@ -94,6 +94,11 @@ class QWeightConfig(C.Structure):
 
 QTYPE_Q8_0, QTYPE_Q4_K, QTYPE_Q6_K = 8, 12, 14
 
+
+class GgufTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("type", C.c_int32), ("n_dims", C.c_int32), ("ne", C.c_int64 * 4),
+                ("offset", C.c_uint64), ("n_bytes", C.c_uint64)]
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -161,6 +166,23 @@ SIGNATURES = {
     "vxk_qweight_matmul": (_I32, [_P, _P, _I32, _P, _P]),
     "vxk_qweight_matmul_group": (_I32, [C.POINTER(C.c_void_p), _I32, _P, _I32, C.POINTER(C.c_void_p), _P]),
     "vxk_qweight_sync": (_I32, [_P, _P, _I32]),
+    "vxk_gguf_open": (_I32, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "vxk_gguf_close": (None, [_P]),
+    "vxk_gguf_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_gguf_version": (C.c_uint32, [_P]),
+    "vxk_gguf_n_tensors": (_I64, [_P]),
+    "vxk_gguf_get_tensor": (_I32, [_P, _I64, C.POINTER(GgufTensor)]),
+    "vxk_gguf_find_tensor": (_I64, [_P, C.c_char_p]),
+    "vxk_gguf_tensor_data": (_P, [_P, _I64]),
+    "vxk_gguf_n_keys": (_I64, [_P]),
+    "vxk_gguf_key": (C.c_char_p, [_P, _I64]),
+    "vxk_gguf_key_type": (_I32, [_P, C.c_char_p]),
+    "vxk_gguf_get_int": (_I32, [_P, C.c_char_p, _I64P]),
+    "vxk_gguf_get_float": (_I32, [_P, C.c_char_p, C.POINTER(C.c_double)]),
+    "vxk_gguf_get_str": (_I32, [_P, C.c_char_p, C.POINTER(C.c_char_p)]),
+    "vxk_gguf_get_array": (_I32, [_P, C.c_char_p, _I32P, _I64P, C.POINTER(C.c_void_p)]),
+    "vxk_gguf_get_array_str": (_I32, [_P, C.c_char_p, _I64, C.POINTER(C.c_char_p)]),
+    "vxk_qweight_create_from_gguf": (_I32, [_P, C.c_char_p, _I32, _I32, C.POINTER(C.c_void_p)]),
 }
 
 _lib = None
@@ -537,3 +559,108 @@ def qweight_repack(qtype: int, n_rows: int, n_cols: int, gguf_blocks):
     if st != OK:
         raise VxkError(st, "repack")
     return out
+
+
+class Gguf:
+    """A GGUF file opened by vxk_gguf_open (metadata, tensor table, mapped bytes)."""
+
+    def __init__(self, path):
+        self.lib = load()
+        h = C.c_void_p()
+        st = self.lib.vxk_gguf_open(str(path).encode(), C.byref(h))
+        if st != OK:
+            buf = C.create_string_buffer(1024)
+            self.lib.vxk_gguf_last_error(None, buf, 1024)
+            raise VxkError(st, buf.value.decode())
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def version(self):
+        return int(self.lib.vxk_gguf_version(self.h))
+
+    def tensors(self):
+        out = []
+        for i in range(self.lib.vxk_gguf_n_tensors(self.h)):
+            t = GgufTensor()
+            if self.lib.vxk_gguf_get_tensor(self.h, i, C.byref(t)) != OK:
+                raise VxkError(1, "get_tensor")
+            out.append(dict(name=t.name.decode(), type=t.type, n_dims=t.n_dims, ne=list(t.ne)[: t.n_dims],
+                            offset=int(t.offset), n_bytes=int(t.n_bytes)))
+        return out
+
+    def find_tensor(self, name):
+        return int(self.lib.vxk_gguf_find_tensor(self.h, name.encode()))
+
+    def tensor_bytes(self, name):
+        import numpy as np
+
+        i = self.find_tensor(name)
+        if i < 0:
+            raise KeyError(name)
+        t = self.tensors()[i]
+        ptr = self.lib.vxk_gguf_tensor_data(self.h, i)
+        if not ptr:
+            raise VxkError(1, "tensor data not available")
+        return np.ctypeslib.as_array((C.c_uint8 * t["n_bytes"]).from_address(ptr)).copy()
+
+    def keys(self):
+        return [self.lib.vxk_gguf_key(self.h, i).decode() for i in range(self.lib.vxk_gguf_n_keys(self.h))]
+
+    def key_type(self, key):
+        return int(self.lib.vxk_gguf_key_type(self.h, key.encode()))
+
+    def get(self, key):
+        """Scalar or array value of a key (ints widened, floats as float)."""
+        import numpy as np
+
+        t = self.key_type(key)
+        k = key.encode()
+        if t < 0:
+            raise KeyError(key)
+        if t == 8:
+            s = C.c_char_p()
+            self.lib.vxk_gguf_get_str(self.h, k, C.byref(s))
+            return s.value.decode()
+        if t in (6, 12):
+            d = C.c_double()
+            self.lib.vxk_gguf_get_float(self.h, k, C.byref(d))
+            return d.value
+        if t == 9:
+            et, n, p = C.c_int32(), C.c_int64(), C.c_void_p()
+            self.lib.vxk_gguf_get_array(self.h, k, C.byref(et), C.byref(n), C.byref(p))
+            if et.value == 8:
+                out = []
+                for i in range(n.value):
+                    s = C.c_char_p()
+                    self.lib.vxk_gguf_get_array_str(self.h, k, i, C.byref(s))
+                    out.append(s.value.decode())
+                return out
+            dt = {0: np.uint8, 1: np.int8, 2: np.uint16, 3: np.int16, 4: np.uint32, 5: np.int32, 6: np.float32,
+                  7: np.bool_, 10: np.uint64, 11: np.int64, 12: np.float64}[et.value]
+            nb = n.value * np.dtype(dt).itemsize
+            raw = np.ctypeslib.as_array((C.c_uint8 * nb).from_address(p.value)).copy() if nb else np.zeros(0, np.uint8)
+            return raw.view(dt)
+        v = C.c_int64()
+        self.lib.vxk_gguf_get_int(self.h, k, C.byref(v))
+        return bool(v.value) if t == 7 else int(v.value)
+
+    def qweight(self, name, device=0, max_batch=64):
+        q = QWeight.__new__(QWeight)
+        q.lib = self.lib
+        h = C.c_void_p()
+        st = self.lib.vxk_qweight_create_from_gguf(self.h, name.encode(), device, max_batch, C.byref(h))
+        if st != OK:
+            raise VxkError(st, q.last_error(None))
+        q.h = h
+        return q

@@ -54,6 +54,12 @@ CONFIGS = {
                  mats=(("q", 4096, 3072, 12), ("k", 1024, 3072, 12), ("v", 1024, 3072, 14), ("o", 3072, 4096, 12)),
                  desc="decoder attention projections q/k/v/o of 30 layers for 64 batched streams/GPU, "
                       "Q4_K_M types (attn_q/k/o Q4_K, attn_v Q6_K), distinct weights per layer"),
+    "decoder": dict(kind="decoder", layers=26, streams=64, ctx=(400, 4096), dim=3072, hidden=9216, vocab=131072,
+                    capacity=8192, dtype=1,
+                    desc="whole 4B-realtime decoder step (26 layers, 3072 / 9216, vocab 131072, Q4_K_M weights: "
+                         "attn_q/k/o, ffn_w1/w3 Q4_K; attn_v, ffn_w2, tok_embeddings Q6_K) for 64 streams/GPU, "
+                         "ctx~U[400,4096] f16 16-token pages: embeddings + audio, norms, time scale, projections, "
+                         "attention, SwiGLU FFN, logits + argmax"),
     "4": dict(kind="encoder", layers=32, streams=128, heads=20, rows=4, window=750, capacity=878, dtype=30,
               desc="streaming encoder, 128 streams, 20 heads x 64, 4 new rows per 80 ms chunk, "
                    "750-frame window in an 878-slot bf16 ring (steady state, rings wrapped)"),
@@ -642,6 +648,271 @@ def head_cpu_sample(cfg, seed, seconds):
     return 4 * done / el / 8.0, done
 
 
+def write_decoder_gguf(path, cfg, seed):
+    """A seeded Q4_K_M-typed decoder with the reference's tensor names and keys
+    (src/voxtral.cpp:1097-1110, 1225-1252), written with the gguf package.
+    Returns the host tensors (vx_decoder.Tensor) for the CPU sample."""
+    import gguf
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_decoder as vd
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    L, D, H, V = cfg["layers"], cfg["dim"], cfg["hidden"], cfg["vocab"]
+    gt = {vd.Q4_K: gguf.GGMLQuantizationType.Q4_K, vd.Q6_K: gguf.GGMLQuantizationType.Q6_K}
+    w = gguf.GGUFWriter(str(path), "voxtral_realtime") if path else None
+    if w is None:  # host tensors only (the CPU arm)
+        class _NoWriter:
+            def __getattr__(self, name):
+                return lambda *a, **k: None
+        w = _NoWriter()
+    for k, v in (("dim", D), ("n_layers", L), ("n_heads", NQ), ("head_dim", HD), ("hidden_dim", H),
+                 ("n_kv_heads", NKV)):
+        w.add_int32(f"voxtral.decoder.{k}", v)
+    w.add_float32("voxtral.decoder.norm_eps", 1e-5)
+    w.add_float32("voxtral.decoder.rope_theta", 1e6)
+    w.add_bool("voxtral.ada_rms_norm_t_cond", True)
+    tensors = {}
+
+    def mat(name, t, rows, cols):
+        blocks = vx_oracle.random_qblocks(t, rows, cols, rng, zero_mean=True)
+        tensors[name] = vd.Tensor(t, rows, cols, blocks)
+        w.add_tensor(name, blocks, raw_dtype=gt[t])
+
+    def vec(name, n):
+        a = rng.uniform(0.8, 1.2, n).astype(np.float32)
+        tensors[name] = vd.Tensor(vd.F32, 1, n, a)
+        w.add_tensor(name, a)
+
+    mat("tok_embeddings.weight", vd.Q6_K, V, D)
+    for l in range(L):
+        p = f"dec.blk.{l}."
+        mat(p + "attn_q.weight", vd.Q4_K, NQ * HD, D)
+        mat(p + "attn_k.weight", vd.Q4_K, NKV * HD, D)
+        mat(p + "attn_v.weight", vd.Q6_K, NKV * HD, D)
+        mat(p + "attn_o.weight", vd.Q4_K, D, NQ * HD)
+        mat(p + "ffn_w1.weight", vd.Q4_K, H, D)
+        mat(p + "ffn_w3.weight", vd.Q4_K, H, D)
+        mat(p + "ffn_w2.weight", vd.Q6_K, D, H)
+        mat(p + "ada0.weight", vd.Q4_K, 32, D)
+        a2 = rng.normal(0, 1.0 / np.sqrt(32), (D, 32)).astype(np.float16)
+        tensors[p + "ada2.weight"] = vd.Tensor(vd.F16, D, 32, a2)
+        w.add_tensor(p + "ada2.weight", a2)
+        vec(p + "attn_norm.weight", D)
+        vec(p + "ffn_norm.weight", D)
+    vec("dec.norm.weight", D)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return tensors
+
+
+def decoder_weight_bytes(cfg):
+    """GGUF bytes of every matrix one decoder step streams (all layers + head)."""
+    L, D, H, V = cfg["layers"], cfg["dim"], cfg["hidden"], cfg["vocab"]
+    q4 = lambda n, k: n * (k // 256) * 144  # noqa: E731
+    q6 = lambda n, k: n * (k // 256) * 210  # noqa: E731
+    per_layer = (q4(NQ * HD, D) + q4(NKV * HD, D) + q6(NKV * HD, D) + q4(D, NQ * HD) + 2 * q4(H, D) + q6(D, H))
+    return L * per_layer + q6(V, D)
+
+
+def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
+    """Whole decoder step: one step = one token of every stream through the
+    embeddings, all layers and the greedy head (vxk_decoder_forward over the
+    pool's planned batch), caches prefilled to seeded contexts."""
+    import tempfile
+
+    L, S, cap = cfg["layers"], cfg["streams"], cfg["capacity"]
+    tmpdir = tempfile.mkdtemp(prefix="vxk_bench_")
+    path = Path(tmpdir) / f"decoder_{rank}.gguf"
+    tensors = write_decoder_gguf(path, cfg, args.seed)
+    rng = np.random.default_rng(args.seed)
+    lo, hi = cfg["ctx"]
+    ctx_all = rng.integers(lo, hi + 1, size=S * world)
+    ctx0 = ctx_all[assign_streams(ctx_all, world, S)[rank]]
+    total_steps = args.warmup + args.steps * (1 if args.no_e2e else 2) + 2
+    pages = [min(cap // BT, (int(c) + total_steps) // BT + 2) for c in ctx0]
+    prefill_chunk = min(int(ctx0.max()), 4096)
+    pool = vxk.Pool(device=local, n_layers=L, n_q_heads=NQ, n_kv_heads=NKV, head_dim=HD, block_tokens=BT,
+                    capacity=cap, n_blocks=int(sum(pages)) + 64, max_streams=S, max_rows=max(S, prefill_chunk),
+                    max_position=int(ctx0.max()) + total_steps + BT + 16, dtype=cfg["dtype"], alloc_seed=1234 + rank)
+    g = vxk.Gguf(path)
+    dec = vxk.Decoder(g, pool, audio_capacity=256, enc_capacity=0)
+    g.close()
+    os.unlink(path)
+    os.rmdir(tmpdir)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    streams = [pool.open_stream() for _ in range(S)]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    kfill = torch.randn((prefill_chunk, NKV, HD), device="cuda", generator=gen) * 0.5
+    vfill = torch.randn((prefill_chunk, NKV, HD), device="cuda", generator=gen) * 0.5
+    for s, c in zip(streams, ctx0):
+        left = int(c)
+        while left > 0:
+            n = min(left, prefill_chunk)
+            pool.plan([s], [n], sh)
+            for layer in range(L):
+                pool.append_layer(layer, kfill.data_ptr(), vfill.data_ptr(), sh)
+            pool.commit()
+            left -= n
+    audio = torch.randn((256, cfg["dim"]), device="cuda", generator=gen) * 0.05
+    for s in streams:
+        dec.write_audio(s, 0, 256, audio.data_ptr(), sh)
+    torch.cuda.synchronize()
+    del kfill, vfill
+    ones = [1] * S
+    pos = [int(c) for c in ctx0]
+    tok_rng = np.random.default_rng(args.seed + 7 + rank)
+    tokens = [int(t) for t in tok_rng.integers(0, cfg["vocab"], S)]
+    amax = torch.zeros(S, dtype=torch.int32, device="cuda")
+
+    def step():
+        pool.plan(streams, ones, sh)
+        dec.forward(tokens, [p % 256 for p in pos], amax.data_ptr(), 0, 0, sh)
+        pool.commit()
+        for j in range(S):
+            pos[j] += 1
+
+    for _ in range(args.warmup):
+        step()
+    dec.sync(sh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    ctx_sum = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+            ctx_sum.append(sum(min(cap, p) for p in pos))
+        e1.record(stream)
+        torch.cuda.synchronize()
+    dec.sync(sh)
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    step_s = ms / 1000.0 / args.steps
+    w_bytes = decoder_weight_bytes(cfg)
+    kv_bytes = L * 4096 * statistics.mean(ctx_sum)
+    # per row and layer: x / xn / q / k / v / att / proj / gate / up / ffn fp32 reads and writes, the append
+    act_bytes = S * L * 4 * (6 * cfg["dim"] + 3 * NQ * HD + 4 * NKV * HD + 4 * cfg["hidden"]) + S * L * 4096
+    bytes_per_step = w_bytes + kv_bytes + act_bytes
+    achieved = bytes_per_step / step_s / 1e9
+    peak, peak_kind = load_peaks()
+    traffic_ratio, traffic_src = load_traffic(args.config)
+
+    e2e = None
+    if not args.no_e2e:
+        # the serving loop through the public API: tokens from the previous
+        # step's argmax read back to the host (4 bytes per stream), as the
+        # reference's hot loop does
+        host_amax = torch.zeros(S, dtype=torch.int32).pin_memory()
+        toks = list(tokens)
+
+        def host_step():
+            pool.plan(streams, ones, sh)
+            dec.forward(toks, [p % 256 for p in pos], amax.data_ptr(), 0, 0, sh)
+            host_amax.copy_(amax, non_blocking=True)
+            stream.synchronize()
+            pool.commit()
+            for j in range(S):
+                pos[j] += 1
+            toks[:] = [int(t) for t in host_amax.tolist()]
+
+        host_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            host_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(dist, f0.elapsed_time(f1), "cuda")
+        e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": S * 8 + S * 16, "d2h_bytes_per_step": S * 4,
+               "ms_per_step": round(ems / args.steps, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, done, mctx = decoder_cpu_sample(tensors, cfg, int(statistics.mean([int(c) for c in ctx0])),
+                                             args.seed, args.cpu_seconds)
+        cpu = {"value": round(tps, 5), "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{done} single-token steps of one stream (cache prefilled to ctx {mctx}) through all "
+                         f"{L} layers and the head by the oracle (oracle/vx_decoder.py over vx_qmm.c / vx_oracle.c, "
+                         f"one thread)"}
+    del tensors
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        per_layer = 12
+        line = {
+            "metric": "whole decoder step tokens/s (Q4_K_M, 26 layers + head)",
+            "value": round(world * S * args.steps / (ms / 1000.0), 1),
+            "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "Q4_K / Q6_K weights with Q8_K rows (exact integer dots), f16 KV cache, fp32 activations",
+            "data": "synthetic",
+            "config": {"workload": f"config decoder: {cfg['desc']}", "layers": L, "streams_per_gpu": S,
+                       "mean_ctx_timed": round(statistics.mean(ctx_sum) / S, 1),
+                       "parallelism": f"streams sharded, {S}/GPU, no collective",
+                       "l2": f"inputs larger than L2 ({w_bytes / 1e9:.2f} GB of weights per step)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": None if traffic_ratio is None else round(traffic_ratio * bytes_per_step),
+                         "traffic_source": traffic_src,
+                         "algorithmic_bytes_per_step": round(bytes_per_step),
+                         "weight_bytes": w_bytes, "kv_bytes": round(kv_bytes),
+                         "avg_step_us": round(step_s * 1e6, 1), "kernel": "whole step (all kernels)"},
+            "cpu_baseline": cpu, "e2e": e2e,
+            # embed + per layer (q/k/v quantize + product, attention, o quantize + product, norm, w1/w3
+            # quantize + product, swiglu, w2 quantize + product, norm) + head (quantize, product, argmax)
+            "gpu_launches": int(args.steps * (1 + per_layer * L + 3)),
+            "launch": "eager C-ABI calls per step: vxk_batch_plan, vxk_decoder_forward, vxk_batch_commit",
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    pool.close()
+
+
+def decoder_cpu_sample(tensors, cfg, ctx, seed, seconds):
+    """Times the oracle's whole decoder step on one stream whose cache holds
+    ctx random rows; returns (tokens/s, steps, ctx)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_decoder as vd
+
+    rng = np.random.default_rng(seed + 11)
+    ref = vd.Decoder(tensors, cfg["layers"], capacity=cfg["capacity"])
+    st = ref.stream(0)
+    rb = NKV * HD * 2
+    for l in range(cfg["layers"]):
+        kk = rng.normal(0, 0.5, (ctx, NKV * HD)).astype(np.float16).view(np.uint8).reshape(ctx, rb)
+        vv = rng.normal(0, 0.5, (ctx, NKV * HD)).astype(np.float16).view(np.uint8).reshape(ctx, rb)
+        st.k[l] = list(kk)
+        st.v[l] = list(vv)
+    st.next_pos = ctx
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        ref.forward([(0, [int(rng.integers(0, cfg["vocab"]))])],
+                    rng.normal(0, 0.05, (1, cfg["dim"])).astype(np.float32))
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 8:
+            break
+    return done / el, done, ctx
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -683,6 +954,7 @@ TRAFFIC_PROFILES = {
     "head": "head_kernel_config_head.md",
     "proj": "qmm_kernel_config_proj.md",
     "headq": "qtc_kernel_config_headq.md",
+    "decoder": "decoder_step_config_decoder.md",
 }
 
 
@@ -887,6 +1159,24 @@ def run_reference(args, cfg, rank, world):
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
+    if cfg.get("kind") == "decoder":
+        tensors = write_decoder_gguf(None, cfg, args.seed)
+        rng = np.random.default_rng(args.seed)
+        lo, hi = cfg["ctx"]
+        mctx = int(rng.integers(lo, hi + 1, size=cfg["streams"]).mean())
+        tps, done, mctx = decoder_cpu_sample(tensors, cfg, mctx, args.seed, 20.0)
+        line = {"impl": "reference", "metric": "whole decoder step tokens/s (Q4_K_M, 26 layers + head)",
+                "value": round(tps, 5), "unit": "tokens/s", "n_gpus": args.gpus, "steps": done, "warmup": 0,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "Q4_K / Q6_K weights, Q8_K rows, exact integer dots, fp64 attention", "data": "synthetic",
+                "config": {"workload": f"config decoder: {cfg['desc']}"},
+                "cpu_baseline": {"value": round(tps, 5), "unit": "tokens/s", "cores": 1, "kind": "port",
+                                 "sample": f"{done} single-token steps of one stream (ctx {mctx}) through every layer "
+                                           f"and the head by the oracle (oracle/vx_decoder.py, one thread)"},
+                "e2e": {"value": round(tps, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if cfg.get("kind") == "encoder":
         cps, done = encoder_cpu_sample(cfg, args.seed, 20.0)
         line = {"impl": "reference", "metric": "encoder chunks/s (KV append + windowed attention, 4 rows/chunk)",
@@ -974,6 +1264,12 @@ def main():
         return
     if cfg.get("kind") == "qmm":
         run_qmm(args, cfg, world, rank, local, dist, torch, vxk)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if cfg.get("kind") == "decoder":
+        run_decoder(args, cfg, world, rank, local, dist, torch, vxk)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

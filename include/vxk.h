@@ -584,6 +584,106 @@ VXK_API vxk_status vxk_qweight_create_from_gguf(const vxk_gguf * g, const char *
 /** Bounded wait for cuda_stream, then the matrix's device error word. */
 VXK_API vxk_status vxk_qweight_sync(vxk_qweight * w, void * cuda_stream, int32_t timeout_ms);
 
+/* ======================================================================== */
+/* Whole decoder step over a batch of streams, and the audio adapter ring    */
+/* ======================================================================== */
+
+/**
+ * A decoder loaded from a GGUF model onto the pool's device: every layer's
+ * quantized projections and FFN (Q8_0 / Q4_K / Q6_K), the norms, the time
+ * conditioning, the tied (or untied output) head, the adapter and, per pool
+ * stream, an encoder-output ring and an audio-embedding ring.  It runs
+ * build_decoder_step_graph_reusable / build_decoder_prefill_graph
+ * (src/voxtral.cpp:2900-2965, 3047-3104) for the pool's planned batch, with
+ * the rows of many streams in one pass: x = tok_embeddings[token] +
+ * audio_emb[slot], then per layer RMSNorm, q/k/v, RoPE + append + attention,
+ * o + residual, RMSNorm, time scale (1 + ada), SwiGLU FFN + residual, and the
+ * final norm, logits and argmax of each stream's last row.  Not thread-safe:
+ * one caller (or vxk_batcher) at a time.
+ */
+typedef struct vxk_decoder vxk_decoder;
+
+typedef struct vxk_decoder_config {
+    uint32_t struct_size;
+    uint32_t api_version;
+    int32_t audio_capacity;  /* audio-embedding ring slots per stream: 256 (VOXTRAL_AEMB_RING_CAP) */
+    int32_t enc_capacity;    /* encoder-output ring frames per stream: 256 (VOXTRAL_ENC_OUT_RING_CAP);
+                                0 = no adapter (adapter tensors not loaded) */
+    float time_value;        /* time conditioning t: VOXTRAL_N_DELAY_TOKENS = 6 */
+    int32_t reserved[3];
+} vxk_decoder_config;
+
+VXK_API vxk_decoder_config vxk_decoder_default_config(void);
+
+/**
+ * Loads the decoder of GGUF file g (keys voxtral.decoder.*, tensors
+ * dec.blk.N.*, tok_embeddings.weight, dec.norm.weight, output.weight when
+ * present, adapter.0/2.weight; src/voxtral.cpp:1097-1110, 1225-1252) for
+ * pool, whose layers, heads and head_dim must match the file.  Projection,
+ * FFN and adapter matrices must be Q8_0, Q4_K or Q6_K; the embeddings may
+ * also be F16 or BF16; norms F32, F16 or BF16.  g may be closed afterwards.
+ */
+VXK_API vxk_status vxk_decoder_create(const vxk_gguf * g, vxk_pool * pool, const vxk_decoder_config * config,
+                                      vxk_decoder ** out);
+VXK_API void vxk_decoder_destroy(vxk_decoder * d);
+/** Last error of d, or of the last failed vxk_decoder_create when d is NULL. */
+VXK_API vxk_status vxk_decoder_last_error(const vxk_decoder * d, char * buf, size_t capacity);
+
+typedef struct vxk_decoder_info {
+    int32_t n_layers, dim, hidden, n_q_heads, n_kv_heads, head_dim, vocab, ada_dim;
+    int32_t emb_type;        /* ggml type of tok_embeddings (or output.weight) */
+    int32_t max_rows;        /* rows of one forward (the pool's max_rows) */
+    int32_t max_streams;
+    int32_t audio_capacity, enc_capacity, enc_dim;
+    int64_t device_bytes;    /* weights, rings and scratch */
+} vxk_decoder_info;
+
+VXK_API vxk_status vxk_decoder_get_info(const vxk_decoder * d, vxk_decoder_info * out);
+
+/**
+ * One forward pass over the pool's planned batch (vxk_batch_plan; rows in
+ * plan order, each stream's n_new rows at consecutive positions).  Host
+ * arrays per row: tokens[rows] (0 <= token < vocab) and audio_slots[rows]
+ * (the audio-embedding ring slot added to the row, audio_pos % capacity).
+ * Device outputs per planned stream (its last row): argmax[n_streams] int32,
+ * and optionally logits[n_streams][vocab] and hidden[n_streams][dim] (the
+ * final-normed hidden state, decoder_hidden_diagnostic).  The KV caches are
+ * appended; the caller commits (vxk_batch_commit) after vxk_decoder_sync.
+ * Asynchronous on cuda_stream; allocates nothing after the first call with
+ * a given row count.
+ */
+VXK_API vxk_status vxk_decoder_forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slots,
+                                       int32_t * argmax, float * logits, float * hidden, void * cuda_stream);
+
+/** Writes n encoder-output rows ([n][enc_dim] fp32, device memory) of stream
+ *  into its ring at absolute frames frame .. frame+n-1 (slot = frame %
+ *  enc_capacity); copy_chunk_to_enc_out_ring (src/voxtral.cpp:4018-4045). */
+VXK_API vxk_status vxk_decoder_write_enc(vxk_decoder * d, int32_t stream, int64_t frame, int32_t n,
+                                         const float * rows, void * cuda_stream);
+/** Writes n audio-embedding rows ([n][dim] fp32, device memory) into stream's
+ *  ring at absolute positions pos .. pos+n-1 (slot = pos % audio_capacity). */
+VXK_API vxk_status vxk_decoder_write_audio(vxk_decoder * d, int32_t stream, int64_t pos, int32_t n,
+                                           const float * rows, void * cuda_stream);
+
+/**
+ * The adapter over the encoder-output rings, n groups of any streams in one
+ * pass (build_adapter_ring_graph_reusable, src/voxtral.cpp:2589-2620): group
+ * g reads the 4 frames enc_frame[g] .. +3 of streams[g] (enc_frame a multiple
+ * of 4), x = adapter.2 . gelu_erf(adapter.0 . concat(frames)), stored in the
+ * stream's audio ring at audio_pos[g] % audio_capacity.  Host arrays; n in
+ * [1, max_rows].
+ */
+VXK_API vxk_status vxk_decoder_adapt(vxk_decoder * d, int32_t n, const int32_t * streams,
+                                     const int64_t * enc_frame, const int64_t * audio_pos, void * cuda_stream);
+
+/** Reads n rows of a stream's audio ring back (device destination), for tests. */
+VXK_API vxk_status vxk_decoder_read_audio(vxk_decoder * d, int32_t stream, int64_t pos, int32_t n, float * rows,
+                                          void * cuda_stream);
+
+/** Bounded wait for cuda_stream, then every device error word the decoder's
+ *  launches use (pool, products, head). */
+VXK_API vxk_status vxk_decoder_sync(vxk_decoder * d, void * cuda_stream, int32_t timeout_ms);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -305,10 +305,13 @@ def qmatmul(wtype: int, w_blocks: np.ndarray, n: int, k: int, x: np.ndarray):
     return y, mag, int(terms)
 
 
-def random_qblocks(wtype: int, n: int, k: int, rng: np.random.Generator) -> np.ndarray:
+def random_qblocks(wtype: int, n: int, k: int, rng: np.random.Generator, zero_mean: bool = False) -> np.ndarray:
     """Valid random GGUF blocks for an n x k weight (test input): random
     quants and sub-block scales, block scales drawn so that the dequantized
-    weights are O(0.05), like a trained projection's."""
+    weights are O(0.05).  Q4_K's random mins bias its weights positive;
+    zero_mean=True draws Q4_K blocks with dmin = 7.5 d and each min equal to
+    its scale (weights symmetric about 0, mean |w| ~ 1/sqrt(k)), which keeps
+    the activations of a stack of such layers O(1)."""
     per, size = QBLOCK[wtype]
     nb = k // per
     blk = rng.integers(0, 256, size=(n, nb, size), dtype=np.uint8)
@@ -317,6 +320,16 @@ def random_qblocks(wtype: int, n: int, k: int, rng: np.random.Generator) -> np.n
     if wtype == Q8_0:
         blk[:, :, 0:2] = f16(rng.uniform(2e-4, 8e-4, (n, nb)))
         blk[:, :, 2:] = rng.integers(-127, 128, size=(n, nb, 32)).astype(np.int8).view(np.uint8)
+    elif wtype == Q4_K and zero_mean:
+        d = np.asarray(rng.uniform(0.5, 1.5, (n, nb)) / (126.0 * np.sqrt(k)), np.float16)
+        blk[:, :, 0:2] = f16(d)
+        blk[:, :, 2:4] = f16(d.astype(np.float32) * 7.5)
+        sc = rng.integers(0, 64, size=(n, nb, 8)).astype(np.uint8)
+        s = blk[:, :, 4:16]
+        s[..., 0:4] = sc[..., 0:4] | ((sc[..., 4:8] >> 4) << 6)
+        s[..., 4:8] = sc[..., 0:4] | ((sc[..., 4:8] >> 4) << 6)
+        s[..., 8:12] = (sc[..., 4:8] & 0xF) | ((sc[..., 4:8] & 0xF) << 4)
+        blk[:, :, 4:16] = s
     elif wtype == Q4_K:
         blk[:, :, 0:2] = f16(rng.uniform(5e-4, 2e-3, (n, nb)))
         blk[:, :, 2:4] = f16(rng.uniform(1e-3, 4e-3, (n, nb)))
@@ -324,3 +337,74 @@ def random_qblocks(wtype: int, n: int, k: int, rng: np.random.Generator) -> np.n
         blk[:, :, 192:208] = rng.integers(-128, 128, size=(n, nb, 16)).astype(np.int8).view(np.uint8)
         blk[:, :, 208:210] = f16(rng.uniform(2e-5, 6e-5, (n, nb)))
     return blk.reshape(n, nb * size)
+
+
+def quantize_blocks(wtype: int, x: np.ndarray) -> np.ndarray:
+    """Encodes fp32 rows x [n][k] as valid GGUF blocks of Q8_0 / Q4_K / Q6_K
+    (test input: weights with a chosen distribution).  Q8_0 is ggml's rule;
+    for the K-quants this is a plain absmax / min-max encoder of the block
+    format (not ggml's search for the best scales): Q6_K scale per 16 values
+    max|x| / 31, Q4_K scale and offset per 32 values from the min and max,
+    the block's d / dmin = largest sub-block scale / 127 (Q6_K) or 63 (Q4_K)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, k = x.shape
+    if wtype == Q8_0:
+        return np.stack([quantize_q8_0(x[i]) for i in range(n)]).reshape(n, -1)
+    nb = k // 256
+    xb = x.reshape(n, nb, 256).astype(np.float64)
+    f16 = lambda a: np.asarray(a, np.float16)  # noqa: E731
+    if wtype == Q6_K:
+        sub = xb.reshape(n, nb, 16, 16)
+        s = np.abs(sub).max(axis=3) / 31.0                      # [n, nb, 16]
+        d = f16(s.max(axis=2) / 127.0)                          # [n, nb]
+        df = d.astype(np.float64)
+        sc = np.where(df[..., None] > 0, np.rint(s / np.where(df[..., None] > 0, df[..., None], 1)), 0)
+        sc = np.clip(sc, -128, 127).astype(np.int8)
+        step = df[..., None] * sc.astype(np.float64)            # [n, nb, 16]
+        q = np.where(step[..., None] > 0, np.rint(sub / np.where(step[..., None] > 0, step[..., None], 1)), 0)
+        q6 = (np.clip(q, -32, 31) + 32).astype(np.uint8).reshape(n, nb, 2, 4, 32)   # [half, g, l]
+        low, high = q6 & 0xF, q6 >> 4
+        ql = np.empty((n, nb, 2, 64), np.uint8)
+        ql[..., 0:32] = low[:, :, :, 0] | (low[:, :, :, 2] << 4)
+        ql[..., 32:64] = low[:, :, :, 1] | (low[:, :, :, 3] << 4)
+        qh = (high[:, :, :, 0] | (high[:, :, :, 1] << 2) | (high[:, :, :, 2] << 4) | (high[:, :, :, 3] << 6))
+        out = np.empty((n, nb, 210), np.uint8)
+        out[..., 0:128] = ql.reshape(n, nb, 128)
+        out[..., 128:192] = qh.astype(np.uint8).reshape(n, nb, 64)
+        out[..., 192:208] = sc.view(np.uint8)
+        out[..., 208:210] = d.view(np.uint16).view(np.uint8).reshape(n, nb, 2)
+        return out.reshape(n, nb * 210)
+    if wtype == Q4_K:
+        sub = xb.reshape(n, nb, 8, 32)
+        mn = np.minimum(sub.min(axis=3), 0.0)
+        mx = sub.max(axis=3)
+        scale = (mx - mn) / 15.0
+        off = -mn
+        d = f16(scale.max(axis=2) / 63.0)
+        dmin = f16(off.max(axis=2) / 63.0)
+        df, mf = d.astype(np.float64)[..., None], dmin.astype(np.float64)[..., None]
+        sc = np.clip(np.where(df > 0, np.rint(scale / np.where(df > 0, df, 1)), 0), 0, 63).astype(np.uint8)
+        m = np.clip(np.where(mf > 0, np.rint(off / np.where(mf > 0, mf, 1)), 0), 0, 63).astype(np.uint8)
+        step = df * sc
+        q = np.where(step[..., None] > 0,
+                     np.rint((sub + (mf * m)[..., None]) / np.where(step[..., None] > 0, step[..., None], 1)), 0)
+        q = np.clip(q, 0, 15).astype(np.uint8).reshape(n, nb, 4, 2, 32)
+        qs = (q[:, :, :, 0] | (q[:, :, :, 1] << 4)).reshape(n, nb, 128)
+        s = np.empty((n, nb, 12), np.uint8)
+        s[..., 0:4] = sc[..., 0:4] | ((sc[..., 4:8] >> 4) << 6)
+        s[..., 4:8] = m[..., 0:4] | ((m[..., 4:8] >> 4) << 6)
+        s[..., 8:12] = (sc[..., 4:8] & 0xF) | ((m[..., 4:8] & 0xF) << 4)
+        out = np.empty((n, nb, 144), np.uint8)
+        out[..., 0:2] = d.view(np.uint16).view(np.uint8).reshape(n, nb, 2)
+        out[..., 2:4] = dmin.view(np.uint16).view(np.uint8).reshape(n, nb, 2)
+        out[..., 4:16] = s
+        out[..., 16:144] = qs
+        return out.reshape(n, nb * 144)
+    raise ValueError(f"unsupported weight type {wtype}")
+
+
+def normal_qblocks(wtype: int, n: int, k: int, rng: np.random.Generator, sigma: float | None = None) -> np.ndarray:
+    """GGUF blocks of an n x k weight drawn from N(0, sigma^2), sigma = 1/sqrt(k)
+    by default (a projection that keeps activations O(1)), then quantized."""
+    sigma = 1.0 / np.sqrt(k) if sigma is None else sigma
+    return quantize_blocks(wtype, rng.normal(0.0, sigma, (n, k)).astype(np.float32))

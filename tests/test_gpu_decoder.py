@@ -1,0 +1,264 @@
+"""GPU parity of the whole decoder step (vxk_decoder_forward) and the adapter
+ring (vxk_decoder_adapt) through the C ABI against the oracle's node-by-node
+restatement (oracle/vx_decoder.py) on the same seeded GGUF model.
+
+Two comparisons per step:
+  composition  the oracle with the device attention plugged in (the pool's
+               own kernels on the oracle's q / k / v, a second pool): every
+               other node (embedding gather, norms, time scale, the quantized
+               products, SwiGLU, residuals, head) follows the oracle.
+  end to end   the pure fp64 oracle.
+Why the bar is 5e-2 of max |ref| for every step: every product quantizes its
+input rows to 8 bits.  The products sum their fp32 block terms in another
+order than the oracle's fp64 target (and the attention kernels are within
+2e-3 of fp64), so now and then an activation lands on the other side of a
+rounding step; that changes the product's outputs by ~1e-3 of their size,
+which moves a few percent of the next product's inputs across their own
+steps, and so on: one such event decorrelates the rest of the network at
+the 1e-2 level (observed 1.3-2.4e-2).  Steps with no such event match the
+composition oracle to ~1e-6, so each test also asserts that at least one
+of its steps is within 1e-4 of it (the composition itself is exact).
+argmax: equal to the composition oracle's wherever its top-2 gap exceeds
+twice that step's measured logit error (then no rounding can swap them).
+adapter: max |d| <= 1e-3 * max |ref| (no requantized chain on its path
+beyond two products).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+STEP_BAR = 5e-2
+EXACT_BAR = 1e-4
+
+
+class DeviceAttention:
+    """The pool kernels' attention for the oracle (a second pool of the same
+    shape, fed the oracle's q / k / v)."""
+
+    def __init__(self, vxk, cfg):
+        import torch
+
+        self.torch = torch
+        self.pool = vxk.Pool(**cfg)
+        self.ids = {}
+        self.batch = None
+
+    def begin(self, batch):
+        for s, _ in batch:
+            if s not in self.ids:
+                self.ids[s] = self.pool.open_stream()
+        self.batch = batch
+        self.pool.plan([self.ids[s] for s, _ in batch], [n for _, n in batch])
+
+    def layer(self, l, q, k, v):
+        torch = self.torch
+        qd = torch.from_numpy(np.ascontiguousarray(q, np.float32)).cuda()
+        kd = torch.from_numpy(np.ascontiguousarray(k, np.float32)).cuda()
+        vd_ = torch.from_numpy(np.ascontiguousarray(v, np.float32)).cuda()
+        out = torch.empty_like(qd)
+        if all(n == 1 for _, n in self.batch):
+            self.pool.decode_layer(l, qd.data_ptr(), kd.data_ptr(), vd_.data_ptr(), out.data_ptr())
+        else:
+            self.pool.append_layer(l, kd.data_ptr(), vd_.data_ptr())
+            self.pool.attend_layer(l, qd.data_ptr(), out.data_ptr())
+        self.pool.sync()
+        return out.cpu().numpy()
+
+    def end(self):
+        self.pool.commit()
+
+    def close(self):
+        self.pool.close()
+
+
+@pytest.fixture(scope="module")
+def vd():
+    import vx_decoder as mod
+
+    return mod
+
+
+def _setup(vxk, vd, tmp_path, seed, types, cache_dtype, untied=False, audio_cap=32):
+    import decoder_model
+
+    path = tmp_path / f"m{seed}.gguf"
+    tensors = decoder_model.build(path, seed, types=types, untied_f16_head=untied)
+    g = vxk.Gguf(path)
+    cfg = dict(n_layers=2, n_blocks=96, capacity=512, max_streams=4, max_rows=64, max_position=1024,
+               dtype=cache_dtype)
+    pool = vxk.Pool(**cfg)
+    dec = vxk.Decoder(g, pool, audio_capacity=audio_cap, enc_capacity=16)
+    g.close()
+    dev_att = DeviceAttention(vxk, cfg)
+    ref = (vd.Decoder(tensors, 2, cache_dtype=cache_dtype, capacity=512, attention=dev_att),
+           vd.Decoder(tensors, 2, cache_dtype=cache_dtype, capacity=512), dev_att)
+    return tensors, pool, dec, ref
+
+
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / np.abs(ref).max())
+
+
+def _compare(got_h, got_l, got_a, ref_h, ref_l, ref_a, e2e_h, e2e_l):
+    h_err, l_err = _rel(got_h, ref_h), _rel(got_l, ref_l)
+    e_h, e_l = _rel(got_h, e2e_h), _rel(got_l, e2e_l)
+    assert max(h_err, l_err) <= STEP_BAR, f"composition rel err hidden {h_err:.3g} logits {l_err:.3g}"
+    assert max(e_h, e_l) <= STEP_BAR, f"end-to-end rel err hidden {e_h:.3g} logits {e_l:.3g}"
+    gap_bar = 2 * np.abs(got_l - ref_l).max()
+    for r in range(ref_l.shape[0]):
+        top2 = np.sort(ref_l[r])[-2:]
+        if top2[1] - top2[0] > gap_bar:
+            assert got_a[r] == ref_a[r], f"row {r}: argmax {got_a[r]} != {ref_a[r]}"
+    return h_err, l_err, e_h, e_l
+
+
+def _run_steps(vxk, pool, dec, refs, streams, steps, audio, rng, vocab):
+    import torch
+
+    ref, e2e, _ = refs
+
+    cs = torch.cuda.current_stream().cuda_stream
+    errs = []
+    for batch in steps:
+        ids = [streams[i] for i, _ in batch]
+        n_new = [n for _, n in batch]
+        pool.plan(ids, n_new, cs)
+        toks, slots, audio_rows, ref_batch = [], [], [], []
+        for (i, n) in batch:
+            pos0 = e2e.stream(streams[i]).next_pos
+            t = [int(v) for v in rng.integers(0, vocab, n)]
+            toks += t
+            slots += [(pos0 + j) % audio.shape[1] for j in range(n)]
+            audio_rows += [audio[i, (pos0 + j) % audio.shape[1]] for j in range(n)]
+            ref_batch.append((streams[i], t))
+        ns = len(batch)
+        amax = torch.full((ns,), -1, dtype=torch.int32, device="cuda")
+        logits = torch.empty((ns, vocab), device="cuda")
+        hidden = torch.empty((ns, dec.info["dim"]), device="cuda")
+        dec.forward(toks, slots, amax.data_ptr(), logits.data_ptr(), hidden.data_ptr(), cs)
+        dec.sync(cs)
+        pool.commit()
+        ref_h, ref_l, ref_a = ref.forward(ref_batch, np.stack(audio_rows))
+        e_h, e_l, _ = e2e.forward(ref_batch, np.stack(audio_rows))
+        got_h, got_l = hidden.cpu().numpy(), logits.cpu().numpy().astype(np.float64)
+        err = _compare(got_h, got_l, amax.cpu().numpy(), ref_h, ref_l, ref_a, e_h, e_l)
+        print("\nstep", batch, "composition hidden / logits rel err %.3g %.3g, end to end %.3g %.3g" % err)
+        errs.append(err)
+    return errs
+
+
+@pytest.mark.parametrize("kind", ["q4_k_m", "q8_0"])
+def test_decoder_steps_match_oracle(vxk, vd, tmp_path, kind):
+    """Three fresh streams' first tokens (every row attends one key), a
+    multi-token append on two of them (append + causal attention over the
+    cache), then single-token steps in changing orders."""
+    import torch
+    import decoder_model
+
+    types = decoder_model.Q4_K_M if kind == "q4_k_m" else decoder_model.Q8_0_ALL
+    tensors, pool, dec, ref = _setup(vxk, vd, tmp_path, 11 if kind == "q4_k_m" else 12, types, 1)
+    rng = np.random.default_rng(3)
+    streams = [pool.open_stream() for _ in range(3)]
+    dim = dec.info["dim"]
+    audio = rng.normal(0, 0.05, (3, 32, dim)).astype(np.float32)
+    cs = torch.cuda.current_stream().cuda_stream
+    dev_audio = torch.from_numpy(audio).cuda()
+    for i, s in enumerate(streams):
+        dec.write_audio(s, 0, 32, dev_audio[i].data_ptr(), cs)
+    steps = [[(0, 1), (1, 1), (2, 1)], [(0, 5), (1, 3)], [(2, 1), (0, 1), (1, 1)], [(1, 1), (2, 1)]]
+    errs = _run_steps(vxk, pool, dec, ref, streams, steps, audio, rng, dec.info["vocab"])
+    assert min(max(e[0], e[1]) for e in errs) <= EXACT_BAR
+    ref[2].close()
+    dec.close()
+    pool.close()
+
+
+def test_decoder_q8_cache_and_untied_f16_head(vxk, vd, tmp_path):
+    """A q8_0 KV cache and an untied f16 output.weight head."""
+    import torch
+    import decoder_model
+
+    tensors, pool, dec, ref = _setup(vxk, vd, tmp_path, 13, decoder_model.Q4_K_M, 8, untied=True)
+    rng = np.random.default_rng(4)
+    streams = [pool.open_stream() for _ in range(2)]
+    audio = rng.normal(0, 0.05, (2, 32, dec.info["dim"])).astype(np.float32)
+    cs = torch.cuda.current_stream().cuda_stream
+    dev_audio = torch.from_numpy(audio).cuda()
+    for i, s in enumerate(streams):
+        dec.write_audio(s, 0, 32, dev_audio[i].data_ptr(), cs)
+    steps = [[(0, 4)], [(0, 1), (1, 1)], [(1, 1), (0, 1)]]
+    errs = _run_steps(vxk, pool, dec, ref, streams, steps, audio, rng, dec.info["vocab"])
+    assert min(max(e[0], e[1]) for e in errs) <= EXACT_BAR
+    ref[2].close()
+    dec.close()
+    pool.close()
+
+
+def test_adapter_ring(vxk, vd, tmp_path):
+    """Encoder frames -> adapter -> audio ring slots, groups of several
+    streams in one call, across the encoder ring's wrap."""
+    import torch
+    import decoder_model
+
+    tensors, pool, dec, ref = _setup(vxk, vd, tmp_path, 14, decoder_model.Q4_K_M, 1)
+    rng = np.random.default_rng(5)
+    enc_dim = dec.info["enc_dim"]
+    assert enc_dim == 256 and dec.info["enc_capacity"] == 16
+    cs = torch.cuda.current_stream().cuda_stream
+    s0, s1 = pool.open_stream(), pool.open_stream()
+    frames = {s: rng.normal(0, 1, (24, enc_dim)).astype(np.float32) for s in (s0, s1)}
+    # frames 0..11 then 12..23 (the second write wraps the 16-frame ring)
+    for s in (s0, s1):
+        d = torch.from_numpy(frames[s]).cuda()
+        dec.write_enc(s, 0, 12, d[:12].data_ptr(), cs)
+    groups = [(s0, 0, 0), (s1, 4, 7), (s0, 8, 1)]
+    dec.adapt([g[0] for g in groups], [g[1] for g in groups], [g[2] for g in groups], cs)
+    for s in (s0, s1):
+        d = torch.from_numpy(frames[s]).cuda()
+        dec.write_enc(s, 12, 12, d[12:].data_ptr(), cs)
+    groups2 = [(s1, 12, 40), (s0, 20, 34)]   # frame 12 -> slot 12, frame 20 -> slot 4 (wrapped); audio 40 -> 8, 34 -> 2
+    dec.adapt([g[0] for g in groups2], [g[1] for g in groups2], [g[2] for g in groups2], cs)
+    dec.sync(cs)
+    for s, f, a in groups + groups2:
+        out = torch.empty((1, dec.info["dim"]), device="cuda")
+        dec.read_audio(s, a, 1, out.data_ptr(), cs)
+        torch.cuda.synchronize()
+        want = ref[1].adapt(frames[s][f:f + 4][None])[0]
+        got = out.cpu().numpy()[0]
+        err = np.abs(got - want).max() / np.abs(want).max()
+        assert err <= 1e-3, f"group {(s, f, a)}: rel err {err:.3g}"
+    ref[2].close()
+    dec.close()
+    pool.close()
+
+
+def test_decoder_rejects_bad_calls(vxk, vd, tmp_path):
+    import torch
+    import decoder_model
+
+    tensors, pool, dec, ref = _setup(vxk, vd, tmp_path, 15, decoder_model.Q4_K_M, 1)
+    s = pool.open_stream()
+    amax = torch.zeros(4, dtype=torch.int32, device="cuda")
+    with pytest.raises(vxk.VxkError):      # nothing planned
+        dec.forward([1], [0], amax.data_ptr())
+    pool.plan([s], [1])
+    with pytest.raises(vxk.VxkError):      # token beyond the vocabulary
+        dec.forward([dec.info["vocab"]], [0], amax.data_ptr())
+    with pytest.raises(vxk.VxkError):      # audio slot beyond the ring
+        dec.forward([1], [32], amax.data_ptr())
+    pool.abort()
+    with pytest.raises(vxk.VxkError):      # enc_frame not a multiple of 4
+        dec.adapt([s], [2], [0])
+    # a pool whose layer count differs from the model's is refused
+    other = vxk.Pool(n_layers=3, n_blocks=16, capacity=64, max_streams=2, max_rows=8, max_position=128)
+    g = vxk.Gguf(tmp_path / "m15.gguf")
+    with pytest.raises(vxk.VxkError):
+        vxk.Decoder(g, other)
+    g.close()
+    other.close()
+    ref[2].close()
+    dec.close()
+    pool.close()

@@ -7,7 +7,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 struct vxk_qweight;
+struct vxk_pool;
 
 namespace vxk {
 
@@ -327,6 +330,10 @@ struct QweightShape {
     int32_t device, type, n_rows, n_cols, max_batch;
 };
 QweightShape qweight_shape(const vxk_qweight * w);
+// Points the matrix's device error word at `word` (shared by an owner that
+// reads one word for many matrices); nullptr restores its own.  The owner
+// keeps `word` alive until the matrix is destroyed or detached.
+void qweight_attach_error(vxk_qweight * w, int32_t * word);
 
 // Record bytes of one 16 x 256 tile (4352 / 2368 / 3360), 0 for other types.
 int qmm_record_bytes(int type);
@@ -338,5 +345,85 @@ int qmm_ctas_per_sm(const QmmParams & p, int smem);
 // Activation quantization, then the product (both with programmatic
 // dependent launch on `stream`; the product's splits as one cluster).
 cudaError_t launch_qmm(const QmmParams & p, cudaStream_t stream);
+
+// ---- whole decoder step (vxk_decoder.cu, vxk_decoder_host.cpp) ------------
+
+// The pool's planned batch as the decoder needs it.
+struct PoolBatchView {
+    std::vector<int32_t> row_stream;  // per query row
+    std::vector<int32_t> row_pos;
+    std::vector<int32_t> last_rows;   // per planned stream: its last row
+    bool single_token = false;
+};
+bool pool_batch_view(const vxk_pool * pool, PoolBatchView * out);
+
+struct PoolShape {
+    int32_t device, n_layers, n_q, n_kv, head_dim, max_streams, max_rows;
+    float rope_theta;
+};
+PoolShape pool_shape(const vxk_pool * pool);
+
+// One query row of a decoder forward.
+struct DecRow {
+    int32_t stream;
+    int32_t token;
+    int32_t audio_slot;
+    int32_t out_index;  // this row's stream index in the plan when it is the stream's last row, else -1
+};
+static_assert(sizeof(DecRow) == 16, "DecRow layout");
+
+// x = embedding row + audio row, xn = rms_norm(x) * w.
+struct EmbedParams {
+    const uint8_t * emb;      // tok_embeddings rows in their GGUF type
+    int64_t emb_row_bytes;
+    int32_t emb_type;         // ggml type: 0 F32, 1 F16, 8 Q8_0, 12 Q4_K, 14 Q6_K, 30 BF16
+    int32_t audio_cap;
+    const float * audio;      // [max_streams][audio_cap][dim]
+    const DecRow * rows;
+    int32_t n_rows;
+    int32_t dim;
+    const float * norm_w;
+    float eps;
+    float * x;                // [rows][dim] residual stream
+    float * xn;               // [rows][dim]
+};
+
+// x += add (when add != nullptr); out = rms_norm(x) * w, then out + out * ada
+// when ada != nullptr.  compact: only rows with out_index >= 0, written to
+// out row out_index.
+struct NormParams {
+    float * x;
+    const float * add;
+    const float * w;
+    const float * ada;
+    float * out;
+    const DecRow * rows;
+    int32_t compact;
+    int32_t n_rows;
+    int32_t dim;
+    float eps;
+};
+
+// One adapter group: 4 encoder frames of a stream into one audio slot.
+struct AdaptRow {
+    int32_t stream;
+    int32_t enc_slot;     // slot of the group's first frame (a multiple of 4)
+    int32_t audio_slot;
+    int32_t reserved;
+};
+static_assert(sizeof(AdaptRow) == 16, "AdaptRow layout");
+
+cudaError_t launch_embed_norm(const EmbedParams & p, cudaStream_t stream);
+cudaError_t launch_add_norm(const NormParams & p, cudaStream_t stream);
+// out = silu(gate) * up over n values.
+cudaError_t launch_swiglu(const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream);
+// x = gelu_erf(x) over n values.
+cudaError_t launch_gelu_erf(float * x, int64_t n, cudaStream_t stream);
+// out[g] = the 4 frames of group g, concatenated ([n][4 * enc_dim]).
+cudaError_t launch_adapter_gather(const float * enc, int32_t enc_cap, int32_t enc_dim, const AdaptRow * rows,
+                                  int32_t n, float * out, cudaStream_t stream);
+// audio[stream][audio_slot] = y[g] for each group.
+cudaError_t launch_audio_scatter(const float * y, float * audio, int32_t audio_cap, int32_t dim,
+                                 const AdaptRow * rows, int32_t n, cudaStream_t stream);
 
 }  // namespace vxk

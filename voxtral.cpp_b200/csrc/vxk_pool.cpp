@@ -609,6 +609,34 @@ void check_error_word(vxk_pool * p) {
 
 }  // namespace
 
+namespace vxk {
+
+bool pool_batch_view(const vxk_pool * pool, PoolBatchView * out) {
+    if (!pool || !out || !pool->planned) return false;
+    out->row_stream.resize(pool->rows.size());
+    out->row_pos.resize(pool->rows.size());
+    for (size_t r = 0; r < pool->rows.size(); ++r) {
+        out->row_stream[r] = pool->rows[r].stream;
+        out->row_pos[r] = pool->rows[r].pos;
+    }
+    out->last_rows.clear();
+    int32_t end = 0;
+    for (const PlanEntry & e : pool->plan) {
+        end += e.plan.n_new;
+        out->last_rows.push_back(end - 1);
+    }
+    out->single_token = pool->single_token;
+    return true;
+}
+
+PoolShape pool_shape(const vxk_pool * pool) {
+    const vxk_pool_config & c = pool->cfg;
+    return PoolShape{c.device, c.n_layers, c.n_q_heads, c.n_kv_heads, c.head_dim, c.max_streams, c.max_rows,
+                     c.rope_theta};
+}
+
+}  // namespace vxk
+
 extern "C" {
 
 vxk_pool_config vxk_pool_default_config(void) {

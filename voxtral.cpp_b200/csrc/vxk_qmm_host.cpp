@@ -244,6 +244,7 @@ struct vxk_qweight {
     uint8_t * tc_bmin = nullptr;
     float * tc_dx = nullptr;
     int32_t * d_error = nullptr;
+    int32_t * own_error = nullptr;   // d_error unless an owner attached a shared word
     cudaEvent_t ev_sync = nullptr;
     std::string last_error;
 };
@@ -271,7 +272,7 @@ void free_qweight(vxk_qweight * w) {
     if (!w) return;
     QwDevice scope(w->cfg.device);
     for (void * p : {(void *) w->w, (void *) w->act, (void *) w->act_d, (void *) w->act_ms, (void *) w->w_tc,
-                     (void *) w->dd_tc, (void *) w->tc_b, (void *) w->tc_bmin, (void *) w->tc_dx, (void *) w->d_error})
+                     (void *) w->dd_tc, (void *) w->tc_b, (void *) w->tc_bmin, (void *) w->tc_dx, (void *) w->own_error})
         if (p) cudaFree(p);
     if (w->ev_sync) cudaEventDestroy(w->ev_sync);
     delete w;
@@ -448,6 +449,8 @@ QweightShape qweight_shape(const vxk_qweight * w) {
     return QweightShape{w->cfg.device, (int32_t) w->cfg.type, w->cfg.n_rows, w->cfg.n_cols, w->cfg.max_batch};
 }
 
+void qweight_attach_error(vxk_qweight * w, int32_t * word) { w->d_error = word ? word : w->own_error; }
+
 }  // namespace vxk
 
 extern "C" {
@@ -553,6 +556,7 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
             VXK_QCUDA(cudaMalloc(&w->tc_dx, (size_t) w->n_units * 64 * sizeof(float)));
         }
         VXK_QCUDA(cudaMalloc(&w->d_error, sizeof(int32_t)));
+        w->own_error = w->d_error;
         VXK_QCUDA(cudaMemset(w->d_error, 0, sizeof(int32_t)));
         VXK_QCUDA(cudaEventCreateWithFlags(&w->ev_sync, cudaEventDisableTiming));
         VXK_QCUDA(cudaDeviceSynchronize());

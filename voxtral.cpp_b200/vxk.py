@@ -99,6 +99,17 @@ class GgufTensor(C.Structure):
     _fields_ = [("name", C.c_char_p), ("type", C.c_int32), ("n_dims", C.c_int32), ("ne", C.c_int64 * 4),
                 ("offset", C.c_uint64), ("n_bytes", C.c_uint64)]
 
+class DecoderConfig(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("audio_capacity", C.c_int32),
+                ("enc_capacity", C.c_int32), ("time_value", C.c_float), ("reserved", C.c_int32 * 3)]
+
+
+class DecoderInfo(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("n_layers", "dim", "hidden", "n_q_heads", "n_kv_heads", "head_dim",
+                                         "vocab", "ada_dim", "emb_type", "max_rows", "max_streams",
+                                         "audio_capacity", "enc_capacity", "enc_dim")] + [("device_bytes", C.c_int64)]
+
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -183,6 +194,17 @@ SIGNATURES = {
     "vxk_gguf_get_array": (_I32, [_P, C.c_char_p, _I32P, _I64P, C.POINTER(C.c_void_p)]),
     "vxk_gguf_get_array_str": (_I32, [_P, C.c_char_p, _I64, C.POINTER(C.c_char_p)]),
     "vxk_qweight_create_from_gguf": (_I32, [_P, C.c_char_p, _I32, _I32, C.POINTER(C.c_void_p)]),
+    "vxk_decoder_default_config": (DecoderConfig, []),
+    "vxk_decoder_create": (_I32, [_P, _P, C.POINTER(DecoderConfig), C.POINTER(C.c_void_p)]),
+    "vxk_decoder_destroy": (None, [_P]),
+    "vxk_decoder_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_decoder_get_info": (_I32, [_P, C.POINTER(DecoderInfo)]),
+    "vxk_decoder_forward": (_I32, [_P, _I32P, _I32P, _P, _P, _P, _P]),
+    "vxk_decoder_write_enc": (_I32, [_P, _I32, _I64, _I32, _P, _P]),
+    "vxk_decoder_write_audio": (_I32, [_P, _I32, _I64, _I32, _P, _P]),
+    "vxk_decoder_adapt": (_I32, [_P, _I32, _I32P, _I64P, _I64P, _P]),
+    "vxk_decoder_read_audio": (_I32, [_P, _I32, _I64, _I32, _P, _P]),
+    "vxk_decoder_sync": (_I32, [_P, _P, _I32]),
 }
 
 _lib = None
@@ -664,3 +686,74 @@ class Gguf:
             raise VxkError(st, q.last_error(None))
         q.h = h
         return q
+
+
+class Decoder:
+    """Owns one vxk_decoder: a GGUF model's decoder, head and adapter on the
+    pool's device, run over the pool's planned batch (vxk_decoder_forward)."""
+
+    def __init__(self, gguf: "Gguf", pool: Pool, **cfg):
+        self.lib = load()
+        c = self.lib.vxk_decoder_default_config()
+        for k, v in cfg.items():
+            if not hasattr(c, k):
+                raise AttributeError(k)
+            setattr(c, k, v)
+        self.config = c
+        self.pool = pool
+        h = C.c_void_p()
+        st = self.lib.vxk_decoder_create(gguf.h, pool.h, C.byref(c), C.byref(h))
+        if st != OK:
+            raise VxkError(st, self._error(None))
+        self.h = h
+        info = DecoderInfo()
+        self._check(self.lib.vxk_decoder_get_info(self.h, C.byref(info)))
+        self.info = {n: getattr(info, n) for n, _ in DecoderInfo._fields_}
+
+    def _error(self, h) -> str:
+        buf = C.create_string_buffer(1024)
+        self.lib.vxk_decoder_last_error(h, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st: int):
+        if st != OK:
+            raise VxkError(st, self._error(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, tokens, audio_slots, argmax_ptr: int, logits_ptr: int = 0, hidden_ptr: int = 0,
+                cuda_stream: int = 0):
+        """tokens / audio_slots: one int per row of the planned batch (host)."""
+        t = _i32_array(list(tokens))
+        a = _i32_array(list(audio_slots))
+        self._check(self.lib.vxk_decoder_forward(self.h, t, a, argmax_ptr, logits_ptr or None, hidden_ptr or None,
+                                                 cuda_stream or None))
+
+    def write_enc(self, stream: int, frame: int, n: int, rows_ptr: int, cuda_stream: int = 0):
+        self._check(self.lib.vxk_decoder_write_enc(self.h, stream, frame, n, rows_ptr, cuda_stream or None))
+
+    def write_audio(self, stream: int, pos: int, n: int, rows_ptr: int, cuda_stream: int = 0):
+        self._check(self.lib.vxk_decoder_write_audio(self.h, stream, pos, n, rows_ptr, cuda_stream or None))
+
+    def read_audio(self, stream: int, pos: int, n: int, rows_ptr: int, cuda_stream: int = 0):
+        self._check(self.lib.vxk_decoder_read_audio(self.h, stream, pos, n, rows_ptr, cuda_stream or None))
+
+    def adapt(self, streams, enc_frames, audio_pos, cuda_stream: int = 0):
+        n = len(streams)
+        s = _i32_array(list(streams))
+        e = (C.c_int64 * n)(*enc_frames)
+        a = (C.c_int64 * n)(*audio_pos)
+        self._check(self.lib.vxk_decoder_adapt(self.h, n, s, e, a, cuda_stream or None))
+
+    def sync(self, cuda_stream: int = 0, timeout_ms: int = 10000):
+        self._check(self.lib.vxk_decoder_sync(self.h, cuda_stream or None, timeout_ms))
+

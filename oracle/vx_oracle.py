@@ -296,7 +296,7 @@ def qmatmul(wtype: int, w_blocks: np.ndarray, n: int, k: int, x: np.ndarray):
     w_blocks = np.ascontiguousarray(w_blocks, dtype=np.uint8)
     x = np.ascontiguousarray(x, dtype=np.float32)
     rows = x.shape[0]
-    assert x.shape[1] == k and k <= 8192 and w_blocks.size == n * qrow_bytes(wtype, k)
+    assert x.shape[1] == k and k <= 16384 and w_blocks.size == n * qrow_bytes(wtype, k)
     y = np.empty((rows, n), np.float64)
     mag = np.empty((rows, n), np.float64)
     terms = lib().vxo_qmatmul(wtype, _ptr(w_blocks), n, k, _ptr(x), rows, _ptr(y), _ptr(mag))

@@ -171,7 +171,7 @@ int32_t vxo_qmatmul(int32_t type, const uint8_t * w, int32_t n, int32_t k, const
     int v[256];
     if (type == T_Q8_0) {
         const int nb = k / 32;
-        uint8_t xq[34 * 256];  /* k <= 8192 */
+        uint8_t xq[34 * 512];  /* k <= 16384 */
         for (int32_t r = 0; r < rows; ++r) {
             vxo_quantize_row_q8_0(x + (int64_t) r * k, k, xq);
             for (int32_t i = 0; i < n; ++i) {
@@ -192,9 +192,9 @@ int32_t vxo_qmatmul(int32_t type, const uint8_t * w, int32_t n, int32_t k, const
         return nb;
     }
     const int nb = k / 256;
-    float dx[32];
-    int8_t qx[256 * 32];
-    int16_t bs[16 * 32];  /* k <= 8192 */
+    float dx[64];
+    int8_t qx[256 * 64];
+    int16_t bs[16 * 64];  /* k <= 16384 */
     for (int32_t r = 0; r < rows; ++r) {
         vxo_quantize_row_q8_K(x + (int64_t) r * k, k, dx, qx, bs);
         for (int32_t i = 0; i < n; ++i) {

@@ -7,7 +7,6 @@
 //                      of the GGUF type, ggml_add), xn = rms_norm(x) * attn_norm
 //   add_norm_kernel    x += proj (ggml_add), out = rms_norm(x) * w, optional
 //                      out + out * ada (the time conditioning, 2862-2874)
-//   swiglu_kernel      silu(gate) * up (2877-2880)
 //   gelu_erf_kernel    the adapter's and time MLP's ggml_gelu_erf
 //   adapter gather / audio scatter: 4 encoder frames per group, audio ring rows
 //
@@ -58,45 +57,81 @@ __global__ void __launch_bounds__(kNormThreads) embed_norm_kernel(EmbedParams p)
     for (int i = threadIdx.x; i < p.dim; i += kNormThreads) xn[i] = __fmul_rn(__fmul_rn(x[i], scale), p.norm_w[i]);
 }
 
+// One row per CTA; V float4 per thread held in registers, every load issued
+// before the first store (x and add may not be assumed apart otherwise).
+// Launched as a programmatic dependent of the previous kernel: nothing is read
+// or written before griddepcontrol.wait (the producer grid has completed and
+// its memory is visible); the next launch may start right after.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <int V>
 __global__ void __launch_bounds__(kNormThreads) add_norm_kernel(NormParams p) {
     __shared__ double red[kNormThreads / 32];
+    pdl_enter();
     const int r = blockIdx.x;
     int out_row = r;
     if (p.compact) {
         out_row = p.rows[r].out_index;
         if (out_row < 0) return;  // the last norm: only each stream's last row goes on
     }
-    float * x = p.x + (int64_t) r * p.dim;
-    const float * add = p.add ? p.add + (int64_t) r * p.dim : nullptr;
-    double sum = 0.0;
-    for (int i = threadIdx.x; i < p.dim; i += kNormThreads) {
-        float v = x[i];
-        if (add) {
-            v = __fadd_rn(v, add[i]);
-            x[i] = v;
+    const int n4 = p.dim / 4;
+    float4 * x = reinterpret_cast<float4 *>(p.x + (int64_t) r * p.dim);
+    const float4 * add = p.add ? reinterpret_cast<const float4 *>(p.add + (int64_t) r * p.dim) : nullptr;
+    float4 v[V];
+    float4 a[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < n4) {
+            v[j] = x[i];
+            if (add) a[j] = add[i];
         }
-        sum += (double) __fmul_rn(v, v);
+    }
+    double sum = 0.0;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < n4) {
+            if (add) {
+                v[j].x = __fadd_rn(v[j].x, a[j].x);
+                v[j].y = __fadd_rn(v[j].y, a[j].y);
+                v[j].z = __fadd_rn(v[j].z, a[j].z);
+                v[j].w = __fadd_rn(v[j].w, a[j].w);
+                x[i] = v[j];
+            }
+            sum += (double) __fmul_rn(v[j].x, v[j].x);
+            sum += (double) __fmul_rn(v[j].y, v[j].y);
+            sum += (double) __fmul_rn(v[j].z, v[j].z);
+            sum += (double) __fmul_rn(v[j].w, v[j].w);
+        }
     }
     sum = block_sum(sum, red);
     const float scale = rms_scale(sum, p.dim, p.eps);
-    float * out = p.out + (int64_t) out_row * p.dim;
-    for (int i = threadIdx.x; i < p.dim; i += kNormThreads) {
-        float y = __fmul_rn(__fmul_rn(x[i], scale), p.w[i]);
-        if (p.ada) y = __fadd_rn(y, __fmul_rn(y, p.ada[i]));
-        out[i] = y;
-    }
-}
-
-__global__ void swiglu_kernel(const float4 * gate, const float4 * up, float4 * out, int64_t n4) {
-    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n4; i += (int64_t) gridDim.x * blockDim.x) {
-        const float4 g = gate[i];
-        const float4 u = up[i];
-        float4 o;
-        o.x = __fmul_rn(__fdiv_rn(g.x, __fadd_rn(1.0f, expf(-g.x))), u.x);
-        o.y = __fmul_rn(__fdiv_rn(g.y, __fadd_rn(1.0f, expf(-g.y))), u.y);
-        o.z = __fmul_rn(__fdiv_rn(g.z, __fadd_rn(1.0f, expf(-g.z))), u.z);
-        o.w = __fmul_rn(__fdiv_rn(g.w, __fadd_rn(1.0f, expf(-g.w))), u.w);
-        out[i] = o;
+    const float4 * w = reinterpret_cast<const float4 *>(p.w);
+    const float4 * ada = p.ada ? reinterpret_cast<const float4 *>(p.ada) : nullptr;
+    float4 * out = reinterpret_cast<float4 *>(p.out + (int64_t) out_row * p.dim);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < n4) {
+            const float4 wv = w[i];
+            float4 y;
+            y.x = __fmul_rn(__fmul_rn(v[j].x, scale), wv.x);
+            y.y = __fmul_rn(__fmul_rn(v[j].y, scale), wv.y);
+            y.z = __fmul_rn(__fmul_rn(v[j].z, scale), wv.z);
+            y.w = __fmul_rn(__fmul_rn(v[j].w, scale), wv.w);
+            if (ada) {
+                const float4 av = ada[i];
+                y.x = __fadd_rn(y.x, __fmul_rn(y.x, av.x));
+                y.y = __fadd_rn(y.y, __fmul_rn(y.y, av.y));
+                y.z = __fadd_rn(y.z, __fmul_rn(y.z, av.z));
+                y.w = __fadd_rn(y.w, __fmul_rn(y.w, av.w));
+            }
+            out[i] = y;
+        }
     }
 }
 
@@ -126,6 +161,21 @@ __global__ void audio_scatter_kernel(const float4 * y, float4 * audio, int32_t a
     for (int i = threadIdx.x; i < dim4; i += blockDim.x) dst[i] = src[i];
 }
 
+template <typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, unsigned block, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int grid_for(int64_t n, int threads) {
     const int64_t g = (n + threads - 1) / threads;
     return (int) (g < 148 * 16 ? (g > 0 ? g : 1) : 148 * 16);
@@ -141,17 +191,14 @@ cudaError_t launch_embed_norm(const EmbedParams & p, cudaStream_t stream) {
 
 cudaError_t launch_add_norm(const NormParams & p, cudaStream_t stream) {
     if (p.n_rows <= 0) return cudaSuccess;
-    add_norm_kernel<<<p.n_rows, kNormThreads, 0, stream>>>(p);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_swiglu(const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream) {
-    if (n <= 0 || n % 4) return n ? cudaErrorInvalidValue : cudaSuccess;
-    const int64_t n4 = n / 4;
-    swiglu_kernel<<<grid_for(n4, 256), 256, 0, stream>>>(reinterpret_cast<const float4 *>(gate),
-                                                         reinterpret_cast<const float4 *>(up),
-                                                         reinterpret_cast<float4 *>(out), n4);
-    return cudaGetLastError();
+    if (p.dim % 4 || p.dim > 16 * 4 * kNormThreads) return cudaErrorInvalidValue;
+    const int v = (p.dim / 4 + kNormThreads - 1) / kNormThreads;
+    const dim3 grid((unsigned) p.n_rows);
+    if (v <= 1) return launch_pdl(add_norm_kernel<1>, grid, kNormThreads, stream, p);
+    if (v <= 2) return launch_pdl(add_norm_kernel<2>, grid, kNormThreads, stream, p);
+    if (v <= 4) return launch_pdl(add_norm_kernel<4>, grid, kNormThreads, stream, p);
+    if (v <= 8) return launch_pdl(add_norm_kernel<8>, grid, kNormThreads, stream, p);
+    return launch_pdl(add_norm_kernel<16>, grid, kNormThreads, stream, p);
 }
 
 cudaError_t launch_gelu_erf(float * x, int64_t n, cudaStream_t stream) {

@@ -12,7 +12,8 @@
 //                                    vxk_append_layer + vxk_attend_layer (prefill)
 //     proj = Wo att
 //     add_norm                       x += proj; xn = norm(x) * ffn_norm[l] * (1 + ada[l])
-//     gate, up = W1 xn, W3 xn; ffn = silu(gate) * up; proj = W2 ffn
+//     gate, up = W1 xn, W3 xn; proj = W2 (silu(gate) * up), the SwiGLU
+//                                    inside W2's activation quantization
 //     add_norm                       x += proj; xn = norm(x) * attn_norm[l + 1]
 //                                    (after the last layer: dec_norm, each stream's last row only)
 //   head                             logits and argmax of those rows
@@ -119,7 +120,6 @@ struct vxk_decoder {
     float * proj = nullptr;
     float * gate = nullptr;
     float * up = nullptr;
-    float * ffn = nullptr;
     float * hn = nullptr;
     float * ad_in = nullptr;
     float * ad_mid = nullptr;
@@ -177,7 +177,7 @@ void destroy(vxk_decoder * d) {
     for (void * p : {(void *) d->emb, (void *) d->head_w16_own, (void *) d->attn_norm, (void *) d->ffn_norm,
                      (void *) d->dec_norm, (void *) d->ada, (void *) d->audio, (void *) d->enc, (void *) d->x,
                      (void *) d->xn, (void *) d->q, (void *) d->k, (void *) d->v, (void *) d->att, (void *) d->proj,
-                     (void *) d->gate, (void *) d->up, (void *) d->ffn, (void *) d->hn, (void *) d->ad_in,
+                     (void *) d->gate, (void *) d->up, (void *) d->hn, (void *) d->ad_in,
                      (void *) d->ad_mid, (void *) d->ad_out, (void *) d->d_rows, (void *) d->d_adapt,
                      (void *) d->d_error})
         if (p) cudaFree(p);
@@ -510,7 +510,6 @@ void create(vxk_decoder * d, const vxk_gguf * g, vxk_pool * pool) {
     d->proj = dalloc<float>(d, R * d->dim);
     d->gate = dalloc<float>(d, C * d->hidden);
     d->up = dalloc<float>(d, C * d->hidden);
-    d->ffn = dalloc<float>(d, C * d->hidden);
     d->hn = dalloc<float>(d, (size_t) ps.max_streams * d->dim);
     d->d_rows = dalloc<vxk::DecRow>(d, R);
     d->stage_bytes = R * sizeof(vxk::DecRow);
@@ -613,11 +612,10 @@ void forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slot
             float * ys[2] = {d->gate, d->up};
             const int64_t st[2] = {d->hidden, d->hidden};
             products(d, ws, 2, d->xn + (int64_t) r0 * dim, dim, nr, ys, st, cs);
-            VXK_DCUDA(vxk::launch_swiglu(d->gate, d->up, d->ffn, (int64_t) nr * d->hidden, cs));
-            vxk_qweight * w2[1] = {L.w2};
-            float * y2[1] = {d->proj + (int64_t) r0 * dim};
-            const int64_t s2[1] = {dim};
-            products(d, w2, 1, d->ffn, d->hidden, nr, y2, s2, cs);
+            // w2 . (silu(gate) * up): SwiGLU inside w2's activation quantization
+            VXK_DCALL((vxk_status) vxk::qweight_matmul_swiglu(L.w2, d->gate, d->up, nr, d->proj + (int64_t) r0 * dim,
+                                                              cs),
+                      "quantized product");
         }
         const bool last = l + 1 == d->n_layers;
         np.w = last ? d->dec_norm : d->attn_norm + (int64_t) (l + 1) * dim;

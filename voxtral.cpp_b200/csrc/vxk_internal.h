@@ -278,6 +278,7 @@ struct QmmParams {
     int32_t units_per_split;   // column units per CTA
     int32_t n_splits;          // ceil(n_units / units_per_split) <= kQmmMaxSplits: one cluster
     const float * x;           // [rows][K] fp32
+    const float * x_up;        // nullptr, or [rows][K]: the row is silu(x) * x_up (SwiGLU)
     uint8_t * act;             // [n_units][nt][8 blocks][32 lanes][8 B] int8 B fragments
     float * act_d;             // Q8_0: [n_units * 8][nt * 8]; K-quants: [n_units][nt * 8]
     uint8_t * act_ms;          // K-quants: [n_units][nt][32 lanes][8 B] sums of 32 quantized
@@ -314,6 +315,7 @@ struct QtcParams {
     int32_t units_per_split;
     int32_t n_splits;          // <= kQmmMaxSplits: one cluster
     const float * x;           // [rows][K] fp32
+    const float * x_up;        // nullptr, or [rows][K]: the row is silu(x) * x_up (SwiGLU)
     uint8_t * b_tiles;         // [n_units][npad x 256 f16, 4 SW128 atoms]
     uint8_t * bmin_tiles;      // [n_units][npad rows of 128 B, SW128; K 0..15 used]
     float * dx;                // [n_units][npad]
@@ -334,6 +336,18 @@ QweightShape qweight_shape(const vxk_qweight * w);
 // reads one word for many matrices); nullptr restores its own.  The owner
 // keeps `word` alive until the matrix is destroyed or detached.
 void qweight_attach_error(vxk_qweight * w, int32_t * word);
+// y = W (silu(gate) * up), the SwiGLU product computed inside the activation
+// quantization (silu(g) = g / (1 + expf(-g)), each step rounded like the
+// separate kernel would); 0 or a vxk_status number.
+int32_t qweight_matmul_swiglu(vxk_qweight * w, const float * gate, const float * up, int32_t rows, float * y,
+                              cudaStream_t stream);
+// silu(g) * u with separately rounded steps (ggml_silu then ggml_mul,
+// src/voxtral.cpp:2877-2880), evaluated inside the activation quantization.
+#ifdef __CUDACC__
+__device__ __forceinline__ float swiglu_value(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+#endif
 
 // Record bytes of one 16 x 256 tile (4352 / 2368 / 3360), 0 for other types.
 int qmm_record_bytes(int type);
@@ -415,8 +429,6 @@ static_assert(sizeof(AdaptRow) == 16, "AdaptRow layout");
 
 cudaError_t launch_embed_norm(const EmbedParams & p, cudaStream_t stream);
 cudaError_t launch_add_norm(const NormParams & p, cudaStream_t stream);
-// out = silu(gate) * up over n values.
-cudaError_t launch_swiglu(const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream);
 // x = gelu_erf(x) over n values.
 cudaError_t launch_gelu_erf(float * x, int64_t n, cudaStream_t stream);
 // out[g] = the 4 frames of group g, concatenated ([n][4 * enc_dim]).

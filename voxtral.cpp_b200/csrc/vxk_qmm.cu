@@ -210,7 +210,8 @@ __global__ void __launch_bounds__(256) qmm_act_kernel(const QmmParams p) {
     const int lane = t & 31, warp = t >> 5;
     const int64_t K = (int64_t) p.n_units * kQmmUnit;
     const int ncol = p.nt * 8;
-    const float x = r < p.rows ? p.x[(int64_t) r * K + (int64_t) u * kQmmUnit + t] : 0.0f;
+    const int64_t xi = (int64_t) r * K + (int64_t) u * kQmmUnit + t;
+    const float x = r < p.rows ? (p.x_up ? swiglu_value(p.x[xi], p.x_up[xi]) : p.x[xi]) : 0.0f;
     int q = 0;
     if constexpr (FAM == 0) {
         float amax = fabsf(x);

@@ -370,8 +370,8 @@ void plan_split_tc(int32_t n_units, int32_t sms, int64_t blocks, vxk::QtcParams 
     p.n_splits = (n_units + best - 1) / best;
 }
 
-void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
-            int32_t * error, cudaStream_t stream) {
+void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * x_up, int32_t rows,
+            float * const * ys, int32_t * error, cudaStream_t stream) {
     vxk_qweight * w0 = ws[0];
     vxk::QtcParams p{};
     p.n_mats = n;
@@ -390,6 +390,7 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, 
     }
     plan_split_tc(w0->n_units, w0->sms, block0, p);
     p.x = x;
+    p.x_up = x_up;
     p.b_tiles = w0->tc_b;
     p.bmin_tiles = w0->tc_bmin;
     p.dx = w0->tc_dx;
@@ -397,8 +398,8 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, 
     VXK_QCUDA(vxk::launch_qtc(p, stream));
 }
 
-void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
-              int32_t * error, cudaStream_t stream) {
+void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, const float * x_up, int32_t rows,
+              float * const * ys, int32_t * error, cudaStream_t stream) {
     vxk_qweight * w0 = ws[0];
     vxk::QmmParams p{};
     p.n_mats = n;
@@ -412,6 +413,7 @@ void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows
     }
     plan_split(w0->n_units, w0->sms, p);
     p.x = x;
+    p.x_up = x_up;
     p.act = w0->act;
     p.act_d = w0->act_d;
     p.act_ms = w0->act_ms;
@@ -424,7 +426,7 @@ void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows
 // launch, the others in one int8 mma.sync launch, each with its own
 // quantization of x (the two kernels read different operand layouts).
 void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
-               cudaStream_t stream) {
+               cudaStream_t stream, const float * x_up = nullptr) {
     vxk_qweight * tw[vxk::kQmmMaxGroup], * sw[vxk::kQmmMaxGroup];
     float * ty[vxk::kQmmMaxGroup], * sy[vxk::kQmmMaxGroup];
     int nt = 0, ns = 0;
@@ -437,8 +439,8 @@ void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t row
             sy[ns++] = ys[i];
         }
     }
-    if (nt) run_tc(tw, nt, x, rows, ty, ws[0]->d_error, stream);
-    if (ns) run_sync(sw, ns, x, rows, sy, ws[0]->d_error, stream);
+    if (nt) run_tc(tw, nt, x, x_up, rows, ty, ws[0]->d_error, stream);
+    if (ns) run_sync(sw, ns, x, x_up, rows, sy, ws[0]->d_error, stream);
 }
 
 }  // namespace
@@ -450,6 +452,19 @@ QweightShape qweight_shape(const vxk_qweight * w) {
 }
 
 void qweight_attach_error(vxk_qweight * w, int32_t * word) { w->d_error = word ? word : w->own_error; }
+
+int32_t qweight_matmul_swiglu(vxk_qweight * w, const float * gate, const float * up, int32_t rows, float * y,
+                              cudaStream_t stream) {
+    if (!w) return VXK_STATUS_INVALID_ARGUMENT;
+    return qguarded(w, [&] {
+        if (!gate || !up || !y) qfail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        if (rows < 1 || rows > w->cfg.max_batch) qfail(VXK_STATUS_INVALID_ARGUMENT, "rows must be in [1, max_batch]");
+        QwDevice scope(w->cfg.device);
+        vxk_qweight * one[1] = {w};
+        float * yv[1] = {y};
+        run_group(one, 1, gate, rows, yv, stream, up);
+    });
+}
 
 }  // namespace vxk
 

@@ -306,7 +306,8 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     const int u = blockIdx.x, r = blockIdx.y, t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
     const int64_t K = (int64_t) p.n_units * kQmmUnit;
-    const float x = r < p.rows ? p.x[(int64_t) r * K + (int64_t) u * kQmmUnit + t] : 0.0f;
+    const int64_t xi = (int64_t) r * K + (int64_t) u * kQmmUnit + t;
+    const float x = r < p.rows ? (p.x_up ? swiglu_value(p.x[xi], p.x_up[xi]) : p.x[xi]) : 0.0f;
     __shared__ unsigned long long red[8];
     __shared__ float s_max;
     unsigned long long key = ((unsigned long long) __float_as_uint(fabsf(x)) << 32) | (unsigned) (255 - t);

@@ -684,6 +684,72 @@ VXK_API vxk_status vxk_decoder_read_audio(vxk_decoder * d, int32_t stream, int64
  *  launches use (pool, products, head). */
 VXK_API vxk_status vxk_decoder_sync(vxk_decoder * d, void * cuda_stream, int32_t timeout_ms);
 
+/* ======================================================================== */
+/* Cross-context batcher                                                     */
+/* ======================================================================== */
+
+/**
+ * Gathers the single-token decoder steps of many contexts into one batch per
+ * GPU.  In the reference every voxtral_context runs its own step graph
+ * (voxtral_ctx_decoder_step, src/voxtral-internal.h:243-251, called by
+ * pump_incremental, src/voxtral-stream-decoder.cpp:92-98, 163-164, each
+ * context on its own thread, include/voxtral.h:223); behind the unchanged C
+ * ABI that call becomes vxk_batcher_step, which blocks its thread until the
+ * batch holding its row has run.  A dispatcher thread inside the batcher
+ * starts a batch when max_rows requests are queued, when `expected` are
+ * queued, or max_wait_us after the oldest queued request, whichever comes
+ * first; requests of one stream never share a batch.  Thread-safe.
+ */
+typedef struct vxk_batcher vxk_batcher;
+
+typedef struct vxk_batcher_config {
+    uint32_t struct_size;
+    uint32_t api_version;
+    int32_t max_rows;       /* rows per batch, 1..4096 */
+    int32_t max_wait_us;    /* the oldest request waits at most this long for company */
+    int32_t expected;       /* 0, or start as soon as this many requests are queued */
+    int32_t timeout_ms;     /* bounded wait of vxk_batcher_step for its result */
+} vxk_batcher_config;
+
+VXK_API vxk_batcher_config vxk_batcher_default_config(void);
+
+/** Runs one batch: n rows (stream, token, audio slot), writes each row's next
+ *  token.  Called on the dispatcher thread, one batch at a time. */
+typedef vxk_status (*vxk_batch_fn)(void * user, int32_t n, const int32_t * streams, const int32_t * tokens,
+                                   const int32_t * audio_slots, int32_t * out_tokens);
+
+VXK_API vxk_status vxk_batcher_create(const vxk_batcher_config * config, vxk_batch_fn fn, void * user,
+                                      vxk_batcher ** out);
+/**
+ * A batcher whose batches run the decoder: vxk_batch_plan (one token per
+ * stream), vxk_decoder_forward, the argmax read back (4 bytes per row),
+ * vxk_decoder_sync, then vxk_batch_commit (vxk_batch_abort on failure), on
+ * cuda_stream from the dispatcher thread.
+ */
+VXK_API vxk_status vxk_batcher_create_for_decoder(const vxk_batcher_config * config, vxk_decoder * d,
+                                                  vxk_pool * pool, void * cuda_stream, vxk_batcher ** out);
+/** Stops the dispatcher after the running batch; queued requests get
+ *  VXK_STATUS_INVALID_STATE; returns once every vxk_batcher_step in progress
+ *  has returned (none may start afterwards).  NULL is safe. */
+VXK_API void vxk_batcher_destroy(vxk_batcher * b);
+
+/** One decoder step of `stream` (its token and audio slot); blocks until the
+ *  batch ran (out_token = the greedy next token) or timeout_ms passed
+ *  (VXK_STATUS_TIMEOUT; the row still runs with its batch if already taken). */
+VXK_API vxk_status vxk_batcher_step(vxk_batcher * b, int32_t stream, int32_t token, int32_t audio_slot,
+                                    int32_t * out_token);
+
+typedef struct vxk_batcher_stats {
+    int64_t batches;
+    int64_t rows;
+    int64_t max_rows_seen;
+    int64_t failed_batches;
+    int64_t timeouts;
+    double mean_wait_us;    /* request queued -> its batch started */
+} vxk_batcher_stats;
+
+VXK_API vxk_status vxk_batcher_get_stats(const vxk_batcher * b, vxk_batcher_stats * out);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -262,3 +262,67 @@ def test_decoder_rejects_bad_calls(vxk, vd, tmp_path):
     ref[2].close()
     dec.close()
     pool.close()
+
+
+def test_batcher_runs_the_decoder(vxk, vd, tmp_path):
+    """Four context threads decoding greedily through vxk_batcher (expected =
+    4: every batch holds all four streams) produce exactly the tokens of the
+    same steps run directly as one batch per step on a second pool: a row's
+    result does not depend on the other rows or their order."""
+    import threading
+
+    import torch
+    import decoder_model
+
+    path = tmp_path / "mb.gguf"
+    decoder_model.build(path, 16)
+    cfg = dict(n_layers=2, n_blocks=64, capacity=512, max_streams=4, max_rows=64, max_position=1024, dtype=1)
+    g = vxk.Gguf(path)
+    pools = [vxk.Pool(**cfg), vxk.Pool(**cfg)]
+    decs = [vxk.Decoder(g, p, audio_capacity=32, enc_capacity=0) for p in pools]
+    g.close()
+    n, steps = 4, 6
+    first = [11, 222, 333, 1444]
+    cs = torch.cuda.current_stream().cuda_stream
+    # direct: one batch per step
+    ids = [pools[1].open_stream() for _ in range(n)]
+    amax = torch.zeros(n, dtype=torch.int32, device="cuda")
+    toks = list(first)
+    direct = {s: [] for s in range(n)}
+    for i in range(steps):
+        pools[1].plan(ids, [1] * n, cs)
+        decs[1].forward(toks, [i % 32] * n, amax.data_ptr(), 0, 0, cs)
+        decs[1].sync(cs)
+        pools[1].commit()
+        toks = [int(t) for t in amax.cpu().tolist()]
+        for s in range(n):
+            direct[s].append(toks[s])
+    # through the batcher, one thread per context
+    sids = [pools[0].open_stream() for _ in range(n)]
+    side = torch.cuda.Stream()
+    b = vxk.Batcher(decoder=decs[0], pool=pools[0], cuda_stream=side.cuda_stream, max_rows=4, max_wait_us=200000,
+                    expected=4, timeout_ms=60000)
+    got, errors = {s: [] for s in range(n)}, []
+
+    def ctx(s):
+        try:
+            tok = first[s]
+            for i in range(steps):
+                tok = b.step(sids[s], tok, i % 32)
+                got[s].append(tok)
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+    ts = [threading.Thread(target=ctx, args=(s,)) for s in range(n)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(120)
+    assert not errors, errors
+    st = b.stats()
+    b.close()
+    assert st["batches"] == steps and st["rows"] == n * steps
+    assert got == direct
+    for d in decs:
+        d.close()
+    for p in pools:
+        p.close()

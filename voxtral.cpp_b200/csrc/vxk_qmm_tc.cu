@@ -52,7 +52,7 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kRawBytes = kQtcRecordBytesQ6K;                      // ring stage: the larger record
 constexpr int kActB = kMaxN * 512;                                  // f16 B tile, 4 SW128 atoms
 constexpr int kActBMin = kMaxN * 128;                               // mins B tile (32 B used per row)
-constexpr int kActStage = kActB + kActBMin + 1024;                  // + dx (N floats), padded
+constexpr int kActStage = kActB + kActBMin;
 constexpr int kAMin = 128 * 128;                                    // mins A tile
 constexpr int kOffRaw = 0;
 constexpr int kOffAct = kOffRaw + kRawStages * kRawBytes;
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         }
         for (int s = 0; s < kActStages; ++s) {
             mbar_init(&bars[kBarActFull + s], 1);
-            mbar_init(&bars[kBarActEmpty + s], 1 + 128);   // MMA commit + epilogue threads
+            mbar_init(&bars[kBarActEmpty + s], 1);         // MMA commit
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars[kBarAFull + b], 128);
@@ -539,19 +539,22 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         const uint32_t lane_off = (uint32_t) (32 * q) << 16;
         const uint32_t * dd = reinterpret_cast<const uint32_t *>(m.dd) + ((int64_t) blk * p.n_units + u0) * 128 + r;
         uint32_t ddn = nu > 0 ? __ldg(dd) : 0u;
+        // d_x of each unit straight from global memory (written by the
+        // quantization kernel: wait for it), so an activation stage is free
+        // as soon as its MMAs complete
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         float acc[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) acc[j] = 0.0f;
         for (int i = 0; i < nu; ++i) {
-            const int b = i & 1, t = i % kActStages;
+            const int b = i & 1;
             const uint32_t ddc = ddn;
             if (i + 1 < nu) ddn = __ldg(dd + (int64_t) (i + 1) * 128);
-            bool ok = tc_wait(&bars[kBarDFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error);
-            ok = ok && tc_wait(&bars[kBarActFull + t], (uint32_t) (i / kActStages) & 1u, abort_flag, p.error);
+            const bool ok = tc_wait(&bars[kBarDFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error);
             if (!__all_sync(kFull, ok)) break;
             tc_fence_after();
             const float2 dw = __half22float2(*reinterpret_cast<const __half2 *>(&ddc));  // (d, dmin)
-            const float * dx = reinterpret_cast<const float *>(base + kOffAct + t * kActStage + kActB + kActBMin);
+            const float * dx = p.dx + (int64_t) (u0 + i) * N;
             if (m.type == 14) {
                 // Q6_K: acc += (d_w * d_x) * D
 #pragma unroll
@@ -593,7 +596,6 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarDEmpty + b]);
-            mbar_arrive(&bars[kBarActEmpty + t]);
         }
         // Partial block into the raw ring: every raw read of this CTA happened
         // before the last unit's MMAs, which this thread has waited for.
@@ -631,10 +633,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 if (!tc_wait(&bars[kBarActEmpty + t], ((uint32_t) (i / kActStages) & 1u) ^ 1u, abort_flag, p.error))
                     break;
                 uint8_t * st = base + kOffAct + t * kActStage;
-                mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 128 + N * 4));
+                mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 128));
                 bulk_g2s(st, p.b_tiles + (int64_t) u * N * 512, N * 512, &bars[kBarActFull + t], pol);
                 bulk_g2s(st + kActB, p.bmin_tiles + (int64_t) u * N * 128, N * 128, &bars[kBarActFull + t], pol);
-                bulk_g2s(st + kActB + kActBMin, p.dx + (int64_t) u * N, N * 4, &bars[kBarActFull + t], pol);
             }
             if (*abort_flag)
                 for (int d = i > kActStages ? i - kActStages : 0; d < i; ++d)

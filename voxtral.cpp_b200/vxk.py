@@ -110,6 +110,19 @@ class DecoderInfo(C.Structure):
                                          "audio_capacity", "enc_capacity", "enc_dim")] + [("device_bytes", C.c_int64)]
 
 
+class BatcherConfig(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("max_rows", C.c_int32),
+                ("max_wait_us", C.c_int32), ("expected", C.c_int32), ("timeout_ms", C.c_int32)]
+
+
+class BatcherStats(C.Structure):
+    _fields_ = [("batches", C.c_int64), ("rows", C.c_int64), ("max_rows_seen", C.c_int64),
+                ("failed_batches", C.c_int64), ("timeouts", C.c_int64), ("mean_wait_us", C.c_double)]
+
+
+BATCH_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                       C.POINTER(C.c_int32), C.POINTER(C.c_int32))
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -205,6 +218,12 @@ SIGNATURES = {
     "vxk_decoder_adapt": (_I32, [_P, _I32, _I32P, _I64P, _I64P, _P]),
     "vxk_decoder_read_audio": (_I32, [_P, _I32, _I64, _I32, _P, _P]),
     "vxk_decoder_sync": (_I32, [_P, _P, _I32]),
+    "vxk_batcher_default_config": (BatcherConfig, []),
+    "vxk_batcher_create": (_I32, [C.POINTER(BatcherConfig), BATCH_FN, _P, C.POINTER(C.c_void_p)]),
+    "vxk_batcher_create_for_decoder": (_I32, [C.POINTER(BatcherConfig), _P, _P, _P, C.POINTER(C.c_void_p)]),
+    "vxk_batcher_destroy": (None, [_P]),
+    "vxk_batcher_step": (_I32, [_P, _I32, _I32, _I32, _I32P]),
+    "vxk_batcher_get_stats": (_I32, [_P, C.POINTER(BatcherStats)]),
 }
 
 _lib = None
@@ -756,4 +775,63 @@ class Decoder:
 
     def sync(self, cuda_stream: int = 0, timeout_ms: int = 10000):
         self._check(self.lib.vxk_decoder_sync(self.h, cuda_stream or None, timeout_ms))
+
+
+class Batcher:
+    """Owns one vxk_batcher.  `fn(streams, tokens, audio_slots) -> (status,
+    out_tokens)` runs a batch on the dispatcher thread (a host executor), or
+    pass decoder= / pool= for the built-in decoder executor."""
+
+    def __init__(self, fn=None, decoder=None, pool=None, cuda_stream=0, **cfg):
+        self.lib = load()
+        c = self.lib.vxk_batcher_default_config()
+        for k, v in cfg.items():
+            if not hasattr(c, k):
+                raise AttributeError(k)
+            setattr(c, k, v)
+        self.config = c
+        h = C.c_void_p()
+        if fn is not None:
+            def tramp(user, n, streams, tokens, slots, outs):
+                try:
+                    st, res = fn([streams[i] for i in range(n)], [tokens[i] for i in range(n)],
+                                 [slots[i] for i in range(n)])
+                    for i, v in enumerate(res):
+                        outs[i] = int(v)
+                    return int(st)
+                except Exception:
+                    return 10
+            self._cb = BATCH_FN(tramp)  # kept alive with the batcher
+            st = self.lib.vxk_batcher_create(C.byref(c), self._cb, None, C.byref(h))
+        else:
+            st = self.lib.vxk_batcher_create_for_decoder(C.byref(c), decoder.h, pool.h, cuda_stream or None,
+                                                         C.byref(h))
+        if st != OK:
+            raise VxkError(st, "vxk_batcher_create failed")
+        self.h = h
+
+    def step(self, stream: int, token: int, audio_slot: int) -> int:
+        out = C.c_int32(-1)
+        st = self.lib.vxk_batcher_step(self.h, stream, token, audio_slot, C.byref(out))
+        if st != OK:
+            raise VxkError(st, "vxk_batcher_step failed")
+        return out.value
+
+    def stats(self) -> dict:
+        s = BatcherStats()
+        st = self.lib.vxk_batcher_get_stats(self.h, C.byref(s))
+        if st != OK:
+            raise VxkError(st, "vxk_batcher_get_stats failed")
+        return {n: getattr(s, n) for n, _ in BatcherStats._fields_}
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_batcher_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 

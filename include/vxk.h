@@ -685,6 +685,57 @@ VXK_API vxk_status vxk_decoder_read_audio(vxk_decoder * d, int32_t stream, int64
 VXK_API vxk_status vxk_decoder_sync(vxk_decoder * d, void * cuda_stream, int32_t timeout_ms);
 
 /* ======================================================================== */
+/* Streaming encoder stack                                                   */
+/* ======================================================================== */
+
+/**
+ * The realtime model's encoder loaded from a GGUF file onto an encoder pool's
+ * device (tensors enc.conv0/1.*, enc.blk.N.*, enc.norm.weight; keys
+ * voxtral.encoder.*, src/voxtral.cpp:1085-1095, 1190-1222).  One forward runs
+ * build_encoder_steady_graph (src/voxtral.cpp:2386-2511) for the pool's planned
+ * batch of many streams: the causal conv stem over each stream's Mel window,
+ * then every layer (RMS norm, q/k/v with q and v biases, vxk_enc_layer's RoPE +
+ * ring append + windowed attention, o with bias + residual, RMS norm, SwiGLU
+ * FFN with the w2 bias + residual) and the final norm.  Projection and FFN
+ * matrices must be Q8_0, Q4_K or Q6_K; conv weights, norms and biases F32,
+ * F16 or BF16.  The offline LayerNorm encoder is refused.  Not thread-safe.
+ */
+typedef struct vxk_encoder vxk_encoder;
+
+typedef struct vxk_encoder_info {
+    int32_t n_layers, dim, hidden, n_heads, head_dim, n_mel, max_rows;
+    int32_t reserved;
+    int64_t device_bytes;
+} vxk_encoder_info;
+
+/** max_rows: rows of one forward (0: max_streams x 4, the steady step). */
+VXK_API vxk_status vxk_encoder_create(const vxk_gguf * g, vxk_enc_pool * pool, int32_t max_rows,
+                                      vxk_encoder ** out);
+VXK_API void vxk_encoder_destroy(vxk_encoder * e);
+/** Last error of e, or of the last failed vxk_encoder_create when e is NULL. */
+VXK_API vxk_status vxk_encoder_last_error(const vxk_encoder * e, char * buf, size_t capacity);
+VXK_API vxk_status vxk_encoder_get_info(const vxk_encoder * e, vxk_encoder_info * out);
+
+/**
+ * One forward over the encoder pool's planned batch (vxk_enc_batch_plan: n new
+ * frames per stream at q_start).  mel (device): for each planned stream in
+ * plan order its Mel window [n_mel][2 n + 4] fp32, channel-major, frames
+ * 2 (q_start - 2) .. 2 (q_start + n) - 1 with zeros before frame 0 (the
+ * reference's conv_cm, src/voxtral.cpp:4072-4101).  out (device): [rows][dim]
+ * fp32, the final-normed encoder frames q_start .. q_start + n - 1 of each
+ * stream, which vxk_decoder_write_enc stores for the adapter.  The rings are
+ * appended; the caller commits (vxk_enc_batch_commit) after vxk_encoder_sync.
+ */
+VXK_API vxk_status vxk_encoder_forward(vxk_encoder * e, const float * mel, float * out, void * cuda_stream);
+/** The conv stem alone for the planned batch (same arguments as
+ *  vxk_encoder_forward): out [rows][dim] = gelu(conv1(gelu(conv0(mel)))) at
+ *  each stream's new frames, before the first layer.  Touches no ring. */
+VXK_API vxk_status vxk_encoder_stem(vxk_encoder * e, const float * mel, float * out, void * cuda_stream);
+/** Bounded wait for cuda_stream, then the encoder pool's and the products'
+ *  device error words. */
+VXK_API vxk_status vxk_encoder_sync(vxk_encoder * e, void * cuda_stream, int32_t timeout_ms);
+
+/* ======================================================================== */
 /* Cross-context batcher                                                     */
 /* ======================================================================== */
 

@@ -261,3 +261,91 @@ class Decoder:
         x = np.asarray(enc_rows, np.float32).reshape(enc_rows.shape[0], -1)
         h = gelu_erf_exact(qproduct(self.t["adapter.0.weight"], x))
         return qproduct(self.t["adapter.2.weight"], h)
+
+
+def conv1d_causal_f16(x: np.ndarray, w: Tensor, b: np.ndarray, stride: int, pad_left: int, outputs) -> np.ndarray:
+    """ggml_conv_1d after ggml_pad_ext (causal_conv1d_graph, src/voxtral.cpp:1767-1814)
+    at the output positions `outputs`: im2col rounds x to f16 and the f16 dot
+    product takes the weights as f16; sums in fp64, then + bias in fp32.
+    x [in_ch][len] fp32, w: Tensor of ne [3, in, out] (rows = out, data [out][in][3])."""
+    xin = np.asarray(x, np.float32).astype(np.float16).astype(np.float64)
+    in_ch, length = xin.shape
+    wf = np.asarray(w.data).reshape(-1, in_ch, 3).astype(np.float32).astype(np.float16).astype(np.float64)
+    out = np.empty((len(outputs), wf.shape[0]), np.float32)
+    for n, t in enumerate(outputs):
+        cols = np.zeros((in_ch, 3))
+        for k in range(3):
+            j = stride * t + k - pad_left
+            if 0 <= j < length:
+                cols[:, k] = xin[:, j]
+        out[n] = (np.einsum("oik,ik->o", wf, cols).astype(np.float32) + np.asarray(b, np.float32))
+    return out
+
+
+class Encoder:
+    """The reference streaming encoder stack (build_encoder_steady_graph,
+    src/voxtral.cpp:2386-2511) over host tensors: conv stem, layers with
+    biases and RMS norms, final norm.  attention: None for the fp64
+    restatement (vx_oracle.attn_row over the window), or an object like
+    Decoder's that supplies each layer's attention."""
+
+    def __init__(self, tensors: dict, n_layers: int, n_heads: int, head_dim: int = 64, eps: float = 1e-5,
+                 theta: float = 1e6, cache_dtype: int = BF16, window: int = 750, attention=None):
+        self.t, self.L, self.H, self.hd = tensors, n_layers, n_heads, head_dim
+        self.eps, self.theta, self.dtype, self.window = eps, theta, cache_dtype, window
+        self.attention = attention
+        self.dim = tensors["enc.norm.weight"].cols
+        self.hist: dict = {}
+
+    def vec(self, name):
+        return dequant_rows(self.t[name]).reshape(-1)
+
+    def stem(self, mel_window: np.ndarray, n_new: int) -> np.ndarray:
+        win = 2 * n_new + 4
+        assert mel_window.shape[1] == win
+        c0 = conv1d_causal_f16(mel_window, self.t["enc.conv0.weight"], self.vec("enc.conv0.bias"), 1, 2, range(win))
+        y = gelu_erf_exact(c0).T  # [dim][win]
+        c1 = conv1d_causal_f16(y, self.t["enc.conv1.weight"], self.vec("enc.conv1.bias"), 2, 1,
+                               range(2, 2 + n_new))
+        return gelu_erf_exact(c1)
+
+    def forward(self, batch, x0=None):
+        """batch: list of (stream, q_start, n_new, mel_window [n_mel][2 n + 4]).
+        x0: None, or the stem output to start from (rows of dim).  Returns the
+        final-normed rows [sum n_new][dim]."""
+        x = np.concatenate([self.stem(m, n) for _, _, n, m in batch]) if x0 is None else np.asarray(x0, np.float32)
+        rows = [(s, q0 + j) for s, q0, n, _ in batch for j in range(n)]
+        n = len(rows)
+        scale = float(np.float32(1.0 / math.sqrt(self.hd)))
+        if self.attention is not None:
+            self.attention.begin([(s, nn) for s, _, nn, _ in batch])
+        for l in range(self.L):
+            p = f"enc.blk.{l}."
+            xn = rms_norm(x, self.vec(p + "attn_norm.weight"), self.eps)
+
+            def proj(name, inp):
+                y = qproduct(self.t[p + name + ".weight"], inp)
+                if p + name + ".bias" in self.t:
+                    y = y + self.vec(p + name + ".bias")
+                return y
+            q = proj("attn_q", xn).reshape(n, self.H, self.hd)
+            k = proj("attn_k", xn).reshape(n, self.H, self.hd)
+            v = proj("attn_v", xn).reshape(n, self.H, self.hd)
+            for r, (s, pos) in enumerate(rows):
+                self.hist[(s, l, pos)] = vo.kv_row(k[r], v[r], pos, self.theta, self.dtype)
+            if self.attention is not None:
+                att = self.attention.layer(l, q, k, v)
+            else:
+                att = np.empty((n, self.H, self.hd), np.float32)
+                for r, (s, pos) in enumerate(rows):
+                    lo = max(0, pos - self.window + 1)
+                    kk = np.stack([self.hist[(s, l, a)][0] for a in range(lo, pos + 1)])
+                    vv = np.stack([self.hist[(s, l, a)][1] for a in range(lo, pos + 1)])
+                    att[r] = vo.attn_row(q[r], pos, self.theta, kk, vv, self.dtype, self.H, scale)
+            x = x + proj("attn_o", att.reshape(n, -1))
+            h = rms_norm(x, self.vec(p + "ffn_norm.weight"), self.eps)
+            g = silu(qproduct(self.t[p + "ffn_w1.weight"], h)) * qproduct(self.t[p + "ffn_w3.weight"], h)
+            x = x + proj("ffn_w2", g)
+        if self.attention is not None:
+            self.attention.end()
+        return rms_norm(x, self.vec("enc.norm.weight"), self.eps)

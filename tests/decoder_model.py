@@ -86,3 +86,61 @@ def build(path: Path, seed: int, n_layers: int = 2, dim: int = 1024, hidden: int
     w.write_tensors_to_file()
     w.close()
     return t
+
+
+def build_encoder(path: Path, seed: int, n_layers: int = 2, dim: int = 512, n_heads: int = 8, hidden: int = 1024,
+                  n_mel: int = 128, types: dict = Q4_K_M):
+    """A seeded streaming encoder (tensor names and keys of src/voxtral.cpp:1085-1095,
+    1190-1222) written as a GGUF file; returns {name: vd.Tensor}."""
+    import gguf
+
+    rng = np.random.default_rng(seed)
+    qdim = n_heads * 64
+    t: dict[str, vd.Tensor] = {}
+
+    def conv(name, out_ch, in_ch):
+        w = rng.normal(0.0, 1.0 / np.sqrt(3 * in_ch), (out_ch, in_ch, 3)).astype(np.float16)
+        t[name] = vd.Tensor(vd.F16, out_ch, in_ch * 3, w)
+
+    def vec(name, n, lo=-0.1, hi=0.1):
+        t[name] = vd.Tensor(vd.F32, 1, n, rng.uniform(lo, hi, n).astype(np.float32))
+
+    conv("enc.conv0.weight", dim, n_mel)
+    vec("enc.conv0.bias", dim)
+    conv("enc.conv1.weight", dim, dim)
+    vec("enc.conv1.bias", dim)
+    for l in range(n_layers):
+        p = f"enc.blk.{l}."
+        t[p + "attn_q.weight"] = _matrix(rng, types["q"], qdim, dim)
+        t[p + "attn_k.weight"] = _matrix(rng, types["k"], qdim, dim)
+        t[p + "attn_v.weight"] = _matrix(rng, types["v"], qdim, dim)
+        t[p + "attn_o.weight"] = _matrix(rng, types["o"], dim, qdim)
+        t[p + "ffn_w1.weight"] = _matrix(rng, types["w1"], hidden, dim)
+        t[p + "ffn_w3.weight"] = _matrix(rng, types["w3"], hidden, dim)
+        t[p + "ffn_w2.weight"] = _matrix(rng, types["w2"], dim, hidden)
+        vec(p + "attn_q.bias", qdim)
+        vec(p + "attn_v.bias", qdim)
+        vec(p + "attn_o.bias", dim)
+        vec(p + "ffn_w2.bias", dim)
+        vec(p + "attn_norm.weight", dim, 0.8, 1.2)
+        vec(p + "ffn_norm.weight", dim, 0.8, 1.2)
+    vec("enc.norm.weight", dim, 0.8, 1.2)
+
+    w = gguf.GGUFWriter(str(path), "voxtral_realtime")
+    for key, val in (("dim", dim), ("n_layers", n_layers), ("n_heads", n_heads), ("head_dim", 64),
+                     ("hidden_dim", hidden), ("n_kv_heads", n_heads)):
+        w.add_int32(f"voxtral.encoder.{key}", val)
+    w.add_float32("voxtral.encoder.norm_eps", 1e-5)
+    w.add_float32("voxtral.encoder.rope_theta", 1e6)
+    gtype = {vd.Q8_0: gguf.GGMLQuantizationType.Q8_0, vd.Q4_K: gguf.GGMLQuantizationType.Q4_K,
+             vd.Q6_K: gguf.GGMLQuantizationType.Q6_K}
+    for name, ten in t.items():
+        if ten.type in gtype:
+            w.add_tensor(name, np.asarray(ten.data, np.uint8).reshape(ten.rows, -1), raw_dtype=gtype[ten.type])
+        else:
+            w.add_tensor(name, np.asarray(ten.data))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return t

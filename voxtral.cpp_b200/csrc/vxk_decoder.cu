@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(kNormThreads) add_norm_kernel(NormParams p) {
     const int n4 = p.dim / 4;
     float4 * x = reinterpret_cast<float4 *>(p.x + (int64_t) r * p.dim);
     const float4 * add = p.add ? reinterpret_cast<const float4 *>(p.add + (int64_t) r * p.dim) : nullptr;
+    const float4 * ab = p.add_bias ? reinterpret_cast<const float4 *>(p.add_bias) : nullptr;
     float4 v[V];
     float4 a[V];
 #pragma unroll
@@ -88,6 +89,19 @@ __global__ void __launch_bounds__(kNormThreads) add_norm_kernel(NormParams p) {
         if (i < n4) {
             v[j] = x[i];
             if (add) a[j] = add[i];
+        }
+    }
+    if (add && ab) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int i = threadIdx.x + j * kNormThreads;
+            if (i < n4) {
+                const float4 bb = ab[i];
+                a[j].x = __fadd_rn(a[j].x, bb.x);
+                a[j].y = __fadd_rn(a[j].y, bb.y);
+                a[j].z = __fadd_rn(a[j].z, bb.z);
+                a[j].w = __fadd_rn(a[j].w, bb.w);
+            }
         }
     }
     double sum = 0.0;

@@ -157,6 +157,31 @@ vxk::EncParams enc_params(vxk_enc_pool * p, int32_t layer, const float * q, cons
 
 }  // namespace
 
+namespace vxk {
+
+bool enc_pool_batch_view(const vxk_enc_pool * pool, EncBatchView * out) {
+    if (!pool || !out || !pool->planned) return false;
+    out->streams.clear();
+    out->n_new.clear();
+    out->q_start.clear();
+    for (const EncPlan & e : pool->plan) {
+        out->streams.push_back(e.stream);
+        out->n_new.push_back(e.plan.n_new);
+        out->q_start.push_back(e.plan.q_start);
+    }
+    out->rows = (int32_t) pool->rows.size();
+    return true;
+}
+
+int32_t * enc_pool_error_word(const vxk_enc_pool * pool) { return pool->d_error; }
+
+EncShape enc_pool_shape(const vxk_enc_pool * pool) {
+    const vxk_enc_config & c = pool->cfg;
+    return EncShape{c.device, c.n_layers, c.n_heads, c.head_dim, c.max_streams, c.max_new, c.rope_theta};
+}
+
+}  // namespace vxk
+
 extern "C" {
 
 vxk_enc_config vxk_enc_default_config(void) {

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -11,6 +12,7 @@
 
 struct vxk_qweight;
 struct vxk_pool;
+struct vxk_enc_pool;
 
 namespace vxk {
 
@@ -402,12 +404,14 @@ struct EmbedParams {
     float * xn;               // [rows][dim]
 };
 
-// x += add (when add != nullptr); out = rms_norm(x) * w, then out + out * ada
+// x += add (when add != nullptr; add + add_bias first when that is set);
+// out = rms_norm(x) * w, then out + out * ada
 // when ada != nullptr.  compact: only rows with out_index >= 0, written to
 // out row out_index.
 struct NormParams {
     float * x;
     const float * add;
+    const float * add_bias;   // nullptr, or [dim]: x += (add + add_bias) (a product with its bias)
     const float * w;
     const float * ada;
     float * out;
@@ -437,5 +441,50 @@ cudaError_t launch_adapter_gather(const float * enc, int32_t enc_cap, int32_t en
 // audio[stream][audio_slot] = y[g] for each group.
 cudaError_t launch_audio_scatter(const float * y, float * audio, int32_t audio_cap, int32_t dim,
                                  const AdaptRow * rows, int32_t n, cudaStream_t stream);
+
+// ---- encoder stack (vxk_encoder_stack.cu, vxk_encoder_model_host.cpp) -------
+
+struct EncBatchView {
+    std::vector<int32_t> streams;   // per planned stream, plan order
+    std::vector<int32_t> n_new;
+    std::vector<int64_t> q_start;
+    int32_t rows = 0;
+};
+struct EncShape {
+    int32_t device, n_layers, n_heads, head_dim, max_streams, max_new;
+    float rope_theta;
+};
+bool enc_pool_batch_view(const vxk_enc_pool * pool, EncBatchView * out);
+EncShape enc_pool_shape(const vxk_enc_pool * pool);
+int32_t * enc_pool_error_word(const vxk_enc_pool * pool);
+
+// One planned stream's conv work: its mel window and output rows.
+struct ConvStream {
+    int32_t mel_offset;   // first float of its [n_mel][win] window in the mel buffer
+    int32_t win;          // 2 n_new + 4 frames
+    int32_t n_new;
+    int32_t row0;         // its first output row
+};
+static_assert(sizeof(ConvStream) == 16, "ConvStream layout");
+
+struct ConvParams {
+    const float * mel;          // concatenated [n_mel][win] windows, channel-major
+    const ConvStream * streams;
+    int32_t n_streams;
+    int32_t n_mel;
+    int32_t dim;
+    int32_t max_win;
+    const __half * w0;          // conv0 weights [n_mel][3][dim] (f16, c fastest)
+    const float * b0;           // [dim]
+    const __half * w1;          // conv1 weights [dim][3][dim]
+    const float * b1;
+    float * y0;                 // [n_streams][max_win][dim] gelu(conv0), fp32
+    float * x;                  // [rows][dim] encoder rows (gelu(conv1) at local 2 .. 2 + n_new - 1)
+};
+
+cudaError_t launch_conv_stem(const ConvParams & p, cudaStream_t stream);
+// y[r][i] += b[i] for rows of n values (ggml_add of a bias), two tensors at once.
+cudaError_t launch_bias2(float * y0, const float * b0, int32_t n0, float * y1, const float * b1, int32_t n1,
+                         int32_t rows, cudaStream_t stream);
 
 }  // namespace vxk

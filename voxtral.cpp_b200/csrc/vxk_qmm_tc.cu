@@ -18,16 +18,20 @@
 // h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
 // d_x*d_w and d_x*dmin_w in fp32.
 //
-// CTA = 128 weight rows x a range of 256-column units; 11 warps:
-//   warps 0-3   dequant: thread = weight row (TMEM lane); per unit it reads the
-//               row's 128 quant bytes and 16 scale/min bytes from the raw
-//               ring, writes 128 columns of f16 pairs sc*q into TMEM
-//               (tcgen05.st) and the row's mins row into shared memory
-//   warps 4-7   epilogue: thread = weight row; tcgen05.ld of the unit's
-//               accumulators, fp32 block factors into registers
-//   warp 8      bulk copies of the raw weight records (HBM stream, evict-first)
-//   warp 9      bulk copies of the quantized activations (L2)
-//   warp 10     tcgen05.mma issuer: 16 MMAs (M = 128, N = rows padded to 16,
+// CTA = 128 weight rows x a range of 256-column units; 19 warps, two per SM
+// sub-partition for each of the per-row roles (a warp reaches only the TMEM
+// lanes of its sub-partition, warp % 4):
+//   warps 0-7   dequant: thread = weight row (TMEM lane), warps w and w + 4
+//               split the unit's columns; per unit they read the row's quant
+//               bytes and scale/min bytes from the raw ring, write f16 pairs
+//               sc*q into TMEM (tcgen05.st) and (warps 0-3) the row's mins row
+//               into shared memory
+//   warps 8-15  epilogue: thread = weight row, warps w and w + 4 split the
+//               activation columns; tcgen05.ld of the unit's accumulators,
+//               fp32 block factors into registers
+//   warp 16     bulk copies of the raw weight records (HBM stream, evict-first)
+//   warp 17     bulk copies of the quantized activations (L2)
+//   warp 18     tcgen05.mma issuer: 16 MMAs (M = 128, N = rows padded to 16,
 //               K = 16, A from TMEM) + 1 mins MMA per unit
 // Column splits of a 128-row block are one thread-block cluster and reduce
 // their partial blocks through distributed shared memory, in split order.
@@ -41,7 +45,10 @@
 namespace vxk {
 namespace {
 
-constexpr int kThreads = 352;
+constexpr int kThreads = 608;
+constexpr int kDqWarps = 8;                     // dequant warps 0-7
+constexpr int kEpWarp0 = 8;                     // epilogue warps 8-15
+constexpr int kRawWarp = 16, kActWarp = 17, kMmaWarp = 18;
 constexpr int kRawStages = 4;
 constexpr int kActStages = 2;
 constexpr int kMaxN = 64;
@@ -354,7 +361,7 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
 // 33+l, 35+l} (l = 16c4 + 4k) of the half, the low (gg = 0) or high nibbles of
 // the quant bytes at l and 32+l and 2-bit fields 4gg and 4gg+2 of the high
 // plane byte at l.  Both parts are exact f16 integers.
-__device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int h, uint32_t abase) {
+__device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int h, int gg, uint32_t abase) {
     const uint8_t * ql = raw + r * 128;
     const uint8_t * qh = raw + 16384 + r * 64;
     uint4 A[2], B[2], H[2];
@@ -367,38 +374,37 @@ __device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int 
     const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
     const __half2 c1056 = __float2half2_rn(1056.0f);
+    // part 0: A_hi = 16*(sc>>4)*q at abase + 32 gg; part 1: A_lo = (sc&15)*q at abase + 64 + 32 gg
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg) {
-        uint32_t hi[32], lo[32];
+    for (int part = 0; part < 2; ++part) {
+        uint32_t out[32];
 #pragma unroll
         for (int c4 = 0; c4 < 2; ++c4) {
-            const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two parts
+            const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two quant bytes
             const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
             const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
-            const __half2 fah = __float2half2_rn((float) (16 * (sa >> 4))), fal = __float2half2_rn((float) (sa & 15));
-            const __half2 fbh = __float2half2_rn((float) (16 * (sb >> 4))), fbl = __float2half2_rn((float) (sb & 15));
+            const __half2 fa = __float2half2_rn(part == 0 ? (float) (16 * (sa >> 4)) : (float) (sa & 15));
+            const __half2 fb = __float2half2_rn(part == 0 ? (float) (16 * (sb >> 4)) : (float) (sb & 15));
             const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
             const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
             const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int ns = 4 * gg, fa = 4 * gg, fb = 4 * gg + 2;
+                const int ns = 4 * gg, fpa = 4 * gg, fpb = 4 * gg + 2;
                 uint32_t pv[4];
-                pv[0] = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fa) & 0x00030003u) << 4) | 0x64006400u;
-                pv[1] = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fb) & 0x00030003u) << 4) | 0x64006400u;
-                pv[2] = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fa + 8)) & 0x00030003u) << 4) | 0x64006400u;
-                pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4) | 0x64006400u;
+                pv[0] = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fpa) & 0x00030003u) << 4) | 0x64006400u;
+                pv[1] = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fpb) & 0x00030003u) << 4) | 0x64006400u;
+                pv[2] = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fpa + 8)) & 0x00030003u) << 4) | 0x64006400u;
+                pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fpb + 8)) & 0x00030003u) << 4) | 0x64006400u;
 #pragma unroll
                 for (int x = 0; x < 4; ++x) {
                     const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&pv[x]), c1056);
-                    const bool pa = (x & 1) == 0;  // pv[0], pv[2] from the bytes at l, pv[1], pv[3] at 32+l
-                    hi[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fah : fbh));
-                    lo[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fal : fbl));
+                    // pv[0], pv[2] come from the bytes at l, pv[1], pv[3] from the bytes at 32 + l
+                    out[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, (x & 1) == 0 ? fa : fb));
                 }
             }
         }
-        tmem_st32(abase + 32 * gg, hi);
-        tmem_st32(abase + 64 + 32 * gg, lo);
+        tmem_st32(abase + 64 * part + 32 * gg, out);
     }
 }
 
@@ -427,17 +433,17 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     if (tid == 0) {
         for (int s = 0; s < kRawStages; ++s) {
             mbar_init(&bars[kBarRawFull + s], 1);
-            mbar_init(&bars[kBarRawEmpty + s], 128);
+            mbar_init(&bars[kBarRawEmpty + s], 32 * kDqWarps);
         }
         for (int s = 0; s < kActStages; ++s) {
             mbar_init(&bars[kBarActFull + s], 1);
             mbar_init(&bars[kBarActEmpty + s], 1);         // MMA commit
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&bars[kBarAFull + b], 128);
+            mbar_init(&bars[kBarAFull + b], 32 * kDqWarps);
             mbar_init(&bars[kBarAEmpty + b], 1);
             mbar_init(&bars[kBarDFull + b], 1);
-            mbar_init(&bars[kBarDEmpty + b], 128);
+            mbar_init(&bars[kBarDEmpty + b], 128 * (N >= 32 ? 2 : 1));  // epilogue warps with columns
         }
         mbar_init(&bars[kBarDrain], 1);
         *abort_flag = 0;
@@ -455,10 +461,11 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     const uint32_t tmem = *tmem_slot;
     float * ptile = reinterpret_cast<float *>(base + kOffRaw);  // [N][128] partial block at the end
 
-    if (warp < 4) {
-        // ---------------- dequant: row r = 32 warp + lane ----------------
-        const int r = 32 * warp + lane;
-        const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
+    if (warp < kDqWarps) {
+        // ---------------- dequant: row r = 32 (warp % 4) + lane, column half warp / 4 ----------------
+        const int qd = warp & 3, hs = warp >> 2;
+        const int r = 32 * qd + lane;
+        const uint32_t lane_off = (uint32_t) (32 * qd) << 16;
         const bool q6 = m.type == 14;
         const int phases = q6 ? 2 : 1;  // A buffers filled per unit (Q6_K: two halves)
         int j = 0;                      // A-phase counter: buffer j & 1, use j >> 1
@@ -478,14 +485,16 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 }
                 tc_fence_after();
                 if (q6) {
-                    dequant_q6_half(raw, r, h, tmem + 128 * b + lane_off);
+                    dequant_q6_half(raw, r, h, hs, tmem + 128 * b + lane_off);
                 } else {
                     const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
                     const uint32_t scw[2] = {scm.x, scm.y};
                     const uint32_t mnw[2] = {scm.z, scm.w};
-                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word)
+                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word);
+                    // this warp: chunks 4 hs .. 4 hs + 3 (TMEM columns 64 hs .. 64 hs + 63)
 #pragma unroll
-                    for (int half = 0; half < 4; ++half) {
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int half = 2 * hs + hh;
                         uint32_t cols[32];
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
@@ -513,6 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
                     }
                     // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact)
+                    if (hs == 0) {
                     uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 1024 + (r & 7) * 128;
                     uint32_t m0[4], m1[4];
 #pragma unroll
@@ -524,6 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     }
                     *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
                     *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
+                    }
                 }
                 if (h == phases - 1) mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -532,20 +543,23 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 mbar_arrive(&bars[kBarAFull + b]);
             }
         }
-    } else if (warp < 8) {
-        // ---------------- epilogue: row r = 32 (warp - 4) + lane ----------------
-        const int q = warp & 3;
+    } else if (warp < kEpWarp0 + 8) {
+        // ---------------- epilogue: row r = 32 (warp % 4) + lane, columns ch * NC .. ----------------
+        constexpr int EPC = N >= 32 ? 2 : 1;  // column groups (tcgen05.ld moves 16 columns)
+        constexpr int NC = N / EPC;
+        const int q = warp & 3, ch = (warp - kEpWarp0) >> 2;
         const int r = 32 * q + lane;
         const uint32_t lane_off = (uint32_t) (32 * q) << 16;
+        if (ch < EPC) {
         const uint32_t * dd = reinterpret_cast<const uint32_t *>(m.dd) + ((int64_t) blk * p.n_units + u0) * 128 + r;
         uint32_t ddn = nu > 0 ? __ldg(dd) : 0u;
         // d_x of each unit straight from global memory (written by the
         // quantization kernel: wait for it), so an activation stage is free
         // as soon as its MMAs complete
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        float acc[N];
+        float acc[NC];
 #pragma unroll
-        for (int j = 0; j < N; ++j) acc[j] = 0.0f;
+        for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
         for (int i = 0; i < nu; ++i) {
             const int b = i & 1;
             const uint32_t ddc = ddn;
@@ -554,45 +568,34 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             if (!__all_sync(kFull, ok)) break;
             tc_fence_after();
             const float2 dw = __half22float2(*reinterpret_cast<const __half2 *>(&ddc));  // (d, dmin)
-            const float * dx = p.dx + (int64_t) (u0 + i) * N;
+            const float * dx = p.dx + (int64_t) (u0 + i) * N + ch * NC;
+            const uint32_t dcol = tmem + 256 + 64 * b + ch * NC + lane_off;
             if (m.type == 14) {
                 // Q6_K: acc += (d_w * d_x) * D
 #pragma unroll
-                for (int c0 = 0; c0 < N; c0 += 32) {
-                    constexpr int W = N < 32 ? N : 32;
-                    uint32_t v[2][16];
-#pragma unroll
-                    for (int hh = 0; hh < W / 16; ++hh) tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * hh + lane_off, v[hh]);
+                for (int c0 = 0; c0 < NC; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16_nowait(dcol + c0, v);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int hh = 0; hh < W / 16; ++hh)
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj)
-                            acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dx[c0 + 16 * hh + jj]),
-                                                          __uint_as_float(v[hh][jj]), acc[c0 + 16 * hh + jj]);
+                    for (int jj = 0; jj < 16; ++jj)
+                        acc[c0 + jj] = fmaf(__fmul_rn(dw.x, dx[c0 + jj]), __uint_as_float(v[jj]), acc[c0 + jj]);
                 }
             } else {
-                // Q4_K: 32 columns of D and of Dmin in flight per wait
+                // Q4_K: 16 columns of D and of Dmin in flight per wait
 #pragma unroll
-                for (int c0 = 0; c0 < N; c0 += 32) {
-                constexpr int W = N < 32 ? N : 32;
-                uint32_t v[2][16], mm[2][16];
-#pragma unroll
-                for (int h = 0; h < W / 16; ++h) {
-                    tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * h + lane_off, v[h]);
-                    tmem_ld16_nowait(tmem + 384 + 64 * b + c0 + 16 * h + lane_off, mm[h]);
-                }
-                tmem_ld_wait();
-#pragma unroll
-                for (int h = 0; h < W / 16; ++h)
+                for (int c0 = 0; c0 < NC; c0 += 16) {
+                    uint32_t v[16], mm[16];
+                    tmem_ld16_nowait(dcol + c0, v);
+                    tmem_ld16_nowait(dcol + 128 + c0, mm);
+                    tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float x = dx[c0 + 16 * h + j];
-                        acc[c0 + 16 * h + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[h][j]),
-                                                    fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[h][j]),
-                                                         acc[c0 + 16 * h + j]));
+                        const float x = dx[c0 + j];
+                        acc[c0 + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[j]),
+                                           fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[j]), acc[c0 + j]));
                     }
-            }
+                }
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarDEmpty + b]);
@@ -601,9 +604,10 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         // before the last unit's MMAs, which this thread has waited for.
         if (!*abort_flag) {
 #pragma unroll
-            for (int j = 0; j < N; ++j) ptile[j * 128 + r] = acc[j];
+            for (int j = 0; j < NC; ++j) ptile[(ch * NC + j) * 128 + r] = acc[j];
         }
-    } else if (warp == 8) {
+        }
+    } else if (warp == kRawWarp) {
         // ---------------- raw weight records (HBM) ----------------
         if (lane == 0) {
             const uint64_t pol = l2_policy(true);
@@ -622,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     tc_drain(&bars[kBarRawFull + d % kRawStages], (uint32_t) (d / kRawStages) & 1u);
         }
         __syncwarp();
-    } else if (warp == 9) {
+    } else if (warp == kActWarp) {
         // ---------------- quantized activations (L2), after the producer kernel ----------------
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0) {

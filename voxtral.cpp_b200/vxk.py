@@ -110,6 +110,11 @@ class DecoderInfo(C.Structure):
                                          "audio_capacity", "enc_capacity", "enc_dim")] + [("device_bytes", C.c_int64)]
 
 
+class EncoderInfo(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("n_layers", "dim", "hidden", "n_heads", "head_dim", "n_mel", "max_rows",
+                                         "reserved")] + [("device_bytes", C.c_int64)]
+
+
 class BatcherConfig(C.Structure):
     _fields_ = [("struct_size", C.c_uint32), ("api_version", C.c_uint32), ("max_rows", C.c_int32),
                 ("max_wait_us", C.c_int32), ("expected", C.c_int32), ("timeout_ms", C.c_int32)]
@@ -218,6 +223,13 @@ SIGNATURES = {
     "vxk_decoder_adapt": (_I32, [_P, _I32, _I32P, _I64P, _I64P, _P]),
     "vxk_decoder_read_audio": (_I32, [_P, _I32, _I64, _I32, _P, _P]),
     "vxk_decoder_sync": (_I32, [_P, _P, _I32]),
+    "vxk_encoder_create": (_I32, [_P, _P, _I32, C.POINTER(C.c_void_p)]),
+    "vxk_encoder_destroy": (None, [_P]),
+    "vxk_encoder_last_error": (_I32, [_P, C.c_char_p, C.c_size_t]),
+    "vxk_encoder_get_info": (_I32, [_P, C.POINTER(EncoderInfo)]),
+    "vxk_encoder_forward": (_I32, [_P, _P, _P, _P]),
+    "vxk_encoder_stem": (_I32, [_P, _P, _P, _P]),
+    "vxk_encoder_sync": (_I32, [_P, _P, _I32]),
     "vxk_batcher_default_config": (BatcherConfig, []),
     "vxk_batcher_create": (_I32, [C.POINTER(BatcherConfig), BATCH_FN, _P, C.POINTER(C.c_void_p)]),
     "vxk_batcher_create_for_decoder": (_I32, [C.POINTER(BatcherConfig), _P, _P, _P, C.POINTER(C.c_void_p)]),
@@ -827,6 +839,51 @@ class Batcher:
     def close(self):
         if getattr(self, "h", None):
             self.lib.vxk_batcher_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Encoder:
+    """Owns one vxk_encoder: a GGUF model's streaming encoder stack on an
+    encoder pool's device, run over the pool's planned batch."""
+
+    def __init__(self, gguf: "Gguf", pool: "EncPool", max_rows: int = 0):
+        self.lib = load()
+        h = C.c_void_p()
+        st = self.lib.vxk_encoder_create(gguf.h, pool.h, max_rows, C.byref(h))
+        if st != OK:
+            raise VxkError(st, self._error(None))
+        self.h = h
+        info = EncoderInfo()
+        self._check(self.lib.vxk_encoder_get_info(self.h, C.byref(info)))
+        self.info = {n: getattr(info, n) for n, _ in EncoderInfo._fields_}
+
+    def _error(self, h) -> str:
+        buf = C.create_string_buffer(1024)
+        self.lib.vxk_encoder_last_error(h, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st: int):
+        if st != OK:
+            raise VxkError(st, self._error(self.h))
+
+    def forward(self, mel_ptr: int, out_ptr: int, cuda_stream: int = 0):
+        self._check(self.lib.vxk_encoder_forward(self.h, mel_ptr, out_ptr, cuda_stream or None))
+
+    def stem(self, mel_ptr: int, out_ptr: int, cuda_stream: int = 0):
+        self._check(self.lib.vxk_encoder_stem(self.h, mel_ptr, out_ptr, cuda_stream or None))
+
+    def sync(self, cuda_stream: int = 0, timeout_ms: int = 10000):
+        self._check(self.lib.vxk_encoder_sync(self.h, cuda_stream or None, timeout_ms))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.vxk_encoder_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -60,6 +60,11 @@ CONFIGS = {
                          "attn_q/k/o, ffn_w1/w3 Q4_K; attn_v, ffn_w2, tok_embeddings Q6_K) for 64 streams/GPU, "
                          "ctx~U[400,4096] f16 16-token pages: embeddings + audio, norms, time scale, projections, "
                          "attention, SwiGLU FFN, logits + argmax"),
+    "encstack": dict(kind="encstack", layers=32, streams=128, heads=20, rows=4, window=750, capacity=878, dtype=30,
+                     dim=1280, hidden=5120,
+                     desc="whole streaming encoder step (conv stem, 32 layers: RMS norms, q/k/v/o with biases, "
+                          "RoPE + ring append + 750-frame window attention, SwiGLU FFN; final norm) for 128 "
+                          "streams x 4 new frames, 20 heads x 64, d_model 1280, FFN 5120, Q4_K_M weights, bf16 rings"),
     "4": dict(kind="encoder", layers=32, streams=128, heads=20, rows=4, window=750, capacity=878, dtype=30,
               desc="streaming encoder, 128 streams, 20 heads x 64, 4 new rows per 80 ms chunk, "
                    "750-frame window in an 878-slot bf16 ring (steady state, rings wrapped)"),
@@ -709,6 +714,186 @@ def write_decoder_gguf(path, cfg, seed):
     return tensors
 
 
+def write_encoder_gguf(path, cfg, seed):
+    """A seeded Q4_K_M-typed streaming encoder with the reference's tensor names
+    and keys (src/voxtral.cpp:1085-1095, 1190-1222), written with the gguf package."""
+    import gguf
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    rng = np.random.default_rng(seed)
+    L, D, H, F = cfg["layers"], cfg["dim"], cfg["heads"], cfg["hidden"]
+    qd = H * 64
+    q4, q6 = gguf.GGMLQuantizationType.Q4_K, gguf.GGMLQuantizationType.Q6_K
+    w = gguf.GGUFWriter(str(path), "voxtral_realtime")
+    for k, v in (("dim", D), ("n_layers", L), ("n_heads", H), ("head_dim", 64), ("hidden_dim", F), ("n_kv_heads", H)):
+        w.add_int32(f"voxtral.encoder.{k}", v)
+    w.add_float32("voxtral.encoder.norm_eps", 1e-5)
+    w.add_float32("voxtral.encoder.rope_theta", 1e6)
+
+    def mat(name, t, gt, rows, cols):
+        w.add_tensor(name, vx_oracle.random_qblocks(t, rows, cols, rng, zero_mean=True), raw_dtype=gt)
+
+    def vec(name, n, lo, hi):
+        w.add_tensor(name, rng.uniform(lo, hi, n).astype(np.float32))
+
+    w.add_tensor("enc.conv0.weight", rng.normal(0, 1 / np.sqrt(384), (D, 128, 3)).astype(np.float16))
+    vec("enc.conv0.bias", D, -0.1, 0.1)
+    w.add_tensor("enc.conv1.weight", rng.normal(0, 1 / np.sqrt(3 * D), (D, D, 3)).astype(np.float16))
+    vec("enc.conv1.bias", D, -0.1, 0.1)
+    for l in range(L):
+        p = f"enc.blk.{l}."
+        mat(p + "attn_q.weight", 12, q4, qd, D)
+        mat(p + "attn_k.weight", 12, q4, qd, D)
+        mat(p + "attn_v.weight", 14, q6, qd, D)
+        mat(p + "attn_o.weight", 12, q4, D, qd)
+        mat(p + "ffn_w1.weight", 12, q4, F, D)
+        mat(p + "ffn_w3.weight", 12, q4, F, D)
+        mat(p + "ffn_w2.weight", 14, q6, D, F)
+        vec(p + "attn_q.bias", qd, -0.1, 0.1)
+        vec(p + "attn_v.bias", qd, -0.1, 0.1)
+        vec(p + "attn_o.bias", D, -0.1, 0.1)
+        vec(p + "ffn_w2.bias", D, -0.1, 0.1)
+        vec(p + "attn_norm.weight", D, 0.8, 1.2)
+        vec(p + "ffn_norm.weight", D, 0.8, 1.2)
+    vec("enc.norm.weight", D, 0.8, 1.2)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+def encoder_weight_bytes(cfg):
+    L, D, F, qd = cfg["layers"], cfg["dim"], cfg["hidden"], cfg["heads"] * 64
+    q4 = lambda n, k: n * (k // 256) * 144  # noqa: E731
+    q6 = lambda n, k: n * (k // 256) * 210  # noqa: E731
+    return L * (2 * q4(qd, D) + q6(qd, D) + q4(D, qd) + 2 * q4(F, D) + q6(D, F)) + 2 * (128 * 3 * D + 3 * D * D)
+
+
+def run_encstack(args, cfg, world, rank, local, dist, torch, vxk):
+    """Whole streaming encoder step: one 80 ms chunk (4 new frames) of every
+    stream through the conv stem, all layers and the final norm
+    (vxk_encoder_forward), rings prefilled so every window holds 750 frames."""
+    import tempfile
+
+    L, S, H, P, W, CAP = cfg["layers"], cfg["streams"], cfg["heads"], cfg["rows"], cfg["window"], cfg["capacity"]
+    tmpdir = tempfile.mkdtemp(prefix="vxk_bench_")
+    path = Path(tmpdir) / f"encoder_{rank}.gguf"
+    write_encoder_gguf(path, cfg, args.seed)
+    pool = vxk.EncPool(device=local, n_layers=L, n_heads=H, head_dim=64, window=W, capacity=CAP, max_streams=S,
+                       max_new=CAP - W, dtype=cfg["dtype"], max_position=65536)
+    g = vxk.Gguf(path)
+    enc = vxk.Encoder(g, pool, max_rows=S * P)
+    g.close()
+    os.unlink(path)
+    os.rmdir(tmpdir)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    streams = [pool.open_stream() for _ in range(S)]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed + rank)
+    fill = CAP - W
+    fq = torch.randn((S * fill, H, 64), device="cuda", generator=gen) * 0.5
+    fo = torch.empty_like(fq)
+    pos = 0
+    while pos < CAP + 128:  # wrap every ring so each chunk sees a full 750-frame window
+        pool.plan(streams, [fill] * S, sh)
+        for layer in range(L):
+            pool.layer(layer, fq.data_ptr(), fq.data_ptr(), fq.data_ptr(), fo.data_ptr(), sh)
+        pool.commit()
+        pos += fill
+    torch.cuda.synchronize()
+    del fq, fo
+    mel = torch.randn((S, 128, 2 * P + 4), device="cuda", generator=gen)
+    out = torch.empty((S * P, cfg["dim"]), device="cuda")
+
+    def step():
+        pool.plan(streams, [P] * S, sh)
+        enc.forward(mel.data_ptr(), out.data_ptr(), sh)
+        pool.commit()
+
+    for _ in range(args.warmup):
+        step()
+    enc.sync(sh)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(local)
+    gpu_id = str(getattr(props, "uuid", local))
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    enc.sync(sh)
+    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    step_s = ms / 1000.0 / args.steps
+    w_bytes = encoder_weight_bytes(cfg)
+    keys = W + P - 1
+    ring_bytes = L * S * keys * H * 64 * 2 * 2
+    rows = S * P
+    flops = 2 * rows * (w_bytes * 0 + L * (4 * H * 64 * cfg["dim"] + 3 * cfg["dim"] * cfg["hidden"])) \
+        + L * S * P * H * keys * 64 * 4
+    e2e = None
+    if not args.no_e2e:
+        hmel = torch.randn((S, 128, 2 * P + 4)).pin_memory()
+        hout = torch.empty((S * P, cfg["dim"])).pin_memory()
+
+        def host_step():
+            mel.copy_(hmel, non_blocking=True)
+            step()
+            hout.copy_(out, non_blocking=True)
+
+        host_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            host_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(dist, f0.elapsed_time(f1), "cuda")
+        e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "stream-chunks/s",
+               "h2d_bytes_per_step": int(hmel.numel()) * 4, "d2h_bytes_per_step": int(hout.numel()) * 4,
+               "ms_per_step": round(ems / args.steps, 4)}
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        achieved = (w_bytes + ring_bytes) / step_s / 1e9
+        line = {
+            "metric": "whole encoder step stream-chunks/s (conv stem + 32 layers + norm, 4 frames per chunk)",
+            "value": round(world * S * args.steps / (ms / 1000.0), 1),
+            "unit": "stream-chunks/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "Q4_K / Q6_K weights with Q8_K rows, f16 conv operands, bf16 rings, fp32 activations",
+            "data": "synthetic",
+            "config": {"workload": f"config encstack: {cfg['desc']}", "layers": L, "streams_per_gpu": S,
+                       "parallelism": f"streams sharded, {S}/GPU, no collective",
+                       "l2": f"inputs larger than L2 ({ring_bytes / 1e6:.0f} MB of ring reads per step)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_step": int(w_bytes + ring_bytes),
+                         "tflops": round(flops / step_s / 1e12, 2), "avg_step_us": round(step_s * 1e6, 1),
+                         "kernel": "whole step (all kernels); products re-stream their weights per 64-row chunk"},
+            "cpu_baseline": None, "e2e": e2e,
+            "gpu_launches": int(args.steps * (2 + 1 + L * (2 * 8 + 1 + 1 + 2 * 8 + 1 + 8 * (2 + 2) + 1))),
+            "launch": "eager C-ABI calls per step: vxk_enc_batch_plan, vxk_encoder_forward, vxk_enc_batch_commit",
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    enc.close()
+    pool.close()
+
+
 def decoder_weight_bytes(cfg):
     """GGUF bytes of every matrix one decoder step streams (all layers + head)."""
     L, D, H, V = cfg["layers"], cfg["dim"], cfg["hidden"], cfg["vocab"]
@@ -1159,6 +1344,11 @@ def run_reference(args, cfg, rank, world):
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
+    if cfg.get("kind") == "encstack":
+        print(json.dumps({"impl": "reference", "unavailable": "config encstack has no CPU restatement timing yet "
+                                                               "(the oracle encoder is a per-row Python checker)"}),
+              flush=True)
+        return
     if cfg.get("kind") == "decoder":
         tensors = write_decoder_gguf(None, cfg, args.seed)
         rng = np.random.default_rng(args.seed)
@@ -1264,6 +1454,12 @@ def main():
         return
     if cfg.get("kind") == "qmm":
         run_qmm(args, cfg, world, rank, local, dist, torch, vxk)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if cfg.get("kind") == "encstack":
+        run_encstack(args, cfg, world, rank, local, dist, torch, vxk)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

@@ -485,7 +485,8 @@ typedef struct vxk_qweight_config {
     vxk_qtype type;
     int32_t n_rows;      /* output features N (ggml ne[1]); a multiple of 64 */
     int32_t n_cols;      /* input features K (ggml ne[0]); a multiple of 256, <= 16384 */
-    int32_t max_batch;   /* activation rows per product, 1..64 */
+    int32_t max_batch;   /* activation rows per product, 1..512 (Q4_K / Q6_K from 17 rows: one
+                            launch, 64-row chunks side by side; otherwise 64 rows per launch) */
     int32_t reserved;
 } vxk_qweight_config;
 

@@ -98,7 +98,7 @@ def test_rejects_bad_calls(vxk, oracle):
     rng = np.random.default_rng(9)
     w = oracle.random_qblocks(Q4_K, 64, 256, rng)
     with pytest.raises(vxk.VxkError):
-        vxk.QWeight(w, type=Q4_K, n_rows=64, n_cols=256, max_batch=65)
+        vxk.QWeight(w, type=Q4_K, n_rows=64, n_cols=256, max_batch=513)
     with pytest.raises(vxk.VxkError):
         vxk.QWeight(w[:32], type=Q4_K, n_rows=64, n_cols=256, max_batch=4)
     qw = vxk.QWeight(w, type=Q4_K, n_rows=64, n_cols=256, max_batch=4)
@@ -192,3 +192,17 @@ def test_qweight_from_gguf_file(vxk, oracle, tmp_path):
     with pytest.raises(vxk.VxkError):
         g.qweight("absent")
     g.close()
+
+
+@pytest.mark.parametrize("t,n,k,rows", [
+    (Q4_K, 1280, 1280, 512),   # the encoder's q of 128 streams x 4 frames, 8 chunks in one launch
+    (Q6_K, 1280, 5120, 200),   # the encoder's w2, a ragged last chunk
+    (Q8_0, 256, 512, 130),     # Q8_0 (int8 mma.sync): 64 rows per launch
+])
+def test_many_rows_in_one_call(vxk, oracle, t, n, k, rows):
+    rng = np.random.default_rng(300 + rows + t)
+    w = oracle.random_qblocks(t, n, k, rng)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    (got,) = _run(vxk, w, t, n, k, x, max_batch=rows)
+    _check(oracle, t, w, n, k, x, got)
+

@@ -6,7 +6,7 @@
 // One forward (the reference builds it per context as the step graph,
 // src/voxtral.cpp:3047-3104, or the prefill graph, 2891-2965):
 //   embed_norm                       x = emb[token] + audio[slot]; xn = norm(x) * attn_norm[0]
-//   per layer l (products in chunks of <= 64 rows):
+//   per layer l (products in calls of <= 512 rows):
 //     q, k, v = W{q,k,v} xn          one activation quantization for the three
 //     attention                      vxk_decode_layer (one token per stream) or
 //                                    vxk_append_layer + vxk_attend_layer (prefill)
@@ -91,7 +91,7 @@ struct vxk_decoder {
     vxk_pool * pool = nullptr;
     vxk::PoolShape ps{};
     int32_t dim = 0, hidden = 0, vocab = 0, ada_dim = 0, n_layers = 0, enc_dim = 0;
-    int32_t chunk = 64;  // rows per product call
+    int32_t chunk = 64;  // rows per product call (up to 512)
     float eps = 1e-5f;
     std::vector<Layer> layers;
     std::vector<vxk_qweight *> all_q;
@@ -372,7 +372,7 @@ void create(vxk_decoder * d, const vxk_gguf * g, vxk_pool * pool) {
     if (d->cfg.enc_capacity < 0 || d->cfg.enc_capacity % 4)
         dfail(VXK_STATUS_INVALID_ARGUMENT, "enc_capacity must be a non-negative multiple of 4");
     DevScope scope(ps.device);
-    d->chunk = std::min<int32_t>(vxk::kQmmMaxBatch, ps.max_rows);
+    d->chunk = std::min<int32_t>(vxk::kQmmMaxRows, ps.max_rows);
 
     const TensorRef emb = need(g, "tok_embeddings.weight");
     if (emb.info.n_dims != 2) dfail(VXK_STATUS_INVALID_ARGUMENT, "tok_embeddings.weight must be 2-D");

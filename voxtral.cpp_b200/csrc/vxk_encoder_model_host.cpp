@@ -5,7 +5,7 @@
 //
 // One forward:
 //   conv stem                         gelu(conv1(gelu(conv0(mel window)))) -> x
-//   per layer l (products in chunks of <= 64 rows):
+//   per layer l (products in calls of <= 512 rows):
 //     xn = rms_norm(x) * attn_norm    (the previous layer's add_norm; the stem's for l = 0)
 //     q, k, v = W{q,k,v} xn           one quantization for the three; q += bq, v += bv
 //     attention                       vxk_enc_layer: RoPE, ring append, windowed MHA
@@ -254,7 +254,7 @@ void ecreate(vxk_encoder * e, const vxk_gguf * g, vxk_enc_pool * pool, int32_t m
     Scope scope(es.device);
     e->max_rows = max_rows > 0 ? max_rows : es.max_streams * 4;
     if (e->max_rows > es.max_streams * es.max_new) e->max_rows = es.max_streams * es.max_new;
-    e->chunk = std::min<int32_t>(vxk::kQmmMaxBatch, e->max_rows);
+    e->chunk = std::min<int32_t>(vxk::kQmmMaxRows, e->max_rows);
     e->max_win = 2 * es.max_new + 4;
 
     const TRef c0 = tneed(g, "enc.conv0.weight");

@@ -256,7 +256,8 @@ cudaError_t launch_head_argmax(const float * logits, int32_t rows, int32_t vocab
 
 constexpr int kQmmRows = 64;       // weight rows per CTA (4 warps x 16-row tiles)
 constexpr int kQmmUnit = 256;      // columns per record and per activation unit
-constexpr int kQmmMaxBatch = 64;   // activation rows per product (8 n-tiles of 8)
+constexpr int kQmmMaxBatch = 64;   // activation rows per mma.sync product (8 n-tiles of 8)
+constexpr int kQmmMaxRows = 512;   // activation rows per vxk_qweight call (tcgen05: chunks of 64 in one launch)
 
 constexpr int kQmmMaxGroup = 4;   // matrices sharing one activation quantization
 constexpr int kQmmMaxSplits = 8;  // column splits of a 64-row block = CTAs of one (portable) cluster
@@ -314,6 +315,7 @@ struct QtcParams {
     int32_t n_units;
     int32_t rows;              // activation rows, 1 .. npad
     int32_t npad;              // MMA N: rows padded to 16, 32 or 64
+    int32_t n_chunks;          // row chunks of npad rows (more than one only with npad 64), grid z
     int32_t units_per_split;
     int32_t n_splits;          // <= kQmmMaxSplits: one cluster
     const float * x;           // [rows][K] fp32

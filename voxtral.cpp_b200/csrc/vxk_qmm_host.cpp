@@ -378,6 +378,7 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * 
     p.n_units = w0->n_units;
     p.rows = rows;
     p.npad = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+    p.n_chunks = (rows + p.npad - 1) / p.npad;
     int32_t block0 = 0;
     for (int i = 0; i < n; ++i) {
         p.mats[i].w = ws[i]->w_tc;
@@ -388,7 +389,7 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * 
         p.mats[i].type = (int32_t) ws[i]->cfg.type;
         block0 += ws[i]->cfg.n_rows / 128;
     }
-    plan_split_tc(w0->n_units, w0->sms, block0, p);
+    plan_split_tc(w0->n_units, w0->sms, (int64_t) block0 * p.n_chunks, p);
     p.x = x;
     p.x_up = x_up;
     p.b_tiles = w0->tc_b;
@@ -440,7 +441,15 @@ void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t row
         }
     }
     if (nt) run_tc(tw, nt, x, x_up, rows, ty, ws[0]->d_error, stream);
-    if (ns) run_sync(sw, ns, x, x_up, rows, sy, ws[0]->d_error, stream);
+    // the int8 mma.sync kernel takes at most 64 rows per launch
+    const int64_t K = ws[0]->cfg.n_cols;
+    for (int32_t r0 = 0; ns && r0 < rows; r0 += vxk::kQmmMaxBatch) {
+        const int32_t nr = std::min<int32_t>(vxk::kQmmMaxBatch, rows - r0);
+        float * syc[vxk::kQmmMaxGroup];
+        for (int i = 0; i < ns; ++i) syc[i] = sy[i] + (int64_t) r0 * sw[i]->cfg.n_rows;
+        run_sync(sw, ns, x + (int64_t) r0 * K, x_up ? x_up + (int64_t) r0 * K : nullptr, nr, syc, ws[0]->d_error,
+                 stream);
+    }
 }
 
 }  // namespace
@@ -530,13 +539,13 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
         const vxk_qweight_config & c = *config;
         if (c.struct_size < sizeof(vxk_qweight_config)) qfail(VXK_STATUS_INVALID_ARGUMENT, "config struct_size too small");
         check_shape((int) c.type, c.n_rows, c.n_cols);
-        if (c.max_batch < 1 || c.max_batch > vxk::kQmmMaxBatch)
-            qfail(VXK_STATUS_INVALID_ARGUMENT, "max_batch must be in [1, 64]");
+        if (c.max_batch < 1 || c.max_batch > vxk::kQmmMaxRows)
+            qfail(VXK_STATUS_INVALID_ARGUMENT, "max_batch must be in [1, 512]");
         const int64_t rb = gguf_row_bytes((int) c.type, c.n_cols);
         if (gguf_bytes != (size_t) (rb * c.n_rows)) qfail(VXK_STATUS_INVALID_ARGUMENT, "gguf_bytes != n_rows * row bytes");
         w->cfg = c;
         w->n_units = c.n_cols / vxk::kQmmUnit;
-        w->nt_max = nt_for(c.max_batch);
+        w->nt_max = nt_for(std::min(c.max_batch, vxk::kQmmMaxBatch));
         int n_dev = 0;
         VXK_QCUDA(cudaGetDeviceCount(&n_dev));
         if (c.device < 0 || c.device >= n_dev) qfail(VXK_STATUS_INVALID_ARGUMENT, "no such CUDA device");
@@ -566,9 +575,10 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
             VXK_QCUDA(cudaMemcpy(w->w_tc, hrec.data(), hrec.size(), cudaMemcpyHostToDevice));
             VXK_QCUDA(cudaMalloc(&w->dd_tc, hdd.size()));
             VXK_QCUDA(cudaMemcpy(w->dd_tc, hdd.data(), hdd.size(), cudaMemcpyHostToDevice));
-            VXK_QCUDA(cudaMalloc(&w->tc_b, (size_t) w->n_units * 64 * 512));
-            VXK_QCUDA(cudaMalloc(&w->tc_bmin, (size_t) w->n_units * 64 * 128));
-            VXK_QCUDA(cudaMalloc(&w->tc_dx, (size_t) w->n_units * 64 * sizeof(float)));
+            const size_t chunks = (size_t) (c.max_batch + 63) / 64;  // 64-row chunks of one launch
+            VXK_QCUDA(cudaMalloc(&w->tc_b, chunks * w->n_units * 64 * 512));
+            VXK_QCUDA(cudaMalloc(&w->tc_bmin, chunks * w->n_units * 64 * 128));
+            VXK_QCUDA(cudaMalloc(&w->tc_dx, chunks * w->n_units * 64 * sizeof(float)));
         }
         VXK_QCUDA(cudaMalloc(&w->d_error, sizeof(int32_t)));
         w->own_error = w->d_error;

@@ -18,20 +18,18 @@
 // h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
 // d_x*d_w and d_x*dmin_w in fp32.
 //
-// CTA = 128 weight rows x a range of 256-column units; 19 warps, two per SM
-// sub-partition for each of the per-row roles (a warp reaches only the TMEM
-// lanes of its sub-partition, warp % 4):
-//   warps 0-7   dequant: thread = weight row (TMEM lane), warps w and w + 4
-//               split the unit's columns; per unit they read the row's quant
-//               bytes and scale/min bytes from the raw ring, write f16 pairs
-//               sc*q into TMEM (tcgen05.st) and (warps 0-3) the row's mins row
-//               into shared memory
-//   warps 8-15  epilogue: thread = weight row, warps w and w + 4 split the
-//               activation columns; tcgen05.ld of the unit's accumulators,
-//               fp32 block factors into registers
-//   warp 16     bulk copies of the raw weight records (HBM stream, evict-first)
-//   warp 17     bulk copies of the quantized activations (L2)
-//   warp 18     tcgen05.mma issuer: 16 MMAs (M = 128, N = rows padded to 16,
+// CTA = 128 weight rows x a range of 256-column units x one chunk of up to 64
+// activation rows (grid z: a product of more rows runs its 64-row chunks side
+// by side in one launch); 11 warps:
+//   warps 0-3   dequant: thread = weight row (TMEM lane); per unit it reads the
+//               row's 128 quant bytes and 16 scale/min bytes from the raw
+//               ring, writes 128 columns of f16 pairs sc*q into TMEM
+//               (tcgen05.st) and the row's mins row into shared memory
+//   warps 4-7   epilogue: thread = weight row; tcgen05.ld of the unit's
+//               accumulators, fp32 block factors into registers
+//   warp 8      bulk copies of the raw weight records (HBM stream, evict-first)
+//   warp 9      bulk copies of the quantized activations (L2)
+//   warp 10     tcgen05.mma issuer: 16 MMAs (M = 128, N = rows padded to 16,
 //               K = 16, A from TMEM) + 1 mins MMA per unit
 // Column splits of a 128-row block are one thread-block cluster and reduce
 // their partial blocks through distributed shared memory, in split order.
@@ -45,10 +43,7 @@
 namespace vxk {
 namespace {
 
-constexpr int kThreads = 608;
-constexpr int kDqWarps = 8;                     // dequant warps 0-7
-constexpr int kEpWarp0 = 8;                     // epilogue warps 8-15
-constexpr int kRawWarp = 16, kActWarp = 17, kMmaWarp = 18;
+constexpr int kThreads = 352;
 constexpr int kRawStages = 4;
 constexpr int kActStages = 2;
 constexpr int kMaxN = 64;
@@ -310,11 +305,13 @@ __device__ __forceinline__ int tc_tile_off(int n, int p, int rows) {
 __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int u = blockIdx.x, r = blockIdx.y, t = threadIdx.x;
+    const int u = blockIdx.x, rg = blockIdx.y, t = threadIdx.x;
+    const int chunk = rg / p.npad, r = rg - chunk * p.npad;  // row r of 64-row chunk `chunk`
     const int lane = t & 31, warp = t >> 5;
     const int64_t K = (int64_t) p.n_units * kQmmUnit;
-    const int64_t xi = (int64_t) r * K + (int64_t) u * kQmmUnit + t;
-    const float x = r < p.rows ? (p.x_up ? swiglu_value(p.x[xi], p.x_up[xi]) : p.x[xi]) : 0.0f;
+    const int64_t xi = (int64_t) rg * K + (int64_t) u * kQmmUnit + t;
+    const float x = rg < p.rows ? (p.x_up ? swiglu_value(p.x[xi], p.x_up[xi]) : p.x[xi]) : 0.0f;
+    const int64_t cu = (int64_t) chunk * p.n_units + u;  // this chunk's unit
     __shared__ unsigned long long red[8];
     __shared__ float s_max;
     unsigned long long key = ((unsigned long long) __float_as_uint(fabsf(x)) << 32) | (unsigned) (255 - t);
@@ -340,18 +337,18 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
         d = __fdiv_rn(1.0f, iscale);
     }
     const int np = p.npad;
-    uint8_t * tile = p.b_tiles + (int64_t) u * np * 512;
+    uint8_t * tile = p.b_tiles + cu * np * 512;
     *reinterpret_cast<__half *>(tile + tc_tile_off(r, tc_position(t), np)) = __int2half_rn(q);
     int s = q;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
     if (lane == 0) {
         // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j)
-        uint8_t * mrow = p.bmin_tiles + (int64_t) u * np * 128 + (r >> 3) * 1024 + (r & 7) * 128;
+        uint8_t * mrow = p.bmin_tiles + cu * np * 128 + (r >> 3) * 1024 + (r & 7) * 128;
         *reinterpret_cast<__half *>(mrow + ((0 ^ (r & 7)) << 4) + warp * 2) = __int2half_rn(s & 127);
         *reinterpret_cast<__half *>(mrow + ((1 ^ (r & 7)) << 4) + warp * 2) = __int2half_rn(s >> 7);
     }
-    if (t == 0) p.dx[(int64_t) u * np + r] = d;
+    if (t == 0) p.dx[cu * np + r] = d;
 }
 
 // One half (128 columns) of a Q6_K unit for row r into TMEM: A_hi = 16*(sc>>4)*q
@@ -361,7 +358,7 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
 // 33+l, 35+l} (l = 16c4 + 4k) of the half, the low (gg = 0) or high nibbles of
 // the quant bytes at l and 32+l and 2-bit fields 4gg and 4gg+2 of the high
 // plane byte at l.  Both parts are exact f16 integers.
-__device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int h, int gg, uint32_t abase) {
+__device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int h, uint32_t abase) {
     const uint8_t * ql = raw + r * 128;
     const uint8_t * qh = raw + 16384 + r * 64;
     uint4 A[2], B[2], H[2];
@@ -374,37 +371,38 @@ __device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int 
     const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
     const __half2 c1056 = __float2half2_rn(1056.0f);
-    // part 0: A_hi = 16*(sc>>4)*q at abase + 32 gg; part 1: A_lo = (sc&15)*q at abase + 64 + 32 gg
 #pragma unroll
-    for (int part = 0; part < 2; ++part) {
-        uint32_t out[32];
+    for (int gg = 0; gg < 2; ++gg) {
+        uint32_t hi[32], lo[32];
 #pragma unroll
         for (int c4 = 0; c4 < 2; ++c4) {
-            const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two quant bytes
+            const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two parts
             const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
             const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
-            const __half2 fa = __float2half2_rn(part == 0 ? (float) (16 * (sa >> 4)) : (float) (sa & 15));
-            const __half2 fb = __float2half2_rn(part == 0 ? (float) (16 * (sb >> 4)) : (float) (sb & 15));
+            const __half2 fah = __float2half2_rn((float) (16 * (sa >> 4))), fal = __float2half2_rn((float) (sa & 15));
+            const __half2 fbh = __float2half2_rn((float) (16 * (sb >> 4))), fbl = __float2half2_rn((float) (sb & 15));
             const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
             const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
             const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int ns = 4 * gg, fpa = 4 * gg, fpb = 4 * gg + 2;
+                const int ns = 4 * gg, fa = 4 * gg, fb = 4 * gg + 2;
                 uint32_t pv[4];
-                pv[0] = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fpa) & 0x00030003u) << 4) | 0x64006400u;
-                pv[1] = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fpb) & 0x00030003u) << 4) | 0x64006400u;
-                pv[2] = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fpa + 8)) & 0x00030003u) << 4) | 0x64006400u;
-                pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fpb + 8)) & 0x00030003u) << 4) | 0x64006400u;
+                pv[0] = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fa) & 0x00030003u) << 4) | 0x64006400u;
+                pv[1] = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fb) & 0x00030003u) << 4) | 0x64006400u;
+                pv[2] = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fa + 8)) & 0x00030003u) << 4) | 0x64006400u;
+                pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4) | 0x64006400u;
 #pragma unroll
                 for (int x = 0; x < 4; ++x) {
                     const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&pv[x]), c1056);
-                    // pv[0], pv[2] come from the bytes at l, pv[1], pv[3] from the bytes at 32 + l
-                    out[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, (x & 1) == 0 ? fa : fb));
+                    const bool pa = (x & 1) == 0;  // pv[0], pv[2] from the bytes at l, pv[1], pv[3] at 32+l
+                    hi[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fah : fbh));
+                    lo[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fal : fbl));
                 }
             }
         }
-        tmem_st32(abase + 64 * part + 32 * gg, out);
+        tmem_st32(abase + 32 * gg, hi);
+        tmem_st32(abase + 64 + 32 * gg, lo);
     }
 }
 
@@ -427,23 +425,25 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         if (i < p.n_mats && (int) blockIdx.x >= p.mats[i].block0) m = p.mats[i];
     const int blk = (int) blockIdx.x - m.block0;
     const int split = (int) blockIdx.y;
+    const int chunk = (int) blockIdx.z;                    // activation rows chunk * N ..
+    const int64_t cbase = (int64_t) chunk * p.n_units;     // this chunk's unit index base
     const int u0 = split * p.units_per_split;
     const int nu = min(p.n_units, u0 + p.units_per_split) - u0;
 
     if (tid == 0) {
         for (int s = 0; s < kRawStages; ++s) {
             mbar_init(&bars[kBarRawFull + s], 1);
-            mbar_init(&bars[kBarRawEmpty + s], 32 * kDqWarps);
+            mbar_init(&bars[kBarRawEmpty + s], 128);
         }
         for (int s = 0; s < kActStages; ++s) {
             mbar_init(&bars[kBarActFull + s], 1);
             mbar_init(&bars[kBarActEmpty + s], 1);         // MMA commit
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&bars[kBarAFull + b], 32 * kDqWarps);
+            mbar_init(&bars[kBarAFull + b], 128);
             mbar_init(&bars[kBarAEmpty + b], 1);
             mbar_init(&bars[kBarDFull + b], 1);
-            mbar_init(&bars[kBarDEmpty + b], 128 * (N >= 32 ? 2 : 1));  // epilogue warps with columns
+            mbar_init(&bars[kBarDEmpty + b], 128);
         }
         mbar_init(&bars[kBarDrain], 1);
         *abort_flag = 0;
@@ -461,11 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     const uint32_t tmem = *tmem_slot;
     float * ptile = reinterpret_cast<float *>(base + kOffRaw);  // [N][128] partial block at the end
 
-    if (warp < kDqWarps) {
-        // ---------------- dequant: row r = 32 (warp % 4) + lane, column half warp / 4 ----------------
-        const int qd = warp & 3, hs = warp >> 2;
-        const int r = 32 * qd + lane;
-        const uint32_t lane_off = (uint32_t) (32 * qd) << 16;
+    if (warp < 4) {
+        // ---------------- dequant: row r = 32 warp + lane ----------------
+        const int r = 32 * warp + lane;
+        const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
         const bool q6 = m.type == 14;
         const int phases = q6 ? 2 : 1;  // A buffers filled per unit (Q6_K: two halves)
         int j = 0;                      // A-phase counter: buffer j & 1, use j >> 1
@@ -485,16 +484,14 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 }
                 tc_fence_after();
                 if (q6) {
-                    dequant_q6_half(raw, r, h, hs, tmem + 128 * b + lane_off);
+                    dequant_q6_half(raw, r, h, tmem + 128 * b + lane_off);
                 } else {
                     const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
                     const uint32_t scw[2] = {scm.x, scm.y};
                     const uint32_t mnw[2] = {scm.z, scm.w};
-                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word);
-                    // this warp: chunks 4 hs .. 4 hs + 3 (TMEM columns 64 hs .. 64 hs + 63)
+                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word)
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const int half = 2 * hs + hh;
+                    for (int half = 0; half < 4; ++half) {
                         uint32_t cols[32];
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
@@ -522,7 +519,6 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
                     }
                     // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact)
-                    if (hs == 0) {
                     uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 1024 + (r & 7) * 128;
                     uint32_t m0[4], m1[4];
 #pragma unroll
@@ -534,7 +530,6 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     }
                     *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
                     *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
-                    }
                 }
                 if (h == phases - 1) mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -543,23 +538,20 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 mbar_arrive(&bars[kBarAFull + b]);
             }
         }
-    } else if (warp < kEpWarp0 + 8) {
-        // ---------------- epilogue: row r = 32 (warp % 4) + lane, columns ch * NC .. ----------------
-        constexpr int EPC = N >= 32 ? 2 : 1;  // column groups (tcgen05.ld moves 16 columns)
-        constexpr int NC = N / EPC;
-        const int q = warp & 3, ch = (warp - kEpWarp0) >> 2;
+    } else if (warp < 8) {
+        // ---------------- epilogue: row r = 32 (warp - 4) + lane ----------------
+        const int q = warp & 3;
         const int r = 32 * q + lane;
         const uint32_t lane_off = (uint32_t) (32 * q) << 16;
-        if (ch < EPC) {
         const uint32_t * dd = reinterpret_cast<const uint32_t *>(m.dd) + ((int64_t) blk * p.n_units + u0) * 128 + r;
         uint32_t ddn = nu > 0 ? __ldg(dd) : 0u;
         // d_x of each unit straight from global memory (written by the
         // quantization kernel: wait for it), so an activation stage is free
         // as soon as its MMAs complete
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        float acc[NC];
+        float acc[N];
 #pragma unroll
-        for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
+        for (int j = 0; j < N; ++j) acc[j] = 0.0f;
         for (int i = 0; i < nu; ++i) {
             const int b = i & 1;
             const uint32_t ddc = ddn;
@@ -568,34 +560,45 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             if (!__all_sync(kFull, ok)) break;
             tc_fence_after();
             const float2 dw = __half22float2(*reinterpret_cast<const __half2 *>(&ddc));  // (d, dmin)
-            const float * dx = p.dx + (int64_t) (u0 + i) * N + ch * NC;
-            const uint32_t dcol = tmem + 256 + 64 * b + ch * NC + lane_off;
+            const float * dx = p.dx + (cbase + u0 + i) * N;
             if (m.type == 14) {
                 // Q6_K: acc += (d_w * d_x) * D
 #pragma unroll
-                for (int c0 = 0; c0 < NC; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16_nowait(dcol + c0, v);
+                for (int c0 = 0; c0 < N; c0 += 32) {
+                    constexpr int W = N < 32 ? N : 32;
+                    uint32_t v[2][16];
+#pragma unroll
+                    for (int hh = 0; hh < W / 16; ++hh) tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * hh + lane_off, v[hh]);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        acc[c0 + jj] = fmaf(__fmul_rn(dw.x, dx[c0 + jj]), __uint_as_float(v[jj]), acc[c0 + jj]);
+                    for (int hh = 0; hh < W / 16; ++hh)
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dx[c0 + 16 * hh + jj]),
+                                                          __uint_as_float(v[hh][jj]), acc[c0 + 16 * hh + jj]);
                 }
             } else {
-                // Q4_K: 16 columns of D and of Dmin in flight per wait
+                // Q4_K: 32 columns of D and of Dmin in flight per wait
 #pragma unroll
-                for (int c0 = 0; c0 < NC; c0 += 16) {
-                    uint32_t v[16], mm[16];
-                    tmem_ld16_nowait(dcol + c0, v);
-                    tmem_ld16_nowait(dcol + 128 + c0, mm);
-                    tmem_ld_wait();
+                for (int c0 = 0; c0 < N; c0 += 32) {
+                constexpr int W = N < 32 ? N : 32;
+                uint32_t v[2][16], mm[2][16];
+#pragma unroll
+                for (int h = 0; h < W / 16; ++h) {
+                    tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * h + lane_off, v[h]);
+                    tmem_ld16_nowait(tmem + 384 + 64 * b + c0 + 16 * h + lane_off, mm[h]);
+                }
+                tmem_ld_wait();
+#pragma unroll
+                for (int h = 0; h < W / 16; ++h)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float x = dx[c0 + j];
-                        acc[c0 + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[j]),
-                                           fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[j]), acc[c0 + j]));
+                        const float x = dx[c0 + 16 * h + j];
+                        acc[c0 + 16 * h + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[h][j]),
+                                                    fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[h][j]),
+                                                         acc[c0 + 16 * h + j]));
                     }
-                }
+            }
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarDEmpty + b]);
@@ -604,10 +607,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         // before the last unit's MMAs, which this thread has waited for.
         if (!*abort_flag) {
 #pragma unroll
-            for (int j = 0; j < NC; ++j) ptile[(ch * NC + j) * 128 + r] = acc[j];
+            for (int j = 0; j < N; ++j) ptile[j * 128 + r] = acc[j];
         }
-        }
-    } else if (warp == kRawWarp) {
+    } else if (warp == 8) {
         // ---------------- raw weight records (HBM) ----------------
         if (lane == 0) {
             const uint64_t pol = l2_policy(true);
@@ -626,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     tc_drain(&bars[kBarRawFull + d % kRawStages], (uint32_t) (d / kRawStages) & 1u);
         }
         __syncwarp();
-    } else if (warp == kActWarp) {
+    } else if (warp == 9) {
         // ---------------- quantized activations (L2), after the producer kernel ----------------
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0) {
@@ -638,8 +640,8 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     break;
                 uint8_t * st = base + kOffAct + t * kActStage;
                 mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 128));
-                bulk_g2s(st, p.b_tiles + (int64_t) u * N * 512, N * 512, &bars[kBarActFull + t], pol);
-                bulk_g2s(st + kActB, p.bmin_tiles + (int64_t) u * N * 128, N * 128, &bars[kBarActFull + t], pol);
+                bulk_g2s(st, p.b_tiles + (cbase + u) * N * 512, N * 512, &bars[kBarActFull + t], pol);
+                bulk_g2s(st + kActB, p.bmin_tiles + (cbase + u) * N * 128, N * 128, &bars[kBarActFull + t], pol);
             }
             if (*abort_flag)
                 for (int d = i > kActStages ? i - kActStages : 0; d < i; ++d)
@@ -710,9 +712,11 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     cluster_sync();
     if (live) {
         const int S = p.n_splits;
-        const int E4 = p.rows * 128 / 4;
+        const int rows_c = min(N, p.rows - chunk * N);
+        const int E4 = rows_c * 128 / 4;
         const int e0 = (int) ((int64_t) E4 * split / S), e1 = (int) ((int64_t) E4 * (split + 1) / S);
-        cluster_reduce_store<128>(smem_u32(ptile), S, e0, e1, tid, kThreads, m.y, m.n_rows, (int64_t) blk * 128);
+        cluster_reduce_store<128>(smem_u32(ptile), S, e0, e1, tid, kThreads, m.y + (int64_t) chunk * N * m.n_rows,
+                                  m.n_rows, (int64_t) blk * 128);
     }
     cluster_sync();
     if (warp == 0) {
@@ -754,8 +758,8 @@ cudaError_t launch_n(const QtcParams & p, cudaStream_t stream) {
         raised[dev] = true;
     }
     const int blocks = p.mats[p.n_mats - 1].block0 + p.mats[p.n_mats - 1].n_rows / 128;
-    return launch_ex(qtc_kernel<N>, dim3((unsigned) blocks, (unsigned) p.n_splits), kThreads, kSmem, stream, p,
-                     (unsigned) p.n_splits);
+    return launch_ex(qtc_kernel<N>, dim3((unsigned) blocks, (unsigned) p.n_splits, (unsigned) p.n_chunks), kThreads,
+                     kSmem, stream, p, (unsigned) p.n_splits);
 }
 
 template <int N>
@@ -795,13 +799,16 @@ int qtc_max_active_clusters(int npad, int cluster_y) {
 }
 
 cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream) {
-    if (p.n_mats < 1 || p.n_mats > kQmmMaxGroup || p.rows < 1 || p.rows > p.npad || p.units_per_split < 1 ||
+    if (p.n_chunks < 1 || (p.n_chunks > 1 && p.npad != 64) || p.rows <= p.npad * (p.n_chunks - 1))
+        return cudaErrorInvalidValue;
+    if (p.n_mats < 1 || p.n_mats > kQmmMaxGroup || p.rows < 1 || p.rows > p.npad * p.n_chunks || p.units_per_split < 1 ||
         p.n_splits < 1 || p.n_splits > kQmmMaxSplits || (int64_t) p.units_per_split * (p.n_splits - 1) >= p.n_units)
         return cudaErrorInvalidValue;
     if (p.npad != 16 && p.npad != 32 && p.npad != 64) return cudaErrorInvalidValue;
     for (int i = 0; i < p.n_mats; ++i)
         if (p.mats[i].n_rows % 128 != 0) return cudaErrorInvalidValue;
-    cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) p.npad), 256, 0, stream, p, 1);
+    cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) (p.npad * p.n_chunks)), 256, 0,
+                              stream, p, 1);
     if (e != cudaSuccess) return e;
     switch (p.npad) {
         case 16: return launch_n<16>(p, stream);

@@ -326,3 +326,32 @@ def test_batcher_runs_the_decoder(vxk, vd, tmp_path):
         d.close()
     for p in pools:
         p.close()
+
+
+def test_long_prefill_then_steps(vxk, vd, tmp_path):
+    """A 100-token and a 40-token prefill in one batch (140 rows: every product
+    takes them in one call, 64-row chunks side by side), then two steps."""
+    import torch
+    import decoder_model
+
+    path = tmp_path / "mp.gguf"
+    tensors = decoder_model.build(path, 17)
+    cfg = dict(n_layers=2, n_blocks=96, capacity=512, max_streams=4, max_rows=160, max_position=1024, dtype=1)
+    g = vxk.Gguf(path)
+    pool = vxk.Pool(**cfg)
+    dec = vxk.Decoder(g, pool, audio_capacity=128, enc_capacity=0)
+    g.close()
+    dev_att = DeviceAttention(vxk, cfg)
+    refs = (vd.Decoder(tensors, 2, capacity=512, attention=dev_att), vd.Decoder(tensors, 2, capacity=512), dev_att)
+    rng = np.random.default_rng(6)
+    streams = [pool.open_stream() for _ in range(2)]
+    audio = rng.normal(0, 0.05, (2, 128, dec.info["dim"])).astype(np.float32)
+    cs = torch.cuda.current_stream().cuda_stream
+    dev_audio = torch.from_numpy(audio).cuda()
+    for i, s in enumerate(streams):
+        dec.write_audio(s, 0, 128, dev_audio[i].data_ptr(), cs)
+    steps = [[(0, 100), (1, 40)], [(0, 1), (1, 1)], [(1, 1), (0, 1)]]
+    _run_steps(vxk, pool, dec, refs, streams, steps, audio, rng, dec.info["vocab"])
+    dev_att.close()
+    dec.close()
+    pool.close()

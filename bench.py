@@ -764,6 +764,56 @@ def write_encoder_gguf(path, cfg, seed):
     w.close()
 
 
+def encoder_cpu_stack_sample(cfg, seed, seconds):
+    """Times the oracle's whole encoder step (oracle/vx_decoder.py Encoder: conv stem,
+    every layer with fp64 window attention over a prefilled 750-frame history, final
+    norm) on one stream's 4-frame chunk, one thread; returns (chunks/s, chunks)."""
+    import tempfile
+
+    import gguf
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_decoder as vd
+    import vx_oracle
+
+    path = Path(tempfile.mkdtemp(prefix="vxk_cpu_")) / "enc.gguf"
+    write_encoder_gguf(path, cfg, seed)
+    r = gguf.GGUFReader(str(path))
+    tensors = {}
+    for t in r.tensors:
+        ne = [int(v) for v in t.shape]
+        qt = int(t.tensor_type)
+        data = np.asarray(t.data)
+        rows = int(np.prod(ne[1:])) if len(ne) > 1 else 1
+        cols = ne[0]
+        if qt in (vd.Q8_0, vd.Q4_K, vd.Q6_K):
+            tensors[t.name] = vd.Tensor(qt, rows, cols, data.reshape(rows, -1).copy())
+        elif len(ne) == 3:
+            tensors[t.name] = vd.Tensor(qt, ne[2], ne[1] * ne[0], data.reshape(ne[2], ne[1], ne[0]).copy())
+        else:
+            tensors[t.name] = vd.Tensor(qt, rows, cols, data.copy())
+    os.unlink(path)
+    H, W, P = cfg["heads"], cfg["window"], cfg["rows"]
+    enc = vd.Encoder(tensors, cfg["layers"], H, cache_dtype=cfg["dtype"], window=W)
+    rng = np.random.default_rng(seed + 3)
+    q0 = W
+    rb = H * 64 * 2
+    for l in range(cfg["layers"]):
+        kk = rng.normal(0, 0.5, (W, H * 64)).astype(np.float32)
+        bits = vx_oracle.f32_to_bf16_bits(kk).view(np.uint8).reshape(W, rb)
+        for j in range(W):
+            enc.hist[(0, l, q0 - W + j)] = (bits[j], bits[(j + 1) % W])
+    mel = rng.normal(0, 1, (128, 2 * P + 4)).astype(np.float32)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        enc.forward([(0, q0 + done * P, P, mel)])
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 4:
+            break
+    return done / el, done
+
+
 def encoder_weight_bytes(cfg):
     L, D, F, qd = cfg["layers"], cfg["dim"], cfg["hidden"], cfg["heads"] * 64
     q4 = lambda n, k: n * (k // 256) * 144  # noqa: E731
@@ -862,6 +912,12 @@ def run_encstack(args, cfg, world, rank, local, dist, torch, vxk):
         e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "stream-chunks/s",
                "h2d_bytes_per_step": int(hmel.numel()) * 4, "d2h_bytes_per_step": int(hout.numel()) * 4,
                "ms_per_step": round(ems / args.steps, 4)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cps, done = encoder_cpu_stack_sample(cfg, args.seed, args.cpu_seconds)
+        cpu = {"value": round(cps, 5), "unit": "stream-chunks/s", "cores": 1, "kind": "port",
+               "sample": f"{done} chunks of one stream (4 frames, 750-frame window) through the conv stem, all "
+                         f"{L} layers and the final norm by the oracle (oracle/vx_decoder.py Encoder, one thread)"}
     if dist:
         dist.barrier()
     if rank == 0:
@@ -884,8 +940,8 @@ def run_encstack(args, cfg, world, rank, local, dist, torch, vxk):
                          "algorithmic_bytes_per_step": int(w_bytes + ring_bytes),
                          "tflops": round(flops / step_s / 1e12, 2), "avg_step_us": round(step_s * 1e6, 1),
                          "kernel": "whole step (all kernels); products re-stream their weights per 64-row chunk"},
-            "cpu_baseline": None, "e2e": e2e,
-            "gpu_launches": int(args.steps * (2 + 1 + L * (2 * 8 + 1 + 1 + 2 * 8 + 1 + 8 * (2 + 2) + 1))),
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(args.steps * (2 + 1 + L * 10)),
             "launch": "eager C-ABI calls per step: vxk_enc_batch_plan, vxk_encoder_forward, vxk_enc_batch_commit",
             "clocks": clocks.summary(),
         }
@@ -1345,9 +1401,19 @@ def run_reference(args, cfg, rank, world):
         print(json.dumps(line), flush=True)
         return
     if cfg.get("kind") == "encstack":
-        print(json.dumps({"impl": "reference", "unavailable": "config encstack has no CPU restatement timing yet "
-                                                               "(the oracle encoder is a per-row Python checker)"}),
-              flush=True)
+        cps, done = encoder_cpu_stack_sample(cfg, args.seed, 20.0)
+        line = {"impl": "reference", "metric": "whole encoder step stream-chunks/s (conv stem + 32 layers + norm, "
+                                               "4 frames per chunk)",
+                "value": round(cps, 5), "unit": "stream-chunks/s", "n_gpus": args.gpus, "steps": done, "warmup": 0,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "Q4_K / Q6_K weights, Q8_K rows, exact integer dots, fp64 attention", "data": "synthetic",
+                "config": {"workload": f"config encstack: {cfg['desc']}"},
+                "cpu_baseline": {"value": round(cps, 5), "unit": "stream-chunks/s", "cores": 1, "kind": "port",
+                                 "sample": f"{done} chunks of one stream through the stem, every layer and the norm by "
+                                           f"the oracle (oracle/vx_decoder.py Encoder, one thread)"},
+                "e2e": {"value": round(cps, 5), "unit": "stream-chunks/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     if cfg.get("kind") == "decoder":
         tensors = write_decoder_gguf(None, cfg, args.seed)

@@ -517,7 +517,7 @@ VXK_API vxk_status vxk_qweight_last_error(const vxk_qweight * w, char * buf, siz
  * quantize_row_q8_0_ref (Q8_0 weights) or quantize_row_q8_K_ref (K-quants),
  * block dot products are exact integers, and the blocks' scale factors are
  * applied in fp32.
- *   x [rows][n_cols] fp32, device;  y [rows][n_rows] fp32, device.
+ *   x [rows][n_cols] fp32, device, 16-byte aligned;  y [rows][n_rows] fp32, device.
  * Asynchronous on cuda_stream; vxk_qweight_sync reports device errors.
  */
 VXK_API vxk_status vxk_qweight_matmul(vxk_qweight * w, const float * x, int32_t rows, float * y,

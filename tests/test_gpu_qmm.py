@@ -109,6 +109,8 @@ def test_rejects_bad_calls(vxk, oracle):
             qw.matmul(x.data_ptr(), rows, y.data_ptr())
     with pytest.raises(vxk.VxkError):
         qw.matmul(0, 1, y.data_ptr())
+    with pytest.raises(vxk.VxkError):        # x not 16-byte aligned
+        qw.matmul(x.data_ptr() + 4, 1, y.data_ptr())
     qw.close()
 
 

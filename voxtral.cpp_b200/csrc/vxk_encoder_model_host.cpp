@@ -391,6 +391,8 @@ int32_t estem(vxk_encoder * e, const float * mel, float * x, cudaStream_t cs) {
     cp.b1 = e->b1;
     cp.y0 = e->y0;
     cp.x = x;
+    cp.steady = 1;
+    for (int32_t i = 0; i < ns; ++i) cp.steady = cp.steady && bv.n_new[(size_t) i] == 4;
     VXK_ECUDA(vxk::launch_conv_stem(cp, cs));
     return rows;
 }

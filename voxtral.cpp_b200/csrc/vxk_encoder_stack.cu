@@ -15,6 +15,8 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 namespace vxk {
 namespace {
 
@@ -96,24 +98,144 @@ __global__ void __launch_bounds__(kConvThreads) conv1_kernel(const ConvParams p)
     }
 }
 
-__global__ void bias2_kernel(float * y0, const float * b0, int32_t n0, float * y1, const float * b1, int32_t n1,
-                             int32_t rows) {
-    const int64_t total0 = (int64_t) rows * n0, total = total0 + (int64_t) rows * n1;
-    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < total;
-         i += (int64_t) gridDim.x * blockDim.x) {
-        if (i < total0) {
-            y0[i] = __fadd_rn(y0[i], b0[i % n0]);
-        } else {
-            const int64_t j = i - total0;
-            y1[j] = __fadd_rn(y1[j], b1[j % n1]);
+// Steady chunks (every stream n_new = 4, windows of 12 frames): a block computes
+// 128 channels for kSteadyStreams streams, so each weight load feeds 4 streams,
+// and a stream's inputs of one input channel are read from shared memory once
+// for every tap and position.  conv0 is needed at local positions 3 .. 11 only
+// (conv1's inputs), conv1 at 2 .. 5.
+constexpr int kSteadyStreams = 4;
+constexpr int kSteadyWin = 12;
+
+// conv0: y0[s][t][c] for t = 3 .. 11.  Grid (channel tiles, stream groups).
+__global__ void __launch_bounds__(kConvThreads) conv0_steady_kernel(const ConvParams p) {
+    extern __shared__ float smel[];  // [kSteadyStreams][n_mel][12], f16-rounded
+    const int s0 = blockIdx.y * kSteadyStreams;
+    const int ns = min(kSteadyStreams, p.n_streams - s0);
+    const int per = p.n_mel * kSteadyWin;
+    for (int i = threadIdx.x; i < ns * per; i += kConvThreads) {
+        const int ss = i / per, o = i - ss * per;
+        smel[i] = f16r(p.mel[p.streams[s0 + ss].mel_offset + o]);
+    }
+    __syncthreads();
+    const int c = blockIdx.x * kConvThreads + threadIdx.x;
+    if (c >= p.dim) return;
+    float acc[kSteadyStreams][9];
+#pragma unroll
+    for (int ss = 0; ss < kSteadyStreams; ++ss)
+#pragma unroll
+        for (int t = 0; t < 9; ++t) acc[ss][t] = 0.0f;
+    for (int ci = 0; ci < p.n_mel; ++ci) {
+        const float w0 = __half2float(p.w0[((int64_t) ci * 3 + 0) * p.dim + c]);
+        const float w1 = __half2float(p.w0[((int64_t) ci * 3 + 1) * p.dim + c]);
+        const float w2 = __half2float(p.w0[((int64_t) ci * 3 + 2) * p.dim + c]);
+#pragma unroll
+        for (int ss = 0; ss < kSteadyStreams; ++ss) {
+            if (ss < ns) {
+                const float * xr = smel + (ss * p.n_mel + ci) * kSteadyWin;
+                float xv[11];  // mel local 1 .. 11
+#pragma unroll
+                for (int m = 0; m < 11; ++m) xv[m] = xr[m + 1];
+#pragma unroll
+                for (int t = 0; t < 9; ++t) {  // local position 3 + t reads mel local 1 + t + k
+                    acc[ss][t] = fmaf(w0, xv[t], acc[ss][t]);
+                    acc[ss][t] = fmaf(w1, xv[t + 1], acc[ss][t]);
+                    acc[ss][t] = fmaf(w2, xv[t + 2], acc[ss][t]);
+                }
+            }
         }
     }
+    const float bias = p.b0[c];
+#pragma unroll
+    for (int ss = 0; ss < kSteadyStreams; ++ss) {
+        if (ss < ns) {
+            float * y0 = p.y0 + (int64_t) (s0 + ss) * p.max_win * p.dim;
+#pragma unroll
+            for (int t = 0; t < 9; ++t) y0[(int64_t) (3 + t) * p.dim + c] = gelu_erf_f(__fadd_rn(acc[ss][t], bias));
+        }
+    }
+}
+
+// conv1: encoder rows 4 s .. 4 s + 3 (positions 2 .. 5) from y0 positions 3 .. 11.
+__global__ void __launch_bounds__(kConvThreads) conv1_steady_kernel(const ConvParams p) {
+    extern __shared__ __half sy2[];  // [kSteadyStreams][dim][10]: f16-rounded y0 positions 3 .. 11
+    const int s0 = blockIdx.y * kSteadyStreams;
+    const int ns = min(kSteadyStreams, p.n_streams - s0);
+    for (int i = threadIdx.x; i < ns * p.dim * 9; i += kConvThreads) {
+        const int ss = i / (p.dim * 9), o = i - ss * p.dim * 9;
+        const int ci = o / 9, rr = o - ci * 9;
+        sy2[(ss * p.dim + ci) * 10 + rr] =
+            __float2half_rn(p.y0[(int64_t) (s0 + ss) * p.max_win * p.dim + (int64_t) (3 + rr) * p.dim + ci]);
+    }
+    __syncthreads();
+    const int c = blockIdx.x * kConvThreads + threadIdx.x;
+    if (c >= p.dim) return;
+    float acc[kSteadyStreams][4];
+#pragma unroll
+    for (int ss = 0; ss < kSteadyStreams; ++ss)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[ss][j] = 0.0f;
+    for (int ci = 0; ci < p.dim; ++ci) {
+        const float w0 = __half2float(p.w1[((int64_t) ci * 3 + 0) * p.dim + c]);
+        const float w1 = __half2float(p.w1[((int64_t) ci * 3 + 1) * p.dim + c]);
+        const float w2 = __half2float(p.w1[((int64_t) ci * 3 + 2) * p.dim + c]);
+#pragma unroll
+        for (int ss = 0; ss < kSteadyStreams; ++ss) {
+            if (ss < ns) {
+                const __half * yr = sy2 + (ss * p.dim + ci) * 10;
+                float yv[9];
+#pragma unroll
+                for (int m = 0; m < 9; ++m) yv[m] = __half2float(yr[m]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {  // output 2 + j reads y0 positions 3 + 2j + k
+                    acc[ss][j] = fmaf(w0, yv[2 * j], acc[ss][j]);
+                    acc[ss][j] = fmaf(w1, yv[2 * j + 1], acc[ss][j]);
+                    acc[ss][j] = fmaf(w2, yv[2 * j + 2], acc[ss][j]);
+                }
+            }
+        }
+    }
+    const float bias = p.b1[c];
+#pragma unroll
+    for (int ss = 0; ss < kSteadyStreams; ++ss)
+        if (ss < ns)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                p.x[(int64_t) (4 * (s0 + ss) + j) * p.dim + c] = gelu_erf_f(__fadd_rn(acc[ss][j], bias));
+}
+
+// Grid (column tiles, rows, 2): z = 0 adds b0 to the rows of y0, z = 1 b1 to y1.
+__global__ void bias2_kernel(float * y0, const float * b0, int32_t n0, float * y1, const float * b1, int32_t n1) {
+    float * y = blockIdx.z == 0 ? y0 : y1;
+    const float * b = blockIdx.z == 0 ? b0 : b1;
+    const int n = blockIdx.z == 0 ? n0 : n1;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (!b || i >= n) return;
+    float * row = y + (int64_t) blockIdx.y * n;
+    row[i] = __fadd_rn(row[i], b[i]);
 }
 
 }  // namespace
 
 cudaError_t launch_conv_stem(const ConvParams & p, cudaStream_t stream) {
     if (p.n_streams <= 0) return cudaSuccess;
+    if (p.steady) {
+        // every stream has n_new = 4 (rows 4 s .. 4 s + 3), windows of 12 frames
+        const dim3 grid((unsigned) ((p.dim + kConvThreads - 1) / kConvThreads),
+                        (unsigned) ((p.n_streams + kSteadyStreams - 1) / kSteadyStreams));
+        const size_t smem0 = (size_t) kSteadyStreams * p.n_mel * kSteadyWin * sizeof(float);
+        const size_t smem1 = (size_t) kSteadyStreams * p.dim * 10 * sizeof(__half);
+        if (smem0 > 227 * 1024 || smem1 > 227 * 1024 || p.max_win < kSteadyWin) return cudaErrorInvalidValue;
+        cudaError_t e = cudaFuncSetAttribute(conv0_steady_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int) smem0);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(conv1_steady_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem1);
+        if (e != cudaSuccess) return e;
+        conv0_steady_kernel<<<grid, kConvThreads, smem0, stream>>>(p);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        conv1_steady_kernel<<<grid, kConvThreads, smem1, stream>>>(p);
+        return cudaGetLastError();
+    }
     const dim3 grid((unsigned) ((p.dim + kConvThreads - 1) / kConvThreads), (unsigned) p.n_streams);
     const size_t smem0 = (size_t) p.n_mel * p.max_win * sizeof(float);
     const size_t smem1 = (size_t) (2 * kConv1Chunk + 1) * p.dim * sizeof(__half);
@@ -131,10 +253,9 @@ cudaError_t launch_conv_stem(const ConvParams & p, cudaStream_t stream) {
 
 cudaError_t launch_bias2(float * y0, const float * b0, int32_t n0, float * y1, const float * b1, int32_t n1,
                          int32_t rows, cudaStream_t stream) {
-    if (rows <= 0) return cudaSuccess;
-    const int64_t total = (int64_t) rows * (n0 + n1);
-    const int grid = (int) ((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    bias2_kernel<<<grid, 256, 0, stream>>>(y0, b0, n0, y1, b1, n1, rows);
+    if (rows <= 0 || (!b0 && !b1)) return cudaSuccess;
+    const int n = std::max(b0 ? n0 : 0, b1 ? n1 : 0);
+    bias2_kernel<<<dim3((unsigned) ((n + 255) / 256), (unsigned) rows, 2), 256, 0, stream>>>(y0, b0, n0, y1, b1, n1);
     return cudaGetLastError();
 }
 

@@ -482,6 +482,7 @@ struct ConvParams {
     const float * b1;
     float * y0;                 // [n_streams][max_win][dim] gelu(conv0), fp32
     float * x;                  // [rows][dim] encoder rows (gelu(conv1) at local 2 .. 2 + n_new - 1)
+    int32_t steady;             // every stream has n_new = 4, in plan order (rows 4 s .. 4 s + 3)
 };
 
 cudaError_t launch_conv_stem(const ConvParams & p, cudaStream_t stream);

@@ -428,6 +428,9 @@ void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, const float 
 // quantization of x (the two kernels read different operand layouts).
 void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
                cudaStream_t stream, const float * x_up = nullptr) {
+    // the quantization kernels read rows as float4
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(x_up) & 15))
+        qfail(VXK_STATUS_INVALID_ARGUMENT, "x must be 16-byte aligned");
     vxk_qweight * tw[vxk::kQmmMaxGroup], * sw[vxk::kQmmMaxGroup];
     float * ty[vxk::kQmmMaxGroup], * sy[vxk::kQmmMaxGroup];
     int nt = 0, ns = 0;

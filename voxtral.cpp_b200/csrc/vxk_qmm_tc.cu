@@ -300,55 +300,84 @@ __device__ __forceinline__ int tc_tile_off(int n, int p, int rows) {
 // ---------------------------------------------------------------------------
 // Activation quantization for the tcgen05 product (quantize_row_q8_K_ref):
 // f16 B tiles in the K order above, the mins B rows (l_j, h_j) and d_x.
-// Grid (units, npad rows), 256 threads: thread t holds column 256u + t.
+// Grid (units, padded rows / 8), 256 threads: warp w quantizes row 8 y + w of
+// unit x, lane L its columns 8L .. 8L + 7 (sub-block j = lanes 4j .. 4j + 3);
+// every reduction is a warp shuffle.  Rows are read as float4 (16-byte
+// aligned x, checked by the host).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int u = blockIdx.x, rg = blockIdx.y, t = threadIdx.x;
+    const int u = blockIdx.x, lane = threadIdx.x & 31;
+    const int rg = blockIdx.y * 8 + (threadIdx.x >> 5);      // padded row over all chunks
     const int chunk = rg / p.npad, r = rg - chunk * p.npad;  // row r of 64-row chunk `chunk`
-    const int lane = t & 31, warp = t >> 5;
     const int64_t K = (int64_t) p.n_units * kQmmUnit;
-    const int64_t xi = (int64_t) rg * K + (int64_t) u * kQmmUnit + t;
-    const float x = rg < p.rows ? (p.x_up ? swiglu_value(p.x[xi], p.x_up[xi]) : p.x[xi]) : 0.0f;
-    const int64_t cu = (int64_t) chunk * p.n_units + u;  // this chunk's unit
-    __shared__ unsigned long long red[8];
-    __shared__ float s_max;
-    unsigned long long key = ((unsigned long long) __float_as_uint(fabsf(x)) << 32) | (unsigned) (255 - t);
+    const int64_t cu = (int64_t) chunk * p.n_units + u;      // this chunk's unit
+    float x[8];
+    if (rg < p.rows) {
+        const float4 * src = reinterpret_cast<const float4 *>(p.x + (int64_t) rg * K + (int64_t) u * kQmmUnit) + 2 * lane;
+        const float4 a = src[0], b = src[1];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        if (p.x_up) {
+            const float4 * up =
+                reinterpret_cast<const float4 *>(p.x_up + (int64_t) rg * K + (int64_t) u * kQmmUnit) + 2 * lane;
+            const float4 c = up[0], e = up[1];
+            const float uv[8] = {c.x, c.y, c.z, c.w, e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = swiglu_value(x[i], uv[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = 0.0f;
+    }
+    // the value of largest magnitude, first column on ties: key = |x| bits, then
+    // the inverted column (non-negative floats order as integers)
+    unsigned long long key = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const unsigned long long kx =
+            ((unsigned long long) __float_as_uint(fabsf(x[i])) << 32) | (unsigned) (255 - (8 * lane + i));
+        key = kx > key ? kx : key;
+    }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
         const unsigned long long other = __shfl_xor_sync(kFull, key, o);
         key = other > key ? other : key;
     }
-    if (lane == 0) red[warp] = key;
-    __syncthreads();
-    unsigned long long best = red[0];
+    const int arg = 255 - (int) (key & 0xffffffffu);
+    float mine = x[0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) best = red[w] > best ? red[w] : best;
-    const int arg = 255 - (int) (best & 0xffffffffu);
-    if (t == arg) s_max = x;
-    __syncthreads();
-    const float amax = __uint_as_float((unsigned) (best >> 32));
-    int q = 0;
+    for (int i = 1; i < 8; ++i)
+        if ((arg & 7) == i) mine = x[i];
+    const float s_max = __shfl_sync(kFull, mine, arg >> 3);
+    const float amax = __uint_as_float((unsigned) (key >> 32));
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float d = 0.0f;
     if (amax != 0.0f) {
         const float iscale = __fdiv_rn(-127.0f, s_max);
-        q = min(127, __float2int_rn(__fmul_rn(iscale, x)));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, x[i])));
         d = __fdiv_rn(1.0f, iscale);
     }
     const int np = p.npad;
     uint8_t * tile = p.b_tiles + cu * np * 512;
-    *reinterpret_cast<__half *>(tile + tc_tile_off(r, tc_position(t), np)) = __int2half_rn(q);
-    int s = q;
+    int sum = 0;
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
-    if (lane == 0) {
-        // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j)
-        uint8_t * mrow = p.bmin_tiles + cu * np * 128 + (r >> 3) * 1024 + (r & 7) * 128;
-        *reinterpret_cast<__half *>(mrow + ((0 ^ (r & 7)) << 4) + warp * 2) = __int2half_rn(s & 127);
-        *reinterpret_cast<__half *>(mrow + ((1 ^ (r & 7)) << 4) + warp * 2) = __int2half_rn(s >> 7);
+    for (int i = 0; i < 8; ++i) {
+        *reinterpret_cast<__half *>(tile + tc_tile_off(r, tc_position(8 * lane + i), np)) = __int2half_rn(q[i]);
+        sum += q[i];
     }
-    if (t == 0) p.dx[cu * np + r] = d;
+    sum += __shfl_xor_sync(kFull, sum, 1);
+    sum += __shfl_xor_sync(kFull, sum, 2);
+    if ((lane & 3) == 0) {
+        // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j)
+        const int j = lane >> 2;
+        uint8_t * mrow = p.bmin_tiles + cu * np * 128 + (r >> 3) * 1024 + (r & 7) * 128;
+        *reinterpret_cast<__half *>(mrow + ((0 ^ (r & 7)) << 4) + j * 2) = __int2half_rn(sum & 127);
+        *reinterpret_cast<__half *>(mrow + ((1 ^ (r & 7)) << 4) + j * 2) = __int2half_rn(sum >> 7);
+    }
+    if (lane == 0) p.dx[cu * np + r] = d;
 }
 
 // One half (128 columns) of a Q6_K unit for row r into TMEM: A_hi = 16*(sc>>4)*q
@@ -807,7 +836,7 @@ cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream) {
     if (p.npad != 16 && p.npad != 32 && p.npad != 64) return cudaErrorInvalidValue;
     for (int i = 0; i < p.n_mats; ++i)
         if (p.mats[i].n_rows % 128 != 0) return cudaErrorInvalidValue;
-    cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) (p.npad * p.n_chunks)), 256, 0,
+    cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) (p.npad * p.n_chunks / 8)), 256, 0,
                               stream, p, 1);
     if (e != cudaSuccess) return e;
     switch (p.npad) {

@@ -156,51 +156,66 @@ __global__ void __launch_bounds__(kConvThreads) conv0_steady_kernel(const ConvPa
 }
 
 // conv1: encoder rows 4 s .. 4 s + 3 (positions 2 .. 5) from y0 positions 3 .. 11.
-__global__ void __launch_bounds__(kConvThreads) conv1_steady_kernel(const ConvParams p) {
+// 256 threads: thread t computes channel blockIdx.x * 128 + t % 128 for two of
+// the block's four streams (t / 128 picks which two).
+constexpr int kConv1Threads = 256;
+
+__global__ void __launch_bounds__(kConv1Threads) conv1_steady_kernel(const ConvParams p) {
     extern __shared__ __half sy2[];  // [kSteadyStreams][dim][10]: f16-rounded y0 positions 3 .. 11
     const int s0 = blockIdx.y * kSteadyStreams;
     const int ns = min(kSteadyStreams, p.n_streams - s0);
-    for (int i = threadIdx.x; i < ns * p.dim * 9; i += kConvThreads) {
+    for (int i = threadIdx.x; i < ns * p.dim * 9; i += kConv1Threads) {
         const int ss = i / (p.dim * 9), o = i - ss * p.dim * 9;
         const int ci = o / 9, rr = o - ci * 9;
         sy2[(ss * p.dim + ci) * 10 + rr] =
             __float2half_rn(p.y0[(int64_t) (s0 + ss) * p.max_win * p.dim + (int64_t) (3 + rr) * p.dim + ci]);
     }
     __syncthreads();
-    const int c = blockIdx.x * kConvThreads + threadIdx.x;
-    if (c >= p.dim) return;
-    float acc[kSteadyStreams][4];
+    // the two halves of the block take streams 0, 1 and 2, 3 of the group; each
+    // thread sums its column over all input channels in order, as conv1_kernel does
+    constexpr int kPer = kSteadyStreams / 2;
+    const int sb = (threadIdx.x >> 7) * kPer;
+    const int c = blockIdx.x * 128 + (threadIdx.x & 127);
+    if (c >= p.dim || sb >= ns) return;
+    float acc[kPer][4];
 #pragma unroll
-    for (int ss = 0; ss < kSteadyStreams; ++ss)
+    for (int ss = 0; ss < kPer; ++ss)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[ss][j] = 0.0f;
-    for (int ci = 0; ci < p.dim; ++ci) {
-        const float w0 = __half2float(p.w1[((int64_t) ci * 3 + 0) * p.dim + c]);
-        const float w1 = __half2float(p.w1[((int64_t) ci * 3 + 1) * p.dim + c]);
-        const float w2 = __half2float(p.w1[((int64_t) ci * 3 + 2) * p.dim + c]);
+    // weights of 8 input channels loaded before they are used: 24 independent
+    // loads in flight per thread (dim is a multiple of 8)
+    for (int ci0 = 0; ci0 < p.dim; ci0 += 8) {
+        float w[8][3];
 #pragma unroll
-        for (int ss = 0; ss < kSteadyStreams; ++ss) {
-            if (ss < ns) {
-                const __half * yr = sy2 + (ss * p.dim + ci) * 10;
-                float yv[9];
+        for (int uu = 0; uu < 8; ++uu)
 #pragma unroll
-                for (int m = 0; m < 9; ++m) yv[m] = __half2float(yr[m]);
+            for (int k = 0; k < 3; ++k) w[uu][k] = __half2float(p.w1[((int64_t) (ci0 + uu) * 3 + k) * p.dim + c]);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {  // output 2 + j reads y0 positions 3 + 2j + k
-                    acc[ss][j] = fmaf(w0, yv[2 * j], acc[ss][j]);
-                    acc[ss][j] = fmaf(w1, yv[2 * j + 1], acc[ss][j]);
-                    acc[ss][j] = fmaf(w2, yv[2 * j + 2], acc[ss][j]);
+        for (int uu = 0; uu < 8; ++uu) {
+#pragma unroll
+            for (int ss = 0; ss < kPer; ++ss) {
+                if (sb + ss < ns) {
+                    const __half * yr = sy2 + ((sb + ss) * p.dim + ci0 + uu) * 10;
+                    float yv[9];
+#pragma unroll
+                    for (int m = 0; m < 9; ++m) yv[m] = __half2float(yr[m]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {  // output 2 + j reads y0 positions 3 + 2j + k
+                        acc[ss][j] = fmaf(w[uu][0], yv[2 * j], acc[ss][j]);
+                        acc[ss][j] = fmaf(w[uu][1], yv[2 * j + 1], acc[ss][j]);
+                        acc[ss][j] = fmaf(w[uu][2], yv[2 * j + 2], acc[ss][j]);
+                    }
                 }
             }
         }
     }
     const float bias = p.b1[c];
 #pragma unroll
-    for (int ss = 0; ss < kSteadyStreams; ++ss)
-        if (ss < ns)
+    for (int ss = 0; ss < kPer; ++ss)
+        if (sb + ss < ns)
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-                p.x[(int64_t) (4 * (s0 + ss) + j) * p.dim + c] = gelu_erf_f(__fadd_rn(acc[ss][j], bias));
+                p.x[(int64_t) (4 * (s0 + sb + ss) + j) * p.dim + c] = gelu_erf_f(__fadd_rn(acc[ss][j], bias));
 }
 
 // Grid (column tiles, rows, 2): z = 0 adds b0 to the rows of y0, z = 1 b1 to y1.
@@ -224,7 +239,8 @@ cudaError_t launch_conv_stem(const ConvParams & p, cudaStream_t stream) {
                         (unsigned) ((p.n_streams + kSteadyStreams - 1) / kSteadyStreams));
         const size_t smem0 = (size_t) kSteadyStreams * p.n_mel * kSteadyWin * sizeof(float);
         const size_t smem1 = (size_t) kSteadyStreams * p.dim * 10 * sizeof(__half);
-        if (smem0 > 227 * 1024 || smem1 > 227 * 1024 || p.max_win < kSteadyWin) return cudaErrorInvalidValue;
+        if (smem0 > 227 * 1024 || smem1 > 227 * 1024 || p.max_win < kSteadyWin || p.dim % 8)
+            return cudaErrorInvalidValue;
         cudaError_t e = cudaFuncSetAttribute(conv0_steady_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int) smem0);
         if (e != cudaSuccess) return e;
@@ -233,7 +249,7 @@ cudaError_t launch_conv_stem(const ConvParams & p, cudaStream_t stream) {
         conv0_steady_kernel<<<grid, kConvThreads, smem0, stream>>>(p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
-        conv1_steady_kernel<<<grid, kConvThreads, smem1, stream>>>(p);
+        conv1_steady_kernel<<<grid, kConv1Threads, smem1, stream>>>(p);
         return cudaGetLastError();
     }
     const dim3 grid((unsigned) ((p.dim + kConvThreads - 1) / kConvThreads), (unsigned) p.n_streams);

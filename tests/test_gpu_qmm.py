@@ -199,6 +199,7 @@ def test_qweight_from_gguf_file(vxk, oracle, tmp_path):
 @pytest.mark.parametrize("t,n,k,rows", [
     (Q4_K, 1280, 1280, 512),   # the encoder's q of 128 streams x 4 frames, 8 chunks in one launch
     (Q6_K, 1280, 5120, 200),   # the encoder's w2, a ragged last chunk
+    (Q4_K, 1024, 2048, 130),   # three chunks, the last of 2 rows
     (Q8_0, 256, 512, 130),     # Q8_0 (int8 mma.sync): 64 rows per launch
 ])
 def test_many_rows_in_one_call(vxk, oracle, t, n, k, rows):
@@ -207,4 +208,5 @@ def test_many_rows_in_one_call(vxk, oracle, t, n, k, rows):
     x = rng.normal(0, 1, (rows, k)).astype(np.float32)
     (got,) = _run(vxk, w, t, n, k, x, max_batch=rows)
     _check(oracle, t, w, n, k, x, got)
+
 

@@ -333,7 +333,8 @@ void ecreate(vxk_encoder * e, const vxk_gguf * g, vxk_enc_pool * pool, int32_t m
 }
 
 void eproducts(vxk_encoder * e, vxk_qweight * const * ws, int n, const float * x, int64_t x_stride, int32_t rows,
-               float * const * ys, const int64_t * y_strides, cudaStream_t cs) {
+               float * const * ys, const int64_t * y_strides, cudaStream_t cs,
+               const float * const * biases = nullptr) {
     bool same = true;
     const bool fam0 = vxk::qweight_shape(ws[0]).type == VXK_QTYPE_Q8_0;
     for (int i = 1; i < n; ++i) same = same && ((vxk::qweight_shape(ws[i]).type == VXK_QTYPE_Q8_0) == fam0);
@@ -343,9 +344,12 @@ void eproducts(vxk_encoder * e, vxk_qweight * const * ws, int n, const float * x
         for (int i = 0; i < n; ++i) yc[i] = ys[i] + (int64_t) r0 * y_strides[i];
         const float * xc = x + (int64_t) r0 * x_stride;
         if (same) {
-            VXK_ECALL(vxk_qweight_matmul_group(ws, n, xc, nr, yc, cs), "quantized product");
+            VXK_ECALL((vxk_status) vxk::qweight_matmul_group_bias(ws, n, xc, nr, yc, biases, cs), "quantized product");
         } else {
-            for (int i = 0; i < n; ++i) VXK_ECALL(vxk_qweight_matmul(ws[i], xc, nr, yc[i], cs), "quantized product");
+            for (int i = 0; i < n; ++i)
+                VXK_ECALL((vxk_status) vxk::qweight_matmul_group_bias(&ws[i], 1, xc, nr, &yc[i],
+                                                                      biases ? &biases[i] : nullptr, cs),
+                          "quantized product");
         }
     }
 }
@@ -416,10 +420,9 @@ void eforward(vxk_encoder * e, const float * mel, float * out, cudaStream_t cs) 
             vxk_qweight * ws[3] = {L.q, L.k, L.v};
             float * ys[3] = {e->q, e->k, e->v};
             const int64_t st[3] = {qdim, qdim, qdim};
-            eproducts(e, ws, 3, e->xn, dim, rows, ys, st, cs);
+            const float * bs[3] = {L.bq, nullptr, L.bv};  // the q and v biases, added in the products' stores
+            eproducts(e, ws, 3, e->xn, dim, rows, ys, st, cs, bs);
         }
-        if (L.bq || L.bv)
-            VXK_ECUDA(vxk::launch_bias2(e->q, L.bq, L.bq ? qdim : 0, e->v, L.bv, L.bv ? qdim : 0, rows, cs));
         VXK_ECALL(vxk_enc_layer(e->pool, l, e->q, e->k, e->v, e->att, cs), "vxk_enc_layer");
         {
             vxk_qweight * ws[1] = {L.o};

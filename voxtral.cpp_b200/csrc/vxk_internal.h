@@ -307,6 +307,7 @@ struct QtcMat {
     int32_t block0;            // first 128-row block of this matrix in the grid
     int32_t type;              // 12 = Q4_K, 14 = Q6_K
     int32_t reserved;
+    const float * bias;        // nullptr, or [n_rows] fp32 added to every row of y after the column sum
 };
 
 struct QtcParams {
@@ -345,6 +346,11 @@ void qweight_attach_error(vxk_qweight * w, int32_t * word);
 // separate kernel would); 0 or a vxk_status number.
 int32_t qweight_matmul_swiglu(vxk_qweight * w, const float * gate, const float * up, int32_t rows, float * y,
                               cudaStream_t stream);
+// vxk_qweight_matmul_group, then y_i += bias_i on every row (ggml_mul_mat
+// then ggml_add: one rounded fp32 add); biases or any bias_i may be nullptr.
+// Matrices on the tcgen05 kernel add the bias in the product's store.
+int32_t qweight_matmul_group_bias(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows,
+                                  float * const * ys, const float * const * biases, cudaStream_t stream);
 // silu(g) * u with separately rounded steps (ggml_silu then ggml_mul,
 // src/voxtral.cpp:2877-2880), evaluated inside the activation quantization.
 #ifdef __CUDACC__

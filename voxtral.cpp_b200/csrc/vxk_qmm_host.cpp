@@ -371,7 +371,7 @@ void plan_split_tc(int32_t n_units, int32_t sms, int64_t blocks, vxk::QtcParams 
 }
 
 void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * x_up, int32_t rows,
-            float * const * ys, int32_t * error, cudaStream_t stream) {
+            float * const * ys, const float * const * biases, int32_t * error, cudaStream_t stream) {
     vxk_qweight * w0 = ws[0];
     vxk::QtcParams p{};
     p.n_mats = n;
@@ -387,6 +387,7 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * 
         p.mats[i].n_rows = ws[i]->cfg.n_rows;
         p.mats[i].block0 = block0;
         p.mats[i].type = (int32_t) ws[i]->cfg.type;
+        p.mats[i].bias = biases ? biases[i] : nullptr;
         block0 += ws[i]->cfg.n_rows / 128;
     }
     plan_split_tc(w0->n_units, w0->sms, (int64_t) block0 * p.n_chunks, p);
@@ -426,24 +427,30 @@ void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, const float 
 // and activation family): the matrices that take the tcgen05 kernel in one
 // launch, the others in one int8 mma.sync launch, each with its own
 // quantization of x (the two kernels read different operand layouts).
+// biases[i] (when given) is added to every row of ys[i]: in the tcgen05
+// product's store, or by a separate kernel after the mma.sync product.
 void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys,
-               cudaStream_t stream, const float * x_up = nullptr) {
+               cudaStream_t stream, const float * x_up = nullptr, const float * const * biases = nullptr) {
     // the quantization kernels read rows as float4
     if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(x_up) & 15))
         qfail(VXK_STATUS_INVALID_ARGUMENT, "x must be 16-byte aligned");
     vxk_qweight * tw[vxk::kQmmMaxGroup], * sw[vxk::kQmmMaxGroup];
     float * ty[vxk::kQmmMaxGroup], * sy[vxk::kQmmMaxGroup];
+    const float * tb[vxk::kQmmMaxGroup], * sb[vxk::kQmmMaxGroup];
     int nt = 0, ns = 0;
     for (int i = 0; i < n; ++i) {
+        const float * b = biases ? biases[i] : nullptr;
         if (use_tc(ws[i], rows)) {
             tw[nt] = ws[i];
+            tb[nt] = b;
             ty[nt++] = ys[i];
         } else {
             sw[ns] = ws[i];
+            sb[ns] = b;
             sy[ns++] = ys[i];
         }
     }
-    if (nt) run_tc(tw, nt, x, x_up, rows, ty, ws[0]->d_error, stream);
+    if (nt) run_tc(tw, nt, x, x_up, rows, ty, tb, ws[0]->d_error, stream);
     // the int8 mma.sync kernel takes at most 64 rows per launch
     const int64_t K = ws[0]->cfg.n_cols;
     for (int32_t r0 = 0; ns && r0 < rows; r0 += vxk::kQmmMaxBatch) {
@@ -452,6 +459,25 @@ void run_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t row
         for (int i = 0; i < ns; ++i) syc[i] = sy[i] + (int64_t) r0 * sw[i]->cfg.n_rows;
         run_sync(sw, ns, x + (int64_t) r0 * K, x_up ? x_up + (int64_t) r0 * K : nullptr, nr, syc, ws[0]->d_error,
                  stream);
+    }
+    for (int i = 0; i < ns; ++i)
+        if (sb[i]) VXK_QCUDA(vxk::launch_bias2(sy[i], sb[i], sw[i]->cfg.n_rows, nullptr, nullptr, 0, rows, stream));
+}
+
+// Argument checks of a group product (shared device, n_cols and activation
+// family; rows within every matrix's max_batch).
+void check_group(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows, float * const * ys) {
+    vxk_qweight * w0 = ws[0];
+    if (!x) qfail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+    const bool fam0 = w0->cfg.type == VXK_QTYPE_Q8_0;
+    for (int32_t i = 0; i < n; ++i) {
+        const vxk_qweight_config & c = ws[i]->cfg;
+        if (!ys[i]) qfail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        if (c.device != w0->cfg.device || c.n_cols != w0->cfg.n_cols)
+            qfail(VXK_STATUS_INVALID_ARGUMENT, "group matrices must share device and n_cols");
+        if ((c.type == VXK_QTYPE_Q8_0) != fam0)
+            qfail(VXK_STATUS_INVALID_ARGUMENT, "a group is all Q8_0 or all K-quants (one x quantization)");
+        if (rows < 1 || rows > c.max_batch) qfail(VXK_STATUS_INVALID_ARGUMENT, "rows must be in [1, max_batch]");
     }
 }
 
@@ -475,6 +501,18 @@ int32_t qweight_matmul_swiglu(vxk_qweight * w, const float * gate, const float *
         vxk_qweight * one[1] = {w};
         float * yv[1] = {y};
         run_group(one, 1, gate, rows, yv, stream, up);
+    });
+}
+
+int32_t qweight_matmul_group_bias(vxk_qweight * const * ws, int32_t n, const float * x, int32_t rows,
+                                  float * const * ys, const float * const * biases, cudaStream_t stream) {
+    if (!ws || n < 1 || n > kQmmMaxGroup || !ys) return VXK_STATUS_INVALID_ARGUMENT;
+    for (int32_t i = 0; i < n; ++i)
+        if (!ws[i]) return VXK_STATUS_INVALID_ARGUMENT;
+    return qguarded(ws[0], [&] {
+        check_group(ws, n, x, rows, ys);
+        QwDevice scope(ws[0]->cfg.device);
+        run_group(ws, n, x, rows, ys, stream, nullptr, biases);
     });
 }
 
@@ -629,17 +667,7 @@ vxk_status vxk_qweight_matmul_group(vxk_qweight * const * ws, int32_t n, const f
         if (!ws[i]) return VXK_STATUS_INVALID_ARGUMENT;
     vxk_qweight * w0 = ws[0];
     return qguarded(w0, [&] {
-        if (!x) qfail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
-        const bool fam0 = w0->cfg.type == VXK_QTYPE_Q8_0;
-        for (int32_t i = 0; i < n; ++i) {
-            const vxk_qweight_config & c = ws[i]->cfg;
-            if (!ys[i]) qfail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
-            if (c.device != w0->cfg.device || c.n_cols != w0->cfg.n_cols)
-                qfail(VXK_STATUS_INVALID_ARGUMENT, "group matrices must share device and n_cols");
-            if ((c.type == VXK_QTYPE_Q8_0) != fam0)
-                qfail(VXK_STATUS_INVALID_ARGUMENT, "a group is all Q8_0 or all K-quants (one x quantization)");
-            if (rows < 1 || rows > c.max_batch) qfail(VXK_STATUS_INVALID_ARGUMENT, "rows must be in [1, max_batch]");
-        }
+        check_group(ws, n, x, rows, ys);
         QwDevice scope(w0->cfg.device);
         run_group(ws, n, x, rows, ys, static_cast<cudaStream_t>(cuda_stream));
     });

@@ -240,10 +240,11 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
 
 // Sums column-major partial blocks [cols][R] of the S cluster CTAs (same
 // shared-memory offset `local` in each) for elements [4*e0, 4*e1), in split
-// order, four rows per load; every split's loads are issued before the sum.
+// order, four rows per load; every split's loads are issued before the sum;
+// then adds bias[row0 + row] when bias is given.
 template <int R>
 __device__ __forceinline__ void cluster_reduce_store(uint32_t local, int S, int e0, int e1, int tid, int nthreads,
-                                                     float * y, int64_t n_rows, int64_t row0) {
+                                                     float * y, int64_t n_rows, int64_t row0, const float * bias) {
     const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
     for (int e = e0 + tid; e < e1; e += nthreads) {
         float4 v[kQmmMaxSplits];
@@ -260,6 +261,13 @@ __device__ __forceinline__ void cluster_reduce_store(uint32_t local, int S, int 
                 s.w += v[sp].w;
             }
         const int col = (4 * e) / R, row = (4 * e) % R;
+        if (bias) {
+            const float * b = bias + row0 + row;
+            s.x = __fadd_rn(s.x, b[0]);
+            s.y = __fadd_rn(s.y, b[1]);
+            s.z = __fadd_rn(s.z, b[2]);
+            s.w = __fadd_rn(s.w, b[3]);
+        }
         float * dst = y + (int64_t) col * n_rows + row0 + row;
         if (vec) {
             *reinterpret_cast<float4 *>(dst) = s;
@@ -745,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         const int E4 = rows_c * 128 / 4;
         const int e0 = (int) ((int64_t) E4 * split / S), e1 = (int) ((int64_t) E4 * (split + 1) / S);
         cluster_reduce_store<128>(smem_u32(ptile), S, e0, e1, tid, kThreads, m.y + (int64_t) chunk * N * m.n_rows,
-                                  m.n_rows, (int64_t) blk * 128);
+                                  m.n_rows, (int64_t) blk * 128, m.bias);
     }
     cluster_sync();
     if (warp == 0) {

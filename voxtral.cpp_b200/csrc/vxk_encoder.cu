@@ -18,10 +18,12 @@
 // tensor-map boxes.
 //
 // Work unit = (row group, head).  Persistent CTAs, one per SM, walk their
-// units through a warp-specialised pipeline (7 warps):
+// units through a warp-specialised pipeline (8 warps):
 //   warp 4     TMA producer: 16 KB stages (128 keys of K or V) into a
 //              10-stage shared-memory ring
-//   warp 5     tcgen05.mma issuer (one lane)
+//   warp 5     tcgen05.mma issuer of S^T = K.Q^T (one lane)
+//   warp 7     tcgen05.mma issuer of O^T += V^T.P^T (one lane): the two
+//              products of consecutive units are issued side by side
 //   warp 6     Q^T producer (RoPE, scale, bf16 hi/lo split)
 //   warps 0-3  own TMEM lane quadrants 0-3: softmax and epilogue
 // Per unit, two phases with an exact softmax (no online rescaling):
@@ -47,7 +49,7 @@ namespace vxk {
 namespace {
 
 constexpr int kEncHd = 64;
-constexpr int kTcThreads = 224;         // 7 warps
+constexpr int kTcThreads = 256;         // 8 warps
 constexpr int kTcStages = 10;
 constexpr int kTcMaxTiles = 6;          // keys per group <= 6 x 128
 constexpr int kTcBoxes = 16;            // 8-slot boxes per 128-key tile
@@ -73,7 +75,7 @@ constexpr int kBarPFull = kBarSEmpty + 2;      // [2] P^T written
 constexpr int kBarPEmpty = kBarPFull + 2;      // [2] PV MMAs done reading P^T
 constexpr int kBarOFull = kBarPEmpty + 2;      // [2] O^T complete in TMEM
 constexpr int kBarOEmpty = kBarOFull + 2;      // [2] O^T read by the epilogue
-constexpr int kBarDrain = kBarOEmpty + 2;      // all MMAs of the CTA done
+constexpr int kBarDrain = kBarOEmpty + 2;      // all MMAs of the CTA done (both issuers)
 constexpr int kNumBars = kBarDrain + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;                 // tmem addr, abort flag
 constexpr int kOffRed = kOffMisc + 16;                           // max [4][8], sums [2][4][8]
@@ -334,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             mbar_init(&bars[kBarOFull + b], 1);
             mbar_init(&bars[kBarOEmpty + b], 128);
         }
-        mbar_init(&bars[kBarDrain], 1);
+        mbar_init(&bars[kBarDrain], 2);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -404,9 +406,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             }
         }
         __syncwarp();
-    } else if (warp == 5) {
-        // ---------------- tcgen05.mma issuer ----------------
+    } else if (warp == 5 || warp == 7) {
+        // ---------------- tcgen05.mma issuers: S (warp 5), PV (warp 7) ----------------
         if (lane == 0) {
+            const bool s_role = warp == 5;
             constexpr uint32_t fmt = DT == 30 ? 1u : 0u;  // BF16 / F16 operands
             // fp32 accumulate.  S: M = 128 keys, N = 16, K-major A.  PV: M = 128 (dims of
             // keys 0-63, then dims of keys 64-127: the V tile's two 64-key halves are two
@@ -479,17 +482,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
                 tc_commit(&bars[kBarOFull + b]);
                 return true;
             };
+            // Ring loads in the producer's order: K tiles of unit i at [kc, kc + T_i),
+            // then V tiles of unit i - 1 at [kc + T_i, kc + T_i + T_(i-1)); each
+            // issuer walks the same sequence and consumes its own tiles.
             bool ok = true;
             EncUnit prev{};
             int i = 0;
+            uint32_t kc = 0;
             for (int u = blockIdx.x; ok && u < n_units; u += stride, ++i) {
                 const EncUnit U = enc_unit(p, u, vslots);
-                ok = s_unit(U, i);
-                if (ok && i > 0) ok = pv_unit(prev, i - 1);
+                if (s_role) {
+                    c = kc;
+                    ok = s_unit(U, i);
+                } else if (i > 0) {
+                    c = kc + (uint32_t) U.T;
+                    ok = pv_unit(prev, i - 1);
+                }
+                kc += (uint32_t) U.T + (i > 0 ? (uint32_t) prev.T : 0u);
                 prev = U;
             }
-            if (ok && i > 0) pv_unit(prev, i - 1);
+            if (!s_role && ok && i > 0) {
+                c = kc;
+                pv_unit(prev, i - 1);
+            }
             // every MMA issued so far completes before the CTA frees TMEM
+            // (the barrier completes once both issuers' MMAs are done)
             tc_commit(&bars[kBarDrain]);
             enc_drain(&bars[kBarDrain], 0);
         }

@@ -610,13 +610,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             float mx[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
+            // slot and absolute position of key row r: for the boxes walked
+            // (gb < nb) s0 + 8 gb < 2 vslots and (we % cap) - slot + cap lies in
+            // (0, 2 cap), so one conditional subtraction replaces each modulo;
+            // the other rows are masked whatever they compute
+            const int wem = U.we % cap;
 #pragma unroll
             for (int t = 0; t < kTcMaxTiles; ++t) {
                 if (t >= U.T) break;
                 const int gb = t * kTcBoxes + (r >> 3);
-                const int slot = (U.s0 + 8 * gb) % vslots + (r & 7);
+                int sb = U.s0 + 8 * gb;
+                sb = sb >= vslots ? sb - vslots : sb;
+                const int slot = sb + (r & 7);
                 bool valid = have_s && gb < U.nb && slot < cap;
-                const int kp = U.we - (((U.we % cap) - slot + cap) % cap);
+                int back = wem - slot + cap;
+                back = back >= cap ? back - cap : back;
+                const int kp = U.we - back;
                 valid = valid && kp >= U.ws;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {

@@ -175,6 +175,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The same load without the wait (tcgen05.wait::ld before using the values).
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ float2 enc_rope_pair(float2 x, float2 cs) {
     float2 r;
     r.x = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(x.y, cs.y));
@@ -559,13 +570,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             for (int q = 0; q < 8; ++q) ov[q] = 0.0f;
             const int half = warp >> 1;  // lanes 0-63: keys 0-63 of each tile; lanes 64-127: keys 64-127
             if (have_o) {
+                uint32_t acc[4][16];
 #pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    float acc[16];
-                    tmem_ld16(tmem + 192 + 128 * b + 32 * a + 16 * half + lane_off, acc);
+                for (int a = 0; a < 4; ++a) tmem_ld16_nw(tmem + 192 + 128 * b + 32 * a + 16 * half + lane_off, acc[a]);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) ov[q] += acc[q] + acc[8 + q];
-                }
+                for (int a = 0; a < 4; ++a)
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) ov[q] += __uint_as_float(acc[a][q]) + __uint_as_float(acc[a][8 + q]);
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarOEmpty + b]);

@@ -322,7 +322,7 @@ struct QtcParams {
     const float * x;           // [rows][K] fp32
     const float * x_up;        // nullptr, or [rows][K]: the row is silu(x) * x_up (SwiGLU)
     uint8_t * b_tiles;         // [n_units][npad x 256 f16, 4 SW128 atoms]
-    uint8_t * bmin_tiles;      // [n_units][npad rows of 128 B, SW128; K 0..15 used]
+    uint8_t * bmin_tiles;      // [n_units][npad rows x 16 f16, unswizzled K-major core matrices (32 B per row)]
     float * dx;                // [n_units][npad]
     int32_t * error;
 };

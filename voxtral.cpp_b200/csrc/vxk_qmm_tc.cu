@@ -53,7 +53,7 @@ constexpr unsigned kFull = 0xffffffffu;
 // shared-memory map (offsets from a 1024-aligned base)
 constexpr int kRawBytes = kQtcRecordBytesQ6K;                      // ring stage: the larger record
 constexpr int kActB = kMaxN * 512;                                  // f16 B tile, 4 SW128 atoms
-constexpr int kActBMin = kMaxN * 128;                               // mins B tile (32 B used per row)
+constexpr int kActBMin = kMaxN * 32;                                // mins B tile, 32 B per row (no swizzle)
 constexpr int kActStage = kActB + kActBMin;
 constexpr int kAMin = 128 * 128;                                    // mins A tile
 constexpr int kOffRaw = 0;
@@ -164,6 +164,13 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t) ((saddr >> 4) & 0x3FFFu) | ((uint64_t) ((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t) ((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// The same without swizzle: K-major core matrices of 8 rows x 16 B, lbo
+// bytes between the two K halves of a row group, sbo between row groups.
+__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t) ((saddr >> 4) & 0x3FFFu) | ((uint64_t) ((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t) ((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
 // D (TMEM) (+)= A (TMEM) . B (shared memory descriptor), kind::f16.
@@ -379,11 +386,12 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     sum += __shfl_xor_sync(kFull, sum, 1);
     sum += __shfl_xor_sync(kFull, sum, 2);
     if ((lane & 3) == 0) {
-        // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j)
+        // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j); unswizzled
+        // K-major core matrices: row group r / 8 at 256 B, K half at 128 B, row r % 8 at 16 B
         const int j = lane >> 2;
-        uint8_t * mrow = p.bmin_tiles + cu * np * 128 + (r >> 3) * 1024 + (r & 7) * 128;
-        *reinterpret_cast<__half *>(mrow + ((0 ^ (r & 7)) << 4) + j * 2) = __int2half_rn(sum & 127);
-        *reinterpret_cast<__half *>(mrow + ((1 ^ (r & 7)) << 4) + j * 2) = __int2half_rn(sum >> 7);
+        uint8_t * mrow = p.bmin_tiles + cu * np * 32 + (r >> 3) * 256 + (r & 7) * 16;
+        *reinterpret_cast<__half *>(mrow + j * 2) = __int2half_rn(sum & 127);
+        *reinterpret_cast<__half *>(mrow + 128 + j * 2) = __int2half_rn(sum >> 7);
     }
     if (lane == 0) p.dx[cu * np + r] = d;
 }
@@ -676,9 +684,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 if (!tc_wait(&bars[kBarActEmpty + t], ((uint32_t) (i / kActStages) & 1u) ^ 1u, abort_flag, p.error))
                     break;
                 uint8_t * st = base + kOffAct + t * kActStage;
-                mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 128));
+                mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 32));
                 bulk_g2s(st, p.b_tiles + (cbase + u) * N * 512, N * 512, &bars[kBarActFull + t], pol);
-                bulk_g2s(st + kActB, p.bmin_tiles + (cbase + u) * N * 128, N * 128, &bars[kBarActFull + t], pol);
+                bulk_g2s(st + kActB, p.bmin_tiles + (cbase + u) * N * 32, N * 32, &bars[kBarActFull + t], pol);
             }
             if (*abort_flag)
                 for (int d = i > kActStages ? i - kActStages : 0; d < i; ++d)
@@ -723,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                             mma_ts(dacc, tmem + 128 * b + 8 * ks,
                                    sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024), idesc, ks != 0);
                         mma_ss(tmem + 384 + 64 * bd, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
-                               sw128_desc(bt + kActB, 16, 1024), idesc, 0);
+                               plain_desc(bt + kActB, 128, 256), idesc, 0);
                     }
                     tc_commit(&bars[kBarAEmpty + b]);
                 }

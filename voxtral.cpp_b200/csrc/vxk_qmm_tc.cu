@@ -592,20 +592,35 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         uint32_t ddn = nu > 0 ? __ldg(dd) : 0u;
         // d_x of each unit straight from global memory (written by the
         // quantization kernel: wait for it), so an activation stage is free
-        // as soon as its MMAs complete
+        // as soon as its MMAs complete.  Lane l holds d_x of activation rows l
+        // and 32 + l (xa, xb), loaded one unit ahead; the FMAs take them by
+        // shuffle, so no L2 round trip sits between the accumulators' arrival
+        // and their use.
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        const float * dxu = p.dx + (cbase + u0) * N;
+        float xa = 0.0f, xb = 0.0f;
+        if (nu > 0) {
+            if (lane < N) xa = __ldg(dxu + lane);
+            if (N > 32) xb = __ldg(dxu + 32 + lane);
+        }
         float acc[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) acc[j] = 0.0f;
         for (int i = 0; i < nu; ++i) {
             const int b = i & 1;
             const uint32_t ddc = ddn;
-            if (i + 1 < nu) ddn = __ldg(dd + (int64_t) (i + 1) * 128);
+            float na = 0.0f, nb = 0.0f;
+            if (i + 1 < nu) {
+                ddn = __ldg(dd + (int64_t) (i + 1) * 128);
+                if (lane < N) na = __ldg(dxu + (int64_t) (i + 1) * N + lane);
+                if (N > 32) nb = __ldg(dxu + (int64_t) (i + 1) * N + 32 + lane);
+            }
             const bool ok = tc_wait(&bars[kBarDFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error);
             if (!__all_sync(kFull, ok)) break;
             tc_fence_after();
             const float2 dw = __half22float2(*reinterpret_cast<const __half2 *>(&ddc));  // (d, dmin)
-            const float * dx = p.dx + (cbase + u0 + i) * N;
+            // d_x of activation row e of this unit
+            auto dxe = [&](int e) { return __shfl_sync(kFull, e < 32 ? xa : xb, e & 31); };
             if (m.type == 14) {
                 // Q6_K: acc += (d_w * d_x) * D
 #pragma unroll
@@ -619,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     for (int hh = 0; hh < W / 16; ++hh)
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj)
-                            acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dx[c0 + 16 * hh + jj]),
+                            acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dxe(c0 + 16 * hh + jj)),
                                                           __uint_as_float(v[hh][jj]), acc[c0 + 16 * hh + jj]);
                 }
             } else {
@@ -638,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 for (int h = 0; h < W / 16; ++h)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float x = dx[c0 + 16 * h + j];
+                        const float x = dxe(c0 + 16 * h + j);
                         acc[c0 + 16 * h + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[h][j]),
                                                     fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[h][j]),
                                                          acc[c0 + 16 * h + j]));
@@ -647,6 +662,8 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarDEmpty + b]);
+            xa = na;
+            xb = nb;
         }
         // Partial block into the raw ring: every raw read of this CTA happened
         // before the last unit's MMAs, which this thread has waited for.

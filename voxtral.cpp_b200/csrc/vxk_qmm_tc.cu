@@ -29,8 +29,11 @@
 //               accumulators, fp32 block factors into registers
 //   warp 8      bulk copies of the raw weight records (HBM stream, evict-first)
 //   warp 9      bulk copies of the quantized activations (L2)
-//   warp 10     tcgen05.mma issuer: 16 MMAs (M = 128, N = rows padded to 16,
-//               K = 16, A from TMEM) + 1 mins MMA per unit
+//   warps 10-11 tcgen05.mma issuers: 16 MMAs (M = 128, N = rows padded to 16,
+//               K = 16, A from TMEM) + 1 mins MMA per unit; for Q4_K warp 10
+//               issues the even units and warp 11 the odd ones (every buffer
+//               and barrier of a unit alternates with its parity), for Q6_K
+//               (both A buffers per unit) warp 10 issues them all
 // Column splits of a 128-row block are one thread-block cluster and reduce
 // their partial blocks through distributed shared memory, in split order.
 #include "vxk_internal.h"
@@ -43,9 +46,9 @@
 namespace vxk {
 namespace {
 
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kRawStages = 4;
-constexpr int kActStages = 2;
+constexpr int kActStages = 2;  // = 2: a Q4_K unit's stage is its parity, like its A and D buffers
 constexpr int kMaxN = 64;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr unsigned kFull = 0xffffffffu;
@@ -74,6 +77,7 @@ constexpr int kNumBars = kBarDrain + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;       // tmem base, abort flag
 constexpr int kSmem = kOffMisc + 16 + 1024;            // + alignment slack
 static_assert(kSmem <= 232448, "tcgen05 quantized product exceeds 227 KB of shared memory");
+static_assert(kActStages == 2, "the two MMA issuers split Q4_K units by parity");
 static_assert(kRawStages * kRawBytes >= kMaxN * 128 * 4, "the reduction tile fits the raw ring");
 static_assert(kOffAct % 1024 == 0 && kOffAMin % 1024 == 0 && kActStage % 1024 == 0, "128-byte swizzle atoms align");
 // TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] 384..511
@@ -490,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             mbar_init(&bars[kBarDFull + b], 1);
             mbar_init(&bars[kBarDEmpty + b], 128);
         }
-        mbar_init(&bars[kBarDrain], 1);
+        mbar_init(&bars[kBarDrain], 2);  // one commit per issuer
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -711,16 +715,19 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         }
         __syncwarp();
     } else {
-        // ---------------- tcgen05.mma issuer ----------------
+        // ---------------- tcgen05.mma issuers (warps 10, 11) ----------------
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         if (lane == 0) {
             // fp32 D, f16 A and B, both K-major, N, M = 128
             const uint32_t idesc = (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
             const bool q6 = m.type == 14;
             const int phases = q6 ? 2 : 1;
-            int j = 0;
+            const int which = warp - 10;
+            // Q4_K: units of this issuer's parity; Q6_K: warp 10 takes every unit
+            const int first = q6 ? (which == 0 ? 0 : nu) : which, step = q6 ? 1 : 2;
             bool stop = false;
-            for (int i = 0; i < nu && !stop; ++i) {
+            for (int i = first; i < nu && !stop; i += step) {
+                int j = phases * i;  // A phase of the unit's first half
                 const int bd = i & 1, t = i % kActStages;
                 if (!tc_wait(&bars[kBarActFull + t], (uint32_t) (i / kActStages) & 1u, abort_flag, p.error)) break;
                 if (!tc_wait(&bars[kBarDEmpty + bd], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error)) break;
@@ -756,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                 tc_commit(&bars[kBarActEmpty + t]);
                 tc_commit(&bars[kBarDFull + bd]);
             }
-            // every MMA issued completes before the CTA frees TMEM
+            // every MMA issued (by both issuers) completes before the CTA frees TMEM
             tc_commit(&bars[kBarDrain]);
             tc_drain(&bars[kBarDrain], 0);
         }

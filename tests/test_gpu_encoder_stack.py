@@ -66,14 +66,18 @@ def _window(mel, q0, n):
     return out
 
 
-@pytest.mark.parametrize("dtype", [BF16, F16])
-def test_encoder_stack_matches_oracle(vxk, tmp_path, dtype):
+@pytest.mark.parametrize("dtype,kind", [(BF16, "q4_k_m"), (F16, "q4_k_m"), (BF16, "q8_0")])
+def test_encoder_stack_matches_oracle(vxk, tmp_path, dtype, kind):
+    # q4_k_m: the products on the tcgen05 kernel, the q/v biases added in its
+    # store; q8_0: every product on the int8 mma.sync kernel, biases added by
+    # the separate bias kernel after it
     import torch
     import decoder_model
     import vx_decoder as vd
 
     path = tmp_path / "enc.gguf"
-    t = decoder_model.build_encoder(path, 21)
+    types = decoder_model.Q4_K_M if kind == "q4_k_m" else decoder_model.Q8_0_ALL
+    t = decoder_model.build_encoder(path, 21, types=types)
     cfg = dict(n_layers=2, n_heads=8, head_dim=64, window=750, capacity=878, max_streams=4, max_new=8, dtype=dtype,
                max_position=4096)
     pool = vxk.EncPool(**cfg)

@@ -33,7 +33,10 @@
 //               K = 16, A from TMEM) + 1 mins MMA per unit; for Q4_K warp 10
 //               issues the even units and warp 11 the odd ones (every buffer
 //               and barrier of a unit alternates with its parity), for Q6_K
-//               (both A buffers per unit) warp 10 issues them all
+//               (both A buffers per unit) warp 10 issues them all: a second
+//               waiter on an A buffer would wait for its completion k + 1
+//               while completion k is still pending, and a parity wait cannot
+//               tell that from the phase before k (it passes at once)
 // Column splits of a 128-row block are one thread-block cluster and reduce
 // their partial blocks through distributed shared memory, in split order.
 #include "vxk_internal.h"

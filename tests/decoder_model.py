@@ -144,3 +144,15 @@ def build_encoder(path: Path, seed: int, n_layers: int = 2, dim: int = 512, n_he
     w.write_tensors_to_file()
     w.close()
     return t
+
+
+def mel_window(mel: np.ndarray, q0: int, n: int) -> np.ndarray:
+    """The conv stem's input for encoder rows q0 .. q0 + n - 1 of one stream:
+    mel frames 2 (q0 - 2) .. 2 (q0 + n) - 1, channel-major, zeros before frame 0."""
+    win = 2 * n + 4
+    out = np.zeros((mel.shape[0], win), np.float32)
+    f0 = 2 * (q0 - 2)
+    for i in range(win):
+        if f0 + i >= 0:
+            out[:, i] = mel[:, f0 + i]
+    return out

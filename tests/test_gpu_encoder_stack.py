@@ -55,17 +55,6 @@ class DeviceEncAttention:
         self.pool.close()
 
 
-def _window(mel, q0, n):
-    """Mel frames 2 (q0 - 2) .. 2 (q0 + n) - 1 channel-major, zeros before frame 0."""
-    win = 2 * n + 4
-    out = np.zeros((mel.shape[0], win), np.float32)
-    f0 = 2 * (q0 - 2)
-    for i in range(win):
-        if f0 + i >= 0:
-            out[:, i] = mel[:, f0 + i]
-    return out
-
-
 @pytest.mark.parametrize("dtype,kind", [(BF16, "q4_k_m"), (F16, "q4_k_m"), (BF16, "q8_0")])
 def test_encoder_stack_matches_oracle(vxk, tmp_path, dtype, kind):
     # q4_k_m: the products on the tcgen05 kernel, the q/v biases added in its
@@ -98,7 +87,7 @@ def test_encoder_stack_matches_oracle(vxk, tmp_path, dtype, kind):
         ids = [streams[i] for i, _ in step]
         ns = [n for _, n in step]
         rows = pool.plan(ids, ns, cs)
-        batch = [(s, nxt[s], n, _window(mel[s], nxt[s], n)) for s, n in zip(ids, ns)]
+        batch = [(s, nxt[s], n, decoder_model.mel_window(mel[s], nxt[s], n)) for s, n in zip(ids, ns)]
         dmel = torch.from_numpy(np.concatenate([b[3].reshape(-1) for b in batch])).cuda()
         stem = torch.full((rows, enc.info["dim"]), float("nan"), device="cuda")
         enc.stem(dmel.data_ptr(), stem.data_ptr(), cs)

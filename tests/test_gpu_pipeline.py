@@ -22,16 +22,6 @@ BF16 = 30
 BAR = 5e-2
 
 
-def _window(mel, q0, n):
-    win = 2 * n + 4
-    out = np.zeros((mel.shape[0], win), np.float32)
-    f0 = 2 * (q0 - 2)
-    for i in range(win):
-        if f0 + i >= 0:
-            out[:, i] = mel[:, f0 + i]
-    return out
-
-
 def test_mel_to_token_pipeline(vxk, tmp_path):
     import torch
     import decoder_model
@@ -63,7 +53,7 @@ def test_mel_to_token_pipeline(vxk, tmp_path):
         q0 = 4 * chunk
         # encoder: 4 new frames per stream
         rows = epool.plan(es, [4] * n_streams, cs)
-        wins = [_window(m, q0, 4) for m in mel]
+        wins = [decoder_model.mel_window(m, q0, 4) for m in mel]
         dmel = torch.from_numpy(np.concatenate([w.reshape(-1) for w in wins])).cuda()
         eout = torch.empty((rows, enc_dim), device="cuda")
         enc.forward(dmel.data_ptr(), eout.data_ptr(), cs)

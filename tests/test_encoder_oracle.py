@@ -39,6 +39,7 @@ def _run(t, mel, chunks, window, dtype, n_layers=2, n_heads=4):
 
 @pytest.fixture(scope="module")
 def model(tmp_path_factory):
+    pytest.importorskip("gguf")
     import decoder_model
 
     path = tmp_path_factory.mktemp("enc") / "enc.gguf"

@@ -3,19 +3,26 @@
 
 One "step" = every stream appends one token and attends over its cache in all
 decoder layers (fused RoPE + K/V append + GQA flash-decoding attention per
-layer, through libvxk.so's C ABI).  Default workload = BASELINE config 2:
-64 streams per GPU, 30 layers (Voxtral-Mini-3B decoder shape: 32 q / 8 kv
-heads x 128), f16 cache in 16-token pages with a seeded random block table,
-contexts seeded uniform in [400, 4096].  Synthetic N(0, 0.5^2) activations.
+layer, through libvxk.so's C ABI).  Default workload: 64 streams per GPU,
+30 layers (Voxtral-Mini-3B decoder shape: 32 q / 8 kv heads x 128), f16 cache
+in 16-token pages with a seeded random block table, contexts seeded uniform
+in [400, 4096].  Synthetic N(0, 0.5^2) activations.  After the timed region
+a sample of the outputs (three streams, first and last layer) is compared
+with the CPU oracle and the result is printed in the line's "checked" key.
 
-Multi-GPU: one process per GPU (torchrun); the job has 64 streams per GPU,
-whose contexts are drawn once from the seed and dealt to ranks by
-longest-processing-time (vxk_shard.assign_streams); each rank owns its streams'
-pages (weak scaling, no data-path collective); timing is max over ranks.
+Multi-GPU: one process per GPU (torchrun).  The job's contexts are drawn once
+from the seed and dealt to ranks by longest-processing-time
+(vxk_shard.assign_streams); each rank owns its streams' pages (no data-path
+collective); timing is max over ranks, and every rank's time is reported.
+The default workload has 64 streams per GPU (weak scaling); `--config 3`
+(256 realtime streams) and `--config 5` (128 q8_0 streams) fix the job's
+total and shard it (strong scaling), running on each GPU the streams that
+fit its memory.
 
 `--impl reference` times the CPU restatement of the same path (the reference's
 ggml CPU backend cannot be built here: ggml is fetched at configure time and
-is absent) on the host cores, on rank 0.
+is absent) on the host cores, on rank 0, over streams taken from the same
+seeded context list.
 """
 from __future__ import annotations
 
@@ -33,17 +40,18 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "voxtral.cpp_b200"))
-from vxk_shard import assign_streams, max_over_ranks  # noqa: E402
+from vxk_shard import assign_streams, gather_over_ranks, max_over_ranks  # noqa: E402
 
 HD, NQ, NKV, BT = 128, 32, 8, 16
 CONFIGS = {
     # name: layers, streams per GPU, ctx range, dtype, capacity
     "2": dict(layers=30, streams=64, ctx=(400, 4096), dtype=1, capacity=8192,
               desc="3B decoder, 64 streams/GPU, ctx~U[400,4096], f16 16-token pages, random block table"),
-    "3": dict(layers=26, streams=64, ctx=(8192, 8192), dtype=1, capacity=8192,
-              desc="4B realtime decoder, full 8192-slot sliding rings (steady state: one eviction per step)"),
-    "5": dict(layers=30, streams=32, ctx=(8192, 32768), dtype=8, capacity=32768 + 1024,
-              desc="3B decoder, q8_0 cache, ctx~U[8192,32768] (streams that fit one GPU)"),
+    "3": dict(layers=26, total_streams=256, ctx=(8192, 8192), dtype=1, capacity=8192,
+              desc="4B realtime decoder, 256 streams sharded by stream, full 8192-slot sliding rings "
+                   "(steady state: one eviction per stream and step)"),
+    "5": dict(layers=30, total_streams=128, ctx=(8192, 32768), dtype=8, capacity=32768 + 1024,
+              desc="3B decoder, 128 streams sharded by stream, q8_0 cache, ctx~U[8192,32768]"),
     "head": dict(kind="head", rows=64, vocab=131072, dim=3072, dtype=1,
                  desc="greedy head: tied logits (131072 x 3072 f16 embeddings) + argmax for 64 streams/GPU, "
                       "logits written like the reference's decoder_logits"),
@@ -1276,15 +1284,17 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, warmup=0, dtype=1):
+def cpu_sample(layers, ctx0, seed, seconds=None, steps=None, warmup=0, dtype=1):
     """Times the CPU restatement (oracle/vx_cpu_step.c) of the same decode
-    step on all host cores, for an f16 (1) or q8_0 (8) cache.  Returns
-    (tokens/s, steps done, threads, mean context)."""
+    step on all host cores, for an f16 (1) or q8_0 (8) cache, over streams
+    whose starting contexts are `ctx0`.  Returns (tokens/s, steps done,
+    threads, mean context, algorithmic bytes/s)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import vx_oracle
 
     rng = np.random.default_rng(seed)
-    ctx0 = rng.integers(ctx_range[0], ctx_range[1] + 1, size=n_streams)
+    ctx0 = np.asarray(ctx0, dtype=np.int64)
+    n_streams = len(ctx0)
     total = (steps or 0) + warmup + 64
     cap = int(ctx0.max()) + total + 16
     if dtype == 8:
@@ -1304,7 +1314,7 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
     k = rng.standard_normal((n_streams, layers, NKV, HD), dtype=np.float32) * 0.5
     v = rng.standard_normal((n_streams, layers, NKV, HD), dtype=np.float32) * 0.5
     rope = vx_oracle.rope_table(cap + 1, HD, 1e6)
-    pos = ctx0.astype(np.int64)
+    pos = ctx0.copy()
     win = np.zeros(n_streams, dtype=np.int64)
     threads = os.cpu_count() or 1
     scale = float(np.float32(1.0 / np.sqrt(HD)))
@@ -1312,9 +1322,11 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
         vx_oracle.cpu_decode_step(dtype, kc, vc, q, k, v, pos, win, rope, scale, threads)
         pos += 1
     done = 0
+    nbytes = 0
     t0 = time.perf_counter()
     while True:
         vx_oracle.cpu_decode_step(dtype, kc, vc, q, k, v, pos, win, rope, scale, threads)
+        nbytes += layers * sum(algorithmic_bytes(int(p) + 1, dtype) for p in pos)
         pos += 1
         done += 1
         el = time.perf_counter() - t0
@@ -1323,13 +1335,50 @@ def cpu_sample(layers, n_streams, ctx_range, seed, seconds=None, steps=None, war
         if seconds is not None and el >= seconds:
             break
     el = time.perf_counter() - t0
-    return n_streams * done / el, done, threads, float(np.mean(ctx0))
+    return n_streams * done / el, done, threads, float(np.mean(ctx0)), nbytes / el
 
 
 def cpu_streams(dtype: int) -> int:
     """Streams in the CPU sample: 4, or 2 for the q8_0 config whose contexts
     (up to 32K positions x 30 layers) would otherwise need > 8 GB of host memory."""
     return 2 if dtype == 8 else 4
+
+
+def sample_contexts(ctx, n):
+    """n contexts taken from `ctx` at the centres of n equal quantile bins of
+    its sorted order, so the sample's mean context follows the job's."""
+    srt = sorted(int(c) for c in ctx)
+    return [srt[min(len(srt) - 1, int((i + 0.5) * len(srt) / n))] for i in range(n)]
+
+
+def job_layout(cfg, seed, world):
+    """The decode job: every stream's starting context, drawn once from the
+    seed, and the streams each rank owns (longest-processing-time).  Configs
+    with `total_streams` fix the job's total (strong scaling); the others have
+    `streams` per GPU (weak scaling).  Returns (ctx_all, parts, scaling)."""
+    rng = np.random.default_rng(seed)
+    lo, hi = cfg["ctx"]
+    if cfg.get("total_streams"):
+        total = int(cfg["total_streams"])
+        per = -(-total // world)
+        scaling = "strong"
+    else:
+        per = int(cfg["streams"])
+        total = per * world
+        scaling = "weak"
+    ctx_all = rng.integers(lo, hi + 1, size=total)
+    return ctx_all, assign_streams(ctx_all, world, per), scaling
+
+
+def decode_config(args, cfg, world, ctx_all, parts, scaling):
+    """The `config` object of a decode line: the same for both arms."""
+    per = max(len(p) for p in parts)
+    par = f"streams sharded by stream, {per}/GPU, no collective"
+    return {"workload": f"config {args.config}: {cfg['desc']}", "layers": cfg["layers"],
+            "streams_total": int(len(ctx_all)), "streams_per_gpu": per, "global_batch": int(len(ctx_all)),
+            "ctx_range": list(cfg["ctx"]), "mean_ctx_job": round(float(np.mean(ctx_all)), 1),
+            "scaling": scaling, "parallelism": par,
+            "l2": "inputs larger than L2 (KV read per launch >> 126 MB), no flush"}
 
 
 def encoder_cpu_sample(cfg, seed, seconds):
@@ -1447,10 +1496,11 @@ def run_reference(args, cfg, rank, world):
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
-    n_streams = cpu_streams(cfg["dtype"])
+    ctx_all, parts, scaling = job_layout(cfg, args.seed, world)
+    sample = sample_contexts(ctx_all[parts[0]], cpu_streams(cfg["dtype"]))
     budget = 150.0
-    tps, done, threads, mean_ctx = cpu_sample(cfg["layers"], n_streams, cfg["ctx"], args.seed, seconds=budget,
-                                              steps=args.steps, warmup=min(args.warmup, 3), dtype=cfg["dtype"])
+    tps, done, threads, mean_ctx, bps = cpu_sample(cfg["layers"], sample, args.seed, seconds=budget,
+                                                   steps=args.steps, warmup=min(args.warmup, 3), dtype=cfg["dtype"])
     line = {
         "impl": "reference",
         "metric": "decode tokens/s (KV append+GQA attn)",
@@ -1459,17 +1509,20 @@ def run_reference(args, cfg, rank, world):
         "n_gpus": args.gpus,
         "steps": done,
         "warmup": min(args.warmup, 3),
-        "ms_per_step": round(1000.0 * n_streams / tps, 3),
+        "ms_per_step": round(1000.0 * len(sample) / tps, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": ("q8_0" if cfg["dtype"] == 8 else "f16") + " cache, fp32 accumulate",
         "data": "synthetic",
-        "config": {"workload": f"config {args.config}: {cfg['desc']}", "layers": cfg["layers"],
-                   "streams_sampled": n_streams, "mean_ctx": mean_ctx},
+        "config": decode_config(args, cfg, world, ctx_all, parts, scaling),
+        "bytes_per_s": round(bps, 1),
         "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{n_streams} streams x {cfg['layers']} layers x {done} steps of the CPU "
-                                   f"restatement (oracle/vx_cpu_step.c), ggml absent"},
+                         "bytes_per_s": round(bps, 1),
+                         "sample": f"{len(sample)} streams of rank 0's share of the job (starting contexts "
+                                   f"{sample}, quantile centres of the job's seeded list, mean {mean_ctx:.0f}) x "
+                                   f"{cfg['layers']} layers x {done} steps of the CPU restatement "
+                                   f"(oracle/vx_cpu_step.c), ggml absent"},
         "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -1479,7 +1532,7 @@ def main():
     args = parse()
     cfg = dict(CONFIGS[args.config])
     if args.streams:
-        cfg["streams"] = args.streams
+        cfg["total_streams" if cfg.get("total_streams") else "streams"] = args.streams
         if cfg.get("kind") == "qmm":
             cfg["rows"] = args.streams
     if args.layers:
@@ -1543,21 +1596,81 @@ def main():
             dist.destroy_process_group()
         return
 
-    L, S = cfg["layers"], cfg["streams"]
-    dtype = cfg["dtype"]
-    # Contexts of the whole job are drawn once from the seed, then every rank
-    # takes its S streams by longest-processing-time on context length.
-    rng = np.random.default_rng(args.seed)
-    lo, hi = cfg["ctx"]
-    ctx_all = rng.integers(lo, hi + 1, size=S * world)
-    ctx0 = ctx_all[assign_streams(ctx_all, world, S)[rank]]
+    run_decode(args, cfg, world, rank, local, dist, torch, vxk)
+    if dist:
+        dist.destroy_process_group()
+
+
+def page_bytes(L: int, dtype: int) -> int:
+    """Device bytes of one 16-position page across every layer (K and V)."""
+    tile = BT * HD * 2 if dtype == 1 else BT * HD + BT * (HD // 32) * 2
+    return NKV * 2 * tile * L
+
+
+def oracle_check(pool, streams, ctx0, qs, ks, vs, out, st, L, dtype, sh):
+    """Checker run after the timed region: for three streams (shortest,
+    median and longest context) and the first and last layer, the row the
+    last timed step appended must equal the CPU oracle's bytes, and the
+    step's attention output must be within 2e-3 of the oracle's fp64
+    attention over the stream's cache as read back from the device.
+    Returns (max abs error, append bytes exact, rows checked)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vx_oracle
+
+    order = np.argsort(np.asarray(ctx0), kind="stable")
+    picks = sorted({int(order[0]), int(order[len(order) // 2]), int(order[-1])})
+    scale = float(np.float32(1.0 / np.sqrt(HD)))
+    err, exact, n = 0.0, True, 0
+    for j in picks:
+        r = pool.ring(streams[j])
+        pos, lo = r.next_absolute_position - 1, r.oldest_absolute_position
+        for layer in sorted({0, L - 1}):
+            kb, vb = pool.read_rows(layer, streams[j], lo, pos - lo + 1, sh)
+            q = qs[st, layer, j].cpu().numpy()
+            wk, wv = vx_oracle.kv_row(ks[st, layer, j].cpu().numpy(), vs[st, layer, j].cpu().numpy(), pos, 1e6,
+                                      dtype)
+            exact = exact and bool(np.array_equal(kb[-1], wk)) and bool(np.array_equal(vb[-1], wv))
+            want = vx_oracle.attn_row(q, pos, 1e6, kb, vb, dtype, NKV, scale)
+            err = max(err, float(np.abs(out[layer, j].cpu().numpy() - want).max()))
+            n += 1
+    return err, exact, n
+
+
+def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
+    L, dtype, cap = cfg["layers"], cfg["dtype"], cfg["capacity"]
+    ctx_all, parts, scaling = job_layout(cfg, args.seed, world)
+    mine = parts[rank]
     total_steps = args.warmup + args.steps * (1 if args.no_e2e else 2) + 2
-    cap = cfg["capacity"]
+    NSETS = 4
+    prefill_chunk = int(min(cap, 4096, ctx_all.max()))
+
+    def pages_of(c):
+        return min(cap // BT, (int(c) + total_steps) // BT + 2)
+
+    # The rank's streams that fit its memory, taken in index order: the
+    # per-step inputs, outputs, host-path staging, split scratch, fill
+    # buffers and a 3 GiB margin are set aside first.
+    free_b, total_b = torch.cuda.mem_get_info(local)
+    n_mine = len(mine)
+    max_rows = max(n_mine, prefill_chunk)
+    fixed = ((NSETS + 1) * L * n_mine * (NQ + 2 * NKV) * HD * 4
+             + (0 if args.no_e2e else L * n_mine * (2 * NQ + 2 * NKV) * HD * 4)
+             + max(2048, 8 * max_rows) * NQ * 132 * 4 + 2 * prefill_chunk * NKV * HD * 4 + (3 << 30))
+    budget = free_b - fixed
+    pb = page_bytes(L, dtype)
+    run, used = [], 0
+    for i in mine:
+        b = pages_of(ctx_all[i]) * pb
+        if used + b > budget:
+            break
+        run.append(i)
+        used += b
+    if not run:
+        raise RuntimeError(f"rank {rank}: no stream fits {free_b / 1e9:.1f} GB of free device memory")
+    S = len(run)
+    ctx0 = ctx_all[run]
     need_pos = int(ctx0.max()) + total_steps + BT
-    pages_per_stream = [min(cap // BT, (int(c) + total_steps) // BT + 2) for c in ctx0]
-    n_blocks = int(sum(pages_per_stream)) + 64
-    max_prefill = int(min(cap, ctx0.max()))
-    prefill_chunk = min(max_prefill, 4096)
+    n_blocks = int(sum(pages_of(c) for c in ctx0)) + 64
     pool = vxk.Pool(device=local, n_layers=L, n_q_heads=NQ, n_kv_heads=NKV, head_dim=HD, block_tokens=BT,
                     capacity=cap, n_blocks=n_blocks, max_streams=S, max_rows=max(S, prefill_chunk),
                     max_position=need_pos + 16, dtype=dtype, alloc_seed=1234 + rank)
@@ -1583,7 +1696,6 @@ def main():
     del kfill, vfill
 
     # ---- per-step inputs resident in HBM (4 rotating sets) -------------------
-    NSETS = 4
     qs = torch.randn((NSETS, L, S, NQ, HD), device="cuda", generator=gen) * 0.5
     ks = torch.randn((NSETS, L, S, NKV, HD), device="cuda", generator=gen) * 0.5
     vs = torch.randn((NSETS, L, S, NKV, HD), device="cuda", generator=gen) * 0.5
@@ -1628,9 +1740,22 @@ def main():
         torch.cuda.synchronize()
     pool.sync(sh)
     launches = pool.stats().kernel_launches - launches0
-    ms = start.elapsed_time(end)
-    ms = max_over_ranks(dist, ms, "cuda")
-    value = world * S * args.steps / (ms / 1000.0)
+    ms_local = start.elapsed_time(end)
+    rank_ms = gather_over_ranks(dist, ms_local, "cuda")
+    rank_streams = [int(x) for x in gather_over_ranks(dist, float(S), "cuda")]
+    ms = max(rank_ms)
+    streams_run = sum(rank_streams)
+    value = streams_run * args.steps / (ms / 1000.0)
+
+    # ---- sampled check against the CPU oracle (outside the timed region) ----
+    chk_err, chk_exact, chk_rows = oracle_check(pool, streams, ctx0, qs, ks, vs, out,
+                                                (args.warmup + args.steps - 1) % NSETS, L, dtype, sh)
+    chk_err = max_over_ranks(dist, chk_err, "cuda")
+    chk_bad = max_over_ranks(dist, 0.0 if chk_exact else 1.0, "cuda")
+    checked = {"passed": bool(chk_err <= 2e-3 and chk_bad == 0.0), "max_abs_err": chk_err, "tolerance": 2e-3,
+               "append_bit_exact": chk_bad == 0.0, "rows_per_gpu": chk_rows,
+               "what": "last timed step: shortest / median / longest-context stream x first / last layer, "
+                       "appended row bytes and attention output vs the CPU oracle"}
 
     # ---- roofline of the dominant kernel (decode_kernel) --------------------
     peak, peak_kind = load_peaks()
@@ -1638,8 +1763,9 @@ def main():
     # Consecutive layer launches overlap (programmatic dependent launch), so the
     # per-launch duration is the timed region divided by the decode launches
     # in it (the small plan upload per step is charged to them too).
-    avg_launch_s = (ms / 1000.0) / (args.steps * L)
+    avg_launch_s = (ms_local / 1000.0) / (args.steps * L)
     achieved = bytes_per_launch / avg_launch_s / 1e9
+    achieved = max_over_ranks(dist, -achieved, "cuda") * -1.0  # the slowest rank's rate
     traffic_ratio, traffic_src = load_traffic(args.config)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
@@ -1650,6 +1776,8 @@ def main():
                 "algorithmic_bytes_per_launch": round(bytes_per_launch),
                 "avg_launch_us": round(avg_launch_s * 1e6, 2), "kernel": "decode_kernel<f16>" if dtype == 1 else
                 "decode_kernel<q8_0>"}
+    job_bytes_per_s = sum(gather_over_ranks(dist, statistics.mean(bytes_per_step) * L, "cuda")) * args.steps / (
+        ms / 1000.0)
 
     # ---- end to end through the host-buffer C-ABI entry point ----------------
     e2e = None
@@ -1669,23 +1797,25 @@ def main():
             pool.decode_step_host(streams, hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr(), sh)
         e1.record(stream)
         torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1)
-        ems = max_over_ranks(dist, ems, "cuda")
-        e2e = {"value": round(world * S * args.steps / (ems / 1000.0), 1), "unit": "tokens/s",
+        ems = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+        e2e = {"value": round(streams_run * args.steps / (ems / 1000.0), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": int(hq.numel() + hk.numel() + hv.numel()) * 4,
                "d2h_bytes_per_step": int(ho.numel()) * 4, "ms_per_step": round(ems / args.steps, 3)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ns = cpu_streams(dtype)
-        tps, done, threads, mean_ctx = cpu_sample(L, ns, cfg["ctx"], args.seed, seconds=args.cpu_seconds, dtype=dtype)
+        sample = sample_contexts(ctx0, cpu_streams(dtype))
+        tps, done, threads, mean_ctx, bps = cpu_sample(L, sample, args.seed, seconds=args.cpu_seconds, dtype=dtype)
         cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{ns} streams (ctx~U{list(cfg['ctx'])}, mean {mean_ctx:.0f}) x {L} layers x {done} steps, "
+               "bytes_per_s": round(bps, 1),
+               "sample": f"{len(sample)} streams (starting contexts {sample}: quantile centres of this run's "
+                         f"list, mean {mean_ctx:.0f}) x {L} layers x {done} steps, "
                          f"{'q8_0' if dtype == 8 else 'f16'} cache, oracle/vx_cpu_step.c on {threads} host threads"}
 
     if dist:
         dist.barrier()
     if rank == 0:
+        cfg_line = decode_config(args, cfg, world, ctx_all, parts, scaling)
         line = {
             "metric": "decode tokens/s (KV append+GQA attn)",
             "value": round(value, 1),
@@ -1695,15 +1825,21 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling,
             "vs_baseline": None,
             "dtype": "f16 cache, fp32 accumulate" if dtype == 1 else "q8_0 cache, fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": f"config {args.config}: {cfg['desc']}", "layers": L, "streams_per_gpu": S,
-                       "global_batch": S * world, "mean_ctx_timed": round(statistics.mean(ctx_means), 1),
-                       "parallelism": f"streams sharded, {S}/GPU, no collective",
-                       "l2": "inputs larger than L2 (KV read per launch >> 126 MB)"},
+            "config": cfg_line,
+            "streams_run": streams_run,
+            "streams_per_rank": rank_streams,
+            "fits": streams_run == len(ctx_all),
+            "device_memory_gb": round(total_b / 1e9, 1),
+            "mean_ctx_timed": round(statistics.mean(ctx_means), 1),
+            "rank_ms": [round(x, 3) for x in rank_ms],
+            "slowest_rank": int(np.argmax(rank_ms)),
+            "bytes_per_s": round(job_bytes_per_s, 1),
             "roofline": roofline,
+            "checked": checked,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(launches),
@@ -1711,8 +1847,6 @@ def main():
         }
         print(json.dumps(line), flush=True)
     pool.close()
-    if dist:
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

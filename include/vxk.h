@@ -178,6 +178,14 @@ typedef struct vxk_pool_config {
     float rope_theta;       /* 1e6 */
     uint32_t alloc_seed;    /* 0: pages handed out lowest index first; else a
                                seeded permutation (random block tables) */
+    /* ---- fields after this line were added later; a caller whose
+       struct_size ends before one gets that field's default ---- */
+    int32_t split_pages;    /* 0 (default): the attention's split size is
+                               chosen per batch from its pages and the
+                               device's resident CTAs; n > 0: splits of n
+                               pages (rounded up to a power of two, at most
+                               512), still enlarged when a batch would need
+                               more splits than the pool's scratch holds */
 } vxk_pool_config;
 
 /** Defaults: the 4B realtime decoder (26 layers, 32/8 heads x 128, 16-token
@@ -273,9 +281,15 @@ VXK_API vxk_status vxk_decode_layer(vxk_pool * pool, int32_t layer, const float 
  * Limits: a batch may need at most 512 x 32 x 132 partial floats (for 32
  * query heads: 512 splits) and 256 x 8 counters (256 rows of 8 kv heads);
  * larger batches return VXK_STATUS_INVALID_ARGUMENT with the sizes in the
- * pool's error message.  The first call on a device looks up the array's
- * device address (with that device current), so make that first call before
- * any stream capture.  Every call shares the one array and clears its
+ * pool's error message.  The batch must also pass the pool's own planning
+ * limit, which vxk_decode_layer has too: its splits must fit the pool's
+ * split bookkeeping (max(2048, 8 * max_rows) work items); otherwise the call
+ * returns VXK_STATUS_INVALID_ARGUMENT ("batch windows exceed the split
+ * scratch capacity").  The first call on a device looks up the array's
+ * device address (with that device current) and remembers it for the life
+ * of the process, so make that first call before any stream capture, and do
+ * not reset the device (cudaDeviceReset) while libvxk.so is loaded: the
+ * remembered address would no longer be valid.  Every call shares the one array and clears its
  * counters before launching; calls that overlap on the GPU (other streams,
  * other pools on the same device) race on it.  Arguments, results and the
  * launch are otherwise those of vxk_decode_layer.

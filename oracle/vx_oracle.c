@@ -307,6 +307,15 @@ void vxo_kv_row(const float * k, const float * v, int32_t n_kv, int32_t head_dim
     store_row(v, n, dtype, v_out);
 }
 
+void vxo_kv_rows(const float * k, const float * v, int64_t n_rows, int32_t n_kv, int32_t head_dim,
+                 int64_t pos0, float base, int32_t dtype, uint8_t * k_out, uint8_t * v_out) {
+    const int64_t vals = (int64_t) n_kv * head_dim;
+    const int64_t rb = vxo_row_bytes(dtype, n_kv, head_dim);
+    for (int64_t r = 0; r < n_rows; ++r)
+        vxo_kv_row(k + r * vals, v + r * vals, n_kv, head_dim, pos0 + r, base, dtype, k_out + r * rb,
+                   v_out + r * rb);
+}
+
 void vxo_row_to_f32(const uint8_t * row, int32_t dtype, int32_t n_kv, int32_t head_dim,
                     float * out) {
     const int64_t n = (int64_t) n_kv * head_dim;

@@ -120,6 +120,11 @@ void vxo_kv_row(const float * k, const float * v, int32_t n_kv, int32_t head_dim
                 int64_t pos, float base, int32_t dtype,
                 uint8_t * k_out, uint8_t * v_out);
 
+/* n_rows appended tokens at consecutive positions pos0, pos0 + 1, ...:
+ * vxo_kv_row on each; k/v [n_rows][n_kv][head_dim], outputs [n_rows][row bytes]. */
+void vxo_kv_rows(const float * k, const float * v, int64_t n_rows, int32_t n_kv, int32_t head_dim,
+                 int64_t pos0, float base, int32_t dtype, uint8_t * k_out, uint8_t * v_out);
+
 /* Decode a stored row back to fp32 values (n_kv * head_dim). */
 void vxo_row_to_f32(const uint8_t * row, int32_t dtype, int32_t n_kv,
                     int32_t head_dim, float * out);

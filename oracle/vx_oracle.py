@@ -82,6 +82,7 @@ def lib() -> C.CDLL:
         L.vxo_row_bytes.restype = C.c_int64
         L.vxo_row_bytes.argtypes = [C.c_int32, C.c_int32, C.c_int32]
         L.vxo_kv_row.argtypes = [P, P, C.c_int32, C.c_int32, C.c_int64, C.c_float, C.c_int32, P, P]
+        L.vxo_kv_rows.argtypes = [P, P, C.c_int64, C.c_int32, C.c_int32, C.c_int64, C.c_float, C.c_int32, P, P]
         L.vxo_row_to_f32.argtypes = [P, C.c_int32, C.c_int32, C.c_int32, P]
         L.vxo_attn_row.argtypes = [P, C.c_int64, C.c_float, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                    P, P, C.c_int32, C.c_int64, C.c_float, P]
@@ -187,6 +188,19 @@ def kv_row(k: np.ndarray, v: np.ndarray, pos: int, base: float, dtype: int):
     ko = np.empty(rb, dtype=np.uint8)
     vo = np.empty(rb, dtype=np.uint8)
     lib().vxo_kv_row(_ptr(k), _ptr(v), n_kv, hd, pos, base, dtype, _ptr(ko), _ptr(vo))
+    return ko, vo
+
+
+def kv_rows(k: np.ndarray, v: np.ndarray, pos0: int, base: float, dtype: int):
+    """k, v: [n, n_kv, head_dim] fp32 of tokens at positions pos0 .. pos0 + n - 1
+    -> stored row bytes [n, row bytes] (K rotated), like kv_row on each."""
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    n, n_kv, hd = k.shape
+    rb = row_bytes(dtype, n_kv, hd)
+    ko = np.empty((n, rb), dtype=np.uint8)
+    vo = np.empty((n, rb), dtype=np.uint8)
+    lib().vxo_kv_rows(_ptr(k), _ptr(v), n, n_kv, hd, pos0, base, dtype, _ptr(ko), _ptr(vo))
     return ko, vo
 
 

@@ -14,7 +14,7 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT / "voxtral.cpp_b200"))
 
-from vxk_shard import assign_streams, max_over_ranks  # noqa: E402
+from vxk_shard import assign_streams, gather_over_ranks, max_over_ranks  # noqa: E402
 
 
 def test_assignment_is_a_balanced_partition():
@@ -63,8 +63,9 @@ def _rank_main(rank: int, world: int, port: int, queue) -> None:
         dist.all_gather_object(gathered, mine)
         ms = 10.0 + 5.0 * rank  # a slower rank sets the job's time
         slowest = max_over_ranks(dist, ms)
+        per_rank = gather_over_ranks(dist, ms)
         dist.barrier()
-        queue.put((rank, gathered, slowest))
+        queue.put((rank, gathered, slowest, per_rank))
     finally:
         dist.destroy_process_group()
 
@@ -84,9 +85,14 @@ def test_two_gloo_ranks_shard_and_time():
         p.join(timeout=60)
         assert p.exitcode == 0
     results.sort()
-    views = [g for _, g, _ in results]
+    views = [g for _, g, _, _ in results]
     assert views[0] == views[1]  # both ranks agree on the assignment
     parts = views[0]
     assert sorted(parts[0] + parts[1]) == list(range(16 * world))
     assert not set(parts[0]) & set(parts[1])
-    assert all(s == 15.0 for _, _, s in results)
+    assert all(s == 15.0 for _, _, s, _ in results)
+    assert all(p == [10.0, 15.0] for _, _, _, p in results)  # element r is rank r's time
+
+
+def test_gather_over_ranks_without_a_group():
+    assert gather_over_ranks(None, 2.5) == [2.5]

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <numeric>
@@ -238,8 +239,19 @@ T * device_alloc(vxk_pool * p, size_t bytes) {
     return static_cast<T *>(ptr);
 }
 
+// Reads a caller's config: fields past the caller's struct_size (added in a
+// later version of the struct) keep the defaults.
+vxk_pool_config read_config(const vxk_pool_config * in) {
+    vxk_pool_config c = vxk_pool_default_config();
+    if (in->struct_size < offsetof(vxk_pool_config, split_pages))
+        fail(VXK_STATUS_INVALID_ARGUMENT, "config struct_size too small");
+    std::memcpy(&c, in, std::min<size_t>(in->struct_size, sizeof(c)));
+    c.struct_size = sizeof(c);
+    return c;
+}
+
 void validate_config(const vxk_pool_config & c) {
-    if (c.struct_size < sizeof(vxk_pool_config)) fail(VXK_STATUS_INVALID_ARGUMENT, "config struct_size too small");
+    if (c.split_pages < 0) fail(VXK_STATUS_INVALID_ARGUMENT, "split_pages must be >= 0");
     if (c.head_dim != vxk::kHeadDim) fail(VXK_STATUS_INVALID_ARGUMENT, "head_dim must be 128");
     if (c.n_kv_heads < 1 || c.n_q_heads != c.n_kv_heads * vxk::kGroup)
         fail(VXK_STATUS_INVALID_ARGUMENT, "n_q_heads must be 4 * n_kv_heads");
@@ -333,8 +345,7 @@ void build_items(vxk_pool * p) {
         total_pages += row_pages[r];
         max_pages = std::max<int64_t>(max_pages, row_pages[r]);
     }
-    int32_t cp = 0;
-    if (const char * env = std::getenv("VXK_CHUNK_PAGES")) cp = std::atoi(env);
+    int32_t cp = p->cfg.split_pages > 0 ? pow2_ceil(p->cfg.split_pages) : 0;
     if (cp <= 0) {
         // A split pays a fixed prologue (descriptor, block-table and first-copy
         // latency) and epilogue (partials written, read back and combined by
@@ -394,14 +405,9 @@ void build_items(vxk_pool * p) {
     });
     const int32_t nkv = p->cfg.n_kv_heads;
     const int64_t n_units = (int64_t) p->items.size() * nkv;
-    // Persistent grid (one CTA per resident slot, VXK_PERSISTENT=1) or one CTA
-    // per unit, launched longest-first and balanced by the hardware.
-    static const bool persistent = [] {
-        const char * e = std::getenv("VXK_PERSISTENT");
-        return e && e[0] == '1';
-    }();
-    const int32_t G = (int32_t) std::max<int64_t>(
-        1, persistent ? std::min<int64_t>(n_units, p->decode_slots) : n_units);
+    // One CTA per unit, launched longest-first and balanced by the hardware
+    // (measured faster than a persistent grid of one CTA per resident slot).
+    const int32_t G = (int32_t) std::max<int64_t>(1, n_units);
     std::vector<std::pair<int64_t, int32_t>> heap;  // (pages assigned, cta) min-heap
     heap.reserve((size_t) G);
     for (int32_t b = 0; b < G; ++b) heap.emplace_back(0, b);
@@ -509,10 +515,7 @@ void check_attention(vxk_pool * p) {
 // next decode prologue reads (descriptors, block table, other layers' pages).
 // Any other launch of the pool (plan upload, append, attend, compaction,
 // readback) clears the condition.
-bool use_pdl(vxk_pool * p) {
-    static const bool disabled = std::getenv("VXK_NO_PDL") != nullptr;
-    return !disabled && p->batch_decodes > 0;
-}
+bool use_pdl(vxk_pool * p) { return p->batch_decodes > 0; }
 
 void do_plan(vxk_pool * p, const int32_t * ids, const int32_t * n_new, int32_t n, cudaStream_t stream) {
     if (p->planned) fail(VXK_STATUS_INVALID_STATE, "a batch is already planned");
@@ -656,6 +659,8 @@ vxk_pool_config vxk_pool_default_config(void) {
     c.max_position = 32768;
     c.dtype = VXK_DTYPE_F16;
     c.rope_theta = 1000000.0f;
+    c.alloc_seed = 0;
+    c.split_pages = 0;
     return c;
 }
 
@@ -673,8 +678,8 @@ vxk_status vxk_pool_create(const vxk_pool_config * config, vxk_pool ** out_pool)
         return VXK_STATUS_OUT_OF_MEMORY;
     }
     const vxk_status st = guarded(p, [&] {
-        validate_config(*config);
-        p->cfg = *config;
+        p->cfg = read_config(config);
+        validate_config(p->cfg);
         int n_dev = 0;
         VXK_CUDA(cudaGetDeviceCount(&n_dev));
         if (config->device < 0 || config->device >= n_dev) fail(VXK_STATUS_INVALID_ARGUMENT, "no such CUDA device");

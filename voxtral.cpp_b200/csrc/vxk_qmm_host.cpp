@@ -311,13 +311,6 @@ void plan_split(int32_t n_units, int32_t sms, vxk::QmmParams & p) {
             best_cost = cost;
         }
     }
-    if (const char * env = std::getenv("VXK_QMM_UNITS")) {
-        // fixed units per split (tuning); ignored when it does not fit
-        const int per = std::atoi(env);
-        if (per >= 1 && per <= n_units && (n_units + per - 1) / per <= vxk::kQmmMaxSplits &&
-            vxk::qmm_smem_bytes(p, per) <= 232448)
-            best_per = per;
-    }
     if (best_per == 0) qfail(VXK_STATUS_INVALID_ARGUMENT, "no column split of this product fits shared memory");
     p.units_per_split = best_per;
     p.n_splits = (n_units + best_per - 1) / best_per;
@@ -335,17 +328,8 @@ vxk::QmmMat mat_of(const vxk_qweight * w, float * y, int32_t block0) {
 
 // True when a product of `rows` rows with w runs on the tcgen05 kernel: Q4_K
 // and Q6_K weights from 17 rows up, where the int8 mma.sync kernel is bound by
-// instruction issue (VXK_QMM_TC=0 / 1 forces it off / on for every size).
-bool use_tc(const vxk_qweight * w, int32_t rows) {
-    if (!w->w_tc) return false;
-    static const int mode = [] {
-        const char * e = std::getenv("VXK_QMM_TC");
-        return e ? std::atoi(e) : -1;
-    }();
-    if (mode == 0) return false;
-    if (mode == 1) return true;
-    return rows > 16;
-}
+// instruction issue.
+bool use_tc(const vxk_qweight * w, int32_t rows) { return w->w_tc && rows > 16; }
 
 // Column units per CTA of the tcgen05 product (one 191 KB CTA per SM): the
 // fewest whole waves x (units per CTA + 1.5), splits <= 8, fewer splits on

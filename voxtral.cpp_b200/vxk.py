@@ -62,7 +62,7 @@ class PoolConfig(C.Structure):
                 ("head_dim", C.c_int32), ("block_tokens", C.c_int32), ("n_blocks", C.c_int32),
                 ("capacity", C.c_int32), ("max_streams", C.c_int32), ("max_rows", C.c_int32),
                 ("max_position", C.c_int32), ("dtype", C.c_int32), ("rope_theta", C.c_float),
-                ("alloc_seed", C.c_uint32)]
+                ("alloc_seed", C.c_uint32), ("split_pages", C.c_int32)]
 
 
 class PoolStats(C.Structure):

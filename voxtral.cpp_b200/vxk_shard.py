@@ -8,7 +8,9 @@ on the data path.  This module holds the host logic of that split:
   ranks by context length (the per-step HBM bytes of a stream grow with its
   context), with an equal stream count per rank;
 - `max_over_ranks`: the timing reduction every multi-GPU number uses (the
-  slowest rank sets the job's time).
+  slowest rank sets the job's time);
+- `gather_over_ranks`: every rank's value (per-rank times, so that a report
+  can name the slowest rank).
 
 Used by bench.py under torchrun and tested with gloo ranks on CPU.
 """
@@ -63,3 +65,17 @@ def max_over_ranks(dist, value: float, device=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_over_ranks(dist, value: float, device=None) -> List[float]:
+    """All-gather of a per-rank float; element r is rank r's value.  Returns
+    [value] when dist is None."""
+    if dist is None:
+        return [float(value)]
+    import torch
+
+    world = dist.get_world_size()
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]

@@ -123,3 +123,18 @@ def test_rejects_bad_config(vxk):
         vxk.Batcher(fn=_fake([]), max_rows=0)
     with pytest.raises(vxk.VxkError):
         vxk.Batcher(fn=_fake([]), timeout_ms=0)
+
+
+def test_withdrawn_request_forms_no_empty_batch(vxk):
+    """A request withdrawn (timed out) while the dispatcher waits for company
+    leaves an empty queue: no batch is run and nothing counts as failed."""
+    record = []
+    b = vxk.Batcher(fn=_fake(record), max_rows=4, max_wait_us=300000, timeout_ms=50)
+    with pytest.raises(vxk.VxkError) as e:
+        b.step(1, 1, 0)
+    assert e.value.status == vxk.TIMEOUT
+    time.sleep(0.6)  # past the dispatcher's deadline for the withdrawn request
+    st = b.stats()
+    assert record == []
+    assert (st["batches"], st["failed_batches"], st["timeouts"]) == (0, 0, 1)
+    b.close()

@@ -104,3 +104,21 @@ def test_refuses_truncated_and_foreign_files(vxk, tmp_path):
         vxk.Gguf(foreign)
     with pytest.raises(vxk.VxkError):
         vxk.Gguf(tmp_path / "missing.gguf")
+
+
+def test_refuses_a_tensor_offset_that_would_wrap(vxk, tmp_path):
+    """A relative data offset near 2^64 (aligned) must be refused, not wrapped
+    around into the header bytes."""
+    path = tmp_path / "m.gguf"
+    _write(path)
+    r = gguf.GGUFReader(str(path))
+    t = r.tensors[-1]
+    at = int(t.field.offset) + sum(int(p.nbytes) for p in t.field.parts[:-1])
+    data = bytearray(path.read_bytes())
+    assert int.from_bytes(data[at:at + 8], "little") == int(t.data_offset) - int(r.data_offset)
+    data[at:at + 8] = ((1 << 64) - 32).to_bytes(8, "little")
+    bad = tmp_path / "wrap.gguf"
+    bad.write_bytes(bytes(data))
+    with pytest.raises(vxk.VxkError) as e:
+        vxk.Gguf(bad)
+    assert "runs past the file" in str(e.value)

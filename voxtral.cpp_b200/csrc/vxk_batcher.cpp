@@ -134,6 +134,8 @@ void run_dispatcher(vxk_batcher * b) {
             it = b->queue.erase(it);
         }
         const int32_t n = (int32_t) batch.size();
+        // every queued request was withdrawn while the batch formed
+        if (n == 0) continue;
         streams.resize((size_t) n);
         tokens.resize((size_t) n);
         slots.resize((size_t) n);

@@ -205,9 +205,12 @@ void parse(vxk_gguf * g) {
     for (uint64_t i = 0; i < n_tensors; ++i) {
         vxk_gguf_tensor & t = g->tensors[i];
         t.name = g->names[i].c_str();
-        t.offset = g->data_start + rel[i];
         if (rel[i] % a != 0) gfail("tensor " + g->names[i] + " is not aligned");
-        if (t.offset > g->size || t.n_bytes > g->size - t.offset) gfail("tensor " + g->names[i] + " runs past the file");
+        // checked before the sum: a relative offset near 2^64 would wrap it
+        if (g->data_start > g->size || rel[i] > g->size - g->data_start)
+            gfail("tensor " + g->names[i] + " runs past the file");
+        t.offset = g->data_start + rel[i];
+        if (t.n_bytes > g->size - t.offset) gfail("tensor " + g->names[i] + " runs past the file");
         g->tensor_index[g->names[i]] = (int64_t) i;
     }
 }

@@ -1176,6 +1176,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--cache", choices=["f16", "q8_0", "f32"], default=None,
+                    help="override the decoder cache format of configs 2, 3 and 5")
     return ap.parse_args()
 
 
@@ -1184,6 +1186,8 @@ def algorithmic_bytes(ctx: int, dtype: int) -> int:
     unit): K+V window reads + q/k/v fp32 reads + append write + fp32 output."""
     if dtype == 8:
         return 2176 * ctx + 43136
+    if dtype == 0:
+        return 8192 * ctx + 49152
     return 4096 * ctx + 45056
 
 
@@ -1289,6 +1293,8 @@ def cpu_sample(layers, ctx0, seed, seconds=None, steps=None, warmup=0, dtype=1):
     step on all host cores, for an f16 (1) or q8_0 (8) cache, over streams
     whose starting contexts are `ctx0`.  Returns (tokens/s, steps done,
     threads, mean context, algorithmic bytes/s)."""
+    if dtype not in (1, 8):
+        raise ValueError("the CPU step restates the f16 and q8_0 caches only")
     sys.path.insert(0, str(ROOT / "oracle"))
     import vx_oracle
 
@@ -1539,6 +1545,9 @@ def main():
         cfg["layers"] = args.layers
     if args.vocab:
         cfg["vocab"] = args.vocab
+    if args.cache and "dtype" in cfg and cfg.get("kind") is None:
+        cfg["dtype"] = {"f16": 1, "q8_0": 8, "f32": 0}[args.cache]
+        cfg["desc"] += f" ({args.cache} cache)"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1603,7 +1612,7 @@ def main():
 
 def page_bytes(L: int, dtype: int) -> int:
     """Device bytes of one 16-position page across every layer (K and V)."""
-    tile = BT * HD * 2 if dtype == 1 else BT * HD + BT * (HD // 32) * 2
+    tile = {1: BT * HD * 2, 0: BT * HD * 4}.get(dtype, BT * HD + BT * (HD // 32) * 2)
     return NKV * 2 * tile * L
 
 
@@ -1766,7 +1775,7 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
     avg_launch_s = (ms_local / 1000.0) / (args.steps * L)
     achieved = bytes_per_launch / avg_launch_s / 1e9
     achieved = max_over_ranks(dist, -achieved, "cuda") * -1.0  # the slowest rank's rate
-    traffic_ratio, traffic_src = load_traffic(args.config)
+    traffic_ratio, traffic_src = load_traffic(args.config) if not args.cache else (None, None)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "frac_of_nominal_8000": round(achieved / 8000.0, 4),
@@ -1774,8 +1783,8 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
                 "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
                                                   f"scaled to this launch)",
                 "algorithmic_bytes_per_launch": round(bytes_per_launch),
-                "avg_launch_us": round(avg_launch_s * 1e6, 2), "kernel": "decode_kernel<f16>" if dtype == 1 else
-                "decode_kernel<q8_0>"}
+                "avg_launch_us": round(avg_launch_s * 1e6, 2),
+                "kernel": "decode_kernel<" + {1: "f16", 8: "q8_0", 0: "f32"}[dtype] + ">"}
     job_bytes_per_s = sum(gather_over_ranks(dist, statistics.mean(bytes_per_step) * L, "cuda")) * args.steps / (
         ms / 1000.0)
 
@@ -1803,7 +1812,7 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
                "d2h_bytes_per_step": int(ho.numel()) * 4, "ms_per_step": round(ems / args.steps, 3)}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and dtype in (1, 8):
         sample = sample_contexts(ctx0, cpu_streams(dtype))
         tps, done, threads, mean_ctx, bps = cpu_sample(L, sample, args.seed, seconds=args.cpu_seconds, dtype=dtype)
         cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -1827,7 +1836,7 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
             "higher_is_better": True,
             "scaling": scaling,
             "vs_baseline": None,
-            "dtype": "f16 cache, fp32 accumulate" if dtype == 1 else "q8_0 cache, fp32 accumulate",
+            "dtype": {1: "f16", 8: "q8_0", 0: "f32"}[dtype] + " cache, fp32 accumulate",
             "data": "synthetic",
             "config": cfg_line,
             "streams_run": streams_run,

@@ -54,6 +54,7 @@ typedef enum vxk_status {
 
 /** Cache element formats; values are ggml_type numbers. */
 typedef enum vxk_dtype {
+    VXK_DTYPE_F32 = 0,
     VXK_DTYPE_F16 = 1,
     VXK_DTYPE_Q8_0 = 8,
     VXK_DTYPE_BF16 = 30
@@ -174,7 +175,8 @@ typedef struct vxk_pool_config {
     int32_t max_streams;
     int32_t max_rows;       /* max query rows in one planned batch */
     int32_t max_position;   /* RoPE table rows: every position must be below */
-    vxk_dtype dtype;        /* F16 or Q8_0 */
+    vxk_dtype dtype;        /* F16 (default), Q8_0, or F32 (the reference's exact
+                               VOXTRAL_DECODER_KV_TYPE=f32 mode, src/voxtral.cpp:94-98) */
     float rope_theta;       /* 1e6 */
     uint32_t alloc_seed;    /* 0: pages handed out lowest index first; else a
                                seeded permutation (random block tables) */
@@ -298,7 +300,7 @@ VXK_API vxk_status vxk_decode_layer_static_scratch(vxk_pool * pool, int32_t laye
                                                    const float * k, const float * v, float * out,
                                                    void * cuda_stream);
 
-/** Appends the batch's new tokens to one layer (RoPE on K, f16/q8_0 store);
+/** Appends the batch's new tokens to one layer (RoPE on K, f16/q8_0/f32 store);
  *  replaces src/voxtral.cpp:2663-2714 for prefill / multi-token batches. */
 VXK_API vxk_status vxk_append_layer(vxk_pool * pool, int32_t layer, const float * k,
                                     const float * v, void * cuda_stream);

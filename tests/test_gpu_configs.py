@@ -16,7 +16,7 @@ through the C-ABI (libvxk.so) against the CPU oracle on identical seeded inputs.
 - config 2's load: 64 streams with contexts seeded uniform in [400, 4096] in
   16-token pages with a random block table.
 
-Bar: cache bytes bit-exact (f16 RNE / ggml q8_0 blocks); attention outputs
+Bar: cache bytes bit-exact (f16 RNE / ggml q8_0 blocks / f32); attention outputs
 within max-abs 2e-3 of the fp64 oracle.
 """
 from __future__ import annotations
@@ -28,7 +28,7 @@ from gpu_harness import ATOL, Driver, max_err, rand
 
 pytestmark = pytest.mark.gpu
 
-F16, Q8 = 1, 8
+F32, F16, Q8 = 0, 1, 8
 
 
 def _cfg(**kw):
@@ -38,7 +38,7 @@ def _cfg(**kw):
     return base
 
 
-@pytest.mark.parametrize("dtype", [F16, Q8])
+@pytest.mark.parametrize("dtype", [F16, Q8, F32])
 def test_config1_in_full(vxk, oracle, dtype):
     """30 layers, prefill 391, then 128 decode steps with every step checked."""
     d = Driver(vxk, oracle, seed=101, **_cfg(n_layers=30, dtype=dtype, n_blocks=64, max_rows=512))

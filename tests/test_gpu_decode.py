@@ -1,7 +1,7 @@
 """GPU parity of the decoder KV path through the C-ABI (libvxk.so) against the
 CPU oracle on identical seeded inputs.
 
-Bar: cache bytes bit-exact (f16 RNE / ggml q8_0 blocks); attention outputs
+Bar: cache bytes bit-exact (f16 RNE / ggml q8_0 blocks / f32); attention outputs
 within max-abs 2e-3 of the fp64 oracle.  Shapes are the 3B/4B decoder's
 (32 q heads, 8 kv heads, head_dim 128, 16-token pages, RoPE theta 1e6);
 layer counts are trimmed where the oracle would take minutes.
@@ -15,7 +15,7 @@ from gpu_harness import ATOL, Driver, max_err, rand
 
 pytestmark = pytest.mark.gpu
 
-F16, Q8 = 1, 8
+F32, F16, Q8 = 0, 1, 8
 
 
 def _cfg(**kw):
@@ -25,7 +25,7 @@ def _cfg(**kw):
     return base
 
 
-@pytest.mark.parametrize("dtype", [F16, Q8])
+@pytest.mark.parametrize("dtype", [F16, Q8, F32])
 def test_config1_prefill_then_decode(vxk, oracle, dtype):
     """Config 1 shape: one stream, prefill 391 positions, then decode steps."""
     d = Driver(vxk, oracle, seed=1, **_cfg(n_layers=3, dtype=dtype))
@@ -58,7 +58,7 @@ def test_fused_matches_unfused(vxk, oracle):
     d2.check_cache(s2)
 
 
-@pytest.mark.parametrize("dtype", [F16, Q8])
+@pytest.mark.parametrize("dtype", [F16, Q8, F32])
 def test_many_streams_random_block_table(vxk, oracle, dtype):
     """Config 2 in miniature: uneven contexts, seeded random page order."""
     d = Driver(vxk, oracle, seed=2, **_cfg(dtype=dtype, n_blocks=2048, alloc_seed=99, max_rows=2048))
@@ -78,7 +78,7 @@ def test_many_streams_random_block_table(vxk, oracle, dtype):
         d.check_cache(s)
 
 
-@pytest.mark.parametrize("dtype", [F16, Q8])
+@pytest.mark.parametrize("dtype", [F16, Q8, F32])
 def test_ring_wrap_sliding_window(vxk, oracle, dtype):
     """Realtime ring semantics with a small capacity: slots overwrite in place,
     wraps/evictions follow the reference planner, attention sees the window."""
@@ -216,7 +216,7 @@ def test_device_wait_timeout_is_reported_and_the_pool_recovers(vxk, oracle):
     assert e.value.status == vxk.INVALID_ARGUMENT
 
 
-@pytest.mark.parametrize("dtype", [F16, Q8])
+@pytest.mark.parametrize("dtype", [F16, Q8, F32])
 def test_back_to_back_layers(vxk, oracle, dtype):
     """All layers of a step launched back to back with no host sync between
     them (the decode launches after the first overlap their predecessor)."""

@@ -4,7 +4,7 @@ where cudaMalloc may synchronise the device and has no latency bound, and
 hosts whose device memory is owned by another allocator).  Its split scratch
 is a fixed array inside libvxk.so instead of memory the library allocates.
 
-Checked through the C ABI, for f16 and q8_0 caches, on two pools holding the
+Checked through the C ABI, for f16, q8_0 and f32 caches, on two pools holding the
 same caches: on consecutive calls (the shared array keeps the previous call's
 contents) its outputs agree with vxk_decode_layer's and with the CPU oracle
 within the attention tolerance, the appended cache bytes are the oracle's,
@@ -23,7 +23,7 @@ from gpu_harness import ATOL, DecoderMirror
 
 pytestmark = pytest.mark.gpu
 
-F16, Q8 = 1, 8
+F32, F16, Q8 = 0, 1, 8
 CFG = dict(n_layers=2, n_q_heads=32, n_kv_heads=8, head_dim=128, block_tokens=16, capacity=8192,
            n_blocks=1024, max_streams=8, max_rows=4096, max_position=16384, alloc_seed=5)
 
@@ -57,7 +57,7 @@ def _filled_pools(vxk, oracle, ctx, seed, dtype, split_pages=0):
     return a, b, sa, sb, mirror, stream, rng
 
 
-@pytest.mark.parametrize("dtype", [F16, Q8])
+@pytest.mark.parametrize("dtype", [F16, Q8, F32])
 def test_static_scratch_matches_allocating_entry_point_and_oracle(vxk, oracle, dtype):
     import torch
 

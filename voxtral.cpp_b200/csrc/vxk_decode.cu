@@ -16,6 +16,9 @@
 //   q8_0 tile: 16 rows x 128 B int8 values, chunk c of row r at c ^ (r & 7)
 //        (2048 B), then the ggml block scales as f16 [4 blocks][16 rows]
 //        (128 B) in a parallel array.
+//   f32  tile: 16 rows x 512 B; chunk c (0-31) of row r stored at
+//        c ^ (r & 7)  (8192 B).  The reference's f32 cache (its numerical
+//        oracle mode) is exact, so its products run on the CUDA cores in fp32.
 // The XOR swizzle makes the ldmatrix reads of the tensor-core tiles
 // bank-conflict free without any shared-memory re-layout.
 //
@@ -45,26 +48,44 @@ constexpr int kErrTimeout = 2;
 constexpr unsigned kFull = 0xffffffffu;
 
 template <int DT> struct Cfg;
+// kMinBlocks: resident CTAs per SM the launch bounds ask for.  The q8_0
+// kernel is bound by instruction latency (two warps per scheduler left the
+// dependency chains of its int8 dots and conversions exposed): three CTAs
+// per SM with three stages each (161 registers, no spills) measured 0.83 of
+// the copy peak on 128 streams at 8K-32K positions, against 0.75 for two
+// CTAs with five stages.
+template <> struct Cfg<0> {
+    static constexpr int kTile = kBlockTokens * kHeadDim * 4;   // 8192
+    static constexpr int kScale = 0;
+    static constexpr int kStages = 3;
+    static constexpr int kMinBlocks = 1;
+};
 template <> struct Cfg<1> {
     static constexpr int kTile = kBlockTokens * kHeadDim * 2;   // 4096
     static constexpr int kScale = 0;
     static constexpr int kStages = 3;                            // per warp
+    static constexpr int kMinBlocks = 2;
 };
 template <> struct Cfg<8> {
     static constexpr int kTile = kBlockTokens * kHeadDim;       // 2048
     static constexpr int kScale = kBlockTokens * (kHeadDim / kQ8Block) * 2;  // 128
-    static constexpr int kStages = 5;
+    static constexpr int kStages = 3;
+    static constexpr int kMinBlocks = 3;
 };
 template <int DT>
 __host__ __device__ constexpr int stage_bytes() { return 2 * (Cfg<DT>::kTile + Cfg<DT>::kScale); }
+
+constexpr int kPwFloats = kBlockTokens * kGroup + kGroup;
 
 template <int DT>
 struct __align__(128) Smem {
     uint8_t stage[kWarps][Cfg<DT>::kStages][stage_bytes<DT>()];  // [K tile|K scales|V tile|V scales]
     uint64_t full[kWarps][Cfg<DT>::kStages];
     float merge[kWarps * kGroup * kHeadDim];  // per-warp O^T, then split-combine weights
-    uint8_t newk[kHeadDim * 2];      // appended row, plain order
-    uint8_t newv[kHeadDim * 2];
+    uint8_t newk[kHeadDim * (DT == 0 ? 4 : 2)];  // appended row, plain order
+    uint8_t newv[kHeadDim * (DT == 0 ? 4 : 2)];
+    float qf[DT == 0 ? kGroup * kHeadDim : 1];     // f32: the unit's rotated, scaled queries
+    float pw[DT == 0 ? kWarps * kPwFloats : 1];    // f32: per warp P[token][head], then alpha[head]
     uint16_t newk_scale[kHeadDim / kQ8Block];
     uint16_t newv_scale[kHeadDim / kQ8Block];
     float wm[kWarps][kGroup];        // per-warp running max / sum
@@ -208,6 +229,7 @@ __device__ __forceinline__ void set_error(int32_t * err, int code) {
 // Byte offset of element pair / chunk inside a swizzled tile row.
 __device__ __forceinline__ int f16_chunk_off(int row, int chunk) { return row * 256 + ((chunk ^ (row & 7)) << 4); }
 __device__ __forceinline__ int q8_chunk_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+__device__ __forceinline__ int f32_chunk_off(int row, int chunk) { return row * 512 + ((chunk ^ (row & 7)) << 4); }
 
 // ggml quantize_row_q8_0_ref on one 32-value block held as 16 pairs by 16
 // consecutive lanes (lane group aligned to 16): d = amax/127,
@@ -236,7 +258,11 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
     const int i = is_k ? tid : tid - 64;  // pair index 0..63 (dims 2i, 2i+1)
     float2 x = reinterpret_cast<const float2 *>(is_k ? k : v)[i];
     if (is_k) x = rope_pair(x, cs[i]);
-    if constexpr (DT == 1) {
+    if constexpr (DT == 0) {
+        uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<0>::kTile;
+        *reinterpret_cast<float2 *>(t + f32_chunk_off(tok, i >> 1) + (i & 1) * 8) = x;
+        if (sk) reinterpret_cast<float2 *>(is_k ? sk : sv)[i] = x;
+    } else if constexpr (DT == 1) {
         const __half2 h = __floats2half2_rn(x.x, x.y);
         uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<1>::kTile;
         *reinterpret_cast<__half2 *>(t + f16_chunk_off(tok, i >> 2) + (i & 3) * 4) = h;
@@ -266,7 +292,7 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
 // runs ahead across unit boundaries, so the next unit's pages are already in
 // flight while the CTA merges and writes the current one.
 template <int DT>
-__global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem<DT> & S = *reinterpret_cast<Smem<DT> *>(smem_raw);
     constexpr int ST = Cfg<DT>::kStages;
@@ -392,7 +418,19 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
         {
             const float * qrow = p.q + ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup + (g & 3)) * kHeadDim;
             const float2 * cs = p.rope + (int64_t) rd.pos * (kHeadDim / 2);
-            if constexpr (DT == 1) {
+            if constexpr (DT == 0) {
+                // the unit's four query heads, rotated and scaled, for all warps:
+                // warp w writes head w (the previous unit's readers have passed
+                // the barriers that end it)
+                const float * qh = p.q + ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup + warp) * kHeadDim;
+#pragma unroll
+                for (int j = lane; j < kHeadDim / 2; j += 32) {
+                    const float2 r = rope_pair(*reinterpret_cast<const float2 *>(qh + 2 * j), cs[j]);
+                    *reinterpret_cast<float2 *>(S.qf + warp * kHeadDim + 2 * j) =
+                        make_float2(r.x * p.scale_log2, r.y * p.scale_log2);
+                }
+                (void) qrow;
+            } else if constexpr (DT == 1) {
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     const int d0 = 16 * ks + 2 * c;
@@ -461,17 +499,17 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
         }
         __syncthreads();
 
-        float o[8][4];
-#pragma unroll
-        for (int mb = 0; mb < 8; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.0f;
-        float m_run = -INFINITY;
-        float l_part = 0.0f;
         const int share = share_of(n_pages);
         // Replaces the stale copy of the appended row in a stage by the new values.
         auto patch = [&](uint8_t * sk, uint8_t * sv) {
             // Replace the stale copy of the appended row by the new values.
             const int t = rd.pos % kBlockTokens;
-            if constexpr (DT == 1) {
+            if constexpr (DT == 0) {
+                *reinterpret_cast<uint4 *>(sk + f32_chunk_off(t, lane)) =
+                    *reinterpret_cast<const uint4 *>(S.newk + lane * 16);
+                *reinterpret_cast<uint4 *>(sv + f32_chunk_off(t, lane)) =
+                    *reinterpret_cast<const uint4 *>(S.newv + lane * 16);
+            } else if constexpr (DT == 1) {
                 const int ch = lane & 15;
                 const uint4 val = *reinterpret_cast<const uint4 *>((lane < 16 ? S.newk : S.newv) + ch * 16);
                 *reinterpret_cast<uint4 *>((lane < 16 ? sk : sv) + f16_chunk_off(t, ch)) = val;
@@ -492,210 +530,320 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const DecodeParams p) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
         };
-        // This lane's scores of head g for tokens 2c, 2c+1, 8+2c, 9+2c of one
-        // page (log2 domain), masked to the row's window.
-        auto page_scores = [&](const uint8_t * sk, int lp, float (&sc)[4]) {
-            // ---- S^T = Q K^T for the page's 16 tokens (two n-blocks of 8) ---
-            float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            float s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const uint32_t kbase = smem_u32(sk);
-            if constexpr (DT == 1) {
-                const int row = mrow + ((mi >> 1) << 3);
+        if constexpr (DT == 0) {
+            // ---- f32 cache: fp32 products on the CUDA cores ---------------
+            // Scores: lane (t = lane & 15, hp = lane >> 4) computes heads 2hp
+            // and 2hp + 1 against token t of the page (its K row from shared
+            // memory, the queries broadcast from S.qf).  Values: lane owns
+            // dims 4 lane .. 4 lane + 3 of all four heads; the page's
+            // probabilities and the rescale factors pass through S.pw.
+            const int t = lane & 15;
+            const int hp = lane >> 4;
+            float m2[2] = {-INFINITY, -INFINITY};
+            float l2[2] = {0.0f, 0.0f};
+            float of[kGroup][4];
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(kbase + f16_chunk_off(row, 2 * ks + (mi & 1)), b0, b1, b2, b3);
-                    mma16816(s0, qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
-                    mma16816(s1, qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+            for (int h = 0; h < kGroup; ++h) of[h][0] = of[h][1] = of[h][2] = of[h][3] = 0.0f;
+            float * pw = S.pw + warp * kPwFloats;  // [token][head], then alpha[head]
+            const float * qa0 = S.qf + (2 * hp) * kHeadDim;
+            const float * qa1 = qa0 + kHeadDim;
+            for (int i = 0; i < share; ++i) {
+                const bool ready = mbar_wait(&S.full[warp][cst], cph, kWaitNs);
+                if (!__all_sync(kFull, ready)) {
+                    S.abort_flag = 1;
+                    break;
                 }
-            } else {
-                const int row = mrow + ((mi & 1) << 3);
-                const __half2 * dk = reinterpret_cast<const __half2 *>(sk + TILE);
+                const int lp = it.page_begin + warp + kWarps * i;
+                uint8_t * sk = S.stage[warp][cst];
+                uint8_t * sv = sk + TILE;
+                if (do_append && lp == last_page) patch(sk, sv);
+                float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 8
+                for (int ch = 0; ch < kHeadDim / 4; ++ch) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(sk + f32_chunk_off(t, ch));
+                    const float4 a = *reinterpret_cast<const float4 *>(qa0 + 4 * ch);
+                    const float4 b = *reinterpret_cast<const float4 *>(qa1 + 4 * ch);
+                    s0 = fmaf(a.x, k4.x, s0);
+                    s0 = fmaf(a.y, k4.y, s0);
+                    s0 = fmaf(a.z, k4.z, s0);
+                    s0 = fmaf(a.w, k4.w, s0);
+                    s1 = fmaf(b.x, k4.x, s1);
+                    s1 = fmaf(b.y, k4.y, s1);
+                    s1 = fmaf(b.z, k4.z, s1);
+                    s1 = fmaf(b.w, k4.w, s1);
+                }
+                const int pos = lp * kBlockTokens + t;
+                if (pos < rd.win_start || pos > rd.pos) s0 = s1 = -INFINITY;
+                float mx0 = s0, mx1 = s1;
 #pragma unroll
-                for (int blk = 0; blk < 4; ++blk) {
-                    // w0 / w2: tokens 0-7, dims 0-15 / 16-31 of the block; w1 / w3: tokens 8-15
-                    uint32_t w0, w1, w2, w3;
-                    ldsm_x4(kbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
-                    int t0[4], t1[4];
-                    imma16832(t0, qa[2 * blk][0], qa[2 * blk][1], qa[2 * blk + 1][0], qa[2 * blk + 1][1], w0, w2);
-                    imma16832(t1, qa[2 * blk][0], qa[2 * blk][1], qa[2 * blk + 1][0], qa[2 * blk + 1][1], w1, w3);
-                    // t[0], t[1]: hi dots of head g, tokens 2c, 2c+1; t[2], t[3]: lo dots
-                    const float2 d01 = __half22float2(dk[(blk * kBlockTokens + 2 * c) >> 1]);
-                    const float2 d89 = __half22float2(dk[(blk * kBlockTokens + 8 + 2 * c) >> 1]);
-                    s0[0] = fmaf((float) (t0[0] * 254 + t0[2]), d01.x, s0[0]);
-                    s0[1] = fmaf((float) (t0[1] * 254 + t0[3]), d01.y, s0[1]);
-                    s1[0] = fmaf((float) (t1[0] * 254 + t1[2]), d89.x, s1[0]);
-                    s1[1] = fmaf((float) (t1[1] * 254 + t1[3]), d89.y, s1[1]);
+                for (int o = 1; o < 16; o <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, o));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, o));
                 }
-                s0[0] *= qs;
-                s0[1] *= qs;
-                s1[0] *= qs;
-                s1[1] *= qs;
+                // every page of a split holds at least one position of the window
+                const float mn0 = fmaxf(m2[0], mx0), mn1 = fmaxf(m2[1], mx1);
+                const float al0 = exp2f(m2[0] - mn0), al1 = exp2f(m2[1] - mn1);
+                const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1);
+                m2[0] = mn0;
+                m2[1] = mn1;
+                l2[0] = l2[0] * al0 + p0;
+                l2[1] = l2[1] * al1 + p1;
+                *reinterpret_cast<float2 *>(pw + t * kGroup + 2 * hp) = make_float2(p0, p1);
+                if (t == 0) *reinterpret_cast<float2 *>(pw + kBlockTokens * kGroup + 2 * hp) = make_float2(al0, al1);
+                __syncwarp();
+                const float4 al = *reinterpret_cast<const float4 *>(pw + kBlockTokens * kGroup);
+                const float alv[kGroup] = {al.x, al.y, al.z, al.w};
+#pragma unroll
+                for (int h = 0; h < kGroup; ++h) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) of[h][j] *= alv[h];
+                }
+#pragma unroll
+                for (int tt = 0; tt < kBlockTokens; ++tt) {
+                    const float4 v4 = *reinterpret_cast<const float4 *>(sv + f32_chunk_off(tt, lane));
+                    const float4 pp = *reinterpret_cast<const float4 *>(pw + tt * kGroup);
+                    const float pv[kGroup] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        of[h][0] = fmaf(pv[h], v4.x, of[h][0]);
+                        of[h][1] = fmaf(pv[h], v4.y, of[h][1]);
+                        of[h][2] = fmaf(pv[h], v4.z, of[h][2]);
+                        of[h][3] = fmaf(pv[h], v4.w, of[h][3]);
+                    }
+                }
+                __syncwarp();  // pw is rewritten by the next page
+                ++seq_consumed;
+                cst = cst + 1 == ST ? 0 : cst + 1;
+                if (cst == 0) cph ^= 1u;
+                pump(seq_consumed);
             }
+            // ---- this warp's softmax state and O for the merge -----------------
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) {
+                l2[0] += __shfl_xor_sync(kFull, l2[0], o);
+                l2[1] += __shfl_xor_sync(kFull, l2[1], o);
+            }
+            if (t == 0) {
+                S.wm[warp][2 * hp] = m2[0];
+                S.wm[warp][2 * hp + 1] = m2[1];
+                S.wl[warp][2 * hp] = l2[0];
+                S.wl[warp][2 * hp + 1] = l2[1];
+            }
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h)
+                *reinterpret_cast<float4 *>(S.merge + (warp * kGroup + h) * kHeadDim + 4 * lane) =
+                    make_float4(of[h][0], of[h][1], of[h][2], of[h][3]);
+        } else {
+            float o[8][4];
+    #pragma unroll
+            for (int mb = 0; mb < 8; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.0f;
+            float m_run = -INFINITY;
+            float l_part = 0.0f;
+            // This lane's scores of head g for tokens 2c, 2c+1, 8+2c, 9+2c of one
+            // page (log2 domain), masked to the row's window.
+            auto page_scores = [&](const uint8_t * sk, int lp, float (&sc)[4]) {
+                // ---- S^T = Q K^T for the page's 16 tokens (two n-blocks of 8) ---
+                float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                float s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const uint32_t kbase = smem_u32(sk);
+                if constexpr (DT == 1) {
+                    const int row = mrow + ((mi >> 1) << 3);
+    #pragma unroll
+                    for (int ks = 0; ks < 8; ++ks) {
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4(kbase + f16_chunk_off(row, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+                        mma16816(s0, qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+                        mma16816(s1, qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+                    }
+                } else {
+                    const int row = mrow + ((mi & 1) << 3);
+                    const __half2 * dk = reinterpret_cast<const __half2 *>(sk + TILE);
+    #pragma unroll
+                    for (int blk = 0; blk < 4; ++blk) {
+                        // w0 / w2: tokens 0-7, dims 0-15 / 16-31 of the block; w1 / w3: tokens 8-15
+                        uint32_t w0, w1, w2, w3;
+                        ldsm_x4(kbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
+                        int t0[4], t1[4];
+                        imma16832(t0, qa[2 * blk][0], qa[2 * blk][1], qa[2 * blk + 1][0], qa[2 * blk + 1][1], w0, w2);
+                        imma16832(t1, qa[2 * blk][0], qa[2 * blk][1], qa[2 * blk + 1][0], qa[2 * blk + 1][1], w1, w3);
+                        // t[0], t[1]: hi dots of head g, tokens 2c, 2c+1; t[2], t[3]: lo dots
+                        const float2 d01 = __half22float2(dk[(blk * kBlockTokens + 2 * c) >> 1]);
+                        const float2 d89 = __half22float2(dk[(blk * kBlockTokens + 8 + 2 * c) >> 1]);
+                        s0[0] = fmaf((float) (t0[0] * 254 + t0[2]), d01.x, s0[0]);
+                        s0[1] = fmaf((float) (t0[1] * 254 + t0[3]), d01.y, s0[1]);
+                        s1[0] = fmaf((float) (t1[0] * 254 + t1[2]), d89.x, s1[0]);
+                        s1[1] = fmaf((float) (t1[1] * 254 + t1[3]), d89.y, s1[1]);
+                    }
+                    s0[0] *= qs;
+                    s0[1] *= qs;
+                    s1[0] *= qs;
+                    s1[1] *= qs;
+                }
 
-            const int tp = lp * kBlockTokens;
-            sc[0] = s0[0];
-            sc[1] = s0[1];
-            sc[2] = s1[0];
-            sc[3] = s1[1];
-            // Only a page that the window cuts (a split's first page when the
-            // ring has slid, the row's last page) needs the position mask; the
-            // test is warp-uniform.  Lanes 16-31 (padding heads) are not
-            // masked: their probabilities are forced to 0 below and they never
-            // meet the real lanes in a reduction.
-            if (tp < rd.win_start || tp + kBlockTokens - 1 > rd.pos) {
-                const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int pos = tp + tk[j];
-                    if (pos < rd.win_start || pos > rd.pos) sc[j] = -INFINITY;
+                const int tp = lp * kBlockTokens;
+                sc[0] = s0[0];
+                sc[1] = s0[1];
+                sc[2] = s1[0];
+                sc[3] = s1[1];
+                // Only a page that the window cuts (a split's first page when the
+                // ring has slid, the row's last page) needs the position mask; the
+                // test is warp-uniform.  Lanes 16-31 (padding heads) are not
+                // masked: their probabilities are forced to 0 below and they never
+                // meet the real lanes in a reduction.
+                if (tp < rd.win_start || tp + kBlockTokens - 1 > rd.pos) {
+                    const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
+    #pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int pos = tp + tk[j];
+                        if (pos < rd.win_start || pos > rd.pos) sc[j] = -INFINITY;
+                    }
                 }
-            }
-        };
-        // O^T += V^T P^T for one page, P as f16 pairs (tokens 2c,2c+1 | 8+2c,9+2c).
-        auto page_values = [&](const uint8_t * sv, __half2 p01, __half2 p89) {
-            // ---- O^T += V^T P^T ---------------------------------------------
-            const uint32_t vbase = smem_u32(sv);
-            if constexpr (DT == 1) {
-                const uint32_t b0 = h2_bits(p01), b1 = h2_bits(p89);
-                const int row = mrow + ((mi >> 1) << 3);
-#pragma unroll
-                for (int mb = 0; mb < 8; ++mb) {
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4_t(vbase + f16_chunk_off(row, 2 * mb + (mi & 1)), a0, a1, a2, a3);
-                    mma16816(o[mb], a0, a1, a2, a3, b0, b1);
+            };
+            // O^T += V^T P^T for one page, P as f16 pairs (tokens 2c,2c+1 | 8+2c,9+2c).
+            auto page_values = [&](const uint8_t * sv, __half2 p01, __half2 p89) {
+                // ---- O^T += V^T P^T ---------------------------------------------
+                const uint32_t vbase = smem_u32(sv);
+                if constexpr (DT == 1) {
+                    const uint32_t b0 = h2_bits(p01), b1 = h2_bits(p89);
+                    const int row = mrow + ((mi >> 1) << 3);
+    #pragma unroll
+                    for (int mb = 0; mb < 8; ++mb) {
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(vbase + f16_chunk_off(row, 2 * mb + (mi & 1)), a0, a1, a2, a3);
+                        mma16816(o[mb], a0, a1, a2, a3, b0, b1);
+                    }
+                } else {
+                    const int row = mrow + ((mi & 1) << 3);
+                    const __half2 * dv = reinterpret_cast<const __half2 *>(sv + TILE);
+                    // P as rounded for the row sum, x128 (exact) to keep P * d in the
+                    // f16 normal range; the block scale is folded in with one f16 rounding
+                    const __half2 p01s = __hmul2(p01, __float2half2_rn(128.0f));
+                    const __half2 p89s = __hmul2(p89, __float2half2_rn(128.0f));
+    #pragma unroll
+                    for (int blk = 0; blk < 4; ++blk) {
+                        const uint32_t b0 = h2_bits(__hmul2(p01s, dv[(blk * kBlockTokens + 2 * c) >> 1]));
+                        const uint32_t b1 = h2_bits(__hmul2(p89s, dv[(blk * kBlockTokens + 8 + 2 * c) >> 1]));
+                        uint32_t w0, w1, w2, w3;
+                        ldsm_x4_t(vbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
+                        w0 ^= 0x80808080u;
+                        w1 ^= 0x80808080u;
+                        w2 ^= 0x80808080u;
+                        w3 ^= 0x80808080u;
+                        mma16816(o[2 * blk], s8pair_to_h2(w0, 0x4240u), s8pair_to_h2(w0, 0x4341u),
+                                 s8pair_to_h2(w1, 0x4240u), s8pair_to_h2(w1, 0x4341u), b0, b1);
+                        mma16816(o[2 * blk + 1], s8pair_to_h2(w2, 0x4240u), s8pair_to_h2(w2, 0x4341u),
+                                 s8pair_to_h2(w3, 0x4240u), s8pair_to_h2(w3, 0x4341u), b0, b1);
+                    }
                 }
-            } else {
-                const int row = mrow + ((mi & 1) << 3);
-                const __half2 * dv = reinterpret_cast<const __half2 *>(sv + TILE);
-                // P as rounded for the row sum, x128 (exact) to keep P * d in the
-                // f16 normal range; the block scale is folded in with one f16 rounding
-                const __half2 p01s = __hmul2(p01, __float2half2_rn(128.0f));
-                const __half2 p89s = __hmul2(p89, __float2half2_rn(128.0f));
-#pragma unroll
-                for (int blk = 0; blk < 4; ++blk) {
-                    const uint32_t b0 = h2_bits(__hmul2(p01s, dv[(blk * kBlockTokens + 2 * c) >> 1]));
-                    const uint32_t b1 = h2_bits(__hmul2(p89s, dv[(blk * kBlockTokens + 8 + 2 * c) >> 1]));
-                    uint32_t w0, w1, w2, w3;
-                    ldsm_x4_t(vbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
-                    w0 ^= 0x80808080u;
-                    w1 ^= 0x80808080u;
-                    w2 ^= 0x80808080u;
-                    w3 ^= 0x80808080u;
-                    mma16816(o[2 * blk], s8pair_to_h2(w0, 0x4240u), s8pair_to_h2(w0, 0x4341u),
-                             s8pair_to_h2(w1, 0x4240u), s8pair_to_h2(w1, 0x4341u), b0, b1);
-                    mma16816(o[2 * blk + 1], s8pair_to_h2(w2, 0x4240u), s8pair_to_h2(w2, 0x4341u),
-                             s8pair_to_h2(w3, 0x4240u), s8pair_to_h2(w3, 0x4341u), b0, b1);
+            };
+            // Pages are consumed one at a time (f16) or two at a time (q8_0: the two
+            // pages' score, softmax and value work interleave, and the softmax
+            // bookkeeping is shared).
+            int i = 0;
+            while (i < share) {
+                const bool two = DT == 8 && i + 1 < share;
+                const int stA = cst;
+                const bool wrapA = cst + 1 == ST;
+                const int stB = wrapA ? 0 : cst + 1;
+                const uint32_t phB = wrapA ? cph ^ 1u : cph;
+                bool ready = mbar_wait(&S.full[warp][stA], cph, kWaitNs);
+                if (two) ready = ready && mbar_wait(&S.full[warp][stB], phB, kWaitNs);
+                // the outcome is made warp-uniform so the warp never splits
+                if (!__all_sync(kFull, ready)) {
+                    S.abort_flag = 1;
+                    break;
                 }
-            }
-        };
-        // Pages are consumed one at a time (f16) or two at a time (q8_0: the two
-        // pages' score, softmax and value work interleave, and the softmax
-        // bookkeeping is shared).
-        int i = 0;
-        while (i < share) {
-            const bool two = DT == 8 && i + 1 < share;
-            const int stA = cst;
-            const bool wrapA = cst + 1 == ST;
-            const int stB = wrapA ? 0 : cst + 1;
-            const uint32_t phB = wrapA ? cph ^ 1u : cph;
-            bool ready = mbar_wait(&S.full[warp][stA], cph, kWaitNs);
-            if (two) ready = ready && mbar_wait(&S.full[warp][stB], phB, kWaitNs);
-            // the outcome is made warp-uniform so the warp never splits
-            if (!__all_sync(kFull, ready)) {
-                S.abort_flag = 1;
-                break;
-            }
-            const int lpA = it.page_begin + warp + kWarps * i;
-            const int lpB = lpA + kWarps;
-            uint8_t * skA = S.stage[warp][stA];
-            uint8_t * skB = S.stage[warp][stB];
-            if (do_append && lpA == last_page) patch(skA, skA + TILE + SCALE);
-            if (two && do_append && lpB == last_page) patch(skB, skB + TILE + SCALE);
-            float scA[4], scB[4];
-            page_scores(skA, lpA, scA);
-            if (two) {
-                page_scores(skB, lpB, scB);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) scB[j] = -INFINITY;
-            }
-
-            // ---- online softmax (log2 domain) for head g --------------------
-            float mx = fmaxf(fmaxf(fmaxf(scA[0], scA[1]), fmaxf(scA[2], scA[3])),
-                             fmaxf(fmaxf(scB[0], scB[1]), fmaxf(scB[2], scB[3])));
-            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = real ? exp2f(m_run - m_new) : 1.0f;
-            float prA[4], prB[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                prA[j] = real ? exp2f(scA[j] - m_new) : 0.0f;
-                prB[j] = real ? exp2f(scB[j] - m_new) : 0.0f;
-            }
-            if (real) m_run = m_new;
-            const __half2 p01A = __floats2half2_rn(prA[0], prA[1]);
-            const __half2 p89A = __floats2half2_rn(prA[2], prA[3]);
-            const __half2 p01B = __floats2half2_rn(prB[0], prB[1]);
-            const __half2 p89B = __floats2half2_rn(prB[2], prB[3]);
-            {
-                const float2 f0 = __half22float2(p01A), f1 = __half22float2(p89A);
-                float add = (f0.x + f0.y) + (f1.x + f1.y);
+                const int lpA = it.page_begin + warp + kWarps * i;
+                const int lpB = lpA + kWarps;
+                uint8_t * skA = S.stage[warp][stA];
+                uint8_t * skB = S.stage[warp][stB];
+                if (do_append && lpA == last_page) patch(skA, skA + TILE + SCALE);
+                if (two && do_append && lpB == last_page) patch(skB, skB + TILE + SCALE);
+                float scA[4], scB[4];
+                page_scores(skA, lpA, scA);
                 if (two) {
-                    const float2 g0 = __half22float2(p01B), g1 = __half22float2(p89B);
-                    add += (g0.x + g0.y) + (g1.x + g1.y);
+                    page_scores(skB, lpB, scB);
+                } else {
+    #pragma unroll
+                    for (int j = 0; j < 4; ++j) scB[j] = -INFINITY;
                 }
-                l_part = l_part * alpha + add;
-            }
-            // rescale O^T columns (heads 2c, 2c+1) when any running max moved
-            if (__any_sync(kFull, alpha != 1.0f)) {
-                const float a_lo = __shfl_sync(kFull, alpha, (8 * c) & 31);
-                const float a_hi = __shfl_sync(kFull, alpha, (8 * c + 4) & 31);
-#pragma unroll
-                for (int mb = 0; mb < 8; ++mb) {
-                    o[mb][0] *= a_lo;
-                    o[mb][1] *= a_hi;
-                    o[mb][2] *= a_lo;
-                    o[mb][3] *= a_hi;
-                }
-            }
-            page_values(skA + TILE + SCALE, p01A, p89A);
-            if (two) page_values(skB + TILE + SCALE, p01B, p89B);
-            __syncwarp();
-            seq_consumed += two ? 2 : 1;
-            if (two) {
-                const bool wrapB = stB + 1 == ST;
-                cst = wrapB ? 0 : stB + 1;
-                cph = wrapB ? phB ^ 1u : phB;
-            } else {
-                cst = stB;
-                cph = phB;
-            }
-            i += two ? 2 : 1;
-            pump(seq_consumed);
-        }
 
-        // ---- merge the 4 warps' partial softmax states -----------------------
-        {
-            float l_h = l_part + __shfl_xor_sync(kFull, l_part, 1);
-            l_h += __shfl_xor_sync(kFull, l_h, 2);
-            if (real && c == 0) {
-                S.wm[warp][g] = m_run;
-                S.wl[warp][g] = l_h;
+                // ---- online softmax (log2 domain) for head g --------------------
+                float mx = fmaxf(fmaxf(fmaxf(scA[0], scA[1]), fmaxf(scA[2], scA[3])),
+                                 fmaxf(fmaxf(scB[0], scB[1]), fmaxf(scB[2], scB[3])));
+                mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+                const float m_new = fmaxf(m_run, mx);
+                const float alpha = real ? exp2f(m_run - m_new) : 1.0f;
+                float prA[4], prB[4];
+    #pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    prA[j] = real ? exp2f(scA[j] - m_new) : 0.0f;
+                    prB[j] = real ? exp2f(scB[j] - m_new) : 0.0f;
+                }
+                if (real) m_run = m_new;
+                const __half2 p01A = __floats2half2_rn(prA[0], prA[1]);
+                const __half2 p89A = __floats2half2_rn(prA[2], prA[3]);
+                const __half2 p01B = __floats2half2_rn(prB[0], prB[1]);
+                const __half2 p89B = __floats2half2_rn(prB[2], prB[3]);
+                {
+                    const float2 f0 = __half22float2(p01A), f1 = __half22float2(p89A);
+                    float add = (f0.x + f0.y) + (f1.x + f1.y);
+                    if (two) {
+                        const float2 g0 = __half22float2(p01B), g1 = __half22float2(p89B);
+                        add += (g0.x + g0.y) + (g1.x + g1.y);
+                    }
+                    l_part = l_part * alpha + add;
+                }
+                // rescale O^T columns (heads 2c, 2c+1) when any running max moved
+                if (__any_sync(kFull, alpha != 1.0f)) {
+                    const float a_lo = __shfl_sync(kFull, alpha, (8 * c) & 31);
+                    const float a_hi = __shfl_sync(kFull, alpha, (8 * c + 4) & 31);
+    #pragma unroll
+                    for (int mb = 0; mb < 8; ++mb) {
+                        o[mb][0] *= a_lo;
+                        o[mb][1] *= a_hi;
+                        o[mb][2] *= a_lo;
+                        o[mb][3] *= a_hi;
+                    }
+                }
+                page_values(skA + TILE + SCALE, p01A, p89A);
+                if (two) page_values(skB + TILE + SCALE, p01B, p89B);
+                __syncwarp();
+                seq_consumed += two ? 2 : 1;
+                if (two) {
+                    const bool wrapB = stB + 1 == ST;
+                    cst = wrapB ? 0 : stB + 1;
+                    cph = wrapB ? phB ^ 1u : phB;
+                } else {
+                    cst = stB;
+                    cph = phB;
+                }
+                i += two ? 2 : 1;
+                pump(seq_consumed);
             }
-            if (c < 2) {
-                const float post = DT == 1 ? 1.0f : 1.0f / 128.0f;
-#pragma unroll
-                for (int mb = 0; mb < 8; ++mb) {
-                    const int d0 = DT == 1 ? 16 * mb + g : 16 * mb + 2 * g;
-                    const int d1 = DT == 1 ? 16 * mb + 8 + g : 16 * mb + 2 * g + 1;
-                    float * h0 = S.merge + (warp * kGroup + 2 * c) * kHeadDim;
-                    float * h1 = h0 + kHeadDim;
-                    h0[d0] = o[mb][0] * post;
-                    h1[d0] = o[mb][1] * post;
-                    h0[d1] = o[mb][2] * post;
-                    h1[d1] = o[mb][3] * post;
+
+            // ---- merge the 4 warps' partial softmax states -----------------------
+            {
+                float l_h = l_part + __shfl_xor_sync(kFull, l_part, 1);
+                l_h += __shfl_xor_sync(kFull, l_h, 2);
+                if (real && c == 0) {
+                    S.wm[warp][g] = m_run;
+                    S.wl[warp][g] = l_h;
+                }
+                if (c < 2) {
+                    const float post = DT == 1 ? 1.0f : 1.0f / 128.0f;
+    #pragma unroll
+                    for (int mb = 0; mb < 8; ++mb) {
+                        const int d0 = DT == 1 ? 16 * mb + g : 16 * mb + 2 * g;
+                        const int d1 = DT == 1 ? 16 * mb + 8 + g : 16 * mb + 2 * g + 1;
+                        float * h0 = S.merge + (warp * kGroup + 2 * c) * kHeadDim;
+                        float * h1 = h0 + kHeadDim;
+                        h0[d0] = o[mb][0] * post;
+                        h1[d0] = o[mb][1] * post;
+                        h0[d1] = o[mb][2] * post;
+                        h1[d1] = o[mb][3] * post;
+                    }
                 }
             }
         }
@@ -853,13 +1001,13 @@ __global__ void gather_kernel(const GatherParams p) {
     if (pg < 0 || pg >= p.n_blocks) return;
     const int64_t tile = (int64_t) pg * p.n_kv + kvh;
     const int tok = (int) (pos % kBlockTokens);
-    constexpr int row_bytes = DT == 1 ? kHeadDim * 2 : kHeadDim;
+    constexpr int row_bytes = DT == 0 ? kHeadDim * 4 : DT == 1 ? kHeadDim * 2 : kHeadDim;
     constexpr int chunks = row_bytes / 16;
     const int64_t dst = ((int64_t) r * p.n_kv + kvh) * row_bytes;
     const uint8_t * kt = p.k_data + tile * Cfg<DT>::kTile;
     const uint8_t * vt = p.v_data + tile * Cfg<DT>::kTile;
     for (int ch = threadIdx.x; ch < chunks; ch += blockDim.x) {
-        const int off = DT == 1 ? f16_chunk_off(tok, ch) : q8_chunk_off(tok, ch);
+        const int off = DT == 0 ? f32_chunk_off(tok, ch) : DT == 1 ? f16_chunk_off(tok, ch) : q8_chunk_off(tok, ch);
         *reinterpret_cast<uint4 *>(p.k_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(kt + off);
         *reinterpret_cast<uint4 *>(p.v_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(vt + off);
     }
@@ -945,25 +1093,31 @@ cudaError_t launch_wait_probe(int32_t * error, uint64_t limit_ns, cudaStream_t s
     return cudaGetLastError();
 }
 
-int decode_smem_bytes(int dtype) { return dtype == 8 ? (int) sizeof(Smem<8>) : (int) sizeof(Smem<1>); }
+int decode_smem_bytes(int dtype) {
+    return dtype == 8 ? (int) sizeof(Smem<8>) : dtype == 0 ? (int) sizeof(Smem<0>) : (int) sizeof(Smem<1>);
+}
+
+template <int DT>
+int ctas_per_sm_t() {
+    int n = 0;
+    if (cudaFuncSetAttribute(decode_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<DT>)) !=
+        cudaSuccess)
+        return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<DT>, NT, sizeof(Smem<DT>)) != cudaSuccess) return 0;
+    return n;
+}
 
 int decode_ctas_per_sm(int dtype) {
-    int n = 0;
-    if (dtype == 8) {
-        if (cudaFuncSetAttribute(decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<8>)) != cudaSuccess)
-            return 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<8>, NT, sizeof(Smem<8>)) != cudaSuccess) return 0;
-    } else {
-        if (cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<1>)) != cudaSuccess)
-            return 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<1>, NT, sizeof(Smem<1>)) != cudaSuccess) return 0;
-    }
-    return n;
+    if (dtype == 8) return ctas_per_sm_t<8>();
+    if (dtype == 0) return ctas_per_sm_t<0>();
+    return ctas_per_sm_t<1>();
 }
 
 cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream, bool pdl) {
     if (p.n_items <= 0 || p.n_ctas <= 0) return cudaSuccess;
-    return p.dtype == 8 ? launch_decode_t<8>(p, stream, pdl) : launch_decode_t<1>(p, stream, pdl);
+    if (p.dtype == 8) return launch_decode_t<8>(p, stream, pdl);
+    if (p.dtype == 0) return launch_decode_t<0>(p, stream, pdl);
+    return launch_decode_t<1>(p, stream, pdl);
 }
 
 // ---------------------------------------------------------------------------
@@ -1019,7 +1173,9 @@ cudaError_t launch_decode_static_scratch(const DecodeParams & params, cudaStream
     // start at zero (partials are written before they are read).
     e = cudaMemsetAsync(p.counters, 0, (size_t) p.n_rows * p.n_kv * sizeof(int32_t), stream);
     if (e != cudaSuccess) return e;
-    return p.dtype == 8 ? launch_decode_t<8>(p, stream, false) : launch_decode_t<1>(p, stream, false);
+    if (p.dtype == 8) return launch_decode_t<8>(p, stream, false);
+    if (p.dtype == 0) return launch_decode_t<0>(p, stream, false);
+    return launch_decode_t<1>(p, stream, false);
 }
 
 cudaError_t launch_append(const AppendParams & p, cudaStream_t stream) {
@@ -1027,6 +1183,8 @@ cudaError_t launch_append(const AppendParams & p, cudaStream_t stream) {
     const dim3 grid((unsigned) (p.n_rows * p.n_kv));
     if (p.dtype == 8) {
         append_kernel<8><<<grid, NT, 0, stream>>>(p);
+    } else if (p.dtype == 0) {
+        append_kernel<0><<<grid, NT, 0, stream>>>(p);
     } else {
         append_kernel<1><<<grid, NT, 0, stream>>>(p);
     }
@@ -1044,6 +1202,8 @@ cudaError_t launch_gather(const GatherParams & p, cudaStream_t stream) {
     const dim3 grid((unsigned) (p.n * p.n_kv));
     if (p.dtype == 8) {
         gather_kernel<8><<<grid, 32, 0, stream>>>(p);
+    } else if (p.dtype == 0) {
+        gather_kernel<0><<<grid, 32, 0, stream>>>(p);
     } else {
         gather_kernel<1><<<grid, 32, 0, stream>>>(p);
     }

@@ -89,7 +89,7 @@ struct DecodeParams {
     int32_t * counters;      // [max_rows][n_kv], zero between launches
     int32_t * error;         // device error word (0 = ok)
     int32_t fuse_append;     // 1: rows flagged kRowAppend append first
-    int32_t dtype;           // 1 = f16, 8 = q8_0
+    int32_t dtype;           // 0 = f32, 1 = f16, 8 = q8_0
 };
 
 struct AppendParams {

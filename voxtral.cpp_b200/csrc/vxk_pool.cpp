@@ -239,6 +239,10 @@ T * device_alloc(vxk_pool * p, size_t bytes) {
     return static_cast<T *>(ptr);
 }
 
+// Bytes of one cache value in the pool's tiles (q8_0: the int8 value; its
+// block scales are stored apart).
+int64_t elem_bytes(vxk_dtype dt) { return dt == VXK_DTYPE_Q8_0 ? 1 : dt == VXK_DTYPE_F32 ? 4 : 2; }
+
 // Reads a caller's config: fields past the caller's struct_size (added in a
 // later version of the struct) keep the defaults.
 vxk_pool_config read_config(const vxk_pool_config * in) {
@@ -260,8 +264,8 @@ void validate_config(const vxk_pool_config & c) {
         fail(VXK_STATUS_INVALID_ARGUMENT, "capacity must be a positive multiple of block_tokens");
     if (c.n_layers < 1 || c.n_blocks < 1 || c.max_streams < 1 || c.max_rows < 1 || c.max_position < 1)
         fail(VXK_STATUS_INVALID_ARGUMENT, "n_layers, n_blocks, max_streams, max_rows, max_position must be >= 1");
-    if (c.dtype != VXK_DTYPE_F16 && c.dtype != VXK_DTYPE_Q8_0)
-        fail(VXK_STATUS_INVALID_ARGUMENT, "decoder pool dtype must be F16 or Q8_0");
+    if (c.dtype != VXK_DTYPE_F16 && c.dtype != VXK_DTYPE_Q8_0 && c.dtype != VXK_DTYPE_F32)
+        fail(VXK_STATUS_INVALID_ARGUMENT, "decoder pool dtype must be F16, Q8_0 or F32");
     if (!(c.rope_theta > 0.0f)) fail(VXK_STATUS_INVALID_ARGUMENT, "rope_theta must be positive");
 }
 
@@ -688,7 +692,7 @@ vxk_status vxk_pool_create(const vxk_pool_config * config, vxk_pool ** out_pool)
         const vxk_pool_config & c = p->cfg;
         p->bt_cap = c.capacity / c.block_tokens;
         const bool q8 = c.dtype == VXK_DTYPE_Q8_0;
-        p->tile_data_bytes = (int64_t) c.block_tokens * c.head_dim * (q8 ? 1 : 2);
+        p->tile_data_bytes = (int64_t) c.block_tokens * c.head_dim * elem_bytes(c.dtype);
         p->tile_scale_bytes = q8 ? (int64_t) c.block_tokens * (c.head_dim / vxk::kQ8Block) * 2 : 0;
         p->page_data_bytes = p->tile_data_bytes * c.n_kv_heads;
         p->page_scale_bytes = p->tile_scale_bytes * c.n_kv_heads;
@@ -804,7 +808,7 @@ vxk_status vxk_pool_get_stats(const vxk_pool * pool, vxk_pool_stats * out) {
 int64_t vxk_pool_row_bytes(const vxk_pool * pool) {
     if (!pool) return -1;
     const int64_t n = (int64_t) pool->cfg.n_kv_heads * pool->cfg.head_dim;
-    return pool->cfg.dtype == VXK_DTYPE_Q8_0 ? n / 32 * 34 : n * 2;
+    return pool->cfg.dtype == VXK_DTYPE_Q8_0 ? n / 32 * 34 : n * elem_bytes(pool->cfg.dtype);
 }
 
 vxk_status vxk_stream_open(vxk_pool * pool, int32_t * out_stream) {
@@ -1028,10 +1032,24 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
         const size_t hd = (size_t) c.head_dim;
         const size_t q_per_row = (size_t) c.n_q_heads * hd;
         const size_t kv_per_row = (size_t) c.n_kv_heads * hd;
-        const size_t layer_floats = (size_t) c.max_rows * (q_per_row * 2 + kv_per_row * 2);
-        if (!pool->d_io) {
-            pool->io_bytes = layer_floats * (size_t) c.n_layers * sizeof(float);
-            pool->d_io = device_alloc<float>(pool, pool->io_bytes);
+        if (n_streams <= 0 || n_streams > c.max_rows) fail(VXK_STATUS_INVALID_ARGUMENT, "bad stream count");
+        // Device staging for this call's rows of every layer, grown on demand
+        // (not sized by max_rows: a pool planned for long prefills would
+        // otherwise hold gigabytes for a step of a few streams).
+        const size_t layer_floats = (size_t) n_streams * (q_per_row * 2 + kv_per_row * 2);
+        const size_t need = layer_floats * (size_t) c.n_layers * sizeof(float);
+        if (pool->io_bytes < need) {
+            if (pool->d_io) {
+                VXK_CUDA(cudaStreamSynchronize(cs));
+                cudaFree(pool->d_io);
+                pool->device_bytes -= (int64_t) pool->io_bytes;
+                pool->d_io = nullptr;
+                pool->io_bytes = 0;
+            }
+            pool->d_io = device_alloc<float>(pool, need);
+            pool->io_bytes = need;
+        }
+        if (!pool->h2d) {
             VXK_CUDA(cudaStreamCreateWithFlags(&pool->h2d, cudaStreamNonBlocking));
             VXK_CUDA(cudaStreamCreateWithFlags(&pool->d2h, cudaStreamNonBlocking));
             pool->ev_in.resize((size_t) c.n_layers);
@@ -1055,9 +1073,9 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
         VXK_CUDA(cudaStreamWaitEvent(pool->h2d, pool->ev_begin, 0));
         VXK_CUDA(cudaStreamWaitEvent(pool->d2h, pool->ev_begin, 0));
         auto dq = [&](int32_t l) { return pool->d_io + (size_t) l * layer_floats; };
-        auto dk = [&](int32_t l) { return dq(l) + (size_t) c.max_rows * q_per_row; };
-        auto dv = [&](int32_t l) { return dk(l) + (size_t) c.max_rows * kv_per_row; };
-        auto dout = [&](int32_t l) { return dv(l) + (size_t) c.max_rows * kv_per_row; };
+        auto dk = [&](int32_t l) { return dq(l) + rows * q_per_row; };
+        auto dv = [&](int32_t l) { return dk(l) + rows * kv_per_row; };
+        auto dout = [&](int32_t l) { return dv(l) + rows * kv_per_row; };
         for (int32_t l = 0; l < c.n_layers; ++l) {
             VXK_CUDA(cudaMemcpyAsync(dq(l), h_q + (size_t) l * rows * q_per_row, rows * q_per_row * sizeof(float),
                                      cudaMemcpyHostToDevice, pool->h2d));
@@ -1235,7 +1253,7 @@ vxk_status vxk_read_rows(vxk_pool * pool, int32_t layer, int32_t stream, int64_t
         const bool q8 = pool->cfg.dtype == VXK_DTYPE_Q8_0;
         const int32_t nkv = pool->cfg.n_kv_heads;
         const size_t elems = (size_t) n * (size_t) nkv * vxk::kHeadDim;
-        const size_t data_b = elems * (q8 ? 1 : 2);
+        const size_t data_b = elems * (size_t) elem_bytes(pool->cfg.dtype);
         const size_t scale_b = q8 ? (size_t) n * (size_t) nkv * (vxk::kHeadDim / vxk::kQ8Block) * 2 : 0;
         const size_t need = 2 * align_up(data_b, 256) + 2 * align_up(scale_b, 256);
         if (pool->read_bytes < need) {

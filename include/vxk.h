@@ -379,7 +379,9 @@ typedef struct vxk_enc_config {
     int32_t max_streams;
     int32_t max_new;       /* rows per stream per batch, <= capacity - window */
     int32_t max_position;  /* RoPE table rows */
-    vxk_dtype dtype;       /* BF16 or F16 */
+    vxk_dtype dtype;       /* BF16 (default here), F16, or F32 (the reference's default
+                              encoder cache, src/voxtral.cpp:100-105: exact fp32
+                              rows, attention on the CUDA cores) */
     float rope_theta;      /* 1e6 */
     int32_t reserved;
 } vxk_enc_config;

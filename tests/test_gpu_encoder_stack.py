@@ -20,7 +20,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-BF16, F16 = 30, 1
+BF16, F16, F32 = 30, 1, 0
 STEP_BAR = 5e-2
 EXACT_BAR = 1e-4
 STEM_BAR = 2e-4
@@ -55,7 +55,7 @@ class DeviceEncAttention:
         self.pool.close()
 
 
-@pytest.mark.parametrize("dtype,kind", [(BF16, "q4_k_m"), (F16, "q4_k_m"), (BF16, "q8_0")])
+@pytest.mark.parametrize("dtype,kind", [(BF16, "q4_k_m"), (F16, "q4_k_m"), (F32, "q4_k_m"), (BF16, "q8_0")])
 def test_encoder_stack_matches_oracle(vxk, tmp_path, dtype, kind):
     # q4_k_m: the products on the tcgen05 kernel, the q/v biases added in its
     # store; q8_0: every product on the int8 mma.sync kernel, biases added by

@@ -38,6 +38,14 @@
 // bf16 operands carry 8 mantissa bits, so Q and P are each split into a bf16
 // high part and the bf16 residual (x = hi + lo) and both parts are
 // multiplied; products accumulate in fp32.
+//
+// f32 rings (the reference's default encoder cache, src/voxtral.cpp:100-105)
+// keep fp32 rows (256 B, the 16-byte chunk c of slot s at chunk c ^ (s & 7))
+// and take enc_f32_kernel: the same units on the CUDA cores in fp32, one
+// 128-thread CTA per unit, 128-key tiles of K then V by bulk copy into two
+// shared-memory buffers, scores one key per thread, an exact softmax over the
+// window, and P.V with each thread owning 4 dims of every row over an eighth
+// of the keys.
 #include "vxk_internal.h"
 
 #include <cuda.h>
@@ -246,9 +254,16 @@ __global__ void enc_append_kernel(const EncParams p) {
         const float2 vx = *reinterpret_cast<const float2 *>(p.v + src);
         // byte 4i of the row = chunk i / 4, stored at chunk (i / 4) ^ (slot & 7)
         const int64_t row = ring_index(p, rd.stream, h) * p.ring_slots + rd.slot;
-        const int64_t dst = row * (kEncHd * 2) + ((((i >> 2) ^ (rd.slot & 7))) << 4) + (i & 3) * 4;
-        *reinterpret_cast<uint32_t *>(p.k_ring + dst) = pack2<DT>(kx.x, kx.y);
-        *reinterpret_cast<uint32_t *>(p.v_ring + dst) = pack2<DT>(vx.x, vx.y);
+        if constexpr (DT == 0) {
+            // dims 2i, 2i+1 = bytes 8i of the 256-byte row: chunk i / 2
+            const int64_t dst = row * (kEncHd * 4) + ((((i >> 1) ^ (rd.slot & 7))) << 4) + (i & 1) * 8;
+            *reinterpret_cast<float2 *>(p.k_ring + dst) = kx;
+            *reinterpret_cast<float2 *>(p.v_ring + dst) = vx;
+        } else {
+            const int64_t dst = row * (kEncHd * 2) + ((((i >> 2) ^ (rd.slot & 7))) << 4) + (i & 3) * 4;
+            *reinterpret_cast<uint32_t *>(p.k_ring + dst) = pack2<DT>(kx.x, kx.y);
+            *reinterpret_cast<uint32_t *>(p.v_ring + dst) = pack2<DT>(vx.x, vx.y);
+        }
     }
 }
 
@@ -711,6 +726,267 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// f32 rings: window attention on the CUDA cores
+// ---------------------------------------------------------------------------
+constexpr int kF32Threads = 128;
+constexpr int kF32Tile = 128;                  // keys per tile
+constexpr int kF32MaxKeys = 768;               // window - 1 + 8 rows fits (host checks <= 752)
+constexpr int kF32Rows = 8;                    // rows per group (kEncRowsPerGroup)
+constexpr int kF32RowBytes = kEncHd * 4;       // 256
+
+struct __align__(128) EncF32Smem {
+    float kv[2][kF32Tile * kEncHd];            // two tile buffers (rows swizzled as in the ring)
+    float s[kF32MaxKeys][kF32Rows];            // scores, then probabilities: [key][row]
+    float q[kEncHd][kF32Rows];                 // rotated, scaled queries: [dim][row]
+    float red[kF32Threads / 32][kF32Rows];
+    float inv_l[kF32Rows];
+    uint64_t full[2];
+    int32_t abort_flag;
+};
+static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * 2 * kF32Tile * kEncHd,
+              "P.V partial sums fit the tile buffers");
+
+// One CTA per unit (row group of <= 8 rows of one stream, head).
+__global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    EncF32Smem & S = *reinterpret_cast<EncF32Smem *>(smem_raw);
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(&S.full[0], 1);
+        mbar_init(&S.full[1], 1);
+        S.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // nothing an earlier grid writes is read before this point
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int u = blockIdx.x;
+    const int grp = u / p.n_heads;
+    const int h = u - grp * p.n_heads;
+    const int r0 = p.group_first[grp];
+    const int nr = p.group_first[grp + 1] - r0;
+    const EncRowDesc first = p.rows[r0];
+    const int ws = first.win_start;
+    const int we = p.rows[r0 + nr - 1].pos;
+    const int nkeys = we - ws + 1;
+    if (nr < 1 || nr > kF32Rows || nkeys < 1 || nkeys > kF32MaxKeys) {
+        if (tid == 0 && p.error) atomicCAS(p.error, 0, 1);
+        return;
+    }
+    const int T = (nkeys + kF32Tile - 1) / kF32Tile;
+    const int64_t ring = ring_index(p, first.stream, h);
+    // queries: thread t -> row t / 16, dims 4 (t % 16) .. + 3
+    {
+        const int r = tid >> 4;
+        const int c = tid & 15;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r < nr) {
+            const EncRowDesc rd = p.rows[r0 + r];
+            const float * qr = p.q + ((int64_t) (r0 + r) * p.n_heads + h) * kEncHd + 4 * c;
+            const float2 * cs = p.rope + (int64_t) rd.pos * (kEncHd / 2) + 2 * c;
+            const float2 a = enc_rope_pair(*reinterpret_cast<const float2 *>(qr), cs[0]);
+            const float2 b = enc_rope_pair(*reinterpret_cast<const float2 *>(qr + 2), cs[1]);
+            v = make_float4(a.x * p.scale_log2, a.y * p.scale_log2, b.x * p.scale_log2, b.y * p.scale_log2);
+        }
+        S.q[4 * c + 0][r] = v.x;
+        S.q[4 * c + 1][r] = v.y;
+        S.q[4 * c + 2][r] = v.z;
+        S.q[4 * c + 3][r] = v.w;
+    }
+    __syncthreads();
+    // tile j < T: K keys [128 j, ...); tile j >= T: V keys [128 (j - T), ...)
+    auto issue = [&](int j) {
+        const int jj = j < T ? j : j - T;
+        const int k0 = jj * kF32Tile;
+        const int n = min(kF32Tile, nkeys - k0);
+        const int slot0 = (ws + k0) % p.capacity;
+        const int run = min(n, p.capacity - slot0);
+        const uint8_t * base = (j < T ? p.k_ring : p.v_ring) + ring * p.ring_slots * (int64_t) kF32RowBytes;
+        uint64_t * bar = &S.full[j & 1];
+        float * dst = S.kv[j & 1];
+        const uint64_t policy = evict_first_policy();
+        mbar_expect_tx(bar, (uint32_t) (n * kF32RowBytes));
+        bulk_load(dst, base + (int64_t) slot0 * kF32RowBytes, (uint32_t) (run * kF32RowBytes), bar, policy);
+        if (n > run) bulk_load(dst + run * kEncHd, base, (uint32_t) ((n - run) * kF32RowBytes), bar, policy);
+    };
+    if (tid == 0) issue(0);
+    float acc[kF32Rows][4];
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    const int c4 = tid & 15;     // P.V: dims 4 c4 .. + 3
+    const int kg = tid >> 4;     //       keys kg, kg + 8, ... of each tile
+    bool ok = true;
+    for (int j = 0; j < 2 * T; ++j) {
+        // the other buffer was released by the barrier that ended iteration j - 1
+        if (tid == 0 && j + 1 < 2 * T) issue(j + 1);
+        const bool landed = enc_wait(&S.full[j & 1], (uint32_t) ((j >> 1) & 1), &S.abort_flag, p.error);
+        if (!__syncthreads_and(landed ? 1 : 0)) {
+            ok = false;
+            break;
+        }
+        const float * buf = S.kv[j & 1];
+        if (j < T) {
+            // ---- scores of key 128 j + tid for every row ----------------------
+            const int ki = j * kF32Tile + tid;
+            if (ki < nkeys) {
+                const int kp = ws + ki;
+                const int sw = (kp % p.capacity) & 7;
+                float sc[kF32Rows];
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) sc[r] = 0.0f;
+                const float * kr = buf + tid * kEncHd;
+#pragma unroll 4
+                for (int c = 0; c < kEncHd / 4; ++c) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + 4 * (c ^ sw));
+                    const float kd[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) {
+                        const float4 qa = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][0]);
+                        const float4 qb = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][4]);
+                        sc[0] = fmaf(qa.x, kd[d], sc[0]);
+                        sc[1] = fmaf(qa.y, kd[d], sc[1]);
+                        sc[2] = fmaf(qa.z, kd[d], sc[2]);
+                        sc[3] = fmaf(qa.w, kd[d], sc[3]);
+                        if (nr > 4) {
+                            sc[4] = fmaf(qb.x, kd[d], sc[4]);
+                            sc[5] = fmaf(qb.y, kd[d], sc[5]);
+                            sc[6] = fmaf(qb.z, kd[d], sc[6]);
+                            sc[7] = fmaf(qb.w, kd[d], sc[7]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) {
+                    bool in = r < nr;
+                    if (in) {
+                        const EncRowDesc rd = p.rows[r0 + r];
+                        in = kp >= rd.win_start && kp <= rd.pos;
+                    }
+                    if (!in) sc[r] = -INFINITY;
+                }
+                *reinterpret_cast<float4 *>(&S.s[ki][0]) = make_float4(sc[0], sc[1], sc[2], sc[3]);
+                *reinterpret_cast<float4 *>(&S.s[ki][4]) = make_float4(sc[4], sc[5], sc[6], sc[7]);
+            }
+        } else {
+            // ---- P.V over this tile's keys kg, kg + 8, ... --------------------
+            const int k0 = (j - T) * kF32Tile;
+            const int n = min(kF32Tile, nkeys - k0);
+            for (int i = kg; i < n; i += kF32Threads / 16) {
+                const int ki = k0 + i;
+                const int sw = ((ws + ki) % p.capacity) & 7;
+                const float4 v4 = *reinterpret_cast<const float4 *>(buf + i * kEncHd + 4 * (c4 ^ sw));
+                const float4 pa = *reinterpret_cast<const float4 *>(&S.s[ki][0]);
+                const float pr[4] = {pa.x, pa.y, pa.z, pa.w};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    acc[r][0] = fmaf(pr[r], v4.x, acc[r][0]);
+                    acc[r][1] = fmaf(pr[r], v4.y, acc[r][1]);
+                    acc[r][2] = fmaf(pr[r], v4.z, acc[r][2]);
+                    acc[r][3] = fmaf(pr[r], v4.w, acc[r][3]);
+                }
+                if (nr > 4) {
+                    const float4 pb = *reinterpret_cast<const float4 *>(&S.s[ki][4]);
+                    const float pq[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        acc[4 + r][0] = fmaf(pq[r], v4.x, acc[4 + r][0]);
+                        acc[4 + r][1] = fmaf(pq[r], v4.y, acc[4 + r][1]);
+                        acc[4 + r][2] = fmaf(pq[r], v4.z, acc[4 + r][2]);
+                        acc[4 + r][3] = fmaf(pq[r], v4.w, acc[4 + r][3]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (j == T - 1) {
+            // ---- exact softmax over the window, per row ------------------------
+            float mx[kF32Rows];
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r) mx[r] = -INFINITY;
+            for (int ki = tid; ki < nkeys; ki += kF32Threads) {
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) mx[r] = fmaxf(mx[r], S.s[ki][r]);
+            }
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r) {
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], o));
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) S.red[warp][r] = mx[r];
+            }
+            __syncthreads();
+            float M[kF32Rows], ls[kF32Rows];
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r) {
+                M[r] = fmaxf(fmaxf(S.red[0][r], S.red[1][r]), fmaxf(S.red[2][r], S.red[3][r]));
+                ls[r] = 0.0f;
+            }
+            __syncthreads();
+            for (int ki = tid; ki < nkeys; ki += kF32Threads) {
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) {
+                    // every real row holds its own position: M[r] is finite
+                    const float e = r < nr ? exp2f(S.s[ki][r] - M[r]) : 0.0f;
+                    S.s[ki][r] = e;
+                    ls[r] += e;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r) {
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) ls[r] += __shfl_xor_sync(kFull, ls[r], o);
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) S.red[warp][r] = ls[r];
+            }
+            __syncthreads();
+            if (tid < kF32Rows) {
+                const float l = (S.red[0][tid] + S.red[1][tid]) + (S.red[2][tid] + S.red[3][tid]);
+                S.inv_l[tid] = l > 0.0f ? 1.0f / l : 0.0f;
+            }
+            __syncthreads();
+        }
+    }
+    if (!ok) {
+        // let the copies in flight land before the CTA exits
+        if (tid == 0) {
+            enc_drain(&S.full[0], 0);
+            enc_drain(&S.full[1], 0);
+        }
+        return;
+    }
+    // ---- sum the key groups' partial products -----------------------------
+    float * part = S.kv[0];  // [kg][row][dim]
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r)
+        *reinterpret_cast<float4 *>(part + (kg * kF32Rows + r) * kEncHd + 4 * c4) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    __syncthreads();
+    {
+        const int r = tid >> 4;
+        if (r < nr) {
+            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int g = 0; g < kF32Threads / 16; ++g) {
+                const float4 x = *reinterpret_cast<const float4 *>(part + (g * kF32Rows + r) * kEncHd + 4 * c4);
+                o.x += x.x;
+                o.y += x.y;
+                o.z += x.z;
+                o.w += x.w;
+            }
+            const float il = S.inv_l[r];
+            *reinterpret_cast<float4 *>(p.out + ((int64_t) (r0 + r) * p.n_heads + h) * kEncHd + 4 * c4) =
+                make_float4(o.x * il, o.y * il, o.z * il, o.w * il);
+        }
+    }
+}
 }  // namespace
 
 int enc_smem_bytes() { return kTcSmem; }
@@ -738,6 +1014,7 @@ cudaError_t launch_pdl(K kernel, unsigned grid, unsigned block, size_t smem, cud
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream) {
     if (p.n_rows <= 0) return cudaSuccess;
     if (p.dtype == 30) return launch_pdl(enc_append_kernel<30>, (unsigned) p.n_rows, 256, 0, stream, p);
+    if (p.dtype == 0) return launch_pdl(enc_append_kernel<0>, (unsigned) p.n_rows, 256, 0, stream, p);
     return launch_pdl(enc_append_kernel<1>, (unsigned) p.n_rows, 256, 0, stream, p);
 }
 
@@ -749,8 +1026,14 @@ cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream) {
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    // persistent: one CTA per SM (the shared-memory ring allows no second)
     const int units = p.n_groups * p.n_heads;
+    if (p.dtype == 0) {
+        const int smem = (int) sizeof(EncF32Smem);
+        e = cudaFuncSetAttribute(enc_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(enc_f32_kernel, (unsigned) units, kF32Threads, (size_t) smem, stream, p);
+    }
+    // persistent: one CTA per SM (the shared-memory ring allows no second)
     const unsigned grid = (unsigned) (units < sms ? units : sms);
     if (p.dtype == 30) {
         e = cudaFuncSetAttribute(enc_tc_kernel<30>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);

@@ -58,6 +58,9 @@ constexpr int kEncRowsPerGroup = 8;
 // slots form the tensor cores' shared-memory layout after a plain bulk copy.
 int32_t ring_slots_of(int32_t capacity) { return (capacity + 7) & ~7; }
 
+// Bytes of one stored ring value: fp32 rows for F32 rings, 16-bit otherwise.
+size_t ring_elem_bytes(vxk_dtype dt) { return dt == VXK_DTYPE_F32 ? 4 : 2; }
+
 }  // namespace
 
 struct vxk_enc_pool {
@@ -226,15 +229,15 @@ vxk_status vxk_enc_create(const vxk_enc_config * config, vxk_enc_pool ** out) {
             if (7 + (c.window - 1) + (kEncRowsPerGroup - 1) + pad >= 128 * vxk::enc_max_tiles())
                 efail(VXK_STATUS_INVALID_ARGUMENT, "window too large for the encoder attention tiles (max 752)");
         }
-        if (c.dtype != VXK_DTYPE_BF16 && c.dtype != VXK_DTYPE_F16)
-            efail(VXK_STATUS_INVALID_ARGUMENT, "encoder dtype must be BF16 or F16");
+        if (c.dtype != VXK_DTYPE_BF16 && c.dtype != VXK_DTYPE_F16 && c.dtype != VXK_DTYPE_F32)
+            efail(VXK_STATUS_INVALID_ARGUMENT, "encoder dtype must be BF16, F16 or F32");
         p->cfg = c;
         int n_dev = 0;
         VXK_ECUDA(cudaGetDeviceCount(&n_dev));
         if (c.device < 0 || c.device >= n_dev) efail(VXK_STATUS_INVALID_ARGUMENT, "no such CUDA device");
         EncDevice scope(c.device);
-        const size_t ring_bytes =
-            (size_t) c.max_streams * c.n_layers * c.n_heads * (size_t) ring_slots_of(c.capacity) * c.head_dim * 2;
+        const size_t ring_bytes = (size_t) c.max_streams * c.n_layers * c.n_heads * (size_t) ring_slots_of(c.capacity) *
+                                  c.head_dim * ring_elem_bytes(c.dtype);
         VXK_ECUDA(cudaMalloc(&p->k_ring, ring_bytes));
         VXK_ECUDA(cudaMalloc(&p->v_ring, ring_bytes));
         VXK_ECUDA(cudaMemset(p->k_ring, 0, ring_bytes));
@@ -433,7 +436,7 @@ vxk_status vxk_enc_read_slots(vxk_enc_pool * pool, int32_t layer, int32_t stream
         EncDevice scope(c.device);
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         VXK_ECUDA(cudaStreamSynchronize(cs));
-        const size_t row_b = (size_t) c.head_dim * 2;
+        const size_t row_b = (size_t) c.head_dim * ring_elem_bytes(c.dtype);
         const int32_t rs = ring_slots_of(c.capacity);
         uint8_t * outs[2] = {static_cast<uint8_t *>(k_out), static_cast<uint8_t *>(v_out)};
         const uint8_t * rings[2] = {pool->k_ring, pool->v_ring};

@@ -209,7 +209,7 @@ struct EncParams {
     int32_t rope_rows;
     float scale_log2;
     int32_t * error;
-    int32_t dtype;          // 30 = bf16, 1 = f16
+    int32_t dtype;          // 30 = bf16, 1 = f16, 0 = f32
 };
 
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream);

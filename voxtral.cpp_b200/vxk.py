@@ -449,7 +449,7 @@ class EncPool:
     def read_slots(self, layer, sid, slot0, n, cuda_stream=0):
         import numpy as np
         c = self.config
-        k = np.zeros((n, c.n_heads * c.head_dim), dtype=np.uint16)
+        k = np.zeros((n, c.n_heads * c.head_dim), dtype=np.uint32 if c.dtype == 0 else np.uint16)
         v = np.zeros_like(k)
         self._check(self.lib.vxk_enc_read_slots(self.h, layer, sid, slot0, n, k.ctypes.data, v.ctypes.data,
                                                 C.c_void_p(cuda_stream)))

@@ -15,7 +15,8 @@
 //        chunk position c ^ (r & 7)  (4096 B)
 //   q8_0 tile: 16 rows x 128 B int8 values, chunk c of row r at c ^ (r & 7)
 //        (2048 B), then the ggml block scales as f16 [4 blocks][16 rows]
-//        (128 B) in a parallel array.
+//        (128 B) in a parallel array.  V values are stored as the byte of
+//        x + 128 (sign bit flipped); readback restores ggml's int8 bytes.
 //   f32  tile: 16 rows x 512 B; chunk c (0-31) of row r stored at
 //        c ^ (r & 7)  (8192 B).  The reference's f32 cache (its numerical
 //        oracle mode) is exact, so its products run on the CUDA cores in fp32.
@@ -204,9 +205,9 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
-// Exact int8 -> f16 pairs: bias the bytes to unsigned, splice them under the
-// f16 exponent of 1024 (0x64), subtract 1024 + 128.  `sel` picks the two
-// bytes (byte_perm selector with 4 = the 0x64 filler).
+// Exact int8 -> f16 pairs from bytes stored as x + 128 (unsigned): splice
+// them under the f16 exponent of 1024 (0x64), subtract 1024 + 128.  `sel`
+// picks the two bytes (byte_perm selector with 4 = the 0x64 filler).
 __device__ __forceinline__ uint32_t s8pair_to_h2(uint32_t biased, uint32_t sel) {
     const uint32_t h = __byte_perm(biased, 0x64646464u, sel);
     const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&h), __half2half2(__ushort_as_half(0x6480)));
@@ -272,6 +273,12 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
         float d;
         q8_pair(x, q, d);
         uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<8>::kTile;
+        if (!is_k) {
+            // V values are stored with the sign bit flipped (the byte of x + 128):
+            // the decode widens them to f16 without an XOR; readback flips back.
+            q.x = (signed char) (q.x ^ 0x80);
+            q.y = (signed char) (q.y ^ 0x80);
+        }
         *reinterpret_cast<char2 *>(t + q8_chunk_off(tok, i >> 3) + (i & 7) * 2) = q;
         if (sk) reinterpret_cast<char2 *>(is_k ? sk : sv)[i] = q;
         if ((i & 15) == 0) {
@@ -725,10 +732,6 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
                         const uint32_t b1 = h2_bits(__hmul2(p89s, dv[(blk * kBlockTokens + 8 + 2 * c) >> 1]));
                         uint32_t w0, w1, w2, w3;
                         ldsm_x4_t(vbase + q8_chunk_off(row, 2 * blk + (mi >> 1)), w0, w1, w2, w3);
-                        w0 ^= 0x80808080u;
-                        w1 ^= 0x80808080u;
-                        w2 ^= 0x80808080u;
-                        w3 ^= 0x80808080u;
                         mma16816(o[2 * blk], s8pair_to_h2(w0, 0x4240u), s8pair_to_h2(w0, 0x4341u),
                                  s8pair_to_h2(w1, 0x4240u), s8pair_to_h2(w1, 0x4341u), b0, b1);
                         mma16816(o[2 * blk + 1], s8pair_to_h2(w2, 0x4240u), s8pair_to_h2(w2, 0x4341u),
@@ -1009,7 +1012,14 @@ __global__ void gather_kernel(const GatherParams p) {
     for (int ch = threadIdx.x; ch < chunks; ch += blockDim.x) {
         const int off = DT == 0 ? f32_chunk_off(tok, ch) : DT == 1 ? f16_chunk_off(tok, ch) : q8_chunk_off(tok, ch);
         *reinterpret_cast<uint4 *>(p.k_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(kt + off);
-        *reinterpret_cast<uint4 *>(p.v_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(vt + off);
+        uint4 vv = *reinterpret_cast<const uint4 *>(vt + off);
+        if constexpr (DT == 8) {  // q8_0 V bytes are stored as x + 128
+            vv.x ^= 0x80808080u;
+            vv.y ^= 0x80808080u;
+            vv.z ^= 0x80808080u;
+            vv.w ^= 0x80808080u;
+        }
+        *reinterpret_cast<uint4 *>(p.v_out + dst + ch * 16) = vv;
     }
     if constexpr (DT == 8) {
         constexpr int nb = kHeadDim / kQ8Block;

@@ -137,13 +137,14 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
     ms = e0.elapsed_time(e1)
     ms = max_over_ranks(dist, ms, "cuda")
     keys = W + P - 1  # union of the chunk's windows
-    per_stream_layer = keys * H * HDE * 2 * 2 + 3 * P * H * HDE * 4 + P * H * HDE * 4 + 2 * P * H * HDE * 2
+    eb = 4 if cfg["dtype"] == 0 else 2  # ring value bytes (f32 or 16-bit)
+    per_stream_layer = keys * H * HDE * eb * 2 + 3 * P * H * HDE * 4 + P * H * HDE * 4 + 2 * P * H * HDE * eb
     bytes_per_layer = S * per_stream_layer
     layer_s = (ms / 1000.0) / (args.steps * L)
     achieved = bytes_per_layer / layer_s / 1e9
     peak, peak_kind = load_peaks()
     flops_per_layer = S * H * P * keys * HDE * 2 * 2
-    traffic_ratio, traffic_src = load_traffic(args.config)
+    traffic_ratio, traffic_src = load_traffic(args.config) if not args.cache else (None, None)
 
     # ---- end to end: per step, pinned host q/k/v of every layer go up on a
     # copy stream (layer l's copy overlaps layer l-1's kernels), the layers
@@ -213,7 +214,9 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16 ring, bf16 hi+lo operands, fp32 accumulate", "data": "synthetic",
+            "dtype": {30: "bf16 ring, bf16 hi+lo operands, fp32 accumulate",
+                      1: "f16 ring, f16 hi+lo operands, fp32 accumulate",
+                      0: "f32 ring, fp32 CUDA-core products"}[cfg["dtype"]], "data": "synthetic",
             "config": {"workload": f"config 4: {cfg['desc']}", "layers": L, "streams_per_gpu": S, "heads": H,
                        "parallelism": f"streams sharded, {S}/GPU, no collective",
                        "l2": "inputs larger than L2 (window reads per launch >> 126 MB)"},
@@ -223,7 +226,7 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
                          "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
                                                            f"scaled to this launch)",
                          "algorithmic_bytes_per_launch": bytes_per_layer,
-                         "avg_layer_us": round(layer_s * 1e6, 2), "kernel": "enc_tc_kernel (+ enc_append_kernel)",
+                         "avg_layer_us": round(layer_s * 1e6, 2), "kernel": ("enc_f32_kernel" if cfg["dtype"] == 0 else "enc_tc_kernel") + " (+ enc_append_kernel)",
                          "tensor_tflops": round(flops_per_layer / layer_s / 1e12, 2)},
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(args.steps * (L * 2 + 0)),
@@ -1176,8 +1179,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--cache", choices=["f16", "q8_0", "f32"], default=None,
-                    help="override the decoder cache format of configs 2, 3 and 5")
+    ap.add_argument("--cache", choices=["f16", "q8_0", "f32", "bf16"], default=None,
+                    help="override the cache format: decoder configs 2, 3, 5 (f16, q8_0, f32); encoder config 4 "
+                         "(bf16, f16, f32)")
     return ap.parse_args()
 
 
@@ -1545,8 +1549,11 @@ def main():
         cfg["layers"] = args.layers
     if args.vocab:
         cfg["vocab"] = args.vocab
-    if args.cache and "dtype" in cfg and cfg.get("kind") is None:
-        cfg["dtype"] = {"f16": 1, "q8_0": 8, "f32": 0}[args.cache]
+    if args.cache and "dtype" in cfg and cfg.get("kind") in (None, "encoder"):
+        if cfg.get("kind") == "encoder":
+            cfg["dtype"] = {"f16": 1, "bf16": 30, "f32": 0}[args.cache]
+        else:
+            cfg["dtype"] = {"f16": 1, "q8_0": 8, "f32": 0}[args.cache]
         cfg["desc"] += f" ({args.cache} cache)"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -730,186 +730,128 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
 // ---------------------------------------------------------------------------
 // f32 rings: window attention on the CUDA cores
 // ---------------------------------------------------------------------------
-constexpr int kF32Compute = 128;               // 4 compute warps
-constexpr int kF32Threads = kF32Compute + 32;  // + 1 producer warp
-constexpr int kF32Tile = 64;                   // keys per tile (16 KB of fp32 rows)
-constexpr int kF32Stages = 5;
+constexpr int kF32Threads = 128;
+constexpr int kF32Tile = 128;                  // keys per tile
 constexpr int kF32MaxKeys = 768;               // window - 1 + 8 rows fits (host checks <= 752)
 constexpr int kF32Rows = 8;                    // rows per group (kEncRowsPerGroup)
 constexpr int kF32RowBytes = kEncHd * 4;       // 256
 
 struct __align__(128) EncF32Smem {
-    float ring[kF32Stages][kF32Tile * kEncHd];  // tile stages (rows swizzled as in the ring)
-    float s[kF32MaxKeys][kF32Rows];             // scores, then probabilities; then P.V partial sums
-    float q[kEncHd][kF32Rows];                  // rotated, scaled queries: [dim][row]
-    float red[kF32Compute / 32][kF32Rows];
+    float kv[2][kF32Tile * kEncHd];            // two tile buffers (rows swizzled as in the ring)
+    float s[kF32MaxKeys][kF32Rows];            // scores, then probabilities: [key][row]
+    float q[kEncHd][kF32Rows];                 // rotated, scaled queries: [dim][row]
+    float red[kF32Threads / 32][kF32Rows];
     float inv_l[kF32Rows];
-    uint64_t full[kF32Stages];
-    uint64_t empty[kF32Stages];
+    uint64_t full[2];
     int32_t abort_flag;
 };
-static_assert(8 * kF32Rows * kEncHd <= kF32MaxKeys * kF32Rows, "P.V partial sums fit the score buffer");
+static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * 2 * kF32Tile * kEncHd,
+              "P.V partial sums fit the tile buffers");
 
-__device__ __forceinline__ void f32_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Persistent: CTA b takes units b, b + gridDim.x, ... (unit = row group of
-// <= 8 rows of one stream x head).  Warp 4 streams every unit's K tiles and
-// then its V tiles through the stage ring, running ahead across units;
-// warps 0-3 compute.  Per unit: queries; scores of each K tile (two
-// threads per key, 32 dims each); an exact softmax over the window; P.V of
-// each V tile (thread: 4 dims of every row over an eighth of the tile's
-// keys); the eighths summed; out = sum / row sum.
+// One CTA per unit (row group of <= 8 rows of one stream, head).
 __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     EncF32Smem & S = *reinterpret_cast<EncF32Smem *>(smem_raw);
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const int n_units = p.n_groups * p.n_heads;
     if (tid == 0) {
-        for (int i = 0; i < kF32Stages; ++i) {
-            mbar_init(&S.full[i], 1);
-            mbar_init(&S.empty[i], kF32Compute / 32);
-        }
+        mbar_init(&S.full[0], 1);
+        mbar_init(&S.full[1], 1);
         S.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    __syncthreads();
     // nothing an earlier grid writes is read before this point
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    volatile int32_t * abort_flag = &S.abort_flag;
-
-    struct Unit {
-        int r0, nr, h, ws, nkeys, T;
-        int64_t ring;
-    };
-    auto unit_of = [&](int u) -> Unit {
-        Unit U;
-        const int grp = u / p.n_heads;
-        U.h = u - grp * p.n_heads;
-        U.r0 = p.group_first[grp];
-        U.nr = p.group_first[grp + 1] - U.r0;
-        const EncRowDesc first = p.rows[U.r0];
-        U.ws = first.win_start;
-        U.nkeys = p.rows[U.r0 + U.nr - 1].pos - U.ws + 1;
-        U.T = (U.nkeys + kF32Tile - 1) / kF32Tile;
-        U.ring = ring_index(p, first.stream, U.h);
-        return U;
-    };
-    auto bad = [&](const Unit & U) { return U.nr < 1 || U.nr > kF32Rows || U.nkeys < 1 || U.nkeys > kF32MaxKeys; };
-
-    if (warp == kF32Compute / 32) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            const uint64_t policy = evict_first_policy();
-            uint32_t c = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-                const Unit U = unit_of(u);
-                if (bad(U)) break;  // the compute warps report it
-                for (int j = 0; ok && j < 2 * U.T; ++j) {
-                    const int st = (int) (c % kF32Stages);
-                    if (!enc_wait(&S.empty[st], ((c / kF32Stages) & 1) ^ 1, abort_flag, p.error)) {
-                        ok = false;
-                        break;
-                    }
-                    const int jj = j < U.T ? j : j - U.T;
-                    const int k0 = jj * kF32Tile;
-                    const int n = min(kF32Tile, U.nkeys - k0);
-                    const int slot0 = (U.ws + k0) % p.capacity;
-                    const int run = min(n, p.capacity - slot0);
-                    const uint8_t * base =
-                        (j < U.T ? p.k_ring : p.v_ring) + U.ring * p.ring_slots * (int64_t) kF32RowBytes;
-                    float * dst = S.ring[st];
-                    mbar_expect_tx(&S.full[st], (uint32_t) (n * kF32RowBytes));
-                    bulk_load(dst, base + (int64_t) slot0 * kF32RowBytes, (uint32_t) (run * kF32RowBytes), &S.full[st],
-                              policy);
-                    if (n > run)
-                        bulk_load(dst + run * kEncHd, base, (uint32_t) ((n - run) * kF32RowBytes), &S.full[st], policy);
-                    ++c;
-                }
-            }
-            // every issued copy lands before the CTA exits
-            for (uint32_t d = c > (uint32_t) kF32Stages ? c - kF32Stages : 0; d < c; ++d)
-                enc_drain(&S.full[d % kF32Stages], (d / kF32Stages) & 1);
-        }
+    const int u = blockIdx.x;
+    const int grp = u / p.n_heads;
+    const int h = u - grp * p.n_heads;
+    const int r0 = p.group_first[grp];
+    const int nr = p.group_first[grp + 1] - r0;
+    const EncRowDesc first = p.rows[r0];
+    const int ws = first.win_start;
+    const int we = p.rows[r0 + nr - 1].pos;
+    const int nkeys = we - ws + 1;
+    if (nr < 1 || nr > kF32Rows || nkeys < 1 || nkeys > kF32MaxKeys) {
+        if (tid == 0 && p.error) atomicCAS(p.error, 0, 1);
         return;
     }
-
-    // ---------------- compute warps 0-3 ----------------
-    // The loop structure (and so every named barrier) is the same for all four
-    // warps; after an abort the waits return at once and nothing is written.
-    uint32_t c = 0;
-    const int kh = tid >> 1;  // scores: key of the tile
-    const int dh = tid & 1;   //         dims 32 dh .. 32 dh + 31
-    const int c4 = tid & 15;  // P.V: dims 4 c4 .. 4 c4 + 3
-    const int kg = tid >> 4;  //       keys kg, kg + 8, ... of each tile
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const Unit U = unit_of(u);
-        if (bad(U)) {
-            if (tid == 0 && p.error) atomicCAS(p.error, 0, 1);
-            *abort_flag = 1;
-            break;  // uniform: every compute thread reads the same unit
+    const int T = (nkeys + kF32Tile - 1) / kF32Tile;
+    const int64_t ring = ring_index(p, first.stream, h);
+    // queries: thread t -> row t / 16, dims 4 (t % 16) .. + 3
+    {
+        const int r = tid >> 4;
+        const int c = tid & 15;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r < nr) {
+            const EncRowDesc rd = p.rows[r0 + r];
+            const float * qr = p.q + ((int64_t) (r0 + r) * p.n_heads + h) * kEncHd + 4 * c;
+            const float2 * cs = p.rope + (int64_t) rd.pos * (kEncHd / 2) + 2 * c;
+            const float2 a = enc_rope_pair(*reinterpret_cast<const float2 *>(qr), cs[0]);
+            const float2 b = enc_rope_pair(*reinterpret_cast<const float2 *>(qr + 2), cs[1]);
+            v = make_float4(a.x * p.scale_log2, a.y * p.scale_log2, b.x * p.scale_log2, b.y * p.scale_log2);
         }
-        // queries: thread t -> row t / 16, dims 4 (t % 16) .. + 3
-        {
-            const int r = tid >> 4;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (r < U.nr) {
-                const EncRowDesc rd = p.rows[U.r0 + r];
-                const float * qr = p.q + ((int64_t) (U.r0 + r) * p.n_heads + U.h) * kEncHd + 4 * c4;
-                const float2 * cs = p.rope + (int64_t) rd.pos * (kEncHd / 2) + 2 * c4;
-                const float2 x0 = enc_rope_pair(*reinterpret_cast<const float2 *>(qr), cs[0]);
-                const float2 x1 = enc_rope_pair(*reinterpret_cast<const float2 *>(qr + 2), cs[1]);
-                v = make_float4(x0.x * p.scale_log2, x0.y * p.scale_log2, x1.x * p.scale_log2, x1.y * p.scale_log2);
-            }
-            S.q[4 * c4 + 0][r] = v.x;
-            S.q[4 * c4 + 1][r] = v.y;
-            S.q[4 * c4 + 2][r] = v.z;
-            S.q[4 * c4 + 3][r] = v.w;
-        }
-        int qlo[kF32Rows], qhi[kF32Rows];
+        S.q[4 * c + 0][r] = v.x;
+        S.q[4 * c + 1][r] = v.y;
+        S.q[4 * c + 2][r] = v.z;
+        S.q[4 * c + 3][r] = v.w;
+    }
+    __syncthreads();
+    // tile j < T: K keys [128 j, ...); tile j >= T: V keys [128 (j - T), ...)
+    auto issue = [&](int j) {
+        const int jj = j < T ? j : j - T;
+        const int k0 = jj * kF32Tile;
+        const int n = min(kF32Tile, nkeys - k0);
+        const int slot0 = (ws + k0) % p.capacity;
+        const int run = min(n, p.capacity - slot0);
+        const uint8_t * base = (j < T ? p.k_ring : p.v_ring) + ring * p.ring_slots * (int64_t) kF32RowBytes;
+        uint64_t * bar = &S.full[j & 1];
+        float * dst = S.kv[j & 1];
+        const uint64_t policy = evict_first_policy();
+        mbar_expect_tx(bar, (uint32_t) (n * kF32RowBytes));
+        bulk_load(dst, base + (int64_t) slot0 * kF32RowBytes, (uint32_t) (run * kF32RowBytes), bar, policy);
+        if (n > run) bulk_load(dst + run * kEncHd, base, (uint32_t) ((n - run) * kF32RowBytes), bar, policy);
+    };
+    if (tid == 0) issue(0);
+    float acc[kF32Rows][4];
 #pragma unroll
-        for (int r = 0; r < kF32Rows; ++r) {
-            qlo[r] = 1;
-            qhi[r] = 0;  // empty window for padding rows
-            if (r < U.nr) {
-                const EncRowDesc rd = p.rows[U.r0 + r];
-                qlo[r] = rd.win_start;
-                qhi[r] = rd.pos;
-            }
+    for (int r = 0; r < kF32Rows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    const int c4 = tid & 15;     // P.V: dims 4 c4 .. + 3
+    const int kg = tid >> 4;     //       keys kg, kg + 8, ... of each tile
+    bool ok = true;
+    for (int j = 0; j < 2 * T; ++j) {
+        // the other buffer was released by the barrier that ended iteration j - 1
+        if (tid == 0 && j + 1 < 2 * T) issue(j + 1);
+        const bool landed = enc_wait(&S.full[j & 1], (uint32_t) ((j >> 1) & 1), &S.abort_flag, p.error);
+        if (!__syncthreads_and(landed ? 1 : 0)) {
+            ok = false;
+            break;
         }
-        f32_sync();
-        // ---- scores -----------------------------------------------------------
-        for (int j = 0; j < U.T; ++j, ++c) {
-            const int st = (int) (c % kF32Stages);
-            const bool landed =
-                __all_sync(kFull, enc_wait(&S.full[st], (c / kF32Stages) & 1, abort_flag, p.error) ? 1 : 0);
-            const int ki = j * kF32Tile + kh;
-            const int kp = U.ws + ki;
-            // both threads of a key (lanes 2k, 2k + 1) are active or not together
-            const bool active = landed && !*abort_flag && ki < U.nkeys;
-            float sc[kF32Rows];
-#pragma unroll
-            for (int r = 0; r < kF32Rows; ++r) sc[r] = 0.0f;
-            if (active) {
+        const float * buf = S.kv[j & 1];
+        if (j < T) {
+            // ---- scores of key 128 j + tid for every row ----------------------
+            const int ki = j * kF32Tile + tid;
+            if (ki < nkeys) {
+                const int kp = ws + ki;
                 const int sw = (kp % p.capacity) & 7;
-                const float * kr = S.ring[st] + kh * kEncHd;
+                float sc[kF32Rows];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int ch = 8 * dh + i;
-                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + 4 * (ch ^ sw));
+                for (int r = 0; r < kF32Rows; ++r) sc[r] = 0.0f;
+                const float * kr = buf + tid * kEncHd;
+#pragma unroll 4
+                for (int c = 0; c < kEncHd / 4; ++c) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + 4 * (c ^ sw));
                     const float kd[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
                     for (int d = 0; d < 4; ++d) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(&S.q[4 * ch + d][0]);
+                        const float4 qa = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][0]);
+                        const float4 qb = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][4]);
                         sc[0] = fmaf(qa.x, kd[d], sc[0]);
                         sc[1] = fmaf(qa.y, kd[d], sc[1]);
                         sc[2] = fmaf(qa.z, kd[d], sc[2]);
                         sc[3] = fmaf(qa.w, kd[d], sc[3]);
-                        if (U.nr > 4) {
-                            const float4 qb = *reinterpret_cast<const float4 *>(&S.q[4 * ch + d][4]);
+                        if (nr > 4) {
                             sc[4] = fmaf(qb.x, kd[d], sc[4]);
                             sc[5] = fmaf(qb.y, kd[d], sc[5]);
                             sc[6] = fmaf(qb.z, kd[d], sc[6]);
@@ -917,28 +859,55 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                         }
                     }
                 }
-            }
-            // every lane takes part in the exchange; the partner holds the other 32 dims
-#pragma unroll
-            for (int r = 0; r < kF32Rows; ++r) sc[r] += __shfl_xor_sync(kFull, sc[r], 1);
-            if (active) {
 #pragma unroll
                 for (int r = 0; r < kF32Rows; ++r) {
-                    if (kp < qlo[r] || kp > qhi[r]) sc[r] = -INFINITY;
+                    bool in = r < nr;
+                    if (in) {
+                        const EncRowDesc rd = p.rows[r0 + r];
+                        in = kp >= rd.win_start && kp <= rd.pos;
+                    }
+                    if (!in) sc[r] = -INFINITY;
                 }
-                if (dh == 0) *reinterpret_cast<float4 *>(&S.s[ki][0]) = make_float4(sc[0], sc[1], sc[2], sc[3]);
-                else *reinterpret_cast<float4 *>(&S.s[ki][4]) = make_float4(sc[4], sc[5], sc[6], sc[7]);
+                *reinterpret_cast<float4 *>(&S.s[ki][0]) = make_float4(sc[0], sc[1], sc[2], sc[3]);
+                *reinterpret_cast<float4 *>(&S.s[ki][4]) = make_float4(sc[4], sc[5], sc[6], sc[7]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[st]);
+        } else {
+            // ---- P.V over this tile's keys kg, kg + 8, ... --------------------
+            const int k0 = (j - T) * kF32Tile;
+            const int n = min(kF32Tile, nkeys - k0);
+            for (int i = kg; i < n; i += kF32Threads / 16) {
+                const int ki = k0 + i;
+                const int sw = ((ws + ki) % p.capacity) & 7;
+                const float4 v4 = *reinterpret_cast<const float4 *>(buf + i * kEncHd + 4 * (c4 ^ sw));
+                const float4 pa = *reinterpret_cast<const float4 *>(&S.s[ki][0]);
+                const float pr[4] = {pa.x, pa.y, pa.z, pa.w};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    acc[r][0] = fmaf(pr[r], v4.x, acc[r][0]);
+                    acc[r][1] = fmaf(pr[r], v4.y, acc[r][1]);
+                    acc[r][2] = fmaf(pr[r], v4.z, acc[r][2]);
+                    acc[r][3] = fmaf(pr[r], v4.w, acc[r][3]);
+                }
+                if (nr > 4) {
+                    const float4 pb = *reinterpret_cast<const float4 *>(&S.s[ki][4]);
+                    const float pq[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        acc[4 + r][0] = fmaf(pq[r], v4.x, acc[4 + r][0]);
+                        acc[4 + r][1] = fmaf(pq[r], v4.y, acc[4 + r][1]);
+                        acc[4 + r][2] = fmaf(pq[r], v4.z, acc[4 + r][2]);
+                        acc[4 + r][3] = fmaf(pq[r], v4.w, acc[4 + r][3]);
+                    }
+                }
+            }
         }
-        f32_sync();
-        // ---- exact softmax over the window, per row -------------------------
-        {
+        __syncthreads();
+        if (j == T - 1) {
+            // ---- exact softmax over the window, per row ------------------------
             float mx[kF32Rows];
 #pragma unroll
             for (int r = 0; r < kF32Rows; ++r) mx[r] = -INFINITY;
-            for (int ki = tid; ki < U.nkeys; ki += kF32Compute) {
+            for (int ki = tid; ki < nkeys; ki += kF32Threads) {
 #pragma unroll
                 for (int r = 0; r < kF32Rows; ++r) mx[r] = fmaxf(mx[r], S.s[ki][r]);
             }
@@ -951,19 +920,19 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
 #pragma unroll
                 for (int r = 0; r < kF32Rows; ++r) S.red[warp][r] = mx[r];
             }
-            f32_sync();
+            __syncthreads();
             float M[kF32Rows], ls[kF32Rows];
 #pragma unroll
             for (int r = 0; r < kF32Rows; ++r) {
                 M[r] = fmaxf(fmaxf(S.red[0][r], S.red[1][r]), fmaxf(S.red[2][r], S.red[3][r]));
                 ls[r] = 0.0f;
             }
-            f32_sync();
-            for (int ki = tid; ki < U.nkeys; ki += kF32Compute) {
+            __syncthreads();
+            for (int ki = tid; ki < nkeys; ki += kF32Threads) {
 #pragma unroll
                 for (int r = 0; r < kF32Rows; ++r) {
                     // every real row holds its own position: M[r] is finite
-                    const float e = r < U.nr ? exp2f(S.s[ki][r] - M[r]) : 0.0f;
+                    const float e = r < nr ? exp2f(S.s[ki][r] - M[r]) : 0.0f;
                     S.s[ki][r] = e;
                     ls[r] += e;
                 }
@@ -977,83 +946,47 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
 #pragma unroll
                 for (int r = 0; r < kF32Rows; ++r) S.red[warp][r] = ls[r];
             }
-            f32_sync();
+            __syncthreads();
             if (tid < kF32Rows) {
                 const float l = (S.red[0][tid] + S.red[1][tid]) + (S.red[2][tid] + S.red[3][tid]);
                 S.inv_l[tid] = l > 0.0f ? 1.0f / l : 0.0f;
             }
-            f32_sync();
+            __syncthreads();
         }
-        // ---- P.V -----------------------------------------------------------------
-        float acc[kF32Rows][4];
+    }
+    if (!ok) {
+        // let the copies in flight land before the CTA exits
+        if (tid == 0) {
+            enc_drain(&S.full[0], 0);
+            enc_drain(&S.full[1], 0);
+        }
+        return;
+    }
+    // ---- sum the key groups' partial products -----------------------------
+    float * part = S.kv[0];  // [kg][row][dim]
 #pragma unroll
-        for (int r = 0; r < kF32Rows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
-        for (int j = 0; j < U.T; ++j, ++c) {
-            const int st = (int) (c % kF32Stages);
-            const bool landed =
-                __all_sync(kFull, enc_wait(&S.full[st], (c / kF32Stages) & 1, abort_flag, p.error) ? 1 : 0);
-            if (landed && !*abort_flag) {
-                const int k0 = j * kF32Tile;
-                const int n = min(kF32Tile, U.nkeys - k0);
-                const float * buf = S.ring[st];
-                for (int i = kg; i < n; i += kF32Compute / 16) {
-                    const int ki = k0 + i;
-                    const int sw = ((U.ws + ki) % p.capacity) & 7;
-                    const float4 v4 = *reinterpret_cast<const float4 *>(buf + i * kEncHd + 4 * (c4 ^ sw));
-                    const float4 pa = *reinterpret_cast<const float4 *>(&S.s[ki][0]);
-                    const float pr[4] = {pa.x, pa.y, pa.z, pa.w};
+    for (int r = 0; r < kF32Rows; ++r)
+        *reinterpret_cast<float4 *>(part + (kg * kF32Rows + r) * kEncHd + 4 * c4) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    __syncthreads();
+    {
+        const int r = tid >> 4;
+        if (r < nr) {
+            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        acc[r][0] = fmaf(pr[r], v4.x, acc[r][0]);
-                        acc[r][1] = fmaf(pr[r], v4.y, acc[r][1]);
-                        acc[r][2] = fmaf(pr[r], v4.z, acc[r][2]);
-                        acc[r][3] = fmaf(pr[r], v4.w, acc[r][3]);
-                    }
-                    if (U.nr > 4) {
-                        const float4 pb = *reinterpret_cast<const float4 *>(&S.s[ki][4]);
-                        const float pq[4] = {pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-                        for (int r = 0; r < 4; ++r) {
-                            acc[4 + r][0] = fmaf(pq[r], v4.x, acc[4 + r][0]);
-                            acc[4 + r][1] = fmaf(pq[r], v4.y, acc[4 + r][1]);
-                            acc[4 + r][2] = fmaf(pq[r], v4.z, acc[4 + r][2]);
-                            acc[4 + r][3] = fmaf(pq[r], v4.w, acc[4 + r][3]);
-                        }
-                    }
-                }
+            for (int g = 0; g < kF32Threads / 16; ++g) {
+                const float4 x = *reinterpret_cast<const float4 *>(part + (g * kF32Rows + r) * kEncHd + 4 * c4);
+                o.x += x.x;
+                o.y += x.y;
+                o.z += x.z;
+                o.w += x.w;
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[st]);
+            const float il = S.inv_l[r];
+            *reinterpret_cast<float4 *>(p.out + ((int64_t) (r0 + r) * p.n_heads + h) * kEncHd + 4 * c4) =
+                make_float4(o.x * il, o.y * il, o.z * il, o.w * il);
         }
-        // ---- sum the key groups' partial products (in the score buffer) ------
-        f32_sync();
-        float * part = &S.s[0][0];  // [kg][row][dim]
-#pragma unroll
-        for (int r = 0; r < kF32Rows; ++r)
-            *reinterpret_cast<float4 *>(part + (kg * kF32Rows + r) * kEncHd + 4 * c4) =
-                make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-        f32_sync();
-        {
-            const int r = tid >> 4;
-            if (r < U.nr && !*abort_flag) {
-                float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-                for (int g = 0; g < kF32Compute / 16; ++g) {
-                    const float4 x = *reinterpret_cast<const float4 *>(part + (g * kF32Rows + r) * kEncHd + 4 * c4);
-                    o.x += x.x;
-                    o.y += x.y;
-                    o.z += x.z;
-                    o.w += x.w;
-                }
-                const float il = S.inv_l[r];
-                *reinterpret_cast<float4 *>(p.out + ((int64_t) (U.r0 + r) * p.n_heads + U.h) * kEncHd + 4 * c4) =
-                    make_float4(o.x * il, o.y * il, o.z * il, o.w * il);
-            }
-        }
-        f32_sync();  // the score buffer and the queries are rewritten by the next unit
     }
 }
-
 }  // namespace
 
 int enc_smem_bytes() { return kTcSmem; }
@@ -1095,17 +1028,10 @@ cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     const int units = p.n_groups * p.n_heads;
     if (p.dtype == 0) {
-        // persistent: as many CTAs as fit the device (two per SM), each
-        // walking its units with its own copy ring
         const int smem = (int) sizeof(EncF32Smem);
         e = cudaFuncSetAttribute(enc_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        int per_sm = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, enc_f32_kernel, kF32Threads, (size_t) smem);
-        if (e != cudaSuccess) return e;
-        const int slots = sms * (per_sm > 0 ? per_sm : 1);
-        return launch_pdl(enc_f32_kernel, (unsigned) (units < slots ? units : slots), kF32Threads, (size_t) smem,
-                          stream, p);
+        return launch_pdl(enc_f32_kernel, (unsigned) units, kF32Threads, (size_t) smem, stream, p);
     }
     // persistent: one CTA per SM (the shared-memory ring allows no second)
     const unsigned grid = (unsigned) (units < sms ? units : sms);

@@ -1656,7 +1656,7 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
     L, dtype, cap = cfg["layers"], cfg["dtype"], cfg["capacity"]
     ctx_all, parts, scaling = job_layout(cfg, args.seed, world)
     mine = parts[rank]
-    total_steps = args.warmup + args.steps * (1 if args.no_e2e else 2) + 2
+    total_steps = args.warmup + args.steps * (1 if args.no_e2e else 2) + 6  # + the 4 per-launch probe steps
     NSETS = 4
     prefill_chunk = int(min(cap, 4096, ctx_all.max()))
 
@@ -1773,6 +1773,30 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
                "what": "last timed step: shortest / median / longest-context stream x first / last layer, "
                        "appended row bytes and attention output vs the CPU oracle"}
 
+    # ---- per-launch cross-check: a few more steps with CUDA events around
+    # every decode launch (the events keep consecutive layers from overlapping,
+    # so this is each launch's own warm duration) --------------------------------
+    probe_steps = min(4, args.steps)
+    probe_us, probe_bytes = [], []
+    for i in range(probe_steps):
+        pool.plan(streams, ones, sh)
+        st = (args.warmup + args.steps + i) % NSETS
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(L + 1)]
+        evs[0].record(stream)
+        for layer in range(L):
+            pool.decode_layer(layer, qs[st, layer].data_ptr(), ks[st, layer].data_ptr(), vs[st, layer].data_ptr(),
+                              out[layer].data_ptr(), sh)
+            evs[layer + 1].record(stream)
+        pool.commit()
+        for j in range(S):
+            ctx_now[j] = min(cap, ctx_now[j] + 1)
+        torch.cuda.synchronize()
+        probe_bytes.append(sum(algorithmic_bytes(c, dtype) for c in ctx_now))
+        probe_us += [evs[layer].elapsed_time(evs[layer + 1]) * 1000.0 for layer in range(L)]
+    pool.sync(sh)
+    probe_launch_us = statistics.mean(probe_us)
+    probe_gbs = statistics.mean(probe_bytes) / (probe_launch_us / 1e6) / 1e9
+
     # ---- roofline of the dominant kernel (decode_kernel) --------------------
     peak, peak_kind = load_peaks()
     bytes_per_launch = statistics.mean(bytes_per_step)  # one layer launch: every stream's token in that layer
@@ -1791,6 +1815,9 @@ def run_decode(args, cfg, world, rank, local, dist, torch, vxk):
                                                   f"scaled to this launch)",
                 "algorithmic_bytes_per_launch": round(bytes_per_launch),
                 "avg_launch_us": round(avg_launch_s * 1e6, 2),
+                "event_launch_us": round(probe_launch_us, 2), "event_achieved": round(probe_gbs, 1),
+                "event_note": f"{probe_steps} extra steps, CUDA events around each decode launch (no overlap between "
+                              f"layers); avg_launch_us is the timed region over its launches",
                 "kernel": "decode_kernel<" + {1: "f16", 8: "q8_0", 0: "f32"}[dtype] + ">"}
     job_bytes_per_s = sum(gather_over_ranks(dist, statistics.mean(bytes_per_step) * L, "cuda")) * args.steps / (
         ms / 1000.0)

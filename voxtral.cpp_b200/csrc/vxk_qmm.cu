@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 namespace vxk {
@@ -625,12 +626,23 @@ cudaError_t launch_fam(const QmmParams & p, int smem, cudaStream_t stream) {
                       stream, p, (unsigned) p.n_splits);
 }
 
+// Resident CTAs per SM for a shared-memory size: asked of the runtime once per
+// (device, size in 1 KB steps) and remembered, since the planner asks for
+// every candidate split on every product call.
 template <int FAM, int NT>
 int ctas_fam(int smem) {
+    static std::atomic<int> memo[64][233];
     if (raise_smem<FAM, NT>() != cudaSuccess) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || smem < 0 || smem > 232448) return 0;
+    const int key = (smem + 1023) / 1024;
+    std::atomic<int> & slot = memo[dev][key];
+    const int known = slot.load(std::memory_order_relaxed);
+    if (known > 0 && (known >> 20) == (smem & 0x3ff) + 1) return known & 0xfffff;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmm_kernel<FAM, NT>, kThreads, (size_t) smem) != cudaSuccess)
         return 0;
+    if (n > 0 && n < (1 << 20)) slot.store(((smem & 0x3ff) + 1) << 20 | n, std::memory_order_relaxed);
     return n;
 }
 

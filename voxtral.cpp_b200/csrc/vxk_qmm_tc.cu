@@ -44,6 +44,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 namespace vxk {
@@ -836,9 +837,16 @@ cudaError_t launch_n(const QtcParams & p, cudaStream_t stream) {
 
 template <int N>
 int clusters_n(int cluster_y) {
+    // The answer depends only on the device, the instantiation and the
+    // cluster shape: asked of the runtime once, then remembered (the planner
+    // asks for every candidate split on every product call).
+    static std::atomic<int> memo[64][kQmmMaxSplits + 1];
     static bool raised[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cluster_y < 1 || cluster_y > kQmmMaxSplits) return 0;
+    const int known = memo[dev][cluster_y].load(std::memory_order_relaxed);
+    if (known > 0) return known;
     if (!raised[dev]) {
         if (cudaFuncSetAttribute(qtc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
             return 0;
@@ -857,6 +865,7 @@ int clusters_n(int cluster_y) {
     cfg.numAttrs = 1;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, qtc_kernel<N>, &cfg) != cudaSuccess) return 0;
+    if (n > 0) memo[dev][cluster_y].store(n, std::memory_order_relaxed);
     return n;
 }
 

@@ -81,7 +81,8 @@ CONFIGS = {
 
 def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
     """Config 4: one step = one 80 ms chunk (4 new encoder rows) of every
-    stream through every encoder layer (append + tcgen05 window attention)."""
+    stream through every encoder layer (append + tcgen05 window attention; for
+    16-bit rings one launch per layer, the append fused into the attention)."""
     L, S, H, P = cfg["layers"], cfg["streams"], cfg["heads"], cfg["rows"]
     W, CAP, HDE = cfg["window"], cfg["capacity"], 64
     pool = vxk.EncPool(device=local, n_layers=L, n_heads=H, head_dim=HDE, window=W, capacity=CAP, max_streams=S,
@@ -226,10 +227,12 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
                          "traffic_source": traffic_src and f"{traffic_src} (ncu dram bytes per algorithmic byte, "
                                                            f"scaled to this launch)",
                          "algorithmic_bytes_per_launch": bytes_per_layer,
-                         "avg_layer_us": round(layer_s * 1e6, 2), "kernel": ("enc_f32_kernel" if cfg["dtype"] == 0 else "enc_tc_kernel") + " (+ enc_append_kernel)",
+                         "avg_layer_us": round(layer_s * 1e6, 2),
+                         "kernel": "enc_f32_kernel (+ enc_append_kernel)" if cfg["dtype"] == 0
+                         else "enc_tc_kernel (K/V append fused: <= 8 rows per stream)",
                          "tensor_tflops": round(flops_per_layer / layer_s / 1e12, 2)},
             "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": int(args.steps * (L * 2 + 0)),
+            "gpu_launches": int(args.steps * L * (2 if cfg["dtype"] == 0 else 1)),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)

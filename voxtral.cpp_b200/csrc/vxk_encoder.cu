@@ -18,14 +18,24 @@
 // tensor-map boxes.
 //
 // Work unit = (row group, head).  Persistent CTAs, one per SM, walk their
-// units through a warp-specialised pipeline (8 warps):
-//   warp 4     TMA producer: 16 KB stages (128 keys of K or V) into a
-//              10-stage shared-memory ring
-//   warp 5     tcgen05.mma issuer of S^T = K.Q^T (one lane)
-//   warp 7     tcgen05.mma issuer of O^T += V^T.P^T (one lane): the two
+// units through a warp-specialised pipeline (12 warps):
+//   warp 8     TMA producer: 16 KB stages (128 keys of K or V) into a
+//              10-stage shared-memory ring.  One thread issues every copy,
+//              and a copy's issue costs about as long as its bytes take at
+//              the SM's share of HBM, so this thread's path is kept free of
+//              waits other than for ring slots: group descriptors come
+//              precomputed from the host (no divisions, no dependent loads)
+//   warp 9     tcgen05.mma issuer of S^T = K.Q^T (one lane), tile by tile
+//   warp 11    tcgen05.mma issuer of O^T += V^T.P^T (one lane): the two
 //              products of consecutive units are issued side by side
-//   warp 6     Q^T producer (RoPE, scale, bf16 hi/lo split)
-//   warps 0-3  own TMEM lane quadrants 0-3: softmax and epilogue
+//   warp 10    Q^T producer (RoPE, scale, bf16 hi/lo split)
+//   warps 0-3  own TMEM lane quadrants 0-3: softmax and epilogue of the
+//              even units of the CTA; warps 4-7 the same for the odd units
+//              (one set's softmax and epilogue take about a unit's copy time)
+// With fuse_append (every group a whole stream) all warps but the producer
+// first store the new K/V rows of the CTA's units into the ring (replacing
+// enc_append_kernel's launch); the producer copies the tiles holding new
+// rows after their signal.
 // Per unit, two phases with an exact softmax (no online rescaling):
 //   S^T[key][query] = K . Q^T    (M=128 keys per tile, N=16 = 8 queries x
 //                                 {hi, lo}, K=64 dims: 4 MMAs per tile)
@@ -57,7 +67,10 @@ namespace vxk {
 namespace {
 
 constexpr int kEncHd = 64;
-constexpr int kTcThreads = 256;         // 8 warps
+constexpr int kTcSets = 2;              // softmax/epilogue warp sets (4 warps each)
+constexpr int kTcThreads = 128 * kTcSets + 128;
+constexpr int kWarpProducer = 4 * kTcSets, kWarpS = kWarpProducer + 1, kWarpQ = kWarpProducer + 2,
+              kWarpPV = kWarpProducer + 3;
 constexpr int kTcStages = 10;
 constexpr int kTcMaxTiles = 6;          // keys per group <= 6 x 128
 constexpr int kTcBoxes = 16;            // 8-slot boxes per 128-key tile
@@ -84,11 +97,12 @@ constexpr int kBarPEmpty = kBarPFull + 2;      // [2] PV MMAs done reading P^T
 constexpr int kBarOFull = kBarPEmpty + 2;      // [2] O^T complete in TMEM
 constexpr int kBarOEmpty = kBarOFull + 2;      // [2] O^T read by the epilogue
 constexpr int kBarDrain = kBarOEmpty + 2;      // all MMAs of the CTA done (both issuers)
-constexpr int kNumBars = kBarDrain + 1;
+constexpr int kBarRows = kBarDrain + 1;        // every unit's new K/V rows are in the ring (fuse_append)
+constexpr int kNumBars = kBarRows + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;                 // tmem addr, abort flag
-constexpr int kOffRed = kOffMisc + 16;                           // max [4][8], sums [2][4][8]
-constexpr int kOffEpi = kOffRed + (32 + 64) * 4;                 // O^T of keys 64-127 [8 queries][64 dims]
-constexpr int kTcSmem = kOffEpi + 8 * 64 * 4 + 1024;             // + alignment slack
+constexpr int kOffRed = kOffMisc + 16;                           // max [2][4][8], sums [2][4][8]
+constexpr int kOffEpi = kOffRed + (64 + 64) * 4;                 // [2 sets] O^T of keys 64-127 [8 queries][64 dims]
+constexpr int kTcSmem = kOffEpi + 2 * 8 * 64 * 4 + 1024;         // + alignment slack
 static_assert(kTcSmem <= 232448, "encoder attention exceeds 227 KB of shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
@@ -298,26 +312,56 @@ __device__ __forceinline__ void enc_drain(uint64_t * bar, uint32_t parity) {
 // one head, attending the union of their windows, walked as nb 8-slot boxes
 // from slot s0 of the virtual ring, in T tiles of 16 boxes.
 struct EncUnit {
-    int r0, nr, h, ws, we, s0, nb, T;
+    int r0, nr, h, ws, we, wem, s0, nb, T;
     int64_t ring;  // ring index (stream, layer, head)
 };
 
-__device__ __forceinline__ EncUnit enc_unit(const EncParams & p, int u, int vslots) {
-    EncUnit U;
-    const int grp = u / p.n_heads;
-    U.h = u - grp * p.n_heads;
-    U.r0 = p.group_first[grp];
-    U.nr = p.group_first[grp + 1] - U.r0;
-    const EncRowDesc first = p.rows[U.r0];
-    const EncRowDesc last = p.rows[U.r0 + U.nr - 1];
-    U.ring = ring_index(p, first.stream, U.h);
-    U.ws = first.win_start;
-    U.we = last.pos;
-    U.s0 = (U.ws % p.capacity) & ~7;
-    U.nb = (((U.we % p.capacity) - U.s0 + vslots) % vslots) / 8 + 1;
-    U.T = (U.nb + kTcBoxes - 1) / kTcBoxes;  // host guarantees T <= kTcMaxTiles
-    return U;
-}
+// Walks the units u0, u0 + step, ... of a CTA (unit = group * n_heads + head)
+// without divisions, loading each group's 32-byte descriptor (EncParams::groups)
+// one unit ahead so that its latency overlaps the current unit.
+struct UnitWalk {
+    int u, grp, h, dg, dh, step, n_units, n_heads;
+    int4 a, b;
+    __device__ __forceinline__ void init(const EncParams & p, int u0, int step_, int n_units_) {
+        u = u0;
+        step = step_;
+        n_units = n_units_;
+        n_heads = p.n_heads;
+        grp = u0 / n_heads;
+        h = u0 - grp * n_heads;
+        dg = step / n_heads;
+        dh = step - dg * n_heads;
+        if (u < n_units) fetch(p);
+    }
+    __device__ __forceinline__ void fetch(const EncParams & p) {
+        a = __ldg(p.groups + 2 * grp);
+        b = __ldg(p.groups + 2 * grp + 1);
+    }
+    __device__ __forceinline__ bool more() const { return u < n_units; }
+    // the current unit; then moves to the next and starts loading its descriptor
+    __device__ __forceinline__ EncUnit take(const EncParams & p) {
+        EncUnit U;
+        U.h = h;
+        U.r0 = a.x & 0xffffff;
+        U.nr = (int) ((unsigned) a.x >> 24);
+        U.ring = ((int64_t) a.y * p.n_layers + p.layer) * p.n_heads + h;
+        U.ws = a.z;
+        U.we = a.w;
+        U.s0 = b.x;
+        U.nb = b.y;
+        U.wem = b.z;
+        U.T = (U.nb + kTcBoxes - 1) / kTcBoxes;  // host guarantees T <= kTcMaxTiles
+        u += step;
+        h += dh;
+        grp += dg;
+        if (h >= n_heads) {
+            h -= n_heads;
+            ++grp;
+        }
+        if (u < n_units) fetch(p);
+        return U;
+    }
+};
 
 // Persistent, warp-specialised window attention.  CTA b handles units b,
 // b + gridDim.x, ...; unit i of a CTA uses buffer set i & 1 of Q, S, P and O,
@@ -334,9 +378,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     uint64_t * bars = reinterpret_cast<uint64_t *>(base + kOffBar);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(base + kOffMisc);
     volatile int32_t * abort_flag = reinterpret_cast<volatile int32_t *>(base + kOffMisc + 4);
-    float * redmax = reinterpret_cast<float *>(base + kOffRed);  // [4 warps][8]
-    float * redsum = redmax + 32;                                // [2 sets][4 warps][8]
-    float * epi = reinterpret_cast<float *>(base + kOffEpi);     // [8][64]
+    float * redmax = reinterpret_cast<float *>(base + kOffRed);  // [2 sets][4 warps][8]
+    float * redsum = redmax + 64;                                // [2 sets][4 warps][8]
+    float * epi_all = reinterpret_cast<float *>(base + kOffEpi); // [2 sets][8][64]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -361,8 +405,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             mbar_init(&bars[kBarPEmpty + b], 1);
             mbar_init(&bars[kBarOFull + b], 1);
             mbar_init(&bars[kBarOEmpty + b], 128);
+
         }
         mbar_init(&bars[kBarDrain], 2);
+        mbar_init(&bars[kBarRows], kTcThreads / 32 - 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -381,6 +427,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     // read (rows, q, the rings the append kernel just wrote) comes after this.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (p.fuse_append && warp != kWarpProducer) {
+        // Fused append (the set_rows of src/voxtral.cpp:2474-2479): every warp but
+        // the producer stores the new K (rotated) and V rows of some of the CTA's
+        // units into the ring, lane l dims 2l, 2l + 1 of each row; no other unit
+        // reads a unit's (stream, head) ring.  The producer copies the tiles that
+        // hold new rows only after all warps have signalled.
+        constexpr int kStoreWarps = kTcThreads / 32 - 1;
+        constexpr int kRowBytes = kEncHd * 2;
+        UnitWalk W;
+        W.init(p, blockIdx.x + (warp < kWarpProducer ? warp : warp - 1) * stride, kStoreWarps * stride, n_units);
+        while (W.more()) {
+            const EncUnit U = W.take(p);
+            const int pos0 = U.we - U.nr + 1;
+            int slot0 = U.wem - U.nr + 1;  // = pos0 % capacity (rows are consecutive positions)
+            slot0 = slot0 < 0 ? slot0 + cap : slot0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (j < U.nr) {
+                    const int64_t src = ((int64_t) (U.r0 + j) * p.n_heads + U.h) * kEncHd + 2 * lane;
+                    const float2 kr = enc_rope_pair(*reinterpret_cast<const float2 *>(p.k + src),
+                                                    p.rope[(int64_t) (pos0 + j) * (kEncHd / 2) + lane]);
+                    const float2 vx = *reinterpret_cast<const float2 *>(p.v + src);
+                    const int slot = slot0 + j < cap ? slot0 + j : slot0 + j - cap;
+                    // byte 4 lane of the row = chunk lane / 4, stored at chunk (lane / 4) ^ (slot & 7)
+                    const int64_t dst =
+                        (U.ring * vslots + slot) * kRowBytes + (((lane >> 2) ^ (slot & 7)) << 4) + (lane & 3) * 4;
+                    *reinterpret_cast<uint32_t *>(p.k_ring + dst) = pack2<DT>(kr.x, kr.y);
+                    *reinterpret_cast<uint32_t *>(p.v_ring + dst) = pack2<DT>(vx.x, vx.y);
+                }
+            }
+        }
+        // the producer's bulk copies (async proxy) read these rows after the signal
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kBarRows]);
+    }
     // TMEM columns (N = 16: 8 queries' hi parts, then their lo parts):
     //   S^T of set b, tile t      at 96 b + 16 t
     //   O^T of set b, accumulator a at 192 + 128 b + 32 a: an M = 128 x N = 32 block whose
@@ -388,43 +470,69 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
     //   64-127 x columns 16-31 dims 0-63 over keys 64-127 (the other quarters are unused
     //   cross products); accumulators and halves are summed in the epilogue
 
-    if (warp == 4) {
+    if (warp == kWarpProducer) {
         // ---------------- TMA producer ----------------
+        // One thread issues every copy: its per-tile path is kept short (a
+        // running stage and phase, ring bases computed once per unit), since
+        // the copies of a unit are issued back to back at the HBM rate.
         if (lane == 0) {
-            uint32_t c = 0;
+            uint32_t c = 0;           // copies issued
+            int st = 0;               // = c % kTcStages
+            uint32_t ph = 0;          // = (c / kTcStages) & 1
             bool ok = true;
             const uint64_t policy = evict_first_policy();
             constexpr int kRowBytes = kEncHd * 2;
-            auto load = [&](const EncUnit & U, bool is_v, int t) -> bool {
-                const int st = (int) (c % kTcStages);
-                if (!enc_wait(&bars[kBarEmpty + st], ((c / kTcStages) & 1) ^ 1, abort_flag, p.error)) return false;
+            const int64_t ring_bytes = (int64_t) vslots * kRowBytes;
+            // tile t of a unit whose ring starts at `ring`: 128 consecutive slots from
+            // s0 + 128 t, wrapping at the ring's end (rows past the window are read and masked)
+            auto load = [&](const uint8_t * ring, int s0, int t) -> bool {
+                if (!enc_wait(&bars[kBarEmpty + st], ph ^ 1, abort_flag, p.error)) return false;
                 uint8_t * dst = stages + st * kTcStageBytes;
-                const uint8_t * ring = (is_v ? p.v_ring : p.k_ring) + U.ring * vslots * kRowBytes;
-                mbar_expect_tx(&bars[kBarFull + st], kTcStageBytes);
-                // 128 consecutive slots from s0 + 128 t, wrapping at the ring's end
-                // (rows past the window are read and masked)
-                int slot = (U.s0 + 128 * t) % vslots;
-                int done = 0;
-                while (done < 128) {
-                    const int n = min(128 - done, vslots - slot);
-                    bulk_load(dst + done * kRowBytes, ring + (int64_t) slot * kRowBytes, (uint32_t) (n * kRowBytes),
-                              &bars[kBarFull + st], policy);
-                    done += n;
-                    slot = 0;
-                }
+                uint64_t * full = &bars[kBarFull + st];
+                mbar_expect_tx(full, kTcStageBytes);
+                int slot = s0 + 128 * t;
+                slot = slot >= vslots ? slot - vslots : slot;
+                const int n = min(128, vslots - slot);
+                bulk_load(dst, ring + slot * kRowBytes, (uint32_t) (n * kRowBytes), full, policy);
+                if (n < 128) bulk_load(dst + n * kRowBytes, ring, (uint32_t) ((128 - n) * kRowBytes), full, policy);
                 ++c;
+                if (++st == kTcStages) {
+                    st = 0;
+                    ph ^= 1;
+                }
                 return true;
             };
-            EncUnit prev{};
-            bool have_prev = false;
-            for (int u = blockIdx.x; ok && u < n_units; u += stride) {
-                const EncUnit U = enc_unit(p, u, vslots);
-                for (int t = 0; ok && t < U.T; ++t) ok = load(U, false, t);
-                for (int t = 0; ok && have_prev && t < prev.T; ++t) ok = load(prev, true, t);
-                prev = U;
-                have_prev = true;
+            const uint8_t * pv_ring = nullptr;  // V ring and geometry of the previous unit
+            int p_s0 = 0, p_T = 0;
+            bool rows_ready = !p.fuse_append;
+            UnitWalk W;
+            W.init(p, blockIdx.x, stride, n_units);
+            for (int i = 0; ok && W.more(); ++i) {
+                const EncUnit U = W.take(p);
+                const uint8_t * k_ring = p.k_ring + U.ring * ring_bytes;
+                // with fuse_append the tiles from the one holding the unit's first
+                // new row on are copied after the other warps stored the rows
+                int t_new = U.T;
+                if (p.fuse_append) {
+                    int first = U.wem - U.nr + 1;
+                    first = first < 0 ? first + cap : first;
+                    int off = first - U.s0;
+                    off = off < 0 ? off + vslots : off;
+                    t_new = off >> 7;
+                }
+                for (int t = 0; ok && t < U.T; ++t) {
+                    if (t == t_new && !rows_ready) {
+                        ok = enc_wait(&bars[kBarRows], 0, abort_flag, p.error);
+                        rows_ready = true;
+                    }
+                    ok = ok && load(k_ring, U.s0, t);
+                }
+                for (int t = 0; ok && t < p_T; ++t) ok = load(pv_ring, p_s0, t);
+                pv_ring = p.v_ring + U.ring * ring_bytes;
+                p_s0 = U.s0;
+                p_T = U.T;
             }
-            for (int t = 0; ok && have_prev && t < prev.T; ++t) ok = load(prev, true, t);
+            for (int t = 0; ok && t < p_T; ++t) ok = load(pv_ring, p_s0, t);
             if (!ok || *abort_flag) {
                 // let every issued copy land before the CTA exits
                 for (uint32_t d = c > (uint32_t) kTcStages ? c - kTcStages : 0; d < c; ++d)
@@ -432,10 +540,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             }
         }
         __syncwarp();
-    } else if (warp == 5 || warp == 7) {
-        // ---------------- tcgen05.mma issuers: S (warp 5), PV (warp 7) ----------------
+    } else if (warp == kWarpS || warp == kWarpPV) {
+        // ---------------- tcgen05.mma issuers of S and PV ----------------
         if (lane == 0) {
-            const bool s_role = warp == 5;
+            const bool s_role = warp == kWarpS;
             constexpr uint32_t fmt = DT == 30 ? 1u : 0u;  // BF16 / F16 operands
             // fp32 accumulate.  S: M = 128 keys, N = 16, K-major A.  PV: M = 128 (dims of
             // keys 0-63, then dims of keys 64-127: the V tile's two 64-key halves are two
@@ -451,31 +559,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
                 tc_fence_after();
                 const uint32_t qa = smem_u32(qbuf + b * 2048);
                 const uint32_t sd = tmem + 96 * b;
-                // tiles in pairs, their MMAs interleaved so that consecutive
-                // MMAs write different accumulators
-                for (int t = 0; t < U.T; t += 2) {
-                    const bool two = t + 1 < U.T;
-                    const int st0 = (int) (c % kTcStages);
-                    if (!enc_wait(&bars[kBarFull + st0], (c / kTcStages) & 1, abort_flag, p.error)) return false;
-                    const int st1 = (int) ((c + 1) % kTcStages);
-                    if (two && !enc_wait(&bars[kBarFull + st1], ((c + 1) / kTcStages) & 1, abort_flag, p.error))
-                        return false;
-                    tc_fence_after();
-                    const uint32_t sa0 = smem_u32(stages + st0 * kTcStageBytes);
-                    const uint32_t sa1 = smem_u32(stages + st1 * kTcStageBytes);
-                    // S^T tile = K . [Q_hi; Q_lo]^T
+                uint64_t bq[4];
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        const uint64_t bq = sw128_desc(qa + ks * 32, 16, 1024);
-                        tc_mma(sd + 16 * t, sw128_desc(sa0 + ks * 32, 16, 1024), bq, idesc_qk, ks != 0);
-                        if (two) tc_mma(sd + 16 * (t + 1), sw128_desc(sa1 + ks * 32, 16, 1024), bq, idesc_qk, ks != 0);
-                    }
-                    tc_commit(&bars[kBarEmpty + st0]);
+                for (int ks = 0; ks < 4; ++ks) bq[ks] = sw128_desc(qa + ks * 32, 16, 1024);
+                // each tile as soon as it lands (its stage is released by the commit)
+                for (int t = 0; t < U.T; ++t) {
+                    const int st = (int) (c % kTcStages);
+                    if (!enc_wait(&bars[kBarFull + st], (c / kTcStages) & 1, abort_flag, p.error)) return false;
+                    tc_fence_after();
+                    const uint64_t ka = sw128_desc(smem_u32(stages + st * kTcStageBytes), 16, 1024);
+                    // S^T tile = K . [Q_hi; Q_lo]^T; +2 in the descriptor = +32 bytes (16 dims)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) tc_mma(sd + 16 * t, ka + 2 * ks, bq[ks], idesc_qk, ks != 0);
+                    tc_commit(&bars[kBarEmpty + st]);
                     ++c;
-                    if (two) {
-                        tc_commit(&bars[kBarEmpty + st1]);
-                        ++c;
-                    }
                 }
                 tc_commit(&bars[kBarQEmpty + b]);
                 tc_commit(&bars[kBarSFull + b]);
@@ -515,8 +612,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             EncUnit prev{};
             int i = 0;
             uint32_t kc = 0;
-            for (int u = blockIdx.x; ok && u < n_units; u += stride, ++i) {
-                const EncUnit U = enc_unit(p, u, vslots);
+            UnitWalk W;
+            W.init(p, blockIdx.x, stride, n_units);
+            for (; ok && W.more(); ++i) {
+                const EncUnit U = W.take(p);
                 if (s_role) {
                     c = kc;
                     ok = s_unit(U, i);
@@ -537,25 +636,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             enc_drain(&bars[kBarDrain], 0);
         }
         __syncwarp();
-    } else if (warp == 6) {
+    } else if (warp == kWarpQ) {
         // ---------------- Q^T (hi, lo) producer ----------------
         // 8 query rows x 64 dims per unit, rotated, scaled by log2(e)/sqrt(64),
-        // 128-byte swizzled K-major rows.  Lane l handles dims 2l, 2l+1.
-        int i = 0;
-        for (int u = blockIdx.x; u < n_units; u += stride, ++i) {
-            const EncUnit U = enc_unit(p, u, vslots);
+        // 128-byte swizzled K-major rows.  Lane l handles dims 2l, 2l+1 of every
+        // row; rows of a group are consecutive positions ending at U.we.
+        UnitWalk W;
+        W.init(p, blockIdx.x, stride, n_units);
+        for (int i = 0; W.more(); ++i) {
+            const EncUnit U = W.take(p);
             const int b = i & 1;
             const uint32_t k = (uint32_t) (i >> 1) & 1;
+            const int pos0 = U.we - U.nr + 1;
+            float2 xq[8], cs[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                xq[j] = cs[j] = make_float2(0.0f, 0.0f);
+                if (j < U.nr) {
+                    xq[j] = *reinterpret_cast<const float2 *>(p.q + ((int64_t) (U.r0 + j) * p.n_heads + U.h) * kEncHd +
+                                                                2 * lane);
+                    cs[j] = p.rope[(int64_t) (pos0 + j) * (kEncHd / 2) + lane];
+                }
+            }
             if (!__all_sync(kFull, enc_wait(&bars[kBarQEmpty + b], k ^ 1, abort_flag, p.error))) break;
             uint8_t * qb = qbuf + b * 2048;
-#pragma unroll 1
+#pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float2 qv = make_float2(0.0f, 0.0f);
                 if (j < U.nr) {
-                    const EncRowDesc rd = p.rows[U.r0 + j];
-                    const float2 x =
-                        *reinterpret_cast<const float2 *>(p.q + ((int64_t) (U.r0 + j) * p.n_heads + U.h) * kEncHd + 2 * lane);
-                    const float2 rr = enc_rope_pair(x, p.rope[(int64_t) rd.pos * (kEncHd / 2) + lane]);
+                    const float2 rr = enc_rope_pair(xq[j], cs[j]);
                     qv = make_float2(rr.x * p.scale_log2, rr.y * p.scale_log2);
                 }
                 const uint16_t hx = to16<DT>(qv.x), hy = to16<DT>(qv.y);
@@ -569,12 +678,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             if (lane == 0) mbar_arrive(&bars[kBarQFull + b]);
         }
     } else {
-        // ---------------- softmax and epilogue, warps 0-3 ----------------
-        // Thread r owns key row r of every tile (TMEM lane r).  The loop never
-        // leaves early, so the named barriers stay matched; after an abort
-        // every wait returns at once and no result is written.
-        const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
-        const int r = 32 * warp + lane;
+        // ---------------- softmax and epilogue, warps 0-7 ----------------
+        // Set `set` (warps 4 set .. 4 set + 3) takes the CTA's units i with
+        // i & 1 == set, i.e. buffer set b = set of Q, S, P and O.  Thread r
+        // owns key row r of every tile (TMEM lane r, quadrant warp & 3).  The
+        // loop never leaves early, so the set's named barrier stays matched;
+        // after an abort every wait returns at once and no result is written.
+        const int set = warp >> 2;
+        const int wq = warp & 3;
+        const uint32_t lane_off = (uint32_t) (32 * wq) << 16;
+        const int r = 32 * wq + lane;
+        float * epi = epi_all + set * 8 * 64;
+        float * rmax = redmax + set * 32;
         auto epilogue = [&](const EncUnit & U, int j) {
             const int b = j & 1;
             const uint32_t k = (uint32_t) (j >> 1) & 1;
@@ -583,7 +698,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             float ov[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) ov[q] = 0.0f;
-            const int half = warp >> 1;  // lanes 0-63: keys 0-63 of each tile; lanes 64-127: keys 64-127
+            const int half = wq >> 1;  // lanes 0-63: keys 0-63 of each tile; lanes 64-127: keys 64-127
             if (have_o) {
                 uint32_t acc[4][16];
 #pragma unroll
@@ -596,12 +711,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarOEmpty + b]);
-            const int dim = 32 * (warp & 1) + lane;
+            const int dim = 32 * (wq & 1) + lane;
             if (half) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) epi[q * 64 + dim] = ov[q];
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + set) : "memory");
             if (!half && have_o && !*abort_flag) {
                 const float * ls = redsum + b * 32;
                 for (int q = 0; q < U.nr; ++q) {
@@ -609,12 +724,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
                     p.out[((int64_t) (U.r0 + q) * p.n_heads + U.h) * kEncHd + dim] = (ov[q] + epi[q * 64 + dim]) / L;
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // epi is rewritten by the next epilogue
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + set) : "memory");  // epi is rewritten by the next epilogue
         };
+        UnitWalk W;
+        W.init(p, blockIdx.x + set * stride, kTcSets * stride, n_units);
         EncUnit prev{};
-        int i = 0;
-        for (int u = blockIdx.x; u < n_units; u += stride, ++i) {
-            const EncUnit U = enc_unit(p, u, vslots);
+        int iprev = -1;
+        for (int i = set; W.more(); i += kTcSets) {
+            const EncUnit U = W.take(p);
             const int b = i & 1;
             const uint32_t k = (uint32_t) (i >> 1) & 1;
             float sv[kTcMaxTiles][8];
@@ -633,7 +750,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             mbar_arrive(&bars[kBarSEmpty + b]);
             int qpos[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) qpos[q] = q < U.nr ? p.rows[U.r0 + q].pos : -1;
+            for (int q = 0; q < 8; ++q) qpos[q] = q < U.nr ? U.we - U.nr + 1 + q : -1;
             float mx[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
@@ -641,7 +758,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             // (gb < nb) s0 + 8 gb < 2 vslots and (we % cap) - slot + cap lies in
             // (0, 2 cap), so one conditional subtraction replaces each modulo;
             // the other rows are masked whatever they compute
-            const int wem = U.we % cap;
+            const int wem = U.wem;
 #pragma unroll
             for (int t = 0; t < kTcMaxTiles; ++t) {
                 if (t >= U.T) break;
@@ -668,13 +785,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             }
             if (lane == 0) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) redmax[warp * 8 + q] = mx[q];
+                for (int q = 0; q < 8; ++q) rmax[wq * 8 + q] = mx[q];
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + set) : "memory");
             float M[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                M[q] = fmaxf(fmaxf(redmax[q], redmax[8 + q]), fmaxf(redmax[16 + q], redmax[24 + q]));
+                M[q] = fmaxf(fmaxf(rmax[q], rmax[8 + q]), fmaxf(rmax[16 + q], rmax[24 + q]));
                 if (M[q] == -INFINITY) M[q] = 0.0f;  // padding queries
             }
             // P of set b is free once the PV MMAs of unit i-2 completed
@@ -710,13 +827,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
             }
             if (lane == 0) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) redsum[b * 32 + warp * 8 + q] = ls[q];
+                for (int q = 0; q < 8; ++q) redsum[b * 32 + wq * 8 + q] = ls[q];
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (i > 0) epilogue(prev, i - 1);
-            prev = U;
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + set) : "memory");
+            if (kTcSets == 2) {
+                // this set's next unit is two units away: finish this one first
+                epilogue(U, i);
+            } else {
+                // one set: the previous unit's products are done by now
+                if (iprev >= 0) epilogue(prev, iprev);
+                prev = U;
+                iprev = i;
+            }
         }
-        if (i > 0) epilogue(prev, i - 1);
+        if (kTcSets == 1 && iprev >= 0) epilogue(prev, iprev);
     }
     tc_fence_before();
     __syncthreads();

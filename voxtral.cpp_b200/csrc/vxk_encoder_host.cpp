@@ -75,11 +75,14 @@ struct vxk_enc_pool {
     size_t stage_bytes = 0;
     size_t off_groups = 0;   // capacity of the row region
     size_t cur_groups = 0;   // the current batch's group table, right after its rows
+    size_t cur_gdesc = 0;    // and its group descriptors, right after the table
     std::vector<EncStream> streams;
     bool planned = false;
     std::vector<EncPlan> plan;
     std::vector<vxk::EncRowDesc> rows;
     std::vector<int32_t> group_first;
+    std::vector<int32_t> gdesc;  // 8 ints per group (vxk::EncParams::groups)
+    bool one_group_per_stream = false;  // every stream of the batch has <= kEncRowsPerGroup new rows
     std::vector<uint8_t> h_read;  // readback staging of vxk_enc_read_slots
     std::string last_error;
 };
@@ -146,6 +149,7 @@ vxk::EncParams enc_params(vxk_enc_pool * p, int32_t layer, const float * q, cons
     e.n_rows = (int32_t) p->rows.size();
     e.group_first = reinterpret_cast<const int32_t *>(p->d_stage + p->cur_groups);
     e.n_groups = (int32_t) p->group_first.size() - 1;
+    e.groups = reinterpret_cast<const int4 *>(p->d_stage + p->cur_gdesc);
     e.q = q;
     e.k = k;
     e.v = v;
@@ -261,7 +265,8 @@ vxk_status vxk_enc_create(const vxk_enc_config * config, vxk_enc_pool ** out) {
         const size_t max_rows = (size_t) c.max_streams * c.max_new;
         const size_t max_groups = max_rows;  // at most one group per row
         p->off_groups = (max_rows * sizeof(vxk::EncRowDesc) + 255) / 256 * 256;
-        p->stage_bytes = p->off_groups + (max_groups + 1) * sizeof(int32_t);
+        p->stage_bytes = p->off_groups + ((max_groups + 1) * sizeof(int32_t) + 15) / 16 * 16 +
+                         (size_t) max_groups * 8 * sizeof(int32_t);
         VXK_ECUDA(cudaMalloc(&p->d_stage, p->stage_bytes));
         VXK_ECUDA(cudaMallocHost(reinterpret_cast<void **>(&p->h_stage), p->stage_bytes));
         VXK_ECUDA(cudaEventCreateWithFlags(&p->stage_ev, cudaEventDisableTiming));
@@ -373,14 +378,36 @@ vxk_status vxk_enc_batch_plan(vxk_enc_pool * pool, const int32_t * stream_ids, c
             pool->plan.push_back({stream_ids[i], pl});
         }
         pool->group_first.push_back((int32_t) pool->rows.size());
+        pool->one_group_per_stream = true;
+        for (int32_t i = 0; i < n_streams; ++i)
+            if (n_new[i] > kEncRowsPerGroup) pool->one_group_per_stream = false;
         EncDevice scope(c.device);
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         VXK_ECUDA(cudaEventSynchronize(pool->stage_ev));
         const size_t rows_b = pool->rows.size() * sizeof(vxk::EncRowDesc);
+        const size_t n_groups = pool->group_first.size() - 1;
+        pool->gdesc.resize(8 * n_groups);
+        const int32_t vslots = ring_slots_of(c.capacity);
+        for (size_t g = 0; g < n_groups; ++g) {
+            const int32_t r0 = pool->group_first[g], nr = pool->group_first[g + 1] - r0;
+            const int32_t ws = pool->rows[(size_t) r0].win_start, we = pool->rows[(size_t) (r0 + nr - 1)].pos;
+            const int32_t s0 = (ws % c.capacity) & ~7, wem = we % c.capacity;
+            int32_t * d = &pool->gdesc[8 * g];
+            d[0] = r0 | (nr << 24);
+            d[1] = pool->rows[(size_t) r0].stream;
+            d[2] = ws;
+            d[3] = we;
+            d[4] = s0;                                    // first 8-slot box of the window walk
+            d[5] = ((wem - s0 + vslots) % vslots) / 8 + 1;  // boxes walked
+            d[6] = wem;                                   // slot of the last row
+            d[7] = 0;
+        }
         pool->cur_groups = (rows_b + 255) / 256 * 256;  // <= off_groups: one copy of the used bytes
+        pool->cur_gdesc = pool->cur_groups + (pool->group_first.size() * sizeof(int32_t) + 15) / 16 * 16;
         std::memcpy(pool->h_stage, pool->rows.data(), rows_b);
         std::memcpy(pool->h_stage + pool->cur_groups, pool->group_first.data(), pool->group_first.size() * sizeof(int32_t));
-        VXK_ECUDA(cudaMemcpyAsync(pool->d_stage, pool->h_stage, pool->cur_groups + pool->group_first.size() * sizeof(int32_t),
+        std::memcpy(pool->h_stage + pool->cur_gdesc, pool->gdesc.data(), pool->gdesc.size() * sizeof(int32_t));
+        VXK_ECUDA(cudaMemcpyAsync(pool->d_stage, pool->h_stage, pool->cur_gdesc + pool->gdesc.size() * sizeof(int32_t),
                                   cudaMemcpyHostToDevice, cs));
         VXK_ECUDA(cudaEventRecord(pool->stage_ev, cs));
         pool->planned = true;
@@ -419,8 +446,13 @@ vxk_status vxk_enc_layer(vxk_enc_pool * pool, int32_t layer, const float * q, co
         if (!q || !k || !v || !out) efail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
         EncDevice scope(pool->cfg.device);
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
-        const vxk::EncParams e = enc_params(pool, layer, q, k, v, out);
-        VXK_ECUDA(vxk::launch_enc_append(e, cs));
+        vxk::EncParams e = enc_params(pool, layer, q, k, v, out);
+        // One group per stream (the steady chunk of <= 8 frames): no other
+        // group reads a group's new rows, so the attention kernel stores them
+        // itself; otherwise later groups of a stream read the rows of earlier
+        // ones, which the separate append kernel writes first.
+        e.fuse_append = pool->one_group_per_stream && pool->cfg.dtype != VXK_DTYPE_F32 ? 1 : 0;
+        if (!e.fuse_append) VXK_ECUDA(vxk::launch_enc_append(e, cs));
         VXK_ECUDA(vxk::launch_enc_attention(e, cs));
     });
 }

@@ -201,6 +201,12 @@ struct EncParams {
     int32_t n_rows;
     const int32_t * group_first;  // first row of each (stream) group
     int32_t n_groups;
+    // per group two int4: {first row | rows << 24, stream, first row's window
+    // start, last row's position} and {first 8-slot box of the window walk
+    // (window start % capacity rounded down to 8), boxes walked, last row's
+    // slot, 0}: what the attention kernel needs of a group, without divisions
+    // (rows of a group are consecutive positions)
+    const int4 * groups;
     const float * q;        // [rows][n_heads][64]
     const float * k;
     const float * v;
@@ -210,6 +216,10 @@ struct EncParams {
     float scale_log2;
     int32_t * error;
     int32_t dtype;          // 30 = bf16, 1 = f16, 0 = f32
+    // 1 when every group is a whole stream (<= 8 new rows each): the attention
+    // kernel then stores its own group's new K/V rows before loading the
+    // window, and launch_enc_attention needs no launch_enc_append before it
+    int32_t fuse_append;
 };
 
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream);

@@ -55,21 +55,26 @@ template <int DT> struct Cfg;
 // per SM with three stages each (161 registers, no spills) measured 0.83 of
 // the copy peak on 128 streams at 8K-32K positions, against 0.75 for two
 // CTAs with five stages.
+// kTile: bytes of a tile's values; kScale: of its q8_0 block scales; kRec: the
+// tile's record in the cache arrays (values, then scales: one bulk copy).
 template <> struct Cfg<0> {
     static constexpr int kTile = kBlockTokens * kHeadDim * 4;   // 8192
     static constexpr int kScale = 0;
+    static constexpr int kRec = kTile;
     static constexpr int kStages = 3;
     static constexpr int kMinBlocks = 1;
 };
 template <> struct Cfg<1> {
     static constexpr int kTile = kBlockTokens * kHeadDim * 2;   // 4096
     static constexpr int kScale = 0;
+    static constexpr int kRec = kTile;
     static constexpr int kStages = 3;                            // per warp
     static constexpr int kMinBlocks = 2;
 };
 template <> struct Cfg<8> {
     static constexpr int kTile = kBlockTokens * kHeadDim;       // 2048
     static constexpr int kScale = kBlockTokens * (kHeadDim / kQ8Block) * 2;  // 128
+    static constexpr int kRec = kTile + kScale;                             // 2176
     static constexpr int kStages = 3;
     static constexpr int kMinBlocks = 3;
 };
@@ -251,8 +256,7 @@ __device__ __forceinline__ void q8_pair(float2 x, char2 & q, float & d) {
 // given (the fused decode patches them into its copy of the tile).
 template <int DT>
 __device__ __forceinline__ void append_head_row(const float * k, const float * v, const float2 * cs,
-                                                uint8_t * k_data, uint8_t * v_data, uint8_t * k_scale,
-                                                uint8_t * v_scale, int64_t tile, int tok, uint8_t * sk,
+                                                uint8_t * k_data, uint8_t * v_data, int64_t tile, int tok, uint8_t * sk,
                                                 uint8_t * sv, uint16_t * sks, uint16_t * svs) {
     const int tid = threadIdx.x;
     const bool is_k = tid < 64;
@@ -272,7 +276,7 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
         char2 q;
         float d;
         q8_pair(x, q, d);
-        uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<8>::kTile;
+        uint8_t * t = (is_k ? k_data : v_data) + tile * Cfg<8>::kRec;
         if (!is_k) {
             // V values are stored with the sign bit flipped (the byte of x + 128):
             // the decode widens them to f16 without an XOR; readback flips back.
@@ -284,7 +288,7 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
         if ((i & 15) == 0) {
             const __half dh = __float2half_rn(d);
             const int blk = i >> 4;
-            uint8_t * sb = (is_k ? k_scale : v_scale) + tile * Cfg<8>::kScale;
+            uint8_t * sb = t + Cfg<8>::kTile;  // the record's scales follow its values
             reinterpret_cast<__half *>(sb)[blk * kBlockTokens + tok] = dh;
             if (sks) (is_k ? sks : svs)[blk] = __half_as_ushort(dh);
         }
@@ -305,6 +309,7 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
     constexpr int ST = Cfg<DT>::kStages;
     constexpr int TILE = Cfg<DT>::kTile;
     constexpr int SCALE = Cfg<DT>::kScale;
+    constexpr int REC = Cfg<DT>::kRec;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -371,13 +376,10 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
                 const int64_t tile = (int64_t) pg * p.n_kv + cur.kvh;
                 uint64_t * bar = &S.full[warp][st];
                 uint8_t * dst = S.stage[warp][st];
+                // one copy per record: the stage is [K values | K scales | V values | V scales]
                 mbar_expect_tx(bar, stage_bytes<DT>());
-                bulk_g2s(dst, p.k_data + tile * TILE, TILE, bar, policy);
-                bulk_g2s(dst + TILE + SCALE, p.v_data + tile * TILE, TILE, bar, policy);
-                if constexpr (SCALE > 0) {
-                    bulk_g2s(dst + TILE, p.k_scale + tile * SCALE, SCALE, bar, policy);
-                    bulk_g2s(dst + 2 * TILE + SCALE, p.v_scale + tile * SCALE, SCALE, bar, policy);
-                }
+                bulk_g2s(dst, p.k_data + tile * REC, REC, bar, policy);
+                bulk_g2s(dst + REC, p.v_data + tile * REC, REC, bar, policy);
             }
             ++seq_issued;
             ist = ist + 1 == ST ? 0 : ist + 1;
@@ -501,7 +503,7 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
             const int64_t tile = (int64_t) pg * p.n_kv + kvh;
             const int64_t krow = ((int64_t) it.row * p.n_kv + kvh) * kHeadDim;
             append_head_row<DT>(p.k + krow, p.v + krow, p.rope + (int64_t) rd.pos * (kHeadDim / 2), p.k_data,
-                                p.v_data, p.k_scale, p.v_scale, tile, rd.pos % kBlockTokens, S.newk, S.newv,
+                                p.v_data, tile, rd.pos % kBlockTokens, S.newk, S.newv,
                                 S.newk_scale, S.newv_scale);
         }
         __syncthreads();
@@ -984,7 +986,7 @@ __global__ void __launch_bounds__(NT) append_kernel(const AppendParams p) {
     const int64_t tile = (int64_t) pg * p.n_kv + kvh;
     const int64_t krow = ((int64_t) row * p.n_kv + kvh) * kHeadDim;
     append_head_row<DT>(p.k + krow, p.v + krow, p.rope + (int64_t) rd.pos * (kHeadDim / 2), p.k_data, p.v_data,
-                        p.k_scale, p.v_scale, tile, rd.pos % kBlockTokens, nullptr, nullptr, nullptr, nullptr);
+                        tile, rd.pos % kBlockTokens, nullptr, nullptr, nullptr, nullptr);
 }
 
 __global__ void table_update_kernel(int32_t * table, const TableUpdate * up, int32_t n) {
@@ -1007,8 +1009,8 @@ __global__ void gather_kernel(const GatherParams p) {
     constexpr int row_bytes = DT == 0 ? kHeadDim * 4 : DT == 1 ? kHeadDim * 2 : kHeadDim;
     constexpr int chunks = row_bytes / 16;
     const int64_t dst = ((int64_t) r * p.n_kv + kvh) * row_bytes;
-    const uint8_t * kt = p.k_data + tile * Cfg<DT>::kTile;
-    const uint8_t * vt = p.v_data + tile * Cfg<DT>::kTile;
+    const uint8_t * kt = p.k_data + tile * Cfg<DT>::kRec;
+    const uint8_t * vt = p.v_data + tile * Cfg<DT>::kRec;
     for (int ch = threadIdx.x; ch < chunks; ch += blockDim.x) {
         const int off = DT == 0 ? f32_chunk_off(tok, ch) : DT == 1 ? f16_chunk_off(tok, ch) : q8_chunk_off(tok, ch);
         *reinterpret_cast<uint4 *>(p.k_out + dst + ch * 16) = *reinterpret_cast<const uint4 *>(kt + off);
@@ -1024,8 +1026,8 @@ __global__ void gather_kernel(const GatherParams p) {
     if constexpr (DT == 8) {
         constexpr int nb = kHeadDim / kQ8Block;
         const int64_t sdst = ((int64_t) r * p.n_kv + kvh) * nb;
-        const uint16_t * ks = reinterpret_cast<const uint16_t *>(p.k_scale + tile * Cfg<8>::kScale);
-        const uint16_t * vs = reinterpret_cast<const uint16_t *>(p.v_scale + tile * Cfg<8>::kScale);
+        const uint16_t * ks = reinterpret_cast<const uint16_t *>(kt + Cfg<8>::kTile);
+        const uint16_t * vs = reinterpret_cast<const uint16_t *>(vt + Cfg<8>::kTile);
         for (int b = threadIdx.x; b < nb; b += blockDim.x) {
             reinterpret_cast<uint16_t *>(p.k_scale_out)[sdst + b] = ks[b * kBlockTokens + tok];
             reinterpret_cast<uint16_t *>(p.v_scale_out)[sdst + b] = vs[b * kBlockTokens + tok];
@@ -1045,13 +1047,6 @@ __global__ void __launch_bounds__(256) compact_kernel(const CompactParams p) {
         const uint4 * src = reinterpret_cast<const uint4 *>(base + (int64_t) mv.x * p.page_data_bytes);
         uint4 * dst = reinterpret_cast<uint4 *>(base + (int64_t) mv.y * p.page_data_bytes);
         const int64_t n = p.page_data_bytes / 16;
-        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
-    }
-    if (p.page_scale_bytes > 0) {
-        uint8_t * base = (is_v ? p.v_scale : p.k_scale) + (int64_t) layer * p.layer_scale_bytes;
-        const uint4 * src = reinterpret_cast<const uint4 *>(base + (int64_t) mv.x * p.page_scale_bytes);
-        uint4 * dst = reinterpret_cast<uint4 *>(base + (int64_t) mv.y * p.page_scale_bytes);
-        const int64_t n = p.page_scale_bytes / 16;
         for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
     }
 }

@@ -61,11 +61,11 @@ constexpr int kPartialStride = kHeadDim + 4;
 constexpr int kMaxSplitPages = 512;
 
 struct DecodeParams {
-    // cache of one layer
-    uint8_t * k_data;        // f16 halves or q8_0 int8 values
+    // cache of one layer: one record per (page, kv head): the swizzled tile's
+    // f32 / f16 values, or for q8_0 its int8 values followed by its f16 block
+    // scales ([4 blocks][16 rows]), 2176 bytes
+    uint8_t * k_data;
     uint8_t * v_data;
-    uint8_t * k_scale;       // q8_0 f16 scales (nullptr for f16)
-    uint8_t * v_scale;
     int32_t n_blocks;
     int32_t n_kv;
     int32_t n_q;
@@ -93,10 +93,8 @@ struct DecodeParams {
 };
 
 struct AppendParams {
-    uint8_t * k_data;
+    uint8_t * k_data;  // records as in DecodeParams
     uint8_t * v_data;
-    uint8_t * k_scale;
-    uint8_t * v_scale;
     int32_t n_blocks;
     int32_t n_kv;
     int32_t bt_cap;
@@ -112,10 +110,8 @@ struct AppendParams {
 };
 
 struct GatherParams {
-    const uint8_t * k_data;
+    const uint8_t * k_data;  // records as in DecodeParams
     const uint8_t * v_data;
-    const uint8_t * k_scale;
-    const uint8_t * v_scale;
     int32_t n_blocks;
     int32_t n_kv;
     int32_t bt_cap;
@@ -132,12 +128,8 @@ struct GatherParams {
 struct CompactParams {
     uint8_t * k_data;           // base of layer 0
     uint8_t * v_data;
-    uint8_t * k_scale;
-    uint8_t * v_scale;
     int64_t layer_data_bytes;   // bytes per layer of k_data
-    int64_t layer_scale_bytes;
-    int64_t page_data_bytes;    // bytes per page per layer (all kv heads)
-    int64_t page_scale_bytes;
+    int64_t page_data_bytes;    // bytes per page per layer (all kv heads' records)
     int32_t n_layers;
     const int2 * moves;         // (src, dst)
     int32_t n_moves;

@@ -107,16 +107,11 @@ struct vxk_pool {
     int32_t decode_slots = 0;        // resident decode CTAs on the device
     int32_t bt_cap = 0;
     int64_t tile_data_bytes = 0;
-    int64_t tile_scale_bytes = 0;
     int64_t page_data_bytes = 0;
-    int64_t page_scale_bytes = 0;
     int64_t layer_data_bytes = 0;
-    int64_t layer_scale_bytes = 0;
 
     uint8_t * k_data = nullptr;
     uint8_t * v_data = nullptr;
-    uint8_t * k_scale = nullptr;
-    uint8_t * v_scale = nullptr;
     int32_t * d_table = nullptr;
     float2 * d_rope = nullptr;
     float * d_partials = nullptr;
@@ -205,8 +200,6 @@ vxk_status guarded(vxk_pool * pool, F && body) {
 void release_device(vxk_pool * p) {
     cudaFree(p->k_data);
     cudaFree(p->v_data);
-    cudaFree(p->k_scale);
-    cudaFree(p->v_scale);
     cudaFree(p->d_table);
     cudaFree(p->d_rope);
     cudaFree(p->d_partials);
@@ -476,8 +469,6 @@ vxk::DecodeParams decode_params(vxk_pool * p, int32_t layer, const float * q, co
     vxk::DecodeParams d{};
     d.k_data = p->k_data + (int64_t) layer * p->layer_data_bytes;
     d.v_data = p->v_data + (int64_t) layer * p->layer_data_bytes;
-    d.k_scale = p->k_scale ? p->k_scale + (int64_t) layer * p->layer_scale_bytes : nullptr;
-    d.v_scale = p->v_scale ? p->v_scale + (int64_t) layer * p->layer_scale_bytes : nullptr;
     d.n_blocks = p->cfg.n_blocks;
     d.n_kv = p->cfg.n_kv_heads;
     d.n_q = p->cfg.n_q_heads;
@@ -692,24 +683,17 @@ vxk_status vxk_pool_create(const vxk_pool_config * config, vxk_pool ** out_pool)
         const vxk_pool_config & c = p->cfg;
         p->bt_cap = c.capacity / c.block_tokens;
         const bool q8 = c.dtype == VXK_DTYPE_Q8_0;
-        p->tile_data_bytes = (int64_t) c.block_tokens * c.head_dim * elem_bytes(c.dtype);
-        p->tile_scale_bytes = q8 ? (int64_t) c.block_tokens * (c.head_dim / vxk::kQ8Block) * 2 : 0;
+        // a tile's record: its values, then (q8_0) its f16 block scales, so that
+        // one bulk copy brings both
+        p->tile_data_bytes = (int64_t) c.block_tokens * c.head_dim * elem_bytes(c.dtype) +
+                             (q8 ? (int64_t) c.block_tokens * (c.head_dim / vxk::kQ8Block) * 2 : 0);
         p->page_data_bytes = p->tile_data_bytes * c.n_kv_heads;
-        p->page_scale_bytes = p->tile_scale_bytes * c.n_kv_heads;
         p->layer_data_bytes = p->page_data_bytes * c.n_blocks;
-        p->layer_scale_bytes = p->page_scale_bytes * c.n_blocks;
         const size_t data_bytes = (size_t) p->layer_data_bytes * (size_t) c.n_layers;
         p->k_data = device_alloc<uint8_t>(p, data_bytes);
         p->v_data = device_alloc<uint8_t>(p, data_bytes);
         VXK_CUDA(cudaMemset(p->k_data, 0, data_bytes));
         VXK_CUDA(cudaMemset(p->v_data, 0, data_bytes));
-        if (q8) {
-            const size_t sb = (size_t) p->layer_scale_bytes * (size_t) c.n_layers;
-            p->k_scale = device_alloc<uint8_t>(p, sb);
-            p->v_scale = device_alloc<uint8_t>(p, sb);
-            VXK_CUDA(cudaMemset(p->k_scale, 0, sb));
-            VXK_CUDA(cudaMemset(p->v_scale, 0, sb));
-        }
         const size_t table_n = (size_t) c.max_streams * (size_t) p->bt_cap;
         p->d_table = device_alloc<int32_t>(p, table_n * sizeof(int32_t));
         VXK_CUDA(cudaMemset(p->d_table, 0xff, table_n * sizeof(int32_t)));
@@ -985,8 +969,6 @@ vxk_status vxk_append_layer(vxk_pool * pool, int32_t layer, const float * k, con
         vxk::AppendParams a{};
         a.k_data = pool->k_data + (int64_t) layer * pool->layer_data_bytes;
         a.v_data = pool->v_data + (int64_t) layer * pool->layer_data_bytes;
-        a.k_scale = pool->k_scale ? pool->k_scale + (int64_t) layer * pool->layer_scale_bytes : nullptr;
-        a.v_scale = pool->v_scale ? pool->v_scale + (int64_t) layer * pool->layer_scale_bytes : nullptr;
         a.n_blocks = pool->cfg.n_blocks;
         a.n_kv = pool->cfg.n_kv_heads;
         a.bt_cap = pool->bt_cap;
@@ -1171,7 +1153,7 @@ vxk_status vxk_pool_compact(vxk_pool * pool, void * cuda_stream, int64_t * out_p
                 if (pool->owner_stream[(size_t) i] < 0) pool->free_pages.push_back(i);
             }
         }
-        const int64_t per_page = (pool->page_data_bytes + pool->page_scale_bytes) * 2 * c.n_layers;
+        const int64_t per_page = pool->page_data_bytes * 2 * c.n_layers;
         if (!moves.empty()) {
             if (!pool->d_moves) {
                 pool->d_moves = device_alloc<int2>(pool, (size_t) c.n_blocks * sizeof(int2));
@@ -1185,12 +1167,8 @@ vxk_status vxk_pool_compact(vxk_pool * pool, void * cuda_stream, int64_t * out_p
             vxk::CompactParams cp{};
             cp.k_data = pool->k_data;
             cp.v_data = pool->v_data;
-            cp.k_scale = pool->k_scale;
-            cp.v_scale = pool->v_scale;
             cp.layer_data_bytes = pool->layer_data_bytes;
-            cp.layer_scale_bytes = pool->layer_scale_bytes;
             cp.page_data_bytes = pool->page_data_bytes;
-            cp.page_scale_bytes = pool->page_scale_bytes;
             cp.n_layers = c.n_layers;
             cp.moves = pool->d_moves;
             cp.n_moves = (int32_t) moves.size();
@@ -1267,8 +1245,6 @@ vxk_status vxk_read_rows(vxk_pool * pool, int32_t layer, int32_t stream, int64_t
         vxk::GatherParams g{};
         g.k_data = pool->k_data + (int64_t) layer * pool->layer_data_bytes;
         g.v_data = pool->v_data + (int64_t) layer * pool->layer_data_bytes;
-        g.k_scale = q8 ? pool->k_scale + (int64_t) layer * pool->layer_scale_bytes : nullptr;
-        g.v_scale = q8 ? pool->v_scale + (int64_t) layer * pool->layer_scale_bytes : nullptr;
         g.n_blocks = pool->cfg.n_blocks;
         g.n_kv = nkv;
         g.bt_cap = pool->bt_cap;

@@ -855,24 +855,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
 // f32 rings: window attention on the CUDA cores
 // ---------------------------------------------------------------------------
 constexpr int kF32Threads = 128;
-constexpr int kF32Tile = 128;                  // keys per tile
+constexpr int kF32Tile = 128;                  // keys per stage
+constexpr int kF32Stages = 2;                  // a stage in flight while the other is used
 constexpr int kF32MaxKeys = 768;               // window - 1 + 8 rows fits (host checks <= 752)
 constexpr int kF32Rows = 8;                    // rows per group (kEncRowsPerGroup)
 constexpr int kF32RowBytes = kEncHd * 4;       // 256
 
 struct __align__(128) EncF32Smem {
-    float kv[2][kF32Tile * kEncHd];            // two tile buffers (rows swizzled as in the ring)
+    float kv[kF32Stages][kF32Tile * kEncHd];   // 128-key stages (rows swizzled as in the ring)
     float s[kF32MaxKeys][kF32Rows];            // scores, then probabilities: [key][row]
     float q[kEncHd][kF32Rows];                 // rotated, scaled queries: [dim][row]
     float red[kF32Threads / 32][kF32Rows];
     float inv_l[kF32Rows];
-    uint64_t full[2];
+    uint64_t full[kF32Stages];
     int32_t abort_flag;
 };
-static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * 2 * kF32Tile * kEncHd,
-              "P.V partial sums fit the tile buffers");
+static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * kF32Stages * kF32Tile * kEncHd,
+              "P.V partial sums fit the stage buffers");
 
-// One CTA per unit (row group of <= 8 rows of one stream, head).
+// One CTA per unit (row group of <= 8 rows of one stream, head).  The unit's
+// keys stream through two 128-key stages (K stages, then V stages); thread 0
+// refills a stage as soon as every thread has finished with it.  Row bounds
+// and ring slots come from the group descriptor (rows of a group are
+// consecutive positions), with no division per key.  Measured and dropped:
+// five 64-key stages with two threads per key (slower: the kernel is bound
+// by the latency of its shared-memory loads and FMA chains, not by copies in
+// flight).
 __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     EncF32Smem & S = *reinterpret_cast<EncF32Smem *>(smem_raw);
@@ -880,8 +888,7 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
     const int lane = tid & 31;
     const int warp = tid >> 5;
     if (tid == 0) {
-        mbar_init(&S.full[0], 1);
-        mbar_init(&S.full[1], 1);
+        for (int st = 0; st < kF32Stages; ++st) mbar_init(&S.full[st], 1);
         S.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -891,27 +898,49 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
     const int u = blockIdx.x;
     const int grp = u / p.n_heads;
     const int h = u - grp * p.n_heads;
-    const int r0 = p.group_first[grp];
-    const int nr = p.group_first[grp + 1] - r0;
-    const EncRowDesc first = p.rows[r0];
-    const int ws = first.win_start;
-    const int we = p.rows[r0 + nr - 1].pos;
+    const int4 ga = __ldg(p.groups + 2 * grp), gb = __ldg(p.groups + 2 * grp + 1);
+    const int r0 = ga.x & 0xffffff;
+    const int nr = (int) ((unsigned) ga.x >> 24);
+    const int ws = ga.z;
+    const int we = ga.w;
     const int nkeys = we - ws + 1;
     if (nr < 1 || nr > kF32Rows || nkeys < 1 || nkeys > kF32MaxKeys) {
         if (tid == 0 && p.error) atomicCAS(p.error, 0, 1);
         return;
     }
-    const int T = (nkeys + kF32Tile - 1) / kF32Tile;
-    const int64_t ring = ring_index(p, first.stream, h);
+    const int cap = p.capacity;
+    int slot0 = gb.z - (nkeys - 1);  // ws % capacity: the window is shorter than the ring
+    slot0 = slot0 < 0 ? slot0 + cap : slot0;
+    const int T = (nkeys + kF32Tile - 1) / kF32Tile;  // stages of K, then as many of V
+    const int64_t ring = ring_index(p, ga.y, h);
+    const uint64_t policy = evict_first_policy();
+    // stage j < T: K keys [64 j, ...); stage j >= T: V keys [64 (j - T), ...)
+    auto issue = [&](int j) {
+        const int jj = j < T ? j : j - T;
+        const int k0 = jj * kF32Tile;
+        const int n = min(kF32Tile, nkeys - k0);
+        int slot = slot0 + k0;
+        slot = slot >= cap ? slot - cap : slot;
+        const int run = min(n, cap - slot);
+        const uint8_t * base = (j < T ? p.k_ring : p.v_ring) + ring * p.ring_slots * (int64_t) kF32RowBytes;
+        uint64_t * bar = &S.full[j % kF32Stages];
+        float * dst = S.kv[j % kF32Stages];
+        mbar_expect_tx(bar, (uint32_t) (n * kF32RowBytes));
+        bulk_load(dst, base + (int64_t) slot * kF32RowBytes, (uint32_t) (run * kF32RowBytes), bar, policy);
+        if (n > run) bulk_load(dst + run * kEncHd, base, (uint32_t) ((n - run) * kF32RowBytes), bar, policy);
+    };
+    int issued = 0;  // thread 0: stages issued so far
+    if (tid == 0)
+        for (; issued < kF32Stages && issued < 2 * T; ++issued) issue(issued);
     // queries: thread t -> row t / 16, dims 4 (t % 16) .. + 3
     {
         const int r = tid >> 4;
         const int c = tid & 15;
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (r < nr) {
-            const EncRowDesc rd = p.rows[r0 + r];
+            const int pos = we - (nr - 1) + r;
             const float * qr = p.q + ((int64_t) (r0 + r) * p.n_heads + h) * kEncHd + 4 * c;
-            const float2 * cs = p.rope + (int64_t) rd.pos * (kEncHd / 2) + 2 * c;
+            const float2 * cs = p.rope + (int64_t) pos * (kEncHd / 2) + 2 * c;
             const float2 a = enc_rope_pair(*reinterpret_cast<const float2 *>(qr), cs[0]);
             const float2 b = enc_rope_pair(*reinterpret_cast<const float2 *>(qr + 2), cs[1]);
             v = make_float4(a.x * p.scale_log2, a.y * p.scale_log2, b.x * p.scale_log2, b.y * p.scale_log2);
@@ -921,44 +950,37 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
         S.q[4 * c + 2][r] = v.z;
         S.q[4 * c + 3][r] = v.w;
     }
+    // row r attends [max(0, pos_r - window + 1), pos_r], pos_r = we - (nr - 1) + r
+    int lo[kF32Rows], hi[kF32Rows];
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r) {
+        hi[r] = r < nr ? we - (nr - 1) + r : -1;
+        lo[r] = max(0, hi[r] - (p.window - 1));
+    }
     __syncthreads();
-    // tile j < T: K keys [128 j, ...); tile j >= T: V keys [128 (j - T), ...)
-    auto issue = [&](int j) {
-        const int jj = j < T ? j : j - T;
-        const int k0 = jj * kF32Tile;
-        const int n = min(kF32Tile, nkeys - k0);
-        const int slot0 = (ws + k0) % p.capacity;
-        const int run = min(n, p.capacity - slot0);
-        const uint8_t * base = (j < T ? p.k_ring : p.v_ring) + ring * p.ring_slots * (int64_t) kF32RowBytes;
-        uint64_t * bar = &S.full[j & 1];
-        float * dst = S.kv[j & 1];
-        const uint64_t policy = evict_first_policy();
-        mbar_expect_tx(bar, (uint32_t) (n * kF32RowBytes));
-        bulk_load(dst, base + (int64_t) slot0 * kF32RowBytes, (uint32_t) (run * kF32RowBytes), bar, policy);
-        if (n > run) bulk_load(dst + run * kEncHd, base, (uint32_t) ((n - run) * kF32RowBytes), bar, policy);
-    };
-    if (tid == 0) issue(0);
     float acc[kF32Rows][4];
 #pragma unroll
     for (int r = 0; r < kF32Rows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
     const int c4 = tid & 15;     // P.V: dims 4 c4 .. + 3
-    const int kg = tid >> 4;     //       keys kg, kg + 8, ... of each tile
+    const int kg = tid >> 4;     //       keys kg, kg + 8, ... of each stage
     bool ok = true;
-    for (int j = 0; j < 2 * T; ++j) {
-        // the other buffer was released by the barrier that ended iteration j - 1
-        if (tid == 0 && j + 1 < 2 * T) issue(j + 1);
-        const bool landed = enc_wait(&S.full[j & 1], (uint32_t) ((j >> 1) & 1), &S.abort_flag, p.error);
+    int j = 0;
+    for (; j < 2 * T; ++j) {
+        // stage (j - 1) % S was released by the barrier that ended iteration j - 1
+        if (tid == 0 && j > 0 && j + kF32Stages - 1 < 2 * T) issue(issued++);
+        const bool landed = enc_wait(&S.full[j % kF32Stages], (uint32_t) ((j / kF32Stages) & 1), &S.abort_flag, p.error);
         if (!__syncthreads_and(landed ? 1 : 0)) {
             ok = false;
             break;
         }
-        const float * buf = S.kv[j & 1];
+        const float * buf = S.kv[j % kF32Stages];
         if (j < T) {
-            // ---- scores of key 128 j + tid for every row ----------------------
+            // ---- scores of key 128 j + tid for every row ------------------------
             const int ki = j * kF32Tile + tid;
             if (ki < nkeys) {
-                const int kp = ws + ki;
-                const int sw = (kp % p.capacity) & 7;
+                int slot = slot0 + ki;
+                slot = slot >= cap ? slot - cap : slot;
+                const int sw = slot & 7;
                 float sc[kF32Rows];
 #pragma unroll
                 for (int r = 0; r < kF32Rows; ++r) sc[r] = 0.0f;
@@ -970,12 +992,12 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
 #pragma unroll
                     for (int d = 0; d < 4; ++d) {
                         const float4 qa = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][0]);
-                        const float4 qb = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][4]);
                         sc[0] = fmaf(qa.x, kd[d], sc[0]);
                         sc[1] = fmaf(qa.y, kd[d], sc[1]);
                         sc[2] = fmaf(qa.z, kd[d], sc[2]);
                         sc[3] = fmaf(qa.w, kd[d], sc[3]);
                         if (nr > 4) {
+                            const float4 qb = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][4]);
                             sc[4] = fmaf(qb.x, kd[d], sc[4]);
                             sc[5] = fmaf(qb.y, kd[d], sc[5]);
                             sc[6] = fmaf(qb.z, kd[d], sc[6]);
@@ -983,25 +1005,24 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                         }
                     }
                 }
+                const int kp = ws + ki;
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r) {
-                    bool in = r < nr;
-                    if (in) {
-                        const EncRowDesc rd = p.rows[r0 + r];
-                        in = kp >= rd.win_start && kp <= rd.pos;
-                    }
-                    if (!in) sc[r] = -INFINITY;
-                }
+                for (int r = 0; r < kF32Rows; ++r)
+                    if (!(kp >= lo[r] && kp <= hi[r])) sc[r] = -INFINITY;
                 *reinterpret_cast<float4 *>(&S.s[ki][0]) = make_float4(sc[0], sc[1], sc[2], sc[3]);
                 *reinterpret_cast<float4 *>(&S.s[ki][4]) = make_float4(sc[4], sc[5], sc[6], sc[7]);
             }
         } else {
-            // ---- P.V over this tile's keys kg, kg + 8, ... --------------------
+            // ---- P.V over this stage's keys kg, kg + 8, ... --------------------
             const int k0 = (j - T) * kF32Tile;
             const int n = min(kF32Tile, nkeys - k0);
+            int slot = slot0 + k0 + kg;
+            slot = slot >= cap ? slot - cap : slot;
             for (int i = kg; i < n; i += kF32Threads / 16) {
                 const int ki = k0 + i;
-                const int sw = ((ws + ki) % p.capacity) & 7;
+                const int sw = slot & 7;
+                slot += kF32Threads / 16;
+                slot = slot >= cap ? slot - cap : slot;
                 const float4 v4 = *reinterpret_cast<const float4 *>(buf + i * kEncHd + 4 * (c4 ^ sw));
                 const float4 pa = *reinterpret_cast<const float4 *>(&S.s[ki][0]);
                 const float pr[4] = {pa.x, pa.y, pa.z, pa.w};
@@ -1079,11 +1100,9 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
         }
     }
     if (!ok) {
-        // let the copies in flight land before the CTA exits
-        if (tid == 0) {
-            enc_drain(&S.full[0], 0);
-            enc_drain(&S.full[1], 0);
-        }
+        // let the copies in flight (stages j .. issued - 1) land before the CTA exits
+        if (tid == 0)
+            for (int d = j; d < issued; ++d) enc_drain(&S.full[d % kF32Stages], (uint32_t) ((d / kF32Stages) & 1));
         return;
     }
     // ---- sum the key groups' partial products -----------------------------

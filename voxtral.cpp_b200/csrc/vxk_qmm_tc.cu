@@ -540,9 +540,27 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     dequant_q6_half(raw, r, h, tmem + 128 * b + lane_off);
                 } else {
                     const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
-                    const uint32_t scw[2] = {scm.x, scm.y};
                     const uint32_t mnw[2] = {scm.z, scm.w};
-                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word)
+                    // the 8 sub-block scales as f16 pairs (s, s) by splicing each byte under
+                    // the exponent of 1024 and subtracting 1024 (exact for s < 1024)
+                    __half2 scl[8], sch[8];
+                    {
+                        const uint32_t scw[2] = {scm.x, scm.y};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t bj = (scw[j >> 2] >> (8 * (j & 3))) & 0xffu;
+                            const uint32_t hb = bj | (bj << 16) | 0x64006400u;
+                            scl[j] = __hsub2(*reinterpret_cast<const __half2 *>(&hb), __half2half2(__ushort_as_half(0x6400)));
+                            // high nibbles come out as 1024 + 16 q: multiply by s / 16 (exact)
+                            sch[j] = __hmul2(scl[j], __half2half2(__ushort_as_half(0x2c00)));
+                        }
+                    }
+                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word).
+                    // Word v holds bytes (b0, b1, b2, b3): the low nibbles of b0, b2 and their
+                    // high nibbles, then the same of b1, b3 (v >> 8), each pair spliced under
+                    // the f16 exponent of 1024 (high nibbles at 16x, which the scale absorbs);
+                    // one fused multiply-add per pair removes the 1024 (or 1024 + 0) offset:
+                    // (1024 + q) s - 1024 s and (1024 + 16 q) s/16 - 64 s are q s exactly.
 #pragma unroll
                     for (int half = 0; half < 4; ++half) {
                         uint32_t cols[32];
@@ -551,18 +569,17 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                             const int c = 2 * half + cc;  // chunk: words 4c .. 4c+3, group c / 2
                             const uint4 v4 = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
                             const int g = c >> 1;
-                            const float sl = (float) ((scw[g >> 1] >> (8 * ((2 * g) & 3))) & 0xffu);
-                            const float sh = (float) ((scw[g >> 1] >> (8 * ((2 * g + 1) & 3))) & 0xffu);
-                            const __half2 slo = __float2half2_rn(sl), shi = __float2half2_rn(sh);
-                            const __half2 blo = __float2half2_rn(-1024.0f * sl), bhi = __float2half2_rn(-1024.0f * sh);
+                            const __half2 slo = scl[2 * g], shi = sch[2 * g + 1];
+                            const __half2 blo = __hmul2(scl[2 * g], __half2half2(__ushort_as_half(0xe400)));     // -1024 s
+                            const __half2 bhi = __hmul2(scl[2 * g + 1], __half2half2(__ushort_as_half(0xd400))); // -64 s
                             const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
-                                const uint32_t v = vw[k];
+                                const uint32_t v = vw[k], v8 = v >> 8;
                                 const uint32_t h0 = (v & 0x000F000Fu) | 0x64006400u;
-                                const uint32_t h1 = ((v >> 4) & 0x000F000Fu) | 0x64006400u;
-                                const uint32_t h2 = ((v >> 8) & 0x000F000Fu) | 0x64006400u;
-                                const uint32_t h3 = ((v >> 12) & 0x000F000Fu) | 0x64006400u;
+                                const uint32_t h1 = (v & 0x00F000F0u) | 0x64006400u;
+                                const uint32_t h2 = (v8 & 0x000F000Fu) | 0x64006400u;
+                                const uint32_t h3 = (v8 & 0x00F000F0u) | 0x64006400u;
                                 cols[16 * cc + 4 * k + 0] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h0), slo, blo));
                                 cols[16 * cc + 4 * k + 1] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h1), shi, bhi));
                                 cols[16 * cc + 4 * k + 2] = h2_bits(__hfma2(*reinterpret_cast<const __half2 *>(&h2), slo, blo));
@@ -744,20 +761,25 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         break;
                     }
                     tc_fence_after();
+                    // descriptors: the stage's base descriptor plus constant offsets (the
+                    // address field counts 16-byte units), so the issuing thread spends
+                    // one add per MMA
+                    const uint64_t bdesc0 = sw128_desc(bt, 16, 1024);
+                    const uint32_t a0 = tmem + 128 * b;
                     if (q6) {
                         // half h: K positions 128h .. 128h+127, A_hi then A_lo per step
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
                             const int ks = 8 * h + kk;
-                            const uint64_t bdesc = sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024);
-                            mma_ts(dacc, tmem + 128 * b + 8 * kk, bdesc, idesc, (h | kk) != 0);
-                            mma_ts(dacc, tmem + 128 * b + 64 + 8 * kk, bdesc, idesc, 1);
+                            const uint64_t bdesc = bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4);
+                            mma_ts(dacc, a0 + 8 * kk, bdesc, idesc, (h | kk) != 0);
+                            mma_ts(dacc, a0 + 64 + 8 * kk, bdesc, idesc, 1);
                         }
                     } else {
 #pragma unroll
                         for (int ks = 0; ks < 16; ++ks)
-                            mma_ts(dacc, tmem + 128 * b + 8 * ks,
-                                   sw128_desc(bt + (ks >> 2) * N * 128 + (ks & 3) * 32, 16, 1024), idesc, ks != 0);
+                            mma_ts(dacc, a0 + 8 * ks, bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4),
+                                   idesc, ks != 0);
                         mma_ss(tmem + 384 + 64 * bd, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
                                plain_desc(bt + kActB, 128, 256), idesc, 0);
                     }

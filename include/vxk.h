@@ -411,6 +411,10 @@ VXK_API vxk_status vxk_enc_batch_commit(vxk_enc_pool * pool);
  * window [max(0, q - window + 1), q] (src/voxtral.cpp:2459-2487 with the
  * mask of src/voxtral.cpp:4104-4119), scale 1/sqrt(head_dim), MHA.
  *   q, out [rows][n_heads][head_dim] fp32; k, v [rows][n_heads][head_dim].
+ * When every stream of the batch has at most 8 new rows (the steady chunk) and
+ * the ring is 16-bit, this is one kernel launch (the store is fused into the
+ * attention); otherwise two (store, then attention).  Either way q/k/v must be
+ * complete on cuda_stream before the call's work starts.
  */
 VXK_API vxk_status vxk_enc_layer(vxk_enc_pool * pool, int32_t layer, const float * q,
                                  const float * k, const float * v, float * out,

@@ -535,11 +535,16 @@ vxk_status vxk_encoder_sync(vxk_encoder * e, void * cuda_stream, int32_t timeout
             if (q == cudaSuccess) break;
             if (q != cudaErrorNotReady) break;
             q = cudaSuccess;
-            if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+            const auto waited = std::chrono::steady_clock::now() - t0;
+            if (waited > std::chrono::milliseconds(timeout_ms)) {
                 cudaEventDestroy(ev);
                 efail2(VXK_STATUS_TIMEOUT, "stream did not drain within the timeout");
             }
-            std::this_thread::sleep_for(std::chrono::microseconds(50));
+            // poll short waits (a step of a few ms); sleep between polls after 20 ms
+            if (waited < std::chrono::milliseconds(20))
+                std::this_thread::yield();
+            else
+                std::this_thread::sleep_for(std::chrono::microseconds(50));
         }
         cudaEventDestroy(ev);
         if (q != cudaSuccess) efail2(VXK_STATUS_BACKEND_ERROR, cudaGetErrorString(q));

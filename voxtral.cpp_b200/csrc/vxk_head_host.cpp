@@ -266,7 +266,11 @@ vxk_status vxk_head_sync(vxk_head * head, void * cuda_stream, int32_t timeout_ms
             const auto ms =
                 std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
             if (ms > timeout_ms) hfail(VXK_STATUS_TIMEOUT, "stream did not drain within the timeout");
-            std::this_thread::sleep_for(std::chrono::microseconds(50));
+            // poll short waits (a step of a few ms); sleep between polls after 20 ms
+            if (ms < 20)
+                std::this_thread::yield();
+            else
+                std::this_thread::sleep_for(std::chrono::microseconds(50));
         }
         int32_t err = 0;
         VXK_HCUDA(cudaMemcpy(&err, head->d_error, sizeof(err), cudaMemcpyDeviceToHost));

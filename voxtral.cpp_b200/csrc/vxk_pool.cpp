@@ -588,7 +588,13 @@ vxk_status bounded_wait(cudaEvent_t ev, int32_t timeout_ms) {
         const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
             std::chrono::steady_clock::now() - t0).count();
         if (ms > timeout_ms) return VXK_STATUS_TIMEOUT;
-        if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(50));
+        // a step of a few milliseconds is waited for by polling (a 50 us sleep
+        // per poll cost up to ~0.1 ms of idle GPU per step); longer waits sleep
+        if (ms < 20) {
+            std::this_thread::yield();
+        } else if (++spins > 64) {
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
     }
 }
 
@@ -1070,7 +1076,9 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
         for (int32_t l = 0; l < c.n_layers; ++l) {
             VXK_CUDA(cudaStreamWaitEvent(cs, pool->ev_in[(size_t) l], 0));
             ++pool->launches;
-            VXK_CUDA(vxk::launch_decode(decode_params(pool, l, dq(l), dk(l), dv(l), dout(l), 1), cs, false));
+            // layers after the first overlap their prologue (page copies of their own
+            // layer) with the previous layer's tail, as in vxk_decode_layer
+            VXK_CUDA(vxk::launch_decode(decode_params(pool, l, dq(l), dk(l), dv(l), dout(l), 1), cs, l > 0));
             VXK_CUDA(cudaEventRecord(pool->ev_out[(size_t) l], cs));
             VXK_CUDA(cudaStreamWaitEvent(pool->d2h, pool->ev_out[(size_t) l], 0));
             VXK_CUDA(cudaMemcpyAsync(h_out + (size_t) l * rows * q_per_row, dout(l), rows * q_per_row * sizeof(float),

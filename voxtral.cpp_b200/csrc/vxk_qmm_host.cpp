@@ -670,7 +670,11 @@ vxk_status vxk_qweight_sync(vxk_qweight * w, void * cuda_stream, int32_t timeout
             const auto ms =
                 std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
             if (ms > timeout_ms) qfail(VXK_STATUS_TIMEOUT, "stream did not drain within the timeout");
-            std::this_thread::sleep_for(std::chrono::microseconds(50));
+            // poll short waits (a step of a few ms); sleep between polls after 20 ms
+            if (ms < 20)
+                std::this_thread::yield();
+            else
+                std::this_thread::sleep_for(std::chrono::microseconds(50));
         }
         int32_t err = 0;
         VXK_QCUDA(cudaMemcpy(&err, w->d_error, sizeof(err), cudaMemcpyDeviceToHost));

@@ -856,22 +856,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) enc_tc_kernel(const EncParams p
 // ---------------------------------------------------------------------------
 constexpr int kF32Threads = 128;
 constexpr int kF32Tile = 128;                  // keys per stage
-constexpr int kF32Stages = 2;                  // a stage in flight while the other is used
 constexpr int kF32MaxKeys = 768;               // window - 1 + 8 rows fits (host checks <= 752)
 constexpr int kF32Rows = 8;                    // rows per group (kEncRowsPerGroup)
+// Kernel variants: R = rows per group the scores are kept for (8, or 4 for the
+// steady chunk, whose smaller score buffer leaves room for a third stage at two
+// CTAs per SM), NS = 128-key stages in flight.
 constexpr int kF32RowBytes = kEncHd * 4;       // 256
 
+template <int R, int NS>
 struct __align__(128) EncF32Smem {
-    float kv[kF32Stages][kF32Tile * kEncHd];   // 128-key stages (rows swizzled as in the ring)
-    float s[kF32MaxKeys][kF32Rows];            // scores, then probabilities: [key][row]
-    float q[kEncHd][kF32Rows];                 // rotated, scaled queries: [dim][row]
-    float red[kF32Threads / 32][kF32Rows];
-    float inv_l[kF32Rows];
-    uint64_t full[kF32Stages];
+    float kv[NS][kF32Tile * kEncHd];           // 128-key stages (rows swizzled as in the ring)
+    float s[kF32MaxKeys][R];                   // scores, then probabilities: [key][row]
+    float q[kEncHd][R];                        // rotated, scaled queries: [dim][row]
+    float red[kF32Threads / 32][R];
+    float inv_l[R];
+    uint64_t full[NS];
     int32_t abort_flag;
 };
-static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * kF32Stages * kF32Tile * kEncHd,
-              "P.V partial sums fit the stage buffers");
+static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * kF32Tile * kEncHd,
+              "P.V partial sums fit one stage buffer");
 
 // One CTA per unit (row group of <= 8 rows of one stream, head).  The unit's
 // keys stream through two 128-key stages (K stages, then V stages); thread 0
@@ -881,14 +884,15 @@ static_assert(sizeof(float) * kF32Rows * 8 * kEncHd <= sizeof(float) * kF32Stage
 // five 64-key stages with two threads per key (slower: the kernel is bound
 // by the latency of its shared-memory loads and FMA chains, not by copies in
 // flight).
+template <int R, int NS>
 __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    EncF32Smem & S = *reinterpret_cast<EncF32Smem *>(smem_raw);
+    EncF32Smem<R, NS> & S = *reinterpret_cast<EncF32Smem<R, NS> *>(smem_raw);
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
     if (tid == 0) {
-        for (int st = 0; st < kF32Stages; ++st) mbar_init(&S.full[st], 1);
+        for (int st = 0; st < NS; ++st) mbar_init(&S.full[st], 1);
         S.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -904,7 +908,7 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
     const int ws = ga.z;
     const int we = ga.w;
     const int nkeys = we - ws + 1;
-    if (nr < 1 || nr > kF32Rows || nkeys < 1 || nkeys > kF32MaxKeys) {
+    if (nr < 1 || nr > R || nkeys < 1 || nkeys > kF32MaxKeys) {
         if (tid == 0 && p.error) atomicCAS(p.error, 0, 1);
         return;
     }
@@ -923,15 +927,15 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
         slot = slot >= cap ? slot - cap : slot;
         const int run = min(n, cap - slot);
         const uint8_t * base = (j < T ? p.k_ring : p.v_ring) + ring * p.ring_slots * (int64_t) kF32RowBytes;
-        uint64_t * bar = &S.full[j % kF32Stages];
-        float * dst = S.kv[j % kF32Stages];
+        uint64_t * bar = &S.full[j % NS];
+        float * dst = S.kv[j % NS];
         mbar_expect_tx(bar, (uint32_t) (n * kF32RowBytes));
         bulk_load(dst, base + (int64_t) slot * kF32RowBytes, (uint32_t) (run * kF32RowBytes), bar, policy);
         if (n > run) bulk_load(dst + run * kEncHd, base, (uint32_t) ((n - run) * kF32RowBytes), bar, policy);
     };
     int issued = 0;  // thread 0: stages issued so far
     if (tid == 0)
-        for (; issued < kF32Stages && issued < 2 * T; ++issued) issue(issued);
+        for (; issued < NS && issued < 2 * T; ++issued) issue(issued);
     // queries: thread t -> row t / 16, dims 4 (t % 16) .. + 3
     {
         const int r = tid >> 4;
@@ -945,35 +949,37 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
             const float2 b = enc_rope_pair(*reinterpret_cast<const float2 *>(qr + 2), cs[1]);
             v = make_float4(a.x * p.scale_log2, a.y * p.scale_log2, b.x * p.scale_log2, b.y * p.scale_log2);
         }
-        S.q[4 * c + 0][r] = v.x;
-        S.q[4 * c + 1][r] = v.y;
-        S.q[4 * c + 2][r] = v.z;
-        S.q[4 * c + 3][r] = v.w;
+        if (r < R) {
+            S.q[4 * c + 0][r] = v.x;
+            S.q[4 * c + 1][r] = v.y;
+            S.q[4 * c + 2][r] = v.z;
+            S.q[4 * c + 3][r] = v.w;
+        }
     }
     // row r attends [max(0, pos_r - window + 1), pos_r], pos_r = we - (nr - 1) + r
-    int lo[kF32Rows], hi[kF32Rows];
+    int lo[R], hi[R];
 #pragma unroll
-    for (int r = 0; r < kF32Rows; ++r) {
+    for (int r = 0; r < R; ++r) {
         hi[r] = r < nr ? we - (nr - 1) + r : -1;
         lo[r] = max(0, hi[r] - (p.window - 1));
     }
     __syncthreads();
-    float acc[kF32Rows][4];
+    float acc[R][4];
 #pragma unroll
-    for (int r = 0; r < kF32Rows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
+    for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
     const int c4 = tid & 15;     // P.V: dims 4 c4 .. + 3
     const int kg = tid >> 4;     //       keys kg, kg + 8, ... of each stage
     bool ok = true;
     int j = 0;
     for (; j < 2 * T; ++j) {
         // stage (j - 1) % S was released by the barrier that ended iteration j - 1
-        if (tid == 0 && j > 0 && j + kF32Stages - 1 < 2 * T) issue(issued++);
-        const bool landed = enc_wait(&S.full[j % kF32Stages], (uint32_t) ((j / kF32Stages) & 1), &S.abort_flag, p.error);
+        if (tid == 0 && j > 0 && j + NS - 1 < 2 * T) issue(issued++);
+        const bool landed = enc_wait(&S.full[j % NS], (uint32_t) ((j / NS) & 1), &S.abort_flag, p.error);
         if (!__syncthreads_and(landed ? 1 : 0)) {
             ok = false;
             break;
         }
-        const float * buf = S.kv[j % kF32Stages];
+        const float * buf = S.kv[j % NS];
         if (j < T) {
             // ---- scores of key 128 j + tid for every row ------------------------
             const int ki = j * kF32Tile + tid;
@@ -981,9 +987,9 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                 int slot = slot0 + ki;
                 slot = slot >= cap ? slot - cap : slot;
                 const int sw = slot & 7;
-                float sc[kF32Rows];
+                float sc[R];
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r) sc[r] = 0.0f;
+                for (int r = 0; r < R; ++r) sc[r] = 0.0f;
                 const float * kr = buf + tid * kEncHd;
 #pragma unroll 4
                 for (int c = 0; c < kEncHd / 4; ++c) {
@@ -996,7 +1002,7 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                         sc[1] = fmaf(qa.y, kd[d], sc[1]);
                         sc[2] = fmaf(qa.z, kd[d], sc[2]);
                         sc[3] = fmaf(qa.w, kd[d], sc[3]);
-                        if (nr > 4) {
+                        if constexpr (R > 4) if (nr > 4) {
                             const float4 qb = *reinterpret_cast<const float4 *>(&S.q[4 * c + d][4]);
                             sc[4] = fmaf(qb.x, kd[d], sc[4]);
                             sc[5] = fmaf(qb.y, kd[d], sc[5]);
@@ -1007,10 +1013,11 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                 }
                 const int kp = ws + ki;
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r)
+                for (int r = 0; r < R; ++r)
                     if (!(kp >= lo[r] && kp <= hi[r])) sc[r] = -INFINITY;
                 *reinterpret_cast<float4 *>(&S.s[ki][0]) = make_float4(sc[0], sc[1], sc[2], sc[3]);
-                *reinterpret_cast<float4 *>(&S.s[ki][4]) = make_float4(sc[4], sc[5], sc[6], sc[7]);
+                if constexpr (R > 4)
+                    *reinterpret_cast<float4 *>(&S.s[ki][4]) = make_float4(sc[4], sc[5], sc[6], sc[7]);
             }
         } else {
             // ---- P.V over this stage's keys kg, kg + 8, ... --------------------
@@ -1033,7 +1040,7 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                     acc[r][2] = fmaf(pr[r], v4.z, acc[r][2]);
                     acc[r][3] = fmaf(pr[r], v4.w, acc[r][3]);
                 }
-                if (nr > 4) {
+                if constexpr (R > 4) if (nr > 4) {
                     const float4 pb = *reinterpret_cast<const float4 *>(&S.s[ki][4]);
                     const float pq[4] = {pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
@@ -1049,33 +1056,33 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
         __syncthreads();
         if (j == T - 1) {
             // ---- exact softmax over the window, per row ------------------------
-            float mx[kF32Rows];
+            float mx[R];
 #pragma unroll
-            for (int r = 0; r < kF32Rows; ++r) mx[r] = -INFINITY;
+            for (int r = 0; r < R; ++r) mx[r] = -INFINITY;
             for (int ki = tid; ki < nkeys; ki += kF32Threads) {
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r) mx[r] = fmaxf(mx[r], S.s[ki][r]);
+                for (int r = 0; r < R; ++r) mx[r] = fmaxf(mx[r], S.s[ki][r]);
             }
 #pragma unroll
-            for (int r = 0; r < kF32Rows; ++r) {
+            for (int r = 0; r < R; ++r) {
 #pragma unroll
                 for (int o = 16; o >= 1; o >>= 1) mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], o));
             }
             if (lane == 0) {
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r) S.red[warp][r] = mx[r];
+                for (int r = 0; r < R; ++r) S.red[warp][r] = mx[r];
             }
             __syncthreads();
-            float M[kF32Rows], ls[kF32Rows];
+            float M[R], ls[R];
 #pragma unroll
-            for (int r = 0; r < kF32Rows; ++r) {
+            for (int r = 0; r < R; ++r) {
                 M[r] = fmaxf(fmaxf(S.red[0][r], S.red[1][r]), fmaxf(S.red[2][r], S.red[3][r]));
                 ls[r] = 0.0f;
             }
             __syncthreads();
             for (int ki = tid; ki < nkeys; ki += kF32Threads) {
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r) {
+                for (int r = 0; r < R; ++r) {
                     // every real row holds its own position: M[r] is finite
                     const float e = r < nr ? exp2f(S.s[ki][r] - M[r]) : 0.0f;
                     S.s[ki][r] = e;
@@ -1083,16 +1090,16 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
                 }
             }
 #pragma unroll
-            for (int r = 0; r < kF32Rows; ++r) {
+            for (int r = 0; r < R; ++r) {
 #pragma unroll
                 for (int o = 16; o >= 1; o >>= 1) ls[r] += __shfl_xor_sync(kFull, ls[r], o);
             }
             if (lane == 0) {
 #pragma unroll
-                for (int r = 0; r < kF32Rows; ++r) S.red[warp][r] = ls[r];
+                for (int r = 0; r < R; ++r) S.red[warp][r] = ls[r];
             }
             __syncthreads();
-            if (tid < kF32Rows) {
+            if (tid < R) {
                 const float l = (S.red[0][tid] + S.red[1][tid]) + (S.red[2][tid] + S.red[3][tid]);
                 S.inv_l[tid] = l > 0.0f ? 1.0f / l : 0.0f;
             }
@@ -1102,14 +1109,14 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
     if (!ok) {
         // let the copies in flight (stages j .. issued - 1) land before the CTA exits
         if (tid == 0)
-            for (int d = j; d < issued; ++d) enc_drain(&S.full[d % kF32Stages], (uint32_t) ((d / kF32Stages) & 1));
+            for (int d = j; d < issued; ++d) enc_drain(&S.full[d % NS], (uint32_t) ((d / NS) & 1));
         return;
     }
     // ---- sum the key groups' partial products -----------------------------
     float * part = S.kv[0];  // [kg][row][dim]
 #pragma unroll
-    for (int r = 0; r < kF32Rows; ++r)
-        *reinterpret_cast<float4 *>(part + (kg * kF32Rows + r) * kEncHd + 4 * c4) =
+    for (int r = 0; r < R; ++r)
+        *reinterpret_cast<float4 *>(part + (kg * R + r) * kEncHd + 4 * c4) =
             make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
     __syncthreads();
     {
@@ -1118,7 +1125,7 @@ __global__ void __launch_bounds__(kF32Threads) enc_f32_kernel(const EncParams p)
             float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
             for (int g = 0; g < kF32Threads / 16; ++g) {
-                const float4 x = *reinterpret_cast<const float4 *>(part + (g * kF32Rows + r) * kEncHd + 4 * c4);
+                const float4 x = *reinterpret_cast<const float4 *>(part + (g * R + r) * kEncHd + 4 * c4);
                 o.x += x.x;
                 o.y += x.y;
                 o.z += x.z;
@@ -1171,10 +1178,16 @@ cudaError_t launch_enc_attention(const EncParams & p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     const int units = p.n_groups * p.n_heads;
     if (p.dtype == 0) {
-        const int smem = (int) sizeof(EncF32Smem);
-        e = cudaFuncSetAttribute(enc_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (p.max_group_rows <= 4) {
+            const int smem = (int) sizeof(EncF32Smem<4, 3>);
+            e = cudaFuncSetAttribute(enc_f32_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            return launch_pdl(enc_f32_kernel<4, 3>, (unsigned) units, kF32Threads, (size_t) smem, stream, p);
+        }
+        const int smem = (int) sizeof(EncF32Smem<8, 2>);
+        e = cudaFuncSetAttribute(enc_f32_kernel<8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        return launch_pdl(enc_f32_kernel, (unsigned) units, kF32Threads, (size_t) smem, stream, p);
+        return launch_pdl(enc_f32_kernel<8, 2>, (unsigned) units, kF32Threads, (size_t) smem, stream, p);
     }
     // persistent: one CTA per SM (the shared-memory ring allows no second)
     const unsigned grid = (unsigned) (units < sms ? units : sms);

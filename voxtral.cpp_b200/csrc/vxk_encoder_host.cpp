@@ -83,6 +83,7 @@ struct vxk_enc_pool {
     std::vector<int32_t> group_first;
     std::vector<int32_t> gdesc;  // 8 ints per group (vxk::EncParams::groups)
     bool one_group_per_stream = false;  // every stream of the batch has <= kEncRowsPerGroup new rows
+    int32_t max_group_rows = 0;         // most rows in one group of the batch
     std::vector<uint8_t> h_read;  // readback staging of vxk_enc_read_slots
     std::string last_error;
 };
@@ -159,6 +160,7 @@ vxk::EncParams enc_params(vxk_enc_pool * p, int32_t layer, const float * q, cons
     e.scale_log2 = (1.0f / sqrtf((float) p->cfg.head_dim)) * 1.4426950408889634f;
     e.error = p->d_error;
     e.dtype = (int32_t) p->cfg.dtype;
+    e.max_group_rows = p->max_group_rows;
     return e;
 }
 
@@ -381,6 +383,9 @@ vxk_status vxk_enc_batch_plan(vxk_enc_pool * pool, const int32_t * stream_ids, c
         pool->one_group_per_stream = true;
         for (int32_t i = 0; i < n_streams; ++i)
             if (n_new[i] > kEncRowsPerGroup) pool->one_group_per_stream = false;
+        pool->max_group_rows = 0;
+        for (size_t g = 0; g + 1 < pool->group_first.size(); ++g)
+            pool->max_group_rows = std::max(pool->max_group_rows, pool->group_first[g + 1] - pool->group_first[g]);
         EncDevice scope(c.device);
         cudaStream_t cs = static_cast<cudaStream_t>(cuda_stream);
         VXK_ECUDA(cudaEventSynchronize(pool->stage_ev));

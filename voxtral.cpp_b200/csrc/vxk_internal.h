@@ -212,6 +212,7 @@ struct EncParams {
     // kernel then stores its own group's new K/V rows before loading the
     // window, and launch_enc_attention needs no launch_enc_append before it
     int32_t fuse_append;
+    int32_t max_group_rows;  // most rows in one group of the batch (<= 8)
 };
 
 cudaError_t launch_enc_append(const EncParams & p, cudaStream_t stream);

@@ -336,16 +336,21 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     const int chunk = rg / p.npad, r = rg - chunk * p.npad;  // row r of 64-row chunk `chunk`
     const int64_t K = (int64_t) p.n_units * kQmmUnit;
     const int64_t cu = (int64_t) chunk * p.n_units + u;      // this chunk's unit
+    // Lane L produces K positions 8L .. 8L + 7 of the unit's tile (one 16-byte
+    // chunk): the elements 64g + l .. l + 3 and 64g + 32 + l .. + 3 (g = L / 8,
+    // l = 4 (L % 8)) in the position order of tc_position, so it loads two
+    // aligned float4 and stores the chunk at once.  x[0..3] = A, x[4..7] = B.
+    const int g = lane >> 3, l = 4 * (lane & 7);
+    const int eA = 64 * g + l, eB = eA + 32;  // element (column) indices of the two quads
     float x[8];
     if (rg < p.rows) {
-        const float4 * src = reinterpret_cast<const float4 *>(p.x + (int64_t) rg * K + (int64_t) u * kQmmUnit) + 2 * lane;
-        const float4 a = src[0], b = src[1];
+        const float * row = p.x + (int64_t) rg * K + (int64_t) u * kQmmUnit;
+        const float4 a = *reinterpret_cast<const float4 *>(row + eA), b = *reinterpret_cast<const float4 *>(row + eB);
         x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
         x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
         if (p.x_up) {
-            const float4 * up =
-                reinterpret_cast<const float4 *>(p.x_up + (int64_t) rg * K + (int64_t) u * kQmmUnit) + 2 * lane;
-            const float4 c = up[0], e = up[1];
+            const float * up = p.x_up + (int64_t) rg * K + (int64_t) u * kQmmUnit;
+            const float4 c = *reinterpret_cast<const float4 *>(up + eA), e = *reinterpret_cast<const float4 *>(up + eB);
             const float uv[8] = {c.x, c.y, c.z, c.w, e.x, e.y, e.z, e.w};
 #pragma unroll
             for (int i = 0; i < 8; ++i) x[i] = swiglu_value(x[i], uv[i]);
@@ -359,8 +364,8 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     unsigned long long key = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const unsigned long long kx =
-            ((unsigned long long) __float_as_uint(fabsf(x[i])) << 32) | (unsigned) (255 - (8 * lane + i));
+        const int col = (i < 4 ? eA : eB) + (i & 3);
+        const unsigned long long kx = ((unsigned long long) __float_as_uint(fabsf(x[i])) << 32) | (unsigned) (255 - col);
         key = kx > key ? kx : key;
     }
 #pragma unroll
@@ -369,11 +374,14 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
         key = other > key ? other : key;
     }
     const int arg = 255 - (int) (key & 0xffffffffu);
+    // the lane holding column arg, and which of its eight values it is
+    const int a_within = arg & 63, a_hi = a_within >= 32 ? 1 : 0, a_l = a_within & 31;
+    const int a_lane = 8 * (arg >> 6) + (a_l >> 2), a_idx = 4 * a_hi + (a_l & 3);
     float mine = x[0];
 #pragma unroll
     for (int i = 1; i < 8; ++i)
-        if ((arg & 7) == i) mine = x[i];
-    const float s_max = __shfl_sync(kFull, mine, arg >> 3);
+        if (a_idx == i) mine = x[i];
+    const float s_max = __shfl_sync(kFull, mine, a_lane);
     const float amax = __uint_as_float((unsigned) (key >> 32));
     int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float d = 0.0f;
@@ -385,21 +393,28 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     }
     const int np = p.npad;
     uint8_t * tile = p.b_tiles + cu * np * 512;
-    int sum = 0;
+    // positions 8L + s hold elements A0, A2, B0, B2, A1, A3, B1, B3 (tc_position)
+    auto h2 = [](int lo, int hi) {
+        const __half2 v = __halves2half2(__int2half_rn(lo), __int2half_rn(hi));
+        return *reinterpret_cast<const uint32_t *>(&v);
+    };
+    *reinterpret_cast<uint4 *>(tile + tc_tile_off(r, 8 * lane, np)) =
+        make_uint4(h2(q[0], q[2]), h2(q[4], q[6]), h2(q[1], q[3]), h2(q[5], q[7]));
+    // sums of sub-blocks 2g (the A quads) and 2g + 1 (the B quads) over the group's 8 lanes
+    int sa = q[0] + q[1] + q[2] + q[3], sb = q[4] + q[5] + q[6] + q[7];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        *reinterpret_cast<__half *>(tile + tc_tile_off(r, tc_position(8 * lane + i), np)) = __int2half_rn(q[i]);
-        sum += q[i];
+    for (int o = 1; o < 8; o <<= 1) {
+        sa += __shfl_xor_sync(kFull, sa, o);
+        sb += __shfl_xor_sync(kFull, sb, o);
     }
-    sum += __shfl_xor_sync(kFull, sum, 1);
-    sum += __shfl_xor_sync(kFull, sum, 2);
-    if ((lane & 3) == 0) {
+    if ((lane & 7) == 0) {
         // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j); unswizzled
         // K-major core matrices: row group r / 8 at 256 B, K half at 128 B, row r % 8 at 16 B
-        const int j = lane >> 2;
         uint8_t * mrow = p.bmin_tiles + cu * np * 32 + (r >> 3) * 256 + (r & 7) * 16;
-        *reinterpret_cast<__half *>(mrow + j * 2) = __int2half_rn(sum & 127);
-        *reinterpret_cast<__half *>(mrow + 128 + j * 2) = __int2half_rn(sum >> 7);
+        *reinterpret_cast<__half *>(mrow + (2 * g) * 2) = __int2half_rn(sa & 127);
+        *reinterpret_cast<__half *>(mrow + 128 + (2 * g) * 2) = __int2half_rn(sa >> 7);
+        *reinterpret_cast<__half *>(mrow + (2 * g + 1) * 2) = __int2half_rn(sb & 127);
+        *reinterpret_cast<__half *>(mrow + 128 + (2 * g + 1) * 2) = __int2half_rn(sb >> 7);
     }
     if (lane == 0) p.dx[cu * np + r] = d;
 }

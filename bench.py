@@ -1107,7 +1107,7 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
     if dist:
         dist.barrier()
     if rank == 0:
-        per_layer = 12
+        per_layer = 11
         line = {
             "metric": "whole decoder step tokens/s (Q4_K_M, 26 layers + head)",
             "value": round(world * S * args.steps / (ms / 1000.0), 1),
@@ -1130,8 +1130,9 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
                          "avg_step_us": round(step_s * 1e6, 1), "kernel": "whole step (all kernels)"},
             "cpu_baseline": cpu, "e2e": e2e,
             # embed + per layer (q/k/v quantize + product, attention, o quantize + product, norm, w1/w3
-            # quantize + product, swiglu, w2 quantize + product, norm) + head (quantize, product, argmax)
-            "gpu_launches": int(args.steps * (1 + per_layer * L + 3)),
+            # quantize + product, w2 quantize (SwiGLU inside) + product, norm) + head (quantize, product,
+            # argmax, token ids)
+            "gpu_launches": int(args.steps * (1 + per_layer * L + 4)),
             "launch": "eager C-ABI calls per step: vxk_batch_plan, vxk_decoder_forward, vxk_batch_commit",
             "clocks": clocks.summary(),
         }

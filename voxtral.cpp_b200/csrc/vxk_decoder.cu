@@ -7,6 +7,8 @@
 //                      of the GGUF type, ggml_add), xn = rms_norm(x) * attn_norm
 //   add_norm_kernel    x += proj (ggml_add), out = rms_norm(x) * w, optional
 //                      out + out * ada (the time conditioning, 2862-2874)
+//   add_norm_quant_kernel  the same, with the output rows quantized straight
+//                      into the next tcgen05 product's activation tiles
 //   gelu_erf_kernel    the adapter's and time MLP's ggml_gelu_erf
 //   adapter gather / audio scatter: 4 encoder frames per group, audio ring rows
 //
@@ -15,6 +17,7 @@
 // y = x * scale, then * w; every product and sum is rounded separately.
 #include "vxk_dequant.h"
 #include "vxk_internal.h"
+#include "vxk_qtc_quant.h"
 
 namespace vxk {
 namespace {
@@ -149,6 +152,93 @@ __global__ void __launch_bounds__(kNormThreads) add_norm_kernel(NormParams p) {
     }
 }
 
+// add_norm_kernel's arithmetic with the output quantized for the tcgen05
+// product that takes it (vxk_qtc_quant.h) instead of stored: one CTA per row
+// (padded to the product's rows; padding rows get zero tiles), one warp per
+// 256-column unit, lane L holding the columns of the unit's K positions 8L ..
+// 8L + 7, so the row never leaves registers between the norm and the tiles.
+// The squares are summed in fp64 per lane, over the warp and then over the
+// warps in a fixed order.
+__global__ void __launch_bounds__(1024) add_norm_quant_kernel(NormParams p) {
+    __shared__ double red[32];
+    pdl_enter();
+    const int r = blockIdx.x, u = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int c0 = 256 * u + qtc_lane_col_a(lane), c1 = c0 + 32;
+    float y[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const bool live = r < p.n_rows;
+    float4 v[2];
+    double sum = 0.0;
+    if (live) {
+        float * xr = p.x + (int64_t) r * p.dim;
+        v[0] = *reinterpret_cast<const float4 *>(xr + c0);
+        v[1] = *reinterpret_cast<const float4 *>(xr + c1);
+        if (p.add) {
+            const float * ar = p.add + (int64_t) r * p.dim;
+            float4 a[2] = {*reinterpret_cast<const float4 *>(ar + c0), *reinterpret_cast<const float4 *>(ar + c1)};
+            if (p.add_bias) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float4 bb = *reinterpret_cast<const float4 *>(p.add_bias + (h ? c1 : c0));
+                    a[h].x = __fadd_rn(a[h].x, bb.x);
+                    a[h].y = __fadd_rn(a[h].y, bb.y);
+                    a[h].z = __fadd_rn(a[h].z, bb.z);
+                    a[h].w = __fadd_rn(a[h].w, bb.w);
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                v[h].x = __fadd_rn(v[h].x, a[h].x);
+                v[h].y = __fadd_rn(v[h].y, a[h].y);
+                v[h].z = __fadd_rn(v[h].z, a[h].z);
+                v[h].w = __fadd_rn(v[h].w, a[h].w);
+            }
+            *reinterpret_cast<float4 *>(xr + c0) = v[0];
+            *reinterpret_cast<float4 *>(xr + c1) = v[1];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            sum += (double) __fmul_rn(v[h].x, v[h].x);
+            sum += (double) __fmul_rn(v[h].y, v[h].y);
+            sum += (double) __fmul_rn(v[h].z, v[h].z);
+            sum += (double) __fmul_rn(v[h].w, v[h].w);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[u] = sum;
+    __syncthreads();
+    double t = 0.0;
+    for (int w = 0; w < nw; ++w) t += red[w];
+    if (live) {
+        const float scale = rms_scale(t, p.dim, p.eps);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int c = h ? c1 : c0;
+            const float4 wv = *reinterpret_cast<const float4 *>(p.w + c);
+            float4 o;
+            o.x = __fmul_rn(__fmul_rn(v[h].x, scale), wv.x);
+            o.y = __fmul_rn(__fmul_rn(v[h].y, scale), wv.y);
+            o.z = __fmul_rn(__fmul_rn(v[h].z, scale), wv.z);
+            o.w = __fmul_rn(__fmul_rn(v[h].w, scale), wv.w);
+            if (p.ada) {
+                const float4 av = *reinterpret_cast<const float4 *>(p.ada + c);
+                o.x = __fadd_rn(o.x, __fmul_rn(o.x, av.x));
+                o.y = __fadd_rn(o.y, __fmul_rn(o.y, av.y));
+                o.z = __fadd_rn(o.z, __fmul_rn(o.z, av.z));
+                o.w = __fadd_rn(o.w, __fmul_rn(o.w, av.w));
+            }
+            if (p.out) *reinterpret_cast<float4 *>(p.out + (int64_t) r * p.dim + c) = o;
+            y[4 * h + 0] = o.x;
+            y[4 * h + 1] = o.y;
+            y[4 * h + 2] = o.z;
+            y[4 * h + 3] = o.w;
+        }
+    }
+    const int np = p.q_npad, chunk = r / np, rr = r - chunk * np;
+    const int64_t cu = (int64_t) chunk * nw + u;  // this chunk's unit
+    qtc_quantize_unit(y, lane, rr, np, p.q_tiles + cu * np * 512, p.q_bmin + cu * np * 32, p.q_dx + cu * np + rr);
+}
+
 __device__ __forceinline__ float gelu_erf(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(__fmul_rn(x, 0.70710678118654752440f))));
 }
@@ -213,6 +303,18 @@ cudaError_t launch_add_norm(const NormParams & p, cudaStream_t stream) {
     if (v <= 4) return launch_pdl(add_norm_kernel<4>, grid, kNormThreads, stream, p);
     if (v <= 8) return launch_pdl(add_norm_kernel<8>, grid, kNormThreads, stream, p);
     return launch_pdl(add_norm_kernel<16>, grid, kNormThreads, stream, p);
+}
+
+cudaError_t launch_add_norm_quant(const NormParams & p, cudaStream_t stream) {
+    if (p.n_rows <= 0) return cudaSuccess;
+    if (p.compact || !p.q_tiles || !p.q_bmin || !p.q_dx || p.dim % 256 || p.dim / 256 > 32 ||
+        (p.q_npad != 16 && p.q_npad != 32 && p.q_npad != 64) || p.q_rows_padded < p.n_rows ||
+        p.q_rows_padded % p.q_npad || (p.q_npad != 64 && p.q_rows_padded != p.q_npad))
+        return cudaErrorInvalidValue;
+    for (const void * a : {(const void *) p.x, (const void *) p.add, (const void *) p.add_bias, (const void *) p.w,
+                           (const void *) p.ada, (const void *) p.out})
+        if (reinterpret_cast<uintptr_t>(a) & 15) return cudaErrorInvalidValue;
+    return launch_pdl(add_norm_quant_kernel, dim3((unsigned) p.q_rows_padded), (unsigned) (p.dim / 256 * 32), stream, p);
 }
 
 cudaError_t launch_gelu_erf(float * x, int64_t n, cudaStream_t stream) {

@@ -540,6 +540,29 @@ void products(vxk_decoder * d, vxk_qweight * const * ws, int n, const float * x,
     }
 }
 
+// The residual + norm in front of the group product ws: when that product of
+// `rows` rows runs on the tcgen05 kernel in one call, the norm quantizes its
+// rows straight into the product's activation tiles (np.out is not written)
+// and the function returns true: the caller then runs
+// qweight_matmul_group_prequantized as the very next launch.  Otherwise the
+// plain norm into np.out.
+bool norm_into(vxk_decoder * d, vxk::NormParams np, vxk_qweight * const * ws, int n, int32_t rows, cudaStream_t cs) {
+    vxk::QtcTiles t{};
+    if (!np.compact && rows <= d->chunk && d->dim % 256 == 0 && d->dim <= 8192 &&
+        vxk::qweight_group_tiles(ws, n, rows, &t)) {
+        np.out = nullptr;
+        np.q_tiles = t.b;
+        np.q_bmin = t.bmin;
+        np.q_dx = t.dx;
+        np.q_npad = t.npad;
+        np.q_rows_padded = t.rows_padded;
+        VXK_DCUDA(vxk::launch_add_norm_quant(np, cs));
+        return true;
+    }
+    VXK_DCUDA(vxk::launch_add_norm(np, cs));
+    return false;
+}
+
 void forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slots, int32_t * argmax, float * logits,
              float * hidden, cudaStream_t cs) {
     if (!vxk::pool_batch_view(d->pool, &d->view)) dfail(VXK_STATUS_INVALID_STATE, "no batch is planned on the pool");
@@ -574,13 +597,18 @@ void forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slot
     ep.xn = d->xn;
     VXK_DCUDA(vxk::launch_embed_norm(ep, cs));
 
+    bool qkv_tiles = false;  // the previous norm wrote this layer's q/k/v activation tiles
     for (int32_t l = 0; l < d->n_layers; ++l) {
         const Layer & L = d->layers[(size_t) l];
         {
             vxk_qweight * ws[3] = {L.q, L.k, L.v};
             float * ys[3] = {d->q, d->k, d->v};
             const int64_t st[3] = {qdim, kvdim, kvdim};
-            products(d, ws, 3, d->xn, dim, rows, ys, st, cs);
+            if (qkv_tiles)
+                VXK_DCALL((vxk_status) vxk::qweight_matmul_group_prequantized(ws, 3, rows, ys, nullptr, cs),
+                          "quantized product");
+            else
+                products(d, ws, 3, d->xn, dim, rows, ys, st, cs);
         }
         if (bv.single_token) {
             VXK_DCALL(vxk_decode_layer(d->pool, l, d->q, d->k, d->v, d->att, cs), "vxk_decode_layer");
@@ -605,13 +633,17 @@ void forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slot
         np.n_rows = rows;
         np.dim = dim;
         np.eps = d->eps;
-        VXK_DCUDA(vxk::launch_add_norm(np, cs));
+        vxk_qweight * w13[2] = {L.w1, L.w3};
+        const bool ffn_tiles = norm_into(d, np, w13, 2, rows, cs);
         for (int32_t r0 = 0; r0 < rows; r0 += d->chunk) {
             const int32_t nr = std::min(d->chunk, rows - r0);
-            vxk_qweight * ws[2] = {L.w1, L.w3};
             float * ys[2] = {d->gate, d->up};
             const int64_t st[2] = {d->hidden, d->hidden};
-            products(d, ws, 2, d->xn + (int64_t) r0 * dim, dim, nr, ys, st, cs);
+            if (ffn_tiles)  // rows <= chunk: one pass
+                VXK_DCALL((vxk_status) vxk::qweight_matmul_group_prequantized(w13, 2, nr, ys, nullptr, cs),
+                          "quantized product");
+            else
+                products(d, w13, 2, d->xn + (int64_t) r0 * dim, dim, nr, ys, st, cs);
             // w2 . (silu(gate) * up): SwiGLU inside w2's activation quantization
             VXK_DCALL((vxk_status) vxk::qweight_matmul_swiglu(L.w2, d->gate, d->up, nr, d->proj + (int64_t) r0 * dim,
                                                               cs),
@@ -622,7 +654,13 @@ void forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slot
         np.ada = nullptr;
         np.out = last ? d->hn : d->xn;
         np.compact = last ? 1 : 0;
-        VXK_DCUDA(vxk::launch_add_norm(np, cs));
+        if (last) {
+            VXK_DCUDA(vxk::launch_add_norm(np, cs));
+        } else {
+            const Layer & N = d->layers[(size_t) l + 1];
+            vxk_qweight * wn[3] = {N.q, N.k, N.v};
+            qkv_tiles = norm_into(d, np, wn, 3, rows, cs);
+        }
     }
 
     for (int32_t r0 = 0; r0 < n_out; r0 += vxk::kHeadRows) {

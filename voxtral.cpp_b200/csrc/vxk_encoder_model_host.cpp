@@ -401,6 +401,28 @@ int32_t estem(vxk_encoder * e, const float * mel, float * x, cudaStream_t cs) {
     return rows;
 }
 
+// The (residual +) norm in front of the group product ws: when that product of
+// `rows` rows runs on the tcgen05 kernel in one call, the norm quantizes its
+// rows straight into the product's activation tiles (np.out is not written)
+// and the function returns true: the caller then runs
+// qweight_matmul_group_prequantized as the very next launch.  Otherwise the
+// plain norm into np.out.
+bool enorm_into(vxk_encoder * e, vxk::NormParams np, vxk_qweight * const * ws, int n, int32_t rows, cudaStream_t cs) {
+    vxk::QtcTiles t{};
+    if (rows <= e->chunk && e->dim % 256 == 0 && e->dim <= 8192 && vxk::qweight_group_tiles(ws, n, rows, &t)) {
+        np.out = nullptr;
+        np.q_tiles = t.b;
+        np.q_bmin = t.bmin;
+        np.q_dx = t.dx;
+        np.q_npad = t.npad;
+        np.q_rows_padded = t.rows_padded;
+        VXK_ECUDA(vxk::launch_add_norm_quant(np, cs));
+        return true;
+    }
+    VXK_ECUDA(vxk::launch_add_norm(np, cs));
+    return false;
+}
+
 void eforward(vxk_encoder * e, const float * mel, float * out, cudaStream_t cs) {
     if (!out) efail2(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
     const int32_t rows = estem(e, mel, e->x, cs);
@@ -413,7 +435,13 @@ void eforward(vxk_encoder * e, const float * mel, float * out, cudaStream_t cs) 
     np.eps = e->eps;
     np.w = e->attn_norm;
     np.out = e->xn;
-    VXK_ECUDA(vxk::launch_add_norm(np, cs));
+    bool qkv_tiles = false;  // the previous norm wrote this layer's q/k/v activation tiles
+    if (e->n_layers > 0) {
+        vxk_qweight * w0[3] = {e->layers[0].q, e->layers[0].k, e->layers[0].v};
+        qkv_tiles = enorm_into(e, np, w0, 3, rows, cs);
+    } else {
+        VXK_ECUDA(vxk::launch_add_norm(np, cs));
+    }
     for (int32_t l = 0; l < e->n_layers; ++l) {
         const EncLayerW & L = e->layers[(size_t) l];
         {
@@ -421,7 +449,11 @@ void eforward(vxk_encoder * e, const float * mel, float * out, cudaStream_t cs) 
             float * ys[3] = {e->q, e->k, e->v};
             const int64_t st[3] = {qdim, qdim, qdim};
             const float * bs[3] = {L.bq, nullptr, L.bv};  // the q and v biases, added in the products' stores
-            eproducts(e, ws, 3, e->xn, dim, rows, ys, st, cs, bs);
+            if (qkv_tiles)
+                VXK_ECALL((vxk_status) vxk::qweight_matmul_group_prequantized(ws, 3, rows, ys, bs, cs),
+                          "quantized product");
+            else
+                eproducts(e, ws, 3, e->xn, dim, rows, ys, st, cs, bs);
         }
         VXK_ECALL(vxk_enc_layer(e->pool, l, e->q, e->k, e->v, e->att, cs), "vxk_enc_layer");
         {
@@ -434,13 +466,17 @@ void eforward(vxk_encoder * e, const float * mel, float * out, cudaStream_t cs) 
         np.add_bias = L.bo;
         np.w = e->ffn_norm + (int64_t) l * dim;
         np.out = e->xn;
-        VXK_ECUDA(vxk::launch_add_norm(np, cs));
+        vxk_qweight * w13[2] = {L.w1, L.w3};
+        const bool ffn_tiles = enorm_into(e, np, w13, 2, rows, cs);
         for (int32_t r0 = 0; r0 < rows; r0 += e->chunk) {
             const int32_t nr = std::min(e->chunk, rows - r0);
-            vxk_qweight * ws[2] = {L.w1, L.w3};
             float * ys[2] = {e->gate, e->up};
             const int64_t st[2] = {e->hidden, e->hidden};
-            eproducts(e, ws, 2, e->xn + (int64_t) r0 * dim, dim, nr, ys, st, cs);
+            if (ffn_tiles)  // rows <= chunk: one pass
+                VXK_ECALL((vxk_status) vxk::qweight_matmul_group_prequantized(w13, 2, nr, ys, nullptr, cs),
+                          "quantized product");
+            else
+                eproducts(e, w13, 2, e->xn + (int64_t) r0 * dim, dim, nr, ys, st, cs);
             VXK_ECALL((vxk_status) vxk::qweight_matmul_swiglu(L.w2, e->gate, e->up, nr, e->proj + (int64_t) r0 * dim,
                                                               cs),
                       "quantized product");
@@ -450,7 +486,13 @@ void eforward(vxk_encoder * e, const float * mel, float * out, cudaStream_t cs) 
         np.add_bias = L.b2;
         np.w = last ? e->enc_norm : e->attn_norm + (int64_t) (l + 1) * dim;
         np.out = last ? out : e->xn;
-        VXK_ECUDA(vxk::launch_add_norm(np, cs));
+        if (last) {
+            VXK_ECUDA(vxk::launch_add_norm(np, cs));
+        } else {
+            const EncLayerW & N = e->layers[(size_t) l + 1];
+            vxk_qweight * wn[3] = {N.q, N.k, N.v};
+            qkv_tiles = enorm_into(e, np, wn, 3, rows, cs);
+        }
     }
 }
 

@@ -330,8 +330,10 @@ struct QtcParams {
     int32_t * error;
 };
 
-// Quantization of x into the f16 tiles, then the tcgen05 product.
-cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream);
+// Quantization of x into the f16 tiles, then the tcgen05 product; with
+// prequantized, the product alone over tiles the previous launch on the stream
+// wrote (launch_add_norm_quant).
+cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream, bool prequantized = false);
 // Clusters of cluster_y product CTAs the device runs at once (0 on error).
 int qtc_max_active_clusters(int npad, int cluster_y);
 
@@ -347,6 +349,24 @@ void qweight_attach_error(vxk_qweight * w, int32_t * word);
 // y = W (silu(gate) * up), the SwiGLU product computed inside the activation
 // quantization (silu(g) = g / (1 + expf(-g)), each step rounded like the
 // separate kernel would); 0 or a vxk_status number.
+// Activation tiles of a tcgen05 group product (QtcParams b_tiles, bmin_tiles,
+// dx of its first matrix) for `rows` rows, padded to npad x chunks.
+struct QtcTiles {
+    uint8_t * b;
+    uint8_t * bmin;
+    float * dx;
+    int32_t npad;
+    int32_t rows_padded;
+};
+// True when the group product of ws over `rows` rows runs entirely on the
+// tcgen05 kernel in one launch (every matrix a K-quant taking that kernel,
+// shared device and n_cols, rows within every max_batch); then *t holds the
+// tiles a producer writes before qweight_matmul_group_prequantized.
+bool qweight_group_tiles(vxk_qweight * const * ws, int32_t n, int32_t rows, QtcTiles * t);
+// The group product over the tiles the previous launch on `stream` wrote
+// (no quantization launch); biases[i] as in qweight_matmul_group_bias.
+int32_t qweight_matmul_group_prequantized(vxk_qweight * const * ws, int32_t n, int32_t rows, float * const * ys,
+                                          const float * const * biases, cudaStream_t stream);
 int32_t qweight_matmul_swiglu(vxk_qweight * w, const float * gate, const float * up, int32_t rows, float * y,
                               cudaStream_t stream);
 // vxk_qweight_matmul_group, then y_i += bias_i on every row (ggml_mul_mat
@@ -431,6 +451,13 @@ struct NormParams {
     int32_t n_rows;
     int32_t dim;
     float eps;
+    // launch_add_norm_quant only: the output rows quantized into a tcgen05
+    // product's activation tiles (QtcTiles), out optional
+    uint8_t * q_tiles;
+    uint8_t * q_bmin;
+    float * q_dx;
+    int32_t q_npad;
+    int32_t q_rows_padded;     // q_npad x the product's row chunks
 };
 
 // One adapter group: 4 encoder frames of a stream into one audio slot.
@@ -444,6 +471,9 @@ static_assert(sizeof(AdaptRow) == 16, "AdaptRow layout");
 
 cudaError_t launch_embed_norm(const EmbedParams & p, cudaStream_t stream);
 cudaError_t launch_add_norm(const NormParams & p, cudaStream_t stream);
+// add_norm_kernel's rows quantized into p.q_tiles / q_bmin / q_dx (dim a
+// multiple of 256, at most 8192; no compact rows).
+cudaError_t launch_add_norm_quant(const NormParams & p, cudaStream_t stream);
 // x = gelu_erf(x) over n values.
 cudaError_t launch_gelu_erf(float * x, int64_t n, cudaStream_t stream);
 // out[g] = the 4 frames of group g, concatenated ([n][4 * enc_dim]).

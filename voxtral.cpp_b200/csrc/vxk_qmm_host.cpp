@@ -355,7 +355,8 @@ void plan_split_tc(int32_t n_units, int32_t sms, int64_t blocks, vxk::QtcParams 
 }
 
 void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * x_up, int32_t rows,
-            float * const * ys, const float * const * biases, int32_t * error, cudaStream_t stream) {
+            float * const * ys, const float * const * biases, int32_t * error, cudaStream_t stream,
+            bool prequantized = false) {
     vxk_qweight * w0 = ws[0];
     vxk::QtcParams p{};
     p.n_mats = n;
@@ -381,7 +382,7 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * 
     p.bmin_tiles = w0->tc_bmin;
     p.dx = w0->tc_dx;
     p.error = error;
-    VXK_QCUDA(vxk::launch_qtc(p, stream));
+    VXK_QCUDA(vxk::launch_qtc(p, stream, prequantized));
 }
 
 void run_sync(vxk_qweight * const * ws, int32_t n, const float * x, const float * x_up, int32_t rows,
@@ -485,6 +486,35 @@ int32_t qweight_matmul_swiglu(vxk_qweight * w, const float * gate, const float *
         vxk_qweight * one[1] = {w};
         float * yv[1] = {y};
         run_group(one, 1, gate, rows, yv, stream, up);
+    });
+}
+
+bool qweight_group_tiles(vxk_qweight * const * ws, int32_t n, int32_t rows, QtcTiles * t) {
+    if (!ws || n < 1 || n > kQmmMaxGroup || !t) return false;
+    for (int32_t i = 0; i < n; ++i) {
+        const vxk_qweight * w = ws[i];
+        if (!w || !use_tc(w, rows) || rows > w->cfg.max_batch || w->cfg.device != ws[0]->cfg.device ||
+            w->cfg.n_cols != ws[0]->cfg.n_cols)
+            return false;
+    }
+    const int32_t npad = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+    t->b = ws[0]->tc_b;
+    t->bmin = ws[0]->tc_bmin;
+    t->dx = ws[0]->tc_dx;
+    t->npad = npad;
+    t->rows_padded = npad * ((rows + npad - 1) / npad);
+    return true;
+}
+
+int32_t qweight_matmul_group_prequantized(vxk_qweight * const * ws, int32_t n, int32_t rows, float * const * ys,
+                                          const float * const * biases, cudaStream_t stream) {
+    QtcTiles t{};
+    if (!qweight_group_tiles(ws, n, rows, &t) || !ys) return VXK_STATUS_INVALID_ARGUMENT;
+    return qguarded(ws[0], [&] {
+        for (int32_t i = 0; i < n; ++i)
+            if (!ys[i]) qfail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        QwDevice scope(ws[0]->cfg.device);
+        run_tc(ws, n, nullptr, nullptr, rows, ys, biases, ws[0]->d_error, stream, true);
     });
 }
 

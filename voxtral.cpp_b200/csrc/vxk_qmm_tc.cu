@@ -10,9 +10,10 @@
 // quantized activations (|q8| <= 127); the fp32 accumulator of one 256-column
 // unit then holds d-free sum_j sc_j * sum q4*q8 exactly (well below 2^24).
 // Q6_K's scaled quants sc*q reach 4096, past f16's exact integers, so they
-// are two exact operands, 16*(sc>>4)*q and (sc&15)*q, multiplied into the
-// same accumulator (a unit in two halves of 128 columns, so both fit one A
-// buffer).
+// are two exact operands, (sc>>4)*q and (sc&15)*q, multiplied into two
+// accumulators that the epilogue combines as 16 D_hi + D_lo (both exact fp32
+// integers below 2^24; a unit in two halves of 128 columns, so both operands
+// of a half fit one A buffer).
 // Q4_K's mins term sum_j m_j * s_j (s_j = sums of 32 quantized activations)
 // is one more K = 16 product: A = (m_0..m_7, 128 m_0..128 m_7), B = (l_0..l_7,
 // h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
@@ -40,6 +41,7 @@
 // Column splits of a 128-row block are one thread-block cluster and reduce
 // their partial blocks through distributed shared memory, in split order.
 #include "vxk_internal.h"
+#include "vxk_qtc_quant.h"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -84,7 +86,7 @@ static_assert(kSmem <= 232448, "tcgen05 quantized product exceeds 227 KB of shar
 static_assert(kActStages == 2, "the two MMA issuers split Q4_K units by parity");
 static_assert(kRawStages * kRawBytes >= kMaxN * 128 * 4, "the reduction tile fits the raw ring");
 static_assert(kOffAct % 1024 == 0 && kOffAMin % 1024 == 0 && kActStage % 1024 == 0, "128-byte swizzle atoms align");
-// TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] 384..511
+// TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] (Q6_K: D_lo[b]) 384..511
 constexpr int kTmemCols = 512;
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
@@ -298,34 +300,12 @@ __device__ __forceinline__ void cluster_reduce_store(uint32_t local, int S, int 
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
-// K position (0..255, the order of the tensor-core operands) of element e of a
-// 256-column unit.  Dequant word w (quant bytes 4w..4w+3 of the row, group
-// g = w/8 of 64 elements, l = 4(w%8)) fills positions 8w..8w+7 with elements
-// g*64 + {l, l+2, 32+l, 34+l, l+1, l+3, 33+l, 35+l}: the order in which
-// masking the nibbles of one 32-bit word yields f16 pairs.
-__device__ __forceinline__ int tc_position(int e) {
-    const int g = e >> 6, within = e & 63;
-    const int hi = within >= 32;
-    const int l = within & 31;
-    const int w = 8 * g + (l >> 2);
-    const int bb = l & 3;
-    const int s = (bb == 0 ? 0 : bb == 2 ? 1 : bb == 1 ? 4 : 5) + (hi ? 2 : 0);
-    return 8 * w + s;
-}
-
-// Byte offset of K position p of operand row n in a unit tile of `rows` rows:
-// 4 atoms of 64 positions, each [rows][128 B] with 128-byte swizzle.
-__device__ __forceinline__ int tc_tile_off(int n, int p, int rows) {
-    const int a = p >> 6, q = p & 63;
-    return a * rows * 128 + (n >> 3) * 1024 + (n & 7) * 128 + ((((q >> 3) ^ (n & 7))) << 4) + (q & 7) * 2;
-}
-
 // ---------------------------------------------------------------------------
 // Activation quantization for the tcgen05 product (quantize_row_q8_K_ref):
-// f16 B tiles in the K order above, the mins B rows (l_j, h_j) and d_x.
-// Grid (units, padded rows / 8), 256 threads: warp w quantizes row 8 y + w of
-// unit x, lane L its columns 8L .. 8L + 7 (sub-block j = lanes 4j .. 4j + 3);
-// every reduction is a warp shuffle.  Rows are read as float4 (16-byte
+// f16 B tiles in the K order of tc_position (vxk_qtc_quant.h), the mins B rows
+// (l_j, h_j) and d_x.  Grid (units, padded rows / 8), 256 threads: warp w
+// quantizes row 8 y + w of unit x, lane L the columns of K positions 8L .. 8L
+// + 7; every reduction is a warp shuffle.  Rows are read as float4 (16-byte
 // aligned x, checked by the host).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
@@ -340,8 +320,7 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
     // chunk): the elements 64g + l .. l + 3 and 64g + 32 + l .. + 3 (g = L / 8,
     // l = 4 (L % 8)) in the position order of tc_position, so it loads two
     // aligned float4 and stores the chunk at once.  x[0..3] = A, x[4..7] = B.
-    const int g = lane >> 3, l = 4 * (lane & 7);
-    const int eA = 64 * g + l, eB = eA + 32;  // element (column) indices of the two quads
+    const int eA = qtc_lane_col_a(lane), eB = eA + 32;  // element (column) indices of the two quads
     float x[8];
     if (rg < p.rows) {
         const float * row = p.x + (int64_t) rg * K + (int64_t) u * kQmmUnit;
@@ -359,67 +338,11 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) x[i] = 0.0f;
     }
-    // the value of largest magnitude, first column on ties: key = |x| bits, then
-    // the inverted column (non-negative floats order as integers)
-    unsigned long long key = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int col = (i < 4 ? eA : eB) + (i & 3);
-        const unsigned long long kx = ((unsigned long long) __float_as_uint(fabsf(x[i])) << 32) | (unsigned) (255 - col);
-        key = kx > key ? kx : key;
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(kFull, key, o);
-        key = other > key ? other : key;
-    }
-    const int arg = 255 - (int) (key & 0xffffffffu);
-    // the lane holding column arg, and which of its eight values it is
-    const int a_within = arg & 63, a_hi = a_within >= 32 ? 1 : 0, a_l = a_within & 31;
-    const int a_lane = 8 * (arg >> 6) + (a_l >> 2), a_idx = 4 * a_hi + (a_l & 3);
-    float mine = x[0];
-#pragma unroll
-    for (int i = 1; i < 8; ++i)
-        if (a_idx == i) mine = x[i];
-    const float s_max = __shfl_sync(kFull, mine, a_lane);
-    const float amax = __uint_as_float((unsigned) (key >> 32));
-    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    float d = 0.0f;
-    if (amax != 0.0f) {
-        const float iscale = __fdiv_rn(-127.0f, s_max);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, x[i])));
-        d = __fdiv_rn(1.0f, iscale);
-    }
     const int np = p.npad;
-    uint8_t * tile = p.b_tiles + cu * np * 512;
-    // positions 8L + s hold elements A0, A2, B0, B2, A1, A3, B1, B3 (tc_position)
-    auto h2 = [](int lo, int hi) {
-        const __half2 v = __halves2half2(__int2half_rn(lo), __int2half_rn(hi));
-        return *reinterpret_cast<const uint32_t *>(&v);
-    };
-    *reinterpret_cast<uint4 *>(tile + tc_tile_off(r, 8 * lane, np)) =
-        make_uint4(h2(q[0], q[2]), h2(q[4], q[6]), h2(q[1], q[3]), h2(q[5], q[7]));
-    // sums of sub-blocks 2g (the A quads) and 2g + 1 (the B quads) over the group's 8 lanes
-    int sa = q[0] + q[1] + q[2] + q[3], sb = q[4] + q[5] + q[6] + q[7];
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-        sa += __shfl_xor_sync(kFull, sa, o);
-        sb += __shfl_xor_sync(kFull, sb, o);
-    }
-    if ((lane & 7) == 0) {
-        // mins row: K position j = l_j, 8 + j = h_j (s_j = 128 h_j + l_j); unswizzled
-        // K-major core matrices: row group r / 8 at 256 B, K half at 128 B, row r % 8 at 16 B
-        uint8_t * mrow = p.bmin_tiles + cu * np * 32 + (r >> 3) * 256 + (r & 7) * 16;
-        *reinterpret_cast<__half *>(mrow + (2 * g) * 2) = __int2half_rn(sa & 127);
-        *reinterpret_cast<__half *>(mrow + 128 + (2 * g) * 2) = __int2half_rn(sa >> 7);
-        *reinterpret_cast<__half *>(mrow + (2 * g + 1) * 2) = __int2half_rn(sb & 127);
-        *reinterpret_cast<__half *>(mrow + 128 + (2 * g + 1) * 2) = __int2half_rn(sb >> 7);
-    }
-    if (lane == 0) p.dx[cu * np + r] = d;
+    qtc_quantize_unit(x, lane, r, np, p.b_tiles + cu * np * 512, p.bmin_tiles + cu * np * 32, p.dx + cu * np + r);
 }
 
-// One half (128 columns) of a Q6_K unit for row r into TMEM: A_hi = 16*(sc>>4)*q
+// One half (128 columns) of a Q6_K unit for row r into TMEM: A_hi = (sc>>4)*q
 // at columns [abase, abase+64) and A_lo = (sc&15)*q at [abase+64, abase+128),
 // q = q6 - 32, in the K order of the Q4_K words (see tc_position): word
 // 8gg + 4c4 + k of half h holds elements 64gg + {l, l+2, 32+l, 34+l, l+1, l+3,
@@ -438,7 +361,6 @@ __device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int 
     }
     const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-    const __half2 c1056 = __float2half2_rn(1056.0f);
 #pragma unroll
     for (int gg = 0; gg < 2; ++gg) {
         uint32_t hi[32], lo[32];
@@ -447,8 +369,12 @@ __device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int 
             const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two parts
             const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
             const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
-            const __half2 fah = __float2half2_rn((float) (16 * (sa >> 4))), fal = __float2half2_rn((float) (sa & 15));
-            const __half2 fbh = __float2half2_rn((float) (16 * (sb >> 4))), fbl = __float2half2_rn((float) (sb & 15));
+            // a spliced pair holds 1024 + q6 = 1056 + q: one fused multiply-add
+            // per part, (1056 + q) f - 1056 f = q f, exact (|1056 f| <= 15840)
+            const __half2 fah = __float2half2_rn((float) (sa >> 4)), fal = __float2half2_rn((float) (sa & 15));
+            const __half2 fbh = __float2half2_rn((float) (sb >> 4)), fbl = __float2half2_rn((float) (sb & 15));
+            const __half2 bah = __float2half2_rn(-1056.0f * (float) (sa >> 4)), bal = __float2half2_rn(-1056.0f * (float) (sa & 15));
+            const __half2 bbh = __float2half2_rn(-1056.0f * (float) (sb >> 4)), bbl = __float2half2_rn(-1056.0f * (float) (sb & 15));
             const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
             const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
             const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
@@ -462,10 +388,10 @@ __device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int 
                 pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4) | 0x64006400u;
 #pragma unroll
                 for (int x = 0; x < 4; ++x) {
-                    const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&pv[x]), c1056);
+                    const __half2 q = *reinterpret_cast<const __half2 *>(&pv[x]);
                     const bool pa = (x & 1) == 0;  // pv[0], pv[2] from the bytes at l, pv[1], pv[3] at 32+l
-                    hi[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fah : fbh));
-                    lo[16 * c4 + 4 * k + x] = h2_bits(__hmul2(q, pa ? fal : fbl));
+                    hi[16 * c4 + 4 * k + x] = h2_bits(__hfma2(q, pa ? fah : fbh, pa ? bah : bbh));
+                    lo[16 * c4 + 4 * k + x] = h2_bits(__hfma2(q, pa ? fal : fbl, pa ? bal : bbl));
                 }
             }
         }
@@ -662,20 +588,25 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             // d_x of activation row e of this unit
             auto dxe = [&](int e) { return __shfl_sync(kFull, e < 32 ? xa : xb, e & 31); };
             if (m.type == 14) {
-                // Q6_K: acc += (d_w * d_x) * D
+                // Q6_K: acc += (d_w * d_x) * (16 D_hi + D_lo)
 #pragma unroll
                 for (int c0 = 0; c0 < N; c0 += 32) {
                     constexpr int W = N < 32 ? N : 32;
-                    uint32_t v[2][16];
+                    uint32_t v[2][16], lo[2][16];
 #pragma unroll
-                    for (int hh = 0; hh < W / 16; ++hh) tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * hh + lane_off, v[hh]);
+                    for (int hh = 0; hh < W / 16; ++hh) {
+                        tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * hh + lane_off, v[hh]);
+                        tmem_ld16_nowait(tmem + 384 + 64 * b + c0 + 16 * hh + lane_off, lo[hh]);
+                    }
                     tmem_ld_wait();
 #pragma unroll
                     for (int hh = 0; hh < W / 16; ++hh)
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj)
                             acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dxe(c0 + 16 * hh + jj)),
-                                                          __uint_as_float(v[hh][jj]), acc[c0 + 16 * hh + jj]);
+                                                          fmaf(16.0f, __uint_as_float(v[hh][jj]),
+                                                               __uint_as_float(lo[hh][jj])),
+                                                          acc[c0 + 16 * hh + jj]);
                 }
             } else {
                 // Q4_K: 32 columns of D and of Dmin in flight per wait
@@ -782,13 +713,13 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     const uint64_t bdesc0 = sw128_desc(bt, 16, 1024);
                     const uint32_t a0 = tmem + 128 * b;
                     if (q6) {
-                        // half h: K positions 128h .. 128h+127, A_hi then A_lo per step
+                        // half h: K positions 128h .. 128h+127, A_hi into D, A_lo into D_lo
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
                             const int ks = 8 * h + kk;
                             const uint64_t bdesc = bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4);
                             mma_ts(dacc, a0 + 8 * kk, bdesc, idesc, (h | kk) != 0);
-                            mma_ts(dacc, a0 + 64 + 8 * kk, bdesc, idesc, 1);
+                            mma_ts(dacc + 128, a0 + 64 + 8 * kk, bdesc, idesc, (h | kk) != 0);
                         }
                     } else {
 #pragma unroll
@@ -916,7 +847,7 @@ int qtc_max_active_clusters(int npad, int cluster_y) {
     }
 }
 
-cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream) {
+cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream, bool prequantized) {
     if (p.n_chunks < 1 || (p.n_chunks > 1 && p.npad != 64) || p.rows <= p.npad * (p.n_chunks - 1))
         return cudaErrorInvalidValue;
     if (p.n_mats < 1 || p.n_mats > kQmmMaxGroup || p.rows < 1 || p.rows > p.npad * p.n_chunks || p.units_per_split < 1 ||
@@ -925,9 +856,11 @@ cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream) {
     if (p.npad != 16 && p.npad != 32 && p.npad != 64) return cudaErrorInvalidValue;
     for (int i = 0; i < p.n_mats; ++i)
         if (p.mats[i].n_rows % 128 != 0) return cudaErrorInvalidValue;
-    cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) (p.npad * p.n_chunks / 8)), 256, 0,
-                              stream, p, 1);
-    if (e != cudaSuccess) return e;
+    if (!prequantized) {
+        const cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) (p.npad * p.n_chunks / 8)),
+                                        256, 0, stream, p, 1);
+        if (e != cudaSuccess) return e;
+    }
     switch (p.npad) {
         case 16: return launch_n<16>(p, stream);
         case 32: return launch_n<32>(p, stream);

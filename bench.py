@@ -955,7 +955,10 @@ def run_encstack(args, cfg, world, rank, local, dist, torch, vxk):
                          "tflops": round(flops / step_s / 1e12, 2), "avg_step_us": round(step_s * 1e6, 1),
                          "kernel": "whole step (all kernels); products re-stream their weights per 64-row chunk"},
             "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": int(args.steps * (2 + 1 + L * 10)),
+            # conv stem (2), the first norm (quantizing into layer 0's q/k/v tiles), per layer (q/k/v
+            # product, attention with the fused ring append, o quantize + product, norm into the
+            # w1/w3 tiles, w1/w3 product, w2 quantize + product, norm)
+            "gpu_launches": int(args.steps * (2 + 1 + L * 9)),
             "launch": "eager C-ABI calls per step: vxk_enc_batch_plan, vxk_encoder_forward, vxk_enc_batch_commit",
             "clocks": clocks.summary(),
         }
@@ -1107,7 +1110,7 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
     if dist:
         dist.barrier()
     if rank == 0:
-        per_layer = 11
+        per_layer = 9
         line = {
             "metric": "whole decoder step tokens/s (Q4_K_M, 26 layers + head)",
             "value": round(world * S * args.steps / (ms / 1000.0), 1),
@@ -1129,10 +1132,11 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
                          "weight_bytes": w_bytes, "kv_bytes": round(kv_bytes),
                          "avg_step_us": round(step_s * 1e6, 1), "kernel": "whole step (all kernels)"},
             "cpu_baseline": cpu, "e2e": e2e,
-            # embed + per layer (q/k/v quantize + product, attention, o quantize + product, norm, w1/w3
-            # quantize + product, w2 quantize (SwiGLU inside) + product, norm) + head (quantize, product,
-            # argmax, token ids)
-            "gpu_launches": int(args.steps * (1 + per_layer * L + 4)),
+            # embed, layer 0's q/k/v quantization, per layer (q/k/v product, attention, o quantize +
+            # product, norm quantizing into the w1/w3 tiles, w1/w3 product, w2 quantize (SwiGLU inside)
+            # + product, norm quantizing into the next q/k/v tiles), head (quantize, product, argmax,
+            # token ids)
+            "gpu_launches": int(args.steps * (1 + 1 + per_layer * L + 4)),
             "launch": "eager C-ABI calls per step: vxk_batch_plan, vxk_decoder_forward, vxk_batch_commit",
             "clocks": clocks.summary(),
         }

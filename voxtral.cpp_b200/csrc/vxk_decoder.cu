@@ -236,7 +236,9 @@ __global__ void __launch_bounds__(1024) add_norm_quant_kernel(NormParams p) {
     }
     const int np = p.q_npad, chunk = r / np, rr = r - chunk * np;
     const int64_t cu = (int64_t) chunk * nw + u;  // this chunk's unit
-    qtc_quantize_unit(y, lane, rr, np, p.q_tiles + cu * np * 512, p.q_bmin + cu * np * 32, p.q_dx + cu * np + rr);
+    qtc_quantize_unit(y, lane, rr, np, p.q_tiles ? p.q_tiles + cu * np * 512 : nullptr,
+                      p.q_bmin ? p.q_bmin + cu * np * 32 : nullptr, p.q_tiles8 ? p.q_tiles8 + cu * np * 256 : nullptr,
+                      p.q_dx + cu * np + rr);
 }
 
 __device__ __forceinline__ float gelu_erf(float x) {
@@ -307,7 +309,8 @@ cudaError_t launch_add_norm(const NormParams & p, cudaStream_t stream) {
 
 cudaError_t launch_add_norm_quant(const NormParams & p, cudaStream_t stream) {
     if (p.n_rows <= 0) return cudaSuccess;
-    if (p.compact || !p.q_tiles || !p.q_bmin || !p.q_dx || p.dim % 256 || p.dim / 256 > 32 ||
+    if (p.compact || (!p.q_tiles && !p.q_tiles8) || (p.q_tiles && !p.q_bmin) || !p.q_dx || p.dim % 256 ||
+        p.dim / 256 > 32 ||
         (p.q_npad != 16 && p.q_npad != 32 && p.q_npad != 64) || p.q_rows_padded < p.n_rows ||
         p.q_rows_padded % p.q_npad || (p.q_npad != 64 && p.q_rows_padded != p.q_npad))
         return cudaErrorInvalidValue;

@@ -553,6 +553,7 @@ bool norm_into(vxk_decoder * d, vxk::NormParams np, vxk_qweight * const * ws, in
         np.out = nullptr;
         np.q_tiles = t.b;
         np.q_bmin = t.bmin;
+        np.q_tiles8 = t.b8;
         np.q_dx = t.dx;
         np.q_npad = t.npad;
         np.q_rows_padded = t.rows_padded;

@@ -413,6 +413,7 @@ bool enorm_into(vxk_encoder * e, vxk::NormParams np, vxk_qweight * const * ws, i
         np.out = nullptr;
         np.q_tiles = t.b;
         np.q_bmin = t.bmin;
+        np.q_tiles8 = t.b8;
         np.q_dx = t.dx;
         np.q_npad = t.npad;
         np.q_rows_padded = t.rows_padded;

@@ -324,8 +324,9 @@ struct QtcParams {
     int32_t n_splits;          // <= kQmmMaxSplits: one cluster
     const float * x;           // [rows][K] fp32
     const float * x_up;        // nullptr, or [rows][K]: the row is silu(x) * x_up (SwiGLU)
-    uint8_t * b_tiles;         // [n_units][npad x 256 f16, 4 SW128 atoms]
-    uint8_t * bmin_tiles;      // [n_units][npad rows x 16 f16, unswizzled K-major core matrices (32 B per row)]
+    uint8_t * b_tiles;         // Q4_K operands: [n_units][npad x 256 f16, 4 SW128 atoms], or nullptr
+    uint8_t * bmin_tiles;      // Q4_K: [n_units][npad rows x 16 f16, unswizzled K-major core matrices (32 B per row)]
+    uint8_t * b8_tiles;        // Q6_K operands: [n_units][npad x 256 int8, 2 SW128 atoms], or nullptr
     float * dx;                // [n_units][npad]
     int32_t * error;
 };
@@ -352,8 +353,9 @@ void qweight_attach_error(vxk_qweight * w, int32_t * word);
 // Activation tiles of a tcgen05 group product (QtcParams b_tiles, bmin_tiles,
 // dx of its first matrix) for `rows` rows, padded to npad x chunks.
 struct QtcTiles {
-    uint8_t * b;
+    uint8_t * b;      // nullptr when no matrix of the group is Q4_K
     uint8_t * bmin;
+    uint8_t * b8;     // nullptr when no matrix of the group is Q6_K
     float * dx;
     int32_t npad;
     int32_t rows_padded;
@@ -455,6 +457,7 @@ struct NormParams {
     // product's activation tiles (QtcTiles), out optional
     uint8_t * q_tiles;
     uint8_t * q_bmin;
+    uint8_t * q_tiles8;
     float * q_dx;
     int32_t q_npad;
     int32_t q_rows_padded;     // q_npad x the product's row chunks

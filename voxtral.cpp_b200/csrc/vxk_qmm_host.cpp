@@ -242,6 +242,7 @@ struct vxk_qweight {
     uint8_t * dd_tc = nullptr;
     uint8_t * tc_b = nullptr;
     uint8_t * tc_bmin = nullptr;
+    uint8_t * tc_b8 = nullptr;
     float * tc_dx = nullptr;
     int32_t * d_error = nullptr;
     int32_t * own_error = nullptr;   // d_error unless an owner attached a shared word
@@ -272,7 +273,7 @@ void free_qweight(vxk_qweight * w) {
     if (!w) return;
     QwDevice scope(w->cfg.device);
     for (void * p : {(void *) w->w, (void *) w->act, (void *) w->act_d, (void *) w->act_ms, (void *) w->w_tc,
-                     (void *) w->dd_tc, (void *) w->tc_b, (void *) w->tc_bmin, (void *) w->tc_dx, (void *) w->own_error})
+                     (void *) w->dd_tc, (void *) w->tc_b, (void *) w->tc_bmin, (void *) w->tc_b8, (void *) w->tc_dx, (void *) w->own_error})
         if (p) cudaFree(p);
     if (w->ev_sync) cudaEventDestroy(w->ev_sync);
     delete w;
@@ -378,8 +379,12 @@ void run_tc(vxk_qweight * const * ws, int32_t n, const float * x, const float * 
     plan_split_tc(w0->n_units, w0->sms, (int64_t) block0 * p.n_chunks, p);
     p.x = x;
     p.x_up = x_up;
-    p.b_tiles = w0->tc_b;
-    p.bmin_tiles = w0->tc_bmin;
+    // operand tiles of the types in the group: f16 (+ mins) for Q4_K, int8 for Q6_K
+    bool q4 = false, q6 = false;
+    for (int i = 0; i < n; ++i) (ws[i]->cfg.type == VXK_QTYPE_Q6_K ? q6 : q4) = true;
+    p.b_tiles = q4 ? w0->tc_b : nullptr;
+    p.bmin_tiles = q4 ? w0->tc_bmin : nullptr;
+    p.b8_tiles = q6 ? w0->tc_b8 : nullptr;
     p.dx = w0->tc_dx;
     p.error = error;
     VXK_QCUDA(vxk::launch_qtc(p, stream, prequantized));
@@ -498,8 +503,11 @@ bool qweight_group_tiles(vxk_qweight * const * ws, int32_t n, int32_t rows, QtcT
             return false;
     }
     const int32_t npad = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
-    t->b = ws[0]->tc_b;
-    t->bmin = ws[0]->tc_bmin;
+    bool q4 = false, q6 = false;
+    for (int32_t i = 0; i < n; ++i) (ws[i]->cfg.type == VXK_QTYPE_Q6_K ? q6 : q4) = true;
+    t->b = q4 ? ws[0]->tc_b : nullptr;
+    t->bmin = q4 ? ws[0]->tc_bmin : nullptr;
+    t->b8 = q6 ? ws[0]->tc_b8 : nullptr;
     t->dx = ws[0]->tc_dx;
     t->npad = npad;
     t->rows_padded = npad * ((rows + npad - 1) / npad);
@@ -633,6 +641,7 @@ vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gg
             const size_t chunks = (size_t) (c.max_batch + 63) / 64;  // 64-row chunks of one launch
             VXK_QCUDA(cudaMalloc(&w->tc_b, chunks * w->n_units * 64 * 512));
             VXK_QCUDA(cudaMalloc(&w->tc_bmin, chunks * w->n_units * 64 * 128));
+            VXK_QCUDA(cudaMalloc(&w->tc_b8, chunks * w->n_units * 64 * 256));
             VXK_QCUDA(cudaMalloc(&w->tc_dx, chunks * w->n_units * 64 * sizeof(float)));
         }
         VXK_QCUDA(cudaMalloc(&w->d_error, sizeof(int32_t)));

@@ -9,11 +9,11 @@
 // sub-block scale sc is an integer <= 945, exact in f16, and so are the
 // quantized activations (|q8| <= 127); the fp32 accumulator of one 256-column
 // unit then holds d-free sum_j sc_j * sum q4*q8 exactly (well below 2^24).
-// Q6_K's scaled quants sc*q reach 4096, past f16's exact integers, so they
-// are two exact operands, (sc>>4)*q and (sc&15)*q, multiplied into two
-// accumulators that the epilogue combines as 16 D_hi + D_lo (both exact fp32
-// integers below 2^24; a unit in two halves of 128 columns, so both operands
-// of a half fit one A buffer).
+// Q6_K's scaled quants p = sc*q reach 4096, past f16's exact integers; they
+// become two int8 operands, hi = floor(p / 64) and lo = p mod 64, multiplied
+// by the int8 activations in kind::i8 MMAs (K = 32, int32 accumulators) that
+// the epilogue combines as 64 D_hi + D_lo, an exact int32 sum (the
+// activation tiles of Q6_K matrices are int8).
 // Q4_K's mins term sum_j m_j * s_j (s_j = sums of 32 quantized activations)
 // is one more K = 16 product: A = (m_0..m_7, 128 m_0..128 m_7), B = (l_0..l_7,
 // h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
@@ -24,20 +24,18 @@
 // by side in one launch); 11 warps:
 //   warps 0-3   dequant: thread = weight row (TMEM lane); per unit it reads the
 //               row's 128 quant bytes and 16 scale/min bytes from the raw
-//               ring, writes 128 columns of f16 pairs sc*q into TMEM
-//               (tcgen05.st) and the row's mins row into shared memory
+//               ring, writes 128 columns of f16 pairs sc*q (Q4_K) or of
+//               int8 quads hi, lo (Q6_K) into TMEM (tcgen05.st) and the
+//               row's mins row into shared memory (Q4_K)
 //   warps 4-7   epilogue: thread = weight row; tcgen05.ld of the unit's
 //               accumulators, fp32 block factors into registers
 //   warp 8      bulk copies of the raw weight records (HBM stream, evict-first)
 //   warp 9      bulk copies of the quantized activations (L2)
-//   warps 10-11 tcgen05.mma issuers: 16 MMAs (M = 128, N = rows padded to 16,
-//               K = 16, A from TMEM) + 1 mins MMA per unit; for Q4_K warp 10
-//               issues the even units and warp 11 the odd ones (every buffer
-//               and barrier of a unit alternates with its parity), for Q6_K
-//               (both A buffers per unit) warp 10 issues them all: a second
-//               waiter on an A buffer would wait for its completion k + 1
-//               while completion k is still pending, and a parity wait cannot
-//               tell that from the phase before k (it passes at once)
+//   warps 10-11 tcgen05.mma issuers, warp 10 the even units and warp 11 the
+//               odd ones (every buffer and barrier of a unit alternates with
+//               its parity): Q4_K 16 kind::f16 MMAs (M = 128, N = rows padded
+//               to 16, K = 16, A from TMEM) + 1 mins MMA per unit; Q6_K 2 x 8
+//               kind::i8 MMAs (K = 32)
 // Column splits of a 128-row block are one thread-block cluster and reduce
 // their partial blocks through distributed shared memory, in split order.
 #include "vxk_internal.h"
@@ -54,7 +52,7 @@ namespace {
 
 constexpr int kThreads = 384;
 constexpr int kRawStages = 4;
-constexpr int kActStages = 2;  // = 2: a Q4_K unit's stage is its parity, like its A and D buffers
+constexpr int kActStages = 2;  // = 2: a unit's stage is its parity, like its A and D buffers
 constexpr int kMaxN = 64;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr unsigned kFull = 0xffffffffu;
@@ -83,7 +81,7 @@ constexpr int kNumBars = kBarDrain + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;       // tmem base, abort flag
 constexpr int kSmem = kOffMisc + 16 + 1024;            // + alignment slack
 static_assert(kSmem <= 232448, "tcgen05 quantized product exceeds 227 KB of shared memory");
-static_assert(kActStages == 2, "the two MMA issuers split Q4_K units by parity");
+static_assert(kActStages == 2, "the two MMA issuers split the units by parity");
 static_assert(kRawStages * kRawBytes >= kMaxN * 128 * 4, "the reduction tile fits the raw ring");
 static_assert(kOffAct % 1024 == 0 && kOffAMin % 1024 == 0 && kActStage % 1024 == 0, "128-byte swizzle atoms align");
 // TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] (Q6_K: D_lo[b]) 384..511
@@ -202,6 +200,17 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM) . B (shared memory descriptor), kind::i8 (s32 D).
+__device__ __forceinline__ void mma_ts_i8(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -339,64 +348,70 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
         for (int i = 0; i < 8; ++i) x[i] = 0.0f;
     }
     const int np = p.npad;
-    qtc_quantize_unit(x, lane, r, np, p.b_tiles + cu * np * 512, p.bmin_tiles + cu * np * 32, p.dx + cu * np + r);
+    qtc_quantize_unit(x, lane, r, np, p.b_tiles ? p.b_tiles + cu * np * 512 : nullptr,
+                      p.bmin_tiles ? p.bmin_tiles + cu * np * 32 : nullptr,
+                      p.b8_tiles ? p.b8_tiles + cu * np * 256 : nullptr, p.dx + cu * np + r);
 }
 
-// One half (128 columns) of a Q6_K unit for row r into TMEM: A_hi = (sc>>4)*q
-// at columns [abase, abase+64) and A_lo = (sc&15)*q at [abase+64, abase+128),
-// q = q6 - 32, in the K order of the Q4_K words (see tc_position): word
-// 8gg + 4c4 + k of half h holds elements 64gg + {l, l+2, 32+l, 34+l, l+1, l+3,
-// 33+l, 35+l} (l = 16c4 + 4k) of the half, the low (gg = 0) or high nibbles of
-// the quant bytes at l and 32+l and 2-bit fields 4gg and 4gg+2 of the high
-// plane byte at l.  Both parts are exact f16 integers.
-__device__ __forceinline__ void dequant_q6_half(const uint8_t * raw, int r, int h, uint32_t abase) {
+// A Q6_K unit of row r into TMEM as int8 operands of kind::i8 MMAs: p = q sc
+// (q = q6 - 32, sc the int8 sub-block scale, |p| <= 4096) is split as p =
+// 64 hi + lo with hi = floor(p / 64) in [-64, 64] and lo = p mod 64 in [0, 64),
+// hi at columns [abase, abase + 64) and lo at [abase + 64, abase + 128); column t
+// holds K positions 4t .. 4t + 3, the unit's elements in natural order.  Two
+// elements of one sub-block sit in the 16-bit halves of a word (the 6-bit
+// quants at the bytes l and l + 2 of the low-nibble and high-plane words), so
+// one 32-bit multiply-add forms both (p + 8192, always in [4128, 12288]: no
+// carry between the halves); bits 6..13 of each half are hi + 128 and bits
+// 0..5 are lo, and a byte permute gathers four of each into a word (hi + 128
+// turned into the int8 hi by flipping bit 7).
+__device__ __forceinline__ void dequant_q6_i8(const uint8_t * raw, int r, uint32_t abase) {
     const uint8_t * ql = raw + r * 128;
     const uint8_t * qh = raw + 16384 + r * 64;
-    uint4 A[2], B[2], H[2];
-#pragma unroll
-    for (int c4 = 0; c4 < 2; ++c4) {
-        A[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + c4) ^ (r & 7)) << 4));
-        B[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + 2 + c4) ^ (r & 7)) << 4));
-        H[c4] = *reinterpret_cast<const uint4 *>(qh + (((2 * h + c4) ^ ((r >> 1) & 3)) << 4));
-    }
     const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg) {
-        uint32_t hi[32], lo[32];
+    for (int h = 0; h < 2; ++h) {
+        uint4 A[2], B[2], H[2];
 #pragma unroll
         for (int c4 = 0; c4 < 2; ++c4) {
-            const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;  // sub-block scales of the two parts
-            const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
-            const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
-            // a spliced pair holds 1024 + q6 = 1056 + q: one fused multiply-add
-            // per part, (1056 + q) f - 1056 f = q f, exact (|1056 f| <= 15840)
-            const __half2 fah = __float2half2_rn((float) (sa >> 4)), fal = __float2half2_rn((float) (sa & 15));
-            const __half2 fbh = __float2half2_rn((float) (sb >> 4)), fbl = __float2half2_rn((float) (sb & 15));
-            const __half2 bah = __float2half2_rn(-1056.0f * (float) (sa >> 4)), bal = __float2half2_rn(-1056.0f * (float) (sa & 15));
-            const __half2 bbh = __float2half2_rn(-1056.0f * (float) (sb >> 4)), bbl = __float2half2_rn(-1056.0f * (float) (sb & 15));
-            const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
-            const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
-            const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
+            A[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + c4) ^ (r & 7)) << 4));
+            B[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + 2 + c4) ^ (r & 7)) << 4));
+            H[c4] = *reinterpret_cast<const uint4 *>(qh + (((2 * h + c4) ^ ((r >> 1) & 3)) << 4));
+        }
+        uint32_t hi[32], lo[32];  // words t - 32 h of this half
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int ns = 4 * gg, fa = 4 * gg, fb = 4 * gg + 2;
-                uint32_t pv[4];
-                pv[0] = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fa) & 0x00030003u) << 4) | 0x64006400u;
-                pv[1] = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fb) & 0x00030003u) << 4) | 0x64006400u;
-                pv[2] = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fa + 8)) & 0x00030003u) << 4) | 0x64006400u;
-                pv[3] = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4) | 0x64006400u;
+        for (int gg = 0; gg < 2; ++gg) {
 #pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                    const __half2 q = *reinterpret_cast<const __half2 *>(&pv[x]);
-                    const bool pa = (x & 1) == 0;  // pv[0], pv[2] from the bytes at l, pv[1], pv[3] at 32+l
-                    hi[16 * c4 + 4 * k + x] = h2_bits(__hfma2(q, pa ? fah : fbh, pa ? bah : bbh));
-                    lo[16 * c4 + 4 * k + x] = h2_bits(__hfma2(q, pa ? fal : fbl, pa ? bal : bbl));
+            for (int c4 = 0; c4 < 2; ++c4) {
+                // elements 128h + 64gg + 16c4 + (0..15) (part a, scale ia) and + 32 (part b, ia + 2)
+                const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;
+                const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
+                const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
+                const uint32_t ca = (uint32_t) (8192 - 32 * sa) * 0x00010001u;
+                const uint32_t cb = (uint32_t) (8192 - 32 * sb) * 0x00010001u;
+                const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
+                const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
+                const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int ns = 4 * gg, fa = 4 * gg, fb = 4 * gg + 2;
+                    // 6-bit quants of positions (l, l + 2) and (l + 1, l + 3), l = 16 c4 + 4 k
+                    const uint32_t a02 = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fa) & 0x00030003u) << 4);
+                    const uint32_t a13 = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fa + 8)) & 0x00030003u) << 4);
+                    const uint32_t b02 = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fb) & 0x00030003u) << 4);
+                    const uint32_t b13 = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4);
+                    const uint32_t pa02 = a02 * (uint32_t) sa + ca, pa13 = a13 * (uint32_t) sa + ca;
+                    const uint32_t pb02 = b02 * (uint32_t) sb + cb, pb13 = b13 * (uint32_t) sb + cb;
+                    const int ta = 16 * gg + 4 * c4 + k, tb = ta + 8;
+                    hi[ta] = __byte_perm(pa02 >> 6, pa13 >> 6, 0x6240) ^ 0x80808080u;
+                    lo[ta] = __byte_perm(pa02, pa13, 0x6240) & 0x3F3F3F3Fu;
+                    hi[tb] = __byte_perm(pb02 >> 6, pb13 >> 6, 0x6240) ^ 0x80808080u;
+                    lo[tb] = __byte_perm(pb02, pb13, 0x6240) & 0x3F3F3F3Fu;
                 }
             }
         }
-        tmem_st32(abase + 32 * gg, hi);
-        tmem_st32(abase + 64 + 32 * gg, lo);
+        tmem_st32(abase + 32 * h, hi);
+        tmem_st32(abase + 64 + 32 * h, lo);
     }
 }
 
@@ -460,25 +475,20 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         const int r = 32 * warp + lane;
         const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
         const bool q6 = m.type == 14;
-        const int phases = q6 ? 2 : 1;  // A buffers filled per unit (Q6_K: two halves)
-        int j = 0;                      // A-phase counter: buffer j & 1, use j >> 1
-        bool stop = false;
-        for (int i = 0; i < nu && !stop; ++i) {
+        for (int i = 0; i < nu; ++i) {
             const int s = i % kRawStages;
             if (!__all_sync(kFull, tc_wait(&bars[kBarRawFull + s], (uint32_t) (i / kRawStages) & 1u, abort_flag,
                                            p.error)))
                 break;
             const uint8_t * raw = base + kOffRaw + s * kRawBytes;
-            for (int h = 0; h < phases; ++h, ++j) {
-                const int b = j & 1;
-                if (!__all_sync(kFull, tc_wait(&bars[kBarAEmpty + b], ((uint32_t) (j >> 1) & 1u) ^ 1u, abort_flag,
-                                               p.error))) {
-                    stop = true;
+            {
+                const int b = i & 1;  // the A buffer of the unit's parity
+                if (!__all_sync(kFull, tc_wait(&bars[kBarAEmpty + b], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag,
+                                               p.error)))
                     break;
-                }
                 tc_fence_after();
                 if (q6) {
-                    dequant_q6_half(raw, r, h, tmem + 128 * b + lane_off);
+                    dequant_q6_i8(raw, r, tmem + 128 * b + lane_off);
                 } else {
                     const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
                     const uint32_t mnw[2] = {scm.z, scm.w};
@@ -542,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
                     *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
                 }
-                if (h == phases - 1) mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
+                mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 tc_fence_before();
@@ -588,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             // d_x of activation row e of this unit
             auto dxe = [&](int e) { return __shfl_sync(kFull, e < 32 ? xa : xb, e & 31); };
             if (m.type == 14) {
-                // Q6_K: acc += (d_w * d_x) * (16 D_hi + D_lo)
+                // Q6_K: acc += (d_w * d_x) * (64 D_hi + D_lo), an exact int32 sum
 #pragma unroll
                 for (int c0 = 0; c0 < N; c0 += 32) {
                     constexpr int W = N < 32 ? N : 32;
@@ -603,10 +613,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     for (int hh = 0; hh < W / 16; ++hh)
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj)
-                            acc[c0 + 16 * hh + jj] = fmaf(__fmul_rn(dw.x, dxe(c0 + 16 * hh + jj)),
-                                                          fmaf(16.0f, __uint_as_float(v[hh][jj]),
-                                                               __uint_as_float(lo[hh][jj])),
-                                                          acc[c0 + 16 * hh + jj]);
+                            acc[c0 + 16 * hh + jj] =
+                                fmaf(__fmul_rn(dw.x, dxe(c0 + 16 * hh + jj)),
+                                     __int2float_rn(64 * (int) v[hh][jj] + (int) lo[hh][jj]), acc[c0 + 16 * hh + jj]);
                 }
             } else {
                 // Q4_K: 32 columns of D and of Dmin in flight per wait
@@ -666,15 +675,21 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0) {
             const uint64_t pol = l2_policy(false);
+            const bool q6 = m.type == 14;
             int i = 0;
             for (; i < nu; ++i) {
                 const int t = i % kActStages, u = u0 + i;
                 if (!tc_wait(&bars[kBarActEmpty + t], ((uint32_t) (i / kActStages) & 1u) ^ 1u, abort_flag, p.error))
                     break;
                 uint8_t * st = base + kOffAct + t * kActStage;
-                mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 32));
-                bulk_g2s(st, p.b_tiles + (cbase + u) * N * 512, N * 512, &bars[kBarActFull + t], pol);
-                bulk_g2s(st + kActB, p.bmin_tiles + (cbase + u) * N * 32, N * 32, &bars[kBarActFull + t], pol);
+                if (q6) {  // the int8 tile
+                    mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 256));
+                    bulk_g2s(st, p.b8_tiles + (cbase + u) * N * 256, N * 256, &bars[kBarActFull + t], pol);
+                } else {   // the f16 tile and the mins tile
+                    mbar_expect_tx(&bars[kBarActFull + t], (uint32_t) (N * 512 + N * 32));
+                    bulk_g2s(st, p.b_tiles + (cbase + u) * N * 512, N * 512, &bars[kBarActFull + t], pol);
+                    bulk_g2s(st + kActB, p.bmin_tiles + (cbase + u) * N * 32, N * 32, &bars[kBarActFull + t], pol);
+                }
             }
             if (*abort_flag)
                 for (int d = i > kActStages ? i - kActStages : 0; d < i; ++d)
@@ -685,55 +700,45 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
         // ---------------- tcgen05.mma issuers (warps 10, 11) ----------------
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         if (lane == 0) {
-            // fp32 D, f16 A and B, both K-major, N, M = 128
-            const uint32_t idesc = (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
+            // Q4_K: fp32 D, f16 A and B; Q6_K: s32 D, s8 A and B; both K-major, N, M = 128
             const bool q6 = m.type == 14;
-            const int phases = q6 ? 2 : 1;
-            const int which = warp - 10;
-            // Q4_K: units of this issuer's parity; Q6_K: warp 10 takes every unit
-            const int first = q6 ? (which == 0 ? 0 : nu) : which, step = q6 ? 1 : 2;
-            bool stop = false;
-            for (int i = first; i < nu && !stop; i += step) {
-                int j = phases * i;  // A phase of the unit's first half
-                const int bd = i & 1, t = i % kActStages;
+            const uint32_t idesc = q6 ? (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (N >> 3) << 17) |
+                                            ((uint32_t) (128 >> 4) << 24)
+                                      : (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
+            // the units of this issuer's parity
+            for (int i = warp - 10; i < nu; i += 2) {
+                const int b = i & 1, t = i % kActStages;
                 if (!tc_wait(&bars[kBarActFull + t], (uint32_t) (i / kActStages) & 1u, abort_flag, p.error)) break;
-                if (!tc_wait(&bars[kBarDEmpty + bd], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error)) break;
+                if (!tc_wait(&bars[kBarDEmpty + b], ((uint32_t) (i >> 1) & 1u) ^ 1u, abort_flag, p.error)) break;
+                if (!tc_wait(&bars[kBarAFull + b], (uint32_t) (i >> 1) & 1u, abort_flag, p.error)) break;
+                tc_fence_after();
                 const uint32_t bt = smem_u32(base + kOffAct + t * kActStage);
-                const uint32_t dacc = tmem + 256 + 64 * bd;
-                for (int h = 0; h < phases; ++h, ++j) {
-                    const int b = j & 1;
-                    if (!tc_wait(&bars[kBarAFull + b], (uint32_t) (j >> 1) & 1u, abort_flag, p.error)) {
-                        stop = true;
-                        break;
-                    }
-                    tc_fence_after();
-                    // descriptors: the stage's base descriptor plus constant offsets (the
-                    // address field counts 16-byte units), so the issuing thread spends
-                    // one add per MMA
-                    const uint64_t bdesc0 = sw128_desc(bt, 16, 1024);
-                    const uint32_t a0 = tmem + 128 * b;
-                    if (q6) {
-                        // half h: K positions 128h .. 128h+127, A_hi into D, A_lo into D_lo
+                const uint32_t dacc = tmem + 256 + 64 * b;
+                // descriptors: the stage's base descriptor plus constant offsets (the
+                // address field counts 16-byte units), so the issuing thread spends
+                // one add per MMA
+                const uint64_t bdesc0 = sw128_desc(bt, 16, 1024);
+                const uint32_t a0 = tmem + 128 * b;
+                if (q6) {
+                    // K 32 per MMA (32 bytes of each operand row, like K 16 of f16):
+                    // hi into D, lo into D_lo
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const int ks = 8 * h + kk;
-                            const uint64_t bdesc = bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4);
-                            mma_ts(dacc, a0 + 8 * kk, bdesc, idesc, (h | kk) != 0);
-                            mma_ts(dacc + 128, a0 + 64 + 8 * kk, bdesc, idesc, (h | kk) != 0);
-                        }
-                    } else {
-#pragma unroll
-                        for (int ks = 0; ks < 16; ++ks)
-                            mma_ts(dacc, a0 + 8 * ks, bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4),
-                                   idesc, ks != 0);
-                        mma_ss(tmem + 384 + 64 * bd, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
-                               plain_desc(bt + kActB, 128, 256), idesc, 0);
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const uint64_t bdesc = bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4);
+                        mma_ts_i8(dacc, a0 + 8 * ks, bdesc, idesc, ks != 0);
+                        mma_ts_i8(dacc + 128, a0 + 64 + 8 * ks, bdesc, idesc, ks != 0);
                     }
-                    tc_commit(&bars[kBarAEmpty + b]);
+                } else {
+#pragma unroll
+                    for (int ks = 0; ks < 16; ++ks)
+                        mma_ts(dacc, a0 + 8 * ks, bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4),
+                               idesc, ks != 0);
+                    mma_ss(tmem + 384 + 64 * b, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
+                           plain_desc(bt + kActB, 128, 256), idesc, 0);
                 }
-                if (stop) break;
+                tc_commit(&bars[kBarAEmpty + b]);
                 tc_commit(&bars[kBarActEmpty + t]);
-                tc_commit(&bars[kBarDFull + bd]);
+                tc_commit(&bars[kBarDFull + b]);
             }
             // every MMA issued (by both issuers) completes before the CTA frees TMEM
             tc_commit(&bars[kBarDrain]);
@@ -854,8 +859,11 @@ cudaError_t launch_qtc(const QtcParams & p, cudaStream_t stream, bool prequantiz
         p.n_splits < 1 || p.n_splits > kQmmMaxSplits || (int64_t) p.units_per_split * (p.n_splits - 1) >= p.n_units)
         return cudaErrorInvalidValue;
     if (p.npad != 16 && p.npad != 32 && p.npad != 64) return cudaErrorInvalidValue;
-    for (int i = 0; i < p.n_mats; ++i)
+    for (int i = 0; i < p.n_mats; ++i) {
         if (p.mats[i].n_rows % 128 != 0) return cudaErrorInvalidValue;
+        if (p.mats[i].type == 14 ? !p.b8_tiles : (!p.b_tiles || !p.bmin_tiles)) return cudaErrorInvalidValue;
+    }
+    if (!p.dx) return cudaErrorInvalidValue;
     if (!prequantized) {
         const cudaError_t e = launch_ex(qtc_act_kernel, dim3((unsigned) p.n_units, (unsigned) (p.npad * p.n_chunks / 8)),
                                         256, 0, stream, p, 1);

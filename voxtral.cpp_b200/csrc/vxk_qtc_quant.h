@@ -2,8 +2,9 @@
 // tiles (vxk_qmm_tc.cu: the quantization kernel; vxk_decoder.cu: the residual
 // + RMS norm kernel that quantizes its output rows for the next product):
 // quantize_row_q8_K_ref over one 256-column unit of one row, written as the f16
-// B tile in the product's K order, the mins B row and d_x.  Included by .cu
-// files only.
+// B tile in the product's K order and the mins B row (operands of Q4_K
+// matrices), as the int8 B tile in natural order (operands of Q6_K matrices),
+// and d_x.  Included by .cu files only.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -34,6 +35,13 @@ __device__ __forceinline__ int tc_tile_off(int n, int p, int rows) {
     return a * rows * 128 + (n >> 3) * 1024 + (n & 7) * 128 + ((((q >> 3) ^ (n & 7))) << 4) + (q & 7) * 2;
 }
 
+// Byte offset of K position k (0..255, the natural column order) of operand
+// row n in an int8 unit tile of `rows` rows: 2 atoms of 128 positions, each
+// [rows][128 B] with 128-byte swizzle.
+__device__ __forceinline__ int tc8_tile_off(int n, int k, int rows) {
+    return (k >> 7) * rows * 128 + (n >> 3) * 1024 + (n & 7) * 128 + ((((k >> 4) & 7) ^ (n & 7)) << 4) + (k & 15);
+}
+
 // Columns of a unit that lane L holds: x[0..3] = eA .. eA + 3 and x[4..7] =
 // eB .. eB + 3, eA = 64 (L / 8) + 4 (L % 8), eB = eA + 32, i.e. the elements of
 // K positions 8L .. 8L + 7 (tc_position), so the lane's tile chunk is one
@@ -43,12 +51,15 @@ __device__ __forceinline__ int qtc_lane_col_a(int lane) { return 64 * (lane >> 3
 // One warp quantizes row r (of np padded rows) of one unit like
 // quantize_row_q8_K_ref: iscale = -127 / (the value of largest magnitude,
 // first column on ties), q = min(127, round-half-even(iscale x)), d = 1 /
-// iscale (0 and all-zero q for a zero row).  Writes the lane's 16-byte chunk of
-// the f16 tile (unit tile base `tile`), the row's mins B entries (the sums s_j
-// of sub-blocks j = 2g, 2g + 1 as (l_j, h_j), s_j = 128 h_j + l_j; unit mins
-// base `bmin`) and, from lane 0, *dx = d.  Every lane of the warp calls it.
+// iscale (0 and all-zero q for a zero row).  Writes, when `tile` is given
+// (operands of Q4_K matrices), the lane's 16-byte chunk of the f16 tile (unit
+// tile base) and the row's mins B entries (the sums s_j of sub-blocks j = 2g,
+// 2g + 1 as (l_j, h_j), s_j = 128 h_j + l_j; unit mins base `bmin`); when
+// `tile8` is given (operands of Q6_K matrices), the lane's two 4-byte words of
+// the int8 tile in natural column order; and, from lane 0, *dx = d.  Every
+// lane of the warp calls it.
 __device__ __forceinline__ void qtc_quantize_unit(const float (&x)[8], int lane, int r, int np, uint8_t * tile,
-                                                  uint8_t * bmin, float * dx) {
+                                                  uint8_t * bmin, uint8_t * tile8, float * dx) {
     constexpr unsigned kAll = 0xffffffffu;
     const int g = lane >> 3;
     const int eA = qtc_lane_col_a(lane), eB = eA + 32;
@@ -84,6 +95,16 @@ __device__ __forceinline__ void qtc_quantize_unit(const float (&x)[8], int lane,
         for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, x[i])));
         d = __fdiv_rn(1.0f, iscale);
     }
+    if (tile8) {
+        auto b4 = [](int a, int b, int c, int d) {
+            return (uint32_t) (a & 0xff) | ((uint32_t) (b & 0xff) << 8) | ((uint32_t) (c & 0xff) << 16) |
+                   ((uint32_t) (d & 0xff) << 24);
+        };
+        *reinterpret_cast<uint32_t *>(tile8 + tc8_tile_off(r, eA, np)) = b4(q[0], q[1], q[2], q[3]);
+        *reinterpret_cast<uint32_t *>(tile8 + tc8_tile_off(r, eB, np)) = b4(q[4], q[5], q[6], q[7]);
+    }
+    if (lane == 0) *dx = d;
+    if (!tile) return;
     // positions 8L + s hold elements A0, A2, B0, B2, A1, A3, B1, B3 (tc_position)
     auto h2 = [](int lo, int hi) {
         const __half2 v = __halves2half2(__int2half_rn(lo), __int2half_rn(hi));
@@ -107,7 +128,6 @@ __device__ __forceinline__ void qtc_quantize_unit(const float (&x)[8], int lane,
         *reinterpret_cast<__half *>(mrow + (2 * g + 1) * 2) = __int2half_rn(sb & 127);
         *reinterpret_cast<__half *>(mrow + 128 + (2 * g + 1) * 2) = __int2half_rn(sb >> 7);
     }
-    if (lane == 0) *dx = d;
 }
 
 }  // namespace vxk

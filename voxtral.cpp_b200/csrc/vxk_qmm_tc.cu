@@ -10,10 +10,10 @@
 // quantized activations (|q8| <= 127); the fp32 accumulator of one 256-column
 // unit then holds d-free sum_j sc_j * sum q4*q8 exactly (well below 2^24).
 // Q6_K's scaled quants p = sc*q reach 4096, past f16's exact integers; they
-// become two int8 operands, hi = floor(p / 64) and lo = p mod 64, multiplied
-// by the int8 activations in kind::i8 MMAs (K = 32, int32 accumulators) that
-// the epilogue combines as 64 D_hi + D_lo, an exact int32 sum (the
-// activation tiles of Q6_K matrices are int8).
+// become two 8-bit operands, hi = floor(p / 64) (s8) and 4 (p mod 64) (u8),
+// multiplied by the int8 activations in kind::i8 MMAs (K = 32, int32
+// accumulators) that the epilogue combines as 64 D_hi + D_lo / 4, an exact
+// int32 sum (the activation tiles of Q6_K matrices are int8).
 // Q4_K's mins term sum_j m_j * s_j (s_j = sums of 32 quantized activations)
 // is one more K = 16 product: A = (m_0..m_7, 128 m_0..128 m_7), B = (l_0..l_7,
 // h_0..h_7) with s_j = 128 h_j + l_j.  Per unit the epilogue applies
@@ -354,64 +354,63 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
 }
 
 // A Q6_K unit of row r into TMEM as int8 operands of kind::i8 MMAs: p = q sc
-// (q = q6 - 32, sc the int8 sub-block scale, |p| <= 4096) is split as p =
-// 64 hi + lo with hi = floor(p / 64) in [-64, 64] and lo = p mod 64 in [0, 64),
-// hi at columns [abase, abase + 64) and lo at [abase + 64, abase + 128); column t
-// holds K positions 4t .. 4t + 3, the unit's elements in natural order.  Two
-// elements of one sub-block sit in the 16-bit halves of a word (the 6-bit
-// quants at the bytes l and l + 2 of the low-nibble and high-plane words), so
-// one 32-bit multiply-add forms both (p + 8192, always in [4128, 12288]: no
-// carry between the halves); bits 6..13 of each half are hi + 128 and bits
-// 0..5 are lo, and a byte permute gathers four of each into a word (hi + 128
-// turned into the int8 hi by flipping bit 7).
+// (q = q6 - 32, sc the int8 scale of the 16-quant sub-block, |p| <= 4096) is
+// split as p = 64 hi + lo with hi = floor(p / 64) in [-64, 64] (s8) and lo =
+// p mod 64, stored as 4 lo (u8), hi at columns [abase, abase + 64) and 4 lo at
+// [abase + 64, abase + 128); column t holds K positions 4t .. 4t + 3, the
+// unit's elements in natural order.  The record holds sub-block g as words X,
+// Y (low nibbles, slots paired by a shift of 4j) and Z (high parts, paired by a
+// rotation of 4j or 4j + 2; see repack_q6k_tc): a pair word carries two 6-bit
+// quants v in its 16-bit halves, and one 32-bit multiply-add forms both
+// 4 p + 32768 = 4 (v - 32) sc + 32768 in [16512, 49152] (no carry between the
+// halves), whose high byte is hi + 128 and low byte 4 lo; byte permutes gather
+// four of each into a word (hi + 128 turned into hi by flipping bit 7).
 __device__ __forceinline__ void dequant_q6_i8(const uint8_t * raw, int r, uint32_t abase) {
-    const uint8_t * ql = raw + r * 128;
-    const uint8_t * qh = raw + 16384 + r * 64;
+    const uint8_t * xy = raw + r * 128;
+    const uint8_t * zz = raw + 16384 + r * 64;
     const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    uint4 Zc[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        uint4 A[2], B[2], H[2];
+    for (int c = 0; c < 4; ++c) Zc[c] = *reinterpret_cast<const uint4 *>(zz + ((c ^ ((r >> 1) & 3)) << 4));
 #pragma unroll
-        for (int c4 = 0; c4 < 2; ++c4) {
-            A[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + c4) ^ (r & 7)) << 4));
-            B[c4] = *reinterpret_cast<const uint4 *>(ql + (((4 * h + 2 + c4) ^ (r & 7)) << 4));
-            H[c4] = *reinterpret_cast<const uint4 *>(qh + (((2 * h + c4) ^ ((r >> 1) & 3)) << 4));
-        }
-        uint32_t hi[32], lo[32];  // words t - 32 h of this half
+    for (int half = 0; half < 2; ++half) {
+        uint32_t hi[32], lo[32];  // columns 32 half + t
 #pragma unroll
-        for (int gg = 0; gg < 2; ++gg) {
+        for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * half + cc;  // X, Y chunk: sub-blocks 2c, 2c + 1
+            const uint4 v = *reinterpret_cast<const uint4 *>(xy + ((c ^ (r & 7)) << 4));
 #pragma unroll
-            for (int c4 = 0; c4 < 2; ++c4) {
-                // elements 128h + 64gg + 16c4 + (0..15) (part a, scale ia) and + 32 (part b, ia + 2)
-                const int ia = 8 * h + 4 * gg + c4, ib = ia + 2;
-                const int sa = (int) (int8_t) (scw[ia >> 2] >> (8 * (ia & 3)));
-                const int sb = (int) (int8_t) (scw[ib >> 2] >> (8 * (ib & 3)));
-                const uint32_t ca = (uint32_t) (8192 - 32 * sa) * 0x00010001u;
-                const uint32_t cb = (uint32_t) (8192 - 32 * sb) * 0x00010001u;
-                const uint32_t aw[4] = {A[c4].x, A[c4].y, A[c4].z, A[c4].w};
-                const uint32_t bw[4] = {B[c4].x, B[c4].y, B[c4].z, B[c4].w};
-                const uint32_t hw[4] = {H[c4].x, H[c4].y, H[c4].z, H[c4].w};
+            for (int s2 = 0; s2 < 2; ++s2) {
+                const int g = 2 * c + s2;
+                const uint32_t X = s2 ? v.z : v.x, Y = s2 ? v.w : v.y;
+                const uint4 zq = Zc[g >> 2];
+                const uint32_t Z = (g & 3) == 0 ? zq.x : (g & 3) == 1 ? zq.y : (g & 3) == 2 ? zq.z : zq.w;
+                const int sc = (int) (int8_t) (scw[g >> 2] >> (8 * (g & 3)));
+                const uint32_t m4 = (uint32_t) (4 * sc);
+                const uint32_t c4 = (uint32_t) (32768 - 128 * sc) * 0x00010001u;
+                uint32_t rx[4], ry[4];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int ns = 4 * gg, fa = 4 * gg, fb = 4 * gg + 2;
-                    // 6-bit quants of positions (l, l + 2) and (l + 1, l + 3), l = 16 c4 + 4 k
-                    const uint32_t a02 = ((aw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fa) & 0x00030003u) << 4);
-                    const uint32_t a13 = ((aw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fa + 8)) & 0x00030003u) << 4);
-                    const uint32_t b02 = ((bw[k] >> ns) & 0x000F000Fu) | (((hw[k] >> fb) & 0x00030003u) << 4);
-                    const uint32_t b13 = ((bw[k] >> (ns + 8)) & 0x000F000Fu) | (((hw[k] >> (fb + 8)) & 0x00030003u) << 4);
-                    const uint32_t pa02 = a02 * (uint32_t) sa + ca, pa13 = a13 * (uint32_t) sa + ca;
-                    const uint32_t pb02 = b02 * (uint32_t) sb + cb, pb13 = b13 * (uint32_t) sb + cb;
-                    const int ta = 16 * gg + 4 * c4 + k, tb = ta + 8;
-                    hi[ta] = __byte_perm(pa02 >> 6, pa13 >> 6, 0x6240) ^ 0x80808080u;
-                    lo[ta] = __byte_perm(pa02, pa13, 0x6240) & 0x3F3F3F3Fu;
-                    hi[tb] = __byte_perm(pb02 >> 6, pb13 >> 6, 0x6240) ^ 0x80808080u;
-                    lo[tb] = __byte_perm(pb02, pb13, 0x6240) & 0x3F3F3F3Fu;
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t px = ((X >> (4 * j)) & 0x000F000Fu) | (__funnelshift_r(Z, Z, 4 * j) & 0x00300030u);
+                    const uint32_t py = ((Y >> (4 * j)) & 0x000F000Fu) | (__funnelshift_r(Z, Z, 4 * j + 2) & 0x00300030u);
+                    rx[j] = px * m4 + c4;
+                    ry[j] = py * m4 + c4;
                 }
+                // pair words (e0, e2), (e1, e3), (e4, e6), (e5, e7) of each half of the sub-block
+                const int t = 4 * (g & 7);
+                hi[t + 0] = __byte_perm(rx[0], rx[1], 0x7351) ^ 0x80808080u;
+                hi[t + 1] = __byte_perm(rx[2], rx[3], 0x7351) ^ 0x80808080u;
+                hi[t + 2] = __byte_perm(ry[0], ry[1], 0x7351) ^ 0x80808080u;
+                hi[t + 3] = __byte_perm(ry[2], ry[3], 0x7351) ^ 0x80808080u;
+                lo[t + 0] = __byte_perm(rx[0], rx[1], 0x6240);
+                lo[t + 1] = __byte_perm(rx[2], rx[3], 0x6240);
+                lo[t + 2] = __byte_perm(ry[0], ry[1], 0x6240);
+                lo[t + 3] = __byte_perm(ry[2], ry[3], 0x6240);
             }
         }
-        tmem_st32(abase + 32 * h, hi);
-        tmem_st32(abase + 64 + 32 * h, lo);
+        tmem_st32(abase + 32 * half, hi);
+        tmem_st32(abase + 64 + 32 * half, lo);
     }
 }
 
@@ -598,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             // d_x of activation row e of this unit
             auto dxe = [&](int e) { return __shfl_sync(kFull, e < 32 ? xa : xb, e & 31); };
             if (m.type == 14) {
-                // Q6_K: acc += (d_w * d_x) * (64 D_hi + D_lo), an exact int32 sum
+                // Q6_K: acc += (d_w * d_x) * (64 D_hi + D_lo / 4), an exact int32 sum
 #pragma unroll
                 for (int c0 = 0; c0 < N; c0 += 32) {
                     constexpr int W = N < 32 ? N : 32;
@@ -615,7 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         for (int jj = 0; jj < 16; ++jj)
                             acc[c0 + 16 * hh + jj] =
                                 fmaf(__fmul_rn(dw.x, dxe(c0 + 16 * hh + jj)),
-                                     __int2float_rn(64 * (int) v[hh][jj] + (int) lo[hh][jj]), acc[c0 + 16 * hh + jj]);
+                                     __int2float_rn(64 * (int) v[hh][jj] + ((int) lo[hh][jj] >> 2)),
+                                     acc[c0 + 16 * hh + jj]);
                 }
             } else {
                 // Q4_K: 32 columns of D and of Dmin in flight per wait
@@ -705,6 +705,8 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             const uint32_t idesc = q6 ? (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (N >> 3) << 17) |
                                             ((uint32_t) (128 >> 4) << 24)
                                       : (1u << 4) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
+            // Q6_K's 4 lo operand is unsigned (u8 A, s8 B)
+            const uint32_t idesc_lo = idesc & ~(1u << 7);
             // the units of this issuer's parity
             for (int i = warp - 10; i < nu; i += 2) {
                 const int b = i & 1, t = i % kActStages;
@@ -726,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     for (int ks = 0; ks < 8; ++ks) {
                         const uint64_t bdesc = bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4);
                         mma_ts_i8(dacc, a0 + 8 * ks, bdesc, idesc, ks != 0);
-                        mma_ts_i8(dacc + 128, a0 + 64 + 8 * ks, bdesc, idesc, ks != 0);
+                        mma_ts_i8(dacc + 128, a0 + 64 + 8 * ks, bdesc, idesc_lo, ks != 0);
                     }
                 } else {
 #pragma unroll

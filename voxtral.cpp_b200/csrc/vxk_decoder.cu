@@ -166,12 +166,19 @@ __global__ void __launch_bounds__(1024) add_norm_quant_kernel(NormParams p) {
     const int c0 = 256 * u + qtc_lane_col_a(lane), c1 = c0 + 32;
     float y[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
     const bool live = r < p.n_rows;
-    float4 v[2];
+    float4 v[2], wv[2], av[2];
     double sum = 0.0;
     if (live) {
         float * xr = p.x + (int64_t) r * p.dim;
         v[0] = *reinterpret_cast<const float4 *>(xr + c0);
         v[1] = *reinterpret_cast<const float4 *>(xr + c1);
+        // the norm weights (and time scale) are loaded with the row, before the reduction
+        wv[0] = *reinterpret_cast<const float4 *>(p.w + c0);
+        wv[1] = *reinterpret_cast<const float4 *>(p.w + c1);
+        if (p.ada) {
+            av[0] = *reinterpret_cast<const float4 *>(p.ada + c0);
+            av[1] = *reinterpret_cast<const float4 *>(p.ada + c1);
+        }
         if (p.add) {
             const float * ar = p.add + (int64_t) r * p.dim;
             float4 a[2] = {*reinterpret_cast<const float4 *>(ar + c0), *reinterpret_cast<const float4 *>(ar + c1)};
@@ -214,18 +221,16 @@ __global__ void __launch_bounds__(1024) add_norm_quant_kernel(NormParams p) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int c = h ? c1 : c0;
-            const float4 wv = *reinterpret_cast<const float4 *>(p.w + c);
             float4 o;
-            o.x = __fmul_rn(__fmul_rn(v[h].x, scale), wv.x);
-            o.y = __fmul_rn(__fmul_rn(v[h].y, scale), wv.y);
-            o.z = __fmul_rn(__fmul_rn(v[h].z, scale), wv.z);
-            o.w = __fmul_rn(__fmul_rn(v[h].w, scale), wv.w);
+            o.x = __fmul_rn(__fmul_rn(v[h].x, scale), wv[h].x);
+            o.y = __fmul_rn(__fmul_rn(v[h].y, scale), wv[h].y);
+            o.z = __fmul_rn(__fmul_rn(v[h].z, scale), wv[h].z);
+            o.w = __fmul_rn(__fmul_rn(v[h].w, scale), wv[h].w);
             if (p.ada) {
-                const float4 av = *reinterpret_cast<const float4 *>(p.ada + c);
-                o.x = __fadd_rn(o.x, __fmul_rn(o.x, av.x));
-                o.y = __fadd_rn(o.y, __fmul_rn(o.y, av.y));
-                o.z = __fadd_rn(o.z, __fmul_rn(o.z, av.z));
-                o.w = __fadd_rn(o.w, __fmul_rn(o.w, av.w));
+                o.x = __fadd_rn(o.x, __fmul_rn(o.x, av[h].x));
+                o.y = __fadd_rn(o.y, __fmul_rn(o.y, av[h].y));
+                o.z = __fadd_rn(o.z, __fmul_rn(o.z, av[h].z));
+                o.w = __fadd_rn(o.w, __fmul_rn(o.w, av[h].w));
             }
             if (p.out) *reinterpret_cast<float4 *>(p.out + (int64_t) r * p.dim + c) = o;
             y[4 * h + 0] = o.x;

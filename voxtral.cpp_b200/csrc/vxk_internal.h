@@ -296,13 +296,13 @@ struct QmmParams {
 // [128 rows][128 quant bytes, 16-byte chunk c at c ^ (row % 8)] then
 // [128 rows][6-bit scales[8], mins[8]]; (d, dmin) f16 pairs in a separate
 // [blocks][units][128 rows] array read by the epilogue.
-// Q6_K: [128 rows][128 bytes: per 16-quant sub-block g the low-nibble words
-// X_g, Y_g, chunk c = (X_2c, Y_2c, X_2c+1, Y_2c+1) at c ^ (row % 8)], then
-// [128 rows][64 bytes: the high-part words Z_g, chunk c = Z_4c..Z_4c+3 at
-// c ^ ((row / 2) % 4)], then [128 rows][16 int8 scales]; `dd` holds (d, 0)
-// (slot order of the words: repack_q6k_tc).
+// Q6_K: [128 rows][256 bytes: the 6-bit quants q6 = q + 32, one per byte in
+// column order, 16-byte chunk c at c ^ (row % 8)], then [128 rows][16 int8
+// scales]; `dd` holds (d, 0).  One byte per quant (30% more than GGUF's
+// 210 bytes per 256) so that forming the tensor-core operands takes no bit
+// unpacking; the product is bound by that arithmetic, not by HBM.
 constexpr int kQtcRecordBytes = 128 * 128 + 128 * 16;
-constexpr int kQtcRecordBytesQ6K = 128 * 128 + 128 * 64 + 128 * 16;
+constexpr int kQtcRecordBytesQ6K = 128 * 256 + 128 * 16;
 
 struct QtcMat {
     const uint8_t * w;         // records [n_rows / 128][n_units][record bytes of the type]

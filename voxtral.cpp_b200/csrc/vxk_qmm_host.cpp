@@ -184,21 +184,13 @@ void repack_record(int type, const uint8_t * src, int64_t row_bytes, int64_t til
 int nt_for(int32_t rows) { return rows <= 8 ? 1 : rows <= 16 ? 2 : rows <= 32 ? 4 : 8; }
 
 // Q6_K rows -> the tcgen05 layout (vxk_internal.h, kQtcRecordBytesQ6K): per
-// 128-row block and unit, each row's 16 sub-blocks g of 16 quants as three
-// words: X_g and Y_g hold the low nibbles of elements 16g + 0..7 and 16g +
-// 8..15, element i of a half in nibble slot kQ6Slot[i] (so that shifting the
-// word by 4j and masking 0x000F000F pairs the elements a 16-bit multiply pairs
-// with their neighbours); Z_g holds the 2-bit high parts, X's slot s at bit
-// (4 + 4s) mod 32 and Y's at (6 + 4s) mod 32 (so that rotating Z by 4j or 4j + 2
-// puts a pair's high parts right above its nibbles).  The X, Y words fill 128
-// bytes (chunk c = X_2c, Y_2c, X_2c+1, Y_2c+1 at c ^ (row % 8)), the Z words 64
-// (chunk c = Z_4c .. Z_4c+3 at c ^ ((row / 2) % 4)), then the 16 int8 scales;
-// (d, 0) pairs to `dd`.  The quant of element e of a GGUF block: low nibble of
+// 128-row block and unit, each row's 256 6-bit quants one per byte in column
+// order (16-byte chunk c at c ^ (row % 8)), then its 16 int8 scales; (d, 0)
+// pairs to `dd`.  The quant of element e of a GGUF block: low nibble of
 // ql[64h + l] (parts 0, 1 of half h = e / 128, l = e % 32, part = (e / 32) % 4:
 // ql[64h + 32 + l] for parts 1 and 3, high nibble for parts 2 and 3), high bits
 // (qh[32h + l] >> 2 part) & 3.
 void repack_q6k_tc(const uint8_t * src, int32_t n_rows, int32_t n_cols, uint8_t * rec, uint8_t * dd) {
-    static const int kQ6Slot[8] = {0, 1, 4, 5, 2, 3, 6, 7};
     const int64_t units = n_cols / vxk::kQmmUnit;
     const int64_t rb = gguf_row_bytes(VXK_QTYPE_Q6_K, n_cols);
     for (int64_t b = 0; b < n_rows / 128; ++b)
@@ -209,28 +201,17 @@ void repack_q6k_tc(const uint8_t * src, int32_t n_rows, int32_t n_cols, uint8_t 
                 const uint8_t * blk = src + (b * 128 + r) * rb + u * 210;
                 const uint8_t * ql = blk;
                 const uint8_t * qh = blk + 128;
-                uint32_t X[16] = {}, Y[16] = {}, Z[16] = {};
+                uint8_t q6[256];
                 for (int e = 0; e < 256; ++e) {
                     const int h = e >> 7, part = (e >> 5) & 3, l = e & 31;
                     const uint8_t qb = ql[64 * h + 32 * (part & 1) + l];
-                    const uint32_t lo = part < 2 ? (qb & 15u) : (uint32_t) (qb >> 4);
-                    const uint32_t hi = (qh[32 * h + l] >> (2 * part)) & 3u;
-                    const int g = e >> 4, i = e & 15, slot = kQ6Slot[i & 7];
-                    if (i < 8) {
-                        X[g] |= lo << (4 * slot);
-                        Z[g] |= hi << ((4 + 4 * slot) & 31);
-                    } else {
-                        Y[g] |= lo << (4 * slot);
-                        Z[g] |= hi << ((6 + 4 * slot) & 31);
-                    }
+                    const int lo = part < 2 ? (qb & 15) : (qb >> 4);
+                    const int hi = (qh[32 * h + l] >> (2 * part)) & 3;
+                    q6[e] = (uint8_t) (lo | (hi << 4));
                 }
-                for (int c = 0; c < 8; ++c) {
-                    const uint32_t w[4] = {X[2 * c], Y[2 * c], X[2 * c + 1], Y[2 * c + 1]};
-                    std::memcpy(out + r * 128 + ((c ^ (r & 7)) << 4), w, 16);
-                }
-                for (int c = 0; c < 4; ++c)
-                    std::memcpy(out + 16384 + r * 64 + ((c ^ ((r >> 1) & 3)) << 4), Z + 4 * c, 16);
-                std::memcpy(out + 24576 + r * 16, blk + 192, 16);
+                for (int c = 0; c < 16; ++c)
+                    std::memcpy(out + r * 256 + ((c ^ (r & 7)) << 4), q6 + 16 * c, 16);
+                std::memcpy(out + 32768 + r * 16, blk + 192, 16);
                 std::memcpy(d + r * 4, blk + 208, 2);
                 d[r * 4 + 2] = d[r * 4 + 3] = 0;
             }

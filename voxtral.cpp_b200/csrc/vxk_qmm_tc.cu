@@ -62,7 +62,7 @@ constexpr int kRawBytes = kQtcRecordBytesQ6K;                      // ring stage
 constexpr int kActB = kMaxN * 512;                                  // f16 B tile, 4 SW128 atoms
 constexpr int kActBMin = kMaxN * 32;                                // mins B tile, 32 B per row (no swizzle)
 constexpr int kActStage = kActB + kActBMin;
-constexpr int kAMin = 128 * 128;                                    // mins A tile
+constexpr int kAMin = 128 * 32;                                     // mins A tile, 32 B per row (no swizzle)
 constexpr int kOffRaw = 0;
 constexpr int kOffAct = kOffRaw + kRawStages * kRawBytes;
 constexpr int kOffAMin = kOffAct + kActStages * kActStage;
@@ -83,7 +83,7 @@ constexpr int kSmem = kOffMisc + 16 + 1024;            // + alignment slack
 static_assert(kSmem <= 232448, "tcgen05 quantized product exceeds 227 KB of shared memory");
 static_assert(kActStages == 2, "the two MMA issuers split the units by parity");
 static_assert(kRawStages * kRawBytes >= kMaxN * 128 * 4, "the reduction tile fits the raw ring");
-static_assert(kOffAct % 1024 == 0 && kOffAMin % 1024 == 0 && kActStage % 1024 == 0, "128-byte swizzle atoms align");
+static_assert(kOffAct % 1024 == 0 && kActStage % 1024 == 0, "128-byte swizzle atoms align");
 // TMEM columns: A[b] 0..255 (128 each), D[b] 256..383, Dmin[b] (Q6_K: D_lo[b]) 384..511
 constexpr int kTmemCols = 512;
 
@@ -358,55 +358,34 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
 // split as p = 64 hi + lo with hi = floor(p / 64) in [-64, 64] (s8) and lo =
 // p mod 64, stored as 4 lo (u8), hi at columns [abase, abase + 64) and 4 lo at
 // [abase + 64, abase + 128); column t holds K positions 4t .. 4t + 3, the
-// unit's elements in natural order.  The record holds sub-block g as words X,
-// Y (low nibbles, slots paired by a shift of 4j) and Z (high parts, paired by a
-// rotation of 4j or 4j + 2; see repack_q6k_tc): a pair word carries two 6-bit
-// quants v in its 16-bit halves, and one 32-bit multiply-add forms both
-// 4 p + 32768 = 4 (v - 32) sc + 32768 in [16512, 49152] (no carry between the
-// halves), whose high byte is hi + 128 and low byte 4 lo; byte permutes gather
-// four of each into a word (hi + 128 turned into hi by flipping bit 7).
+// unit's elements in natural order.  The record holds one quant q6 per byte: a
+// mask and a byte permute put the bytes (0, 2) and (1, 3) of a word in the
+// 16-bit halves of two pair words, and one 32-bit multiply-add per pair word
+// forms both 4 p + 32768 = 4 (q6 - 32) sc + 32768 in [16512, 49152] (no carry
+// between the halves), whose high byte is hi + 128 and low byte 4 lo; byte
+// permutes gather four of each into a word (hi + 128 turned into hi by
+// flipping bit 7).
 __device__ __forceinline__ void dequant_q6_i8(const uint8_t * raw, int r, uint32_t abase) {
-    const uint8_t * xy = raw + r * 128;
-    const uint8_t * zz = raw + 16384 + r * 64;
-    const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 24576 + r * 16);
+    const uint8_t * qrow = raw + r * 256;
+    const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 32768 + r * 16);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-    uint4 Zc[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) Zc[c] = *reinterpret_cast<const uint4 *>(zz + ((c ^ ((r >> 1) & 3)) << 4));
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
         uint32_t hi[32], lo[32];  // columns 32 half + t
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-            const int c = 4 * half + cc;  // X, Y chunk: sub-blocks 2c, 2c + 1
-            const uint4 v = *reinterpret_cast<const uint4 *>(xy + ((c ^ (r & 7)) << 4));
+        for (int cc = 0; cc < 8; ++cc) {
+            const int g = 8 * half + cc;  // sub-block g: chunk g, elements 16g .. 16g + 15
+            const uint4 v = *reinterpret_cast<const uint4 *>(qrow + ((g ^ (r & 7)) << 4));
+            const int sc = (int) (int8_t) (scw[g >> 2] >> (8 * (g & 3)));
+            const uint32_t m4 = (uint32_t) (4 * sc);
+            const uint32_t c4 = (uint32_t) (32768 - 128 * sc) * 0x00010001u;
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int s2 = 0; s2 < 2; ++s2) {
-                const int g = 2 * c + s2;
-                const uint32_t X = s2 ? v.z : v.x, Y = s2 ? v.w : v.y;
-                const uint4 zq = Zc[g >> 2];
-                const uint32_t Z = (g & 3) == 0 ? zq.x : (g & 3) == 1 ? zq.y : (g & 3) == 2 ? zq.z : zq.w;
-                const int sc = (int) (int8_t) (scw[g >> 2] >> (8 * (g & 3)));
-                const uint32_t m4 = (uint32_t) (4 * sc);
-                const uint32_t c4 = (uint32_t) (32768 - 128 * sc) * 0x00010001u;
-                uint32_t rx[4], ry[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t px = ((X >> (4 * j)) & 0x000F000Fu) | (__funnelshift_r(Z, Z, 4 * j) & 0x00300030u);
-                    const uint32_t py = ((Y >> (4 * j)) & 0x000F000Fu) | (__funnelshift_r(Z, Z, 4 * j + 2) & 0x00300030u);
-                    rx[j] = px * m4 + c4;
-                    ry[j] = py * m4 + c4;
-                }
-                // pair words (e0, e2), (e1, e3), (e4, e6), (e5, e7) of each half of the sub-block
-                const int t = 4 * (g & 7);
-                hi[t + 0] = __byte_perm(rx[0], rx[1], 0x7351) ^ 0x80808080u;
-                hi[t + 1] = __byte_perm(rx[2], rx[3], 0x7351) ^ 0x80808080u;
-                hi[t + 2] = __byte_perm(ry[0], ry[1], 0x7351) ^ 0x80808080u;
-                hi[t + 3] = __byte_perm(ry[2], ry[3], 0x7351) ^ 0x80808080u;
-                lo[t + 0] = __byte_perm(rx[0], rx[1], 0x6240);
-                lo[t + 1] = __byte_perm(rx[2], rx[3], 0x6240);
-                lo[t + 2] = __byte_perm(ry[0], ry[1], 0x6240);
-                lo[t + 3] = __byte_perm(ry[2], ry[3], 0x6240);
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t r02 = (w[k] & 0x00FF00FFu) * m4 + c4;           // elements 4k, 4k + 2
+                const uint32_t r13 = __byte_perm(w[k], 0u, 0x4341) * m4 + c4;  // elements 4k + 1, 4k + 3
+                hi[4 * cc + k] = __byte_perm(r02, r13, 0x7351) ^ 0x80808080u;
+                lo[4 * cc + k] = __byte_perm(r02, r13, 0x6240);
             }
         }
         tmem_st32(abase + 32 * half, hi);
@@ -538,8 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         }
                         tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
                     }
-                    // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact)
-                    uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 1024 + (r & 7) * 128;
+                    // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact); unswizzled
+                    // K-major core matrices: row group r / 8 at 256 B, K half at 128 B, row r % 8 at 16 B
+                    uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 256 + (r & 7) * 16;
                     uint32_t m0[4], m1[4];
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj) {
@@ -548,8 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         m0[jj] = h2_bits(__floats2half2_rn(a0, a1));
                         m1[jj] = h2_bits(__floats2half2_rn(128.0f * a0, 128.0f * a1));
                     }
-                    *reinterpret_cast<uint4 *>(amin + ((0 ^ (r & 7)) << 4)) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
-                    *reinterpret_cast<uint4 *>(amin + ((1 ^ (r & 7)) << 4)) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
+                    *reinterpret_cast<uint4 *>(amin) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
+                    *reinterpret_cast<uint4 *>(amin + 128) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
                 }
                 mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -735,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     for (int ks = 0; ks < 16; ++ks)
                         mma_ts(dacc, a0 + 8 * ks, bdesc0 + (uint64_t) (((ks >> 2) * N * 128 + (ks & 3) * 32) >> 4),
                                idesc, ks != 0);
-                    mma_ss(tmem + 384 + 64 * b, sw128_desc(smem_u32(base + kOffAMin + b * kAMin), 16, 1024),
+                    mma_ss(tmem + 384 + 64 * b, plain_desc(smem_u32(base + kOffAMin + b * kAMin), 128, 256),
                            plain_desc(bt + kActB, 128, 256), idesc, 0);
                 }
                 tc_commit(&bars[kBarAEmpty + b]);

@@ -526,7 +526,11 @@ VXK_API vxk_status vxk_qweight_repack(vxk_qtype type, int32_t n_rows, int32_t n_
                                       size_t gguf_bytes, void * out, size_t out_bytes);
 
 /** Repacks the host GGUF rows (n_rows x row bytes, ggml row order) and
- *  uploads them; allocates the product scratch for max_batch rows. */
+ *  uploads them; allocates the product scratch for max_batch rows.  Q4_K and
+ *  Q6_K matrices whose n_rows is a multiple of 128 also keep the layout of the
+ *  tensor-core product used from 17 rows (128-row x 256-column records: Q4_K
+ *  1.03x and Q6_K 1.31x their GGUF bytes with the block scale pairs, Q6_K
+ *  holding one quant per byte). */
 VXK_API vxk_status vxk_qweight_create(const vxk_qweight_config * config, const void * gguf_blocks,
                                       size_t gguf_bytes, vxk_qweight ** out);
 VXK_API void vxk_qweight_destroy(vxk_qweight * w);

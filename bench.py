@@ -136,7 +136,8 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    ms = max_over_ranks(dist, ms, "cuda")
+    rank_ms = gather_over_ranks(dist, ms, "cuda")
+    ms = max(rank_ms)
     keys = W + P - 1  # union of the chunk's windows
     eb = 4 if cfg["dtype"] == 0 else 2  # ring value bytes (f32 or 16-bit)
     per_stream_layer = keys * H * HDE * eb * 2 + 3 * P * H * HDE * 4 + P * H * HDE * 4 + 2 * P * H * HDE * eb
@@ -235,6 +236,7 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
             "gpu_launches": int(args.steps * L * (2 if cfg["dtype"] == 0 else 1)),
             "clocks": clocks.summary(),
         }
+        line.update(rank_fields(rank_ms))
         print(json.dumps(line), flush=True)
     pool.close()
 
@@ -277,7 +279,8 @@ def run_head(args, cfg, world, rank, local, dist, torch, vxk):
         e1.record(stream)
         torch.cuda.synchronize()
     head.sync(sh)
-    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    rank_ms = gather_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    ms = max(rank_ms)
     step_s = ms / 1000.0 / args.steps
     bytes_per_step = V * D * 2 + R * D * 4 + R * V * 4 + R * 4  # W once, x, logits, argmax
     achieved = bytes_per_step / step_s / 1e9
@@ -341,6 +344,7 @@ def run_head(args, cfg, world, rank, local, dist, torch, vxk):
             "gpu_launches": int(args.steps * 3),
             "clocks": clocks.summary(),
         }
+        line.update(rank_fields(rank_ms))
         print(json.dumps(line), flush=True)
     head.close()
 
@@ -413,7 +417,8 @@ def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
     for layer in mats:
         for m in layer.values():
             m.sync(sh)
-    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    rank_ms = gather_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    ms = max(rank_ms)
     step_s = ms / 1000.0 / args.steps
     w_bytes = L * sum(qmm_gguf_bytes(n, k, t) for _, n, k, t in cfg["mats"])
     # x read once for q/k/v (one quantization per group), the attention rows once, every output once
@@ -485,6 +490,7 @@ def run_qmm(args, cfg, world, rank, local, dist, torch, vxk):
                       "vxk_qweight_matmul for o), replayed per step",
             "clocks": clocks.summary(),
         }
+        line.update(rank_fields(rank_ms))
         print(json.dumps(line), flush=True)
     for layer in mats:
         for m in layer.values():
@@ -559,7 +565,8 @@ def run_headq(args, cfg, world, rank, local, dist, torch, vxk):
         torch.cuda.synchronize()
     qw.sync(sh)
     head.sync(sh)
-    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    rank_ms = gather_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    ms = max(rank_ms)
     step_s = ms / 1000.0 / args.steps
     bytes_per_step = qmm_gguf_bytes(V, D, t) + R * D * 4 + R * V * 4 + R * 4  # W once, x, logits, argmax
     achieved = bytes_per_step / step_s / 1e9
@@ -622,6 +629,7 @@ def run_headq(args, cfg, world, rank, local, dist, torch, vxk):
             "gpu_launches": int(args.steps * 4),
             "clocks": clocks.summary(),
         }
+        line.update(rank_fields(rank_ms))
         print(json.dumps(line), flush=True)
     head.close()
     qw.close()
@@ -896,7 +904,8 @@ def run_encstack(args, cfg, world, rank, local, dist, torch, vxk):
         e1.record(stream)
         torch.cuda.synchronize()
     enc.sync(sh)
-    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    rank_ms = gather_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    ms = max(rank_ms)
     step_s = ms / 1000.0 / args.steps
     w_bytes = encoder_weight_bytes(cfg)
     keys = W + P - 1
@@ -962,6 +971,7 @@ def run_encstack(args, cfg, world, rank, local, dist, torch, vxk):
             "launch": "eager C-ABI calls per step: vxk_enc_batch_plan, vxk_encoder_forward, vxk_enc_batch_commit",
             "clocks": clocks.summary(),
         }
+        line.update(rank_fields(rank_ms))
         print(json.dumps(line), flush=True)
     enc.close()
     pool.close()
@@ -1056,7 +1066,8 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
         e1.record(stream)
         torch.cuda.synchronize()
     dec.sync(sh)
-    ms = max_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    rank_ms = gather_over_ranks(dist, e0.elapsed_time(e1), "cuda")
+    ms = max(rank_ms)
     step_s = ms / 1000.0 / args.steps
     w_bytes = decoder_weight_bytes(cfg)
     kv_bytes = L * 4096 * statistics.mean(ctx_sum)
@@ -1140,6 +1151,7 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
             "launch": "eager C-ABI calls per step: vxk_batch_plan, vxk_decoder_forward, vxk_batch_commit",
             "clocks": clocks.summary(),
         }
+        line.update(rank_fields(rank_ms))
         print(json.dumps(line), flush=True)
     dec.close()
     pool.close()
@@ -1171,6 +1183,12 @@ def decoder_cpu_sample(tensors, cfg, ctx, seed, seconds):
         if el >= seconds or done >= 8:
             break
     return done / el, done, ctx
+
+
+def rank_fields(rank_ms):
+    """Every rank's timed-region milliseconds and the slowest rank, which sets
+    the job's time (the data plane has no collective)."""
+    return {"rank_ms": [round(float(x), 3) for x in rank_ms], "slowest_rank": int(np.argmax(rank_ms))}
 
 
 def parse():

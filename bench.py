@@ -1121,7 +1121,7 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
     if dist:
         dist.barrier()
     if rank == 0:
-        per_layer = 9
+        per_layer = 8
         line = {
             "metric": "whole decoder step tokens/s (Q4_K_M, 26 layers + head)",
             "value": round(world * S * args.steps / (ms / 1000.0), 1),
@@ -1143,10 +1143,10 @@ def run_decoder(args, cfg, world, rank, local, dist, torch, vxk):
                          "weight_bytes": w_bytes, "kv_bytes": round(kv_bytes),
                          "avg_step_us": round(step_s * 1e6, 1), "kernel": "whole step (all kernels)"},
             "cpu_baseline": cpu, "e2e": e2e,
-            # embed, layer 0's q/k/v quantization, per layer (q/k/v product, attention, o quantize +
-            # product, norm quantizing into the w1/w3 tiles, w1/w3 product, w2 quantize (SwiGLU inside)
-            # + product, norm quantizing into the next q/k/v tiles), head (quantize, product, argmax,
-            # token ids)
+            # embed, layer 0's q/k/v quantization, per layer (q/k/v product, attention quantizing
+            # its output into the o tiles, o product, norm quantizing into the w1/w3 tiles, w1/w3
+            # product, w2 quantize (SwiGLU inside) + product, norm quantizing into the next q/k/v
+            # tiles), head (quantize, product, argmax, token ids)
             "gpu_launches": int(args.steps * (1 + 1 + per_layer * L + 4)),
             "launch": "eager C-ABI calls per step: vxk_batch_plan, vxk_decoder_forward, vxk_batch_commit",
             "clocks": clocks.summary(),

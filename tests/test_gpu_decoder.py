@@ -81,14 +81,14 @@ def vd():
     return mod
 
 
-def _setup(vxk, vd, tmp_path, seed, types, cache_dtype, untied=False, audio_cap=32):
+def _setup(vxk, vd, tmp_path, seed, types, cache_dtype, untied=False, audio_cap=32, max_streams=4):
     import decoder_model
 
     path = tmp_path / f"m{seed}.gguf"
     tensors = decoder_model.build(path, seed, types=types, untied_f16_head=untied)
     g = vxk.Gguf(path)
-    cfg = dict(n_layers=2, n_blocks=96, capacity=512, max_streams=4, max_rows=64, max_position=1024,
-               dtype=cache_dtype)
+    cfg = dict(n_layers=2, n_blocks=24 * max_streams, capacity=512, max_streams=max_streams, max_rows=64,
+               max_position=1024, dtype=cache_dtype)
     pool = vxk.Pool(**cfg)
     dec = vxk.Decoder(g, pool, audio_capacity=audio_cap, enc_capacity=16)
     g.close()
@@ -169,6 +169,35 @@ def test_decoder_steps_match_oracle(vxk, vd, tmp_path, kind):
     for i, s in enumerate(streams):
         dec.write_audio(s, 0, 32, dev_audio[i].data_ptr(), cs)
     steps = [[(0, 1), (1, 1), (2, 1)], [(0, 5), (1, 3)], [(2, 1), (0, 1), (1, 1)], [(1, 1), (2, 1)]]
+    errs = _run_steps(vxk, pool, dec, ref, streams, steps, audio, rng, dec.info["vocab"])
+    assert min(max(e[0], e[1]) for e in errs) <= EXACT_BAR
+    ref[2].close()
+    dec.close()
+    pool.close()
+
+
+def test_decoder_steps_of_many_streams(vxk, vd, tmp_path):
+    """24 streams, so that a step's rows take the tensor-core products: the
+    norms quantize their rows into the next products' tiles and the
+    single-token attention quantizes its output into the o product's tiles
+    (f16 cache).  Single-token steps of all streams in changing orders around
+    a multi-token append on some of them."""
+    import torch
+    import decoder_model
+
+    n = 24
+    tensors, pool, dec, ref = _setup(vxk, vd, tmp_path, 16, decoder_model.Q4_K_M, 1, max_streams=n)
+    rng = np.random.default_rng(6)
+    streams = [pool.open_stream() for _ in range(n)]
+    audio = rng.normal(0, 0.05, (n, 32, dec.info["dim"])).astype(np.float32)
+    cs = torch.cuda.current_stream().cuda_stream
+    dev_audio = torch.from_numpy(audio).cuda()
+    for i, s in enumerate(streams):
+        dec.write_audio(s, 0, 32, dev_audio[i].data_ptr(), cs)
+    order = list(range(n))
+    rng.shuffle(order)
+    steps = [[(i, 1) for i in range(n)], [(0, 6), (5, 3), (9, 2)], [(i, 1) for i in order],
+             [(i, 1) for i in reversed(range(n))]]
     errs = _run_steps(vxk, pool, dec, ref, streams, steps, audio, rng, dec.info["vocab"])
     assert min(max(e[0], e[1]) for e in errs) <= EXACT_BAR
     ref[2].close()

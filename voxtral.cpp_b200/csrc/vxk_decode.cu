@@ -30,6 +30,7 @@
 // q8_0 tiles are widened to f16 exactly in registers (int8 -> f16 magic
 // numbers) and their ggml block scales are applied per 32-value block.
 #include "vxk_internal.h"
+#include "vxk_qtc_quant.h"
 
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -295,6 +296,35 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
     }
 }
 
+// The 4 heads x 128 dims of (row, kv head) held by thread t as o[h] = dim t of
+// head h: staged in `buf` (512 floats) and quantized like
+// quantize_row_q8_K_ref into units 2 kvh and 2 kvh + 1 of the next product's
+// tiles (vxk_qtc_quant.h), one warp per unit.  Every thread of the CTA calls
+// it; `buf` is free again when it returns.
+__device__ __forceinline__ void quantize_out(const DecodeParams & p, float * buf, int row, int kvh,
+                                             const float (&o)[kGroup]) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) buf[h * kHeadDim + tid] = o[h];
+    __syncthreads();
+    if (warp < 2) {
+        const int eA = qtc_lane_col_a(lane), eB = eA + 32;
+        const float * u = buf + warp * 256;
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            x[i] = u[eA + i];
+            x[4 + i] = u[eB + i];
+        }
+        const int np = p.q_npad, chunk = row / np, rr = row - chunk * np;
+        const int64_t cu = (int64_t) chunk * p.q_units + 2 * kvh + warp;
+        qtc_quantize_unit(x, lane, rr, np, p.q_tiles ? p.q_tiles + cu * np * 512 : nullptr,
+                          p.q_bmin ? p.q_bmin + cu * np * 32 : nullptr,
+                          p.q_tiles8 ? p.q_tiles8 + cu * np * 256 : nullptr, p.q_dx + cu * np + rr);
+    }
+    __syncthreads();
+}
+
 // Persistent flash-decoding kernel.  Grid = one CTA per resident slot; CTA b
 // processes the work units (split, kv head) the host scheduled for it
 // (sched_units[sched_offsets[b] .. sched_offsets[b+1]), longest-first greedy),
@@ -302,7 +332,10 @@ __device__ __forceinline__ void append_head_row(const float * k, const float * v
 // pages (pages warp, warp+4, ...) through its own ring of ST stages; the ring
 // runs ahead across unit boundaries, so the next unit's pages are already in
 // flight while the CTA merges and writes the current one.
-template <int DT>
+// QUANT: the output of each (row, kv head) is also quantized into the next
+// product's activation tiles (DecodeParams q_*), two 256-column units per kv
+// head, by warps 0 and 1 after the row's last split.
+template <int DT, bool QUANT>
 __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem<DT> & S = *reinterpret_cast<Smem<DT> *>(smem_raw);
@@ -883,8 +916,18 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
 
         const int64_t out_base = ((int64_t) it.row * p.n_q + (int64_t) kvh * kGroup) * kHeadDim;
         if (rd.n_chunks == 1) {
+            if constexpr (QUANT) {
+                float o[kGroup];
 #pragma unroll
-            for (int h = 0; h < kGroup; ++h) p.out[out_base + h * kHeadDim + tid] = O[h] / Lsum[h];
+                for (int h = 0; h < kGroup; ++h) o[h] = O[h] / Lsum[h];
+                if (p.out)
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) p.out[out_base + h * kHeadDim + tid] = o[h];
+                quantize_out(p, S.merge, it.row, kvh, o);
+            } else {
+#pragma unroll
+                for (int h = 0; h < kGroup; ++h) p.out[out_base + h * kHeadDim + tid] = O[h] / Lsum[h];
+            }
             continue;
         }
         {
@@ -956,6 +999,7 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
             for (int h = 0; h < kGroup; ++h) S.red_l[warp][h] = ls[h];
         }
         __syncthreads();
+        float o[kGroup];
 #pragma unroll
         for (int h = 0; h < kGroup; ++h) {
             float Lt = 0.0f;
@@ -963,11 +1007,13 @@ __global__ void __launch_bounds__(NT, Cfg<DT>::kMinBlocks) decode_kernel(const D
             for (int w = 0; w < kWarps; ++w) Lt += S.red_l[w][h];
             float acc = 0.0f;
             for (int cc = 0; cc < nc; ++cc) acc = fmaf(comb_w[cc * kGroup + h], __ldcg(part_at(cc, h) + tid), acc);
-            p.out[out_base + h * kHeadDim + tid] = acc / Lt;
+            o[h] = acc / Lt;
+            if (!QUANT || p.out) p.out[out_base + h * kHeadDim + tid] = o[h];
         }
         if (tid == 0) p.counters[it.row * p.n_kv + kvh] = 0;
         // the weights in the merge buffer are read before the next unit writes it
         __syncthreads();
+        if constexpr (QUANT) quantize_out(p, S.merge, it.row, kvh, o);
     }
 }
 
@@ -1051,7 +1097,7 @@ __global__ void __launch_bounds__(256) compact_kernel(const CompactParams p) {
     }
 }
 
-template <int DT>
+template <int DT, bool QUANT = false>
 cudaError_t launch_decode_t(const DecodeParams & p, cudaStream_t stream, bool pdl) {
     const int smem = (int) sizeof(Smem<DT>);
     // The opt-in is per device; remember which devices have it.
@@ -1060,7 +1106,7 @@ cudaError_t launch_decode_t(const DecodeParams & p, cudaStream_t stream, bool pd
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 64 || !(configured & (1ull << dev))) {
-        e = cudaFuncSetAttribute(decode_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(decode_kernel<DT, QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
@@ -1074,7 +1120,7 @@ cudaError_t launch_decode_t(const DecodeParams & p, cudaStream_t stream, bool pd
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_kernel<DT>, p);
+    return cudaLaunchKernelEx(&cfg, decode_kernel<DT, QUANT>, p);
 }
 
 // Failure-path probe: a warp waits, with the decode kernel's own bounded
@@ -1105,10 +1151,10 @@ int decode_smem_bytes(int dtype) {
 template <int DT>
 int ctas_per_sm_t() {
     int n = 0;
-    if (cudaFuncSetAttribute(decode_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<DT>)) !=
+    if (cudaFuncSetAttribute(decode_kernel<DT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sizeof(Smem<DT>)) !=
         cudaSuccess)
         return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<DT>, NT, sizeof(Smem<DT>)) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<DT, false>, NT, sizeof(Smem<DT>)) != cudaSuccess) return 0;
     return n;
 }
 
@@ -1123,6 +1169,15 @@ cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream, bool pdl)
     if (p.dtype == 8) return launch_decode_t<8>(p, stream, pdl);
     if (p.dtype == 0) return launch_decode_t<0>(p, stream, pdl);
     return launch_decode_t<1>(p, stream, pdl);
+}
+
+cudaError_t launch_decode_quant(const DecodeParams & p, cudaStream_t stream, bool pdl) {
+    if (p.dtype != 1 || !p.q_dx || (!p.q_tiles && !p.q_tiles8) || (p.q_tiles && !p.q_bmin) ||
+        (p.q_npad != 16 && p.q_npad != 32 && p.q_npad != 64) || p.q_units != p.n_q * kHeadDim / 256 ||
+        p.n_q != p.n_kv * kGroup)
+        return cudaErrorInvalidValue;
+    if (p.n_items <= 0 || p.n_ctas <= 0) return cudaSuccess;
+    return launch_decode_t<1, true>(p, stream, pdl);
 }
 
 // ---------------------------------------------------------------------------

@@ -611,17 +611,29 @@ void forward(vxk_decoder * d, const int32_t * tokens, const int32_t * audio_slot
             else
                 products(d, ws, 3, d->xn, dim, rows, ys, st, cs);
         }
-        if (bv.single_token) {
+        // single-token rows on an f16 cache: the attention quantizes its output
+        // rows into the o product's tiles in the same launch
+        vxk_qweight * wo[1] = {L.o};
+        vxk::QtcTiles ot{};
+        const bool o_tiles = bv.single_token && rows <= d->chunk && vxk::pool_decode_quant_ok(d->pool) &&
+                             vxk::qweight_group_tiles(wo, 1, rows, &ot);
+        if (o_tiles) {
+            VXK_DCALL((vxk_status) vxk::pool_decode_layer_quant(d->pool, l, d->q, d->k, d->v, nullptr, ot, cs),
+                      "vxk_decode_layer");
+        } else if (bv.single_token) {
             VXK_DCALL(vxk_decode_layer(d->pool, l, d->q, d->k, d->v, d->att, cs), "vxk_decode_layer");
         } else {
             VXK_DCALL(vxk_append_layer(d->pool, l, d->k, d->v, cs), "vxk_append_layer");
             VXK_DCALL(vxk_attend_layer(d->pool, l, d->q, d->att, cs), "vxk_attend_layer");
         }
         {
-            vxk_qweight * ws[1] = {L.o};
             float * ys[1] = {d->proj};
             const int64_t st[1] = {dim};
-            products(d, ws, 1, d->att, qdim, rows, ys, st, cs);
+            if (o_tiles)
+                VXK_DCALL((vxk_status) vxk::qweight_matmul_group_prequantized(wo, 1, rows, ys, nullptr, cs),
+                          "quantized product");
+            else
+                products(d, wo, 1, d->att, qdim, rows, ys, st, cs);
         }
         vxk::NormParams np{};
         np.x = d->x;

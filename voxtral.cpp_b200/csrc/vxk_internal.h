@@ -90,6 +90,14 @@ struct DecodeParams {
     int32_t * error;         // device error word (0 = ok)
     int32_t fuse_append;     // 1: rows flagged kRowAppend append first
     int32_t dtype;           // 0 = f32, 1 = f16, 8 = q8_0
+    // launch_decode_quant only: each row's output also quantized into the next
+    // product's activation tiles (QtcTiles); out may then be nullptr
+    uint8_t * q_tiles;
+    uint8_t * q_bmin;
+    uint8_t * q_tiles8;
+    float * q_dx;
+    int32_t q_npad;
+    int32_t q_units;         // 256-column units of a row: n_q x head_dim / 256
 };
 
 struct AppendParams {
@@ -139,6 +147,9 @@ struct CompactParams {
 // preceding kernel on the stream writes nothing the decode prologue reads
 // (row/work descriptors, block table, cache pages of this layer).
 cudaError_t launch_decode(const DecodeParams & p, cudaStream_t stream, bool pdl);
+// launch_decode for an f16 cache with the quantization of the output rows into
+// p.q_* (the o product's tiles) in the same launch.
+cudaError_t launch_decode_quant(const DecodeParams & p, cudaStream_t stream, bool pdl);
 cudaError_t launch_append(const AppendParams & p, cudaStream_t stream);
 cudaError_t launch_table_updates(int32_t * table, const TableUpdate * updates, int32_t n,
                                  cudaStream_t stream);
@@ -413,6 +424,14 @@ struct PoolShape {
     float rope_theta;
 };
 PoolShape pool_shape(const vxk_pool * pool);
+// True when pool_decode_layer_quant applies (an f16 cache, 4 query heads of
+// 128 dims per kv head).
+bool pool_decode_quant_ok(const vxk_pool * pool);
+// vxk_decode_layer whose output rows are also quantized into `t` (the tiles
+// of the o product, a one-matrix group over the same rows); out may be
+// nullptr.  The product then runs as qweight_matmul_group_prequantized.
+int32_t pool_decode_layer_quant(vxk_pool * pool, int32_t layer, const float * q, const float * k, const float * v,
+                                float * out, const QtcTiles & t, cudaStream_t stream);
 
 // One query row of a decoder forward.
 struct DecRow {

@@ -639,6 +639,36 @@ PoolShape pool_shape(const vxk_pool * pool) {
                      c.rope_theta};
 }
 
+bool pool_decode_quant_ok(const vxk_pool * pool) {
+    return pool && pool->cfg.dtype == VXK_DTYPE_F16 && pool->cfg.head_dim == kHeadDim &&
+           pool->cfg.n_q_heads == pool->cfg.n_kv_heads * kGroup;
+}
+
+int32_t pool_decode_layer_quant(vxk_pool * pool, int32_t layer, const float * q, const float * k, const float * v,
+                                float * out, const QtcTiles & t, cudaStream_t stream) {
+    if (!pool) return VXK_STATUS_INVALID_ARGUMENT;
+    return guarded(pool, [&] {
+        check_layer(pool, layer);
+        if (!pool->single_token) fail(VXK_STATUS_INVALID_STATE, "decode_layer needs a single-token batch");
+        if (!q || !k || !v || !t.dx) fail(VXK_STATUS_INVALID_ARGUMENT, "null buffer");
+        if (!pool_decode_quant_ok(pool)) fail(VXK_STATUS_INVALID_ARGUMENT, "quantized output needs an f16 cache");
+        check_attention(pool);
+        DeviceScope scope(pool->cfg.device);
+        ++pool->launches;
+        const bool pdl = use_pdl(pool);
+        pool->batch_decodes = 0;
+        DecodeParams d = decode_params(pool, layer, q, k, v, out, 1);
+        d.q_tiles = t.b;
+        d.q_bmin = t.bmin;
+        d.q_tiles8 = t.b8;
+        d.q_dx = t.dx;
+        d.q_npad = t.npad;
+        d.q_units = pool->cfg.n_q_heads * pool->cfg.head_dim / 256;
+        VXK_CUDA(launch_decode_quant(d, stream, pdl));
+        pool->batch_decodes = 1;
+    });
+}
+
 }  // namespace vxk
 
 extern "C" {

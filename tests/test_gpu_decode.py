@@ -257,10 +257,13 @@ def test_back_to_back_layers(vxk, oracle, dtype):
         d.check_cache(s)
 
 
-def test_end_to_end_host_step_matches_device_path(vxk, oracle):
+@pytest.mark.parametrize("n_layers", [3, 11])
+def test_end_to_end_host_step_matches_device_path(vxk, oracle, n_layers):
+    """11 layers: the inputs go up in runs [0, 1), [1, 3), [3, 7), [7, 11) and
+    the outputs come down in runs ending at layers 3, 7, 9 and 10."""
     import torch
 
-    cfg = _cfg(n_layers=3)
+    cfg = _cfg(n_layers=n_layers)
     d = Driver(vxk, oracle, seed=9, **cfg)
     streams = [d.open() for _ in range(4)]
     for s in streams:
@@ -268,18 +271,19 @@ def test_end_to_end_host_step_matches_device_path(vxk, oracle):
     c = d.pool.config
     rng = np.random.default_rng(10)
     n = len(streams)
-    q = torch.from_numpy(rand(rng, c.n_layers, n, c.n_q_heads, c.head_dim)).pin_memory()
-    k = torch.from_numpy(rand(rng, c.n_layers, n, c.n_kv_heads, c.head_dim)).pin_memory()
-    v = torch.from_numpy(rand(rng, c.n_layers, n, c.n_kv_heads, c.head_dim)).pin_memory()
-    out = torch.empty((c.n_layers, n, c.n_q_heads, c.head_dim)).pin_memory()
-    d.pool.decode_step_host(streams, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), d.stream)
-    for layer in range(c.n_layers):
-        for r, s in enumerate(streams):
-            pos = d.mirror.next[s]
-            d.mirror.append(s, layer, pos, k[layer, r].numpy(), v[layer, r].numpy())
-            want = d.mirror.attend(s, layer, pos, max(0, pos - c.capacity + 1), q[layer, r].numpy())
-            assert np.max(np.abs(out[layer, r].numpy() - want)) <= ATOL
-    for s in streams:
-        d.mirror.advance(s, 1)
-        assert d.pool.ring(s).next_absolute_position == 258
-        d.check_cache(s)
+    for step in range(2):  # the second step reuses the staging of the first
+        q = torch.from_numpy(rand(rng, c.n_layers, n, c.n_q_heads, c.head_dim)).pin_memory()
+        k = torch.from_numpy(rand(rng, c.n_layers, n, c.n_kv_heads, c.head_dim)).pin_memory()
+        v = torch.from_numpy(rand(rng, c.n_layers, n, c.n_kv_heads, c.head_dim)).pin_memory()
+        out = torch.full((c.n_layers, n, c.n_q_heads, c.head_dim), float("nan")).pin_memory()
+        d.pool.decode_step_host(streams, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), d.stream)
+        for layer in range(c.n_layers):
+            for r, s in enumerate(streams):
+                pos = d.mirror.next[s]
+                d.mirror.append(s, layer, pos, k[layer, r].numpy(), v[layer, r].numpy())
+                want = d.mirror.attend(s, layer, pos, max(0, pos - c.capacity + 1), q[layer, r].numpy())
+                assert np.max(np.abs(out[layer, r].numpy() - want)) <= ATOL
+        for s in streams:
+            d.mirror.advance(s, 1)
+            assert d.pool.ring(s).next_absolute_position == 258 + step
+            d.check_cache(s)

@@ -1087,32 +1087,53 @@ vxk_status vxk_decode_step_host(vxk_pool * pool, const int32_t * stream_ids, int
             check_attention(pool);
         }
         const size_t rows = pool->rows.size();
+        const int32_t L = c.n_layers;
         VXK_CUDA(cudaEventRecord(pool->ev_begin, cs));
         VXK_CUDA(cudaStreamWaitEvent(pool->h2d, pool->ev_begin, 0));
         VXK_CUDA(cudaStreamWaitEvent(pool->d2h, pool->ev_begin, 0));
-        auto dq = [&](int32_t l) { return pool->d_io + (size_t) l * layer_floats; };
-        auto dk = [&](int32_t l) { return dq(l) + rows * q_per_row; };
-        auto dv = [&](int32_t l) { return dk(l) + rows * kv_per_row; };
-        auto dout = [&](int32_t l) { return dv(l) + rows * kv_per_row; };
-        for (int32_t l = 0; l < c.n_layers; ++l) {
-            VXK_CUDA(cudaMemcpyAsync(dq(l), h_q + (size_t) l * rows * q_per_row, rows * q_per_row * sizeof(float),
+        // Staging is blocked like the host buffers: [q of every layer][k][v][out],
+        // so a run of layers moves as one copy per tensor.
+        const size_t qn = rows * q_per_row, kvn = rows * kv_per_row;
+        float * const q0 = pool->d_io;
+        float * const k0 = q0 + (size_t) L * qn;
+        float * const v0 = k0 + (size_t) L * kvn;
+        float * const o0 = v0 + (size_t) L * kvn;
+        // Inputs go up in runs of layers [2^g - 1, 2^(g+1) - 1): layer 0 waits for
+        // its own rows only, and each later run is copied while the layers before
+        // it compute (a run is as long as the layers ahead of it, and a layer's
+        // rows copy far faster than it attends).  Outputs come down in runs that
+        // end at layers L - 2^g, so the copy left after the last layer is that
+        // layer's rows.  The layer kernels wait on an event only at the runs'
+        // edges: every other layer boundary keeps the programmatic overlap of
+        // one layer's prologue with the previous layer's tail.
+        int32_t n_in = 0;
+        for (int32_t first = 0; first < L; first = 2 * first + 1) {
+            const int32_t end = std::min(L, 2 * first + 1);
+            const size_t nl = (size_t) (end - first);
+            VXK_CUDA(cudaMemcpyAsync(q0 + first * qn, h_q + first * qn, nl * qn * sizeof(float),
                                      cudaMemcpyHostToDevice, pool->h2d));
-            VXK_CUDA(cudaMemcpyAsync(dk(l), h_k + (size_t) l * rows * kv_per_row, rows * kv_per_row * sizeof(float),
+            VXK_CUDA(cudaMemcpyAsync(k0 + first * kvn, h_k + first * kvn, nl * kvn * sizeof(float),
                                      cudaMemcpyHostToDevice, pool->h2d));
-            VXK_CUDA(cudaMemcpyAsync(dv(l), h_v + (size_t) l * rows * kv_per_row, rows * kv_per_row * sizeof(float),
+            VXK_CUDA(cudaMemcpyAsync(v0 + first * kvn, h_v + first * kvn, nl * kvn * sizeof(float),
                                      cudaMemcpyHostToDevice, pool->h2d));
-            VXK_CUDA(cudaEventRecord(pool->ev_in[(size_t) l], pool->h2d));
+            VXK_CUDA(cudaEventRecord(pool->ev_in[(size_t) n_in++], pool->h2d));
         }
-        for (int32_t l = 0; l < c.n_layers; ++l) {
-            VXK_CUDA(cudaStreamWaitEvent(cs, pool->ev_in[(size_t) l], 0));
+        int32_t in_run = 0, out_run = 0, out_first = 0;
+        for (int32_t l = 0; l < L; ++l) {
+            if (l == (1 << in_run) - 1) VXK_CUDA(cudaStreamWaitEvent(cs, pool->ev_in[(size_t) in_run++], 0));
             ++pool->launches;
-            // layers after the first overlap their prologue (page copies of their own
-            // layer) with the previous layer's tail, as in vxk_decode_layer
-            VXK_CUDA(vxk::launch_decode(decode_params(pool, l, dq(l), dk(l), dv(l), dout(l), 1), cs, l > 0));
-            VXK_CUDA(cudaEventRecord(pool->ev_out[(size_t) l], cs));
-            VXK_CUDA(cudaStreamWaitEvent(pool->d2h, pool->ev_out[(size_t) l], 0));
-            VXK_CUDA(cudaMemcpyAsync(h_out + (size_t) l * rows * q_per_row, dout(l), rows * q_per_row * sizeof(float),
-                                     cudaMemcpyDeviceToHost, pool->d2h));
+            VXK_CUDA(vxk::launch_decode(decode_params(pool, l, q0 + l * qn, k0 + l * kvn, v0 + l * kvn, o0 + l * qn, 1),
+                                        cs, l > 0));
+            bool run_end = l == L - 1;
+            for (int32_t g = 1; g < 31 && (1 << g) <= L; ++g) run_end = run_end || l == L - (1 << g);
+            if (run_end) {
+                VXK_CUDA(cudaEventRecord(pool->ev_out[(size_t) out_run], cs));
+                VXK_CUDA(cudaStreamWaitEvent(pool->d2h, pool->ev_out[(size_t) out_run++], 0));
+                VXK_CUDA(cudaMemcpyAsync(h_out + out_first * qn, o0 + out_first * qn,
+                                         (size_t) (l + 1 - out_first) * qn * sizeof(float), cudaMemcpyDeviceToHost,
+                                         pool->d2h));
+                out_first = l + 1;
+            }
         }
         VXK_CUDA(cudaMemcpyAsync(pool->h_err, pool->d_error, sizeof(int32_t), cudaMemcpyDeviceToHost, pool->d2h));
         VXK_CUDA(cudaEventRecord(pool->ev_done, pool->d2h));

@@ -158,7 +158,10 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
         hv = torch.randn((L, S * P, H, HDE)).mul_(0.5).pin_memory()
         ho = torch.empty((L, S * P, H, HDE)).pin_memory()
         dq, dk, dv = (torch.empty_like(hq, device="cuda") for _ in range(3))
-        copy_stream = torch.cuda.Stream()
+        # uploads and downloads on two copy streams, so the two PCIe directions
+        # overlap; the next step's uploads wait only for the layers that read
+        # the staging, its layers for the downloads of their outputs
+        copy_stream, down_stream = torch.cuda.Stream(), torch.cuda.Stream()
         up = [torch.cuda.Event() for _ in range(L)]
         done_ev = [torch.cuda.Event() for _ in range(L)]
 
@@ -171,16 +174,16 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
                     dk[layer].copy_(hk[layer], non_blocking=True)
                     dv[layer].copy_(hv[layer], non_blocking=True)
                     up[layer].record(copy_stream)
+            stream.wait_stream(down_stream)
             for layer in range(L):
                 stream.wait_event(up[layer])
                 pool.layer(layer, dq[layer].data_ptr(), dk[layer].data_ptr(), dv[layer].data_ptr(),
                            out[layer].data_ptr(), sh)
                 done_ev[layer].record(stream)
-            with torch.cuda.stream(copy_stream):
+            with torch.cuda.stream(down_stream):
                 for layer in range(L):
-                    copy_stream.wait_event(done_ev[layer])
+                    down_stream.wait_event(done_ev[layer])
                     ho[layer].copy_(out[layer], non_blocking=True)
-            stream.wait_stream(copy_stream)
             pool.commit()
 
         host_step()
@@ -192,6 +195,7 @@ def run_encoder(args, cfg, world, rank, local, dist, torch, vxk):
         f0.record(stream)
         for _ in range(args.steps):
             host_step()
+        stream.wait_stream(down_stream)
         f1.record(stream)
         torch.cuda.synchronize()
         ems = f0.elapsed_time(f1)

@@ -21,12 +21,15 @@
 //
 // CTA = 128 weight rows x a range of 256-column units x one chunk of up to 64
 // activation rows (grid z: a product of more rows runs its 64-row chunks side
-// by side in one launch); 11 warps:
-//   warps 0-3   dequant: thread = weight row (TMEM lane); per unit it reads the
-//               row's 128 quant bytes and 16 scale/min bytes from the raw
-//               ring, writes 128 columns of f16 pairs sc*q (Q4_K) or of
-//               int8 quads hi, lo (Q6_K) into TMEM (tcgen05.st) and the
-//               row's mins row into shared memory (Q4_K)
+// by side in one launch); 16 warps:
+//   warps 0-3, 12-15  dequant: thread = weight row (TMEM lane; warp w reaches
+//               lanes 32 (w % 4) ..); per unit warps 0-3 turn the first half of
+//               the row's quant bytes into TMEM columns 0-63 and warps 12-15
+//               the second half into columns 64-127 (two dequant warps per
+//               scheduler, so one's dependency chains hide behind the
+//               other's): f16 pairs sc*q (Q4_K) or int8 quads hi, lo (Q6_K)
+//               into TMEM (tcgen05.st); warps 0-3 also write the row's mins
+//               row into shared memory (Q4_K)
 //   warps 4-7   epilogue: thread = weight row; tcgen05.ld of the unit's
 //               accumulators, fp32 block factors into registers
 //   warp 8      bulk copies of the raw weight records (HBM stream, evict-first)
@@ -50,7 +53,7 @@
 namespace vxk {
 namespace {
 
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
 constexpr int kRawStages = 4;
 constexpr int kActStages = 2;  // = 2: a unit's stage is its parity, like its A and D buffers
 constexpr int kMaxN = 64;
@@ -243,6 +246,14 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[1
         : "r"(taddr));
 }
 
+// The same for 8 columns.
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void cluster_sync() {
@@ -364,19 +375,21 @@ __global__ void __launch_bounds__(256) qtc_act_kernel(const QtcParams p) {
 // forms both 4 p + 32768 = 4 (q6 - 32) sc + 32768 in [16512, 49152] (no carry
 // between the halves), whose high byte is hi + 128 and low byte 4 lo; byte
 // permutes gather four of each into a word (hi + 128 turned into hi by
-// flipping bit 7).
-__device__ __forceinline__ void dequant_q6_i8(const uint8_t * raw, int r, uint32_t abase) {
+// flipping bit 7).  One call makes half `half` of the row: its elements
+// 128 half .. 128 half + 127, hi columns 32 half + t and lo columns 64 + 32
+// half + t.
+__device__ __forceinline__ void dequant_q6_i8(const uint8_t * raw, int r, uint32_t abase, int half) {
     const uint8_t * qrow = raw + r * 256;
-    const uint4 scv = *reinterpret_cast<const uint4 *>(raw + 32768 + r * 16);
-    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    // the scales of sub-blocks 8 half .. 8 half + 7: bytes 8 half .. of the row's 16
+    const uint2 scv = *reinterpret_cast<const uint2 *>(raw + 32768 + r * 16 + 8 * half);
+    const uint32_t scw[2] = {scv.x, scv.y};
+    {
         uint32_t hi[32], lo[32];  // columns 32 half + t
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
             const int g = 8 * half + cc;  // sub-block g: chunk g, elements 16g .. 16g + 15
             const uint4 v = *reinterpret_cast<const uint4 *>(qrow + ((g ^ (r & 7)) << 4));
-            const int sc = (int) (int8_t) (scw[g >> 2] >> (8 * (g & 3)));
+            const int sc = (int) (int8_t) (scw[cc >> 2] >> (8 * (cc & 3)));
             const uint32_t m4 = (uint32_t) (4 * sc);
             const uint32_t c4 = (uint32_t) (32768 - 128 * sc) * 0x00010001u;
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -420,14 +433,14 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     if (tid == 0) {
         for (int s = 0; s < kRawStages; ++s) {
             mbar_init(&bars[kBarRawFull + s], 1);
-            mbar_init(&bars[kBarRawEmpty + s], 128);
+            mbar_init(&bars[kBarRawEmpty + s], 256);  // both dequant groups
         }
         for (int s = 0; s < kActStages; ++s) {
             mbar_init(&bars[kBarActFull + s], 1);
             mbar_init(&bars[kBarActEmpty + s], 1);         // MMA commit
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&bars[kBarAFull + b], 128);
+            mbar_init(&bars[kBarAFull + b], 256);     // both dequant groups
             mbar_init(&bars[kBarAEmpty + b], 1);
             mbar_init(&bars[kBarDFull + b], 1);
             mbar_init(&bars[kBarDEmpty + b], 128);
@@ -448,10 +461,11 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
     const uint32_t tmem = *tmem_slot;
     float * ptile = reinterpret_cast<float *>(base + kOffRaw);  // [N][128] partial block at the end
 
-    if (warp < 4) {
-        // ---------------- dequant: row r = 32 warp + lane ----------------
-        const int r = 32 * warp + lane;
-        const uint32_t lane_off = (uint32_t) (32 * warp) << 16;
+    if (warp < 4 || warp >= 12) {
+        // ---------------- dequant: row r = 32 (warp % 4) + lane, column half hg ----------------
+        const int hg = warp >> 3 & 1;  // warps 0-3: columns 0-63, warps 12-15: columns 64-127
+        const int r = 32 * (warp & 3) + lane;
+        const uint32_t lane_off = (uint32_t) (32 * (warp & 3)) << 16;
         const bool q6 = m.type == 14;
         for (int i = 0; i < nu; ++i) {
             const int s = i % kRawStages;
@@ -466,41 +480,43 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     break;
                 tc_fence_after();
                 if (q6) {
-                    dequant_q6_i8(raw, r, tmem + 128 * b + lane_off);
+                    dequant_q6_i8(raw, r, tmem + 128 * b + lane_off, hg);
                 } else {
                     const uint4 scm = *reinterpret_cast<const uint4 *>(raw + 16384 + r * 16);  // sc[8], mn[8]
                     const uint32_t mnw[2] = {scm.z, scm.w};
-                    // the 8 sub-block scales as f16 pairs (s, s) by splicing each byte under
-                    // the exponent of 1024 and subtracting 1024 (exact for s < 1024)
-                    __half2 scl[8], sch[8];
+                    // this half's 4 sub-block scales (sub-blocks 4 hg .. 4 hg + 3) as f16
+                    // pairs (s, s) by splicing each byte under the exponent of 1024 and
+                    // subtracting 1024 (exact for s < 1024)
+                    __half2 scl[4], sch[4];
                     {
-                        const uint32_t scw[2] = {scm.x, scm.y};
+                        const uint32_t scw = hg ? scm.y : scm.x;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const uint32_t bj = (scw[j >> 2] >> (8 * (j & 3))) & 0xffu;
+                        for (int j = 0; j < 4; ++j) {
+                            const uint32_t bj = (scw >> (8 * j)) & 0xffu;
                             const uint32_t hb = bj | (bj << 16) | 0x64006400u;
                             scl[j] = __hsub2(*reinterpret_cast<const __half2 *>(&hb), __half2half2(__ushort_as_half(0x6400)));
                             // high nibbles come out as 1024 + 16 q: multiply by s / 16 (exact)
                             sch[j] = __hmul2(scl[j], __half2half2(__ushort_as_half(0x2c00)));
                         }
                     }
-                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word).
+                    // 8 chunks of 16 B = 32 quant words -> 128 TMEM columns (4 per word);
+                    // this group makes chunks 4 hg .. 4 hg + 3 (columns 64 hg ..).
                     // Word v holds bytes (b0, b1, b2, b3): the low nibbles of b0, b2 and their
                     // high nibbles, then the same of b1, b3 (v >> 8), each pair spliced under
                     // the f16 exponent of 1024 (high nibbles at 16x, which the scale absorbs);
                     // one fused multiply-add per pair removes the 1024 (or 1024 + 0) offset:
                     // (1024 + q) s - 1024 s and (1024 + 16 q) s/16 - 64 s are q s exactly.
 #pragma unroll
-                    for (int half = 0; half < 4; ++half) {
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int half = 2 * hg + hh;  // columns 32 half ..
                         uint32_t cols[32];
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
-                            const int c = 2 * half + cc;  // chunk: words 4c .. 4c+3, group c / 2
+                            const int c = 2 * half + cc;  // chunk: words 4c .. 4c+3, group c / 2 = half
                             const uint4 v4 = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
-                            const int g = c >> 1;
-                            const __half2 slo = scl[2 * g], shi = sch[2 * g + 1];
-                            const __half2 blo = __hmul2(scl[2 * g], __half2half2(__ushort_as_half(0xe400)));     // -1024 s
-                            const __half2 bhi = __hmul2(scl[2 * g + 1], __half2half2(__ushort_as_half(0xd400))); // -64 s
+                            const __half2 slo = scl[2 * hh], shi = sch[2 * hh + 1];
+                            const __half2 blo = __hmul2(scl[2 * hh], __half2half2(__ushort_as_half(0xe400)));     // -1024 s
+                            const __half2 bhi = __hmul2(scl[2 * hh + 1], __half2half2(__ushort_as_half(0xd400))); // -64 s
                             const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
@@ -517,8 +533,9 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                         }
                         tmem_st32(tmem + 128 * b + 32 * half + lane_off, cols);
                     }
-                    // mins A row: K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact); unswizzled
+                    // mins A row (warps 0-3): K 0..7 = m_j, K 8..15 = 128 m_j (f16, exact); unswizzled
                     // K-major core matrices: row group r / 8 at 256 B, K half at 128 B, row r % 8 at 16 B
+                    if (hg == 0) {
                     uint8_t * amin = base + kOffAMin + b * kAMin + (r >> 3) * 256 + (r & 7) * 16;
                     uint32_t m0[4], m1[4];
 #pragma unroll
@@ -530,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     }
                     *reinterpret_cast<uint4 *>(amin) = make_uint4(m0[0], m0[1], m0[2], m0[3]);
                     *reinterpret_cast<uint4 *>(amin + 128) = make_uint4(m1[0], m1[1], m1[2], m1[3]);
+                    }
                 }
                 mbar_arrive(&bars[kBarRawEmpty + s]);  // the unit's raw bytes are read
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -577,48 +595,35 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
             // d_x of activation row e of this unit
             auto dxe = [&](int e) { return __shfl_sync(kFull, e < 32 ? xa : xb, e & 31); };
             if (m.type == 14) {
-                // Q6_K: acc += (d_w * d_x) * (64 D_hi + D_lo / 4), an exact int32 sum
+                // Q6_K: acc += (d_w * d_x) * (64 D_hi + D_lo / 4), an exact int32 sum;
+                // 8 columns of D and D_lo in flight per wait (the 512-thread
+                // launch leaves 128 registers a thread, 64 of them acc)
 #pragma unroll
-                for (int c0 = 0; c0 < N; c0 += 32) {
-                    constexpr int W = N < 32 ? N : 32;
-                    uint32_t v[2][16], lo[2][16];
-#pragma unroll
-                    for (int hh = 0; hh < W / 16; ++hh) {
-                        tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * hh + lane_off, v[hh]);
-                        tmem_ld16_nowait(tmem + 384 + 64 * b + c0 + 16 * hh + lane_off, lo[hh]);
-                    }
+                for (int c0 = 0; c0 < N; c0 += 8) {
+                    uint32_t v[8], lo[8];
+                    tmem_ld8_nowait(tmem + 256 + 64 * b + c0 + lane_off, v);
+                    tmem_ld8_nowait(tmem + 384 + 64 * b + c0 + lane_off, lo);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int hh = 0; hh < W / 16; ++hh)
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj)
-                            acc[c0 + 16 * hh + jj] =
-                                fmaf(__fmul_rn(dw.x, dxe(c0 + 16 * hh + jj)),
-                                     __int2float_rn(64 * (int) v[hh][jj] + ((int) lo[hh][jj] >> 2)),
-                                     acc[c0 + 16 * hh + jj]);
+                    for (int jj = 0; jj < 8; ++jj)
+                        acc[c0 + jj] = fmaf(__fmul_rn(dw.x, dxe(c0 + jj)),
+                                            __int2float_rn(64 * (int) v[jj] + ((int) lo[jj] >> 2)), acc[c0 + jj]);
                 }
             } else {
-                // Q4_K: 32 columns of D and of Dmin in flight per wait
+                // Q4_K: 8 columns of D and of Dmin in flight per wait
 #pragma unroll
-                for (int c0 = 0; c0 < N; c0 += 32) {
-                constexpr int W = N < 32 ? N : 32;
-                uint32_t v[2][16], mm[2][16];
+                for (int c0 = 0; c0 < N; c0 += 8) {
+                    uint32_t v[8], mm[8];
+                    tmem_ld8_nowait(tmem + 256 + 64 * b + c0 + lane_off, v);
+                    tmem_ld8_nowait(tmem + 384 + 64 * b + c0 + lane_off, mm);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int h = 0; h < W / 16; ++h) {
-                    tmem_ld16_nowait(tmem + 256 + 64 * b + c0 + 16 * h + lane_off, v[h]);
-                    tmem_ld16_nowait(tmem + 384 + 64 * b + c0 + 16 * h + lane_off, mm[h]);
-                }
-                tmem_ld_wait();
-#pragma unroll
-                for (int h = 0; h < W / 16; ++h)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float x = dxe(c0 + 16 * h + j);
-                        acc[c0 + 16 * h + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[h][j]),
-                                                    fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[h][j]),
-                                                         acc[c0 + 16 * h + j]));
+                    for (int j = 0; j < 8; ++j) {
+                        const float x = dxe(c0 + j);
+                        acc[c0 + j] = fmaf(-__fmul_rn(x, dw.y), __uint_as_float(mm[j]),
+                                           fmaf(__fmul_rn(x, dw.x), __uint_as_float(v[j]), acc[c0 + j]));
                     }
-            }
+                }
             }
             tc_fence_before();
             mbar_arrive(&bars[kBarDEmpty + b]);
@@ -676,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1) qtc_kernel(const QtcParams p) {
                     tc_drain(&bars[kBarActFull + d % kActStages], (uint32_t) (d / kActStages) & 1u);
         }
         __syncwarp();
-    } else {
+    } else if (warp < 12) {
         // ---------------- tcgen05.mma issuers (warps 10, 11) ----------------
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         if (lane == 0) {

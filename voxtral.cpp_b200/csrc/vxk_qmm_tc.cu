@@ -7,8 +7,8 @@
 // The sub-block scales are folded into the tensor-core operand instead of
 // multiplying int32 results: a weight's 4-bit quant q times its 6-bit
 // sub-block scale sc is an integer <= 945, exact in f16, and so are the
-// quantized activations (|q8| <= 127); the fp32 accumulator of one 256-column
-// unit then holds d-free sum_j sc_j * sum q4*q8 exactly (well below 2^24).
+// quantized activations (|q8| <= 127); the fp32 accumulator of one unit holds
+// sum_j sc_j * sum q4*q8 exactly while it stays below 2^24 (mean |q8| < 70).
 // Q6_K's scaled quants p = sc*q reach 4096, past f16's exact integers; they
 // become two 8-bit operands, hi = floor(p / 64) (s8) and 4 (p mod 64) (u8),
 // multiplied by the int8 activations in kind::i8 MMAs (K = 32, int32
